@@ -1,0 +1,132 @@
+// Shared helpers for the dsv4 sm_100a kernels: status plumbing, dtype access, bf16 packing.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "dsv4.h"
+
+namespace dsv4 {
+
+// Thread-local message behind dsv4_last_error().
+void set_error(const char* fmt, ...);
+void clear_error();
+
+// Device error word: kernels record the first failure here (index out of range, wait timeout);
+// dsv4_device_error() reads and clears it. Each translation unit has its own word (no
+// relocatable device code); DSV4_ERROR_READER registers a reader of that word with the library.
+static __device__ int g_device_error = 0;
+
+__device__ __forceinline__ void raise_device_error(int code) { atomicCAS(&g_device_error, 0, code); }
+
+typedef cudaError_t (*error_reader_fn)(int*);
+int register_error_reader(error_reader_fn fn);
+cudaError_t read_all_error_words(int* first);
+
+#define DSV4_ERROR_READER(tag)                                                       \
+  static cudaError_t dsv4_read_error_##tag(int* out) {                               \
+    int v = 0, z = 0;                                                                \
+    cudaError_t e = cudaMemcpyFromSymbol(&v, ::dsv4::g_device_error, sizeof(int));   \
+    if (e != cudaSuccess) return e;                                                  \
+    e = cudaMemcpyToSymbol(::dsv4::g_device_error, &z, sizeof(int));                 \
+    *out = v;                                                                        \
+    return e;                                                                        \
+  }                                                                                  \
+  static int dsv4_error_reader_reg_##tag = ::dsv4::register_error_reader(dsv4_read_error_##tag);
+
+#define DSV4_CHECK_ARG(cond, ...)                 \
+  do {                                            \
+    if (!(cond)) {                                \
+      ::dsv4::set_error(__VA_ARGS__);             \
+      return DSV4_ERR_INVALID_ARGUMENT;           \
+    }                                             \
+  } while (0)
+
+#define DSV4_CHECK_DTYPE(cond, ...)               \
+  do {                                            \
+    if (!(cond)) {                                \
+      ::dsv4::set_error(__VA_ARGS__);             \
+      return DSV4_ERR_UNSUPPORTED_DTYPE;          \
+    }                                             \
+  } while (0)
+
+// After a launch: turn a launch failure into DSV4_ERR_CUDA with the kernel name.
+#define DSV4_LAUNCH_CHECK(name)                                                     \
+  do {                                                                              \
+    cudaError_t e_ = cudaGetLastError();                                            \
+    if (e_ != cudaSuccess) {                                                        \
+      ::dsv4::set_error("%s: launch failed: %s", name, cudaGetErrorString(e_));     \
+      return DSV4_ERR_CUDA;                                                         \
+    }                                                                               \
+  } while (0)
+
+#define DSV4_CUDA_CHECK(expr)                                                            \
+  do {                                                                                   \
+    cudaError_t e_ = (expr);                                                             \
+    if (e_ != cudaSuccess) {                                                             \
+      ::dsv4::set_error("%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
+      return DSV4_ERR_CUDA;                                                              \
+    }                                                                                    \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// ---- element access by runtime dtype ------------------------------------------------------
+__device__ __forceinline__ float load_as_float(const void* p, int64_t i, int dtype) {
+  if (dtype == DSV4_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void store_from_float(void* p, int64_t i, int dtype, float v) {
+  if (dtype == DSV4_BF16)
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<float*>(p)[i] = v;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// rope angle as the reference forms it: fp32 product of the position and the frequency
+// (torch.outer in fp32, ref_torch/norm_rope.py:48-50), then cos/sin of that fp32 angle.
+__device__ __forceinline__ void rope_cos_sin(int pos, float freq, float* c, float* s) {
+  float ang = __fmul_rn(static_cast<float>(pos), freq);
+  sincosf(ang, s, c);
+}
+
+// interleaved-pair complex rotation (x0 + i x1) * (c + i s), conj for the inverse.
+__device__ __forceinline__ void rotate_pair(float x0, float x1, float c, float s, bool inverse,
+                                            float* y0, float* y1) {
+  if (inverse) s = -s;
+  *y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+  *y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
+}  // namespace dsv4

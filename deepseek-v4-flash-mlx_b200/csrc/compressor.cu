@@ -1,0 +1,262 @@
+// KV block compressor (ref_torch/compressor.py:21-50; decode ring oracle/decode_engine.py:96-105).
+//
+// Input: the two projections kv = x wkv^T and score = x wgate^T (fp32, [b, s, 2d]) from the
+// projection GEMM. For compressed row g of a sequence, dim c in [0, d):
+//   slots 0..3: kv[4g-4+r, c],      score[4g-4+r, c]   + ape[r, c]      (group 0: 0 / -inf)
+//   slots 4..7: kv[4g+r,   d + c],  score[4g+r,   d + c] + ape[r, d + c]
+//   pooled[c] = sum_slot softmax_slot(score) * kv
+// then RMSNorm(norm_w), RoPE of the last rope_dim dims at position ratio*g (+pos0), and one
+// 128-bit vectorised store per thread into the cache (bf16) or a plain fp32 output; rows can be
+// scattered into a paged pool through out_rows. One CTA per compressed row, 256 threads, two
+// dims per thread. The decode kernel keeps the per-sequence ring [2*ratio, 2d] on the device.
+#include "common.cuh"
+
+namespace dsv4 {
+namespace cmp {
+
+constexpr int THREADS = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// normalise, rope and store two adjacent dims (c, c+1) of one compressed row
+__device__ __forceinline__ void finish_pair(float v0, float v1, int c, int d, int rope_dim,
+                                            const void* norm_w, int norm_dtype, float rinv,
+                                            const float* freqs, int pos, void* out, int64_t orow,
+                                            int out_dtype) {
+  v0 = v0 * rinv;
+  v1 = v1 * rinv;
+  if (norm_w) {
+    v0 = load_as_float(norm_w, c, norm_dtype) * v0;
+    v1 = load_as_float(norm_w, c + 1, norm_dtype) * v1;
+  }
+  if (c >= d - rope_dim) {
+    float cs, sn;
+    rope_cos_sin(pos, freqs[(c - (d - rope_dim)) >> 1], &cs, &sn);
+    rotate_pair(v0, v1, cs, sn, false, &v0, &v1);
+  }
+  const int64_t off = orow * d + c;
+  if (out_dtype == DSV4_BF16)
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(out) + off) = pack_bf16x2(v0, v1);
+  else
+    *reinterpret_cast<float2*>(reinterpret_cast<float*>(out) + off) = make_float2(v0, v1);
+}
+
+// softmax over 8 slots (max-subtracted, as torch.softmax) and the weighted sum
+__device__ __forceinline__ float pool8(const float* kv8, const float* sc8) {
+  float m = sc8[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m = fmaxf(m, sc8[i]);
+  float den = 0.f, num = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float e = expf(sc8[i] - m);
+    den += e;
+    num = fmaf(e, kv8[i], num);
+  }
+  return num / den;
+}
+
+__global__ void __launch_bounds__(THREADS) pool_kernel(dsv4_compressor_params p) {
+  __shared__ float red[33];
+  const int groups = p.s / p.ratio;
+  const int64_t rowid = blockIdx.x;  // b * groups + g
+  const int b = static_cast<int>(rowid / groups);
+  const int g = static_cast<int>(rowid % groups);
+  const int d = p.head_dim, d2 = 2 * d;
+  const int R = p.ratio;
+  const float* kvb = p.kv + static_cast<int64_t>(b) * p.s * d2;
+  const float* scb = p.score + static_cast<int64_t>(b) * p.s * d2;
+  float vals[2][2];  // up to 2 pairs per thread (d <= 1024)
+  float ss = 0.f;
+  int npairs = 0;
+  for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++npairs) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float kv8[16], sc8[16];
+      const int cc = c + e;
+      for (int r = 0; r < R; ++r) {
+        if (g > 0) {
+          const int64_t t = static_cast<int64_t>(g - 1) * R + r;
+          kv8[r] = kvb[t * d2 + cc];
+          sc8[r] = scb[t * d2 + cc] + p.ape[r * d2 + cc];
+        } else {
+          kv8[r] = 0.f;
+          sc8[r] = -INFINITY;
+        }
+        const int64_t t2 = static_cast<int64_t>(g) * R + r;
+        kv8[R + r] = kvb[t2 * d2 + d + cc];
+        sc8[R + r] = scb[t2 * d2 + d + cc] + p.ape[r * d2 + d + cc];
+      }
+      float v;
+      if (R == 4) {
+        v = pool8(kv8, sc8);
+      } else {
+        float m = sc8[0];
+        for (int i = 1; i < 2 * R; ++i) m = fmaxf(m, sc8[i]);
+        float den = 0.f, num = 0.f;
+        for (int i = 0; i < 2 * R; ++i) {
+          float ex = expf(sc8[i] - m);
+          den += ex;
+          num = fmaf(ex, kv8[i], num);
+        }
+        v = num / den;
+      }
+      vals[npairs][e] = v;
+      ss = fmaf(v, v, ss);
+    }
+  }
+  ss = block_sum(ss, red);
+  const float rinv = rsqrtf(ss / static_cast<float>(d) + p.eps);
+  const int64_t orow = p.out_rows ? p.out_rows[rowid] : rowid;
+  npairs = 0;
+  for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++npairs)
+    finish_pair(vals[npairs][0], vals[npairs][1], c, d, p.rope_dim, p.norm_w, p.norm_dtype, rinv,
+                p.freqs, p.pos0 + R * g, p.out, orow, p.out_dtype);
+}
+
+// decode hand-off ring (ref_torch/compressor.py:67-74; seeding as oracle/decode_engine.py:91-95):
+// rows [0, R) = last full block (kv, score+ape), rows [R, R+rem) = remainder, rest 0 / -inf.
+__global__ void ring_seed_kernel(dsv4_compressor_params p) {
+  const int b = blockIdx.y;
+  const int slot = blockIdx.x;  // 0 .. 2R-1
+  const int R = p.ratio, d2 = 2 * p.head_dim;
+  const int cutoff = p.s - p.s % R;
+  const int rem = p.s % R;
+  int64_t t = -1;
+  int ape_r = 0;
+  if (slot < R) {
+    if (cutoff >= R) {
+      t = cutoff - R + slot;
+      ape_r = slot;
+    }
+  } else if (slot - R < rem) {
+    t = cutoff + (slot - R);
+    ape_r = slot - R;
+  }
+  float* rk = p.ring_kv + (static_cast<int64_t>(b) * 2 * R + slot) * d2;
+  float* rs = p.ring_score + (static_cast<int64_t>(b) * 2 * R + slot) * d2;
+  const float* kvb = p.kv + static_cast<int64_t>(b) * p.s * d2;
+  const float* scb = p.score + static_cast<int64_t>(b) * p.s * d2;
+  for (int c = threadIdx.x; c < d2; c += blockDim.x) {
+    if (t >= 0) {
+      rk[c] = kvb[t * d2 + c];
+      rs[c] = scb[t * d2 + c] + p.ape[ape_r * d2 + c];
+    } else {
+      rk[c] = 0.f;
+      rs[c] = -INFINITY;
+    }
+  }
+}
+
+// one decode token per sequence: ring row R + p%R <- (kv, score + ape[p%R]); when (p+1)%R == 0
+// emit the pooled row at position p+1-R and shift rows [R,2R) to [0,R).
+__global__ void __launch_bounds__(THREADS) decode_kernel(dsv4_compressor_decode_params p) {
+  __shared__ float red[33];
+  const int b = blockIdx.x;
+  const int R = p.ratio, d = p.head_dim, d2 = 2 * d;
+  const int pos = p.positions[b];
+  const int slot = R + pos % R;
+  float* rk = p.ring_kv + static_cast<int64_t>(b) * 2 * R * d2;
+  float* rs = p.ring_score + static_cast<int64_t>(b) * 2 * R * d2;
+  const float* kin = p.kv + static_cast<int64_t>(b) * d2;
+  const float* sin_ = p.score + static_cast<int64_t>(b) * d2;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    rk[slot * d2 + c] = kin[c];
+    rk[slot * d2 + d + c] = kin[d + c];
+    rs[slot * d2 + c] = sin_[c] + p.ape[(pos % R) * d2 + c];
+    rs[slot * d2 + d + c] = sin_[d + c] + p.ape[(pos % R) * d2 + d + c];
+  }
+  if ((pos + 1) % R != 0) return;
+  __syncthreads();  // the pooled read below covers dims written by other threads
+  float vals[2][2];
+  float ss = 0.f;
+  int np = 0;
+  for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++np) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int cc = c + e;
+      float kv8[16], sc8[16];
+      for (int r = 0; r < R; ++r) {
+        kv8[r] = rk[r * d2 + cc];
+        sc8[r] = rs[r * d2 + cc];
+        kv8[R + r] = rk[(R + r) * d2 + d + cc];
+        sc8[R + r] = rs[(R + r) * d2 + d + cc];
+      }
+      float m = sc8[0];
+      for (int i = 1; i < 2 * R; ++i) m = fmaxf(m, sc8[i]);
+      float den = 0.f, num = 0.f;
+      for (int i = 0; i < 2 * R; ++i) {
+        float ex = expf(sc8[i] - m);
+        den += ex;
+        num = fmaf(ex, kv8[i], num);
+      }
+      vals[np][e] = num / den;
+      ss = fmaf(vals[np][e], vals[np][e], ss);
+    }
+  }
+  ss = block_sum(ss, red);  // its barrier also orders the pooled reads before the shift below
+  const float rinv = rsqrtf(ss / static_cast<float>(d) + p.eps);
+  np = 0;
+  for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++np)
+    finish_pair(vals[np][0], vals[np][1], c, d, p.rope_dim, p.norm_w, p.norm_dtype, rinv, p.freqs,
+                pos + 1 - R, p.out, p.out_rows[b], p.out_dtype);
+  for (int c = threadIdx.x; c < d2; c += blockDim.x)
+    for (int r = 0; r < R; ++r) {
+      rk[r * d2 + c] = rk[(R + r) * d2 + c];
+      rs[r * d2 + c] = rs[(R + r) * d2 + c];
+    }
+}
+
+}  // namespace cmp
+}  // namespace dsv4
+
+using namespace dsv4;
+
+extern "C" int dsv4_compressor_pool(const dsv4_compressor_params* p, void* stream) {
+  DSV4_CHECK_ARG(p && p->kv && p->score && p->ape && p->out && p->freqs, "dsv4_compressor_pool: NULL tensor");
+  DSV4_CHECK_ARG(p->b > 0 && p->s >= 0 && p->ratio > 0 && p->ratio <= 8, "dsv4_compressor_pool: bad sizes");
+  DSV4_CHECK_ARG(p->head_dim % 2 == 0 && p->head_dim <= 4 * cmp::THREADS && p->head_dim >= p->rope_dim &&
+                     p->rope_dim % 2 == 0,
+                 "dsv4_compressor_pool: head_dim %d unsupported", p->head_dim);
+  DSV4_CHECK_DTYPE(p->out_dtype == DSV4_F32 || p->out_dtype == DSV4_BF16, "dsv4_compressor_pool: out dtype");
+  DSV4_CHECK_DTYPE(p->norm_w == nullptr || p->norm_dtype == DSV4_F32 || p->norm_dtype == DSV4_BF16,
+                   "dsv4_compressor_pool: norm dtype");
+  const int groups = p->s / p->ratio;
+  if (groups > 0) {
+    cmp::pool_kernel<<<static_cast<unsigned>(static_cast<int64_t>(p->b) * groups), cmp::THREADS, 0,
+                       as_stream(stream)>>>(*p);
+    DSV4_LAUNCH_CHECK("compressor pool_kernel");
+  }
+  if (p->ring_kv && p->ring_score) {
+    dim3 g(2 * p->ratio, p->b);
+    cmp::ring_seed_kernel<<<g, 256, 0, as_stream(stream)>>>(*p);
+    DSV4_LAUNCH_CHECK("compressor ring_seed_kernel");
+  }
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream) {
+  DSV4_CHECK_ARG(p && p->kv && p->score && p->ape && p->ring_kv && p->ring_score && p->positions &&
+                     p->out && p->out_rows && p->freqs,
+                 "dsv4_compressor_decode: NULL tensor");
+  DSV4_CHECK_ARG(p->b > 0 && p->ratio > 0 && p->ratio <= 8 && p->head_dim % 2 == 0 &&
+                     p->head_dim <= 4 * cmp::THREADS && p->rope_dim % 2 == 0 && p->rope_dim <= p->head_dim,
+                 "dsv4_compressor_decode: bad sizes");
+  DSV4_CHECK_DTYPE(p->out_dtype == DSV4_F32 || p->out_dtype == DSV4_BF16, "dsv4_compressor_decode: out dtype");
+  cmp::decode_kernel<<<p->b, cmp::THREADS, 0, as_stream(stream)>>>(*p);
+  DSV4_LAUNCH_CHECK("compressor decode_kernel");
+  return DSV4_OK;
+}

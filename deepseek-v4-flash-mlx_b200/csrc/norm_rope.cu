@@ -1,0 +1,217 @@
+// RMSNorm / per-head norm / interleaved RoPE (ref_torch/norm_rope.py:10-62, v4mlx/mla.py:26-28).
+//
+// All math in fp32: var = mean(x^2), x * rsqrt(var + eps) [* weight], then the rope rotation of
+// the last rope_dim dims as interleaved complex pairs, then one cast to the output dtype.
+// One warp per row; the row lives in registers between the reduction and the write.
+#include "common.cuh"
+
+namespace dsv4 {
+namespace nr {
+
+// generic RMSNorm, any dim (multiple of 2), one warp per row, two passes over L1-resident data
+__global__ void rmsnorm_kernel(dsv4_rmsnorm_params p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const int64_t base = row * p.dim;
+  float ss = 0.f;
+  for (int i = lane; i < p.dim; i += 32) {
+    float v = load_as_float(p.x, base + i, p.x_dtype);
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(p.dim) + p.eps);
+  for (int i = lane; i < p.dim; i += 32) {
+    float v = load_as_float(p.x, base + i, p.x_dtype) * r;
+    if (p.weight) v = load_as_float(p.weight, i, p.w_dtype) * v;
+    store_from_float(p.out, base + i, p.out_dtype, v);
+  }
+}
+
+__global__ void rope_kernel(dsv4_rope_params p) {
+  const int half = p.rope_dim / 2;
+  const int64_t total = p.s * p.heads * half;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int i = static_cast<int>(e % half);
+    const int64_t rowh = e / half;           // (position, head)
+    const int64_t pos_row = rowh / p.heads;
+    float c, s;
+    if (p.cis) {
+      const int64_t tr = pos_row % p.cis_rows;
+      c = p.cis[(tr * half + i) * 2 + 0];
+      s = p.cis[(tr * half + i) * 2 + 1];
+    } else {
+      int pos = p.positions ? p.positions[pos_row] : static_cast<int>(p.pos_offset + pos_row);
+      rope_cos_sin(pos, p.freqs[i], &c, &s);
+    }
+    const int64_t off = rowh * p.dim + (p.dim - p.rope_dim) + 2 * i;
+    float x0 = load_as_float(p.x, off, p.x_dtype), x1 = load_as_float(p.x, off + 1, p.x_dtype);
+    float y0, y1;
+    rotate_pair(x0, x1, c, s, p.inverse != 0, &y0, &y1);
+    store_from_float(p.out, off, p.out_dtype, y0);
+    store_from_float(p.out, off + 1, p.out_dtype, y1);
+  }
+}
+
+// also copies the non-rope part when out != x
+__global__ void copy_nonrope_kernel(dsv4_rope_params p) {
+  const int keep = p.dim - p.rope_dim;
+  const int64_t total = p.s * p.heads * keep;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rowh = e / keep;
+    const int i = static_cast<int>(e % keep);
+    store_from_float(p.out, rowh * p.dim + i, p.out_dtype, load_as_float(p.x, rowh * p.dim + i, p.x_dtype));
+  }
+}
+
+// fused norm + rope + cast for rows of DIM (compile-time) elements: one warp per (row, head).
+template <int DIM>
+__global__ void norm_rope_kernel(dsv4_norm_rope_params p) {
+  constexpr int PER = DIM / 32;  // contiguous elements per lane
+  const int lane = threadIdx.x & 31;
+  const int64_t unit = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (unit >= p.rows * p.heads) return;
+  const int64_t row = unit / p.heads;
+  const int head = static_cast<int>(unit % p.heads);
+  const int64_t src = unit * DIM + lane * PER;
+  float v[PER];
+  if (p.x_dtype == DSV4_BF16) {
+    const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(p.x) + src;
+#pragma unroll
+    for (int e = 0; e < PER; e += 8) {
+      uint4 u = *reinterpret_cast<const uint4*>(x + e);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = __bfloat1622float2(h2[q]);
+        v[e + 2 * q] = f.x;
+        v[e + 2 * q + 1] = f.y;
+      }
+    }
+  } else {
+    const float* x = reinterpret_cast<const float*>(p.x) + src;
+#pragma unroll
+    for (int e = 0; e < PER; e += 4) {
+      float4 f = *reinterpret_cast<const float4*>(x + e);
+      v[e] = f.x;
+      v[e + 1] = f.y;
+      v[e + 2] = f.z;
+      v[e + 3] = f.w;
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) ss = fmaf(v[e], v[e], ss);
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(DIM) + p.eps);
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    float t = v[e] * r;
+    if (p.weight) t = load_as_float(p.weight, lane * PER + e, p.w_dtype) * t;
+    v[e] = t;
+  }
+  const int rope_lo = DIM - p.rope_dim;
+  if (lane * PER + PER > rope_lo) {
+    const int pos = p.positions[row];
+#pragma unroll
+    for (int e = 0; e < PER; e += 2) {
+      const int d = lane * PER + e;
+      if (d >= rope_lo) {
+        float c, s;
+        rope_cos_sin(pos, p.freqs[(d - rope_lo) >> 1], &c, &s);
+        rotate_pair(v[e], v[e + 1], c, s, false, &v[e], &v[e + 1]);
+      }
+    }
+  }
+  int64_t dst;
+  if (p.out_rows) {
+    dst = (p.out_rows[row] * p.heads + head) * DIM + lane * PER;
+  } else {
+    dst = unit * DIM + lane * PER;
+  }
+  if (p.out_dtype == DSV4_BF16) {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + dst;
+#pragma unroll
+    for (int e = 0; e < PER; e += 8) {
+      uint4 u = make_uint4(pack_bf16x2(v[e], v[e + 1]), pack_bf16x2(v[e + 2], v[e + 3]),
+                           pack_bf16x2(v[e + 4], v[e + 5]), pack_bf16x2(v[e + 6], v[e + 7]));
+      *reinterpret_cast<uint4*>(o + e) = u;
+    }
+  } else {
+    float* o = reinterpret_cast<float*>(p.out) + dst;
+#pragma unroll
+    for (int e = 0; e < PER; e += 4) *reinterpret_cast<float4*>(o + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+  }
+}
+
+}  // namespace nr
+}  // namespace dsv4
+
+using namespace dsv4;
+
+static bool is_float_dtype(int d) { return d == DSV4_F32 || d == DSV4_BF16; }
+
+extern "C" int dsv4_rmsnorm(const dsv4_rmsnorm_params* p, void* stream) {
+  DSV4_CHECK_ARG(p && p->x && p->out && p->rows >= 0 && p->dim > 0, "dsv4_rmsnorm: bad arguments");
+  DSV4_CHECK_DTYPE(is_float_dtype(p->x_dtype) && is_float_dtype(p->out_dtype) &&
+                       (p->weight == nullptr || is_float_dtype(p->w_dtype)),
+                   "dsv4_rmsnorm: F32/BF16 only");
+  if (p->rows == 0) return DSV4_OK;
+  const int warps = 8;
+  int64_t blocks = (p->rows + warps - 1) / warps;
+  nr::rmsnorm_kernel<<<static_cast<unsigned>(blocks), warps * 32, 0, as_stream(stream)>>>(*p);
+  DSV4_LAUNCH_CHECK("rmsnorm_kernel");
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_rope(const dsv4_rope_params* p, void* stream) {
+  DSV4_CHECK_ARG(p && p->x && p->out && p->s >= 0 && p->heads > 0 && p->rope_dim > 0 &&
+                     p->rope_dim % 2 == 0 && p->rope_dim <= p->dim,
+                 "dsv4_rope: bad arguments");
+  DSV4_CHECK_ARG((p->cis != nullptr) != (p->freqs != nullptr), "dsv4_rope: give exactly one of cis / freqs");
+  DSV4_CHECK_ARG(p->cis == nullptr || p->cis_rows > 0, "dsv4_rope: cis_rows must be > 0");
+  DSV4_CHECK_DTYPE(is_float_dtype(p->x_dtype) && is_float_dtype(p->out_dtype), "dsv4_rope: F32/BF16 only");
+  if (p->s == 0) return DSV4_OK;
+  const int64_t total = p->s * p->heads * (p->rope_dim / 2);
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > 16 * num_sms()) blocks = 16 * num_sms();
+  if (p->out != p->x && p->dim > p->rope_dim) {
+    nr::copy_nonrope_kernel<<<blocks, 256, 0, as_stream(stream)>>>(*p);
+    DSV4_LAUNCH_CHECK("copy_nonrope_kernel");
+  }
+  nr::rope_kernel<<<blocks, 256, 0, as_stream(stream)>>>(*p);
+  DSV4_LAUNCH_CHECK("rope_kernel");
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_norm_rope(const dsv4_norm_rope_params* p, void* stream) {
+  DSV4_CHECK_ARG(p && p->x && p->out && p->freqs && p->positions && p->rows >= 0 && p->heads > 0,
+                 "dsv4_norm_rope: bad arguments");
+  DSV4_CHECK_ARG(p->rope_dim > 0 && p->rope_dim % 2 == 0 && p->rope_dim <= p->dim,
+                 "dsv4_norm_rope: bad rope_dim");
+  DSV4_CHECK_DTYPE(is_float_dtype(p->x_dtype) && is_float_dtype(p->out_dtype) &&
+                       (p->weight == nullptr || is_float_dtype(p->w_dtype)),
+                   "dsv4_norm_rope: F32/BF16 only");
+  if (p->rows == 0) return DSV4_OK;
+  const int warps = 8;
+  const int64_t units = p->rows * p->heads;
+  const unsigned blocks = static_cast<unsigned>((units + warps - 1) / warps);
+  switch (p->dim) {
+    case 512:
+      nr::norm_rope_kernel<512><<<blocks, warps * 32, 0, as_stream(stream)>>>(*p);
+      break;
+    case 256:
+      nr::norm_rope_kernel<256><<<blocks, warps * 32, 0, as_stream(stream)>>>(*p);
+      break;
+    case 128:
+      nr::norm_rope_kernel<128><<<blocks, warps * 32, 0, as_stream(stream)>>>(*p);
+      break;
+    default:
+      set_error("dsv4_norm_rope: dim %d unsupported (128/256/512)", p->dim);
+      return DSV4_ERR_INVALID_ARGUMENT;
+  }
+  DSV4_LAUNCH_CHECK("norm_rope_kernel");
+  return DSV4_OK;
+}

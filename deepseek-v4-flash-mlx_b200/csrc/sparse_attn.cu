@@ -1,0 +1,560 @@
+// Gathered sparse MLA attention (ref_torch/sparse_attn.py:23-34) for B200.
+//
+// One CTA owns one query, a block of 64 heads and a contiguous range of its index list (a
+// "split"). All heads share the gathered latent rows (MLA: K and V are the same 512-wide row),
+// so the heads are the MMA M dimension. Per tile of 64 gathered rows:
+//   gather   : cp.async 16-byte copies of the rows named by idx into a swizzled smem tile
+//              (double buffered: the next tile's gather overlaps this tile's math)
+//   S = Q K^T: bf16 mma.sync m16n8k16, fp32 accumulate (64 heads x 64 rows, K = 512)
+//   softmax  : online (running max / sum per head, exp2 domain), masked rows are -inf
+//   O += P V : P in bf16, V = the same smem tile read transposed (64 heads x 512 dims)
+// A query whose list spans several CTAs writes an unnormalised partial (O, m, l) to the
+// workspace and a combine kernel merges the partials; the sink enters only the denominator,
+// exactly as the reference: o = sum p v / (sum p + exp(sink - m)).
+#include "common.cuh"
+
+namespace dsv4 {
+namespace sa {
+
+constexpr int D = 512;          // latent row (K and V)
+constexpr int HB = 64;          // heads per CTA
+constexpr int BN = 64;          // gathered rows per tile
+constexpr int THREADS = 256;
+constexpr int ROW_BYTES = D * 2;               // 1024
+constexpr int Q_BYTES = HB * ROW_BYTES;        // 64 KB
+constexpr int KV_BYTES = BN * ROW_BYTES;       // 64 KB
+constexpr int P_BYTES = HB * BN * 2;           // 8 KB
+constexpr float LOG2E = 1.4426950408889634f;
+
+struct Smem {
+  alignas(128) uint8_t q[Q_BYTES];
+  alignas(128) uint8_t kv[2][KV_BYTES];
+  alignas(128) uint8_t p[P_BYTES];
+  float red_max[4][HB];
+  float red_sum[4][HB];
+  float m_run[2][HB];
+  float l_run[HB];
+  float alpha[HB];
+  int32_t rowidx[2][BN];
+};
+
+// swizzled byte offset of 16-byte chunk `c` of row `r` in a tile whose rows are `row_chunks`
+// chunks long (XOR of the low three chunk bits with the row keeps ldmatrix conflict-free).
+__device__ __forceinline__ uint32_t swz(int r, int c, int row_bytes) {
+  return static_cast<uint32_t>(r * row_bytes + ((c ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g, bool valid) {
+  int sz = valid ? 16 : 0;  // 0 source bytes: the 16 destination bytes are zero-filled
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g), "r"(sz));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+struct Params {
+  const void* q;
+  const __nv_bfloat16* kv;
+  const float* sink;
+  const void* idx;
+  void* out;
+  float* part;  // workspace partials [s][hblocks][splits][HB][D] then m,l [s][hblocks][splits][HB][2]
+  int64_t s, n;
+  int h, t, splits, hblocks;
+  int q_dtype, idx_dtype, out_dtype;
+  float scale_log2;  // scale * log2(e)
+  const float* rope_freqs;
+  const int32_t* positions;
+  int rope_dim;
+};
+
+__device__ __forceinline__ int64_t load_idx(const void* idx, int64_t off, int dtype) {
+  if (dtype == DSV4_I64) return __ldg(reinterpret_cast<const long long*>(idx) + off);
+  return __ldg(reinterpret_cast<const int32_t*>(idx) + off);
+}
+
+// Issue the gather of tile rows [t0, t0+BN) of this query into kv buffer `buf`.
+__device__ __forceinline__ void gather_tile(const Params& P, Smem& sm, int buf, int64_t qi,
+                                            int t0, int t_end) {
+  const int tid = threadIdx.x;
+  if (tid < BN) {
+    int t = t0 + tid;
+    int32_t r = -1;
+    if (t < t_end) {
+      int64_t v = load_idx(P.idx, qi * P.t + t, P.idx_dtype);
+      if (v >= P.n) {
+        raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
+        v = -1;
+      }
+      r = v < 0 ? -1 : static_cast<int32_t>(v);
+    }
+    sm.rowidx[buf][tid] = r;
+  }
+  // each thread re-reads the indices of the rows it copies (an L1 broadcast) rather than
+  // waiting on a barrier for the smem copy above.
+  const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(sm.kv[buf]));
+  const int chunk = tid & 63;      // 64 chunks of 16 B per row
+#pragma unroll 4
+  for (int rr = tid >> 6; rr < BN; rr += THREADS / 64) {
+    int t = t0 + rr;
+    int64_t v = -1;
+    if (t < t_end) {
+      v = load_idx(P.idx, qi * P.t + t, P.idx_dtype);
+      if (v >= P.n) v = -1;
+    }
+    const bool valid = v >= 0;
+    const __nv_bfloat16* src = P.kv + (valid ? v : 0) * D + chunk * 8;
+    cp_async16(base + swz(rr, chunk, ROW_BYTES), src, valid);
+  }
+  cp_async_commit();
+}
+
+__global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t qi = blockIdx.x / P.splits;
+  const int split = static_cast<int>(blockIdx.x % P.splits), hblk = blockIdx.y;
+  const int h0 = hblk * HB;
+  const int heads_here = min(HB, P.h - h0);
+
+  // index range of this split (in whole tiles)
+  const int ntiles_all = (P.t + BN - 1) / BN;
+  const int per = (ntiles_all + P.splits - 1) / P.splits;
+  const int tile_begin = split * per;
+  const int tile_end = min(ntiles_all, tile_begin + per);
+  const int t_end = P.t;
+
+  // ---- stage Q (64 heads x 512) as bf16, swizzled ----
+  {
+    const uint32_t qbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
+    for (int c = tid; c < HB * 64; c += THREADS) {
+      int hh = c >> 6, ch = c & 63;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (hh < heads_here) {
+        int64_t off = ((qi * P.h) + h0 + hh) * D + ch * 8;
+        if (P.q_dtype == DSV4_BF16) {
+          v = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(P.q) + off));
+        } else {
+          const float4* f = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(P.q) + off);
+          float4 a = __ldg(f), b = __ldg(f + 1);
+          v.x = pack_bf16x2(a.x, a.y);
+          v.y = pack_bf16x2(a.z, a.w);
+          v.z = pack_bf16x2(b.x, b.y);
+          v.w = pack_bf16x2(b.z, b.w);
+        }
+      }
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(qbase + swz(hh, ch, ROW_BYTES)),
+                   "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+    }
+  }
+  if (tid < HB) {
+    sm.m_run[0][tid] = -INFINITY;
+    sm.m_run[1][tid] = -INFINITY;
+    sm.l_run[tid] = 0.f;
+  }
+
+  float o[4][8][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o[a][b][c] = 0.f;
+
+  if (tile_begin < tile_end) gather_tile(P, sm, 0, qi, tile_begin * BN, t_end);
+
+  const uint32_t q_s = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
+  const uint32_t p_s = static_cast<uint32_t>(__cvta_generic_to_shared(sm.p));
+  // QK warp layout: heads [wm*32, +32), rows [wn*16, +16)
+  const int wm = warp & 1, wn = warp >> 1;
+  int cur = 0;
+
+  for (int tile = tile_begin; tile < tile_end; ++tile) {
+    const int buf = (tile - tile_begin) & 1;
+    cp_async_wait<0>();
+    __syncthreads();  // S1: tile `buf` landed; previous PV finished
+    if (tile + 1 < tile_end) gather_tile(P, sm, buf ^ 1, qi, (tile + 1) * BN, t_end);
+    const uint32_t kv_s = static_cast<uint32_t>(__cvta_generic_to_shared(sm.kv[buf]));
+
+    // ---- S = Q K^T ----
+    float s[2][2][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[a][b][c] = 0.f;
+#pragma unroll 4
+    for (int kc = 0; kc < D / 16; ++kc) {
+      uint32_t a[2][4], b[4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        int r = wm * 32 + mt * 16 + (lane & 15);
+        int c = kc * 2 + (lane >> 4);
+        ldsm_x4(q_s + swz(r, c, ROW_BYTES), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+      }
+      {
+        int r = wn * 16 + (lane & 7) + ((lane >> 4) << 3);
+        int c = kc * 2 + ((lane >> 3) & 1);
+        ldsm_x4(kv_s + swz(r, c, ROW_BYTES), b[0], b[1], b[2], b[3]);
+      }
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        mma_bf16(s[mt][0], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b[0], b[1]);
+        mma_bf16(s[mt][1], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b[2], b[3]);
+      }
+    }
+    // scale to log2 domain, mask invalid rows, partial row max over this warp's 16 rows
+    float pmax[2][2];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) pmax[mt][hf] = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        int row = wn * 16 + nt * 8 + (lane & 3) * 2 + j;
+        bool valid = sm.rowidx[buf][row] >= 0;
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            float v = valid ? s[mt][nt][hf * 2 + j] * P.scale_log2 : -INFINITY;
+            s[mt][nt][hf * 2 + j] = v;
+            pmax[mt][hf] = fmaxf(pmax[mt][hf], v);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float v = pmax[mt][hf];
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+        if ((lane & 3) == 0) sm.red_max[wn][wm * 32 + mt * 16 + hf * 8 + (lane >> 2)] = v;
+      }
+    __syncthreads();  // S2
+
+    // ---- p = exp2(s - m_new), partial sums, P -> smem (bf16) ----
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int hh = wm * 32 + mt * 16 + hf * 8 + (lane >> 2);
+        float mnew = fmaxf(fmaxf(sm.red_max[0][hh], sm.red_max[1][hh]),
+                           fmaxf(sm.red_max[2][hh], sm.red_max[3][hh]));
+        mnew = fmaxf(mnew, sm.m_run[cur][hh]);
+        const float msub = (mnew == -INFINITY) ? 0.f : mnew;
+        float psum = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          float p0 = exp2f(s[mt][nt][hf * 2 + 0] - msub);
+          float p1 = exp2f(s[mt][nt][hf * 2 + 1] - msub);
+          psum += p0 + p1;
+          int row = wn * 16 + nt * 8 + (lane & 3) * 2;
+          uint32_t addr = p_s + swz(hh, row >> 3, BN * 2) + (row & 7) * 2;
+          asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(addr), "r"(pack_bf16x2(p0, p1)));
+        }
+        psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+        psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+        if ((lane & 3) == 0) sm.red_sum[wn][hh] = psum;
+      }
+    }
+    if (tid < HB) {
+      float mold = sm.m_run[cur][tid];
+      float mnew = fmaxf(fmaxf(sm.red_max[0][tid], sm.red_max[1][tid]),
+                         fmaxf(sm.red_max[2][tid], sm.red_max[3][tid]));
+      mnew = fmaxf(mnew, mold);
+      sm.alpha[tid] = (mold == -INFINITY) ? 0.f : exp2f(mold - mnew);
+      sm.m_run[cur ^ 1][tid] = mnew;
+    }
+    __syncthreads();  // S3
+    if (tid < HB)
+      sm.l_run[tid] = sm.l_run[tid] * sm.alpha[tid] +
+                      ((sm.red_sum[0][tid] + sm.red_sum[1][tid]) + (sm.red_sum[2][tid] + sm.red_sum[3][tid]));
+
+    // ---- O = O * alpha + P V  (warp owns dims [warp*64, +64), all 64 heads) ----
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      float a0 = sm.alpha[mt * 16 + (lane >> 2)];
+      float a1 = sm.alpha[mt * 16 + 8 + (lane >> 2)];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        o[mt][nt][0] *= a0;
+        o[mt][nt][1] *= a0;
+        o[mt][nt][2] *= a1;
+        o[mt][nt][3] *= a1;
+      }
+    }
+#pragma unroll
+    for (int kc = 0; kc < BN / 16; ++kc) {
+      uint32_t a[4][4];
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        int r = mt * 16 + (lane & 15);
+        int c = kc * 2 + (lane >> 4);
+        ldsm_x4(p_s + swz(r, c, BN * 2), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+      }
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {  // pairs of n8 tiles
+        uint32_t b[4];
+        int r = kc * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        int c = warp * 8 + np * 2 + (lane >> 4);
+        ldsm_x4_t(kv_s + swz(r, c, ROW_BYTES), b[0], b[1], b[2], b[3]);
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          mma_bf16(o[mt][np * 2 + 0], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b[0], b[1]);
+          mma_bf16(o[mt][np * 2 + 1], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b[2], b[3]);
+        }
+      }
+    }
+    cur ^= 1;
+  }
+  __syncthreads();
+
+  // ---- epilogue ----
+  const int dbase = warp * 64;
+  if (P.splits == 1) {
+    const bool rope = P.rope_freqs != nullptr && dbase + 64 > D - P.rope_dim;
+    const int pos = rope ? P.positions[qi] : 0;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int hh = mt * 16 + hf * 8 + (lane >> 2);
+        if (hh >= heads_here) continue;
+        const float m = sm.m_run[cur][hh];
+        const float l = sm.l_run[hh];
+        float inv;
+        if (m == -INFINITY) {
+          inv = __int_as_float(0x7fc00000);  // no valid index: NaN like the reference
+        } else {
+          const float sink2 = P.sink[h0 + hh] * LOG2E;
+          inv = 1.f / (l + exp2f(sink2 - m));
+        }
+        const int64_t obase = ((qi * P.h) + h0 + hh) * D;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int d = dbase + nt * 8 + (lane & 3) * 2;
+          float v0 = o[mt][nt][hf * 2 + 0] * inv;
+          float v1 = o[mt][nt][hf * 2 + 1] * inv;
+          if (rope && d >= D - P.rope_dim) {
+            float c, sn;
+            rope_cos_sin(pos, P.rope_freqs[(d - (D - P.rope_dim)) >> 1], &c, &sn);
+            rotate_pair(v0, v1, c, sn, true, &v0, &v1);
+          }
+          if (P.out_dtype == DSV4_BF16) {
+            *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(P.out) + obase + d) =
+                pack_bf16x2(v0, v1);
+          } else {
+            *reinterpret_cast<float2*>(reinterpret_cast<float*>(P.out) + obase + d) = make_float2(v0, v1);
+          }
+        }
+      }
+    }
+  } else {
+    const int64_t unit = (qi * P.hblocks + hblk) * P.splits + split;
+    float* po = P.part + unit * (HB * D);
+    float* pml = P.part + (P.s * P.hblocks * P.splits) * (int64_t)(HB * D) + unit * (HB * 2);
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int hh = mt * 16 + hf * 8 + (lane >> 2);
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int d = dbase + nt * 8 + (lane & 3) * 2;
+          *reinterpret_cast<float2*>(po + hh * D + d) =
+              make_float2(o[mt][nt][hf * 2 + 0], o[mt][nt][hf * 2 + 1]);
+        }
+      }
+    if (tid < HB) {
+      pml[tid * 2 + 0] = sm.m_run[cur][tid];
+      pml[tid * 2 + 1] = sm.l_run[tid];
+    }
+  }
+}
+
+// Merge split partials: o = sum_s e^{m_s-M} O_s / (sum_s e^{m_s-M} l_s + e^{sink-M}).
+// One CTA per (query, head block); warp w merges heads w, w+8, ...
+__global__ void __launch_bounds__(256) combine_kernel(Params P) {
+  const int64_t qi = blockIdx.x;
+  const int hblk = blockIdx.y;
+  const int h0 = hblk * HB;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t unit0 = (qi * P.hblocks + hblk) * P.splits;
+  const float* pml = P.part + (P.s * P.hblocks * P.splits) * (int64_t)(HB * D);
+  const bool rope = P.rope_freqs != nullptr;
+  const int pos = rope ? P.positions[qi] : 0;
+  for (int hh = warp; hh < HB && h0 + hh < P.h; hh += 8) {
+    float M = -INFINITY;
+    for (int sp = lane; sp < P.splits; sp += 32) M = fmaxf(M, pml[(unit0 + sp) * (HB * 2) + hh * 2]);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int sp = lane; sp < P.splits; sp += 32) {
+      float m = pml[(unit0 + sp) * (HB * 2) + hh * 2];
+      float l = pml[(unit0 + sp) * (HB * 2) + hh * 2 + 1];
+      L += (m == -INFINITY) ? 0.f : exp2f(m - M) * l;
+    }
+    L = warp_sum(L);
+    const float inv = (M == -INFINITY) ? __int_as_float(0x7fc00000)
+                                       : 1.f / (L + exp2f(P.sink[h0 + hh] * LOG2E - M));
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+    for (int sp = 0; sp < P.splits; ++sp) {
+      const float m = pml[(unit0 + sp) * (HB * 2) + hh * 2];
+      if (m == -INFINITY) continue;
+      const float w = exp2f(m - M);
+      const float* src = P.part + (unit0 + sp) * (HB * D) + hh * D;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float4 v = *reinterpret_cast<const float4*>(src + j * 128 + lane * 4);
+        acc[j * 4 + 0] += w * v.x;
+        acc[j * 4 + 1] += w * v.y;
+        acc[j * 4 + 2] += w * v.z;
+        acc[j * 4 + 3] += w * v.w;
+      }
+    }
+    const int64_t obase = ((qi * P.h) + h0 + hh) * D;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int d = j * 128 + lane * 4;
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = acc[j * 4 + e] * inv;
+      if (rope && d >= D - P.rope_dim) {
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          float c, sn;
+          rope_cos_sin(pos, P.rope_freqs[(d + e - (D - P.rope_dim)) >> 1], &c, &sn);
+          rotate_pair(v[e], v[e + 1], c, sn, true, &v[e], &v[e + 1]);
+        }
+      }
+      if (P.out_dtype == DSV4_BF16) {
+        uint2 pk = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(P.out) + obase + d) = pk;
+      } else {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.out) + obase + d) = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
+  }
+}
+
+static int choose_splits(const dsv4_sparse_attn_params* p) {
+  if (p->num_splits > 0) return p->num_splits;
+  const int hblocks = (p->h + HB - 1) / HB;
+  const int ntiles = (p->t + BN - 1) / BN;
+  const int64_t units = p->s * hblocks;
+  const int sms = num_sms();
+  if (units >= sms || ntiles <= 1) return 1;
+  int want = static_cast<int>((sms + units - 1) / units);
+  if (want > ntiles) want = ntiles;
+  if (want > 64) want = 64;
+  // keep the split count a divisor-friendly size so every split gets whole tiles
+  int per = (ntiles + want - 1) / want;
+  return (ntiles + per - 1) / per;
+}
+
+}  // namespace sa
+DSV4_ERROR_READER(sparse_attn)
+
+}  // namespace dsv4
+
+using namespace dsv4;
+
+extern "C" size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p) {
+  if (!p || p->s <= 0 || p->h <= 0 || p->t <= 0) return 0;
+  const int splits = sa::choose_splits(p);
+  if (splits <= 1) return 0;
+  const int hblocks = (p->h + sa::HB - 1) / sa::HB;
+  const int64_t units = p->s * hblocks * splits;
+  return static_cast<size_t>(units) * (sa::HB * sa::D + sa::HB * 2) * sizeof(float);
+}
+
+extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) {
+  DSV4_CHECK_ARG(p != nullptr, "dsv4_sparse_attn: params is NULL");
+  DSV4_CHECK_ARG(p->q && p->kv && p->sink && p->idx && p->out, "dsv4_sparse_attn: NULL tensor");
+  DSV4_CHECK_ARG(p->d == sa::D, "dsv4_sparse_attn: head dim %d unsupported (512 only)", p->d);
+  DSV4_CHECK_ARG(p->h > 0 && p->h % 16 == 0, "dsv4_sparse_attn: heads %d must be a positive multiple of 16", p->h);
+  DSV4_CHECK_ARG(p->s >= 0 && p->t > 0 && p->n > 0, "dsv4_sparse_attn: bad sizes s=%lld t=%d n=%lld",
+                 (long long)p->s, p->t, (long long)p->n);
+  DSV4_CHECK_DTYPE(p->q_dtype == DSV4_F32 || p->q_dtype == DSV4_BF16, "dsv4_sparse_attn: q dtype");
+  DSV4_CHECK_DTYPE(p->idx_dtype == DSV4_I32 || p->idx_dtype == DSV4_I64, "dsv4_sparse_attn: idx dtype");
+  DSV4_CHECK_DTYPE(p->out_dtype == DSV4_F32 || p->out_dtype == DSV4_BF16, "dsv4_sparse_attn: out dtype");
+  DSV4_CHECK_ARG(p->rope_freqs == nullptr || (p->positions != nullptr && p->rope_dim > 0 &&
+                                               p->rope_dim <= 64 && p->rope_dim % 2 == 0),
+                 "dsv4_sparse_attn: inverse rope needs positions and 0 < rope_dim <= 64");
+  DSV4_CHECK_ARG(p->s * 64 < (int64_t)INT32_MAX, "dsv4_sparse_attn: too many queries per call");
+  if (p->s == 0) return DSV4_OK;
+  sa::Params P;
+  P.q = p->q;
+  P.kv = reinterpret_cast<const __nv_bfloat16*>(p->kv);
+  P.sink = p->sink;
+  P.idx = p->idx;
+  P.out = p->out;
+  P.s = p->s;
+  P.n = p->n;
+  P.h = p->h;
+  P.t = p->t;
+  P.hblocks = (p->h + sa::HB - 1) / sa::HB;
+  P.splits = sa::choose_splits(p);
+  P.q_dtype = p->q_dtype;
+  P.idx_dtype = p->idx_dtype;
+  P.out_dtype = p->out_dtype;
+  P.scale_log2 = p->scale * sa::LOG2E;
+  P.rope_freqs = p->rope_freqs;
+  P.positions = p->positions;
+  P.rope_dim = p->rope_dim;
+  P.part = nullptr;
+  if (P.splits > 1) {
+    size_t need = dsv4_sparse_attn_workspace_size(p);
+    if (p->workspace == nullptr || p->workspace_bytes < need) {
+      set_error("dsv4_sparse_attn: workspace of %zu bytes needed, %zu given", need, p->workspace_bytes);
+      return DSV4_ERR_WORKSPACE;
+    }
+    P.part = reinterpret_cast<float*>(p->workspace);
+  }
+  static bool attr_set = false;
+  const int smem = static_cast<int>(sizeof(sa::Smem));
+  if (!attr_set) {
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(sa::sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set = true;
+  }
+  dim3 grid(static_cast<unsigned>(P.s * P.splits), P.hblocks);
+  sa::sparse_attn_kernel<<<grid, sa::THREADS, smem, as_stream(stream)>>>(P);
+  DSV4_LAUNCH_CHECK("sparse_attn_kernel");
+  if (P.splits > 1) {
+    dim3 g2(static_cast<unsigned>(P.s), P.hblocks);
+    sa::combine_kernel<<<g2, 256, 0, as_stream(stream)>>>(P);
+    DSV4_LAUNCH_CHECK("combine_kernel");
+  }
+  return DSV4_OK;
+}

@@ -1,0 +1,183 @@
+"""Device-resident sparse-MLA decode state and the decode attention step.
+
+The reference keeps the decode state on the host and rebuilds the attended rows every token:
+a 128-row window ring `winr` and a growing `kvbuf` of [window rows | visible compressed rows]
+uploaded per step (oracle/v4_fast.py:93-118, oracle/step12_glue.py:142-173), which its own notes
+flag as the cost that grows with context (oracle/v4_serve_fast.py:116). Here the state lives in
+HBM and is addressed by index:
+
+  kv_pool     bf16 [batch*window + n_pages*page, 512]: first each sequence's window ring
+              (row win_base[b] + p % window), then pages of compressed rows
+  block_table int32 [batch, pages_per_seq]: compressed entry j of sequence b lives at pool row
+              comp_base + block_table[b, j // page] * page + j % page
+  k_idx       fp32 [batch, max_comp, 128]: indexer keys of the compressed entries
+  ring_kv / ring_score fp32 [batch, 2*ratio, 1024]: the compressor's decode ring
+
+`decode_attention` is the measured decode path: per-head norm + RoPE of q, the window index list,
+the indexer top-k written straight into the attention index list, and sparse attention with the
+inverse RoPE fused into its epilogue.
+"""
+import math
+
+import torch
+
+from . import _lib as L
+from .indexer import indexer_topk_into
+from .norm_rope import norm_rope, rope_freqs
+from .sparse_attn import sparse_attn_rope
+
+
+class SparseMLACache:
+    def __init__(self, batch, max_comp, window=128, head_dim=512, idx_dim=128, ratio=4, page=64,
+                 device="cuda", page_order=None):
+        self.batch, self.window, self.head_dim, self.ratio, self.page = batch, window, head_dim, ratio, page
+        self.max_comp = max_comp
+        self.pages_per_seq = math.ceil(max_comp / page)
+        n_pages = batch * self.pages_per_seq
+        self.comp_base = batch * window
+        self.kv_pool = torch.zeros((self.comp_base + n_pages * page, head_dim), dtype=torch.bfloat16,
+                                   device=device)
+        self.win_base = (torch.arange(batch, dtype=torch.int64) * window).to(device)
+        if page_order is None:
+            page_order = torch.arange(n_pages, dtype=torch.int32)
+        self.block_table = page_order.to(torch.int32).reshape(batch, self.pages_per_seq).to(device)
+        self.k_idx = torch.zeros((batch, max_comp, idx_dim), dtype=torch.float32, device=device)
+        self.ring_kv = torch.zeros((batch, 2 * ratio, 2 * head_dim), dtype=torch.float32, device=device)
+        self.ring_score = torch.full((batch, 2 * ratio, 2 * head_dim), float("-inf"), dtype=torch.float32,
+                                     device=device)
+        self.ring_k_idx = torch.zeros((batch, 2 * ratio, 2 * idx_dim), dtype=torch.float32, device=device)
+        self.ring_s_idx = torch.full((batch, 2 * ratio, 2 * idx_dim), float("-inf"), dtype=torch.float32,
+                                     device=device)
+
+    # ---- address helpers (host side) ----
+    def comp_rows(self, b, j):
+        """Pool rows of compressed entries j (tensor) of sequence b."""
+        bt = self.block_table[b].long()
+        return self.comp_base + bt[j // self.page] * self.page + j % self.page
+
+    def window_rows(self, b, positions):
+        return self.win_base[b] + positions % self.window
+
+    def fill_compressed(self, b, rows_bf16, keys_f32):
+        """Place n compressed rows (and their indexer keys) of sequence b (prefill hand-off)."""
+        n = rows_bf16.shape[0]
+        j = torch.arange(n, device=rows_bf16.device)
+        self.kv_pool[self.comp_rows(b, j)] = rows_bf16.to(torch.bfloat16)
+        self.k_idx[b, :n] = keys_f32
+
+    def fill_window(self, b, positions, rows_bf16):
+        self.kv_pool[self.window_rows(b, positions)] = rows_bf16.to(torch.bfloat16)
+
+
+def attention_index_buffer(batch, window, top_k, device):
+    return torch.empty((batch, window + top_k), dtype=torch.int32, device=device)
+
+
+def decode_attention(cache, q, q_idx, w_idx, sink, positions, top_k=512, scale=None, freqs=None, idx_buf=None,
+                     out_dtype=torch.bfloat16):
+    """One decode token per sequence.
+
+    q [b, 64, 512] raw (before the per-head norm), q_idx [b, 64, 128] fp32, w_idx [b, 64] fp32,
+    sink [64] fp32, positions int32 [b] (position p of the new token). Returns o [b, 64, 512] after
+    the inverse RoPE (the input of the output projection, oracle/v4_fast.py:118-119)."""
+    L.require_cuda(q, q_idx, w_idx, sink, positions)
+    b = q.shape[0]
+    if scale is None:
+        scale = cache.head_dim ** -0.5
+    if freqs is None:
+        freqs = rope_freqs(64, q.device)
+    positions = positions.to(torch.int32).contiguous()
+    qr = norm_rope(q, positions, freqs, weight=None)
+    idx = idx_buf if idx_buf is not None else attention_index_buffer(b, cache.window, top_k, q.device)
+    L.check(L.lib().dsv4_decode_window_indices(b, cache.window, L.ptr(positions), L.ptr(cache.win_base),
+                                               L.ptr(idx), idx.shape[1], L.stream_of(q)))
+    indexer_topk_into(idx.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
+                      cache.k_idx, top_k, positions.view(b, 1), cache.ratio, out_col=cache.window,
+                      out_offset=cache.comp_base, block_table=cache.block_table, page=cache.page)
+    return sparse_attn_rope(qr, cache.kv_pool, sink, idx, scale, positions, freqs, 64, out_dtype)
+
+
+class DecodeRunner:
+    """CUDA-graph-backed decode attention for a fixed batch: the serving-loop entry point.
+
+    The first call captures `decode_attention` on static device buffers into a CUDA graph (the
+    reference's per-token path is a Python loop of library calls, oracle/v4_fast.py:82-122; here one
+    graph launch replays the six kernels). `step_device` replays with inputs already on the device;
+    `step_host` copies this token's inputs from pinned host memory, replays, and copies the output
+    back to pinned host memory, all ordered on the runner's stream.
+    """
+
+    def __init__(self, cache, sink, top_k=512, device="cuda", out_dtype=torch.bfloat16, stream=None):
+        self.cache, self.top_k = cache, top_k
+        b = cache.batch
+        dev = torch.device(device)
+        self.sink = sink.float().contiguous().to(dev)
+        self.q = torch.zeros((b, 64, cache.head_dim), dtype=torch.float32, device=dev)
+        self.q_idx = torch.zeros((b, 64, 128), dtype=torch.float32, device=dev)
+        self.w_idx = torch.zeros((b, 64), dtype=torch.float32, device=dev)
+        self.positions = torch.zeros((b,), dtype=torch.int32, device=dev)
+        self.idx = attention_index_buffer(b, cache.window, top_k, dev)
+        self.freqs = rope_freqs(64, dev)
+        self.out_dtype = out_dtype
+        self.out = None
+        self.graph = None
+        self.stream = stream or torch.cuda.Stream(dev)
+        self.h_q = torch.zeros(self.q.shape, dtype=torch.float32).pin_memory()
+        self.h_qi = torch.zeros(self.q_idx.shape, dtype=torch.float32).pin_memory()
+        self.h_w = torch.zeros(self.w_idx.shape, dtype=torch.float32).pin_memory()
+        self.h_pos = torch.zeros(self.positions.shape, dtype=torch.int32).pin_memory()
+        self.h_out = None
+        self._h2d_done = None
+
+    def _body(self):
+        return decode_attention(self.cache, self.q, self.q_idx, self.w_idx, self.sink, self.positions, self.top_k,
+                                freqs=self.freqs, idx_buf=self.idx, out_dtype=self.out_dtype)
+
+    def capture(self):
+        with torch.cuda.stream(self.stream):
+            self._body()  # warm up allocations and one-time attributes outside capture
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.out = self._body()
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+
+    def step_device(self):
+        if self.graph is None:
+            self.capture()
+        with torch.cuda.stream(self.stream):
+            self.graph.replay()
+        return self.out
+
+    def step_host(self, q, q_idx, w_idx, positions):
+        """Host tensors in, host tensor out, ordered on the runner's stream. Pinned inputs are copied
+        directly; other host tensors are staged through pinned buffers (waiting for the previous
+        step's copies first). The returned pinned output is valid after `synchronize()` and until
+        the next step."""
+        if self.graph is None:
+            self.capture()
+        srcs = (q, q_idx, w_idx, positions)
+        if not all(t.is_pinned() for t in srcs):
+            if self._h2d_done is not None:
+                self._h2d_done.synchronize()
+            for dst, src in zip((self.h_q, self.h_qi, self.h_w, self.h_pos), srcs):
+                dst.copy_(src)
+            srcs = (self.h_q, self.h_qi, self.h_w, self.h_pos)
+        with torch.cuda.stream(self.stream):
+            for dst, src in zip((self.q, self.q_idx, self.w_idx, self.positions), srcs):
+                dst.copy_(src, non_blocking=True)
+            if self._h2d_done is None:
+                self._h2d_done = torch.cuda.Event()
+            self._h2d_done.record(self.stream)
+            self.graph.replay()
+            self.h_out.copy_(self.out, non_blocking=True)
+        return self.h_out
+
+    def h2d_bytes(self):
+        return sum(t.numel() * t.element_size() for t in (self.q, self.q_idx, self.w_idx, self.positions))
+
+    def d2h_bytes(self):
+        return self.out.numel() * self.out.element_size() if self.out is not None else 0
+
+    def synchronize(self):
+        self.stream.synchronize()

@@ -1,0 +1,101 @@
+"""Lightning indexer + top-k selection.
+
+The reference has no indexer: it attends to every visible compressed row
+(oracle/decode_engine.py:112-114, oracle/v4_fast.py:114-117). This op scores the visible
+compressed keys, score[j] = sum_h w[h] * relu(q[h] . k[j]) in fp32 with a fixed rounding order,
+and keeps the top_k keys by (score desc, index asc), written in ascending key order and padded
+with -1. When top_k >= the visible count it returns exactly the reference's list.
+"""
+import ctypes
+
+import torch
+
+from . import _lib as L
+
+
+def _params(q, w, k, out, top_k, positions, ratio, out_col, out_offset, block_table, page, scores_out):
+    b, s, h, di = q.shape
+    p = L.IndexerParams()
+    p.q, p.w, p.k, p.out = L.ptr(q), L.ptr(w), L.ptr(k), L.ptr(out)
+    p.scores_out = L.ptr(scores_out) if scores_out is not None else None
+    p.batch, p.s, p.heads, p.n_keys, p.top_k = b, s, h, k.shape[1], top_k
+    p.k_batch_stride = k.shape[1]
+    p.positions = L.ptr(positions) if positions is not None else None
+    p.ratio = ratio
+    p.out_stride, p.out_col, p.out_offset = out.shape[-1], out_col, out_offset
+    p.block_table = L.ptr(block_table) if block_table is not None else None
+    p.table_stride = block_table.shape[-1] if block_table is not None else 0
+    p.page = page
+    return p
+
+
+def _run(p, device, stream_ref):
+    nbytes = L.lib().dsv4_indexer_topk_workspace_size(ctypes.byref(p))
+    ws = L.workspace(nbytes, device)
+    p.workspace, p.workspace_bytes = L.ptr(ws), nbytes
+    L.check(L.lib().dsv4_indexer_topk(ctypes.byref(p), L.stream_of(stream_ref)))
+
+
+@torch.library.custom_op("dsv4::indexer_topk", mutates_args=(), device_types="cuda")
+def _indexer_op(q_idx: torch.Tensor, w: torch.Tensor, k_idx: torch.Tensor, top_k: int,
+                positions: torch.Tensor | None, ratio: int) -> torch.Tensor:
+    b, s = q_idx.shape[0], q_idx.shape[1]
+    out = torch.empty((b, s, top_k), dtype=torch.int32, device=q_idx.device)
+    p = _params(q_idx, w, k_idx, out, top_k, positions, ratio, 0, 0, None, 0, None)
+    _run(p, q_idx.device, q_idx)
+    return out
+
+
+@_indexer_op.register_fake
+def _(q_idx, w, k_idx, top_k, positions, ratio):
+    return torch.empty((q_idx.shape[0], q_idx.shape[1], top_k), dtype=torch.int32, device=q_idx.device)
+
+
+def _prep(q_idx, w, k_idx, positions):
+    L.require_cuda(q_idx, w, k_idx, positions)
+    squeeze = q_idx.dim() == 3
+    if squeeze:  # [s, h, d] -> [1, s, h, d]
+        q_idx, w, k_idx = q_idx[None], w[None], k_idx[None]
+        if positions is not None:
+            positions = positions.reshape(1, -1)
+    if q_idx.dtype != torch.float32 or w.dtype != torch.float32 or k_idx.dtype != torch.float32:
+        raise TypeError("indexer: q_idx, w and k_idx must be float32 (scores are computed in fp32)")
+    if positions is not None:
+        positions = positions.to(torch.int32).contiguous()
+    return q_idx.contiguous(), w.contiguous(), k_idx.contiguous(), positions, squeeze
+
+
+def indexer_topk(q_idx, w, k_idx, top_k, positions=None, ratio=4):
+    """q_idx [b, s, 64, 128] (or [s, 64, 128]), w [b, s, 64], k_idx [b, n, 128] fp32 ->
+    int32 [b, s, top_k] key indices. With `positions`, query i sees keys j < (positions[i]+1)//ratio
+    (the causal compressed-block rule of oracle/decode_engine.py:112)."""
+    q_idx, w, k_idx, positions, squeeze = _prep(q_idx, w, k_idx, positions)
+    out = _indexer_op(q_idx, w, k_idx, int(top_k), positions, int(ratio))
+    return out[0] if squeeze else out
+
+
+def indexer_scores(q_idx, w, k_idx, positions=None, ratio=4):
+    """Raw fp32 scores [b, s, n] (entries beyond each query's visible range are left undefined);
+    exposed for verification against the CPU oracle."""
+    q_idx, w, k_idx, positions, squeeze = _prep(q_idx, w, k_idx, positions)
+    b, s = q_idx.shape[0], q_idx.shape[1]
+    scores = torch.full((b, s, k_idx.shape[1]), float("nan"), dtype=torch.float32, device=q_idx.device)
+    out = torch.empty((b, s, 1), dtype=torch.int32, device=q_idx.device)
+    p = _params(q_idx, w, k_idx, out, 1, positions, ratio, 0, 0, None, 0, scores)
+    _run(p, q_idx.device, q_idx)
+    return scores[0] if squeeze else scores
+
+
+def indexer_topk_into(out, q_idx, w, k_idx, top_k, positions=None, ratio=4, out_col=0, out_offset=0,
+                      block_table=None, page=0):
+    """Write the selection into columns [out_col, out_col+top_k) of an existing int32 index buffer
+    out [b, s, T], mapping key j to pool row out_offset + j, or through a block table
+    (block_table[b, j // page] * page + j % page + out_offset). Used by the decode and prefill
+    pipelines to build the attention index list without a copy."""
+    q_idx, w, k_idx, positions, _ = _prep(q_idx, w, k_idx, positions)
+    if out.dtype != torch.int32 or not out.is_contiguous():
+        raise TypeError("indexer_topk_into: out must be a contiguous int32 tensor")
+    p = _params(q_idx, w, k_idx, out, int(top_k), positions, int(ratio), int(out_col), int(out_offset),
+                block_table, int(page), None)
+    _run(p, q_idx.device, q_idx)
+    return out

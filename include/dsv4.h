@@ -1,0 +1,246 @@
+/*
+ * dsv4.h — C ABI of the B200 (sm_100a) compressed sparse-MLA attention path of DeepSeek-V4-Flash.
+ *
+ * Every entry point takes plain pointers, sizes and a cudaStream_t passed as `void*`; no torch
+ * type crosses this boundary. Tensors are borrowed: the caller owns every buffer, including the
+ * workspace (query its size with the matching *_workspace_size call). The library never frees and
+ * never calls cudaMalloc on these paths. Every call is asynchronous on `stream` and returns a
+ * dsv4_status; on a non-zero status dsv4_last_error() returns a message for the calling thread.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   dsv4_sparse_attn          <- ref_torch/sparse_attn.py:23  sparse_attn(q, kv, attn_sink, topk_idxs, scale)
+ *                                (MLX twin v4mlx/sparse_attn.py:26)
+ *   dsv4_window_topk_idxs     <- ref_torch/sparse_attn.py:9   get_window_topk_idxs(window_size, bsz, seqlen, start_pos)
+ *   dsv4_rmsnorm              <- ref_torch/norm_rope.py:10    rmsnorm(x, weight, eps)
+ *                                and v4mlx/mla.py:26          perhead_norm(q, eps) (weight == NULL)
+ *   dsv4_rope                 <- ref_torch/norm_rope.py:53    apply_rotary_emb(x, freqs_cis, inverse)
+ *   dsv4_norm_rope            <- the rmsnorm -> rope -> cast chains of oracle/decode_engine.py:77-81
+ *                                and oracle/v4_fast.py:87-91 (fused)
+ *   dsv4_yarn_freqs           <- ref_torch/norm_rope.py:19    precompute_freqs(...)
+ *   dsv4_compressor_pool      <- ref_torch/compressor.py:21   compressor_prefill(...) after its two projections
+ *   dsv4_compressor_decode    <- oracle/decode_engine.py:96-105 (decode ring step; MLX twin oracle/v4_fast.py:97-106)
+ *   dsv4_linear               <- v4mlx/mla.py:16-42           linear / q_down / q_up / kv_proj / o_grouped
+ *                                (8-bit grouped weights as oracle/v4_fast.py:31-34 qz/qmm, symmetric here)
+ *   dsv4_indexer_topk         <- no reference code: the reference attends to every visible compressed row
+ *                                (oracle/decode_engine.py:112-114); this is the lightning-indexer selection
+ *                                that replaces that list when more than top_k rows are visible.
+ *   dsv4_decode_window_indices<- oracle/v4_fast.py:108-117 (window rows of the attended list, ring order
+ *                                of ref_torch/sparse_attn.py:11-13)
+ */
+#ifndef DSV4_H_
+#define DSV4_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSV4_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define DSV4_API __attribute__((visibility("default")))
+#else
+#define DSV4_API
+#endif
+
+typedef enum {
+  DSV4_OK = 0,
+  DSV4_ERR_INVALID_ARGUMENT = 1,  /* bad shape, null pointer, unsupported size */
+  DSV4_ERR_UNSUPPORTED_DTYPE = 2,
+  DSV4_ERR_CUDA = 3,              /* a CUDA runtime call failed; message carries cudaGetErrorString */
+  DSV4_ERR_INDEX_OUT_OF_RANGE = 4,/* device error word: a gathered index was outside [-1, n) */
+  DSV4_ERR_WAIT_TIMEOUT = 5,      /* device error word: a bounded wait ran out */
+  DSV4_ERR_WORKSPACE = 6          /* workspace pointer missing or smaller than *_workspace_size */
+} dsv4_status;
+
+typedef enum { DSV4_F32 = 0, DSV4_BF16 = 1, DSV4_I32 = 2, DSV4_I64 = 3, DSV4_I8 = 4 } dsv4_dtype;
+
+/* ---- status ------------------------------------------------------------------------------ */
+DSV4_API const char* dsv4_last_error(void);
+DSV4_API int dsv4_abi_version(void);
+/* Reads (and clears) the device error word of the current device after synchronising `stream`.
+ * *code receives 0 or a dsv4_status raised by a kernel (index out of range, wait timeout). */
+DSV4_API int dsv4_device_error(int* code, void* stream);
+
+/* ---- a1: sparse attention --------------------------------------------------------------------
+ * o[i,h,:] = sum_t p[i,h,t] kv[idx[i,t],:] / (sum_t p[i,h,t] + exp(sink[h] - m[i,h]))
+ * with p = exp(scale * q[i,h,:].kv[idx[i,t],:] - m[i,h]), m the max over valid t, idx < 0 masked.
+ * A query whose indices are all masked yields NaN, as the reference does. */
+typedef struct {
+  const void* q;          /* [s, h, d], q_dtype (F32 or BF16) */
+  const void* kv;         /* [n, d] BF16 */
+  const float* sink;      /* [h] */
+  const void* idx;        /* [s, t], idx_dtype (I32 or I64); -1 = masked */
+  void* out;              /* [s, h, d], out_dtype (F32 or BF16) */
+  int64_t s;              /* queries */
+  int64_t n;              /* kv rows */
+  int32_t h;              /* heads, multiple of 16 */
+  int32_t d;              /* head dim, 512 */
+  int32_t t;              /* indices per query */
+  int32_t q_dtype, idx_dtype, out_dtype;
+  float scale;
+  /* optional fused inverse rope on the last rope_dim dims of the output (freqs == NULL: off) */
+  const float* rope_freqs;      /* [rope_dim/2] angular frequencies */
+  const int32_t* positions;     /* [s] rope position per query */
+  int32_t rope_dim;
+  int32_t num_splits;           /* 0 = automatic split of t across CTAs */
+  void* workspace;
+  size_t workspace_bytes;
+} dsv4_sparse_attn_params;
+
+DSV4_API size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p);
+DSV4_API int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream);
+
+/* ---- a2: window indices (int32 [bsz, seqlen, cols]); cols = window if start_pos > 0 else
+ * min(seqlen, window), exactly the three branches of the reference. */
+DSV4_API int dsv4_window_topk_idxs(int32_t window, int32_t bsz, int32_t seqlen, int32_t start_pos,
+                          int32_t* out, void* stream);
+
+/* ---- a5: RMSNorm / RoPE ---------------------------------------------------------------------- */
+typedef struct {
+  const void* x;          /* [rows, dim], x_dtype */
+  const void* weight;     /* [dim] w_dtype, or NULL for the weightless per-head norm */
+  void* out;              /* [rows, dim], out_dtype */
+  int64_t rows;
+  int32_t dim;
+  int32_t x_dtype, w_dtype, out_dtype;
+  float eps;
+} dsv4_rmsnorm_params;
+DSV4_API int dsv4_rmsnorm(const dsv4_rmsnorm_params* p, void* stream);
+
+typedef struct {
+  const void* x;          /* [s, heads, dim] rows (x_stride elements apart), rope on the LAST rope_dim */
+  void* out;              /* same shape, out_dtype, out_stride */
+  int64_t s;              /* positions (rows of the table) */
+  int32_t heads;          /* rows sharing one position */
+  int32_t dim;            /* full row length */
+  int32_t rope_dim;
+  int32_t x_dtype, out_dtype;
+  /* exactly one of the two angle sources: */
+  const float* cis;             /* [cis_rows, rope_dim/2, 2] (cos, sin) (a freqs_cis table);
+                                   position row r uses table row r % cis_rows */
+  int64_t cis_rows;
+  const float* freqs;           /* [rope_dim/2]; angle = float(pos) * freqs[i] */
+  const int32_t* positions;     /* [s] with freqs; NULL means pos = pos_offset + row */
+  int32_t pos_offset;
+  int32_t inverse;              /* conjugate rotation */
+} dsv4_rope_params;
+DSV4_API int dsv4_rope(const dsv4_rope_params* p, void* stream);
+
+/* fused RMSNorm (or weightless per-head norm) + RoPE on the last rope_dim dims + cast. */
+typedef struct {
+  const void* x;          /* [rows, heads, dim] */
+  const void* weight;     /* [dim] or NULL (per-head weightless norm) */
+  void* out;              /* [rows, heads, dim] out_dtype; or, with out_rows, scattered rows */
+  const int64_t* out_rows;/* optional [rows]: destination row index (in units of heads*dim) */
+  int64_t rows;
+  int32_t heads, dim, rope_dim;
+  int32_t x_dtype, w_dtype, out_dtype;
+  float eps;
+  const float* freqs;     /* [rope_dim/2] */
+  const int32_t* positions; /* [rows] */
+} dsv4_norm_rope_params;
+DSV4_API int dsv4_norm_rope(const dsv4_norm_rope_params* p, void* stream);
+
+/* YaRN frequency table (host, fp32), the reference's precompute_freqs; out has dim/2 floats. */
+DSV4_API int dsv4_yarn_freqs(int32_t dim, int64_t original_seq_len, double base, double factor,
+                    double beta_fast, double beta_slow, float* out_host);
+
+/* ---- a7: lightning indexer + top-k ---------------------------------------------------------------
+ * score[j] = sum_h w[h] * relu(q[h,:] . k[j,:]) in a fixed fp32 order (per head a sequential fmaf
+ * chain over the 128 dims; heads folded four at a time, sequentially, into 16 partials that are
+ * summed by a balanced binary tree). Selection: the top_k visible keys by (score desc, index asc),
+ * written in ascending key order, padded with -1. */
+typedef struct {
+  const float* q;         /* [batch, s, heads, 128] */
+  const float* w;         /* [batch, s, heads] */
+  const float* k;         /* [batch, n_keys, 128] (k_batch_stride rows apart) */
+  int32_t* out;           /* [batch, s, out_stride]; top_k columns written from out_col */
+  float* scores_out;      /* optional [batch, s, n_keys] raw scores (testing); NULL = off */
+  int32_t batch, s, heads, n_keys, top_k;
+  int64_t k_batch_stride; /* in rows */
+  /* visibility: query i of batch b sees keys j < min(n_keys, n_vis) with
+   * n_vis = (positions[b*s+i] + 1) / ratio if positions != NULL, else n_keys */
+  const int32_t* positions;
+  int32_t ratio;
+  /* output mapping: out[b, i, out_col + r] = map(key j) where map(j) = j + out_offset, or, with a
+   * block table, table[b*table_stride + j / page] * page + j % page + out_offset */
+  int32_t out_stride, out_col;
+  int64_t out_offset;
+  const int32_t* block_table;
+  int32_t table_stride, page;
+  void* workspace;
+  size_t workspace_bytes;
+} dsv4_indexer_params;
+
+DSV4_API size_t dsv4_indexer_topk_workspace_size(const dsv4_indexer_params* p);
+DSV4_API int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream);
+
+/* decode attention index list: out[b, 0:window] = window ring rows for position pos[b] in the
+ * reference's ring order (ref_torch/sparse_attn.py:11-15), mapped to pool rows
+ * win_base[b] + slot; masked slots are -1. Columns window.. are left to dsv4_indexer_topk. */
+DSV4_API int dsv4_decode_window_indices(int32_t batch, int32_t window, const int32_t* positions,
+                               const int64_t* win_base, int32_t* out, int32_t out_stride,
+                               void* stream);
+
+/* ---- a3/a4: KV compressor --------------------------------------------------------------------- */
+typedef struct {
+  const float* kv;        /* [b, s, 2*head_dim] projection x.wkv^T (fp32) */
+  const float* score;     /* [b, s, 2*head_dim] projection x.wgate^T (fp32), before ape */
+  const float* ape;       /* [ratio, 2*head_dim] */
+  const void* norm_w;     /* [head_dim], norm_dtype */
+  void* out;              /* [b, s/ratio, head_dim] out_dtype, or pool rows through out_rows */
+  const int64_t* out_rows;/* optional [b, s/ratio] destination row (of head_dim elements) */
+  int32_t b, s, head_dim, ratio, rope_dim;
+  int32_t norm_dtype, out_dtype;
+  float eps;
+  const float* freqs;     /* [rope_dim/2]; compressed row g is roped at position ratio*g + pos0 */
+  int32_t pos0;
+  /* optional decode hand-off state (ref_torch/compressor.py:67-74): ring [b, 2*ratio, 2*head_dim]
+   * for kv (0) and score+ape (-inf) seeded from the last full block and the remainder */
+  float* ring_kv;
+  float* ring_score;
+} dsv4_compressor_params;
+DSV4_API int dsv4_compressor_pool(const dsv4_compressor_params* p, void* stream);
+
+typedef struct {
+  const float* kv;        /* [b, 2*head_dim] this token's x.wkv^T */
+  const float* score;     /* [b, 2*head_dim] this token's x.wgate^T (before ape) */
+  const float* ape;       /* [ratio, 2*head_dim] */
+  const void* norm_w;     /* [head_dim] */
+  float* ring_kv;         /* [b, 2*ratio, 2*head_dim] */
+  float* ring_score;      /* [b, 2*ratio, 2*head_dim] */
+  const int32_t* positions; /* [b] decode position p of this token */
+  void* out;              /* pool base [*, head_dim] out_dtype */
+  const int64_t* out_rows;/* [b] pool row where the emitted row goes (written only when (p+1)%ratio==0) */
+  int32_t b, head_dim, ratio, rope_dim;
+  int32_t norm_dtype, out_dtype;
+  float eps;
+  const float* freqs;
+} dsv4_compressor_decode_params;
+DSV4_API int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream);
+
+/* ---- a6: projections. y[m, n] = sum_k x[m, k] * W[n, k] (W row-major [n, k] as the reference)
+ * W is BF16, or I8 with BF16 scales per (row, group of `group` k). x BF16 or F32, y F32 or BF16.
+ * `groups` > 1 runs a grouped projection: x viewed as [m, groups, k], W as [groups, n, k], y as
+ * [m, groups, n] (the o_grouped first stage, v4mlx/mla.py:42-56). */
+typedef struct {
+  const void* x;
+  const void* w;
+  const void* w_scale;    /* [groups*n, k/group] BF16 when w_dtype == I8 */
+  void* y;
+  int64_t m;
+  int32_t n, k, groups, group;
+  int32_t x_dtype, w_dtype, y_dtype;
+} dsv4_linear_params;
+DSV4_API int dsv4_linear(const dsv4_linear_params* p, void* stream);
+
+/* ---- casts used by the op layer (fp32 <-> bf16) ---- */
+DSV4_API int dsv4_cast(const void* x, int32_t x_dtype, void* y, int32_t y_dtype, int64_t numel, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSV4_H_ */

@@ -1,0 +1,69 @@
+"""The decode attention path (configs 2 and 3, reduced context) against the CPU oracle."""
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close_bf16
+from oracle import layer_ref as LR
+from oracle import norm_rope_ref as NR
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg():
+    return importlib.import_module("deepseek-v4-flash-mlx_b200.configs")
+
+
+@pytest.mark.parametrize("batch,ctx,top_k", [(1, 32768, 512), (4, 8192, 512), (3, 1000, 512), (2, 60, 16),
+                                             (2, 2048, 64)])
+def test_decode_attention_matches_oracle(dsv4, batch, ctx, top_k):
+    C = _cfg()
+    case = C.make_decode_case(batch, ctx, top_k, seeds=[100 + i for i in range(batch)])
+    if ctx < 128:  # young sequences: only positions 0..ctx-1 of the window ring are valid
+        pass
+    out = dsv4.decode_attention(case.cache, case.q, case.q_idx, case.w_idx, case.sink, case.positions, top_k,
+                                out_dtype=torch.float32)
+    pool, win_base, comp_rows = C.decode_case_host_pool(case)
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    h = case.host
+    ref = LR.decode_attention_ref(pool, win_base, comp_rows, h["k_idx"], h["q"], h["q_idx"], h["w_idx"], h["sink"],
+                                  h["positions"], top_k, f)
+    assert_close_bf16(out, ref, what=f"decode b={batch} ctx={ctx}")
+
+
+def test_decode_indices_bit_exact(dsv4):
+    """The attention index list (window ring order + indexer selection through the block table)."""
+    C = _cfg()
+    case = C.make_decode_case(2, 8192, 512, seeds=[100, 101])
+    b = 2
+    idx = torch.empty((b, 128 + 512), dtype=torch.int32, device="cuda")
+    L = importlib.import_module("deepseek-v4-flash-mlx_b200._lib")
+    pos = case.positions
+    L.check(L.lib().dsv4_decode_window_indices(b, 128, L.ptr(pos), L.ptr(case.cache.win_base), L.ptr(idx), 640,
+                                               L.stream_of(idx)))
+    dsv4.indexer_topk_into(idx.view(b, 1, -1), case.q_idx.view(b, 1, 64, 128), case.w_idx.view(b, 1, 64),
+                           case.cache.k_idx, 512, pos.view(b, 1), 4, out_col=128, out_offset=case.cache.comp_base,
+                           block_table=case.cache.block_table, page=case.cache.page)
+    pool, win_base, comp_rows = C.decode_case_host_pool(case)
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    h = case.host
+    _, ref_idx = LR.decode_attention_ref(pool, win_base, comp_rows, h["k_idx"], h["q"], h["q_idx"], h["w_idx"],
+                                         h["sink"], h["positions"], 512, f, return_indices=True)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx.numpy())
+
+
+def test_decode_runner_graph_and_host_path(dsv4):
+    C = _cfg()
+    case = C.make_decode_case(1, 4096, 512, seeds=[1])
+    r = dsv4.DecodeRunner(case.cache, case.sink, 512, out_dtype=torch.float32)
+    r.q.copy_(case.q), r.q_idx.copy_(case.q_idx), r.w_idx.copy_(case.w_idx), r.positions.copy_(case.positions)
+    dev_out = r.step_device().clone()
+    ref = dsv4.decode_attention(case.cache, case.q, case.q_idx, case.w_idx, case.sink, case.positions, 512,
+                                out_dtype=torch.float32)
+    torch.testing.assert_close(dev_out, ref, rtol=0, atol=0)
+    h = case.host
+    out = r.step_host(h["q"], h["q_idx"], h["w_idx"], h["positions"])
+    r.synchronize()
+    torch.testing.assert_close(out, ref.cpu(), rtol=0, atol=0)

@@ -1,0 +1,259 @@
+"""Each dsv4 op on the GPU against the CPU oracle (same seeded inputs)."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close_bf16, rel_rms
+from oracle import compressor_ref as C
+from oracle import indexer_ref as I
+from oracle import mla_ref as M
+from oracle import norm_rope_ref as NR
+from oracle import sparse_attn_ref as SA
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _bf16(x):
+    return x.to(torch.bfloat16).float()
+
+
+# ---------------------------------------------------------------- sparse attention
+def test_sparse_attn_golden_inputs(dsv4, golden):
+    q, kv, sink, idx = (torch.from_numpy(golden[k]) for k in ("sa_q", "sa_kv", "sa_sink", "sa_idx"))
+    kvb = _bf16(kv)
+    ref = SA.sparse_attn(q, kvb, sink, idx, float(golden["sa_scale"]))
+    out = dsv4.sparse_attn(q.to(DEV), kvb.to(DEV), sink.to(DEV), idx.to(DEV), float(golden["sa_scale"]))
+    assert out.dtype == torch.float32
+    assert torch.isnan(out[5]).all()                     # all-masked query -> NaN like the reference
+    assert_close_bf16(out, ref, what="golden")
+
+
+@pytest.mark.parametrize("s,t,n,h,idx_dtype,splits", [
+    (1, 640, 8320, 64, torch.int32, 0),      # C2-like decode (split-K + combine)
+    (3, 640, 2176, 64, torch.int64, 0),
+    (1, 100, 500, 64, torch.int32, 1),        # t not a multiple of 64, single split
+    (1, 1152, 4000, 64, torch.int32, 5),      # explicit splits
+    (40, 256, 700, 64, torch.int32, 0),       # prefill-like, one CTA per query
+    (2, 200, 300, 128, torch.int32, 0),       # two head blocks
+    (2, 64, 300, 32, torch.int32, 0),         # fewer heads than a block
+])
+def test_sparse_attn_shapes(dsv4, s, t, n, h, idx_dtype, splits):
+    g = torch.Generator().manual_seed(s * 1000 + t)
+    q = torch.randn(s, h, 512, generator=g)
+    kv = _bf16(torch.randn(n, 512, generator=g))
+    sink = torch.randn(h, generator=g)
+    idx = torch.randint(0, n, (s, t), generator=g)
+    idx[:, ::7] = -1
+    ref = SA.sparse_attn(q, kv, sink, idx, 512 ** -0.5)
+    L = __import__("importlib").import_module("deepseek-v4-flash-mlx_b200.sparse_attn")
+    out = L._sparse_attn_op(q.to(DEV), kv.to(DEV).bfloat16(), sink.to(DEV), idx.to(DEV, idx_dtype), 512 ** -0.5,
+                            torch.float32, None, None, 0, splits)
+    assert_close_bf16(out, ref, what=f"s={s} t={t}")
+
+
+def test_sparse_attn_known_answers(dsv4):
+    """One-hot rows, sink-only mass, duplicate indices."""
+    h, n = 64, 128
+    kv = torch.zeros(n, 512)
+    kv[torch.arange(n), torch.arange(n)] = 1.0
+    q = torch.zeros(1, h, 512)
+    sink = torch.full((h,), -1e4)
+    idx = torch.tensor([[5, 9, -1, 9]])
+    out = dsv4.sparse_attn(q.to(DEV), kv.to(DEV), sink.to(DEV), idx.to(DEV), 1.0).cpu()
+    # equal logits (0): weights 1/3 each over rows 5, 9, 9
+    assert torch.allclose(out[0, :, 5], torch.full((h,), 1 / 3), atol=1e-3)
+    assert torch.allclose(out[0, :, 9], torch.full((h,), 2 / 3), atol=1e-3)
+    sink2 = torch.full((h,), 30.0)                         # sink dominates the denominator
+    out2 = dsv4.sparse_attn(q.to(DEV), kv.to(DEV), sink2.to(DEV), idx.to(DEV), 1.0).cpu()
+    assert out2.abs().max() < 1e-9
+
+
+def test_sparse_attn_inverse_rope_fused(dsv4):
+    g = torch.Generator().manual_seed(5)
+    s, t, n = 4, 300, 1000
+    q = torch.randn(s, 64, 512, generator=g)
+    kv = _bf16(torch.randn(n, 512, generator=g))
+    sink = torch.randn(64, generator=g)
+    idx = torch.randint(0, n, (s, t), generator=g)
+    pos = torch.tensor([0, 7, 4095, 32767], dtype=torch.int32)
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    ref = NR.rope_at(SA.sparse_attn(q, kv, sink, idx, 512 ** -0.5), pos, f, 64, inverse=True)
+    for splits in (0, 1):
+        L = __import__("importlib").import_module("deepseek-v4-flash-mlx_b200.sparse_attn")
+        out = L._sparse_attn_op(q.to(DEV), kv.to(DEV).bfloat16(), sink.to(DEV), idx.to(DEV), 512 ** -0.5,
+                                torch.float32, f.to(DEV), pos.to(DEV), 64, splits)
+        assert_close_bf16(out, ref, what=f"rope splits={splits}")
+
+
+def test_sparse_attn_out_of_range_index_flags_device_error(dsv4):
+    L = __import__("importlib").import_module("deepseek-v4-flash-mlx_b200._lib")
+    L.device_error()  # clear
+    q = torch.randn(1, 64, 512, device=DEV)
+    kv = torch.randn(10, 512, device=DEV).bfloat16()
+    idx = torch.tensor([[1, 2, 10_000]], device=DEV)       # 10000 >= n: treated as masked and flagged
+    out = dsv4.sparse_attn(q, kv, torch.zeros(64, device=DEV), idx, 0.05)
+    assert torch.isfinite(out).all()
+    assert L.device_error() == 4
+    assert L.device_error() == 0
+
+
+def test_window_indices_gpu(dsv4, golden):
+    i = 0
+    while f"win_{i}_args" in golden:
+        w, b, s, sp = (int(v) for v in golden[f"win_{i}_args"])
+        got = dsv4.get_window_topk_idxs(w, b, s, sp).cpu().numpy()
+        ref = golden[f"win_{i}_out"]
+        ref = np.broadcast_to(ref, got.shape) if ref.shape[1] == 1 else ref
+        np.testing.assert_array_equal(got, ref, err_msg=str((w, b, s, sp)))
+        i += 1
+
+
+# ---------------------------------------------------------------- norm / rope
+def test_rmsnorm_and_perhead(dsv4):
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(37, 1024, generator=g) * 3
+    w = torch.randn(1024, generator=g)
+    assert rel_rms(dsv4.rmsnorm(x.to(DEV), w.to(DEV)), NR.rmsnorm(x, w)) < 1e-6
+    xb = x.bfloat16()
+    out = dsv4.rmsnorm(xb.to(DEV), w.to(DEV))
+    assert out.dtype == torch.bfloat16
+    assert rel_rms(out, NR.rmsnorm(xb, w)) < 8e-3
+    q = torch.randn(5, 64, 512, generator=g)
+    assert rel_rms(dsv4.perhead_norm(q.to(DEV)), NR.perhead_norm(q)) < 1e-6
+
+
+def test_apply_rotary_emb_table_form(dsv4, golden):
+    cis = NR.precompute_freqs_cis(64, 16, 65536, 160000.0, 16, 32, 1)
+    x3, x4 = torch.from_numpy(golden["rope_x3"]), torch.from_numpy(golden["rope_x4"])
+    np.testing.assert_allclose(dsv4.apply_rotary_emb(x3.to(DEV), cis).cpu().numpy(), golden["rope_x3_fwd"], atol=2e-6)
+    np.testing.assert_allclose(dsv4.apply_rotary_emb(x3.to(DEV), cis, inverse=True).cpu().numpy(),
+                               golden["rope_x3_inv"], atol=2e-6)
+    np.testing.assert_allclose(dsv4.apply_rotary_emb(x4.to(DEV), cis).cpu().numpy(), golden["rope_x4_fwd"], atol=2e-6)
+    xb = torch.randn(3, 16, 64)
+    ref = NR.apply_rotary_emb(xb, cis)
+    assert rel_rms(dsv4.apply_rotary_emb(xb.to(DEV), cis), ref) < 1e-6
+
+
+def test_norm_rope_fused(dsv4):
+    g = torch.Generator().manual_seed(2)
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    pos = torch.tensor([0, 1, 5000, 32767, 65535], dtype=torch.int32)
+    q = torch.randn(5, 64, 512, generator=g) * 0.7
+    ref = NR.rope_at(NR.perhead_norm(q), pos, f)
+    out = dsv4.norm_rope(q.to(DEV), pos.to(DEV), f.to(DEV), weight=None, out_dtype=torch.float32)
+    assert rel_rms(out, ref) < 2e-6
+    kv = torch.randn(5, 512, generator=g)
+    w = torch.rand(512, generator=g) + 0.5
+    ref2 = NR.rope_at(NR.rmsnorm(kv, w), pos, f)
+    out2 = dsv4.norm_rope(kv.to(DEV), pos.to(DEV), f.to(DEV), weight=w.to(DEV))
+    assert out2.dtype == torch.bfloat16
+    assert_close_bf16(out2, ref2, what="kv norm_rope")
+
+
+# ---------------------------------------------------------------- indexer
+def _idx_inputs(b, s, n, seed):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(b, s, 64, 128, generator=g)
+    w = torch.randn(b, s, 64, generator=g) / 8
+    k = torch.randn(b, n, 128, generator=g)
+    return q, w, k
+
+
+def test_indexer_scores_bit_exact(dsv4):
+    q, w, k = _idx_inputs(1, 3, 1000, 7)
+    got = dsv4.indexer_scores(q.to(DEV), w.to(DEV), k.to(DEV)).cpu().numpy()
+    for i in range(3):
+        ref = I.scores(q[0, i].numpy(), w[0, i].numpy(), k[0].numpy())
+        np.testing.assert_array_equal(got[0, i].view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("b,s,n,k,causal", [(1, 1, 8192, 512, False), (4, 1, 2048, 512, False),
+                                            (1, 40, 700, 64, True), (2, 3, 300, 512, False)])
+def test_indexer_topk_bit_exact(dsv4, b, s, n, k, causal):
+    q, w, keys = _idx_inputs(b, s, n, b * 100 + s)
+    pos = None
+    if causal:
+        pos = torch.arange(n * 4 - s * 37, n * 4, 37)[:s].repeat(b, 1).to(torch.int32)
+    got = dsv4.indexer_topk(q.to(DEV), w.to(DEV), keys.to(DEV), k, None if pos is None else pos.to(DEV)).cpu().numpy()
+    ref = I.indexer_topk(q.numpy(), w.numpy(), keys.numpy(), k, None if pos is None else pos.numpy())
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_indexer_ties_and_padding(dsv4):
+    """Duplicate keys give exactly equal scores: the lower index must win the boundary."""
+    q, w, keys = _idx_inputs(1, 1, 300, 9)
+    keys[0, 200:] = keys[0, 100:200]                      # rows 200..299 duplicate rows 100..199
+    got = dsv4.indexer_topk(q.to(DEV), w.to(DEV), keys.to(DEV), 77).cpu().numpy()
+    ref = I.indexer_topk(q.numpy(), w.numpy(), keys.numpy(), 77)
+    np.testing.assert_array_equal(got, ref)
+    pos = torch.tensor([[39]], dtype=torch.int32)           # 10 visible keys, k = 16
+    got2 = dsv4.indexer_topk(q.to(DEV), w.to(DEV), keys.to(DEV), 16, pos.to(DEV)).cpu().numpy()
+    np.testing.assert_array_equal(got2[0, 0], list(range(10)) + [-1] * 6)
+
+
+# ---------------------------------------------------------------- projections
+def test_linear_bf16_and_grouped(dsv4):
+    g = torch.Generator().manual_seed(3)
+    x = _bf16(torch.randn(70, 256, generator=g))
+    W = _bf16(torch.randn(192, 256, generator=g) * 0.05)
+    ref = M.linear(x, W)
+    out = dsv4.linear(x.to(DEV).bfloat16(), W.to(DEV).bfloat16())
+    assert rel_rms(out, ref) < 1e-5
+    o = _bf16(torch.randn(3, 8 * 128, generator=g))
+    wa = _bf16(torch.randn(8 * 64, 128, generator=g) * 0.1)
+    wb = _bf16(torch.randn(96, 8 * 64, generator=g) * 0.1)
+    ref2 = M.o_grouped(o, wa, wb, groups=8)
+    out2 = dsv4.o_grouped(o.to(DEV), wa.to(DEV).bfloat16(), wb.to(DEV).bfloat16())
+    assert rel_rms(out2, ref2) < 5e-3
+
+
+def test_linear_int8_g64(dsv4):
+    g = torch.Generator().manual_seed(4)
+    x = _bf16(torch.randn(32, 512, generator=g))
+    qw = dsv4.quantize_int8_g64(torch.randn(384, 512, generator=g) * 0.02)
+    ref = M.linear(x, M.dequant_int8_g64(qw.q, qw.scale))
+    qd = type(qw)(qw.q.to(DEV), qw.scale.to(DEV))
+    out = dsv4.linear(x.to(DEV).bfloat16(), qd)
+    assert rel_rms(out, ref) < 1e-5
+
+
+# ---------------------------------------------------------------- compressor
+def test_compressor_prefill_golden_inputs(dsv4, golden):
+    wkv, wgate, ape, nw = (torch.from_numpy(golden[k]) for k in ("cmp_wkv", "cmp_wgate", "cmp_ape", "cmp_nw"))
+    for s in (18, 16):
+        x = torch.from_numpy(golden[f"cmp{s}_x"])
+        # the GPU consumes bf16 operands: compare with the oracle on the same rounded operands
+        ref, st = C.compressor_prefill(_bf16(x), _bf16(wkv), _bf16(wgate), ape, nw)
+        out, gst = dsv4.compressor_prefill(x.to(DEV), wkv.to(DEV).bfloat16(), wgate.to(DEV).bfloat16(),
+                                           ape.to(DEV), nw.to(DEV))
+        assert_close_bf16(out, ref, 2e-3, 1e-4, what=f"cmp{s}")
+        assert_close_bf16(gst["kv"], st["kv"], 1e-4, 1e-5, what="state kv")
+        assert_close_bf16(gst["score"], st["score"], 1e-4, 1e-5, what="state score")
+        # and against the reference itself (fp32 operands): bf16 operand rounding only
+        assert_close_bf16(out, torch.from_numpy(golden[f"cmp{s}_rows"]), what=f"cmp{s} vs ref")
+
+
+def test_compressor_decode_ring(dsv4):
+    g = torch.Generator().manual_seed(8)
+    dim, s0 = 128, 13
+    wkv = _bf16(torch.randn(1024, dim, generator=g) * 0.05)
+    wgate = _bf16(torch.randn(1024, dim, generator=g) * 0.05)
+    ape = torch.randn(4, 1024, generator=g) * 0.1
+    nw = torch.rand(512, generator=g) + 0.5
+    x = _bf16(torch.randn(1, s0 + 7, dim, generator=g))
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    kvp, scp = x @ wkv.T, x @ wgate.T
+    rk, rs = C.ring_from_prefill(kvp[:, :s0], scp[:, :s0], ape, s0)
+    _, st = dsv4.compressor_prefill(x[:, :s0].to(DEV), wkv.to(DEV).bfloat16(), wgate.to(DEV).bfloat16(), ape.to(DEV),
+                                    nw.to(DEV))
+    assert_close_bf16(st["ring_kv"], rk, 1e-4, 1e-5, what="ring kv")
+    pool = torch.zeros(8, 512, device=DEV)
+    for p in range(s0, s0 + 7):
+        row = C.decode_ring_step(rk[0], rs[0], kvp[0, p], scp[0, p], ape, nw, p, f)
+        dsv4.compressor_decode_step(x[:, p].to(DEV), wkv.to(DEV).bfloat16(), wgate.to(DEV).bfloat16(), ape.to(DEV),
+                                    nw.to(DEV), st["ring_kv"], st["ring_score"],
+                                    torch.tensor([p], dtype=torch.int32, device=DEV), pool,
+                                    torch.tensor([p // 4], device=DEV), freqs=f.to(DEV))
+        if row is not None:
+            assert_close_bf16(pool[p // 4], row, 2e-3, 1e-4, what=f"emit p={p}")

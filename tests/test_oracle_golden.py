@@ -1,0 +1,70 @@
+"""The CPU oracle against the reference's own ref_torch outputs (tests/golden/make_golden.py)."""
+import numpy as np
+import torch
+
+from oracle import compressor_ref as C
+from oracle import norm_rope_ref as NR
+from oracle import sparse_attn_ref as SA
+
+
+def test_window_indices_all_branches(golden):
+    i = 0
+    while f"win_{i}_args" in golden:
+        w, b, s, sp = (int(v) for v in golden[f"win_{i}_args"])
+        got = SA.get_window_topk_idxs(w, b, s, sp).numpy()
+        np.testing.assert_array_equal(got, golden[f"win_{i}_out"], err_msg=f"case {(w, b, s, sp)}")
+        i += 1
+    assert i >= 9
+
+
+def test_sparse_attn_matches_reference(golden):
+    q, kv, sink, idx = (torch.from_numpy(golden[k]) for k in ("sa_q", "sa_kv", "sa_sink", "sa_idx"))
+    out = SA.sparse_attn(q, kv, sink, idx, float(golden["sa_scale"])).numpy()
+    ref = golden["sa_out"]
+    assert np.isnan(ref[5]).all() and np.isnan(out[5]).all()  # all-masked query -> NaN in both
+    np.testing.assert_allclose(out[:5], ref[:5], rtol=1e-4, atol=1e-5)
+
+
+def test_norm_rope_matches_reference(golden):
+    np.testing.assert_allclose(NR.rmsnorm(torch.from_numpy(golden["rms_x"]), torch.from_numpy(golden["rms_w"])).numpy(),
+                               golden["rms_out"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_array_equal(NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1).numpy(), golden["freqs_yarn"])
+    np.testing.assert_array_equal(NR.precompute_freqs(64, 0, 0, 10000.0, 40, 32, 1).numpy(), golden["freqs_plain"])
+    cis = NR.precompute_freqs_cis(64, 16, 65536, 160000.0, 16, 32, 1)
+    np.testing.assert_array_equal(torch.view_as_real(cis).numpy(), golden["cis_real"])
+    x3, x4 = torch.from_numpy(golden["rope_x3"]), torch.from_numpy(golden["rope_x4"])
+    np.testing.assert_allclose(NR.apply_rotary_emb(x3, cis).numpy(), golden["rope_x3_fwd"], atol=1e-6)
+    np.testing.assert_allclose(NR.apply_rotary_emb(x3, cis, True).numpy(), golden["rope_x3_inv"], atol=1e-6)
+    np.testing.assert_allclose(NR.apply_rotary_emb(x4, cis).numpy(), golden["rope_x4_fwd"], atol=1e-6)
+    # the per-position form used by the pipelines equals the table form
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    np.testing.assert_allclose(NR.rope_at(x3[0], torch.arange(16), f).numpy(), golden["rope_x3_fwd"][0], atol=1e-6)
+
+
+def test_compressor_matches_reference(golden):
+    wkv, wgate, ape, nw = (torch.from_numpy(golden[k]) for k in ("cmp_wkv", "cmp_wgate", "cmp_ape", "cmp_nw"))
+    for s in (18, 16):
+        x = torch.from_numpy(golden[f"cmp{s}_x"])
+        rows, st = C.compressor_prefill(x, wkv, wgate, ape, nw)
+        np.testing.assert_allclose(rows.numpy(), golden[f"cmp{s}_rows"], rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(st["kv"].numpy(), golden[f"cmp{s}_state_kv"], rtol=1e-6, atol=1e-6)
+        np.testing.assert_allclose(st["score"].numpy(), golden[f"cmp{s}_state_score"], rtol=1e-6, atol=1e-6)
+        if f"cmp{s}_state_kv_rem" in golden:
+            np.testing.assert_allclose(st["kv_rem"].numpy(), golden[f"cmp{s}_state_kv_rem"], rtol=1e-6, atol=1e-6)
+
+
+def test_decode_ring_continues_prefill(golden):
+    """Stepping the decode ring over tokens 16..19 emits the row prefill would produce for them."""
+    wkv, wgate, ape, nw = (torch.from_numpy(golden[k]) for k in ("cmp_wkv", "cmp_wgate", "cmp_ape", "cmp_nw"))
+    x = torch.from_numpy(golden["cmp18_x"])[:1]
+    torch.manual_seed(0)
+    x20 = torch.cat([x, torch.randn(1, 2, x.shape[-1])], 1)   # 20 tokens
+    full, _ = C.compressor_prefill(x20, wkv, wgate, ape, nw)  # 5 rows
+    kvp, scp = x20.float() @ wkv.T, x20.float() @ wgate.T
+    rk, rs = C.ring_from_prefill(kvp[:, :16], scp[:, :16], ape, 16)
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    row = None
+    for p in range(16, 20):
+        row = C.decode_ring_step(rk[0], rs[0], kvp[0, p], scp[0, p], ape, nw, p, f)
+        assert (row is None) == (p != 19)
+    np.testing.assert_allclose(row.numpy(), full[0, 4].numpy(), rtol=1e-4, atol=1e-5)
