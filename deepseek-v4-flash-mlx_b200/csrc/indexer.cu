@@ -168,6 +168,7 @@ struct SelectParams {
 
 constexpr int SEL_THREADS = 1024;
 constexpr int SEL_MAX_KEYS = 32768;
+static_assert(SEL_THREADS * 4 == 4096, "one thread per 4 histogram bins");
 
 __device__ __forceinline__ int32_t map_key(const SelectParams& P, int b, int j) {
   int64_t row;
@@ -181,14 +182,54 @@ __device__ __forceinline__ int32_t map_key(const SelectParams& P, int b, int j) 
   return static_cast<int32_t>(row + P.out_offset);
 }
 
-// One CTA per query: radix select (4 passes of 8 bits) of the k-th largest ordered score, then
-// an index-ordered compaction that keeps keys above it and the lowest-index keys equal to it.
+// One CTA per query. Pass 1: a 4096-bin histogram of the top 12 bits of every visible key's
+// ordered score finds the boundary bin (keys above it are in, keys below are out). Pass 2 resolves
+// the boundary bin's candidates exactly — by rank counting over (ordered score desc, index asc)
+// when they are few, otherwise by further radix passes over the candidates only. Pass 3 writes the
+// chosen keys in ascending index order through a block prefix sum.
+constexpr int SEL_BINS = 4096;
+constexpr int SEL_RANK_MAX = 1024;   // candidates resolved by O(c^2) rank counting up to this many
+
+struct SelShared {
+  uint32_t hist[SEL_BINS];
+  uint32_t warp_sum[SEL_THREADS / 32];
+  uint32_t cand_key[SEL_RANK_MAX];
+  int32_t cand_idx[SEL_RANK_MAX];
+  uint32_t n_cand, n_above, need, bin, tau, tau_need;
+};
+
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_sum, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) warp_sum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < (SEL_THREADS / 32) ? warp_sum[lane] : 0u;
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      uint32_t t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    if (lane < (SEL_THREADS / 32)) warp_sum[lane] = wi - w;
+    if (lane == (SEL_THREADS / 32) - 1) *total = wi;
+  }
+  __syncthreads();
+  const uint32_t r = warp_sum[warp] + incl - v;
+  __syncthreads();
+  return r;
+}
+
 __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
   extern __shared__ uint32_t keys[];  // [nvis] ordered scores
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t s_prefix, s_kleft;
-  __shared__ uint32_t warp_cnt[2][SEL_THREADS / 32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ SelShared sh;
+  __shared__ uint32_t s_total;
+  const int tid = threadIdx.x;
   const int64_t qrow = blockIdx.x;
   const int b = static_cast<int>(qrow / P.s);
   const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
@@ -199,118 +240,132 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
     for (int r = tid; r < k; r += SEL_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
     return;
   }
-  for (int j = tid; j < nvis; j += SEL_THREADS) keys[j] = ordered_bits(P.scores[qrow * P.n_pad + j]);
-  if (tid == 0) {
-    s_prefix = 0;
-    s_kleft = k;
+  for (int i = tid; i < SEL_BINS; i += SEL_THREADS) sh.hist[i] = 0;
+  if (tid == 0) sh.n_cand = 0;
+  __syncthreads();
+  const float* sc = P.scores + qrow * P.n_pad;
+  for (int j = tid; j < nvis; j += SEL_THREADS) {
+    const uint32_t key = ordered_bits(sc[j]);
+    keys[j] = key;
+    atomicAdd(&sh.hist[key >> 20], 1u);
   }
   __syncthreads();
-  // MSB-first radix select of the k-th largest key
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += SEL_THREADS) hist[i] = 0;
-    __syncthreads();
-    const uint32_t prefix = s_prefix;
-    const uint32_t mask_hi = (shift == 24) ? 0u : (0xffffffffu << (shift + 8));
+  // boundary bin: suffix counts over bins in descending order; thread t owns bins
+  // [4095 - 4t - 3, 4095 - 4t] (SEL_THREADS * 4 == SEL_BINS)
+  {
+    uint32_t c[4], tot = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      c[e] = sh.hist[SEL_BINS - 1 - (tid * 4 + e)];
+      tot += c[e];
+    }
+    const uint32_t before = block_exclusive_scan(tot, sh.warp_sum, &s_total);
+    if (before < static_cast<uint32_t>(k) && static_cast<uint32_t>(k) <= before + tot) {
+      uint32_t run = before;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (run + c[e] >= static_cast<uint32_t>(k)) {
+          sh.bin = SEL_BINS - 1 - (tid * 4 + e);
+          sh.n_above = run;
+          sh.need = k - run;
+          break;
+        }
+        run += c[e];
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t bin = sh.bin;
+  const uint32_t need = sh.need;
+  const uint32_t n_bin = sh.hist[bin];
+  // resolve the boundary bin: find tau (the need-th largest key inside the bin) and how many of the
+  // keys equal to tau are taken (lowest indices first)
+  if (n_bin <= SEL_RANK_MAX) {
     for (int j = tid; j < nvis; j += SEL_THREADS) {
-      uint32_t key = keys[j];
-      if ((key & mask_hi) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1u);
+      const uint32_t key = keys[j];
+      if ((key >> 20) == bin) {
+        const uint32_t slot = atomicAdd(&sh.n_cand, 1u);
+        sh.cand_key[slot] = key;
+        sh.cand_idx[slot] = j;
+      }
     }
     __syncthreads();
-    if (warp == 0) {
-      // walk the 256 bins from the top: each lane owns 8 consecutive bins (descending)
-      uint32_t kleft = s_kleft;
-      uint32_t c[8], tot = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        c[e] = hist[255 - (lane * 8 + e)];
-        tot += c[e];
+    const uint32_t c = sh.n_cand;
+    for (uint32_t i = tid; i < c; i += SEL_THREADS) {
+      const uint32_t ki = sh.cand_key[i];
+      const int32_t ii = sh.cand_idx[i];
+      uint32_t rank = 0;
+      for (uint32_t m = 0; m < c; ++m) {
+        const uint32_t km = sh.cand_key[m];
+        rank += (km > ki) || (km == ki && sh.cand_idx[m] < ii);
       }
-      // exclusive prefix of totals across lanes (in descending-bin order)
-      uint32_t incl = tot;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
+      if (rank == need - 1) {  // the last key taken: defines the cut
+        sh.tau = ki;
+        sh.tau_need = ii;       // keys equal to tau are taken while their index <= this one
       }
-      uint32_t excl = incl - tot;
-      // the lane whose range contains the kleft-th key finds the bin
-      if (excl < kleft && kleft <= incl) {
-        uint32_t run = excl;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          if (run + c[e] >= kleft) {
-            int bin = 255 - (lane * 8 + e);
-            s_prefix = prefix | (static_cast<uint32_t>(bin) << shift);
-            s_kleft = kleft - run;
+    }
+  } else {
+    // many keys share the boundary bin (e.g. heavy ties): radix passes over that bin only, on
+    // bits 19..12, 11..4 and 3..0, then the kleft lowest indices among keys equal to the result
+    uint32_t prefix = bin << 20, kleft = need;
+    const int shifts[3] = {12, 4, 0}, widths[3] = {8, 8, 4};
+    for (int ps = 0; ps < 3; ++ps) {
+      const int shift = shifts[ps], width = widths[ps], hi = shift + width;
+      const uint32_t mask = (1u << width) - 1u;
+      for (int i = tid; i < 256; i += SEL_THREADS) sh.hist[i] = 0;
+      __syncthreads();
+      for (int j = tid; j < nvis; j += SEL_THREADS) {
+        const uint32_t key = keys[j];
+        if ((key >> hi) == (prefix >> hi)) atomicAdd(&sh.hist[(key >> shift) & mask], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t run = 0;
+        for (int d = static_cast<int>(mask); d >= 0; --d) {
+          if (run + sh.hist[d] >= kleft) {
+            sh.bin = d;
+            sh.need = kleft - run;
             break;
           }
-          run += c[e];
+          run += sh.hist[d];
         }
       }
+      __syncthreads();
+      prefix |= sh.bin << shift;
+      kleft = sh.need;
+      __syncthreads();
     }
-    __syncthreads();
+    // the kleft-th key (in index order) equal to prefix is the last one taken
+    const int per = (nvis + SEL_THREADS - 1) / SEL_THREADS;
+    const int jb = tid * per, je = min(nvis, jb + per);
+    uint32_t ne = 0;
+    for (int j = jb; j < je; ++j) ne += keys[j] == prefix;
+    const uint32_t before = block_exclusive_scan(ne, sh.warp_sum, &s_total);
+    if (before < kleft && kleft <= before + ne) {
+      uint32_t seen = before;
+      for (int j = jb; j < je; ++j)
+        if (keys[j] == prefix && ++seen == kleft) {
+          sh.tau_need = j;
+          break;
+        }
+    }
+    if (tid == 0) sh.tau = prefix;
   }
-  const uint32_t tau = s_prefix;      // k-th largest ordered key
-  const uint32_t need_eq = s_kleft;   // how many keys equal to tau are taken (lowest index first)
-
-  // index-ordered compaction: each thread scans a contiguous chunk
+  __syncthreads();
+  const uint32_t tau = sh.tau;
+  const int32_t tau_last = sh.tau_need;
+  // index-ordered compaction of {key > tau} U {key == tau and index <= tau_last}
   const int per = (nvis + SEL_THREADS - 1) / SEL_THREADS;
   const int jb = tid * per, je = min(nvis, jb + per);
-  uint32_t n_gt = 0, n_eq = 0;
+  uint32_t cnt = 0;
   for (int j = jb; j < je; ++j) {
-    uint32_t key = keys[j];
-    n_gt += key > tau;
-    n_eq += key == tau;
+    const uint32_t key = keys[j];
+    cnt += (key > tau) || (key == tau && j <= tau_last);
   }
-  // block exclusive scans of n_gt and n_eq
-  uint32_t ig = n_gt, ie = n_eq;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    uint32_t vg = __shfl_up_sync(0xffffffffu, ig, o);
-    uint32_t ve = __shfl_up_sync(0xffffffffu, ie, o);
-    if (lane >= o) {
-      ig += vg;
-      ie += ve;
-    }
-  }
-  if (lane == 31) {
-    warp_cnt[0][warp] = ig;
-    warp_cnt[1][warp] = ie;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    uint32_t vg = warp_cnt[0][lane], ve = warp_cnt[1][lane];
-    uint32_t sg = vg, se = ve;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      uint32_t tg = __shfl_up_sync(0xffffffffu, sg, o);
-      uint32_t te = __shfl_up_sync(0xffffffffu, se, o);
-      if (lane >= o) {
-        sg += tg;
-        se += te;
-      }
-    }
-    warp_cnt[0][lane] = sg - vg;
-    warp_cnt[1][lane] = se - ve;
-  }
-  __syncthreads();
-  uint32_t gt_before = warp_cnt[0][warp] + ig - n_gt;
-  uint32_t eq_before = warp_cnt[1][warp] + ie - n_eq;
+  uint32_t pos = block_exclusive_scan(cnt, sh.warp_sum, &s_total);
   for (int j = jb; j < je; ++j) {
-    uint32_t key = keys[j];
-    bool take = false;
-    if (key > tau) {
-      take = true;
-    } else if (key == tau) {
-      take = eq_before < need_eq;
-      ++eq_before;
-    }
-    if (take) {
-      // output slot = (#taken with lower index) = gt_before + min(eq_before_excl, need_eq)
-      uint32_t eq_taken = min(eq_before - (key == tau ? 1u : 0u), need_eq);
-      out[gt_before + eq_taken] = map_key(P, b, j);
-    }
-    if (key > tau) ++gt_before;
+    const uint32_t key = keys[j];
+    if ((key > tau) || (key == tau && j <= tau_last)) out[pos++] = map_key(P, b, j);
   }
 }
 
@@ -407,12 +462,12 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
   L.block_table = p->block_table;
   L.table_stride = p->table_stride;
   L.page = p->page;
-  const int smem = p->n_keys * 4;
-  static int attr_smem = 0;
-  if (smem > 48 * 1024 && smem > attr_smem) {
+  const int smem = p->n_keys * 4;  // plus the kernel's static shared memory
+  static bool sel_attr = false;
+  if (!sel_attr) {
     DSV4_CUDA_CHECK(cudaFuncSetAttribute(idx::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          idx::SEL_MAX_KEYS * 4));
-    attr_smem = idx::SEL_MAX_KEYS * 4;
+    sel_attr = true;
   }
   idx::select_kernel<<<static_cast<unsigned>(rows), idx::SEL_THREADS, smem, as_stream(stream)>>>(L);
   DSV4_LAUNCH_CHECK("indexer select_kernel");

@@ -403,68 +403,83 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
 }
 
 // Merge split partials: o = sum_s e^{m_s-M} O_s / (sum_s e^{m_s-M} l_s + e^{sink-M}).
-// One CTA per (query, head block); warp w merges heads w, w+8, ...
-__global__ void __launch_bounds__(256) combine_kernel(Params P) {
-  const int64_t qi = blockIdx.x;
-  const int hblk = blockIdx.y;
+// One CTA of 128 threads per (query, head): each thread merges 4 consecutive dims over all splits,
+// with the split loop unrolled so the partial loads of different splits are in flight together.
+__global__ void __launch_bounds__(128) combine_kernel(Params P) {
+  const int64_t unitq = blockIdx.x;             // qi * hblocks + hblk
+  const int hh = blockIdx.y;
+  const int64_t qi = unitq / P.hblocks;
+  const int hblk = static_cast<int>(unitq % P.hblocks);
   const int h0 = hblk * HB;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t unit0 = (qi * P.hblocks + hblk) * P.splits;
+  if (h0 + hh >= P.h) return;
+  const int64_t unit0 = unitq * P.splits;
   const float* pml = P.part + (P.s * P.hblocks * P.splits) * (int64_t)(HB * D);
-  const bool rope = P.rope_freqs != nullptr;
-  const int pos = rope ? P.positions[qi] : 0;
-  for (int hh = warp; hh < HB && h0 + hh < P.h; hh += 8) {
-    float M = -INFINITY;
-    for (int sp = lane; sp < P.splits; sp += 32) M = fmaxf(M, pml[(unit0 + sp) * (HB * 2) + hh * 2]);
-    M = warp_max(M);
-    float L = 0.f;
-    for (int sp = lane; sp < P.splits; sp += 32) {
-      float m = pml[(unit0 + sp) * (HB * 2) + hh * 2];
-      float l = pml[(unit0 + sp) * (HB * 2) + hh * 2 + 1];
-      L += (m == -INFINITY) ? 0.f : exp2f(m - M) * l;
+  __shared__ float s_w[64];
+  __shared__ float s_inv;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    if (lane < P.splits) {
+      m0 = pml[(unit0 + lane) * (HB * 2) + hh * 2];
+      l0 = pml[(unit0 + lane) * (HB * 2) + hh * 2 + 1];
     }
-    L = warp_sum(L);
-    const float inv = (M == -INFINITY) ? __int_as_float(0x7fc00000)
-                                       : 1.f / (L + exp2f(P.sink[h0 + hh] * LOG2E - M));
-    float acc[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-    for (int sp = 0; sp < P.splits; ++sp) {
-      const float m = pml[(unit0 + sp) * (HB * 2) + hh * 2];
-      if (m == -INFINITY) continue;
-      const float w = exp2f(m - M);
-      const float* src = P.part + (unit0 + sp) * (HB * D) + hh * D;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float4 v = *reinterpret_cast<const float4*>(src + j * 128 + lane * 4);
-        acc[j * 4 + 0] += w * v.x;
-        acc[j * 4 + 1] += w * v.y;
-        acc[j * 4 + 2] += w * v.z;
-        acc[j * 4 + 3] += w * v.w;
-      }
+    if (lane + 32 < P.splits) {
+      m1 = pml[(unit0 + lane + 32) * (HB * 2) + hh * 2];
+      l1 = pml[(unit0 + lane + 32) * (HB * 2) + hh * 2 + 1];
     }
-    const int64_t obase = ((qi * P.h) + h0 + hh) * D;
+    const float M = warp_max(fmaxf(m0, m1));
+    const float w0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M);
+    const float w1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M);
+    if (lane < P.splits) s_w[lane] = w0;
+    if (lane + 32 < P.splits) s_w[lane + 32] = w1;
+    const float L = warp_sum(w0 * l0 + w1 * l1);
+    if (lane == 0)
+      s_inv = (M == -INFINITY) ? __int_as_float(0x7fc00000)
+                               : 1.f / (L + exp2f(P.sink[h0 + hh] * LOG2E - M));
+  }
+  __syncthreads();
+  const int d = threadIdx.x * 4;
+  const float* src = P.part + unit0 * (HB * D) + hh * D + d;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  int sp = 0;
+  for (; sp + 4 <= P.splits; sp += 4) {
+    float4 v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int d = j * 128 + lane * 4;
-      float v[4];
+    for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4*>(src + (int64_t)(sp + u) * (HB * D));
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = acc[j * 4 + e] * inv;
-      if (rope && d >= D - P.rope_dim) {
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          float c, sn;
-          rope_cos_sin(pos, P.rope_freqs[(d + e - (D - P.rope_dim)) >> 1], &c, &sn);
-          rotate_pair(v[e], v[e + 1], c, sn, true, &v[e], &v[e + 1]);
-        }
-      }
-      if (P.out_dtype == DSV4_BF16) {
-        uint2 pk = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
-        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(P.out) + obase + d) = pk;
-      } else {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.out) + obase + d) = make_float4(v[0], v[1], v[2], v[3]);
-      }
+    for (int u = 0; u < 4; ++u) {
+      const float w = s_w[sp + u];
+      acc.x = fmaf(w, v[u].x, acc.x);
+      acc.y = fmaf(w, v[u].y, acc.y);
+      acc.z = fmaf(w, v[u].z, acc.z);
+      acc.w = fmaf(w, v[u].w, acc.w);
     }
+  }
+  for (; sp < P.splits; ++sp) {
+    const float4 v = *reinterpret_cast<const float4*>(src + (int64_t)sp * (HB * D));
+    const float w = s_w[sp];
+    acc.x = fmaf(w, v.x, acc.x);
+    acc.y = fmaf(w, v.y, acc.y);
+    acc.z = fmaf(w, v.z, acc.z);
+    acc.w = fmaf(w, v.w, acc.w);
+  }
+  const float inv = s_inv;
+  float o[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+  if (P.rope_freqs != nullptr && d >= D - P.rope_dim) {
+    const int pos = P.positions[qi];
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      float c, sn;
+      rope_cos_sin(pos, P.rope_freqs[(d + e - (D - P.rope_dim)) >> 1], &c, &sn);
+      rotate_pair(o[e], o[e + 1], c, sn, true, &o[e], &o[e + 1]);
+    }
+  }
+  const int64_t off = ((qi * P.h) + h0 + hh) * D + d;
+  if (P.out_dtype == DSV4_BF16) {
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(P.out) + off) =
+        make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+  } else {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.out) + off) = make_float4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -552,8 +567,8 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
   sa::sparse_attn_kernel<<<grid, sa::THREADS, smem, as_stream(stream)>>>(P);
   DSV4_LAUNCH_CHECK("sparse_attn_kernel");
   if (P.splits > 1) {
-    dim3 g2(static_cast<unsigned>(P.s), P.hblocks);
-    sa::combine_kernel<<<g2, 256, 0, as_stream(stream)>>>(P);
+    dim3 g2(static_cast<unsigned>(P.s * P.hblocks), sa::HB);
+    sa::combine_kernel<<<g2, 128, 0, as_stream(stream)>>>(P);
     DSV4_LAUNCH_CHECK("combine_kernel");
   }
   return DSV4_OK;

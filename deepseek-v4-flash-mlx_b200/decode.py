@@ -147,6 +147,7 @@ class DecodeRunner:
             self.capture()
         with torch.cuda.stream(self.stream):
             self.graph.replay()
+        torch.cuda.current_stream(self.out.device).wait_stream(self.stream)
         return self.out
 
     def step_host(self, q, q_idx, w_idx, positions):

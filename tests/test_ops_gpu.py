@@ -192,6 +192,23 @@ def test_indexer_ties_and_padding(dsv4):
     np.testing.assert_array_equal(got2[0, 0], list(range(10)) + [-1] * 6)
 
 
+def test_indexer_heavy_ties_fallback(dsv4):
+    """All scores equal (zero weights): more than 1024 keys share the boundary bin, so the radix
+    fallback runs; the answer is the lowest indices. Also a crowded bin with distinct scores."""
+    q, w, keys = _idx_inputs(1, 2, 5000, 13)
+    w[0, 0] = 0.0                                           # query 0: every score is +0
+    got = dsv4.indexer_topk(q.to(DEV), w.to(DEV), keys.to(DEV), 512).cpu().numpy()
+    np.testing.assert_array_equal(got[0, 0], np.arange(512))
+    ref = I.indexer_topk(q.numpy(), w.numpy(), keys.numpy(), 512)
+    np.testing.assert_array_equal(got, ref)
+    # scores crowded into one 12-bit bin: keys nearly identical
+    keys2 = keys.clone()
+    keys2[0] = keys[0, :1] + 1e-4 * torch.randn(5000, 128, generator=torch.Generator().manual_seed(1))
+    got2 = dsv4.indexer_topk(q.to(DEV), w.to(DEV), keys2.to(DEV), 512).cpu().numpy()
+    ref2 = I.indexer_topk(q.numpy(), w.numpy(), keys2.numpy(), 512)
+    np.testing.assert_array_equal(got2, ref2)
+
+
 # ---------------------------------------------------------------- projections
 def test_linear_bf16_and_grouped(dsv4):
     g = torch.Generator().manual_seed(3)
