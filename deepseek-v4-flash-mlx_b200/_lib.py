@@ -90,6 +90,7 @@ SIGNATURES = {
                                        ctypes.c_double, ctypes.POINTER(ctypes.c_float)]),
     "dsv4_indexer_topk_workspace_size": (sz, [ctypes.POINTER(IndexerParams)]),
     "dsv4_indexer_topk": (ctypes.c_int, [ctypes.POINTER(IndexerParams), vp]),
+    "dsv4_indexer_topk_noalloc": (ctypes.c_int, [ctypes.POINTER(IndexerParams), vp]),
     "dsv4_decode_window_indices": (ctypes.c_int, [i32, i32, vp, vp, vp, i32, vp]),
     "dsv4_compressor_pool": (ctypes.c_int, [ctypes.POINTER(CompressorParams), vp]),
     "dsv4_compressor_decode": (ctypes.c_int, [ctypes.POINTER(CompressorDecodeParams), vp]),

@@ -12,6 +12,8 @@
 // order-preserving 32-bit image; the top_k visible keys are written in ascending key order,
 // padded with -1. The reference attends to all visible compressed rows (oracle/decode_engine.py
 // :112-114); with top_k >= visible rows this selection returns exactly that list.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace dsv4 {
@@ -482,5 +484,117 @@ extern "C" int dsv4_decode_window_indices(int32_t batch, int32_t window, const i
   idx::decode_window_kernel<<<batch, 128, 0, as_stream(stream)>>>(batch, window, positions, win_base,
                                                                     out, out_stride);
   DSV4_LAUNCH_CHECK("decode_window_kernel");
+  return DSV4_OK;
+}
+
+// ---- allocation-free entry point -------------------------------------------------------------
+// Score scratch of dsv4_indexer_topk_noalloc: a fixed array in the library's device image, so that
+// a caller that cannot allocate device memory can still run the indexer. Every GPU that loads the
+// library holds these 4 MiB until the process exits. Host code must not use `g_noalloc_scores`
+// as a pointer (on the host it names a stand-in, not the device array); it passes the address that
+// cudaGetSymbolAddress returns for the current device.
+static __device__ __align__(256) float g_noalloc_scores[DSV4_INDEXER_NOALLOC_MAX_SCORES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once per device.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  DSV4_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("dsv4_indexer_topk_noalloc: device ordinal %d unsupported", dev);
+    return DSV4_ERR_INVALID_ARGUMENT;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    DSV4_CUDA_CHECK(cudaGetSymbolAddress(&ptr, g_noalloc_scores));
+    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return DSV4_OK;
+}
+}  // namespace
+
+extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* stream) {
+  DSV4_CHECK_ARG(p != nullptr, "dsv4_indexer_topk_noalloc: params is NULL");
+  DSV4_CHECK_ARG(p->q && p->w && p->k && p->out, "dsv4_indexer_topk_noalloc: NULL tensor");
+  DSV4_CHECK_ARG(p->workspace == nullptr && p->scores_out == nullptr,
+                 "dsv4_indexer_topk_noalloc: workspace and scores_out must be NULL (the scratch is built in)");
+  DSV4_CHECK_ARG(p->heads == idx::HI, "dsv4_indexer_topk_noalloc: %d heads unsupported (64 only)", p->heads);
+  DSV4_CHECK_ARG(p->batch > 0 && p->s > 0 && p->n_keys > 0 && p->top_k > 0,
+                 "dsv4_indexer_topk_noalloc: bad sizes");
+  DSV4_CHECK_ARG(p->n_keys <= idx::SEL_MAX_KEYS, "dsv4_indexer_topk_noalloc: n_keys %d above %d", p->n_keys,
+                 idx::SEL_MAX_KEYS);
+  DSV4_CHECK_ARG(p->positions == nullptr || p->ratio > 0, "dsv4_indexer_topk_noalloc: ratio must be > 0");
+  DSV4_CHECK_ARG(p->out_col >= 0 && p->out_col + p->top_k <= p->out_stride,
+                 "dsv4_indexer_topk_noalloc: out_col + top_k exceeds out_stride");
+  DSV4_CHECK_ARG(p->block_table == nullptr || (p->page > 0 && p->table_stride > 0),
+                 "dsv4_indexer_topk_noalloc: block table needs page and table_stride");
+  DSV4_CHECK_ARG(p->k_batch_stride >= p->n_keys || p->batch == 1,
+                 "dsv4_indexer_topk_noalloc: k_batch_stride smaller than n_keys");
+  const int64_t rows = static_cast<int64_t>(p->batch) * p->s;
+  const int n_pad = (p->n_keys + 3) / 4 * 4;
+  if (rows * n_pad > DSV4_INDEXER_NOALLOC_MAX_SCORES) {
+    set_error("dsv4_indexer_topk_noalloc: batch*s*n_keys (padded) = %lld scores exceeds the built-in "
+              "scratch of %d; use dsv4_indexer_topk with a caller-provided workspace",
+              static_cast<long long>(rows * n_pad), DSV4_INDEXER_NOALLOC_MAX_SCORES);
+    return DSV4_ERR_WORKSPACE;
+  }
+  float* scores = nullptr;
+  const int st = noalloc_scratch(&scores);
+  if (st != DSV4_OK) return st;
+
+  // The scores are written for every visible key before the selection reads them, and entries past
+  // a query's visible range are never read, so nothing in the scratch needs clearing between calls.
+  idx::ScoreParams S;
+  S.q = p->q;
+  S.w = p->w;
+  S.k = p->k;
+  S.scores = scores;
+  S.batch = p->batch;
+  S.s = p->s;
+  S.n_keys = p->n_keys;
+  S.n_pad = n_pad;
+  S.k_batch_stride = p->k_batch_stride;
+  S.positions = p->positions;
+  S.ratio = p->ratio;
+  static bool score_attr = false;
+  if (!score_attr) {
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(idx::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         sizeof(idx::ScoreSmem)));
+    score_attr = true;
+  }
+  dim3 g1(static_cast<unsigned>(rows), (p->n_keys + idx::KT - 1) / idx::KT);
+  idx::score_kernel<<<g1, idx::THREADS, sizeof(idx::ScoreSmem), as_stream(stream)>>>(S);
+  DSV4_LAUNCH_CHECK("indexer score_kernel (noalloc)");
+
+  idx::SelectParams L;
+  L.scores = scores;
+  L.out = p->out;
+  L.batch = p->batch;
+  L.s = p->s;
+  L.n_keys = p->n_keys;
+  L.n_pad = n_pad;
+  L.top_k = p->top_k;
+  L.positions = p->positions;
+  L.ratio = p->ratio;
+  L.out_stride = p->out_stride;
+  L.out_col = p->out_col;
+  L.out_offset = p->out_offset;
+  L.block_table = p->block_table;
+  L.table_stride = p->table_stride;
+  L.page = p->page;
+  static bool sel_attr = false;
+  if (!sel_attr) {
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(idx::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         idx::SEL_MAX_KEYS * 4));
+    sel_attr = true;
+  }
+  idx::select_kernel<<<static_cast<unsigned>(rows), idx::SEL_THREADS, p->n_keys * 4, as_stream(stream)>>>(L);
+  DSV4_LAUNCH_CHECK("indexer select_kernel (noalloc)");
   return DSV4_OK;
 }
