@@ -38,6 +38,8 @@ CONFIGS = {
                         "rows each), top-k 512"),
 }
 L2_BYTES = 126 * 1024 * 1024
+# kernels of one decode step: q norm/rope, indexer scores, top-k selection, sparse attention, split merge
+LAUNCHES_PER_STEP = 5
 
 
 def _pkg():
@@ -313,7 +315,7 @@ def main():
                            "l2": f"inputs rotate over {R} replicas x {footprint / 2**20:.1f} MiB = "
                                  f"{R * footprint / 2**20:.0f} MiB > L2 (126 MB)",
                            "cuda_graph": True},
-                "gpu_launches": 6 * args.steps,
+                "gpu_launches": LAUNCHES_PER_STEP * args.steps,
                 "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -326,28 +328,27 @@ def kernel_times(dsv4, cases, runners, stream, dev, n):
     import importlib
     L = importlib.import_module(PKG + "._lib")
     SA = importlib.import_module(PKG + ".sparse_attn")
-    NRm = importlib.import_module(PKG + ".norm_rope")
     IX = importlib.import_module(PKG + ".indexer")
     R = len(cases)
     b = cases[0].cache.batch
     top_k = runners[0].top_k
     freqs = runners[0].freqs
-    qr = [NRm.norm_rope(r.q, r.positions, freqs) for r in runners]
     torch.cuda.synchronize()
     nvis = [min((int(c.host["positions"][i]) + 1) // 4, c.cache.max_comp) for c in cases[:1] for i in range(b)]
     n_keys = sum(nvis)
     funcs = {
-        "norm_rope": (lambda i: NRm.norm_rope(runners[i].q, runners[i].positions, freqs),
-                      b * 64 * 512 * (4 + 2) + b * 4),
+        # score + select (which also writes the window rows): k_idx read once, indices written
         "indexer_topk": (lambda i: IX.indexer_topk_into(runners[i].idx.view(b, 1, -1), runners[i].q_idx.view(b, 1, 64, 128),
                                                         runners[i].w_idx.view(b, 1, 64), cases[i].cache.k_idx, top_k,
                                                         runners[i].positions.view(b, 1), 4, out_col=128,
                                                         out_offset=cases[i].cache.comp_base,
-                                                        block_table=cases[i].cache.block_table, page=cases[i].cache.page),
-                         n_keys * 128 * 4 + b * (64 * 128 * 4 + 64 * 4 + top_k * 4)),
-        "sparse_attn": (lambda i: SA.sparse_attn_rope(qr[i], cases[i].cache.kv_pool, cases[i].sink, runners[i].idx, 512 ** -0.5,
-                                                      runners[i].positions, freqs, 64),
-                        b * ((128 + top_k) * (512 * 2 + 4) + 64 * 512 * 2 * 2)),
+                                                        block_table=cases[i].cache.block_table, page=cases[i].cache.page,
+                                                        win_base=cases[i].cache.win_base, window=128),
+                         n_keys * 128 * 4 + b * (64 * 128 * 4 + 64 * 4 + (128 + top_k) * 4)),
+        # attention (+ split merge): gathered rows, raw q in, o out, indices
+        "sparse_attn": (lambda i: SA.sparse_attn_decode(runners[i].q, cases[i].cache.kv_pool, cases[i].sink,
+                                                        runners[i].idx, 512 ** -0.5, runners[i].positions, freqs, 64),
+                        b * ((128 + top_k) * (512 * 2 + 4) + 64 * 512 * 4 + 64 * 512 * 2)),
     }
     out = {}
     for name, (fn, nbytes) in funcs.items():

@@ -26,7 +26,7 @@ class SparseAttnParams(ctypes.Structure):
                 ("s", i64), ("n", i64), ("h", i32), ("d", i32), ("t", i32),
                 ("q_dtype", i32), ("idx_dtype", i32), ("out_dtype", i32), ("scale", f32),
                 ("rope_freqs", vp), ("positions", vp), ("rope_dim", i32), ("num_splits", i32),
-                ("workspace", vp), ("workspace_bytes", sz)]
+                ("workspace", vp), ("workspace_bytes", sz), ("q_norm_rope", i32), ("q_eps", f32)]
 
 
 class RmsNormParams(ctypes.Structure):
@@ -53,7 +53,7 @@ class IndexerParams(ctypes.Structure):
                 ("k_batch_stride", i64), ("positions", vp), ("ratio", i32),
                 ("out_stride", i32), ("out_col", i32), ("out_offset", i64),
                 ("block_table", vp), ("table_stride", i32), ("page", i32),
-                ("workspace", vp), ("workspace_bytes", sz)]
+                ("workspace", vp), ("workspace_bytes", sz), ("win_base", vp), ("window", i32)]
 
 
 class CompressorParams(ctypes.Structure):

@@ -62,6 +62,8 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
   extern __shared__ __align__(16) uint8_t score_smem[];
   ScoreSmem& sm = *reinterpret_cast<ScoreSmem*>(score_smem);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_trigger();
+  pdl_wait();
   const int64_t qrow = blockIdx.x;
   const int b = static_cast<int>(qrow / P.s);
   const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
@@ -166,11 +168,15 @@ struct SelectParams {
   int64_t out_offset;
   const int32_t* block_table;
   int32_t table_stride, page;
+  const int64_t* win_base;
+  int32_t window;
 };
 
-constexpr int SEL_THREADS = 1024;
+constexpr int SEL_THREADS = 512;
 constexpr int SEL_MAX_KEYS = 32768;
-static_assert(SEL_THREADS * 4 == 4096, "one thread per 4 histogram bins");
+constexpr int SEL_BINS = 4096;
+constexpr int SEL_RANK_MAX = 1024;   // candidates resolved by O(c^2) rank counting up to this many
+static_assert(SEL_BINS % SEL_THREADS == 0, "whole bins per thread");
 
 __device__ __forceinline__ int32_t map_key(const SelectParams& P, int b, int j) {
   int64_t row;
@@ -184,53 +190,55 @@ __device__ __forceinline__ int32_t map_key(const SelectParams& P, int b, int j) 
   return static_cast<int32_t>(row + P.out_offset);
 }
 
-// One CTA per query. Pass 1: a 4096-bin histogram of the top 12 bits of every visible key's
-// ordered score finds the boundary bin (keys above it are in, keys below are out). Pass 2 resolves
-// the boundary bin's candidates exactly — by rank counting over (ordered score desc, index asc)
-// when they are few, otherwise by further radix passes over the candidates only. Pass 3 writes the
-// chosen keys in ascending index order through a block prefix sum.
-constexpr int SEL_BINS = 4096;
-constexpr int SEL_RANK_MAX = 1024;   // candidates resolved by O(c^2) rank counting up to this many
-
 struct SelShared {
   uint32_t hist[SEL_BINS];
   uint32_t warp_sum[SEL_THREADS / 32];
   uint32_t cand_key[SEL_RANK_MAX];
   int32_t cand_idx[SEL_RANK_MAX];
-  uint32_t n_cand, n_above, need, bin, tau, tau_need;
+  uint32_t n_cand, bin, need, tau;
+  int32_t tau_last;
+  uint32_t total;
 };
 
-__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_sum, uint32_t* total) {
+// exclusive prefix sum over the block (3 barriers); sh.total receives the block sum
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, SelShared& sh) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t incl = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += t;
   }
-  if (lane == 31) warp_sum[warp] = incl;
+  if (lane == 31) sh.warp_sum[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    uint32_t w = lane < (SEL_THREADS / 32) ? warp_sum[lane] : 0u;
+    const uint32_t w = lane < SEL_THREADS / 32 ? sh.warp_sum[lane] : 0u;
     uint32_t wi = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      uint32_t t = __shfl_up_sync(0xffffffffu, wi, o);
+      const uint32_t t = __shfl_up_sync(0xffffffffu, wi, o);
       if (lane >= o) wi += t;
     }
-    if (lane < (SEL_THREADS / 32)) warp_sum[lane] = wi - w;
-    if (lane == (SEL_THREADS / 32) - 1) *total = wi;
+    if (lane < SEL_THREADS / 32) sh.warp_sum[lane] = wi - w;
+    if (lane == 31) sh.total = wi;
   }
   __syncthreads();
-  const uint32_t r = warp_sum[warp] + incl - v;
+  const uint32_t r = sh.warp_sum[warp] + incl - v;
   __syncthreads();
   return r;
 }
 
+// One CTA per query. (1) the visible scores are loaded (independent vector loads) into shared memory
+// as order-preserving keys; (2) a 4096-bin histogram of their top 12 bits gives the boundary bin:
+// keys in higher bins are taken, lower bins dropped; (3) the boundary bin is resolved exactly — by
+// rank counting over (key desc, index asc) when it holds at most 1024 keys, else by radix passes
+// over its remaining bits; (4) the taken keys are written in ascending index order through a block
+// prefix sum, mapped to pool rows.
 __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
   extern __shared__ uint32_t keys[];  // [nvis] ordered scores
   __shared__ SelShared sh;
-  __shared__ uint32_t s_total;
+  pdl_trigger();
+  pdl_wait();
   const int tid = threadIdx.x;
   const int64_t qrow = blockIdx.x;
   const int b = static_cast<int>(qrow / P.s);
@@ -238,37 +246,60 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
   int32_t* out = P.out + qrow * P.out_stride + P.out_col;
   const int k = P.top_k;
 
+  if (P.win_base != nullptr && tid < P.window) {
+    // decode window rows, ring order (slot -1 = not yet written)
+    const int p = P.positions[qrow];
+    const int W = P.window;
+    int slot;
+    if (p >= W - 1) {
+      const int sp = p % W;
+      slot = (tid < W - sp - 1) ? (sp + 1 + tid) : (tid - (W - sp - 1));
+    } else {
+      slot = (tid <= p) ? tid : -1;
+    }
+    out[tid - W] = slot < 0 ? -1 : static_cast<int32_t>(P.win_base[b] + slot);
+  }
   if (nvis <= k) {
     for (int r = tid; r < k; r += SEL_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
     return;
   }
-  for (int i = tid; i < SEL_BINS; i += SEL_THREADS) sh.hist[i] = 0;
+  // (1) load
+  const float* sc = P.scores + qrow * P.n_pad;
+  if ((P.n_pad & 3) == 0) {
+    const int n4 = nvis >> 2;
+#pragma unroll 4
+    for (int c = tid; c < n4; c += SEL_THREADS) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(sc) + c);
+      *reinterpret_cast<uint4*>(keys + 4 * c) =
+          make_uint4(ordered_bits(v.x), ordered_bits(v.y), ordered_bits(v.z), ordered_bits(v.w));
+    }
+    for (int j = 4 * n4 + tid; j < nvis; j += SEL_THREADS) keys[j] = ordered_bits(__ldcg(sc + j));
+  } else {
+#pragma unroll 4
+    for (int j = tid; j < nvis; j += SEL_THREADS) keys[j] = ordered_bits(__ldcg(sc + j));
+  }
+#pragma unroll
+  for (int i = 0; i < SEL_BINS / SEL_THREADS; ++i) sh.hist[tid + i * SEL_THREADS] = 0;
   if (tid == 0) sh.n_cand = 0;
   __syncthreads();
-  const float* sc = P.scores + qrow * P.n_pad;
-  for (int j = tid; j < nvis; j += SEL_THREADS) {
-    const uint32_t key = ordered_bits(sc[j]);
-    keys[j] = key;
-    atomicAdd(&sh.hist[key >> 20], 1u);
-  }
+  // (2) histogram of the top 12 bits, then the boundary bin
+  for (int j = tid; j < nvis; j += SEL_THREADS) atomicAdd(&sh.hist[keys[j] >> 20], 1u);
   __syncthreads();
-  // boundary bin: suffix counts over bins in descending order; thread t owns bins
-  // [4095 - 4t - 3, 4095 - 4t] (SEL_THREADS * 4 == SEL_BINS)
   {
-    uint32_t c[4], tot = 0;
+    constexpr int PER = SEL_BINS / SEL_THREADS;  // bins per thread, descending
+    uint32_t c[PER], tot = 0;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      c[e] = sh.hist[SEL_BINS - 1 - (tid * 4 + e)];
+    for (int e = 0; e < PER; ++e) {
+      c[e] = sh.hist[SEL_BINS - 1 - (tid * PER + e)];
       tot += c[e];
     }
-    const uint32_t before = block_exclusive_scan(tot, sh.warp_sum, &s_total);
+    const uint32_t before = block_exclusive_scan(tot, sh);
     if (before < static_cast<uint32_t>(k) && static_cast<uint32_t>(k) <= before + tot) {
       uint32_t run = before;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < PER; ++e) {
         if (run + c[e] >= static_cast<uint32_t>(k)) {
-          sh.bin = SEL_BINS - 1 - (tid * 4 + e);
-          sh.n_above = run;
+          sh.bin = SEL_BINS - 1 - (tid * PER + e);
           sh.need = k - run;
           break;
         }
@@ -279,10 +310,8 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
   __syncthreads();
   const uint32_t bin = sh.bin;
   const uint32_t need = sh.need;
-  const uint32_t n_bin = sh.hist[bin];
-  // resolve the boundary bin: find tau (the need-th largest key inside the bin) and how many of the
-  // keys equal to tau are taken (lowest indices first)
-  if (n_bin <= SEL_RANK_MAX) {
+  // (3) resolve the boundary bin
+  if (sh.hist[bin] <= SEL_RANK_MAX) {
     for (int j = tid; j < nvis; j += SEL_THREADS) {
       const uint32_t key = keys[j];
       if ((key >> 20) == bin) {
@@ -297,24 +326,25 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
       const uint32_t ki = sh.cand_key[i];
       const int32_t ii = sh.cand_idx[i];
       uint32_t rank = 0;
+#pragma unroll 4
       for (uint32_t m = 0; m < c; ++m) {
         const uint32_t km = sh.cand_key[m];
         rank += (km > ki) || (km == ki && sh.cand_idx[m] < ii);
       }
-      if (rank == need - 1) {  // the last key taken: defines the cut
+      if (rank == need - 1) {  // the last key taken
         sh.tau = ki;
-        sh.tau_need = ii;       // keys equal to tau are taken while their index <= this one
+        sh.tau_last = ii;      // keys equal to tau are taken up to this index
       }
     }
   } else {
-    // many keys share the boundary bin (e.g. heavy ties): radix passes over that bin only, on
-    // bits 19..12, 11..4 and 3..0, then the kleft lowest indices among keys equal to the result
+    // a crowded boundary bin (e.g. heavy ties): radix passes over its bits 19..12, 11..4, 3..0
     uint32_t prefix = bin << 20, kleft = need;
     const int shifts[3] = {12, 4, 0}, widths[3] = {8, 8, 4};
+#pragma unroll 1
     for (int ps = 0; ps < 3; ++ps) {
       const int shift = shifts[ps], width = widths[ps], hi = shift + width;
       const uint32_t mask = (1u << width) - 1u;
-      for (int i = tid; i < 256; i += SEL_THREADS) sh.hist[i] = 0;
+      if (tid < 256) sh.hist[tid] = 0;
       __syncthreads();
       for (int j = tid; j < nvis; j += SEL_THREADS) {
         const uint32_t key = keys[j];
@@ -342,12 +372,12 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
     const int jb = tid * per, je = min(nvis, jb + per);
     uint32_t ne = 0;
     for (int j = jb; j < je; ++j) ne += keys[j] == prefix;
-    const uint32_t before = block_exclusive_scan(ne, sh.warp_sum, &s_total);
+    const uint32_t before = block_exclusive_scan(ne, sh);
     if (before < kleft && kleft <= before + ne) {
       uint32_t seen = before;
       for (int j = jb; j < je; ++j)
         if (keys[j] == prefix && ++seen == kleft) {
-          sh.tau_need = j;
+          sh.tau_last = j;
           break;
         }
     }
@@ -355,8 +385,8 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
   }
   __syncthreads();
   const uint32_t tau = sh.tau;
-  const int32_t tau_last = sh.tau_need;
-  // index-ordered compaction of {key > tau} U {key == tau and index <= tau_last}
+  const int32_t tau_last = sh.tau_last;
+  // (4) index-ordered compaction of {key > tau} U {key == tau, index <= tau_last}
   const int per = (nvis + SEL_THREADS - 1) / SEL_THREADS;
   const int jb = tid * per, je = min(nvis, jb + per);
   uint32_t cnt = 0;
@@ -364,10 +394,222 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
     const uint32_t key = keys[j];
     cnt += (key > tau) || (key == tau && j <= tau_last);
   }
-  uint32_t pos = block_exclusive_scan(cnt, sh.warp_sum, &s_total);
+  uint32_t pos = block_exclusive_scan(cnt, sh);
   for (int j = jb; j < je; ++j) {
     const uint32_t key = keys[j];
     if ((key > tau) || (key == tau && j <= tau_last)) out[pos++] = map_key(P, b, j);
+  }
+}
+
+// Register-resident selection for up to SEL_THREADS * PER visible keys: thread t holds keys
+// [t*PER, t*PER + PER) in registers (so every pass is in index order without shared-memory
+// traffic). MSB-first radix over the order-preserving key: 12 bits, then 8, 8 and 4 more, each level
+// histogramming only the keys that still match the prefix (shared-memory atomics). A level
+// whose boundary bin is taken whole ends the search early; otherwise after all 32 bits the keys equal
+// to the threshold are taken lowest index first. The taken keys are written in ascending order.
+struct SelRegShared {
+  uint32_t hist[SEL_BINS];
+  uint32_t warp_sum[SEL_THREADS / 32];
+  uint32_t total, bin, need;
+  int32_t tau_last;
+};
+
+__device__ __forceinline__ uint32_t block_scan_reg(uint32_t v, SelRegShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) sh.warp_sum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t w = lane < SEL_THREADS / 32 ? sh.warp_sum[lane] : 0u;
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    if (lane < SEL_THREADS / 32) sh.warp_sum[lane] = wi - w;
+    if (lane == 31) sh.total = wi;
+  }
+  __syncthreads();
+  const uint32_t r = sh.warp_sum[warp] + incl - v;
+  __syncthreads();
+  return r;
+}
+
+// add 1 to hist[bin] when bin < nbins (plain shared atomics: grouping lanes by bin first with
+// __match_any_sync measured several times slower on B200 than the conflicting atomics it saves)
+__device__ __forceinline__ void warp_hist_add(uint32_t* hist, uint32_t bin, uint32_t nbins) {
+  if (bin < nbins) atomicAdd(&hist[bin], 1u);
+}
+
+template <int PER>
+__global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P) {
+  __shared__ SelRegShared sh;
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t qrow = blockIdx.x;
+  const int b = static_cast<int>(qrow / P.s);
+  const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
+  int32_t* out = P.out + qrow * P.out_stride + P.out_col;
+  const int k = P.top_k;
+
+  if (P.win_base != nullptr && tid < P.window) {
+    const int p = P.positions[qrow];
+    const int W = P.window;
+    int slot;
+    if (p >= W - 1) {
+      const int sp = p % W;
+      slot = (tid < W - sp - 1) ? (sp + 1 + tid) : (tid - (W - sp - 1));
+    } else {
+      slot = (tid <= p) ? tid : -1;
+    }
+    out[tid - W] = slot < 0 ? -1 : static_cast<int32_t>(P.win_base[b] + slot);
+  }
+  if (nvis <= k) {
+    for (int r = tid; r < k; r += SEL_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
+    return;
+  }
+  const int j0 = tid * PER;
+  const float* sc = P.scores + qrow * P.n_pad + j0;
+  uint32_t key[PER];
+  if ((P.n_pad & 3) == 0 && j0 + PER <= nvis) {
+#pragma unroll
+    for (int e = 0; e < PER; e += 4) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(sc + e));
+      key[e] = ordered_bits(v.x);
+      key[e + 1] = ordered_bits(v.y);
+      key[e + 2] = ordered_bits(v.z);
+      key[e + 3] = ordered_bits(v.w);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < PER; ++e) key[e] = (j0 + e < nvis) ? ordered_bits(__ldcg(sc + e)) : 0u;
+  }
+  // number of valid keys of this thread (the rest are padding and never counted)
+  const int nv = max(0, min(PER, nvis - j0));
+
+#pragma unroll
+  for (int i = 0; i < SEL_BINS / SEL_THREADS; ++i) sh.hist[tid + i * SEL_THREADS] = 0;
+  __syncthreads();
+  // level 1: top 12 bits
+#pragma unroll
+  for (int e = 0; e < PER; ++e) warp_hist_add(sh.hist, e < nv ? (key[e] >> 20) : 0xffffffffu, SEL_BINS);
+  __syncthreads();
+  uint32_t prefix, kleft, shift = 20;
+  bool whole = false;
+  {
+    constexpr int PB = SEL_BINS / SEL_THREADS;
+    uint32_t c[PB], tot = 0;
+#pragma unroll
+    for (int e = 0; e < PB; ++e) {
+      c[e] = sh.hist[SEL_BINS - 1 - (tid * PB + e)];
+      tot += c[e];
+    }
+    const uint32_t before = block_scan_reg(tot, sh);
+    if (before < static_cast<uint32_t>(k) && static_cast<uint32_t>(k) <= before + tot) {
+      uint32_t run = before;
+#pragma unroll
+      for (int e = 0; e < PB; ++e) {
+        if (run + c[e] >= static_cast<uint32_t>(k)) {
+          const uint32_t bn = SEL_BINS - 1 - (tid * PB + e);
+          sh.bin = bn;
+          sh.need = (k - run) | ((c[e] == k - run) ? 0x80000000u : 0u);  // top bit: bin taken whole
+          break;
+        }
+        run += c[e];
+      }
+    }
+    __syncthreads();
+    prefix = sh.bin << 20;
+    kleft = sh.need & 0x7fffffffu;
+    whole = (sh.need >> 31) != 0;
+  }
+  // levels 2..4 over the keys inside the boundary bin: bits 19..12, 11..4, 3..0
+#pragma unroll 1
+  for (int level = 0; level < 3 && !whole; ++level) {
+    const uint32_t width = level < 2 ? 8u : 4u;
+    const uint32_t nshift = shift - width;
+    const uint32_t nb = 1u << width;
+    if (tid < 256) sh.hist[tid] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      const bool in = e < nv && (key[e] >> shift) == (prefix >> shift);
+      warp_hist_add(sh.hist, in ? ((key[e] >> nshift) & (nb - 1)) : 0xffffffffu, nb);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // lane l owns sub-bins [nb-1-l*8, nb-8-l*8] (descending); nb <= 256
+      const int per = (nb + 31) / 32;
+      uint32_t cnt[8], tot = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int d = static_cast<int>(nb) - 1 - (lane * per + e);
+        cnt[e] = (e < per && d >= 0) ? sh.hist[d] : 0u;
+        tot += cnt[e];
+      }
+      uint32_t incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const uint32_t before = incl - tot;
+      if (before < kleft && kleft <= incl) {
+        uint32_t run = before;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (e < per && run + cnt[e] >= kleft) {
+            sh.bin = static_cast<uint32_t>(static_cast<int>(nb) - 1 - (lane * per + e));
+            sh.need = (kleft - run) | ((cnt[e] == kleft - run) ? 0x80000000u : 0u);
+            break;
+          }
+          run += cnt[e];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= sh.bin << nshift;
+    kleft = sh.need & 0x7fffffffu;
+    whole = (sh.need >> 31) != 0;
+    shift = nshift;
+    __syncthreads();
+  }
+  // keys equal to the full 32-bit prefix (shift == 0, not whole): the kleft lowest indices
+  int32_t tau_last = 0x7fffffff;
+  if (!whole) {
+    uint32_t ne = 0;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) ne += (e < nv && key[e] == prefix);
+    const uint32_t before = block_scan_reg(ne, sh);
+    if (before < kleft && kleft <= before + ne) {
+      uint32_t seen = before;
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if (e < nv && key[e] == prefix && ++seen == kleft) sh.tau_last = j0 + e;
+    }
+    __syncthreads();
+    tau_last = sh.tau_last;
+  }
+  // take: (key >> shift) above the prefix, or equal to it and (whole, or index <= tau_last)
+  const uint32_t hi = prefix >> shift;
+  uint32_t cnt = 0;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const uint32_t kh = key[e] >> shift;
+    cnt += (e < nv) && (kh > hi || (kh == hi && (whole || j0 + e <= tau_last)));
+  }
+  uint32_t pos = block_scan_reg(cnt, sh);
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const uint32_t kh = key[e] >> shift;
+    if ((e < nv) && (kh > hi || (kh == hi && (whole || j0 + e <= tau_last)))) out[pos++] = map_key(P, b, j0 + e);
   }
 }
 
@@ -388,7 +630,25 @@ __global__ void decode_window_kernel(int32_t batch, int32_t window, const int32_
   }
 }
 
+// the register-resident kernel up to 16384 visible keys, the shared-memory one above
+inline cudaError_t launch_select(const SelectParams& L, unsigned rows, cudaStream_t st) {
+  const dim3 g(rows), blk(SEL_THREADS);
+  if (L.n_keys <= SEL_THREADS * 4) return launch_pdl(select_reg_kernel<4>, g, blk, 0, st, L);
+  if (L.n_keys <= SEL_THREADS * 8) return launch_pdl(select_reg_kernel<8>, g, blk, 0, st, L);
+  if (L.n_keys <= SEL_THREADS * 16) return launch_pdl(select_reg_kernel<16>, g, blk, 0, st, L);
+  if (L.n_keys <= SEL_THREADS * 32) return launch_pdl(select_reg_kernel<32>, g, blk, 0, st, L);
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               SEL_MAX_KEYS * 4);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  return launch_pdl(select_kernel, g, blk, static_cast<size_t>(L.n_keys) * 4, st, L);
+}
+
 }  // namespace idx
+
 DSV4_ERROR_READER(indexer)
 
 }  // namespace dsv4
@@ -416,6 +676,9 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
                  "dsv4_indexer_topk: block table needs page and table_stride");
   DSV4_CHECK_ARG(p->k_batch_stride >= p->n_keys || p->batch == 1,
                  "dsv4_indexer_topk: k_batch_stride smaller than n_keys");
+  DSV4_CHECK_ARG(p->win_base == nullptr || (p->positions != nullptr && p->window > 0 && p->window <= idx::SEL_THREADS &&
+                                            p->out_col >= p->window),
+                 "dsv4_indexer_topk: window columns need positions and out_col >= window");
   const int64_t rows = static_cast<int64_t>(p->batch) * p->s;
   DSV4_CHECK_ARG(rows <= 2147483647LL, "dsv4_indexer_topk: too many queries");
   const size_t need = dsv4_indexer_topk_workspace_size(p);
@@ -445,8 +708,7 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
                                          sizeof(idx::ScoreSmem)));
     score_attr = true;
   }
-  idx::score_kernel<<<g1, idx::THREADS, sizeof(idx::ScoreSmem), as_stream(stream)>>>(S);
-  DSV4_LAUNCH_CHECK("indexer score_kernel");
+  DSV4_CUDA_CHECK(launch_pdl(idx::score_kernel, g1, dim3(idx::THREADS), sizeof(idx::ScoreSmem), as_stream(stream), S));
 
   idx::SelectParams L;
   L.scores = scores;
@@ -464,15 +726,9 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
   L.block_table = p->block_table;
   L.table_stride = p->table_stride;
   L.page = p->page;
-  const int smem = p->n_keys * 4;  // plus the kernel's static shared memory
-  static bool sel_attr = false;
-  if (!sel_attr) {
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(idx::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         idx::SEL_MAX_KEYS * 4));
-    sel_attr = true;
-  }
-  idx::select_kernel<<<static_cast<unsigned>(rows), idx::SEL_THREADS, smem, as_stream(stream)>>>(L);
-  DSV4_LAUNCH_CHECK("indexer select_kernel");
+  L.win_base = p->win_base;
+  L.window = p->window;
+  DSV4_CUDA_CHECK(idx::launch_select(L, static_cast<unsigned>(rows), as_stream(stream)));
   return DSV4_OK;
 }
 
@@ -536,6 +792,9 @@ extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* str
                  "dsv4_indexer_topk_noalloc: block table needs page and table_stride");
   DSV4_CHECK_ARG(p->k_batch_stride >= p->n_keys || p->batch == 1,
                  "dsv4_indexer_topk_noalloc: k_batch_stride smaller than n_keys");
+  DSV4_CHECK_ARG(p->win_base == nullptr || (p->positions != nullptr && p->window > 0 && p->window <= idx::SEL_THREADS &&
+                                            p->out_col >= p->window),
+                 "dsv4_indexer_topk_noalloc: window columns need positions and out_col >= window");
   const int64_t rows = static_cast<int64_t>(p->batch) * p->s;
   const int n_pad = (p->n_keys + 3) / 4 * 4;
   if (rows * n_pad > DSV4_INDEXER_NOALLOC_MAX_SCORES) {
@@ -588,13 +847,8 @@ extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* str
   L.block_table = p->block_table;
   L.table_stride = p->table_stride;
   L.page = p->page;
-  static bool sel_attr = false;
-  if (!sel_attr) {
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(idx::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         idx::SEL_MAX_KEYS * 4));
-    sel_attr = true;
-  }
-  idx::select_kernel<<<static_cast<unsigned>(rows), idx::SEL_THREADS, p->n_keys * 4, as_stream(stream)>>>(L);
-  DSV4_LAUNCH_CHECK("indexer select_kernel (noalloc)");
+  L.win_base = p->win_base;
+  L.window = p->window;
+  DSV4_CUDA_CHECK(idx::launch_select(L, static_cast<unsigned>(rows), as_stream(stream)));
   return DSV4_OK;
 }

@@ -96,38 +96,35 @@ __device__ __forceinline__ int64_t load_idx(const void* idx, int64_t off, int dt
   return __ldg(reinterpret_cast<const int32_t*>(idx) + off);
 }
 
-// Issue the gather of tile rows [t0, t0+BN) of this query into kv buffer `buf`.
-__device__ __forceinline__ void gather_tile(const Params& P, Smem& sm, int buf, int64_t qi,
-                                            int t0, int t_end) {
+// Issue the gather of tile rows [t0, t0+BN) of this query into kv buffer `buf`: every thread first
+// loads the indices of the 16 rows it copies (independent loads, one round trip), then issues its
+// 16-byte cp.async copies; rows past the list or masked (-1) are zero-filled and marked invalid.
+__device__ __forceinline__ void gather_tile(const Params& P, Smem& sm, int buf, int64_t qi, int t0,
+                                            int t_end) {
   const int tid = threadIdx.x;
-  if (tid < BN) {
-    int t = t0 + tid;
-    int32_t r = -1;
-    if (t < t_end) {
-      int64_t v = load_idx(P.idx, qi * P.t + t, P.idx_dtype);
-      if (v >= P.n) {
-        raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
-        v = -1;
-      }
-      r = v < 0 ? -1 : static_cast<int32_t>(v);
-    }
-    sm.rowidx[buf][tid] = r;
-  }
-  // each thread re-reads the indices of the rows it copies (an L1 broadcast) rather than
-  // waiting on a barrier for the smem copy above.
-  const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(sm.kv[buf]));
-  const int chunk = tid & 63;      // 64 chunks of 16 B per row
-#pragma unroll 4
-  for (int rr = tid >> 6; rr < BN; rr += THREADS / 64) {
-    int t = t0 + rr;
+  constexpr int ROWS_PER_THREAD = BN / (THREADS / 64);  // 16
+  const int chunk = tid & 63;                            // 64 chunks of 16 B per row
+  const int r0 = tid >> 6;
+  int32_t rows[ROWS_PER_THREAD];
+#pragma unroll
+  for (int i = 0; i < ROWS_PER_THREAD; ++i) {
+    const int t = t0 + r0 + i * (THREADS / 64);
     int64_t v = -1;
-    if (t < t_end) {
-      v = load_idx(P.idx, qi * P.t + t, P.idx_dtype);
-      if (v >= P.n) v = -1;
+    if (t < t_end) v = load_idx(P.idx, qi * P.t + t, P.idx_dtype);
+    if (v >= P.n) {
+      if (chunk == 0) raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
+      v = -1;
     }
-    const bool valid = v >= 0;
-    const __nv_bfloat16* src = P.kv + (valid ? v : 0) * D + chunk * 8;
+    rows[i] = static_cast<int32_t>(v < 0 ? -1 : v);
+  }
+  const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(sm.kv[buf]));
+#pragma unroll
+  for (int i = 0; i < ROWS_PER_THREAD; ++i) {
+    const int rr = r0 + i * (THREADS / 64);
+    const bool valid = rows[i] >= 0;
+    const __nv_bfloat16* src = P.kv + static_cast<int64_t>(valid ? rows[i] : 0) * D + chunk * 8;
     cp_async16(base + swz(rr, chunk, ROW_BYTES), src, valid);
+    if (chunk == 0) sm.rowidx[buf][rr] = rows[i];
   }
   cp_async_commit();
 }
@@ -148,27 +145,32 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
   const int tile_end = min(ntiles_all, tile_begin + per);
   const int t_end = P.t;
 
+  pdl_trigger();
+  pdl_wait();
   // ---- stage Q (64 heads x 512) as bf16, swizzled ----
-  {
-    const uint32_t qbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
+  const uint32_t qbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
+  if (P.q_dtype == DSV4_BF16) {
+    const __nv_bfloat16* qg = reinterpret_cast<const __nv_bfloat16*>(P.q) + ((qi * P.h) + h0) * D;
+#pragma unroll 4
     for (int c = tid; c < HB * 64; c += THREADS) {
-      int hh = c >> 6, ch = c & 63;
+      const int hh = c >> 6, ch = c & 63;
+      const bool ok = hh < heads_here;
+      cp_async16(qbase + swz(hh, ch, ROW_BYTES), qg + (ok ? hh * D + ch * 8 : 0), ok);
+    }
+    cp_async_commit();
+  } else {
+#pragma unroll 4
+    for (int c = tid; c < HB * 64; c += THREADS) {
+      const int hh = c >> 6, ch = c & 63;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (hh < heads_here) {
-        int64_t off = ((qi * P.h) + h0 + hh) * D + ch * 8;
-        if (P.q_dtype == DSV4_BF16) {
-          v = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(P.q) + off));
-        } else {
-          const float4* f = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(P.q) + off);
-          float4 a = __ldg(f), b = __ldg(f + 1);
-          v.x = pack_bf16x2(a.x, a.y);
-          v.y = pack_bf16x2(a.z, a.w);
-          v.z = pack_bf16x2(b.x, b.y);
-          v.w = pack_bf16x2(b.z, b.w);
-        }
+        const float4* f = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(P.q) +
+                                                          ((qi * P.h) + h0 + hh) * D + ch * 8);
+        const float4 x = __ldg(f), y = __ldg(f + 1);
+        v = make_uint4(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w), pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
       }
-      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(qbase + swz(hh, ch, ROW_BYTES)),
-                   "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(qbase + swz(hh, ch, ROW_BYTES)), "r"(v.x),
+                   "r"(v.y), "r"(v.z), "r"(v.w));
     }
   }
   if (tid < HB) {
@@ -208,7 +210,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
       for (int b = 0; b < 2; ++b)
 #pragma unroll
         for (int c = 0; c < 4; ++c) s[a][b][c] = 0.f;
-#pragma unroll 4
+#pragma unroll 2
     for (int kc = 0; kc < D / 16; ++kc) {
       uint32_t a[2][4], b[4];
 #pragma unroll
@@ -313,7 +315,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
         o[mt][nt][3] *= a1;
       }
     }
-#pragma unroll
+#pragma unroll 1
     for (int kc = 0; kc < BN / 16; ++kc) {
       uint32_t a[4][4];
 #pragma unroll
@@ -339,62 +341,62 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
   }
   __syncthreads();
 
-  // ---- epilogue ----
-  const int dbase = warp * 64;
-  if (P.splits == 1) {
-    const bool rope = P.rope_freqs != nullptr && dbase + 64 > D - P.rope_dim;
-    const int pos = rope ? P.positions[qi] : 0;
+  // ---- epilogue: O (scaled for the final output) -> smem fp32 [64][OSTRIDE] over the kv buffers,
+  // then one rolled, coalesced pass writes it out (inverse rope applied there)
+  constexpr int OSTRIDE = D + 8;
+  float* os = reinterpret_cast<float*>(sm.kv[0]);
+  const bool final_out = P.splits == 1;
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
+  for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int hh = mt * 16 + hf * 8 + (lane >> 2);
-        if (hh >= heads_here) continue;
+    for (int hf = 0; hf < 2; ++hf) {
+      const int hh = mt * 16 + hf * 8 + (lane >> 2);
+      float inv = 1.f;
+      if (final_out) {
         const float m = sm.m_run[cur][hh];
-        const float l = sm.l_run[hh];
-        float inv;
-        if (m == -INFINITY) {
-          inv = __int_as_float(0x7fc00000);  // no valid index: NaN like the reference
-        } else {
-          const float sink2 = P.sink[h0 + hh] * LOG2E;
-          inv = 1.f / (l + exp2f(sink2 - m));
-        }
-        const int64_t obase = ((qi * P.h) + h0 + hh) * D;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-          const int d = dbase + nt * 8 + (lane & 3) * 2;
-          float v0 = o[mt][nt][hf * 2 + 0] * inv;
-          float v1 = o[mt][nt][hf * 2 + 1] * inv;
-          if (rope && d >= D - P.rope_dim) {
-            float c, sn;
-            rope_cos_sin(pos, P.rope_freqs[(d - (D - P.rope_dim)) >> 1], &c, &sn);
-            rotate_pair(v0, v1, c, sn, true, &v0, &v1);
-          }
-          if (P.out_dtype == DSV4_BF16) {
-            *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(P.out) + obase + d) =
-                pack_bf16x2(v0, v1);
-          } else {
-            *reinterpret_cast<float2*>(reinterpret_cast<float*>(P.out) + obase + d) = make_float2(v0, v1);
-          }
-        }
+        inv = (m == -INFINITY) ? __int_as_float(0x7fc00000)  // no valid index: NaN like the reference
+                               : 1.f / (sm.l_run[hh] + exp2f(P.sink[min(h0 + hh, P.h - 1)] * LOG2E - m));
       }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int d = warp * 64 + nt * 8 + (lane & 3) * 2;
+        *reinterpret_cast<float2*>(os + hh * OSTRIDE + d) =
+            make_float2(o[mt][nt][hf * 2 + 0] * inv, o[mt][nt][hf * 2 + 1] * inv);
+      }
+    }
+  __syncthreads();
+  if (final_out) {
+    const bool rope = P.rope_freqs != nullptr;
+    const int pos = rope ? P.positions[qi] : 0;
+#pragma unroll 1
+    for (int c = tid; c < HB * (D / 4); c += THREADS) {
+      const int hh = c / (D / 4), d = (c % (D / 4)) * 4;
+      if (hh >= heads_here) continue;
+      float4 v = *reinterpret_cast<const float4*>(os + hh * OSTRIDE + d);
+      if (rope && d >= D - P.rope_dim) {
+        const int f0 = (d - (D - P.rope_dim)) >> 1;
+        float c0, s0, c1, s1;
+        rope_cos_sin(pos, P.rope_freqs[f0], &c0, &s0);
+        rope_cos_sin(pos, P.rope_freqs[f0 + 1], &c1, &s1);
+        rotate_pair(v.x, v.y, c0, s0, true, &v.x, &v.y);
+        rotate_pair(v.z, v.w, c1, s1, true, &v.z, &v.w);
+      }
+      const int64_t off = ((qi * P.h) + h0 + hh) * D + d;
+      if (P.out_dtype == DSV4_BF16)
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(P.out) + off) =
+            make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+      else
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.out) + off) = v;
     }
   } else {
     const int64_t unit = (qi * P.hblocks + hblk) * P.splits + split;
     float* po = P.part + unit * (HB * D);
     float* pml = P.part + (P.s * P.hblocks * P.splits) * (int64_t)(HB * D) + unit * (HB * 2);
-#pragma unroll
-    for (int mt = 0; mt < 4; ++mt)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int hh = mt * 16 + hf * 8 + (lane >> 2);
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-          const int d = dbase + nt * 8 + (lane & 3) * 2;
-          *reinterpret_cast<float2*>(po + hh * D + d) =
-              make_float2(o[mt][nt][hf * 2 + 0], o[mt][nt][hf * 2 + 1]);
-        }
-      }
+#pragma unroll 1
+    for (int c = tid; c < HB * (D / 4); c += THREADS) {
+      const int hh = c / (D / 4), d = (c % (D / 4)) * 4;
+      *reinterpret_cast<float4*>(po + hh * D + d) = *reinterpret_cast<const float4*>(os + hh * OSTRIDE + d);
+    }
     if (tid < HB) {
       pml[tid * 2 + 0] = sm.m_run[cur][tid];
       pml[tid * 2 + 1] = sm.l_run[tid];
@@ -406,6 +408,8 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
 // One CTA of 128 threads per (query, head): each thread merges 4 consecutive dims over all splits,
 // with the split loop unrolled so the partial loads of different splits are in flight together.
 __global__ void __launch_bounds__(128) combine_kernel(Params P) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t unitq = blockIdx.x;             // qi * hblocks + hblk
   const int hh = blockIdx.y;
   const int64_t qi = unitq / P.hblocks;
@@ -505,13 +509,20 @@ DSV4_ERROR_READER(sparse_attn)
 
 using namespace dsv4;
 
-extern "C" size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p) {
-  if (!p || p->s <= 0 || p->h <= 0 || p->t <= 0) return 0;
+// workspace: [split partials (O, m, l)] [bf16 q after the fused norm/rope pre-pass]
+static size_t partial_bytes(const dsv4_sparse_attn_params* p) {
   const int splits = sa::choose_splits(p);
   if (splits <= 1) return 0;
   const int hblocks = (p->h + sa::HB - 1) / sa::HB;
   const int64_t units = p->s * hblocks * splits;
   return static_cast<size_t>(units) * (sa::HB * sa::D + sa::HB * 2) * sizeof(float);
+}
+
+extern "C" size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p) {
+  if (!p || p->s <= 0 || p->h <= 0 || p->t <= 0) return 0;
+  size_t bytes = (partial_bytes(p) + 255) / 256 * 256;
+  if (p->q_norm_rope) bytes += static_cast<size_t>(p->s) * p->h * p->d * 2;
+  return bytes;
 }
 
 extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) {
@@ -527,6 +538,8 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
   DSV4_CHECK_ARG(p->rope_freqs == nullptr || (p->positions != nullptr && p->rope_dim > 0 &&
                                                p->rope_dim <= 64 && p->rope_dim % 2 == 0),
                  "dsv4_sparse_attn: inverse rope needs positions and 0 < rope_dim <= 64");
+  DSV4_CHECK_ARG(!p->q_norm_rope || p->rope_freqs != nullptr,
+                 "dsv4_sparse_attn: the fused q norm/rope needs rope_freqs, positions and rope_dim");
   DSV4_CHECK_ARG(p->s * 64 < (int64_t)INT32_MAX, "dsv4_sparse_attn: too many queries per call");
   if (p->s == 0) return DSV4_OK;
   sa::Params P;
@@ -549,13 +562,33 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
   P.positions = p->positions;
   P.rope_dim = p->rope_dim;
   P.part = nullptr;
-  if (P.splits > 1) {
-    size_t need = dsv4_sparse_attn_workspace_size(p);
-    if (p->workspace == nullptr || p->workspace_bytes < need) {
-      set_error("dsv4_sparse_attn: workspace of %zu bytes needed, %zu given", need, p->workspace_bytes);
-      return DSV4_ERR_WORKSPACE;
-    }
-    P.part = reinterpret_cast<float*>(p->workspace);
+  const size_t need = dsv4_sparse_attn_workspace_size(p);
+  if (need > 0 && (p->workspace == nullptr || p->workspace_bytes < need)) {
+    set_error("dsv4_sparse_attn: workspace of %zu bytes needed, %zu given", need, p->workspace_bytes);
+    return DSV4_ERR_WORKSPACE;
+  }
+  if (P.splits > 1) P.part = reinterpret_cast<float*>(p->workspace);
+  if (p->q_norm_rope) {
+    // weightless per-head norm + rope of q into bf16 scratch, then attention reads it
+    void* qn = static_cast<char*>(p->workspace) + (partial_bytes(p) + 255) / 256 * 256;
+    dsv4_norm_rope_params n = {};
+    n.x = p->q;
+    n.weight = nullptr;
+    n.out = qn;
+    n.rows = p->s;
+    n.heads = p->h;
+    n.dim = p->d;
+    n.rope_dim = p->rope_dim;
+    n.x_dtype = p->q_dtype;
+    n.w_dtype = DSV4_F32;
+    n.out_dtype = DSV4_BF16;
+    n.eps = p->q_eps;
+    n.freqs = p->rope_freqs;
+    n.positions = p->positions;
+    const int st = dsv4_norm_rope(&n, stream);
+    if (st != DSV4_OK) return st;
+    P.q = qn;
+    P.q_dtype = DSV4_BF16;
   }
   static bool attr_set = false;
   const int smem = static_cast<int>(sizeof(sa::Smem));
@@ -564,12 +597,10 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
     attr_set = true;
   }
   dim3 grid(static_cast<unsigned>(P.s * P.splits), P.hblocks);
-  sa::sparse_attn_kernel<<<grid, sa::THREADS, smem, as_stream(stream)>>>(P);
-  DSV4_LAUNCH_CHECK("sparse_attn_kernel");
+  DSV4_CUDA_CHECK(launch_pdl(sa::sparse_attn_kernel, grid, dim3(sa::THREADS), smem, as_stream(stream), P));
   if (P.splits > 1) {
     dim3 g2(static_cast<unsigned>(P.s * P.hblocks), sa::HB);
-    sa::combine_kernel<<<g2, 128, 0, as_stream(stream)>>>(P);
-    DSV4_LAUNCH_CHECK("combine_kernel");
+    DSV4_CUDA_CHECK(launch_pdl(sa::combine_kernel, g2, dim3(128), 0, as_stream(stream), P));
   }
   return DSV4_OK;
 }

@@ -13,9 +13,10 @@ HBM and is addressed by index:
   k_idx       fp32 [batch, max_comp, 128]: indexer keys of the compressed entries
   ring_kv / ring_score fp32 [batch, 2*ratio, 1024]: the compressor's decode ring
 
-`decode_attention` is the measured decode path: per-head norm + RoPE of q, the window index list,
-the indexer top-k written straight into the attention index list, and sparse attention with the
-inverse RoPE fused into its epilogue.
+`decode_attention` is the measured decode path: on one stream, chained with programmatic dependent
+launch, the indexer scores, the top-k selection (which also writes the window rows) straight into
+the attention index list, sparse attention with the inverse RoPE fused into its epilogue, and the
+split-K merge; q's per-head norm + RoPE runs on a side stream beside the indexer.
 """
 import math
 
@@ -87,14 +88,30 @@ def decode_attention(cache, q, q_idx, w_idx, sink, positions, top_k=512, scale=N
     if freqs is None:
         freqs = rope_freqs(64, q.device)
     positions = positions.to(torch.int32).contiguous()
-    qr = norm_rope(q, positions, freqs, weight=None)
+    main = torch.cuda.current_stream(q.device)
+    side = _side_stream(q.device)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):          # q's norm + rope runs beside the indexer
+        qr = norm_rope(q, positions, freqs, weight=None)
     idx = idx_buf if idx_buf is not None else attention_index_buffer(b, cache.window, top_k, q.device)
-    L.check(L.lib().dsv4_decode_window_indices(b, cache.window, L.ptr(positions), L.ptr(cache.win_base),
-                                               L.ptr(idx), idx.shape[1], L.stream_of(q)))
     indexer_topk_into(idx.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
                       cache.k_idx, top_k, positions.view(b, 1), cache.ratio, out_col=cache.window,
-                      out_offset=cache.comp_base, block_table=cache.block_table, page=cache.page)
+                      out_offset=cache.comp_base, block_table=cache.block_table, page=cache.page,
+                      win_base=cache.win_base, window=cache.window)
+    main.wait_stream(side)
+    qr.record_stream(main)
     return sparse_attn_rope(qr, cache.kv_pool, sink, idx, scale, positions, freqs, 64, out_dtype)
+
+
+_side_streams = {}
+
+
+def _side_stream(device):
+    key = torch.device(device).index
+    st = _side_streams.get(key)
+    if st is None:
+        st = _side_streams[key] = torch.cuda.Stream(device)
+    return st
 
 
 class DecodeRunner:
@@ -102,7 +119,7 @@ class DecodeRunner:
 
     The first call captures `decode_attention` on static device buffers into a CUDA graph (the
     reference's per-token path is a Python loop of library calls, oracle/v4_fast.py:82-122; here one
-    graph launch replays the six kernels). `step_device` replays with inputs already on the device;
+    graph launch replays the five kernels). `step_device` replays with inputs already on the device;
     `step_host` copies this token's inputs from pinned host memory, replays, and copies the output
     back to pinned host memory, all ordered on the runner's stream.
     """

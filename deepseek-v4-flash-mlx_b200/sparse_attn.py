@@ -11,7 +11,8 @@ import torch
 from . import _lib as L
 
 
-def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_dim=0, num_splits=0):
+def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_dim=0, num_splits=0,
+                 q_norm_rope=False, q_eps=1e-6):
     p = L.SparseAttnParams()
     p.q, p.kv, p.sink, p.idx, p.out = L.ptr(q), L.ptr(kv), L.ptr(sink), L.ptr(idx), L.ptr(out)
     p.s, p.n, p.h, p.d, p.t = q.shape[0], kv.shape[0], q.shape[1], q.shape[2], idx.shape[-1]
@@ -21,13 +22,16 @@ def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_
     p.positions = L.ptr(positions) if positions is not None else None
     p.rope_dim = rope_dim
     p.num_splits = num_splits
+    p.q_norm_rope = int(q_norm_rope)
+    p.q_eps = q_eps
     return p
 
 
 @torch.library.custom_op("dsv4::sparse_attn", mutates_args=(), device_types="cuda")
 def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, topk_idxs: torch.Tensor,
                     scale: float, out_dtype: torch.dtype, rope_freqs: torch.Tensor | None,
-                    positions: torch.Tensor | None, rope_dim: int, num_splits: int) -> torch.Tensor:
+                    positions: torch.Tensor | None, rope_dim: int, num_splits: int,
+                    q_norm_rope: bool = False, q_eps: float = 1e-6) -> torch.Tensor:
     q = q.contiguous()
     kv = kv.contiguous()
     if kv.dtype != torch.bfloat16:
@@ -37,7 +41,7 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
     sink = attn_sink.float().contiguous()
     idx = topk_idxs.contiguous()
     out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
-    p = _attn_params(q, kv, sink, idx, out, scale, rope_freqs, positions, rope_dim, num_splits)
+    p = _attn_params(q, kv, sink, idx, out, scale, rope_freqs, positions, rope_dim, num_splits, q_norm_rope, q_eps)
     nbytes = L.lib().dsv4_sparse_attn_workspace_size(ctypes.byref(p))
     ws = L.workspace(nbytes, q.device)
     p.workspace, p.workspace_bytes = L.ptr(ws), nbytes
@@ -46,7 +50,8 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
 
 
 @_sparse_attn_op.register_fake
-def _(q, kv, attn_sink, topk_idxs, scale, out_dtype, rope_freqs, positions, rope_dim, num_splits):
+def _(q, kv, attn_sink, topk_idxs, scale, out_dtype, rope_freqs, positions, rope_dim, num_splits, q_norm_rope=False,
+      q_eps=1e-6):
     return torch.empty(q.shape, dtype=out_dtype, device=q.device)
 
 
@@ -70,6 +75,16 @@ def sparse_attn_rope(q, kv, attn_sink, topk_idxs, scale, positions, freqs, rope_
     L.require_cuda(q, kv, attn_sink, topk_idxs, positions, freqs)
     return _sparse_attn_op(q, kv, attn_sink, topk_idxs, float(scale), out_dtype, freqs.float().contiguous(),
                            positions.to(torch.int32).contiguous(), int(rope_dim), int(num_splits))
+
+
+def sparse_attn_decode(q_raw, kv, attn_sink, topk_idxs, scale, positions, freqs, rope_dim=64, eps=1e-6,
+                       out_dtype=torch.bfloat16, num_splits=0):
+    """The decode attention of oracle/v4_fast.py:88-119 in one op: q_raw (the q_up output) gets the
+    weightless per-head norm and RoPE at `positions` while it is staged, then sparse attention over
+    topk_idxs, then the inverse RoPE of the output in the epilogue."""
+    L.require_cuda(q_raw, kv, attn_sink, topk_idxs, positions, freqs)
+    return _sparse_attn_op(q_raw, kv, attn_sink, topk_idxs, float(scale), out_dtype, freqs.float().contiguous(),
+                           positions.to(torch.int32).contiguous(), int(rope_dim), int(num_splits), True, float(eps))
 
 
 @torch.library.custom_op("dsv4::get_window_topk_idxs", mutates_args=(), device_types="cuda")

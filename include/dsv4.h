@@ -88,6 +88,11 @@ typedef struct {
   int32_t num_splits;           /* 0 = automatic split of t across CTAs */
   void* workspace;
   size_t workspace_bytes;
+  /* optional fused q prologue: weightless per-head RMS norm (eps q_eps) of each q row, then RoPE of
+   * its last rope_dim dims at positions[i] with rope_freqs, applied while q is staged (the decode q
+   * chain of oracle/v4_fast.py:88-89); q is then the raw projection output */
+  int32_t q_norm_rope;
+  float q_eps;
 } dsv4_sparse_attn_params;
 
 DSV4_API size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p);
@@ -173,6 +178,11 @@ typedef struct {
   int32_t table_stride, page;
   void* workspace;
   size_t workspace_bytes;
+  /* optional: also write the decode window rows of query i (ring order of
+   * ref_torch/sparse_attn.py:11-15 at position positions[i], pool row win_base[b] + slot, -1 when the
+   * slot is not yet written) into out columns [out_col - window, out_col) */
+  const int64_t* win_base;
+  int32_t window;
 } dsv4_indexer_params;
 
 DSV4_API size_t dsv4_indexer_topk_workspace_size(const dsv4_indexer_params* p);
