@@ -16,6 +16,8 @@ from . import _lib
 from .compressor import compressor_decode_step, compressor_prefill
 from .decode import DecodeRunner, SparseMLACache, decode_attention
 from .indexer import indexer_scores, indexer_topk, indexer_topk_into
+from .layer import AttentionWeights, DecodeBlock, make_attention_weights, prefill_layer
+from .prefill import CompressorWeights, ShardedPrefill, sparse_mla_prefill
 from .mla import (N_GROUPS, N_HEADS, HEAD_DIM, O_LORA, ROPE_HD, QuantWeight, kv_proj, linear, o_grouped,
                   q_down, q_up, quantize_int8_g64)
 from .norm_rope import (apply_rotary_emb, norm_rope, perhead_norm, precompute_freqs, precompute_freqs_cis,
@@ -27,6 +29,8 @@ __all__ = [
     "rmsnorm", "perhead_norm", "apply_rotary_emb", "precompute_freqs", "precompute_freqs_cis", "norm_rope",
     "rope", "rope_freqs", "indexer_topk", "indexer_scores", "indexer_topk_into", "linear", "q_down", "q_up",
     "kv_proj", "o_grouped", "QuantWeight", "quantize_int8_g64", "SparseMLACache", "decode_attention", "DecodeRunner",
+    "AttentionWeights", "DecodeBlock", "make_attention_weights", "prefill_layer", "CompressorWeights", "ShardedPrefill",
+    "sparse_mla_prefill",
 ]
 
 

@@ -53,7 +53,8 @@ class IndexerParams(ctypes.Structure):
                 ("k_batch_stride", i64), ("positions", vp), ("ratio", i32),
                 ("out_stride", i32), ("out_col", i32), ("out_offset", i64),
                 ("block_table", vp), ("table_stride", i32), ("page", i32),
-                ("workspace", vp), ("workspace_bytes", sz), ("win_base", vp), ("window", i32)]
+                ("workspace", vp), ("workspace_bytes", sz), ("win_base", vp), ("window", i32),
+                ("window_linear", i32)]
 
 
 class CompressorParams(ctypes.Structure):

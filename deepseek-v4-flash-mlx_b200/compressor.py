@@ -35,12 +35,14 @@ def _pool(kv, score, ape, norm_w, out, head_dim, ratio, rope_dim, freqs, ring_kv
 
 def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_head_dim=64,
                        base=160000.0, original_seq_len=65536, factor=16, beta_fast=32, beta_slow=1,
-                       out_dtype=torch.float32):
+                       out_dtype=torch.float32, pos0=0):
     """x [b, s, dim] -> (kv [b, s//ratio, head_dim] post-rope, state).
 
     state: "kv" / "score" = the last full block's kv and score+ape [b, ratio, 2*head_dim] (when
     s >= ratio), "kv_rem" = the remainder rows, and "ring_kv" / "ring_score" [b, 2*ratio, 2*head_dim]
-    the device ring that `compressor_decode_step` continues from (ref_torch/compressor.py:67-74)."""
+    the device ring that `compressor_decode_step` continues from (ref_torch/compressor.py:67-74).
+    `pos0` is the position of x's first token (a slice of a longer sequence): row g is roped at
+    pos0 + ratio*g."""
     L.require_cuda(x, wkv, wgate, ape, norm_w)
     b, s, _ = x.shape
     d2 = 2 * head_dim
@@ -54,7 +56,7 @@ def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_h
     ring_score = torch.empty_like(ring_kv)
     nw = norm_w if norm_w.dtype in (torch.float32, torch.bfloat16) else norm_w.float()
     _pool(kv, score, ape.float().contiguous(), nw.contiguous(), out, head_dim, ratio, rope_head_dim, freqs,
-          ring_kv, ring_score)
+          ring_kv, ring_score, pos0=pos0)
     cutoff = s - s % ratio
     state = {"ring_kv": ring_kv, "ring_score": ring_score}
     if cutoff >= ratio:

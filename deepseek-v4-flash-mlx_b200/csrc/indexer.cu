@@ -152,6 +152,185 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
   }
 }
 
+// Query-tiled scores for prefill: one CTA per (64 queries, 64 keys) of one batch row, skipping tiles
+// the causal rule hides entirely. The 64x128 key tile stays in shared memory while the 64 heads
+// stream through: per head the query tile q[t0..t0+63][h][:] is staged with cp.async (double
+// buffered); each thread computes 4 queries x 4 keys of dot products with sequential fmaf chains
+// over the 128 dims and folds w[t][h] * relu(dot) into its head-group partial. Every four heads the
+// partial enters a binary-counter tree, which forms exactly the balanced tree over the 16 partials
+// of the canonical order (same pairs, same left/right operands).
+constexpr int TQ = 64, TK = 64;
+
+struct TiledSmem {
+  alignas(16) float k[TK * DI];          // swizzled 16-byte chunks
+  alignas(16) float q[2][TQ * DI];       // one head's query tile, double buffered
+  float w[TQ * HI];                      // w[t][h] of the query tile
+  int nvis[TQ];
+};
+
+__device__ __forceinline__ void add4x4(float (&dst)[4][4], const float (&a)[4][4], const float (&b)[4][4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[i][j] = __fadd_rn(a[i][j], b[i][j]);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) score_tiled_kernel(ScoreParams P) {
+  extern __shared__ __align__(16) uint8_t tiled_smem[];
+  TiledSmem& sm = *reinterpret_cast<TiledSmem*>(tiled_smem);
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.y * TQ;
+  const int j0 = blockIdx.x * TK;
+  const int64_t row0 = static_cast<int64_t>(b) * P.s + t0;           // first query row of the tile
+  const int t_cnt = min(TQ, P.s - t0);
+  if (tid < TQ) sm.nvis[tid] = tid < t_cnt ? visible_keys(P.positions, row0 + tid, P.ratio, P.n_keys) : 0;
+  __syncthreads();
+  int nvis_max = 0;
+#pragma unroll 8
+  for (int r = 0; r < TQ; ++r) nvis_max = max(nvis_max, sm.nvis[r]);
+  if (j0 >= nvis_max) return;
+
+  const float* kg = P.k + static_cast<int64_t>(b) * P.k_batch_stride * DI;
+  const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(sm.k));
+  for (int c = tid; c < TK * DI / 4; c += THREADS) {
+    const int r = c >> 5, ch = c & 31;
+    const bool valid = (j0 + r) < nvis_max;
+    cp_async16(ks + (r * 32 + swz_chunk(r, ch)) * 16, kg + static_cast<int64_t>(valid ? j0 + r : 0) * DI + ch * 4,
+               valid);
+  }
+  const uint32_t qs0 = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q[0]));
+  const uint32_t qs1 = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q[1]));
+  auto stage_q = [&](int h, uint32_t qs) {
+    for (int c = tid; c < TQ * DI / 4; c += THREADS) {
+      const int r = c >> 5, ch = c & 31;
+      const bool valid = r < t_cnt;
+      const float* src = P.q + ((row0 + (valid ? r : 0)) * HI + h) * DI + ch * 4;
+      cp_async16(qs + (r * 32 + swz_chunk(r, ch)) * 16, src, valid);
+    }
+  };
+  stage_q(0, qs0);
+  asm volatile("cp.async.commit_group;\n" ::);
+  for (int c = tid; c < TQ * HI; c += THREADS) sm.w[c] = (c / HI) < t_cnt ? P.w[(row0 + c / HI) * HI + c % HI] : 0.f;
+
+  // 16 x 16 thread grid; a warp covers 4 query groups x 8 key groups, so its shared-memory reads hit
+  // 4 (broadcast) query rows and 8 key rows in distinct bank groups
+  const int tq = ((warp >> 1) << 2) | (lane >> 3);
+  const int tk = ((warp & 1) << 3) | (lane & 7);
+  float part[4][4], l0[4][4], l1[4][4], l2[4][4], l3[4][4], fin[4][4];
+#pragma unroll 1
+  for (int h = 0; h < HI; ++h) {
+    if (h + 1 < HI) {
+      stage_q(h + 1, (h & 1) ? qs0 : qs1);
+      asm volatile("cp.async.commit_group;\n" ::);
+      asm volatile("cp.async.wait_group 1;\n" ::);
+    } else {
+      asm volatile("cp.async.wait_group 0;\n" ::);
+    }
+    __syncthreads();
+    const float* qt = sm.q[h & 1];
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+#pragma unroll 2
+    for (int ch = 0; ch < DI / 4; ++ch) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const int r = tq * 4 + a;
+        qv[a] = *reinterpret_cast<const float4*>(&qt[(r * 32 + swz_chunk(r, ch)) * 4]);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int r = tk * 4 + c;
+        kv[c] = *reinterpret_cast<const float4*>(&sm.k[(r * 32 + swz_chunk(r, ch)) * 4]);
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          acc[a][c] = __fmaf_rn(qv[a].x, kv[c].x, acc[a][c]);
+          acc[a][c] = __fmaf_rn(qv[a].y, kv[c].y, acc[a][c]);
+          acc[a][c] = __fmaf_rn(qv[a].z, kv[c].z, acc[a][c]);
+          acc[a][c] = __fmaf_rn(qv[a].w, kv[c].w, acc[a][c]);
+        }
+    }
+    // fold this head into the group partial (heads 4m..4m+3, from +0)
+    if ((h & 3) == 0) {
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) part[a][c] = 0.f;
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const float wv = sm.w[(tq * 4 + a) * HI + h];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float d = acc[a][c];
+        part[a][c] = __fmaf_rn(wv, d > 0.f ? d : 0.f, part[a][c]);
+      }
+    }
+    if ((h & 3) == 3) {
+      const int m = h >> 2;  // head group just completed: binary-counter insert
+      if (!(m & 1)) {
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) l0[a][c] = part[a][c];
+      } else {
+        add4x4(part, l0, part);
+        if (!(m & 2)) {
+#pragma unroll
+          for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) l1[a][c] = part[a][c];
+        } else {
+          add4x4(part, l1, part);
+          if (!(m & 4)) {
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) l2[a][c] = part[a][c];
+          } else {
+            add4x4(part, l2, part);
+            if (!(m & 8)) {
+#pragma unroll
+              for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) l3[a][c] = part[a][c];
+            } else {
+              add4x4(fin, l3, part);
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();  // q buffer (h & 1) is restaged two heads later
+  }
+  // write the visible scores of this thread's 4 queries x 4 keys
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int t = tq * 4 + a;
+    if (t >= t_cnt) continue;
+    const int nv = sm.nvis[t];
+    const int j = j0 + tk * 4;
+    float* dst = P.scores + (row0 + t) * P.n_pad + j;
+    if (j + 4 <= nv && (P.n_pad & 3) == 0) {
+      *reinterpret_cast<float4*>(dst) = make_float4(fin[a][0], fin[a][1], fin[a][2], fin[a][3]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (j + c < nv) dst[c] = fin[a][c];
+    }
+  }
+}
+
+
 // order-preserving image of an fp32 value (larger float -> larger unsigned)
 __device__ __forceinline__ uint32_t ordered_bits(float f) {
   uint32_t u = __float_as_uint(f);
@@ -169,8 +348,24 @@ struct SelectParams {
   const int32_t* block_table;
   int32_t table_stride, page;
   const int64_t* win_base;
-  int32_t window;
+  int32_t window, window_linear;
 };
+
+// window rows of a query at position p: decode ring order, or the prefill (linear) branch
+__device__ __forceinline__ int32_t window_row(const SelectParams& P, int b, int p, int c) {
+  const int W = P.window;
+  int slot;
+  if (P.window_linear) {
+    const int lo = p - W + 1 > 0 ? p - W + 1 : 0;
+    slot = (lo + c <= p) ? lo + c : -1;
+  } else if (p >= W - 1) {
+    const int sp = p % W;
+    slot = (c < W - sp - 1) ? (sp + 1 + c) : (c - (W - sp - 1));
+  } else {
+    slot = (c <= p) ? c : -1;
+  }
+  return slot < 0 ? -1 : static_cast<int32_t>(P.win_base[b] + slot);
+}
 
 constexpr int SEL_THREADS = 512;
 constexpr int SEL_MAX_KEYS = 32768;
@@ -246,19 +441,8 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
   int32_t* out = P.out + qrow * P.out_stride + P.out_col;
   const int k = P.top_k;
 
-  if (P.win_base != nullptr && tid < P.window) {
-    // decode window rows, ring order (slot -1 = not yet written)
-    const int p = P.positions[qrow];
-    const int W = P.window;
-    int slot;
-    if (p >= W - 1) {
-      const int sp = p % W;
-      slot = (tid < W - sp - 1) ? (sp + 1 + tid) : (tid - (W - sp - 1));
-    } else {
-      slot = (tid <= p) ? tid : -1;
-    }
-    out[tid - W] = slot < 0 ? -1 : static_cast<int32_t>(P.win_base[b] + slot);
-  }
+  if (P.win_base != nullptr)
+    for (int c = tid; c < P.window; c += SEL_THREADS) out[c - P.window] = window_row(P, b, P.positions[qrow], c);
   if (nvis <= k) {
     for (int r = tid; r < k; r += SEL_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
     return;
@@ -459,18 +643,8 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
   int32_t* out = P.out + qrow * P.out_stride + P.out_col;
   const int k = P.top_k;
 
-  if (P.win_base != nullptr && tid < P.window) {
-    const int p = P.positions[qrow];
-    const int W = P.window;
-    int slot;
-    if (p >= W - 1) {
-      const int sp = p % W;
-      slot = (tid < W - sp - 1) ? (sp + 1 + tid) : (tid - (W - sp - 1));
-    } else {
-      slot = (tid <= p) ? tid : -1;
-    }
-    out[tid - W] = slot < 0 ? -1 : static_cast<int32_t>(P.win_base[b] + slot);
-  }
+  if (P.win_base != nullptr)
+    for (int c = tid; c < P.window; c += SEL_THREADS) out[c - P.window] = window_row(P, b, P.positions[qrow], c);
   if (nvis <= k) {
     for (int r = tid; r < k; r += SEL_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
     return;
@@ -630,6 +804,30 @@ __global__ void decode_window_kernel(int32_t batch, int32_t window, const int32_
   }
 }
 
+// the query-tiled kernel when a batch row holds many queries (prefill), else one CTA per query
+inline cudaError_t launch_scores(const ScoreParams& S, cudaStream_t st) {
+  if (S.s >= TQ) {
+    static bool attr = false;
+    if (!attr) {
+      const cudaError_t e = cudaFuncSetAttribute(score_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 sizeof(TiledSmem));
+      if (e != cudaSuccess) return e;
+      attr = true;
+    }
+    const dim3 g((S.n_keys + TK - 1) / TK, (S.s + TQ - 1) / TQ, S.batch);
+    return launch_pdl(score_tiled_kernel, g, dim3(THREADS), sizeof(TiledSmem), st, S);
+  }
+  static bool attr1 = false;
+  if (!attr1) {
+    const cudaError_t e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               sizeof(ScoreSmem));
+    if (e != cudaSuccess) return e;
+    attr1 = true;
+  }
+  const dim3 g(static_cast<unsigned>(static_cast<int64_t>(S.batch) * S.s), (S.n_keys + KT - 1) / KT);
+  return launch_pdl(score_kernel, g, dim3(THREADS), sizeof(ScoreSmem), st, S);
+}
+
 // the register-resident kernel up to 16384 visible keys, the shared-memory one above
 inline cudaError_t launch_select(const SelectParams& L, unsigned rows, cudaStream_t st) {
   const dim3 g(rows), blk(SEL_THREADS);
@@ -676,7 +874,7 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
                  "dsv4_indexer_topk: block table needs page and table_stride");
   DSV4_CHECK_ARG(p->k_batch_stride >= p->n_keys || p->batch == 1,
                  "dsv4_indexer_topk: k_batch_stride smaller than n_keys");
-  DSV4_CHECK_ARG(p->win_base == nullptr || (p->positions != nullptr && p->window > 0 && p->window <= idx::SEL_THREADS &&
+  DSV4_CHECK_ARG(p->win_base == nullptr || (p->positions != nullptr && p->window > 0 &&
                                             p->out_col >= p->window),
                  "dsv4_indexer_topk: window columns need positions and out_col >= window");
   const int64_t rows = static_cast<int64_t>(p->batch) * p->s;
@@ -701,14 +899,7 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
   S.k_batch_stride = p->k_batch_stride;
   S.positions = p->positions;
   S.ratio = p->ratio;
-  dim3 g1(static_cast<unsigned>(rows), (p->n_keys + idx::KT - 1) / idx::KT);
-  static bool score_attr = false;
-  if (!score_attr) {
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(idx::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         sizeof(idx::ScoreSmem)));
-    score_attr = true;
-  }
-  DSV4_CUDA_CHECK(launch_pdl(idx::score_kernel, g1, dim3(idx::THREADS), sizeof(idx::ScoreSmem), as_stream(stream), S));
+  DSV4_CUDA_CHECK(idx::launch_scores(S, as_stream(stream)));
 
   idx::SelectParams L;
   L.scores = scores;
@@ -728,6 +919,7 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
   L.page = p->page;
   L.win_base = p->win_base;
   L.window = p->window;
+  L.window_linear = p->window_linear;
   DSV4_CUDA_CHECK(idx::launch_select(L, static_cast<unsigned>(rows), as_stream(stream)));
   return DSV4_OK;
 }
@@ -792,7 +984,7 @@ extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* str
                  "dsv4_indexer_topk_noalloc: block table needs page and table_stride");
   DSV4_CHECK_ARG(p->k_batch_stride >= p->n_keys || p->batch == 1,
                  "dsv4_indexer_topk_noalloc: k_batch_stride smaller than n_keys");
-  DSV4_CHECK_ARG(p->win_base == nullptr || (p->positions != nullptr && p->window > 0 && p->window <= idx::SEL_THREADS &&
+  DSV4_CHECK_ARG(p->win_base == nullptr || (p->positions != nullptr && p->window > 0 &&
                                             p->out_col >= p->window),
                  "dsv4_indexer_topk_noalloc: window columns need positions and out_col >= window");
   const int64_t rows = static_cast<int64_t>(p->batch) * p->s;
@@ -849,6 +1041,7 @@ extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* str
   L.page = p->page;
   L.win_base = p->win_base;
   L.window = p->window;
+  L.window_linear = p->window_linear;
   DSV4_CUDA_CHECK(idx::launch_select(L, static_cast<unsigned>(rows), as_stream(stream)));
   return DSV4_OK;
 }

@@ -14,7 +14,7 @@ from . import _lib as L
 
 
 def _params(q, w, k, out, top_k, positions, ratio, out_col, out_offset, block_table, page, scores_out,
-            win_base=None, window=0):
+            win_base=None, window=0, window_linear=False):
     b, s, h, di = q.shape
     p = L.IndexerParams()
     p.q, p.w, p.k, p.out = L.ptr(q), L.ptr(w), L.ptr(k), L.ptr(out)
@@ -29,6 +29,7 @@ def _params(q, w, k, out, top_k, positions, ratio, out_col, out_offset, block_ta
     p.page = page
     p.win_base = L.ptr(win_base) if win_base is not None else None
     p.window = window
+    p.window_linear = int(window_linear)
     return p
 
 
@@ -90,17 +91,17 @@ def indexer_scores(q_idx, w, k_idx, positions=None, ratio=4):
 
 
 def indexer_topk_into(out, q_idx, w, k_idx, top_k, positions=None, ratio=4, out_col=0, out_offset=0,
-                      block_table=None, page=0, win_base=None, window=0):
+                      block_table=None, page=0, win_base=None, window=0, window_linear=False):
     """Write the selection into columns [out_col, out_col+top_k) of an existing int32 index buffer
     out [b, s, T], mapping key j to pool row out_offset + j, or through a block table
     (block_table[b, j // page] * page + j % page + out_offset). Used by the decode and prefill
     pipelines to build the attention index list without a copy. With `win_base` (int64 [b]) the
-    decode window rows of each query (ring order at positions[b]) also go to columns
-    [out_col - window, out_col)."""
+    window rows of each query also go to columns [out_col - window, out_col): the decode ring order
+    at positions[b], or with window_linear the prefill rows win_base + max(0, p-window+1) .. p."""
     q_idx, w, k_idx, positions, _ = _prep(q_idx, w, k_idx, positions)
     if out.dtype != torch.int32 or not out.is_contiguous():
         raise TypeError("indexer_topk_into: out must be a contiguous int32 tensor")
     p = _params(q_idx, w, k_idx, out, int(top_k), positions, int(ratio), int(out_col), int(out_offset),
-                block_table, int(page), None, win_base, int(window))
+                block_table, int(page), None, win_base, int(window), window_linear)
     _run(p, q_idx.device, q_idx)
     return out

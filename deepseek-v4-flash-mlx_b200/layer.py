@@ -1,0 +1,183 @@
+"""The compressed sparse-MLA attention block: prefill (config 1) and decode (config 5).
+
+Prefill follows oracle/decode_engine.py:75-119 (without the hyper-connection mixing around it):
+  xn = RMSNorm(x); qa = RMSNorm(x_n Wq_a); q = RoPE(per-head-norm(qa Wq_b))
+  kv = RoPE(RMSNorm(xn Wkv))                       -> the window rows (token t is row t)
+  comp = compressor_prefill(xn, ...)               -> compressed rows (row s + j)
+  indexer: k_idx = compressor_prefill(xn, ... 128-wide), q_idx = RoPE(qa Wq_idx), w = xn Wproj
+  index list of query t = [rows max(0,t-127)..t | s + top-k compressed entries visible at t]
+  o = inverse-RoPE(sparse_attn(q, [kv; comp], sinks, list)); out = o_grouped(o, Wo_a, Wo_b)
+With top_k at least the visible count the list is exactly the reference's (all visible rows).
+
+Decode follows oracle/v4_fast.py:82-122: the token's kv row goes into its window ring slot, the
+compressor rings emit a compressed row (and an indexer key) every 4th token, then decode attention
+over the device-resident cache and the grouped output projection. Weights may be bf16 or
+8-bit grouped (`QuantWeight`, config 5).
+"""
+import math
+from dataclasses import dataclass, fields
+
+import torch
+
+from . import _lib as L
+from .compressor import compressor_decode_step, compressor_prefill
+from .configs import DIMS, LayerDims
+from .decode import SparseMLACache, decode_attention
+from .indexer import indexer_topk_into
+from .mla import QuantWeight, linear, o_grouped, quantize_int8_g64
+from .norm_rope import norm_rope, rmsnorm, rope, rope_freqs
+from .sparse_attn import sparse_attn_rope
+
+
+@dataclass
+class AttentionWeights:
+    attn_norm: torch.Tensor     # [dim]
+    wq_a: object                # [q_lora, dim]
+    q_a_norm: torch.Tensor      # [q_lora]
+    wq_b: object                # [heads*head_dim, q_lora]
+    wkv: object                 # [head_dim, dim]
+    kv_a_norm: torch.Tensor     # [head_dim]
+    sinks: torch.Tensor         # [heads]
+    wo_a: object                # [groups*o_lora, heads*head_dim/groups]
+    wo_b: object                # [dim, groups*o_lora]
+    c_wkv: object               # [2*head_dim, dim]  compressor
+    c_wgate: object             # [2*head_dim, dim]
+    c_ape: torch.Tensor         # [ratio, 2*head_dim]
+    c_norm: torch.Tensor        # [head_dim]
+    i_wq: object                # [idx_heads*idx_dim, q_lora]  indexer queries
+    i_wproj: object             # [idx_heads, dim]             indexer head weights
+    i_wkv: object               # [2*idx_dim, dim]             indexer-key compressor
+    i_wgate: object             # [2*idx_dim, dim]
+    i_ape: torch.Tensor         # [ratio, 2*idx_dim]
+    i_norm: torch.Tensor        # [idx_dim]
+
+    def to(self, device):
+        def mv(v):
+            if isinstance(v, QuantWeight):
+                return QuantWeight(v.q.to(device), v.scale.to(device))
+            return v.to(device)
+        return AttentionWeights(**{f.name: mv(getattr(self, f.name)) for f in fields(self)})
+
+
+MATRICES = ("wq_a", "wq_b", "wkv", "wo_a", "wo_b", "c_wkv", "c_wgate", "i_wq", "i_wproj", "i_wkv", "i_wgate")
+
+
+def make_attention_weights(seed, dims: LayerDims = DIMS, quant=False):
+    """Synthetic weights on the CPU: matrices ~N(0, 0.02) rounded to bf16 (or int8-g64 when
+    `quant`), norm weights 1 + N(0, 0.1), ape ~N(0, 0.1), sinks ~N(0, 1). The indexer head-weight
+    matrix carries the 1/sqrt(heads*idx_dim) score scale."""
+    g = torch.Generator().manual_seed(seed)
+    d, hd, ql = dims.dim, dims.head_dim, dims.q_lora
+
+    def mat(o, i, scale=0.02):
+        w = (torch.randn(o, i, generator=g) * scale).to(torch.bfloat16)
+        return quantize_int8_g64(w.float()) if quant else w
+
+    def vec(n, base=1.0, scale=0.1):
+        return base + torch.randn(n, generator=g) * scale
+
+    return AttentionWeights(
+        attn_norm=vec(d), wq_a=mat(ql, d), q_a_norm=vec(ql), wq_b=mat(dims.n_heads * hd, ql),
+        wkv=mat(hd, d), kv_a_norm=vec(hd), sinks=torch.randn(dims.n_heads, generator=g),
+        wo_a=mat(dims.n_groups * dims.o_lora, dims.n_heads * hd // dims.n_groups),
+        wo_b=mat(d, dims.n_groups * dims.o_lora),
+        c_wkv=mat(2 * hd, d), c_wgate=mat(2 * hd, d), c_ape=torch.randn(dims.ratio, 2 * hd, generator=g) * 0.1,
+        c_norm=vec(hd),
+        i_wq=mat(dims.idx_heads * dims.idx_dim, ql), i_wproj=mat(dims.idx_heads, d, 0.02 / math.sqrt(dims.idx_heads * dims.idx_dim) * 8),
+        i_wkv=mat(2 * dims.idx_dim, d), i_wgate=mat(2 * dims.idx_dim, d),
+        i_ape=torch.randn(dims.ratio, 2 * dims.idx_dim, generator=g) * 0.1, i_norm=vec(dims.idx_dim),
+    )
+
+
+def prefill_layer(x, W: AttentionWeights, top_k=512, dims: LayerDims = DIMS, return_aux=False):
+    """x [s, dim] (one sequence from position 0) -> out [s, dim] fp32 (and the int32 index list
+    [s, window + top_k] plus intermediates with return_aux)."""
+    L.require_cuda(x)
+    s = x.shape[0]
+    dev = x.device
+    freqs = rope_freqs(dims.rope_dim, dev)
+    pos = torch.arange(s, dtype=torch.int32, device=dev)
+    xn = rmsnorm(x, W.attn_norm)
+    qa = rmsnorm(linear(xn, W.wq_a, torch.float32), W.q_a_norm)
+    qraw = linear(qa, W.wq_b, torch.float32).view(s, dims.n_heads, dims.head_dim)
+    q = norm_rope(qraw, pos, freqs, weight=None, rope_dim=dims.rope_dim)                  # bf16
+    n_comp = s // dims.ratio
+    kvcat = torch.empty((s + n_comp, dims.head_dim), dtype=torch.bfloat16, device=dev)
+    kvcat[:s] = norm_rope(linear(xn, W.wkv, torch.float32), pos, freqs, weight=W.kv_a_norm, rope_dim=dims.rope_dim)
+    comp, _ = compressor_prefill(xn[None], W.c_wkv, W.c_wgate, W.c_ape, W.c_norm, head_dim=dims.head_dim,
+                                 ratio=dims.ratio, rope_head_dim=dims.rope_dim, out_dtype=torch.bfloat16)
+    kvcat[s:] = comp[0]
+    k_idx, _ = compressor_prefill(xn[None], W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, head_dim=dims.idx_dim,
+                                  ratio=dims.ratio, rope_head_dim=dims.rope_dim, out_dtype=torch.float32)
+    q_idx = rope(linear(qa, W.i_wq, torch.float32).view(s, dims.idx_heads, dims.idx_dim), pos, freqs,
+                 dims.rope_dim)
+    w_idx = linear(xn, W.i_wproj, torch.float32)
+    idx = torch.empty((1, s, dims.window + top_k), dtype=torch.int32, device=dev)
+    win_base = torch.zeros(1, dtype=torch.int64, device=dev)
+    indexer_topk_into(idx, q_idx[None], w_idx[None], k_idx.reshape(1, n_comp, dims.idx_dim), top_k,
+                      positions=pos[None], ratio=dims.ratio, out_col=dims.window, out_offset=s,
+                      win_base=win_base, window=dims.window, window_linear=True)
+    o = sparse_attn_rope(q, kvcat, W.sinks, idx[0], dims.head_dim ** -0.5, pos, freqs, dims.rope_dim)
+    out = o_grouped(o.reshape(s, -1), W.wo_a, W.wo_b)
+    if return_aux:
+        return out, dict(idx=idx[0], o=o, q_idx=q_idx, w_idx=w_idx, k_idx=k_idx, kvcat=kvcat, q=q)
+    return out
+
+
+class DecodeBlock:
+    """Device-resident decode state of one layer for a batch of sequences plus its weights
+    (config 5): `step(x, positions)` runs the whole attention block for one token per sequence."""
+
+    def __init__(self, W: AttentionWeights, batch, max_ctx, top_k=512, dims: LayerDims = DIMS, device="cuda",
+                 page=64, cache=None):
+        self.W, self.dims, self.top_k = W, dims, top_k
+        self.cache = cache if cache is not None else SparseMLACache(
+            batch, max_ctx // dims.ratio, window=dims.window, head_dim=dims.head_dim, idx_dim=dims.idx_dim,
+            ratio=dims.ratio, page=page, device=device)
+        self.freqs = rope_freqs(dims.rope_dim, device)
+        self.batch = batch
+        b = torch.arange(batch, device=device)
+        self._seq = b
+
+    def step(self, x, positions):
+        """x [b, dim] fp32/bf16, positions int32 [b] (position of this token) -> out [b, dim] fp32."""
+        d, W, c = self.dims, self.W, self.cache
+        b = x.shape[0]
+        pos = positions.to(torch.int32).contiguous()
+        xn = rmsnorm(x, W.attn_norm)
+        qa = rmsnorm(linear(xn, W.wq_a, torch.float32), W.q_a_norm)
+        qraw = linear(qa, W.wq_b, torch.float32).view(b, d.n_heads, d.head_dim)
+        # this token's kv row -> its window ring slot
+        win_rows = (c.win_base + pos.long() % d.window).contiguous()
+        kvp = linear(xn, W.wkv, torch.float32)
+        _norm_rope_into(kvp, W.kv_a_norm, pos, self.freqs, c.kv_pool, win_rows, d.rope_dim)
+        # compressor rings: a compressed row / an indexer key is emitted when (p+1) % ratio == 0
+        entry = torch.clamp((pos.long() + 1) // d.ratio - 1, min=0)
+        comp_rows = c.comp_base + c.block_table.long()[self._seq[:b], entry // c.page] * c.page + entry % c.page
+        compressor_decode_step(xn, W.c_wkv, W.c_wgate, W.c_ape, W.c_norm, c.ring_kv, c.ring_score, pos, c.kv_pool,
+                               comp_rows.contiguous(), head_dim=d.head_dim, ratio=d.ratio,
+                               rope_head_dim=d.rope_dim, freqs=self.freqs)
+        key_rows = (self._seq[:b] * c.max_comp + entry).contiguous()
+        compressor_decode_step(xn, W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, c.ring_k_idx, c.ring_s_idx, pos,
+                               c.k_idx.view(-1, d.idx_dim), key_rows, head_dim=d.idx_dim, ratio=d.ratio,
+                               rope_head_dim=d.rope_dim, freqs=self.freqs)
+        q_idx = rope(linear(qa, W.i_wq, torch.float32).view(b, d.idx_heads, d.idx_dim), pos, self.freqs, d.rope_dim)
+        w_idx = linear(xn, W.i_wproj, torch.float32)
+        o = decode_attention(c, qraw, q_idx, w_idx, W.sinks, pos, self.top_k, freqs=self.freqs)
+        return o_grouped(o.reshape(b, -1), W.wo_a, W.wo_b)
+
+
+def _norm_rope_into(x, weight, positions, freqs, pool, rows, rope_dim):
+    """RMSNorm(weight) + RoPE of x [b, dim] written as bf16 into pool rows `rows` (int64 [b])."""
+    p = L.NormRopeParams()
+    p.x, p.weight, p.out, p.out_rows = L.ptr(x), L.ptr(weight), L.ptr(pool), L.ptr(rows)
+    p.rows, p.heads, p.dim, p.rope_dim = x.shape[0], 1, x.shape[-1], rope_dim
+    p.x_dtype, p.w_dtype, p.out_dtype = L.dtype_code(x), L.dtype_code(weight), L.BF16
+    p.eps = 1e-6
+    p.freqs, p.positions = L.ptr(freqs), L.ptr(positions)
+    L.check(L.lib().dsv4_norm_rope(ctypes_byref(p), L.stream_of(x)))
+
+
+def ctypes_byref(p):
+    import ctypes
+    return ctypes.byref(p)

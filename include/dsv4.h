@@ -178,11 +178,14 @@ typedef struct {
   int32_t table_stride, page;
   void* workspace;
   size_t workspace_bytes;
-  /* optional: also write the decode window rows of query i (ring order of
-   * ref_torch/sparse_attn.py:11-15 at position positions[i], pool row win_base[b] + slot, -1 when the
-   * slot is not yet written) into out columns [out_col - window, out_col) */
+  /* optional: also write the window rows of query i into out columns [out_col - window, out_col):
+   * window_linear == 0: the decode ring order of ref_torch/sparse_attn.py:11-15 at position
+   *   positions[i], pool row win_base[b] + slot, -1 for slots not yet written;
+   * window_linear == 1: the prefill branch (ref_torch/sparse_attn.py:17-19), rows
+   *   win_base[b] + max(0, p - window + 1) + c, -1 where that exceeds p = positions[i] */
   const int64_t* win_base;
   int32_t window;
+  int32_t window_linear;
 } dsv4_indexer_params;
 
 DSV4_API size_t dsv4_indexer_topk_workspace_size(const dsv4_indexer_params* p);

@@ -10,7 +10,7 @@ import torch
 
 from . import indexer_ref as I
 from .norm_rope_ref import perhead_norm, rope_at
-from .sparse_attn_ref import sparse_attn
+from .sparse_attn_ref import sparse_attn, sparse_attn_chunked
 
 
 def window_slots(p, window=128):
@@ -43,3 +43,86 @@ def decode_attention_ref(kv_pool, win_base, comp_rows, k_idx, q, q_idx, w_idx, s
         all_idx.append(idx)
     out = torch.stack(outs)
     return (out, torch.stack(all_idx)) if return_indices else out
+
+
+# ---------------------------------------------------------------------------- full block
+def _w(v):
+    """fp32 value of a weight (bf16 tensor or an 8-bit grouped weight)."""
+    if hasattr(v, "q") and hasattr(v, "scale"):
+        return v.q.float() * v.scale.float().repeat_interleave(64, dim=-1)
+    return v.float()
+
+
+def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=512, idx_heads=64, idx_dim=128,
+                      rope_dim=64, groups=8, indexer_inputs=None):
+    """fp32 restatement of oracle/decode_engine.py:75-119 plus the indexer selection.
+    indexer_inputs=(q_idx, w_idx, k_idx) lets a test score the selection on given inputs.
+    Returns (out [s, dim], idx [s, window + top_k], o [s, heads, head_dim])."""
+    from .compressor_ref import compressor_prefill
+    from .mla_ref import o_grouped
+    from .norm_rope_ref import precompute_freqs, rmsnorm
+    s = x.shape[0]
+    f = precompute_freqs(rope_dim, 0, 65536, 160000.0, 16, 32, 1)
+    pos = torch.arange(s)
+    xn = rmsnorm(x.float(), W.attn_norm)
+    qa = rmsnorm(xn @ _w(W.wq_a).T, W.q_a_norm)
+    q = rope_at(perhead_norm((qa @ _w(W.wq_b).T).reshape(s, heads, head_dim)), pos, f, rope_dim)
+    kv = rope_at(rmsnorm(xn @ _w(W.wkv).T, W.kv_a_norm), pos, f, rope_dim)
+    comp, _ = compressor_prefill(xn[None], _w(W.c_wkv), _w(W.c_wgate), W.c_ape, W.c_norm, head_dim=head_dim,
+                                 ratio=ratio, rope_head_dim=rope_dim)
+    if indexer_inputs is None:
+        k_idx, _ = compressor_prefill(xn[None], _w(W.i_wkv), _w(W.i_wgate), W.i_ape, W.i_norm, head_dim=idx_dim,
+                                      ratio=ratio, rope_head_dim=rope_dim)
+        q_idx = rope_at((qa @ _w(W.i_wq).T).reshape(s, idx_heads, idx_dim), pos, f, rope_dim)
+        w_idx = xn @ _w(W.i_wproj).T
+        k_idx = k_idx[0]
+    else:
+        q_idx, w_idx, k_idx = indexer_inputs
+    sel = I.indexer_topk(q_idx.numpy()[None], w_idx.numpy()[None], k_idx.numpy()[None], top_k,
+                         positions=pos.numpy()[None], ratio=ratio)[0]
+    sel_t = torch.from_numpy(sel.astype("int64"))
+    win = torch.stack([torch.tensor([max(0, t - window + 1) + c if max(0, t - window + 1) + c <= t else -1
+                                     for c in range(window)]) for t in range(s)])
+    idx = torch.cat([win, torch.where(sel_t >= 0, sel_t + s, sel_t)], 1)
+    kvcat = torch.cat([kv, comp[0]], 0)
+    o = sparse_attn_chunked(q, kvcat, W.sinks, idx, head_dim ** -0.5)
+    o = rope_at(o, pos, f, rope_dim, inverse=True)
+    out = o_grouped(o.reshape(s, -1), _w(W.wo_a), _w(W.wo_b), groups=groups)
+    return out, idx, o
+
+
+def decode_block_ref(state, W, x, positions, top_k=512, window=128, ratio=4, heads=64, head_dim=512, idx_heads=64,
+                     idx_dim=128, rope_dim=64, groups=8):
+    """One decode token per sequence on host copies of the cache (oracle/v4_fast.py:82-122,
+    oracle/decode_engine.py:96-105). `state` = dict(pool, win_base, comp_rows(b, j), k_idx, ring_kv, ring_score,
+    ring_k, ring_s) and is updated in place. Returns out [b, dim]."""
+    from .compressor_ref import decode_ring_step
+    from .mla_ref import o_grouped
+    from .norm_rope_ref import precompute_freqs, rmsnorm
+    f = precompute_freqs(rope_dim, 0, 65536, 160000.0, 16, 32, 1)
+    b = x.shape[0]
+    xn = rmsnorm(x.float(), W.attn_norm)
+    qa = rmsnorm(xn @ _w(W.wq_a).T, W.q_a_norm)
+    qraw = (qa @ _w(W.wq_b).T).reshape(b, heads, head_dim)
+    kvp = rmsnorm(xn @ _w(W.wkv).T, W.kv_a_norm)
+    ckv, cgt = xn @ _w(W.c_wkv).T, xn @ _w(W.c_wgate).T
+    ikv, igt = xn @ _w(W.i_wkv).T, xn @ _w(W.i_wgate).T
+    q_idx = (qa @ _w(W.i_wq).T).reshape(b, idx_heads, idx_dim)
+    w_idx = xn @ _w(W.i_wproj).T
+    for i in range(b):
+        p = int(positions[i])
+        row = rope_at(kvp[i][None], torch.tensor([p]), f, rope_dim)[0]
+        state["pool"][int(state["win_base"][i]) + p % window] = row.to(torch.bfloat16).float()
+        emitted = decode_ring_step(state["ring_kv"][i], state["ring_score"][i], ckv[i], cgt[i], W.c_ape, W.c_norm, p, f,
+                                   ratio, rope_dim)
+        if emitted is not None:
+            e = (p + 1) // ratio - 1
+            state["pool"][int(state["comp_rows"](i, torch.tensor(e)))] = emitted.to(torch.bfloat16).float()
+        key = decode_ring_step(state["ring_k"][i], state["ring_s"][i], ikv[i], igt[i], W.i_ape, W.i_norm, p, f, ratio,
+                               rope_dim)
+        if key is not None:
+            state["k_idx"][i, (p + 1) // ratio - 1] = key
+        q_idx[i] = rope_at(q_idx[i][None], torch.tensor([p]), f, rope_dim)[0]
+    o = decode_attention_ref(state["pool"], state["win_base"], state["comp_rows"], state["k_idx"], qraw, q_idx, w_idx,
+                             W.sinks, positions, top_k, f, window=window, ratio=ratio, scale=head_dim ** -0.5)
+    return o_grouped(o.reshape(b, -1), _w(W.wo_a), _w(W.wo_b), groups=groups)

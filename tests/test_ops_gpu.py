@@ -169,7 +169,9 @@ def test_indexer_scores_bit_exact(dsv4):
 
 
 @pytest.mark.parametrize("b,s,n,k,causal", [(1, 1, 8192, 512, False), (4, 1, 2048, 512, False),
-                                            (1, 40, 700, 64, True), (2, 3, 300, 512, False)])
+                                            (1, 40, 700, 64, True), (2, 3, 300, 512, False),
+                                            (1, 200, 300, 32, True), (2, 130, 1000, 64, False),
+                                            (1, 64, 20000, 1024, False)])
 def test_indexer_topk_bit_exact(dsv4, b, s, n, k, causal):
     q, w, keys = _idx_inputs(b, s, n, b * 100 + s)
     pos = None
@@ -178,6 +180,17 @@ def test_indexer_topk_bit_exact(dsv4, b, s, n, k, causal):
     got = dsv4.indexer_topk(q.to(DEV), w.to(DEV), keys.to(DEV), k, None if pos is None else pos.to(DEV)).cpu().numpy()
     ref = I.indexer_topk(q.numpy(), w.numpy(), keys.numpy(), k, None if pos is None else pos.numpy())
     np.testing.assert_array_equal(got, ref)
+
+
+def test_indexer_scores_tiled_prefill_bit_exact(dsv4):
+    """The query-tiled (prefill) score kernel: causal visibility, partial query and key tiles."""
+    q, w, k = _idx_inputs(1, 150, 333, 17)
+    pos = torch.arange(1000, 1150, dtype=torch.int32)[None]       # visible counts 250..287
+    got = dsv4.indexer_scores(q.to(DEV), w.to(DEV), k.to(DEV), pos.to(DEV)).cpu().numpy()
+    for i in range(150):
+        nv = min((1000 + i + 1) // 4, 333)
+        ref = I.scores(q[0, i].numpy(), w[0, i].numpy(), k[0, :nv].numpy())
+        np.testing.assert_array_equal(got[0, i, :nv].view(np.uint32), ref.view(np.uint32), err_msg=f"query {i}")
 
 
 def test_indexer_ties_and_padding(dsv4):
