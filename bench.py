@@ -16,6 +16,8 @@ across GPUs with no collective; weak scaling).
 """
 import argparse
 import json
+
+import numpy as np
 import os
 import statistics
 import sys
@@ -29,13 +31,24 @@ sys.path.insert(0, ROOT)
 
 PKG = "deepseek-v4-flash-mlx_b200"
 METRIC = "sparse-MLA decode tok/s at 32K ctx (indexer + top-k + sparse attention + RoPE)"
+METRICS = {"c2": METRIC,
+           "c3": "sparse-MLA batched decode tok/s (indexer + top-k + sparse attention + RoPE)",
+           "c4": "sparse-MLA prefill tok/s at 64K ctx (compressors + indexer top-k + sparse attention)",
+           "c5": "full attention block decode tok/s (projections + compressor + indexer + sparse MLA + o_proj)"}
 CONFIGS = {
-    "c2": dict(batch=1, ctx=32768, top_k=512, seeds=lambda r, i: 1 + 7919 * r,
+    "c2": dict(batch=1, ctx=32768, top_k=512, seeds=lambda r, i: 1 + 7919 * r, strong=False,
                workload="config2: decode, batch 1, 32768-token context (8192 compressed + 128 window rows), "
                         "top-k 512, bf16 cache, fp32 indexer keys"),
-    "c3": dict(batch=64, ctx=8192, top_k=512, seeds=lambda r, i: 100 + i + 7919 * r,
-               workload="config3: batched decode, batch 64, 8192-token contexts (2048 compressed + 128 window "
-                        "rows each), top-k 512"),
+    "c3": dict(batch=64, ctx=8192, top_k=512, seeds=lambda r, i: 100 + i, strong=True,
+               workload="config3: batched decode, global batch 64 split across GPUs, 8192-token contexts "
+                        "(2048 compressed + 128 window rows each), top-k 512"),
+    "c4": dict(batch=1, ctx=65536, top_k=1024, seeds=lambda r, i: 2,
+               workload="config4: long prefill, 65536 tokens: KV + indexer-key compressors (16384 rows), indexer "
+                        "top-k 1024 causal, sparse attention over 128 window + 1024 rows; query-sharded with an NCCL "
+                        "all-gather of compressed KV and keys"),
+    "c5": dict(batch=32, ctx=16384, top_k=512, seeds=lambda r, i: 3 + i, strong=True,
+               workload="config5: full attention block decode, global batch 32 split across GPUs, 16384-token "
+                        "contexts, int8-g64 weights (bf16 scales), top-k 512"),
 }
 L2_BYTES = 126 * 1024 * 1024
 # kernels of one decode step: q norm/rope, indexer scores, top-k selection, sparse attention, split merge
@@ -129,7 +142,7 @@ def _barrier_max(x, world, device):
 # ------------------------------------------------------------------------------ CPU reference leg
 def cpu_reference(cfg_name, samples, threads=None):
     """Time the oracle port (torch fp32 + the C indexer restatement) on the host cores for a bounded
-    sample of decode tokens of the config; returns (tok/s, cores, description)."""
+    sample of the config's workload; returns (tok/s, cores, description)."""
     from oracle import layer_ref as LR
     from oracle import norm_rope_ref as NR
     cfgd = CONFIGS[cfg_name]
@@ -137,11 +150,15 @@ def cpu_reference(cfg_name, samples, threads=None):
     torch.set_num_threads(threads)
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     C = __import__("importlib").import_module(PKG + ".configs")
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    if cfg_name == "c4":
+        return _cpu_prefill(samples, threads)
+    if cfg_name == "c5":
+        return _cpu_block(samples, threads)
     batch = min(cfgd["batch"], samples)
     case = C.make_decode_case(batch, cfgd["ctx"], cfgd["top_k"], seeds=[cfgd["seeds"](0, i) for i in range(batch)],
                               device="cpu", shuffle_pages=True)
     pool, win_base, comp_rows = C.decode_case_host_pool(case)
-    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
     h = case.host
     LR.decode_attention_ref(pool, win_base, comp_rows, h["k_idx"][:1], h["q"][:1], h["q_idx"][:1], h["w_idx"][:1],
                             h["sink"], h["positions"][:1], cfgd["top_k"], f)  # warm-up
@@ -152,23 +169,82 @@ def cpu_reference(cfg_name, samples, threads=None):
     return batch / dt, threads, f"{batch} decode token(s) of {cfg_name} through the CPU oracle ({dt:.2f} s)"
 
 
+def _cpu_prefill(nq, threads):
+    """Config 4 per-token CPU cost: the two compressors over a 4096-token slice (per token), plus
+    the indexer over 16384 keys and attention over 1152 rows for nq queries at the end of the
+    65536-token sequence (per query)."""
+    import importlib
+    from oracle import compressor_ref as CR
+    from oracle import indexer_ref as I
+    from oracle import norm_rope_ref as NR
+    from oracle import sparse_attn_ref as SA
+    Lm = importlib.import_module(PKG + ".layer")
+    W = Lm.make_attention_weights(2)
+    g = torch.Generator().manual_seed(2)
+    xs = torch.randn(4096, 4096, generator=g)
+    t0 = time.perf_counter()
+    CR.compressor_prefill(xs[None], W.c_wkv.float(), W.c_wgate.float(), W.c_ape, W.c_norm)
+    CR.compressor_prefill(xs[None], W.i_wkv.float(), W.i_wgate.float(), W.i_ape, W.i_norm, head_dim=128)
+    t_comp = (time.perf_counter() - t0) / 4096
+    s = 65536
+    keys = torch.randn(16384, 128, generator=g)
+    qi = torch.randn(nq, 64, 128, generator=g)
+    wi = torch.randn(nq, 64, generator=g) / 8
+    q = torch.randn(nq, 64, 512, generator=g)
+    kvcat = torch.randn(s + 16384, 512, generator=g).to(torch.bfloat16).float()
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    pos = np.arange(s // 2 - nq, s // 2)   # mid-sequence queries: the average visible key count
+    t0 = time.perf_counter()
+    sel = I.indexer_topk(qi.numpy()[None], wi.numpy()[None], keys.numpy()[None], 1024, positions=pos[None], ratio=4)[0]
+    win = np.stack([np.arange(t - 127, t + 1) for t in pos])
+    idx = torch.from_numpy(np.concatenate([win, sel + s], 1).astype(np.int64))
+    o = SA.sparse_attn_chunked(q, kvcat, W.sinks, idx, 512 ** -0.5, chunk=16)
+    NR.rope_at(o, torch.from_numpy(pos), f, inverse=True)
+    t_q = (time.perf_counter() - t0) / nq
+    return 1.0 / (t_comp + t_q), threads, (f"oracle port: compressors over 4096 tokens ({t_comp * 4096:.2f} s) + "
+                                          f"indexer/attention for {nq} queries at position 32K, the sequence's "
+                                          f"average ({t_q * nq:.2f} s)")
+
+
+def _cpu_block(nseq, threads):
+    """Config 5 per-token CPU cost: the oracle decode block (dequantised int8 weights in fp32)."""
+    import importlib
+    from oracle import layer_ref as LR
+    Lm = importlib.import_module(PKG + ".layer")
+    C = importlib.import_module(PKG + ".configs")
+    W = Lm.make_attention_weights(3, quant=True)
+    case = C.make_decode_case(nseq, 16384, 512, seeds=[3 + i for i in range(nseq)], device="cpu")
+    pool, win_base, comp_rows = C.decode_case_host_pool(case)
+    c = case.cache
+    state = dict(pool=pool.float(), win_base=win_base, comp_rows=comp_rows, k_idx=c.k_idx.clone(),
+                 ring_kv=c.ring_kv.clone(), ring_score=c.ring_score.clone(), ring_k=c.ring_k_idx.clone(),
+                 ring_s=c.ring_s_idx.clone())
+    x = torch.randn(nseq, 4096, generator=torch.Generator().manual_seed(3))
+    pos = torch.full((nseq,), 16383, dtype=torch.int32)
+    t0 = time.perf_counter()
+    LR.decode_block_ref(state, W, x, pos, top_k=512)
+    dt = time.perf_counter() - t0
+    return nseq / dt, threads, f"{nseq} token(s) of the config-5 block through the CPU oracle ({dt:.2f} s)"
+
+
 def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
         return
     cfgd = CONFIGS[args.config]
     per_step = []
-    n_tok = 1
+    n_tok = 64 if args.config == "c4" else 1
     for _ in range(max(1, args.warmup // 100)):
         cpu_reference(args.config, n_tok)
     for _ in range(min(args.steps, 3)):
         v, cores, desc = cpu_reference(args.config, n_tok)
         per_step.append(v)
     v = statistics.median(per_step)
-    line = {"impl": "reference", "metric": METRIC if args.config == "c2" else METRIC.replace("at 32K ctx", "batched"),
+    line = {"impl": "reference", "metric": METRICS[args.config],
             "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": len(per_step), "warmup": args.warmup,
-            "ms_per_step": 1000.0 * n_tok / v * (cfgd["batch"] // n_tok if args.config == "c3" else 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "ms_per_step": 1000.0 * (cfgd["ctx"] if args.config == "c4" else cfgd["batch"]) / v,
+            "higher_is_better": True, "scaling": "strong" if cfgd.get("strong") or args.config == "c4" else "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfgd["workload"], "global_batch": cfgd["batch"], "ctx": cfgd["ctx"],
                        "parallelism": "cpu"},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
@@ -181,13 +257,18 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2400)
-    ap.add_argument("--warmup", type=int, default=240)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="dsv4", choices=["dsv4", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--replicas", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    args.steps_given, args.warmup_given = args.steps is not None, args.warmup is not None
+    if args.steps is None:
+        args.steps = 2400
+    if args.warmup is None:
+        args.warmup = 240
     if args.impl == "reference":
         return run_reference(args)
 
@@ -201,15 +282,22 @@ def main():
     dsv4 = _pkg()
     C = __import__("importlib").import_module(PKG + ".configs")
     cfgd = CONFIGS[args.config]
+    if args.config == "c4":
+        return bench_prefill(args, world, rank, local, dev)
+    if args.config == "c5":
+        return bench_block(args, world, rank, local, dev)
     batch, ctx, top_k = cfgd["batch"], cfgd["ctx"], cfgd["top_k"]
+    if cfgd.get("strong"):
+        batch = max(1, batch // world)
 
     # ---- replicas of the whole decode state, rotating so that no step starts with warm L2
-    probe = C.make_decode_case(batch, ctx, top_k, seeds=[cfgd["seeds"](rank, i) for i in range(batch)], device=dev)
+    seed_of = (lambda i: cfgd["seeds"](rank, rank * batch + i)) if cfgd.get("strong") else (lambda i: cfgd["seeds"](rank, i))
+    probe = C.make_decode_case(batch, ctx, top_k, seeds=[seed_of(i) for i in range(batch)], device=dev)
     c = probe.cache
     footprint = (c.kv_pool.numel() * 2 + c.k_idx.numel() * 4 + c.block_table.numel() * 4)
     R = args.replicas or max(2, -(-2 * L2_BYTES // footprint) + 1)
-    cases = [probe] + [C.make_decode_case(batch, ctx, top_k, seeds=[cfgd["seeds"](rank, i) + 104729 * r
-                                                                   for i in range(batch)], device=dev)
+    cases = [probe] + [C.make_decode_case(batch, ctx, top_k, seeds=[seed_of(i) + 104729 * r for i in range(batch)],
+                                          device=dev)
                        for r in range(1, R)]
     runners = []
     for cs in cases:
@@ -306,9 +394,10 @@ def main():
         cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
 
     if rank == 0:
-        line = {"metric": METRIC if args.config == "c2" else METRIC.replace("at 32K ctx", "batched"),
+        line = {"metric": METRICS[args.config],
                 "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "strong" if cfgd.get("strong") else "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": cfgd["workload"], "global_batch": batch * world, "ctx": ctx, "top_k": top_k,
                            "parallelism": f"batch-split x{world} (no collective)" if world > 1 else "single GPU",
@@ -317,6 +406,270 @@ def main():
                            "cuda_graph": True},
                 "gpu_launches": LAUNCHES_PER_STEP * args.steps,
                 "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+# ------------------------------------------------------------------------------ config 4 (long prefill)
+def _phase_events(n):
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def bench_prefill(args, world, rank, local, dev):
+    """Config 4: one step = the sparse-MLA prefill core over 65536 tokens (strong scaling: the
+    same sequence split over the ranks; the compressed cache is all-gathered)."""
+    import importlib
+    P = importlib.import_module(PKG + ".prefill")
+    Lm = importlib.import_module(PKG + ".layer")
+    cfgd = CONFIGS["c4"]
+    s, top_k = cfgd["ctx"], cfgd["top_k"]
+    steps = args.steps if args.steps_given else 5
+    warmup = max(3, args.warmup if args.warmup_given else 3)
+    W = Lm.make_attention_weights(2).to(dev)
+    cw = P.CompressorWeights.from_attention_weights(W)
+    g = torch.Generator(device=dev).manual_seed(2)
+    x = torch.randn(s, 4096, device=dev, generator=g).to(torch.bfloat16)
+    q = torch.randn(s, 64, 512, device=dev, generator=g).to(torch.bfloat16)
+    kv = torch.randn(s, 512, device=dev, generator=g).to(torch.bfloat16)
+    qi = torch.randn(s, 64, 128, device=dev, generator=g)
+    wi = torch.randn(s, 64, device=dev, generator=g) / 8
+    sharded = P.ShardedPrefill() if world > 1 else None
+    ranges = P.zigzag_ranges(s, world, rank) if world > 1 else [(0, s)]
+    g0, g1 = P.block_range(s // 4, world, rank)
+    phases = {"compress": 0.0, "gather": 0.0, "indexer+attention": 0.0}
+
+    def step(record=False):
+        ev = _phase_events(4) if record else None
+        if ev:
+            ev[0].record()
+        comp_l, keys_l = P.compress_range(x, cw, g0, g1)
+        if ev:
+            ev[1].record()
+        if sharded is not None:
+            comp, keys = sharded.gather_cache(comp_l, keys_l, s // 4)
+        else:
+            comp, keys = comp_l, keys_l
+        if ev:
+            ev[2].record()
+        outs = [P.attend_queries(q[a:b], qi[a:b], wi[a:b], kv, comp, keys, W.sinks, a, b, top_k, 8192)
+                for a, b in ranges]
+        if ev:
+            ev[3].record()
+        return outs, ev
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.05)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = _barrier_max(e0.elapsed_time(e1), world, dev) / steps
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    _, ev = step(record=True)
+    torch.cuda.synchronize()
+    phases = {"compress": ev[0].elapsed_time(ev[1]), "gather": ev[1].elapsed_time(ev[2]),
+              "indexer+attention": ev[2].elapsed_time(ev[3])}
+    # attention-only timing on this rank's queries for the tensor roofline (indices precomputed)
+    att_ms, att_flops = _prefill_attention_time(P, x, q, qi, wi, kv, W, cw, ranges, s, top_k, dev)
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {"bf16_tflops": 1590.0}
+    achieved = att_flops / (att_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": "sa::sparse_attn_kernel", "achieved": achieved,
+                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                "peak_source": "measured" if "when" in peaks else "fallback", "traffic": None,
+                "algorithmic_flops_per_launch": att_flops, "phases_ms": phases}
+    # e2e: this rank's inputs from pinned host memory, the step, its outputs back
+    hx = x.cpu().pin_memory()
+    hq = [q[a:b].cpu().pin_memory() for a, b in ranges]
+    hqi = [qi[a:b].cpu().pin_memory() for a, b in ranges]
+    hw = [wi[a:b].cpu().pin_memory() for a, b in ranges]
+    hkv = kv.cpu().pin_memory()
+    ho = [torch.empty((b - a, 64, 512), dtype=torch.bfloat16).pin_memory() for a, b in ranges]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    h2d = d2h = 0
+    for _ in range(steps):
+        x.copy_(hx, non_blocking=True)
+        kv.copy_(hkv, non_blocking=True)
+        h2d = hx.numel() * 2 + hkv.numel() * 2
+        for i, (a, b) in enumerate(ranges):
+            q[a:b].copy_(hq[i], non_blocking=True)
+            qi[a:b].copy_(hqi[i], non_blocking=True)
+            wi[a:b].copy_(hw[i], non_blocking=True)
+            h2d += hq[i].numel() * 2 + hqi[i].numel() * 4 + hw[i].numel() * 4
+        outs, _ = step()
+        d2h = 0
+        for i, o in enumerate(outs):
+            ho[i].copy_(o, non_blocking=True)
+            d2h += o.numel() * 2
+    f1.record()
+    torch.cuda.synchronize()
+    ems = _barrier_max(f0.elapsed_time(f1), world, dev) / steps
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, desc = cpu_reference("c4", 64)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
+    if rank == 0:
+        line = {"metric": METRICS["c4"], "value": s / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+                "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": cfgd["workload"], "global_batch": 1, "seq_len": s, "top_k": top_k,
+                           "parallelism": f"query-sharded x{world} (zig-zag) + NCCL all-gather" if world > 1
+                           else "single GPU", "l2": "inputs (~7 GB) larger than L2"},
+                "gpu_launches": None,
+                "e2e": {"value": s / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h, "path": "host inputs -> prefill core -> host outputs"},
+                "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def _prefill_attention_time(P, x, q, qi, wi, kv, W, cw, ranges, s, top_k, dev):
+    """CUDA-event time of the sparse attention kernels alone over this rank's queries (index lists
+    built beforehand). FLOPs = sum over queries of 64 heads x valid rows x 512 x 4 (QK^T and PV)."""
+    import importlib
+    IX = importlib.import_module(PKG + ".indexer")
+    SA = importlib.import_module(PKG + ".sparse_attn")
+    NRm = importlib.import_module(PKG + ".norm_rope")
+    comp, keys = P.compress_range(x, cw, 0, s // 4)
+    kvcat = torch.cat([kv, comp])
+    freqs = NRm.rope_freqs(64, dev)
+    win_base = torch.zeros(1, dtype=torch.int64, device=dev)
+    chunks = []
+    for a, b in ranges:
+        for c0 in range(a, b, 8192):
+            c1 = min(b, c0 + 8192)
+            pos = torch.arange(c0, c1, dtype=torch.int32, device=dev)
+            idx = torch.empty((1, c1 - c0, 128 + top_k), dtype=torch.int32, device=dev)
+            IX.indexer_topk_into(idx, qi[c0:c1][None], wi[c0:c1][None], keys[None], top_k, positions=pos[None],
+                                 ratio=4, out_col=128, out_offset=s, win_base=win_base, window=128, window_linear=True)
+            chunks.append((c0, c1, pos, idx[0]))
+    flops = 0
+    for c0, c1, _, _ in chunks:
+        t = torch.arange(c0, c1, dtype=torch.int64)
+        rows = torch.clamp(t + 1, max=128) + torch.clamp((t + 1) // 4, max=top_k)
+        flops += int(rows.sum()) * 64 * 512 * 4
+    for c0, c1, pos, idx in chunks:  # warm-up
+        SA.sparse_attn_rope(q[c0:c1], kvcat, W.sinks, idx, 512 ** -0.5, pos, freqs, 64)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for c0, c1, pos, idx in chunks:
+        SA.sparse_attn_rope(q[c0:c1], kvcat, W.sinks, idx, 512 ** -0.5, pos, freqs, 64)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1), flops
+
+
+# ------------------------------------------------------------------------------ config 5 (decode block)
+def bench_block(args, world, rank, local, dev):
+    """Config 5: one step = the whole attention block for one token of each sequence (global batch
+    32 split over the ranks), int8-g64 weights, captured in a CUDA graph."""
+    import importlib
+    Lm = importlib.import_module(PKG + ".layer")
+    C = importlib.import_module(PKG + ".configs")
+    M = importlib.import_module(PKG + ".mla")
+    cfgd = CONFIGS["c5"]
+    B, ctx, top_k = max(1, cfgd["batch"] // world), cfgd["ctx"], cfgd["top_k"]
+    steps = args.steps if args.steps_given else 200
+    warmup = max(3, args.warmup if args.warmup_given else 20)
+    W = Lm.make_attention_weights(3, quant=True).to(dev)
+    case = C.make_decode_case(B, ctx, top_k, seeds=[cfgd["seeds"](rank, rank * B + i) for i in range(B)], device=dev)
+    blk = Lm.DecodeBlock(W, B, ctx, top_k=top_k, cache=case.cache)
+    g = torch.Generator().manual_seed(3 + rank)
+    x = torch.randn(B, 4096, generator=g).to(dev)
+    pos = torch.full((B,), ctx - 1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        blk.step(x, pos)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        out = blk.step(x, pos)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.05)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = _barrier_max(e0.elapsed_time(e1), world, dev) / steps
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    # e2e: this token's hidden states from pinned host memory, the graph, the block output back
+    hx = x.cpu().pin_memory()
+    ho = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            x.copy_(hx, non_blocking=True)
+            graph.replay()
+            ho.copy_(out, non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ems = _barrier_max(f0.elapsed_time(f1), world, dev) / steps
+    # algorithmic HBM bytes of one step: every weight once, the visible indexer keys, the gathered rows
+    wbytes = 0
+    for name in Lm.MATRICES:
+        w = getattr(W, name)
+        wbytes += (w.q.numel() + w.scale.numel() * 2) if isinstance(w, M.QuantWeight) else w.numel() * w.element_size()
+    nvis = min(ctx // 4, case.cache.max_comp)
+    step_bytes = wbytes + B * (nvis * 128 * 4 + (128 + top_k) * 1024)
+    peak, peak_kind = _peaks()
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "whole block step", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                "algorithmic_bytes_per_launch": step_bytes}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, desc = cpu_reference("c5", 1)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
+    if rank == 0:
+        line = {"metric": METRICS["c5"], "value": cfgd["batch"] / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+                "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": cfgd["workload"], "global_batch": cfgd["batch"], "ctx": ctx, "top_k": top_k,
+                           "parallelism": f"batch-split x{world} (no collective)" if world > 1 else "single GPU",
+                           "l2": f"weights + caches {step_bytes / 2**20:.0f} MiB per step > L2", "cuda_graph": True},
+                "gpu_launches": None,
+                "e2e": {"value": cfgd["batch"] / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": hx.numel() * 4,
+                        "d2h_bytes_per_step": ho.numel() * 4, "path": "host hidden states -> block graph -> host"},
+                "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
