@@ -686,6 +686,8 @@ def kernel_times(dsv4, cases, runners, stream, dev, n):
     b = cases[0].cache.batch
     top_k = runners[0].top_k
     freqs = runners[0].freqs
+    NRm = importlib.import_module(PKG + ".norm_rope")
+    qn = [NRm.norm_rope(r.q, r.positions, freqs) for r in runners]
     torch.cuda.synchronize()
     nvis = [min((int(c.host["positions"][i]) + 1) // 4, c.cache.max_comp) for c in cases[:1] for i in range(b)]
     n_keys = sum(nvis)
@@ -693,15 +695,15 @@ def kernel_times(dsv4, cases, runners, stream, dev, n):
         # score + select (which also writes the window rows): k_idx read once, indices written
         "indexer_topk": (lambda i: IX.indexer_topk_into(runners[i].idx.view(b, 1, -1), runners[i].q_idx.view(b, 1, 64, 128),
                                                         runners[i].w_idx.view(b, 1, 64), cases[i].cache.k_idx, top_k,
-                                                        runners[i].positions.view(b, 1), 4, out_col=128,
+                                                        runners[i].positions.view(b, 1), 4, out_col=0,
                                                         out_offset=cases[i].cache.comp_base,
-                                                        block_table=cases[i].cache.block_table, page=cases[i].cache.page,
-                                                        win_base=cases[i].cache.win_base, window=128),
-                         n_keys * 128 * 4 + b * (64 * 128 * 4 + 64 * 4 + (128 + top_k) * 4)),
-        # attention (+ split merge): gathered rows, raw q in, o out, indices
-        "sparse_attn": (lambda i: SA.sparse_attn_decode(runners[i].q, cases[i].cache.kv_pool, cases[i].sink,
-                                                        runners[i].idx, 512 ** -0.5, runners[i].positions, freqs, 64),
-                        b * ((128 + top_k) * (512 * 2 + 4) + 64 * 512 * 4 + 64 * 512 * 2)),
+                                                        block_table=cases[i].cache.block_table, page=cases[i].cache.page),
+                         n_keys * 128 * 4 + b * (64 * 128 * 4 + 64 * 4 + top_k * 4)),
+        # attention (+ split merge): gathered rows, normed q in, o out, indices
+        "sparse_attn": (lambda i: SA.sparse_attn_rope(qn[i], cases[i].cache.kv_pool, cases[i].sink, runners[i].idx,
+                                                      512 ** -0.5, runners[i].positions, freqs, 64,
+                                                      win_base=cases[i].cache.win_base, window=128),
+                        b * ((128 + top_k) * 512 * 2 + top_k * 4 + 64 * 512 * 2 * 2)),
     }
     out = {}
     for name, (fn, nbytes) in funcs.items():

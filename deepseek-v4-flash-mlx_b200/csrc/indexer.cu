@@ -21,7 +21,7 @@ namespace idx {
 
 constexpr int DI = 128;         // indexer head dim
 constexpr int HI = 64;          // indexer heads
-constexpr int KT = 64;          // keys per score CTA
+constexpr int KT = 32;          // keys per score CTA (decode)
 constexpr int THREADS = 256;
 
 struct ScoreSmem {
@@ -56,14 +56,19 @@ __device__ __forceinline__ int visible_keys(const int32_t* positions, int64_t qr
   return nv < n_keys ? (nv < 0 ? 0 : nv) : n_keys;
 }
 
-// grid: (batch*s, key tiles). Thread layout: lane = hq_lo<<3 | jq_lo, warp = hq_hi<<1 | jq_hi,
-// so a thread owns heads 4*hq..4*hq+3 and keys 4*jq..4*jq+3 of the tile.
+// grid: (batch*s, key tiles of KT = 32). 256 threads: thread = (head quad hq, key pair jq);
+// lane = hq_lo<<3 | jq_lo, warp = hq_hi<<1 | jq_hi, so a thread owns heads 4*hq..4*hq+3 and keys
+// 2*jq, 2*jq+1 of the tile. Two keys per thread (rather than four) doubles the threads of a decode
+// query (8192 keys -> 256 CTAs) so that each SM holds enough warps to hide FMA and shared-memory
+// latency; the fp32 operation order per (head, key) is unchanged.
+__device__ __forceinline__ int swz_pair(int r, int c) { return c ^ ((r >> 1) & 7); }
+
 __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
   extern __shared__ __align__(16) uint8_t score_smem[];
   ScoreSmem& sm = *reinterpret_cast<ScoreSmem*>(score_smem);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_trigger();
   pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t qrow = blockIdx.x;
   const int b = static_cast<int>(qrow / P.s);
   const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
@@ -76,13 +81,13 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
   const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(sm.k));
   for (int c = tid; c < HI * DI / 4; c += THREADS) {
     int r = c >> 5, ch = c & 31;
-    cp_async16(qs + (r * 32 + swz_chunk(r, ch)) * 16, qg + r * DI + ch * 4, true);
+    cp_async16(qs + (r * 32 + swz_pair(r, ch)) * 16, qg + r * DI + ch * 4, true);
   }
   for (int c = tid; c < KT * DI / 4; c += THREADS) {
     int r = c >> 5, ch = c & 31;
     bool valid = (j0 + r) < nvis;
     const float* src = kg + static_cast<int64_t>(valid ? j0 + r : 0) * DI + ch * 4;
-    cp_async16(ks + (r * 32 + swz_chunk(r, ch)) * 16, src, valid);
+    cp_async16(ks + (r * 32 + swz_pair(r, ch)) * 16, src, valid);
   }
   asm volatile("cp.async.commit_group;\n" ::);
   if (tid < HI) sm.w[tid] = P.w[qrow * HI + tid];
@@ -91,29 +96,29 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
 
   const int hq = ((warp >> 1) << 2) | (lane >> 3);
   const int jq = ((warp & 1) << 3) | (lane & 7);
-  float acc[4][4];
+  float acc[4][2];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+    for (int c = 0; c < 2; ++c) acc[a][c] = 0.f;
 
-#pragma unroll 2
+#pragma unroll 4
   for (int ch = 0; ch < DI / 4; ++ch) {
-    float4 qv[4], kv[4];
+    float4 qv[4], kv[2];
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
       int r = hq * 4 + a;
-      qv[a] = *reinterpret_cast<const float4*>(&sm.q[(r * 32 + swz_chunk(r, ch)) * 4]);
+      qv[a] = *reinterpret_cast<const float4*>(&sm.q[(r * 32 + swz_pair(r, ch)) * 4]);
     }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      int r = jq * 4 + c;
-      kv[c] = *reinterpret_cast<const float4*>(&sm.k[(r * 32 + swz_chunk(r, ch)) * 4]);
+    for (int c = 0; c < 2; ++c) {
+      int r = jq * 2 + c;
+      kv[c] = *reinterpret_cast<const float4*>(&sm.k[(r * 32 + swz_pair(r, ch)) * 4]);
     }
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         acc[a][c] = __fmaf_rn(qv[a].x, kv[c].x, acc[a][c]);
         acc[a][c] = __fmaf_rn(qv[a].y, kv[c].y, acc[a][c]);
         acc[a][c] = __fmaf_rn(qv[a].z, kv[c].z, acc[a][c]);
@@ -121,9 +126,9 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
       }
   }
   // fold this thread's four heads (ascending) per key
-  float part[4];
+  float part[2];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     float p = 0.f;
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
@@ -135,14 +140,14 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
   }
   // tree levels 0 and 1 over hq bits 0,1 (lane bits 3,4)
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     part[c] = __fadd_rn(part[c], __shfl_xor_sync(0xffffffffu, part[c], 8));
     part[c] = __fadd_rn(part[c], __shfl_xor_sync(0xffffffffu, part[c], 16));
   }
   // levels 2 and 3 over hq bits 2,3 (warp bits 1,2)
   if ((lane >> 3) == 0) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) sm.red[warp >> 1][jq * 4 + c] = part[c];
+    for (int c = 0; c < 2; ++c) sm.red[warp >> 1][jq * 2 + c] = part[c];
   }
   __syncthreads();
   if (tid < KT) {

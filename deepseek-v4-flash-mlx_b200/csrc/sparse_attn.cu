@@ -25,6 +25,7 @@ constexpr int Q_BYTES = HB * ROW_BYTES;        // 64 KB
 constexpr int KV_BYTES = BN * ROW_BYTES;       // 64 KB
 constexpr int P_BYTES = HB * BN * 2;           // 8 KB
 constexpr float LOG2E = 1.4426950408889634f;
+constexpr int IDX_CAP = 2048;                  // rows of a CTA's range preloaded into shared memory
 
 struct Smem {
   alignas(128) uint8_t q[Q_BYTES];
@@ -36,6 +37,7 @@ struct Smem {
   float l_run[HB];
   float alpha[HB];
   int32_t rowidx[2][BN];
+  int32_t rows[IDX_CAP];  // pool rows of this CTA's whole index range (loaded once)
 };
 
 // swizzled byte offset of 16-byte chunk `c` of row `r` in a tile whose rows are `row_chunks`
@@ -89,7 +91,41 @@ struct Params {
   const float* rope_freqs;
   const int32_t* positions;
   int rope_dim;
+  const int64_t* win_base;  // implicit window (NULL: the list is idx alone)
+  int win_stride, window, window_linear;
 };
+
+// logical list length of a query: implicit window rows followed by the explicit indices
+__device__ __forceinline__ int list_len(const Params& P) { return (P.win_base ? P.window : 0) + P.t; }
+
+// pool row of logical entry u of query qi (-1 = masked)
+__device__ __forceinline__ int64_t list_row(const Params& P, int64_t qi, int u) {
+  if (P.win_base != nullptr) {
+    if (u < P.window) {
+      const int p = P.positions[qi];
+      const int W = P.window;
+      int slot;
+      if (P.window_linear) {
+        const int lo = p - W + 1 > 0 ? p - W + 1 : 0;
+        slot = (lo + u <= p) ? lo + u : -1;
+      } else if (p >= W - 1) {
+        const int sp = p % W;
+        slot = (u < W - sp - 1) ? (sp + 1 + u) : (u - (W - sp - 1));
+      } else {
+        slot = (u <= p) ? u : -1;
+      }
+      return slot < 0 ? -1 : P.win_base[qi * P.win_stride] + slot;
+    }
+    u -= P.window;
+  }
+  if (P.idx_dtype == DSV4_I64) return __ldg(reinterpret_cast<const long long*>(P.idx) + qi * P.t + u);
+  return __ldg(reinterpret_cast<const int32_t*>(P.idx) + qi * P.t + u);
+}
+
+// whether tile `tile` reads explicit indices (written by the kernel launched before this one)
+__device__ __forceinline__ bool tile_needs_idx(const Params& P, int tile) {
+  return P.win_base == nullptr || (tile + 1) * 64 > P.window;
+}
 
 __device__ __forceinline__ int64_t load_idx(const void* idx, int64_t off, int dtype) {
   if (dtype == DSV4_I64) return __ldg(reinterpret_cast<const long long*>(idx) + off);
@@ -100,7 +136,7 @@ __device__ __forceinline__ int64_t load_idx(const void* idx, int64_t off, int dt
 // loads the indices of the 16 rows it copies (independent loads, one round trip), then issues its
 // 16-byte cp.async copies; rows past the list or masked (-1) are zero-filled and marked invalid.
 __device__ __forceinline__ void gather_tile(const Params& P, Smem& sm, int buf, int64_t qi, int t0,
-                                            int t_end) {
+                                            int t_end, int range0, bool preloaded) {
   const int tid = threadIdx.x;
   constexpr int ROWS_PER_THREAD = BN / (THREADS / 64);  // 16
   const int chunk = tid & 63;                            // 64 chunks of 16 B per row
@@ -109,13 +145,18 @@ __device__ __forceinline__ void gather_tile(const Params& P, Smem& sm, int buf, 
 #pragma unroll
   for (int i = 0; i < ROWS_PER_THREAD; ++i) {
     const int t = t0 + r0 + i * (THREADS / 64);
-    int64_t v = -1;
-    if (t < t_end) v = load_idx(P.idx, qi * P.t + t, P.idx_dtype);
-    if (v >= P.n) {
-      if (chunk == 0) raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
-      v = -1;
+    if (preloaded) {
+      const int32_t v = t < t_end ? sm.rows[t - range0] : -1;
+      rows[i] = (v >= 0 && v < P.n) ? v : -1;  // every entry was checked at preload; kept as a guard
+    } else {
+      int64_t v = -1;
+      if (t < t_end) v = list_row(P, qi, t);
+      if (v >= P.n) {
+        if (chunk == 0) raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
+        v = -1;
+      }
+      rows[i] = static_cast<int32_t>(v < 0 ? -1 : v);
     }
-    rows[i] = static_cast<int32_t>(v < 0 ? -1 : v);
   }
   const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(sm.kv[buf]));
 #pragma unroll
@@ -129,6 +170,20 @@ __device__ __forceinline__ void gather_tile(const Params& P, Smem& sm, int buf, 
   cp_async_commit();
 }
 
+// Load the pool rows of logical entries [a, b) into sm.rows[u - base] (the CTA's range starts at
+// `base`, a >= base, b - base <= IDX_CAP); out-of-range rows are recorded in the device error word
+// and masked.
+__device__ __forceinline__ void preload_rows(const Params& P, Smem& sm, int64_t qi, int base, int a, int b) {
+  for (int u = a + threadIdx.x; u < b; u += THREADS) {
+    int64_t v = list_row(P, qi, u);
+    if (v >= P.n) {
+      raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
+      v = -1;
+    }
+    sm.rows[u - base] = static_cast<int32_t>(v < 0 ? -1 : v);
+  }
+}
+
 __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -138,15 +193,22 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
   const int h0 = hblk * HB;
   const int heads_here = min(HB, P.h - h0);
 
-  // index range of this split (in whole tiles)
-  const int ntiles_all = (P.t + BN - 1) / BN;
+  // index range of this split (in whole tiles) over the logical list [implicit window | idx]
+  const int t_end = list_len(P);
+  const int ntiles_all = (t_end + BN - 1) / BN;
   const int per = (ntiles_all + P.splits - 1) / P.splits;
   const int tile_begin = split * per;
   const int tile_end = min(ntiles_all, tile_begin + per);
-  const int t_end = P.t;
 
   pdl_trigger();
-  pdl_wait();
+  // Programmatic dependent launch: nothing before pdl_wait() writes global memory, and it reads only
+  // q, the pool rows of the implicit window and positions, which no kernel in flight writes. Tiles
+  // that read explicit indices (the previous kernel's output) wait first.
+  bool waited = false;
+  if (P.win_base == nullptr) {
+    pdl_wait();
+    waited = true;
+  }
   // ---- stage Q (64 heads x 512) as bf16, swizzled ----
   const uint32_t qbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
   if (P.q_dtype == DSV4_BF16) {
@@ -187,7 +249,30 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) o[a][b][c] = 0.f;
 
-  if (tile_begin < tile_end) gather_tile(P, sm, 0, qi, tile_begin * BN, t_end);
+  // preload the pool rows of this CTA's whole range into shared memory (one round trip) so that
+  // issuing a tile's gather never waits on global loads; window rows first (no dependency), the
+  // explicit indices after the programmatic-dependency wait
+  const int range0 = tile_begin * BN, range1 = min(t_end, tile_end * BN);
+  const bool preloaded = range1 - range0 <= IDX_CAP;
+  if (preloaded && range0 < range1) {
+    const int wend = P.win_base ? min(range1, P.window) : range0;
+    if (wend > range0) preload_rows(P, sm, qi, range0, range0, wend);
+    if (range1 > wend) {
+      if (!waited) {
+        pdl_wait();
+        waited = true;
+      }
+      preload_rows(P, sm, qi, range0, max(range0, wend), range1);
+    }
+    __syncthreads();
+  }
+  if (tile_begin < tile_end) {
+    if (!waited && tile_needs_idx(P, tile_begin)) {
+      pdl_wait();
+      waited = true;
+    }
+    gather_tile(P, sm, 0, qi, tile_begin * BN, t_end, range0, preloaded);
+  }
 
   const uint32_t q_s = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
   const uint32_t p_s = static_cast<uint32_t>(__cvta_generic_to_shared(sm.p));
@@ -199,7 +284,13 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
     const int buf = (tile - tile_begin) & 1;
     cp_async_wait<0>();
     __syncthreads();  // S1: tile `buf` landed; previous PV finished
-    if (tile + 1 < tile_end) gather_tile(P, sm, buf ^ 1, qi, (tile + 1) * BN, t_end);
+    if (tile + 1 < tile_end) {
+      if (!waited && tile_needs_idx(P, tile + 1)) {
+        pdl_wait();
+        waited = true;
+      }
+      gather_tile(P, sm, buf ^ 1, qi, (tile + 1) * BN, t_end, range0, preloaded);
+    }
     const uint32_t kv_s = static_cast<uint32_t>(__cvta_generic_to_shared(sm.kv[buf]));
 
     // ---- S = Q K^T ----
@@ -341,6 +432,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
   }
   __syncthreads();
 
+  if (!waited) pdl_wait();  // global writes only after the previous kernel has completed
   // ---- epilogue: O (scaled for the final output) -> smem fp32 [64][OSTRIDE] over the kv buffers,
   // then one rolled, coalesced pass writes it out (inverse rope applied there)
   constexpr int OSTRIDE = D + 8;
@@ -490,14 +582,16 @@ __global__ void __launch_bounds__(128) combine_kernel(Params P) {
 static int choose_splits(const dsv4_sparse_attn_params* p) {
   if (p->num_splits > 0) return p->num_splits;
   const int hblocks = (p->h + HB - 1) / HB;
-  const int ntiles = (p->t + BN - 1) / BN;
+  const int len = (p->win_base ? p->window : 0) + p->t;
+  const int ntiles = (len + BN - 1) / BN;
   const int64_t units = p->s * hblocks;
   const int sms = num_sms();
   if (units >= sms || ntiles <= 1) return 1;
-  int want = static_cast<int>((sms + units - 1) / units);
+  // one CTA per SM (the kernel's shared memory allows no more): as many splits as fit in one wave
+  int want = static_cast<int>(sms / units);
+  if (want < 1) want = 1;
   if (want > ntiles) want = ntiles;
   if (want > 64) want = 64;
-  // keep the split count a divisor-friendly size so every split gets whole tiles
   int per = (ntiles + want - 1) / want;
   return (ntiles + per - 1) / per;
 }
@@ -519,7 +613,7 @@ static size_t partial_bytes(const dsv4_sparse_attn_params* p) {
 }
 
 extern "C" size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p) {
-  if (!p || p->s <= 0 || p->h <= 0 || p->t <= 0) return 0;
+  if (!p || p->s <= 0 || p->h <= 0 || (p->t <= 0 && p->win_base == nullptr)) return 0;
   size_t bytes = (partial_bytes(p) + 255) / 256 * 256;
   if (p->q_norm_rope) bytes += static_cast<size_t>(p->s) * p->h * p->d * 2;
   return bytes;
@@ -530,7 +624,8 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
   DSV4_CHECK_ARG(p->q && p->kv && p->sink && p->idx && p->out, "dsv4_sparse_attn: NULL tensor");
   DSV4_CHECK_ARG(p->d == sa::D, "dsv4_sparse_attn: head dim %d unsupported (512 only)", p->d);
   DSV4_CHECK_ARG(p->h > 0 && p->h % 16 == 0, "dsv4_sparse_attn: heads %d must be a positive multiple of 16", p->h);
-  DSV4_CHECK_ARG(p->s >= 0 && p->t > 0 && p->n > 0, "dsv4_sparse_attn: bad sizes s=%lld t=%d n=%lld",
+  DSV4_CHECK_ARG(p->s >= 0 && (p->t > 0 || p->win_base != nullptr) && p->t >= 0 && p->n > 0,
+                 "dsv4_sparse_attn: bad sizes s=%lld t=%d n=%lld",
                  (long long)p->s, p->t, (long long)p->n);
   DSV4_CHECK_DTYPE(p->q_dtype == DSV4_F32 || p->q_dtype == DSV4_BF16, "dsv4_sparse_attn: q dtype");
   DSV4_CHECK_DTYPE(p->idx_dtype == DSV4_I32 || p->idx_dtype == DSV4_I64, "dsv4_sparse_attn: idx dtype");
@@ -538,6 +633,8 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
   DSV4_CHECK_ARG(p->rope_freqs == nullptr || (p->positions != nullptr && p->rope_dim > 0 &&
                                                p->rope_dim <= 64 && p->rope_dim % 2 == 0),
                  "dsv4_sparse_attn: inverse rope needs positions and 0 < rope_dim <= 64");
+  DSV4_CHECK_ARG(p->win_base == nullptr || (p->positions != nullptr && p->window > 0 && p->window % sa::BN == 0),
+                 "dsv4_sparse_attn: the implicit window needs positions and a window that is a multiple of 64");
   DSV4_CHECK_ARG(!p->q_norm_rope || p->rope_freqs != nullptr,
                  "dsv4_sparse_attn: the fused q norm/rope needs rope_freqs, positions and rope_dim");
   DSV4_CHECK_ARG(p->s * 64 < (int64_t)INT32_MAX, "dsv4_sparse_attn: too many queries per call");
@@ -561,6 +658,10 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
   P.rope_freqs = p->rope_freqs;
   P.positions = p->positions;
   P.rope_dim = p->rope_dim;
+  P.win_base = p->win_base;
+  P.win_stride = p->win_stride;
+  P.window = p->win_base ? p->window : 0;
+  P.window_linear = p->window_linear;
   P.part = nullptr;
   const size_t need = dsv4_sparse_attn_workspace_size(p);
   if (need > 0 && (p->workspace == nullptr || p->workspace_bytes < need)) {

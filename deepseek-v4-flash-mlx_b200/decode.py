@@ -14,9 +14,10 @@ HBM and is addressed by index:
   ring_kv / ring_score fp32 [batch, 2*ratio, 1024]: the compressor's decode ring
 
 `decode_attention` is the measured decode path: on one stream, chained with programmatic dependent
-launch, the indexer scores, the top-k selection (which also writes the window rows) straight into
-the attention index list, sparse attention with the inverse RoPE fused into its epilogue, and the
-split-K merge; q's per-head norm + RoPE runs on a side stream beside the indexer.
+launch, the indexer scores, the top-k selection straight into the attention index list (mapped
+through the block table), sparse attention — whose window tiles, computed from the positions, run
+while the selection finishes — with the inverse RoPE fused into its epilogue, and the split-K merge;
+q's per-head norm + RoPE runs on a side stream beside the indexer.
 """
 import math
 
@@ -71,7 +72,9 @@ class SparseMLACache:
 
 
 def attention_index_buffer(batch, window, top_k, device):
-    return torch.empty((batch, window + top_k), dtype=torch.int32, device=device)
+    """The explicit part of a decode token's attention list: its top_k compressed pool rows (the
+    window rows are computed inside the attention kernel)."""
+    return torch.empty((batch, top_k), dtype=torch.int32, device=device)
 
 
 def decode_attention(cache, q, q_idx, w_idx, sink, positions, top_k=512, scale=None, freqs=None, idx_buf=None,
@@ -95,12 +98,12 @@ def decode_attention(cache, q, q_idx, w_idx, sink, positions, top_k=512, scale=N
         qr = norm_rope(q, positions, freqs, weight=None)
     idx = idx_buf if idx_buf is not None else attention_index_buffer(b, cache.window, top_k, q.device)
     indexer_topk_into(idx.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
-                      cache.k_idx, top_k, positions.view(b, 1), cache.ratio, out_col=cache.window,
-                      out_offset=cache.comp_base, block_table=cache.block_table, page=cache.page,
-                      win_base=cache.win_base, window=cache.window)
+                      cache.k_idx, top_k, positions.view(b, 1), cache.ratio, out_col=0,
+                      out_offset=cache.comp_base, block_table=cache.block_table, page=cache.page)
     main.wait_stream(side)
     qr.record_stream(main)
-    return sparse_attn_rope(qr, cache.kv_pool, sink, idx, scale, positions, freqs, 64, out_dtype)
+    return sparse_attn_rope(qr, cache.kv_pool, sink, idx, scale, positions, freqs, 64, out_dtype,
+                            win_base=cache.win_base, window=cache.window)
 
 
 _side_streams = {}

@@ -12,7 +12,7 @@ from . import _lib as L
 
 
 def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_dim=0, num_splits=0,
-                 q_norm_rope=False, q_eps=1e-6):
+                 q_norm_rope=False, q_eps=1e-6, win_base=None, window=0, window_linear=False):
     p = L.SparseAttnParams()
     p.q, p.kv, p.sink, p.idx, p.out = L.ptr(q), L.ptr(kv), L.ptr(sink), L.ptr(idx), L.ptr(out)
     p.s, p.n, p.h, p.d, p.t = q.shape[0], kv.shape[0], q.shape[1], q.shape[2], idx.shape[-1]
@@ -24,6 +24,10 @@ def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_
     p.num_splits = num_splits
     p.q_norm_rope = int(q_norm_rope)
     p.q_eps = q_eps
+    p.win_base = L.ptr(win_base) if win_base is not None else None
+    p.win_stride = 1 if (win_base is not None and win_base.numel() > 1) else 0
+    p.window = window
+    p.window_linear = int(window_linear)
     return p
 
 
@@ -31,7 +35,8 @@ def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_
 def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, topk_idxs: torch.Tensor,
                     scale: float, out_dtype: torch.dtype, rope_freqs: torch.Tensor | None,
                     positions: torch.Tensor | None, rope_dim: int, num_splits: int,
-                    q_norm_rope: bool = False, q_eps: float = 1e-6) -> torch.Tensor:
+                    q_norm_rope: bool = False, q_eps: float = 1e-6, win_base: torch.Tensor | None = None,
+                    window: int = 0, window_linear: bool = False) -> torch.Tensor:
     q = q.contiguous()
     kv = kv.contiguous()
     if kv.dtype != torch.bfloat16:
@@ -41,7 +46,8 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
     sink = attn_sink.float().contiguous()
     idx = topk_idxs.contiguous()
     out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
-    p = _attn_params(q, kv, sink, idx, out, scale, rope_freqs, positions, rope_dim, num_splits, q_norm_rope, q_eps)
+    p = _attn_params(q, kv, sink, idx, out, scale, rope_freqs, positions, rope_dim, num_splits, q_norm_rope, q_eps,
+                     win_base, window, window_linear)
     nbytes = L.lib().dsv4_sparse_attn_workspace_size(ctypes.byref(p))
     ws = L.workspace(nbytes, q.device)
     p.workspace, p.workspace_bytes = L.ptr(ws), nbytes
@@ -51,7 +57,7 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
 
 @_sparse_attn_op.register_fake
 def _(q, kv, attn_sink, topk_idxs, scale, out_dtype, rope_freqs, positions, rope_dim, num_splits, q_norm_rope=False,
-      q_eps=1e-6):
+      q_eps=1e-6, win_base=None, window=0, window_linear=False):
     return torch.empty(q.shape, dtype=out_dtype, device=q.device)
 
 
@@ -69,12 +75,15 @@ def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
 
 
 def sparse_attn_rope(q, kv, attn_sink, topk_idxs, scale, positions, freqs, rope_dim=64,
-                     out_dtype=torch.bfloat16, num_splits=0):
+                     out_dtype=torch.bfloat16, num_splits=0, win_base=None, window=0, window_linear=False):
     """sparse_attn followed by the inverse rope of the output's last rope_dim dims at `positions`
-    (oracle/decode_engine.py:118, oracle/v4_fast.py:119), fused into the attention epilogue."""
-    L.require_cuda(q, kv, attn_sink, topk_idxs, positions, freqs)
+    (oracle/decode_engine.py:118, oracle/v4_fast.py:119), fused into the attention epilogue. With
+    `win_base` (int64, one per query or a single value) the list of query i is [window rows | topk_idxs[i]],
+    the window rows computed in the kernel (decode ring order, or linear with window_linear)."""
+    L.require_cuda(q, kv, attn_sink, topk_idxs, positions, freqs, win_base)
     return _sparse_attn_op(q, kv, attn_sink, topk_idxs, float(scale), out_dtype, freqs.float().contiguous(),
-                           positions.to(torch.int32).contiguous(), int(rope_dim), int(num_splits))
+                           positions.to(torch.int32).contiguous(), int(rope_dim), int(num_splits), False, 1e-6,
+                           win_base, int(window), bool(window_linear))
 
 
 def sparse_attn_decode(q_raw, kv, attn_sink, topk_idxs, scale, positions, freqs, rope_dim=64, eps=1e-6,

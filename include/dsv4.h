@@ -93,6 +93,15 @@ typedef struct {
    * chain of oracle/v4_fast.py:88-89); q is then the raw projection output */
   int32_t q_norm_rope;
   float q_eps;
+  /* optional implicit window (win_base == NULL: off): the list of query i is then
+   * [window rows | idx[i, 0:t]], the window rows computed from positions[i] as in
+   * dsv4_indexer_params (ring order, or linear with window_linear), pool row win_base[i*win_stride] + slot.
+   * window must be a multiple of 64. Window tiles need nothing from the kernel launched before, so
+   * under programmatic dependent launch they run while that kernel (the top-k selection) finishes. */
+  const int64_t* win_base;
+  int32_t win_stride;
+  int32_t window;
+  int32_t window_linear;
 } dsv4_sparse_attn_params;
 
 DSV4_API size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p);

@@ -34,24 +34,48 @@ def test_decode_attention_matches_oracle(dsv4, batch, ctx, top_k):
 
 
 def test_decode_indices_bit_exact(dsv4):
-    """The attention index list (window ring order + indexer selection through the block table)."""
+    """The attention index list: window rows in the reference's ring order (written by the selection
+    kernel's window option) + the indexer's selection mapped through the block table."""
     C = _cfg()
     case = C.make_decode_case(2, 8192, 512, seeds=[100, 101])
     b = 2
     idx = torch.empty((b, 128 + 512), dtype=torch.int32, device="cuda")
-    L = importlib.import_module("deepseek-v4-flash-mlx_b200._lib")
     pos = case.positions
-    L.check(L.lib().dsv4_decode_window_indices(b, 128, L.ptr(pos), L.ptr(case.cache.win_base), L.ptr(idx), 640,
-                                               L.stream_of(idx)))
     dsv4.indexer_topk_into(idx.view(b, 1, -1), case.q_idx.view(b, 1, 64, 128), case.w_idx.view(b, 1, 64),
                            case.cache.k_idx, 512, pos.view(b, 1), 4, out_col=128, out_offset=case.cache.comp_base,
-                           block_table=case.cache.block_table, page=case.cache.page)
+                           block_table=case.cache.block_table, page=case.cache.page, win_base=case.cache.win_base,
+                           window=128)
     pool, win_base, comp_rows = C.decode_case_host_pool(case)
     f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
     h = case.host
     _, ref_idx = LR.decode_attention_ref(pool, win_base, comp_rows, h["k_idx"], h["q"], h["q_idx"], h["w_idx"],
                                          h["sink"], h["positions"], 512, f, return_indices=True)
     np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx.numpy())
+
+
+def test_implicit_window_equals_explicit_list(dsv4):
+    """sparse attention with the window computed in the kernel equals the same list given explicitly."""
+    C = _cfg()
+    for ctx in (8192, 77, 4096):
+        case = C.make_decode_case(2, ctx, 64 if ctx != 4096 else 512, seeds=[7, 8])
+        b = 2
+        k = 64 if ctx != 4096 else 512
+        full = torch.empty((b, 128 + k), dtype=torch.int32, device="cuda")
+        dsv4.indexer_topk_into(full.view(b, 1, -1), case.q_idx.view(b, 1, 64, 128), case.w_idx.view(b, 1, 64),
+                               case.cache.k_idx, k, case.positions.view(b, 1), 4, out_col=128,
+                               out_offset=case.cache.comp_base, block_table=case.cache.block_table,
+                               page=case.cache.page, win_base=case.cache.win_base, window=128)
+        f = dsv4.rope_freqs(64, "cuda")
+        q = torch.randn(b, 64, 512, device="cuda").to(torch.bfloat16)
+        # same split count on both sides (the accumulation order then matches exactly); splits 1-3 put
+        # window and selected rows in one CTA (a range spanning the window boundary)
+        for splits in (0, 1, 2, 3):
+            a = dsv4.sparse_attn_rope(q, case.cache.kv_pool, case.sink, full, 512 ** -0.5, case.positions, f,
+                                      out_dtype=torch.float32, num_splits=splits)
+            bb = dsv4.sparse_attn_rope(q, case.cache.kv_pool, case.sink, full[:, 128:].contiguous(), 512 ** -0.5,
+                                       case.positions, f, out_dtype=torch.float32, win_base=case.cache.win_base,
+                                       window=128, num_splits=splits)
+            torch.testing.assert_close(a, bb, rtol=0, atol=0, msg=f"ctx={ctx} splits={splits}")
 
 
 def test_decode_runner_graph_and_host_path(dsv4):
