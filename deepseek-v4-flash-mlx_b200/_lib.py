@@ -27,7 +27,8 @@ class SparseAttnParams(ctypes.Structure):
                 ("q_dtype", i32), ("idx_dtype", i32), ("out_dtype", i32), ("scale", f32),
                 ("rope_freqs", vp), ("positions", vp), ("rope_dim", i32), ("num_splits", i32),
                 ("workspace", vp), ("workspace_bytes", sz), ("q_norm_rope", i32), ("q_eps", f32),
-                ("win_base", vp), ("win_stride", i32), ("window", i32), ("window_linear", i32)]
+                ("win_base", vp), ("win_stride", i32), ("window", i32), ("window_linear", i32),
+                ("kernel", i32)]
 
 
 class RmsNormParams(ctypes.Structure):

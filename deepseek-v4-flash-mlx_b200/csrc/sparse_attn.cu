@@ -11,6 +11,8 @@
 // A query whose list spans several CTAs writes an unnormalised partial (O, m, l) to the
 // workspace and a combine kernel merges the partials; the sink enters only the denominator,
 // exactly as the reference: o = sum p v / (sum p + exp(sink - m)).
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace dsv4 {
@@ -603,6 +605,18 @@ DSV4_ERROR_READER(sparse_attn)
 
 using namespace dsv4;
 
+int dsv4_sparse_attn_tc(const dsv4_sparse_attn_params* p, void* stream);
+
+// tcgen05 kernel: 64 heads, bf16 q (or the fused prologue, which writes bf16 q), one CTA per query.
+// Automatic choice: when the queries alone fill the GPU, so that no query's list is split.
+static bool tc_shape_ok(const dsv4_sparse_attn_params* p) {
+  return p->h == sa::HB && (p->q_dtype == DSV4_BF16 || p->q_norm_rope);
+}
+static bool use_tc(const dsv4_sparse_attn_params* p, int splits) {
+  if (p->kernel == 1 || !tc_shape_ok(p)) return false;
+  return p->kernel == 2 || (splits == 1 && p->s >= num_sms());
+}
+
 // workspace: [split partials (O, m, l)] [bf16 q after the fused norm/rope pre-pass]
 static size_t partial_bytes(const dsv4_sparse_attn_params* p) {
   const int splits = sa::choose_splits(p);
@@ -638,6 +652,8 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
   DSV4_CHECK_ARG(!p->q_norm_rope || p->rope_freqs != nullptr,
                  "dsv4_sparse_attn: the fused q norm/rope needs rope_freqs, positions and rope_dim");
   DSV4_CHECK_ARG(p->s * 64 < (int64_t)INT32_MAX, "dsv4_sparse_attn: too many queries per call");
+  DSV4_CHECK_ARG(p->kernel >= 0 && p->kernel <= 2 && (p->kernel != 2 || tc_shape_ok(p)),
+                 "dsv4_sparse_attn: kernel %d unavailable for h=%d q_dtype=%d", p->kernel, p->h, p->q_dtype);
   if (p->s == 0) return DSV4_OK;
   sa::Params P;
   P.q = p->q;
@@ -690,6 +706,12 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
     if (st != DSV4_OK) return st;
     P.q = qn;
     P.q_dtype = DSV4_BF16;
+  }
+  if (use_tc(p, P.splits)) {
+    dsv4_sparse_attn_params pt = *p;
+    pt.q = P.q;
+    pt.q_dtype = DSV4_BF16;
+    return dsv4_sparse_attn_tc(&pt, stream);
   }
   static bool attr_set = false;
   const int smem = static_cast<int>(sizeof(sa::Smem));

@@ -12,7 +12,7 @@ from . import _lib as L
 
 
 def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_dim=0, num_splits=0,
-                 q_norm_rope=False, q_eps=1e-6, win_base=None, window=0, window_linear=False):
+                 q_norm_rope=False, q_eps=1e-6, win_base=None, window=0, window_linear=False, kernel=0):
     p = L.SparseAttnParams()
     p.q, p.kv, p.sink, p.idx, p.out = L.ptr(q), L.ptr(kv), L.ptr(sink), L.ptr(idx), L.ptr(out)
     p.s, p.n, p.h, p.d, p.t = q.shape[0], kv.shape[0], q.shape[1], q.shape[2], idx.shape[-1]
@@ -28,6 +28,7 @@ def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_
     p.win_stride = 1 if (win_base is not None and win_base.numel() > 1) else 0
     p.window = window
     p.window_linear = int(window_linear)
+    p.kernel = kernel
     return p
 
 
@@ -36,7 +37,7 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
                     scale: float, out_dtype: torch.dtype, rope_freqs: torch.Tensor | None,
                     positions: torch.Tensor | None, rope_dim: int, num_splits: int,
                     q_norm_rope: bool = False, q_eps: float = 1e-6, win_base: torch.Tensor | None = None,
-                    window: int = 0, window_linear: bool = False) -> torch.Tensor:
+                    window: int = 0, window_linear: bool = False, kernel: int = 0) -> torch.Tensor:
     q = q.contiguous()
     kv = kv.contiguous()
     if kv.dtype != torch.bfloat16:
@@ -47,7 +48,7 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
     idx = topk_idxs.contiguous()
     out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
     p = _attn_params(q, kv, sink, idx, out, scale, rope_freqs, positions, rope_dim, num_splits, q_norm_rope, q_eps,
-                     win_base, window, window_linear)
+                     win_base, window, window_linear, kernel)
     nbytes = L.lib().dsv4_sparse_attn_workspace_size(ctypes.byref(p))
     ws = L.workspace(nbytes, q.device)
     p.workspace, p.workspace_bytes = L.ptr(ws), nbytes
@@ -57,25 +58,27 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
 
 @_sparse_attn_op.register_fake
 def _(q, kv, attn_sink, topk_idxs, scale, out_dtype, rope_freqs, positions, rope_dim, num_splits, q_norm_rope=False,
-      q_eps=1e-6, win_base=None, window=0, window_linear=False):
+      q_eps=1e-6, win_base=None, window=0, window_linear=False, kernel=0):
     return torch.empty(q.shape, dtype=out_dtype, device=q.device)
 
 
-def sparse_attn(q, kv, attn_sink, topk_idxs, scale):
+def sparse_attn(q, kv, attn_sink, topk_idxs, scale, kernel=0):
     """q [s,h,d], kv [n,d], attn_sink [h], topk_idxs [s,T] (-1 masked) -> o [s,h,d].
 
     o = sum_t softmax-numerator_t kv[idx_t] / (sum_t numerator_t + exp(sink_h - rowmax)),
-    the reference's dense-gather formula (ref_torch/sparse_attn.py:23-34)."""
+    the reference's dense-gather formula (ref_torch/sparse_attn.py:23-34). `kernel` picks the
+    implementation (0 automatic, 1 mma.sync split-K, 2 tcgen05; same function)."""
     L.require_cuda(q, kv, attn_sink, topk_idxs)
     if topk_idxs.dim() == 3 and topk_idxs.shape[0] == 1:
         topk_idxs = topk_idxs[0]
     if topk_idxs.dtype not in (torch.int32, torch.int64):
         topk_idxs = topk_idxs.long()
-    return _sparse_attn_op(q, kv, attn_sink, topk_idxs, float(scale), q.dtype, None, None, 0, 0)
+    return _sparse_attn_op(q, kv, attn_sink, topk_idxs, float(scale), q.dtype, None, None, 0, 0, kernel=int(kernel))
 
 
 def sparse_attn_rope(q, kv, attn_sink, topk_idxs, scale, positions, freqs, rope_dim=64,
-                     out_dtype=torch.bfloat16, num_splits=0, win_base=None, window=0, window_linear=False):
+                     out_dtype=torch.bfloat16, num_splits=0, win_base=None, window=0, window_linear=False,
+                     kernel=0):
     """sparse_attn followed by the inverse rope of the output's last rope_dim dims at `positions`
     (oracle/decode_engine.py:118, oracle/v4_fast.py:119), fused into the attention epilogue. With
     `win_base` (int64, one per query or a single value) the list of query i is [window rows | topk_idxs[i]],
@@ -83,17 +86,18 @@ def sparse_attn_rope(q, kv, attn_sink, topk_idxs, scale, positions, freqs, rope_
     L.require_cuda(q, kv, attn_sink, topk_idxs, positions, freqs, win_base)
     return _sparse_attn_op(q, kv, attn_sink, topk_idxs, float(scale), out_dtype, freqs.float().contiguous(),
                            positions.to(torch.int32).contiguous(), int(rope_dim), int(num_splits), False, 1e-6,
-                           win_base, int(window), bool(window_linear))
+                           win_base, int(window), bool(window_linear), int(kernel))
 
 
 def sparse_attn_decode(q_raw, kv, attn_sink, topk_idxs, scale, positions, freqs, rope_dim=64, eps=1e-6,
-                       out_dtype=torch.bfloat16, num_splits=0):
+                       out_dtype=torch.bfloat16, num_splits=0, kernel=0):
     """The decode attention of oracle/v4_fast.py:88-119 in one op: q_raw (the q_up output) gets the
     weightless per-head norm and RoPE at `positions` while it is staged, then sparse attention over
     topk_idxs, then the inverse RoPE of the output in the epilogue."""
     L.require_cuda(q_raw, kv, attn_sink, topk_idxs, positions, freqs)
     return _sparse_attn_op(q_raw, kv, attn_sink, topk_idxs, float(scale), out_dtype, freqs.float().contiguous(),
-                           positions.to(torch.int32).contiguous(), int(rope_dim), int(num_splits), True, float(eps))
+                           positions.to(torch.int32).contiguous(), int(rope_dim), int(num_splits), True, float(eps),
+                           kernel=int(kernel))
 
 
 @torch.library.custom_op("dsv4::get_window_topk_idxs", mutates_args=(), device_types="cuda")

@@ -102,6 +102,12 @@ typedef struct {
   int32_t win_stride;
   int32_t window;
   int32_t window_linear;
+  /* kernel choice: 0 = automatic (the tcgen05 kernel for prefill-shaped calls: 64 heads, bf16 q or
+   * the fused q prologue, one CTA per query filling the GPU; the mma.sync split-K kernel otherwise),
+   * 1 = the mma.sync kernel, 2 = the tcgen05 kernel (64 heads and bf16 q or the fused prologue,
+   * else DSV4_ERR_INVALID_ARGUMENT). Both compute the same function; the choice is for tests and
+   * measurements. */
+  int32_t kernel;
 } dsv4_sparse_attn_params;
 
 DSV4_API size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p);
