@@ -489,7 +489,7 @@ def bench_prefill(args, world, rank, local, dev):
     peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
         os.path.join(ROOT, "MEASURED_PEAKS.json")) else {"bf16_tflops": 1590.0}
     achieved = att_flops / (att_ms * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "kernel": "sa::sparse_attn_kernel", "achieved": achieved,
+    roofline = {"bound": "tensor", "kernel": "tc::attn_tc_kernel", "achieved": achieved,
                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                 "peak_source": "measured" if "when" in peaks else "fallback", "traffic": None,
                 "algorithmic_flops_per_launch": att_flops, "phases_ms": phases}

@@ -56,7 +56,7 @@ class IndexerParams(ctypes.Structure):
                 ("out_stride", i32), ("out_col", i32), ("out_offset", i64),
                 ("block_table", vp), ("table_stride", i32), ("page", i32),
                 ("workspace", vp), ("workspace_bytes", sz), ("win_base", vp), ("window", i32),
-                ("window_linear", i32)]
+                ("window_linear", i32), ("mode", i32)]
 
 
 class CompressorParams(ctypes.Structure):

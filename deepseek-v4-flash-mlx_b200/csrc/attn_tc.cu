@@ -13,6 +13,7 @@
 // (bounded) for what it issued, frees its tensor memory and returns.
 // The sink enters only the denominator, as in ref_torch/sparse_attn.py:33.
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace dsv4 {
 namespace tc {
@@ -24,7 +25,6 @@ constexpr int TMEM_COLS = 512;
 constexpr int COL_O = 0, COL_S = 256;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;   // log2 units: p may reach 2^8 before O is rescaled
-constexpr uint64_t WAIT_NS = 1000000000ull;  // 1 s: an MMA wait longer than this is an error
 
 struct Smem {
   alignas(1024) uint8_t q[8 * SLAB_Q];     // 64 KB
@@ -57,92 +57,7 @@ struct Params {
   int win_stride, window, window_linear;
 };
 
-// ---- PTX helpers --------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-
-// 64-bit shared-memory matrix descriptor: start, leading / stride byte offsets, version 1
-// (sm_100), layout 2 = 128-byte swizzle
-__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  return static_cast<uint64_t>((addr >> 4) & 0x3FFF) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16) |
-         (static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
-}
-
-// instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, M = 128, N = 64
-constexpr uint32_t idesc(bool a_mn_major, bool b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
-         ((64u >> 3) << 17) | ((128u >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
-  asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(id), "r"(acc));
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void bar_init(uint64_t* bar, int count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
-  return t;
-}
-// wait for the phase with the given parity, bounded by WAIT_NS of wall time; false on timeout
-__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
-  const uint32_t a = smem_u32(bar);
-  uint64_t t0 = 0;
-  for (int it = 0;; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (it == 0) t0 = global_ns();
-    else if (global_ns() - t0 > WAIT_NS) return false;
-  }
-}
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
-__device__ __forceinline__ void tc_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void tc_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
-          taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
-
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g, bool valid) {
-  int sz = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g), "r"(sz));
-}
-
-// byte offset of 16-byte chunk c (0..63) of row r in a slab-major, 128-byte-swizzled tile of `rows`
-// rows: slab = c / 8 (64 dims), row r at 128 B, chunk (c % 8) XOR (r % 8)
-__device__ __forceinline__ uint32_t slab_off(int r, int c, int slab_bytes) {
-  return static_cast<uint32_t>((c >> 3) * slab_bytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
+using namespace tc5;
 
 // pool row of logical list entry u of query qi ([implicit window | idx]); -1 = masked
 __device__ __forceinline__ int64_t list_row(const Params& P, int64_t qi, int u) {
@@ -208,17 +123,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
   const int L = (P.win_base ? P.window : 0) + P.t;
   const int ntiles = (L + BN - 1) / BN;
 
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&sm.tmem_base)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
-  }
+  if (warp == 0) tmem_alloc<TMEM_COLS>(&sm.tmem_base);
   if (tid == 0) {
     bar_init(&sm.bar_s, 1);
     bar_init(&sm.bar_o, 1);
     sm.flags = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    bar_init_fence();
   }
   if (tid < HB) {
     sm.m_run[tid] = -INFINITY;
@@ -234,14 +144,14 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
     }
     asm volatile("cp.async.commit_group;\n" ::);
   }
-  tc_before_sync();
+  before_sync();
   __syncthreads();
-  tc_after_sync();
+  after_sync();
   const uint32_t tmem = sm.tmem_base;
   const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;  // this warp's TMEM lane quadrant
 
-  const uint32_t id_s = idesc(false, false);
-  const uint32_t id_o = idesc(true, true);
+  const uint32_t id_s = idesc_bf16<128, HB>(false, false);
+  const uint32_t id_o = idesc_bf16<128, HB>(true, true);
   uint32_t phase = 0;
   bool abort = false;
 
@@ -279,9 +189,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     }
     fence_async_smem();
-    tc_before_sync();
+    before_sync();
     __syncthreads();
-    tc_after_sync();
+    after_sync();
     // (c) S^T = KV . Q^T over K = 512 (8 slabs x 4 steps of 16 dims)
     if (tid == 0) {
       const uint32_t ks = smem_u32(sm.kv), qs = smem_u32(sm.q);
@@ -289,7 +199,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       for (int sl = 0; sl < 8; ++sl)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_f16(tmem + COL_S, sdesc(ks + sl * SLAB_KV + kk * 32, 16, 1024),
+          mma_bf16(tmem + COL_S, sdesc(ks + sl * SLAB_KV + kk * 32, 16, 1024),
                   sdesc(qs + sl * SLAB_Q + kk * 32, 16, 1024), id_s, (sl | kk) ? 1u : 0u);
       mma_commit(&sm.bar_s);
     }
@@ -300,7 +210,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
         break;
       }
     }
-    tc_after_sync();
+    after_sync();
     // (d) this thread's row of S^T: 64 heads
     float s[HB];
 #pragma unroll
@@ -379,9 +289,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       tmem_wait_st();
     }
     fence_async_smem();
-    tc_before_sync();
+    before_sync();
     __syncthreads();
-    tc_after_sync();
+    after_sync();
     if (tid == 0) sm.flags &= ~1;
     // (g) O^T += V^T . P^T : 4 M-tiles of 128 dims, K = 128 rows in 8 steps of 16
     if (tid == 0) {
@@ -390,7 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_f16(tmem + COL_O + mt * HB, sdesc(ks + 2 * mt * SLAB_KV + kk * 2048, SLAB_KV, 1024),
+          mma_bf16(tmem + COL_O + mt * HB, sdesc(ks + 2 * mt * SLAB_KV + kk * 2048, SLAB_KV, 1024),
                   sdesc(ps + kk * 2048, 16384, 1024), id_o, (tile > 0 || kk > 0) ? 1u : 0u);
       mma_commit(&sm.bar_o);
     }
@@ -404,7 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
     bar_wait(&sm.bar_s, phase);
     bar_wait(&sm.bar_o, phase ^ 1);
   }
-  tc_after_sync();
+  after_sync();
   if (ok) {
     // epilogue: lane = dim (within the M-tile), 64 heads per thread; normalise, inverse rope, store
     const bool rope = P.rope_freqs != nullptr;
@@ -452,10 +362,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
     }
   }
   asm volatile("cp.async.wait_group 0;\n" ::: "memory");  // Q copies, when the list was empty
-  tc_before_sync();
+  before_sync();
   __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  if (warp == 0) tmem_dealloc<TMEM_COLS>(tmem);
 }
 
 DSV4_ERROR_READER(attn_tc)

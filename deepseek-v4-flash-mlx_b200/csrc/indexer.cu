@@ -15,6 +15,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "indexer_tc.cuh"
 
 namespace dsv4 {
 namespace idx {
@@ -354,6 +355,14 @@ struct SelectParams {
   int32_t table_stride, page;
   const int64_t* win_base;
   int32_t window, window_linear;
+  // refinement of approximate scores (tensor-core filter): exact rescoring of the uncertain band
+  int32_t refine;
+  const float* q;         // [rows, 64, 128]
+  const float* w;         // [rows, 64]
+  const float* k;         // [batch, n_keys, 128], k_batch_stride rows apart
+  int64_t k_batch_stride;
+  const float* kmax;      // [batch] max key norm
+  float eps_c;            // bound constant C of eps = C * sum_h |w_h| ||q_h|| * kmax
 };
 
 // window rows of a query at position p: decode ring order, or the prefill (linear) branch
@@ -636,42 +645,15 @@ __device__ __forceinline__ void warp_hist_add(uint32_t* hist, uint32_t bin, uint
   if (bin < nbins) atomicAdd(&hist[bin], 1u);
 }
 
+// Radix levels over the order-preserving keys (12, 8, 8 and 4 bits, most significant first) that
+// locate the boundary of the top k. With stop_whole, a level whose boundary bin is taken whole ends
+// the search (prefix then fixes the bits at and above shift); without it the search runs down to
+// shift 0 and prefix is the k-th largest key itself. kleft = keys still needed from the boundary.
 template <int PER>
-__global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P) {
-  __shared__ SelRegShared sh;
-  pdl_trigger();
-  pdl_wait();
+__device__ __forceinline__ void radix_levels(const uint32_t (&key)[PER], int nv, uint32_t k, bool stop_whole,
+                                             SelRegShared& sh, uint32_t& prefix, uint32_t& shift, uint32_t& kleft,
+                                             bool& whole) {
   const int tid = threadIdx.x, lane = tid & 31;
-  const int64_t qrow = blockIdx.x;
-  const int b = static_cast<int>(qrow / P.s);
-  const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
-  int32_t* out = P.out + qrow * P.out_stride + P.out_col;
-  const int k = P.top_k;
-
-  if (P.win_base != nullptr)
-    for (int c = tid; c < P.window; c += SEL_THREADS) out[c - P.window] = window_row(P, b, P.positions[qrow], c);
-  if (nvis <= k) {
-    for (int r = tid; r < k; r += SEL_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
-    return;
-  }
-  const int j0 = tid * PER;
-  const float* sc = P.scores + qrow * P.n_pad + j0;
-  uint32_t key[PER];
-  if ((P.n_pad & 3) == 0 && j0 + PER <= nvis) {
-#pragma unroll
-    for (int e = 0; e < PER; e += 4) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(sc + e));
-      key[e] = ordered_bits(v.x);
-      key[e + 1] = ordered_bits(v.y);
-      key[e + 2] = ordered_bits(v.z);
-      key[e + 3] = ordered_bits(v.w);
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < PER; ++e) key[e] = (j0 + e < nvis) ? ordered_bits(__ldcg(sc + e)) : 0u;
-  }
-  // number of valid keys of this thread (the rest are padding and never counted)
-  const int nv = max(0, min(PER, nvis - j0));
 
 #pragma unroll
   for (int i = 0; i < SEL_BINS / SEL_THREADS; ++i) sh.hist[tid + i * SEL_THREADS] = 0;
@@ -680,8 +662,8 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
 #pragma unroll
   for (int e = 0; e < PER; ++e) warp_hist_add(sh.hist, e < nv ? (key[e] >> 20) : 0xffffffffu, SEL_BINS);
   __syncthreads();
-  uint32_t prefix, kleft, shift = 20;
-  bool whole = false;
+  shift = 20;
+  whole = false;
   {
     constexpr int PB = SEL_BINS / SEL_THREADS;
     uint32_t c[PB], tot = 0;
@@ -691,11 +673,11 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
       tot += c[e];
     }
     const uint32_t before = block_scan_reg(tot, sh);
-    if (before < static_cast<uint32_t>(k) && static_cast<uint32_t>(k) <= before + tot) {
+    if (before < k && k <= before + tot) {
       uint32_t run = before;
 #pragma unroll
       for (int e = 0; e < PB; ++e) {
-        if (run + c[e] >= static_cast<uint32_t>(k)) {
+        if (run + c[e] >= k) {
           const uint32_t bn = SEL_BINS - 1 - (tid * PB + e);
           sh.bin = bn;
           sh.need = (k - run) | ((c[e] == k - run) ? 0x80000000u : 0u);  // top bit: bin taken whole
@@ -711,7 +693,7 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
   }
   // levels 2..4 over the keys inside the boundary bin: bits 19..12, 11..4, 3..0
 #pragma unroll 1
-  for (int level = 0; level < 3 && !whole; ++level) {
+  for (int level = 0; level < 3 && !(whole && stop_whole); ++level) {
     const uint32_t width = level < 2 ? 8u : 4u;
     const uint32_t nshift = shift - width;
     const uint32_t nb = 1u << width;
@@ -760,6 +742,199 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
     shift = nshift;
     __syncthreads();
   }
+}
+
+
+constexpr int BAND_CAP = 512;  // band keys rescored per round
+constexpr float EPS_C = 0x1p-12f;
+
+struct RefineSmem {
+  float4 q[HI * DI / 4];   // the query's 64 x 128 indexer q; chunk c of head h at c ^ ((h / 4) % 8)
+  float w[HI];
+  float wq[HI];
+  int32_t band_idx[BAND_CAP];
+  float band_e[BAND_CAP];
+  float eps;
+};
+
+__device__ __forceinline__ float from_ordered(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+
+// Exact refinement of approximate scores A with |A - score| <= eps for every key (eps from the
+// query's |w_h| ||q_h|| and the largest key norm). With v the k-th largest A:
+//  - a key with A > v + 2 eps is in the top k: any key that ties or beats it has
+//    A >= score - eps >= its score - eps > v, and fewer than k keys have A > v;
+//  - a key with A < v - 2 eps is not: the k keys with A >= v all have score >= v - eps > its score.
+// Keys in between get their exact score in the canonical fp32 order; the certain ones are pinned to
+// the largest / smallest ordered key, so the ordinary selection that follows returns the exact top k
+// (at least k minus the certain count of keys lie in the band, since every key with A >= v is there
+// or certain). Valid for inputs without subnormal elements.
+template <int PER>
+__device__ __forceinline__ void refine_band(const SelectParams& P, int64_t qrow, int b, int k, uint32_t (&key)[PER],
+                                            int nv, int j0, SelRegShared& sh, RefineSmem& rs) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t kth, shift, kleft;
+  bool whole;
+  radix_levels<PER>(key, nv, static_cast<uint32_t>(k), false, sh, kth, shift, kleft, whole);
+
+  const float4* qg = reinterpret_cast<const float4*>(P.q + qrow * (HI * DI));
+  for (int i = tid; i < HI * DI / 4; i += SEL_THREADS) {
+    const int h = i >> 5, c = i & 31;
+    rs.q[h * 32 + (c ^ ((h >> 2) & 7))] = __ldg(qg + i);
+  }
+  if (tid < HI) rs.w[tid] = P.w[qrow * HI + tid];
+  __syncthreads();
+  {  // |w_h| * ||q_h||: 8 threads per head
+    const int h = tid >> 3, part = tid & 7;
+    float ss = 0.f;
+#pragma unroll
+    for (int c = part * 4; c < part * 4 + 4; ++c) {
+      const float4 v = rs.q[h * 32 + (c ^ ((h >> 2) & 7))];
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    if (part == 0) rs.wq[h] = fabsf(rs.w[h]) * sqrtf(ss);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float t = rs.wq[lane] + rs.wq[lane + 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    // the factor covers the fp32 rounding of the norms and sums above
+    if (lane == 0) rs.eps = P.eps_c * t * P.kmax[b] * (1.f + 0x1p-10f) + 1e-30f;
+  }
+  __syncthreads();
+  const float e2 = 2.f * rs.eps;
+  const float vk = from_ordered(kth);
+  const float upper = __fadd_ru(vk, e2), lower = __fsub_rd(vk, e2);
+  uint32_t band = 0, nb = 0;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    if (e < nv) {
+      const float a = from_ordered(key[e]);
+      if (a > upper) {
+        key[e] = 0xffffffffu;
+      } else if (a < lower) {
+        key[e] = 0u;
+      } else {
+        band |= 1u << e;
+        ++nb;
+      }
+    }
+  }
+  const uint32_t pos0 = block_scan_reg(nb, sh);
+  const uint32_t n_band = sh.total;
+  const float* kb = P.k + static_cast<int64_t>(b) * P.k_batch_stride * DI;
+  for (uint32_t r0 = 0; r0 < n_band; r0 += BAND_CAP) {
+    const uint32_t cnt = min(static_cast<uint32_t>(BAND_CAP), n_band - r0);
+    {
+      uint32_t pos = pos0;
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if ((band >> e) & 1u) {
+          if (pos >= r0 && pos < r0 + cnt) rs.band_idx[pos - r0] = j0 + e;
+          ++pos;
+        }
+    }
+    __syncthreads();
+    // exact scores: task = (band entry m, head quad); 16 lanes per entry form the partial tree
+    for (int base = warp * 32; base < static_cast<int>(cnt) * 16; base += SEL_THREADS) {
+      const int task = base + lane;
+      const bool valid = task < static_cast<int>(cnt) * 16;
+      const int m = task >> 4, quad = task & 15;
+      float part = 0.f;
+      if (valid) {
+        const float4* kr = reinterpret_cast<const float4*>(kb + static_cast<int64_t>(rs.band_idx[m]) * DI);
+        const int h0 = quad * 4, sw = quad & 7;
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < DI / 4; ++c) {
+          const float4 kv = __ldg(kr + c);
+          const int cc = c ^ sw;
+          const float4 a0 = rs.q[(h0 + 0) * 32 + cc], a1 = rs.q[(h0 + 1) * 32 + cc];
+          const float4 a2 = rs.q[(h0 + 2) * 32 + cc], a3 = rs.q[(h0 + 3) * 32 + cc];
+          d0 = __fmaf_rn(a0.x, kv.x, d0); d0 = __fmaf_rn(a0.y, kv.y, d0);
+          d0 = __fmaf_rn(a0.z, kv.z, d0); d0 = __fmaf_rn(a0.w, kv.w, d0);
+          d1 = __fmaf_rn(a1.x, kv.x, d1); d1 = __fmaf_rn(a1.y, kv.y, d1);
+          d1 = __fmaf_rn(a1.z, kv.z, d1); d1 = __fmaf_rn(a1.w, kv.w, d1);
+          d2 = __fmaf_rn(a2.x, kv.x, d2); d2 = __fmaf_rn(a2.y, kv.y, d2);
+          d2 = __fmaf_rn(a2.z, kv.z, d2); d2 = __fmaf_rn(a2.w, kv.w, d2);
+          d3 = __fmaf_rn(a3.x, kv.x, d3); d3 = __fmaf_rn(a3.y, kv.y, d3);
+          d3 = __fmaf_rn(a3.z, kv.z, d3); d3 = __fmaf_rn(a3.w, kv.w, d3);
+        }
+        part = __fmaf_rn(rs.w[h0 + 0], d0 > 0.f ? d0 : 0.f, part);
+        part = __fmaf_rn(rs.w[h0 + 1], d1 > 0.f ? d1 : 0.f, part);
+        part = __fmaf_rn(rs.w[h0 + 2], d2 > 0.f ? d2 : 0.f, part);
+        part = __fmaf_rn(rs.w[h0 + 3], d3 > 0.f ? d3 : 0.f, part);
+      }
+      // balanced tree over the 16 partials: pairs (2t, 2t+1) at every level
+      part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 1));
+      part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 2));
+      part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 4));
+      part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 8));
+      if (valid && quad == 0) rs.band_e[m] = part;
+    }
+    __syncthreads();
+    {
+      uint32_t pos = pos0;
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if ((band >> e) & 1u) {
+          if (pos >= r0 && pos < r0 + cnt) key[e] = ordered_bits(rs.band_e[pos - r0]);
+          ++pos;
+        }
+    }
+    __syncthreads();
+  }
+}
+
+template <int PER, bool REFINE>
+__global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P) {
+  __shared__ SelRegShared sh;
+  extern __shared__ __align__(16) uint8_t sel_dyn[];
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t qrow = blockIdx.x;
+  const int b = static_cast<int>(qrow / P.s);
+  const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
+  int32_t* out = P.out + qrow * P.out_stride + P.out_col;
+  const int k = P.top_k;
+
+  if (P.win_base != nullptr)
+    for (int c = tid; c < P.window; c += SEL_THREADS) out[c - P.window] = window_row(P, b, P.positions[qrow], c);
+  if (nvis <= k) {
+    for (int r = tid; r < k; r += SEL_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
+    return;
+  }
+  const int j0 = tid * PER;
+  const float* sc = P.scores + qrow * P.n_pad + j0;
+  uint32_t key[PER];
+  if ((P.n_pad & 3) == 0 && j0 + PER <= nvis) {
+#pragma unroll
+    for (int e = 0; e < PER; e += 4) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(sc + e));
+      key[e] = ordered_bits(v.x);
+      key[e + 1] = ordered_bits(v.y);
+      key[e + 2] = ordered_bits(v.z);
+      key[e + 3] = ordered_bits(v.w);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < PER; ++e) key[e] = (j0 + e < nvis) ? ordered_bits(__ldcg(sc + e)) : 0u;
+  }
+  // number of valid keys of this thread (the rest are padding and never counted)
+  const int nv = max(0, min(PER, nvis - j0));
+  if constexpr (REFINE) refine_band<PER>(P, qrow, b, k, key, nv, j0, sh, *reinterpret_cast<RefineSmem*>(sel_dyn));
+  uint32_t prefix, kleft, shift;
+  bool whole;
+  radix_levels<PER>(key, nv, static_cast<uint32_t>(k), true, sh, prefix, shift, kleft, whole);
   // keys equal to the full 32-bit prefix (shift == 0, not whole): the kleft lowest indices
   int32_t tau_last = 0x7fffffff;
   if (!whole) {
@@ -836,10 +1011,26 @@ inline cudaError_t launch_scores(const ScoreParams& S, cudaStream_t st) {
 // the register-resident kernel up to 16384 visible keys, the shared-memory one above
 inline cudaError_t launch_select(const SelectParams& L, unsigned rows, cudaStream_t st) {
   const dim3 g(rows), blk(SEL_THREADS);
-  if (L.n_keys <= SEL_THREADS * 4) return launch_pdl(select_reg_kernel<4>, g, blk, 0, st, L);
-  if (L.n_keys <= SEL_THREADS * 8) return launch_pdl(select_reg_kernel<8>, g, blk, 0, st, L);
-  if (L.n_keys <= SEL_THREADS * 16) return launch_pdl(select_reg_kernel<16>, g, blk, 0, st, L);
-  if (L.n_keys <= SEL_THREADS * 32) return launch_pdl(select_reg_kernel<32>, g, blk, 0, st, L);
+  if (L.refine) {
+    constexpr size_t rsm = sizeof(RefineSmem);
+    static bool rattr = false;
+    if (!rattr) {
+      for (auto fn : {select_reg_kernel<4, true>, select_reg_kernel<8, true>, select_reg_kernel<16, true>,
+                      select_reg_kernel<32, true>}) {
+        const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(rsm));
+        if (e != cudaSuccess) return e;
+      }
+      rattr = true;
+    }
+    if (L.n_keys <= SEL_THREADS * 4) return launch_pdl(select_reg_kernel<4, true>, g, blk, rsm, st, L);
+    if (L.n_keys <= SEL_THREADS * 8) return launch_pdl(select_reg_kernel<8, true>, g, blk, rsm, st, L);
+    if (L.n_keys <= SEL_THREADS * 16) return launch_pdl(select_reg_kernel<16, true>, g, blk, rsm, st, L);
+    return launch_pdl(select_reg_kernel<32, true>, g, blk, rsm, st, L);
+  }
+  if (L.n_keys <= SEL_THREADS * 4) return launch_pdl(select_reg_kernel<4, false>, g, blk, 0, st, L);
+  if (L.n_keys <= SEL_THREADS * 8) return launch_pdl(select_reg_kernel<8, false>, g, blk, 0, st, L);
+  if (L.n_keys <= SEL_THREADS * 16) return launch_pdl(select_reg_kernel<16, false>, g, blk, 0, st, L);
+  if (L.n_keys <= SEL_THREADS * 32) return launch_pdl(select_reg_kernel<32, false>, g, blk, 0, st, L);
   static bool attr = false;
   if (!attr) {
     const cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -858,10 +1049,32 @@ DSV4_ERROR_READER(indexer)
 
 using namespace dsv4;
 
+namespace {
+// scoring method for a call: 1 exact FMA scores, 2 tensor-core filter + exact band; -1 unavailable
+int resolve_mode(const dsv4_indexer_params* p) {
+  if (p->mode == 1) return 1;
+  const bool tc_ok = p->heads == idx::HI && p->n_keys <= idx::SEL_THREADS * 32;
+  if (p->mode == 2) return tc_ok ? 2 : -1;
+  if (p->mode != 0) return -1;
+  return (tc_ok && static_cast<int64_t>(p->batch) * p->s >= 256 && p->n_keys > p->top_k) ? 2 : 1;
+}
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+// workspace: [scores rows x n_pad fp32] then, for mode 2, [key tile images] [max key norm per batch]
+size_t workspace_layout(const dsv4_indexer_params* p, int mode, size_t* off_kimg, size_t* off_kmax) {
+  const int64_t n_pad = (p->n_keys + 3) / 4 * 4;
+  const size_t sc = static_cast<size_t>(static_cast<int64_t>(p->batch) * p->s * n_pad * sizeof(float));
+  if (mode != 2) return sc;
+  *off_kimg = round_up(sc, 1024);
+  *off_kmax = *off_kimg + itc::kimg_bytes(p->batch, p->n_keys);
+  return *off_kmax + round_up(sizeof(float) * p->batch, 256);
+}
+}  // namespace
+
 extern "C" size_t dsv4_indexer_topk_workspace_size(const dsv4_indexer_params* p) {
   if (!p || p->batch <= 0 || p->s <= 0 || p->n_keys <= 0) return 0;
-  const int64_t n_pad = (p->n_keys + 3) / 4 * 4;
-  return static_cast<size_t>(static_cast<int64_t>(p->batch) * p->s * n_pad * sizeof(float));
+  size_t a = 0, b = 0;
+  const int mode = resolve_mode(p);
+  return workspace_layout(p, mode < 0 ? 1 : mode, &a, &b);
 }
 
 extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
@@ -884,15 +1097,37 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
                  "dsv4_indexer_topk: window columns need positions and out_col >= window");
   const int64_t rows = static_cast<int64_t>(p->batch) * p->s;
   DSV4_CHECK_ARG(rows <= 2147483647LL, "dsv4_indexer_topk: too many queries");
-  const size_t need = dsv4_indexer_topk_workspace_size(p);
+  const int mode = resolve_mode(p);
+  DSV4_CHECK_ARG(mode > 0, "dsv4_indexer_topk: mode %d unavailable (mode 2 needs n_keys <= %d)", p->mode,
+                 idx::SEL_THREADS * 32);
+  size_t off_kimg = 0, off_kmax = 0;
+  const size_t need = workspace_layout(p, mode, &off_kimg, &off_kmax);
   if (p->workspace == nullptr || p->workspace_bytes < need) {
     set_error("dsv4_indexer_topk: workspace of %zu bytes needed, %zu given", need, p->workspace_bytes);
     return DSV4_ERR_WORKSPACE;
   }
   float* scores = p->scores_out ? p->scores_out : reinterpret_cast<float*>(p->workspace);
   const int n_pad = p->scores_out ? p->n_keys : (p->n_keys + 3) / 4 * 4;
+  float* kmax = nullptr;
+  if (mode == 2) {
+    itc::ApproxArgs A = {};
+    A.q = p->q;
+    A.w = p->w;
+    A.k = p->k;
+    A.scores = scores;
+    A.batch = p->batch;
+    A.s = p->s;
+    A.n_keys = p->n_keys;
+    A.n_pad = n_pad;
+    A.k_batch_stride = p->k_batch_stride;
+    A.positions = p->positions;
+    A.ratio = p->ratio;
+    A.kimg = static_cast<uint8_t*>(p->workspace) + off_kimg;
+    A.kmax = kmax = reinterpret_cast<float*>(static_cast<uint8_t*>(p->workspace) + off_kmax);
+    DSV4_CUDA_CHECK(itc::launch_approx_scores(A, as_stream(stream)));
+  }
 
-  idx::ScoreParams S;
+  idx::ScoreParams S = {};
   S.q = p->q;
   S.w = p->w;
   S.k = p->k;
@@ -904,9 +1139,9 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
   S.k_batch_stride = p->k_batch_stride;
   S.positions = p->positions;
   S.ratio = p->ratio;
-  DSV4_CUDA_CHECK(idx::launch_scores(S, as_stream(stream)));
+  if (mode == 1) DSV4_CUDA_CHECK(idx::launch_scores(S, as_stream(stream)));
 
-  idx::SelectParams L;
+  idx::SelectParams L = {};
   L.scores = scores;
   L.out = p->out;
   L.batch = p->batch;
@@ -925,6 +1160,15 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
   L.win_base = p->win_base;
   L.window = p->window;
   L.window_linear = p->window_linear;
+  if (mode == 2) {
+    L.refine = 1;
+    L.q = p->q;
+    L.w = p->w;
+    L.k = p->k;
+    L.k_batch_stride = p->k_batch_stride;
+    L.kmax = kmax;
+    L.eps_c = idx::EPS_C;
+  }
   DSV4_CUDA_CHECK(idx::launch_select(L, static_cast<unsigned>(rows), as_stream(stream)));
   return DSV4_OK;
 }
@@ -1006,7 +1250,7 @@ extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* str
 
   // The scores are written for every visible key before the selection reads them, and entries past
   // a query's visible range are never read, so nothing in the scratch needs clearing between calls.
-  idx::ScoreParams S;
+  idx::ScoreParams S = {};
   S.q = p->q;
   S.w = p->w;
   S.k = p->k;
@@ -1028,7 +1272,7 @@ extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* str
   idx::score_kernel<<<g1, idx::THREADS, sizeof(idx::ScoreSmem), as_stream(stream)>>>(S);
   DSV4_LAUNCH_CHECK("indexer score_kernel (noalloc)");
 
-  idx::SelectParams L;
+  idx::SelectParams L = {};
   L.scores = scores;
   L.out = p->out;
   L.batch = p->batch;

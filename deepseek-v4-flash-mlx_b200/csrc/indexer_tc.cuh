@@ -1,0 +1,43 @@
+// Tensor-core filter of the lightning indexer (internal interface between indexer.cu and
+// indexer_tc.cu).
+//
+// approx score A[i, j] = sum_h w[i,h] * relu(q[i,h,:] . k[j,:]) with every dot product taken on
+// tcgen05 from a two-term bf16 split of both operands (q = qh + ql, k = kh + kl; qh.kh + qh.kl +
+// ql.kh, fp32 accumulate). The select kernel then bounds |A - E| (E: the canonical fp32 score) by
+// eps_i = C * sum_h |w[i,h]| * ||q[i,h,:]|| * max_j ||k[j,:]||, keeps the keys that are certainly in
+// the top-k, drops those certainly out, and rescores only the keys in between in the canonical order.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace dsv4 {
+namespace itc {
+
+constexpr int BM = 128;                 // keys per tile
+constexpr int TILE_BYTES = 64 * 1024;   // one tile's bf16 hi and lo image (2 x 2 swizzled slabs)
+
+struct ApproxArgs {
+  const float* q;       // [batch*s, 64, 128]
+  const float* w;       // [batch*s, 64]
+  const float* k;       // [batch, n_keys, 128] (batch stride k_batch_stride rows)
+  float* scores;        // [batch*s, n_pad] approximate scores
+  int32_t batch, s, n_keys, n_pad;
+  int64_t k_batch_stride;
+  const int32_t* positions;
+  int32_t ratio;
+  uint8_t* kimg;        // workspace: [batch][tiles][TILE_BYTES]
+  float* kmax;          // workspace: [batch] max key norm (zeroed by the launcher)
+};
+
+__host__ __device__ inline int key_tiles(int n_keys) { return (n_keys + BM - 1) / BM; }
+inline size_t kimg_bytes(int batch, int n_keys) {
+  return static_cast<size_t>(batch) * key_tiles(n_keys) * TILE_BYTES;
+}
+
+// key image + norms, then the approximate scores (two launches on `stream`)
+cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream);
+
+}  // namespace itc
+}  // namespace dsv4

@@ -14,7 +14,7 @@ from . import _lib as L
 
 
 def _params(q, w, k, out, top_k, positions, ratio, out_col, out_offset, block_table, page, scores_out,
-            win_base=None, window=0, window_linear=False):
+            win_base=None, window=0, window_linear=False, mode=0):
     b, s, h, di = q.shape
     p = L.IndexerParams()
     p.q, p.w, p.k, p.out = L.ptr(q), L.ptr(w), L.ptr(k), L.ptr(out)
@@ -30,6 +30,7 @@ def _params(q, w, k, out, top_k, positions, ratio, out_col, out_offset, block_ta
     p.win_base = L.ptr(win_base) if win_base is not None else None
     p.window = window
     p.window_linear = int(window_linear)
+    p.mode = mode
     return p
 
 
@@ -42,16 +43,16 @@ def _run(p, device, stream_ref):
 
 @torch.library.custom_op("dsv4::indexer_topk", mutates_args=(), device_types="cuda")
 def _indexer_op(q_idx: torch.Tensor, w: torch.Tensor, k_idx: torch.Tensor, top_k: int,
-                positions: torch.Tensor | None, ratio: int) -> torch.Tensor:
+                positions: torch.Tensor | None, ratio: int, mode: int = 0) -> torch.Tensor:
     b, s = q_idx.shape[0], q_idx.shape[1]
     out = torch.empty((b, s, top_k), dtype=torch.int32, device=q_idx.device)
-    p = _params(q_idx, w, k_idx, out, top_k, positions, ratio, 0, 0, None, 0, None)
+    p = _params(q_idx, w, k_idx, out, top_k, positions, ratio, 0, 0, None, 0, None, mode=mode)
     _run(p, q_idx.device, q_idx)
     return out
 
 
 @_indexer_op.register_fake
-def _(q_idx, w, k_idx, top_k, positions, ratio):
+def _(q_idx, w, k_idx, top_k, positions, ratio, mode=0):
     return torch.empty((q_idx.shape[0], q_idx.shape[1], top_k), dtype=torch.int32, device=q_idx.device)
 
 
@@ -69,29 +70,32 @@ def _prep(q_idx, w, k_idx, positions):
     return q_idx.contiguous(), w.contiguous(), k_idx.contiguous(), positions, squeeze
 
 
-def indexer_topk(q_idx, w, k_idx, top_k, positions=None, ratio=4):
+def indexer_topk(q_idx, w, k_idx, top_k, positions=None, ratio=4, mode=0):
     """q_idx [b, s, 64, 128] (or [s, 64, 128]), w [b, s, 64], k_idx [b, n, 128] fp32 ->
     int32 [b, s, top_k] key indices. With `positions`, query i sees keys j < (positions[i]+1)//ratio
-    (the causal compressed-block rule of oracle/decode_engine.py:112)."""
+    (the causal compressed-block rule of oracle/decode_engine.py:112). `mode`: 1 scores every key
+    in the fixed fp32 order, 2 filters with tensor-core scores and rescores the uncertain band
+    exactly, 0 picks (2 for prefill-shaped calls); the result is the same bit for bit."""
     q_idx, w, k_idx, positions, squeeze = _prep(q_idx, w, k_idx, positions)
-    out = _indexer_op(q_idx, w, k_idx, int(top_k), positions, int(ratio))
+    out = _indexer_op(q_idx, w, k_idx, int(top_k), positions, int(ratio), int(mode))
     return out[0] if squeeze else out
 
 
-def indexer_scores(q_idx, w, k_idx, positions=None, ratio=4):
+def indexer_scores(q_idx, w, k_idx, positions=None, ratio=4, mode=1):
     """Raw fp32 scores [b, s, n] (entries beyond each query's visible range are left undefined);
-    exposed for verification against the CPU oracle."""
+    exposed for verification against the CPU oracle. mode 1: the exact scores; mode 2: the
+    tensor-core approximate scores of the filter stage."""
     q_idx, w, k_idx, positions, squeeze = _prep(q_idx, w, k_idx, positions)
     b, s = q_idx.shape[0], q_idx.shape[1]
     scores = torch.full((b, s, k_idx.shape[1]), float("nan"), dtype=torch.float32, device=q_idx.device)
     out = torch.empty((b, s, 1), dtype=torch.int32, device=q_idx.device)
-    p = _params(q_idx, w, k_idx, out, 1, positions, ratio, 0, 0, None, 0, scores)
+    p = _params(q_idx, w, k_idx, out, 1, positions, ratio, 0, 0, None, 0, scores, mode=int(mode))
     _run(p, q_idx.device, q_idx)
     return scores[0] if squeeze else scores
 
 
 def indexer_topk_into(out, q_idx, w, k_idx, top_k, positions=None, ratio=4, out_col=0, out_offset=0,
-                      block_table=None, page=0, win_base=None, window=0, window_linear=False):
+                      block_table=None, page=0, win_base=None, window=0, window_linear=False, mode=0):
     """Write the selection into columns [out_col, out_col+top_k) of an existing int32 index buffer
     out [b, s, T], mapping key j to pool row out_offset + j, or through a block table
     (block_table[b, j // page] * page + j % page + out_offset). Used by the decode and prefill
@@ -102,6 +106,6 @@ def indexer_topk_into(out, q_idx, w, k_idx, top_k, positions=None, ratio=4, out_
     if out.dtype != torch.int32 or not out.is_contiguous():
         raise TypeError("indexer_topk_into: out must be a contiguous int32 tensor")
     p = _params(q_idx, w, k_idx, out, int(top_k), positions, int(ratio), int(out_col), int(out_offset),
-                block_table, int(page), None, win_base, int(window), window_linear)
+                block_table, int(page), None, win_base, int(window), window_linear, int(mode))
     _run(p, q_idx.device, q_idx)
     return out
