@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       for (int sl = 0; sl < 8; ++sl)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tmem + COL_S, sdesc(ks + sl * SLAB_KV + kk * 32, 16, 1024),
+          mma16(tmem + COL_S, sdesc(ks + sl * SLAB_KV + kk * 32, 16, 1024),
                   sdesc(qs + sl * SLAB_Q + kk * 32, 16, 1024), id_s, (sl | kk) ? 1u : 0u);
       mma_commit(&sm.bar_s);
     }
@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_bf16(tmem + COL_O + mt * HB, sdesc(ks + 2 * mt * SLAB_KV + kk * 2048, SLAB_KV, 1024),
+          mma16(tmem + COL_O + mt * HB, sdesc(ks + 2 * mt * SLAB_KV + kk * 2048, SLAB_KV, 1024),
                   sdesc(ps + kk * 2048, 16384, 1024), id_o, (tile > 0 || kk > 0) ? 1u : 0u);
       mma_commit(&sm.bar_o);
     }

@@ -649,10 +649,11 @@ __device__ __forceinline__ void warp_hist_add(uint32_t* hist, uint32_t bin, uint
 // locate the boundary of the top k. With stop_whole, a level whose boundary bin is taken whole ends
 // the search (prefix then fixes the bits at and above shift); without it the search runs down to
 // shift 0 and prefix is the k-th largest key itself. kleft = keys still needed from the boundary.
+// max_levels < 4 stops early: the k-th largest key then lies in [prefix, prefix + 2^shift).
 template <int PER>
 __device__ __forceinline__ void radix_levels(const uint32_t (&key)[PER], int nv, uint32_t k, bool stop_whole,
                                              SelRegShared& sh, uint32_t& prefix, uint32_t& shift, uint32_t& kleft,
-                                             bool& whole) {
+                                             bool& whole, int max_levels = 4) {
   const int tid = threadIdx.x, lane = tid & 31;
 
 #pragma unroll
@@ -693,7 +694,7 @@ __device__ __forceinline__ void radix_levels(const uint32_t (&key)[PER], int nv,
   }
   // levels 2..4 over the keys inside the boundary bin: bits 19..12, 11..4, 3..0
 #pragma unroll 1
-  for (int level = 0; level < 3 && !(whole && stop_whole); ++level) {
+  for (int level = 0; level < max_levels - 1 && !(whole && stop_whole); ++level) {
     const uint32_t width = level < 2 ? 8u : 4u;
     const uint32_t nshift = shift - width;
     const uint32_t nb = 1u << width;
@@ -746,7 +747,7 @@ __device__ __forceinline__ void radix_levels(const uint32_t (&key)[PER], int nv,
 
 
 constexpr int BAND_CAP = 512;  // band keys rescored per round
-constexpr float EPS_C = 0x1p-12f;
+constexpr float EPS_C = 0x1p-14f;
 
 struct RefineSmem {
   float4 q[HI * DI / 4];   // the query's 64 x 128 indexer q; chunk c of head h at c ^ ((h / 4) % 8)
@@ -754,6 +755,7 @@ struct RefineSmem {
   float wq[HI];
   int32_t band_idx[BAND_CAP];
   float band_e[BAND_CAP];
+  uint8_t band_take[BAND_CAP];
   float eps;
 };
 
@@ -762,21 +764,27 @@ __device__ __forceinline__ float from_ordered(uint32_t u) {
 }
 
 // Exact refinement of approximate scores A with |A - score| <= eps for every key (eps from the
-// query's |w_h| ||q_h|| and the largest key norm). With v the k-th largest A:
-//  - a key with A > v + 2 eps is in the top k: any key that ties or beats it has
+// query's |w_h| ||q_h|| and the largest key norm). With v the k-th largest A, bracketed as
+// lo <= v <= hi by two radix levels (20 of the 32 key bits):
+//  - a key with A > hi + 2 eps is in the top k: any key that ties or beats it has
 //    A >= score - eps >= its score - eps > v, and fewer than k keys have A > v;
-//  - a key with A < v - 2 eps is not: the k keys with A >= v all have score >= v - eps > its score.
-// Keys in between get their exact score in the canonical fp32 order; the certain ones are pinned to
-// the largest / smallest ordered key, so the ordinary selection that follows returns the exact top k
-// (at least k minus the certain count of keys lie in the band, since every key with A >= v is there
-// or certain). Valid for inputs without subnormal elements.
+//  - a key with A < lo - 2 eps is not: the k keys with A >= v all have score >= v - eps > its score.
+// Keys in between (the band; at least k minus the certain count of them, since every key with
+// A >= v is there or certain) get their exact score in the canonical fp32 order. When the band fits
+// one round (BAND_CAP keys) the missing keys are taken from it by rank, (score desc, index asc), and
+// the result is written here (returns true). A wider band leaves the certain keys pinned to the
+// largest / smallest ordered key and the band keys holding their exact scores, for the ordinary
+// selection that follows (returns false). Valid for finite inputs (see the error analysis of the
+// approximate scores).
 template <int PER>
-__device__ __forceinline__ void refine_band(const SelectParams& P, int64_t qrow, int b, int k, uint32_t (&key)[PER],
-                                            int nv, int j0, SelRegShared& sh, RefineSmem& rs) {
+__device__ __forceinline__ bool refine_band(const SelectParams& P, int64_t qrow, int b, int k, uint32_t (&key)[PER],
+                                            int nv, int j0, SelRegShared& sh, RefineSmem& rs, int32_t* out) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t kth, shift, kleft;
+  // bracket [lo, hi] of the k-th largest approximate score: the first two radix levels (20 bits)
+  uint32_t pfx, shift, kleft;
   bool whole;
-  radix_levels<PER>(key, nv, static_cast<uint32_t>(k), false, sh, kth, shift, kleft, whole);
+  radix_levels<PER>(key, nv, static_cast<uint32_t>(k), false, sh, pfx, shift, kleft, whole, 2);
+  const float lo = from_ordered(pfx), hi = from_ordered(pfx | ((1u << shift) - 1u));
 
   const float4* qg = reinterpret_cast<const float4*>(P.q + qrow * (HI * DI));
   for (int i = tid; i < HI * DI / 4; i += SEL_THREADS) {
@@ -811,15 +819,15 @@ __device__ __forceinline__ void refine_band(const SelectParams& P, int64_t qrow,
   }
   __syncthreads();
   const float e2 = 2.f * rs.eps;
-  const float vk = from_ordered(kth);
-  const float upper = __fadd_ru(vk, e2), lower = __fsub_rd(vk, e2);
-  uint32_t band = 0, nb = 0;
+  const float upper = __fadd_ru(hi, e2), lower = __fsub_rd(lo, e2);
+  uint32_t band = 0, nb = 0, nin = 0;
 #pragma unroll
   for (int e = 0; e < PER; ++e) {
     if (e < nv) {
       const float a = from_ordered(key[e]);
       if (a > upper) {
         key[e] = 0xffffffffu;
+        ++nin;
       } else if (a < lower) {
         key[e] = 0u;
       } else {
@@ -830,6 +838,8 @@ __device__ __forceinline__ void refine_band(const SelectParams& P, int64_t qrow,
   }
   const uint32_t pos0 = block_scan_reg(nb, sh);
   const uint32_t n_band = sh.total;
+  const uint32_t in_before = block_scan_reg(nin, sh);
+  const uint32_t n_in = sh.total;
   const float* kb = P.k + static_cast<int64_t>(b) * P.k_batch_stride * DI;
   for (uint32_t r0 = 0; r0 < n_band; r0 += BAND_CAP) {
     const uint32_t cnt = min(static_cast<uint32_t>(BAND_CAP), n_band - r0);
@@ -843,44 +853,98 @@ __device__ __forceinline__ void refine_band(const SelectParams& P, int64_t qrow,
         }
     }
     __syncthreads();
-    // exact scores: task = (band entry m, head quad); 16 lanes per entry form the partial tree
-    for (int base = warp * 32; base < static_cast<int>(cnt) * 16; base += SEL_THREADS) {
+    // exact scores: task = (4 band entries, head quad); the 16 lanes of a quad set form the partial
+    // tree. Each thread keeps 4 heads x 4 keys of fmaf chains, so a q chunk read from shared memory
+    // serves 4 keys and a key chunk 4 heads.
+    const int n_groups = (static_cast<int>(cnt) + 3) >> 2;
+    for (int base = warp * 32; base < n_groups * 16; base += SEL_THREADS) {
       const int task = base + lane;
-      const bool valid = task < static_cast<int>(cnt) * 16;
-      const int m = task >> 4, quad = task & 15;
-      float part = 0.f;
-      if (valid) {
-        const float4* kr = reinterpret_cast<const float4*>(kb + static_cast<int64_t>(rs.band_idx[m]) * DI);
-        const int h0 = quad * 4, sw = quad & 7;
-        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-#pragma unroll 4
-        for (int c = 0; c < DI / 4; ++c) {
-          const float4 kv = __ldg(kr + c);
-          const int cc = c ^ sw;
-          const float4 a0 = rs.q[(h0 + 0) * 32 + cc], a1 = rs.q[(h0 + 1) * 32 + cc];
-          const float4 a2 = rs.q[(h0 + 2) * 32 + cc], a3 = rs.q[(h0 + 3) * 32 + cc];
-          d0 = __fmaf_rn(a0.x, kv.x, d0); d0 = __fmaf_rn(a0.y, kv.y, d0);
-          d0 = __fmaf_rn(a0.z, kv.z, d0); d0 = __fmaf_rn(a0.w, kv.w, d0);
-          d1 = __fmaf_rn(a1.x, kv.x, d1); d1 = __fmaf_rn(a1.y, kv.y, d1);
-          d1 = __fmaf_rn(a1.z, kv.z, d1); d1 = __fmaf_rn(a1.w, kv.w, d1);
-          d2 = __fmaf_rn(a2.x, kv.x, d2); d2 = __fmaf_rn(a2.y, kv.y, d2);
-          d2 = __fmaf_rn(a2.z, kv.z, d2); d2 = __fmaf_rn(a2.w, kv.w, d2);
-          d3 = __fmaf_rn(a3.x, kv.x, d3); d3 = __fmaf_rn(a3.y, kv.y, d3);
-          d3 = __fmaf_rn(a3.z, kv.z, d3); d3 = __fmaf_rn(a3.w, kv.w, d3);
-        }
-        part = __fmaf_rn(rs.w[h0 + 0], d0 > 0.f ? d0 : 0.f, part);
-        part = __fmaf_rn(rs.w[h0 + 1], d1 > 0.f ? d1 : 0.f, part);
-        part = __fmaf_rn(rs.w[h0 + 2], d2 > 0.f ? d2 : 0.f, part);
-        part = __fmaf_rn(rs.w[h0 + 3], d3 > 0.f ? d3 : 0.f, part);
+      const int grp = task >> 4, quad = task & 15;
+      const bool valid = grp < n_groups;
+      const int m0 = grp * 4;
+      const float4* kr[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int m = (valid && m0 + e < static_cast<int>(cnt)) ? m0 + e : 0;
+        kr[e] = reinterpret_cast<const float4*>(kb + static_cast<int64_t>(rs.band_idx[m]) * DI);
       }
-      // balanced tree over the 16 partials: pairs (2t, 2t+1) at every level
-      part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 1));
-      part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 2));
-      part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 4));
-      part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 8));
-      if (valid && quad == 0) rs.band_e[m] = part;
+      const int h0 = quad * 4, sw = quad & 7;
+      float d[4][4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) d[a][e] = 0.f;
+      if (valid) {
+#pragma unroll 2
+        for (int c = 0; c < DI / 4; ++c) {
+          float4 kv[4], qv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) kv[e] = __ldg(kr[e] + c);
+#pragma unroll
+          for (int a = 0; a < 4; ++a) qv[a] = rs.q[(h0 + a) * 32 + (c ^ sw)];
+#pragma unroll
+          for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              d[a][e] = __fmaf_rn(qv[a].x, kv[e].x, d[a][e]);
+              d[a][e] = __fmaf_rn(qv[a].y, kv[e].y, d[a][e]);
+              d[a][e] = __fmaf_rn(qv[a].z, kv[e].z, d[a][e]);
+              d[a][e] = __fmaf_rn(qv[a].w, kv[e].w, d[a][e]);
+            }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float part = 0.f;
+#pragma unroll
+        for (int a = 0; a < 4; ++a) part = __fmaf_rn(rs.w[h0 + a], d[a][e] > 0.f ? d[a][e] : 0.f, part);
+        // balanced tree over the 16 partials: pairs (2t, 2t+1) at every level
+        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 1));
+        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 2));
+        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 4));
+        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 8));
+        if (valid && quad == 0 && m0 + e < static_cast<int>(cnt)) rs.band_e[m0 + e] = part;
+      }
     }
     __syncthreads();
+    if (n_band <= static_cast<uint32_t>(BAND_CAP)) {
+      // one round: take the (k - n_in) best band entries by (score desc, index asc); the entries are
+      // in ascending key order, so the index order is the entry order
+      const uint32_t need = static_cast<uint32_t>(k) - n_in;
+      for (int m = tid; m < static_cast<int>(n_band); m += SEL_THREADS) {
+        const uint32_t km = ordered_bits(rs.band_e[m]);
+        uint32_t rank = 0;
+        for (int m2 = 0; m2 < static_cast<int>(n_band); ++m2) {
+          const uint32_t k2 = ordered_bits(rs.band_e[m2]);
+          rank += (k2 > km) || (k2 == km && m2 < m);
+        }
+        rs.band_take[m] = rank < need ? 1 : 0;
+      }
+      __syncthreads();
+      // write the taken keys in ascending order: certain ones and the chosen band entries
+      uint32_t cnt_t = 0;
+      {
+        uint32_t pos = pos0;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+          const bool bnd = (band >> e) & 1u;
+          cnt_t += (e < nv && key[e] == 0xffffffffu && !bnd) || (bnd && rs.band_take[pos]);
+          pos += bnd;
+        }
+      }
+      uint32_t o = block_scan_reg(cnt_t, sh);
+      {
+        uint32_t pos = pos0;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+          const bool bnd = (band >> e) & 1u;
+          if ((e < nv && key[e] == 0xffffffffu && !bnd) || (bnd && rs.band_take[pos])) out[o++] = map_key(P, b, j0 + e);
+          pos += bnd;
+        }
+      }
+      (void)in_before;
+      return true;
+    }
     {
       uint32_t pos = pos0;
 #pragma unroll
@@ -892,6 +956,8 @@ __device__ __forceinline__ void refine_band(const SelectParams& P, int64_t qrow,
     }
     __syncthreads();
   }
+  // a wide band (many equal or near-equal scores): the ordinary selection over the pinned keys
+  return false;
 }
 
 template <int PER, bool REFINE>
@@ -931,7 +997,9 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
   }
   // number of valid keys of this thread (the rest are padding and never counted)
   const int nv = max(0, min(PER, nvis - j0));
-  if constexpr (REFINE) refine_band<PER>(P, qrow, b, k, key, nv, j0, sh, *reinterpret_cast<RefineSmem*>(sel_dyn));
+  if constexpr (REFINE) {
+    if (refine_band<PER>(P, qrow, b, k, key, nv, j0, sh, *reinterpret_cast<RefineSmem*>(sel_dyn), out)) return;
+  }
   uint32_t prefix, kleft, shift;
   bool whole;
   radix_levels<PER>(key, nv, static_cast<uint32_t>(k), true, sh, prefix, shift, kleft, whole);
@@ -1059,13 +1127,14 @@ int resolve_mode(const dsv4_indexer_params* p) {
   return (tc_ok && static_cast<int64_t>(p->batch) * p->s >= 256 && p->n_keys > p->top_k) ? 2 : 1;
 }
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-// workspace: [scores rows x n_pad fp32] then, for mode 2, [key tile images] [max key norm per batch]
+// workspace: [scores rows x n_pad fp32] then, for mode 2, [key tile images] [key scales]
+// [max key norm per batch]
 size_t workspace_layout(const dsv4_indexer_params* p, int mode, size_t* off_kimg, size_t* off_kmax) {
   const int64_t n_pad = (p->n_keys + 3) / 4 * 4;
   const size_t sc = static_cast<size_t>(static_cast<int64_t>(p->batch) * p->s * n_pad * sizeof(float));
   if (mode != 2) return sc;
   *off_kimg = round_up(sc, 1024);
-  *off_kmax = *off_kimg + itc::kimg_bytes(p->batch, p->n_keys);
+  *off_kmax = *off_kimg + itc::kimg_bytes(p->batch, p->n_keys) + itc::kinv_bytes(p->batch, p->n_keys);
   return *off_kmax + round_up(sizeof(float) * p->batch, 256);
 }
 }  // namespace
@@ -1123,6 +1192,7 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
     A.positions = p->positions;
     A.ratio = p->ratio;
     A.kimg = static_cast<uint8_t*>(p->workspace) + off_kimg;
+    A.kinv = reinterpret_cast<float*>(A.kimg + itc::kimg_bytes(p->batch, p->n_keys));
     A.kmax = kmax = reinterpret_cast<float*>(static_cast<uint8_t*>(p->workspace) + off_kmax);
     DSV4_CUDA_CHECK(itc::launch_approx_scores(A, as_stream(stream)));
   }

@@ -1,18 +1,27 @@
 // Approximate lightning-indexer scores on the 5th-generation tensor cores (the filter stage of the
 // bit-exact top-k; the error bound and the exact rescoring live with the selection in indexer.cu).
 //
-// key_image_kernel: every key row (fp32) -> bf16 hi = rn(k), lo = rn(k - hi), written as the shared
-//   memory image of its 128-key tile ([hi slab 0 | hi slab 1 | lo slab 0 | lo slab 1], 128-byte
-//   swizzled, 16 KB each) so that one bulk copy per half lands a tile ready for the MMA; and the
-//   maximum key norm per batch entry (an upper bound for the error term).
+// Operands are split into two fp16 terms after an exact power-of-two scaling of every row (a key,
+// or one head of a query) that brings its largest element into [2^14, 2^15):
+//   x * 2^s = xh + xl + d,  xh = rn16(x * 2^s),  xl = rn16(x * 2^s - xh),  |d| <= 2^-22 |x * 2^s|
+// and q.k is taken as (qh.kh + qh.kl + ql.kh) * 2^-(s_q + s_k), three fp16 MMAs with fp32
+// accumulation; the dropped terms are below 3.01 * 2^-22 * sum_i |q_i k_i|.
+//
+// key_image_kernel: every key row -> its scaled fp16 hi / lo terms written as the shared-memory image
+//   of its 128-key tile: two slab groups (dims 0-63, 64-127), each [hi slab 16 KB | lo slab 16 KB]
+//   128-byte swizzled, so that one 32 KB bulk copy lands a slab group ready for the MMA; the key's
+//   inverse scale 2^-s_k; and the maximum key norm per batch entry (for the error bound).
 // approx_score_kernel: one CTA per 4 consecutive queries (N = 4 x 64 heads = 256 columns), looping
-//   over the key tiles visible to the last of them. Per tile, on M = 128 keys, K = 128 dims:
-//     S^T[key, (q,h)] = kl.qh  (pass A, reads the lo half)  + kh.qh + kh.ql  (passes B, C)
-//   into one of two 256-column TMEM buffers. Warp 4 (one elected lane) streams the tile halves with
-//   bulk copies and issues the MMAs: the lo half of tile i+1 is fetched while passes B, C of tile i
-//   run, the hi half while pass A of tile i+1 runs. Warps 0-3 (thread = key) read the finished
-//   buffer, fold sum_h w[q,h] * relu(s) for the 4 queries and store 4 scores per key.
+//   over the key tiles visible to the last of them. Per tile and slab group g, on M = 128 keys:
+//     S^T[key, (q,h)] += kl_g.qh_g + kh_g.qh_g + kh_g.ql_g   (12 MMAs of K = 16)
+//   into one of two 256-column TMEM buffers. Warp 4 (one elected lane) issues the bulk copies and the
+//   MMAs; slab groups stream through a ring of three 32 KB slots, so every copy has the MMA time of the
+//   two groups before it to land. Warps 0-7 (thread = key; warp w reads lane quadrant w % 4 for
+//   queries 2 (w / 4) and 2 (w / 4) + 1) read the finished buffer, fold
+//   sum_h (w[q,h] 2^-s_qh) relu(s) per query, scale by 2^-s_k and store the scores.
 // All waits are bounded (1 s); a timeout raises DSV4_ERR_WAIT_TIMEOUT and the CTA winds down.
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "indexer_tc.cuh"
 #include "tcgen05.cuh"
@@ -23,38 +32,66 @@ namespace itc {
 using namespace tc5;
 
 constexpr int DI = 128, HI = 64, QG = 4, NQ = QG * HI;
-constexpr int THREADS = 160;            // warps 0-3 epilogue, warp 4 producer
-constexpr int SLAB_Q = NQ * 128;        // 32 KB: 256 (query, head) rows x 64 bf16 dims
-constexpr int SLAB_K = BM * 128;        // 16 KB: 128 keys x 64 bf16 dims
-constexpr int HALF = 2 * SLAB_K;        // 32 KB: hi or lo of one tile
-static_assert(TILE_BYTES == 2 * HALF, "tile image");
+constexpr int EPI_WARPS = 8;           // two per TMEM lane quadrant, two queries each
+constexpr int THREADS = (EPI_WARPS + 1) * 32;  // + the producer warp
+constexpr int SLAB_Q = NQ * 128;        // 32 KB: 256 (query, head) rows x 64 fp16 dims
+constexpr int SLAB_K = BM * 128;        // 16 KB: 128 keys x 64 fp16 dims
+constexpr int GROUP = 2 * SLAB_K;       // 32 KB: hi + lo slab of one dim group of a tile
+static_assert(TILE_BYTES == 2 * GROUP, "tile image");
 constexpr int TMEM_COLS = 512;
+constexpr int NSLOT = 3;                // slab-group copies in flight: 3 x 32 KB next to the 128 KB of Q
 
 struct Smem {
   alignas(1024) uint8_t qh[2 * SLAB_Q];
   alignas(1024) uint8_t ql[2 * SLAB_Q];
-  alignas(1024) uint8_t kh[HALF];
-  alignas(1024) uint8_t kl[HALF];
-  float w[QG][HI];
-  uint64_t bar_kh, bar_kl, bar_lo_done;
-  uint64_t bar_hi_done[2], bar_free[2];
+  alignas(1024) uint8_t kbuf[NSLOT][GROUP];  // ring of slab groups: group n in slot n % NSLOT
+  float w[QG][HI];                           // w[q,h] * 2^-s_qh
+  uint64_t bar_full[NSLOT], bar_empty[NSLOT];  // slab group landed / its MMAs done
+  uint64_t bar_done[2], bar_free[2];     // TMEM buffer written / read by the epilogue
   uint32_t tmem_base;
   int abort;
 };
 
-__device__ __forceinline__ uint32_t pack2(__nv_bfloat16 a, __nv_bfloat16 b) {
-  return static_cast<uint32_t>(__bfloat16_as_ushort(a)) | (static_cast<uint32_t>(__bfloat16_as_ushort(b)) << 16);
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory above the 227 KB a CTA may opt into");
+
+// exponent s (|s| <= 100) with max_abs * 2^s in [2^14, 2^15); 0 for a zero row
+__device__ __forceinline__ int row_shift(float max_abs) {
+  if (!(max_abs > 0.f)) return 0;
+  int adj = 0;
+  if (max_abs < 0x1p-100f) {
+    max_abs *= 0x1p64f;
+    adj = 64;
+  }
+  const int e = static_cast<int>((__float_as_uint(max_abs) >> 23) & 0xff) - 127 - adj;  // floor(log2)
+  const int s = 14 - e;
+  return s < -100 ? -100 : (s > 100 ? 100 : s);
 }
-// 4 fp32 -> (hi, lo) as two 8-byte groups of 4 bf16
+__device__ __forceinline__ float pow2(int s) { return __uint_as_float(static_cast<uint32_t>(s + 127) << 23); }
+
+__device__ __forceinline__ uint32_t pack2h(__half a, __half b) {
+  return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
+}
+// 4 fp32 (already scaled) -> (hi, lo) as two 8-byte groups of 4 fp16
 __device__ __forceinline__ void split4(float4 v, uint2* hi, uint2* lo) {
-  const __nv_bfloat16 h0 = __float2bfloat16_rn(v.x), h1 = __float2bfloat16_rn(v.y);
-  const __nv_bfloat16 h2 = __float2bfloat16_rn(v.z), h3 = __float2bfloat16_rn(v.w);
-  const __nv_bfloat16 l0 = __float2bfloat16_rn(v.x - __bfloat162float(h0));
-  const __nv_bfloat16 l1 = __float2bfloat16_rn(v.y - __bfloat162float(h1));
-  const __nv_bfloat16 l2 = __float2bfloat16_rn(v.z - __bfloat162float(h2));
-  const __nv_bfloat16 l3 = __float2bfloat16_rn(v.w - __bfloat162float(h3));
-  *hi = make_uint2(pack2(h0, h1), pack2(h2, h3));
-  *lo = make_uint2(pack2(l0, l1), pack2(l2, l3));
+  const __half h0 = __float2half_rn(v.x), h1 = __float2half_rn(v.y);
+  const __half h2 = __float2half_rn(v.z), h3 = __float2half_rn(v.w);
+  const __half l0 = __float2half_rn(v.x - __half2float(h0));
+  const __half l1 = __float2half_rn(v.y - __half2float(h1));
+  const __half l2 = __float2half_rn(v.z - __half2float(h2));
+  const __half l3 = __float2half_rn(v.w - __half2float(h3));
+  *hi = make_uint2(pack2h(h0, h1), pack2h(h2, h3));
+  *lo = make_uint2(pack2h(l0, l1), pack2h(l2, l3));
+}
+__device__ __forceinline__ float4 scale4(float4 v, float f) {
+  return make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
+}
+__device__ __forceinline__ float amax4(float4 v) {
+  return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+// byte offset of float4 f (dims 4f..4f+3) of row r inside a tile image's slab group layout
+__device__ __forceinline__ uint32_t key_off(int r, int f) {
+  const int g = f >> 4, c = (f >> 1) & 7;
+  return static_cast<uint32_t>(g * GROUP + r * 128 + ((c ^ (r & 7)) << 4) + (f & 1) * 8);
 }
 
 // grid (tiles, batch), 128 threads: thread = key row of the tile
@@ -63,24 +100,35 @@ __global__ void __launch_bounds__(BM) key_image_kernel(ApproxArgs P) {
   const int j = t * BM + r;
   const int tiles = key_tiles(P.n_keys);
   uint8_t* img = P.kimg + (static_cast<int64_t>(b) * tiles + t) * TILE_BYTES;
-  const float* kr = P.k + (static_cast<int64_t>(b) * P.k_batch_stride + j) * DI;
-  float ss = 0.f;
+  const float4* kr = reinterpret_cast<const float4*>(P.k + (static_cast<int64_t>(b) * P.k_batch_stride + j) * DI);
+  const bool valid = j < P.n_keys;
+  float ss = 0.f, mx = 0.f;
+  if (valid) {
+#pragma unroll 8
+    for (int f = 0; f < DI / 4; ++f) {
+      const float4 v = __ldg(kr + f);
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+      mx = fmaxf(mx, amax4(v));
+    }
+  }
+  const int sh = row_shift(mx);
+  const float up = pow2(sh);
 #pragma unroll 4
   for (int f = 0; f < DI / 4; ++f) {
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (j < P.n_keys) v = __ldg(reinterpret_cast<const float4*>(kr) + f);
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
-    ss = fmaf(v.z, v.z, ss);
-    ss = fmaf(v.w, v.w, ss);
+    if (valid) v = scale4(__ldg(kr + f), up);
     uint2 hi, lo;
     split4(v, &hi, &lo);
-    const uint32_t off = slab_off(r, f >> 1, SLAB_K) + (f & 1) * 8;
+    const uint32_t off = key_off(r, f);
     *reinterpret_cast<uint2*>(img + off) = hi;
-    *reinterpret_cast<uint2*>(img + HALF + off) = lo;
+    *reinterpret_cast<uint2*>(img + off + SLAB_K) = lo;
   }
+  P.kinv[static_cast<int64_t>(b) * tiles * BM + j] = pow2(-sh);
   // non-negative floats order like their bit patterns
-  if (j < P.n_keys) atomicMax(reinterpret_cast<unsigned int*>(P.kmax + b), __float_as_uint(sqrtf(ss)));
+  if (valid) atomicMax(reinterpret_cast<unsigned int*>(P.kmax + b), __float_as_uint(sqrtf(ss)));
 }
 
 __device__ __forceinline__ int visible(const ApproxArgs& P, int64_t row) {
@@ -94,6 +142,21 @@ __device__ __forceinline__ void set_abort(Smem& sm) {
     *reinterpret_cast<volatile int*>(&sm.abort) = 1;
     raise_device_error(DSV4_ERR_WAIT_TIMEOUT);
   }
+}
+
+// 12 MMAs of slab group g into TMEM column base d; the first of a tile overwrites
+__device__ __forceinline__ void issue_group(uint32_t d, uint32_t kb, uint32_t qh, uint32_t ql, int g, bool first) {
+  constexpr uint32_t id = idesc_f16<128, NQ>(false, false);
+  const uint32_t qhg = qh + g * SLAB_Q, qlg = ql + g * SLAB_Q;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+    mma16(d, sdesc(kb + SLAB_K + kk * 32, 16, 1024), sdesc(qhg + kk * 32, 16, 1024), id, (first && kk == 0) ? 0u : 1u);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+    mma16(d, sdesc(kb + kk * 32, 16, 1024), sdesc(qhg + kk * 32, 16, 1024), id, 1u);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+    mma16(d, sdesc(kb + kk * 32, 16, 1024), sdesc(qlg + kk * 32, 16, 1024), id, 1u);
 }
 
 __global__ void __launch_bounds__(THREADS, 1) approx_score_kernel(ApproxArgs P) {
@@ -112,29 +175,32 @@ __global__ void __launch_bounds__(THREADS, 1) approx_score_kernel(ApproxArgs P) 
   const int T = (nvis + BM - 1) / BM;
   if (T == 0) return;  // block-uniform
 
-  // stage w and the split Q (rows r = q*64 + h)
-  for (int i = tid; i < QG * HI; i += THREADS) {
-    const int q = i / HI;
-    sm.w[q][i % HI] = q < nq ? P.w[(row0 + q) * HI + i % HI] : 0.f;
-  }
-  for (int i = tid; i < NQ * DI / 4; i += THREADS) {
-    const int r = i >> 5, f = i & 31;
+  // stage the scaled, split Q: 160 threads = 5 warps, one (query, head) row of 32 float4 per warp
+  for (int r = warp; r < NQ; r += THREADS / 32) {
+    const int q = r >> 6;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if ((r >> 6) < nq) v = __ldg(reinterpret_cast<const float4*>(P.q + (row0 * HI + r) * DI) + f);
+    if (q < nq) v = __ldg(reinterpret_cast<const float4*>(P.q + (row0 * HI + r) * DI) + lane);
+    float mx = amax4(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int sh = row_shift(mx);
     uint2 hi, lo;
-    split4(v, &hi, &lo);
-    const uint32_t off = slab_off(r, f >> 1, SLAB_Q) + (f & 1) * 8;
+    split4(scale4(v, pow2(sh)), &hi, &lo);
+    const uint32_t off = static_cast<uint32_t>((lane >> 4) * SLAB_Q + r * 128 + ((((lane >> 1) & 7) ^ (r & 7)) << 4) +
+                                               (lane & 1) * 8);
     *reinterpret_cast<uint2*>(sm.qh + off) = hi;
     *reinterpret_cast<uint2*>(sm.ql + off) = lo;
+    if (lane == 0) sm.w[q][r & 63] = q < nq ? P.w[(row0 + q) * HI + (r & 63)] * pow2(-sh) : 0.f;
   }
   if (warp == 0) tmem_alloc<TMEM_COLS>(&sm.tmem_base);
   if (tid == 0) {
-    bar_init(&sm.bar_kh, 1);
-    bar_init(&sm.bar_kl, 1);
-    bar_init(&sm.bar_lo_done, 1);
+    for (int i = 0; i < NSLOT; ++i) {
+      bar_init(&sm.bar_full[i], 1);
+      bar_init(&sm.bar_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      bar_init(&sm.bar_hi_done[i], 1);
-      bar_init(&sm.bar_free[i], 4);
+      bar_init(&sm.bar_done[i], 1);
+      bar_init(&sm.bar_free[i], EPI_WARPS);
     }
     sm.abort = 0;
     bar_init_fence();
@@ -145,105 +211,94 @@ __global__ void __launch_bounds__(THREADS, 1) approx_score_kernel(ApproxArgs P) 
   after_sync();
   const uint32_t tmem = sm.tmem_base;
   const volatile int* abort = &sm.abort;
+  const int tiles = key_tiles(P.n_keys);
 
-  if (warp == 4) {
+  if (warp == EPI_WARPS) {
     if (lane == 0) {
-      const int tiles = key_tiles(P.n_keys);
       const uint8_t* img = P.kimg + static_cast<int64_t>(b) * tiles * TILE_BYTES;
-      constexpr uint32_t id = idesc_bf16<128, NQ>(false, false);
-      const uint32_t qh = smem_u32(sm.qh), ql = smem_u32(sm.ql), kh = smem_u32(sm.kh), kl = smem_u32(sm.kl);
+      const uint32_t qh = smem_u32(sm.qh), ql = smem_u32(sm.ql);
       bool ok = true;
-      bool kl_pending = false, kh_pending = false;  // a bulk copy issued and not yet waited for
-      uint32_t k_par = 0;                           // its phase parity (tile index & 1)
-      uint64_t* last_bar = nullptr;                 // the last commit and its phase parity
-      uint32_t last_par = 0;
-      for (int i = 0; i < T && ok; ++i) {
-        const int buf = i & 1;
-        const uint32_t d = tmem + static_cast<uint32_t>(buf * 256);
-        // the lo half is free once pass A of tile i-1 is done
-        if (i > 0 && !(ok = bar_wait_or_abort(&sm.bar_lo_done, (i - 1) & 1, abort))) break;
-        bar_expect_tx(&sm.bar_kl, HALF);
-        bulk_g2s(sm.kl, img + static_cast<int64_t>(i) * TILE_BYTES + HALF, HALF, &sm.bar_kl);
-        kl_pending = true;
-        k_par = i & 1;
-        // TMEM buffer `buf` is free once the epilogue has read tile i-2
-        if (i >= 2 && !(ok = bar_wait_or_abort(&sm.bar_free[buf], ((i - 2) >> 1) & 1, abort))) break;
-        if (!(ok = bar_wait_or_abort(&sm.bar_kl, i & 1, abort))) break;
-        kl_pending = false;
+      const int ngroups = 2 * T;  // group n = slab group (n & 1) of tile n >> 1
+      int pending[NSLOT];         // group whose copy into slot k is issued and not yet waited for
+      for (int k = 0; k < NSLOT; ++k) pending[k] = -1;
+      int committed = -1;         // the last group whose MMAs were committed
+      auto load = [&](int n) {
+        const int k = n % NSLOT;
+        bar_expect_tx(&sm.bar_full[k], GROUP);
+        bulk_g2s(sm.kbuf[k], img + static_cast<int64_t>(n >> 1) * TILE_BYTES + (n & 1) * GROUP, GROUP,
+                 &sm.bar_full[k]);
+        pending[k] = n;
+      };
+      for (int n = 0; n < NSLOT && n < ngroups; ++n) load(n);
+      for (int n = 0; n < ngroups; ++n) {
+        const int i = n >> 1, g = n & 1, k = n % NSLOT;
+        // the first group of tile i overwrites TMEM buffer i & 1, last read by the epilogue for tile i-2
+        if (g == 0 && i >= 2 && !(ok = bar_wait_or_abort(&sm.bar_free[i & 1], ((i - 2) >> 1) & 1, abort))) break;
+        if (!(ok = bar_wait_or_abort(&sm.bar_full[k], (n / NSLOT) & 1, abort))) break;
+        pending[k] = -1;
         after_sync();
-#pragma unroll
-        for (int k8 = 0; k8 < 8; ++k8)
-          mma_bf16(d, sdesc(kl + (k8 >> 2) * SLAB_K + (k8 & 3) * 32, 16, 1024),
-                   sdesc(qh + (k8 >> 2) * SLAB_Q + (k8 & 3) * 32, 16, 1024), id, k8 > 0 ? 1u : 0u);
-        mma_commit(&sm.bar_lo_done);
-        last_bar = &sm.bar_lo_done;
-        last_par = i & 1;
-        // the hi half is free once passes B, C of tile i-1 are done
-        if (i > 0 && !(ok = bar_wait_or_abort(&sm.bar_hi_done[buf ^ 1], ((i - 1) >> 1) & 1, abort))) break;
-        bar_expect_tx(&sm.bar_kh, HALF);
-        bulk_g2s(sm.kh, img + static_cast<int64_t>(i) * TILE_BYTES, HALF, &sm.bar_kh);
-        kh_pending = true;
-        k_par = i & 1;
-        if (!(ok = bar_wait_or_abort(&sm.bar_kh, i & 1, abort))) break;
-        kh_pending = false;
-        after_sync();
-#pragma unroll
-        for (int k8 = 0; k8 < 8; ++k8)
-          mma_bf16(d, sdesc(kh + (k8 >> 2) * SLAB_K + (k8 & 3) * 32, 16, 1024),
-                   sdesc(qh + (k8 >> 2) * SLAB_Q + (k8 & 3) * 32, 16, 1024), id, 1u);
-#pragma unroll
-        for (int k8 = 0; k8 < 8; ++k8)
-          mma_bf16(d, sdesc(kh + (k8 >> 2) * SLAB_K + (k8 & 3) * 32, 16, 1024),
-                   sdesc(ql + (k8 >> 2) * SLAB_Q + (k8 & 3) * 32, 16, 1024), id, 1u);
-        mma_commit(&sm.bar_hi_done[buf]);
-        last_bar = &sm.bar_hi_done[buf];
-        last_par = (i >> 1) & 1;
+        issue_group(tmem + (i & 1) * 256, smem_u32(sm.kbuf[k]), qh, ql, g, g == 0);
+        mma_commit(&sm.bar_empty[k]);
+        if (g == 1) mma_commit(&sm.bar_done[i & 1]);
+        committed = n;
+        // refill the slot of group n-1 (done before group n runs) with group n-1+NSLOT
+        const int m = n - 1 + NSLOT;
+        if (n >= 1 && m < ngroups) {
+          if (!(ok = bar_wait_or_abort(&sm.bar_empty[(n - 1) % NSLOT], ((n - 1) / NSLOT) & 1, abort))) break;
+          load(m);
+        }
       }
       if (!ok) {
         set_abort(sm);
-        // let what was issued land before the CTA's shared and tensor memory go away
-        if (kl_pending) bar_wait(&sm.bar_kl, k_par);
-        if (kh_pending) bar_wait(&sm.bar_kh, k_par);
-        if (last_bar) bar_wait(last_bar, last_par);
+        // let what was issued finish before the CTA's shared and tensor memory go away
+        for (int k = 0; k < NSLOT; ++k)
+          if (pending[k] >= 0) bar_wait(&sm.bar_full[k], (pending[k] / NSLOT) & 1);
+        if (committed >= 0) bar_wait(&sm.bar_empty[committed % NSLOT], (committed / NSLOT) & 1);
       }
     }
     __syncwarp();
   } else {
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int qb = (warp >> 2) * 2;  // this warp's two queries
+    const float* kinv = P.kinv + static_cast<int64_t>(b) * tiles * BM;
     for (int i = 0; i < T; ++i) {
       const int buf = i & 1;
-      const bool ok = bar_wait_or_abort(&sm.bar_hi_done[buf], (i >> 1) & 1, abort);
+      const bool ok = bar_wait_or_abort(&sm.bar_done[buf], (i >> 1) & 1, abort);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) set_abort(sm);
         break;
       }
       after_sync();
-      float acc[QG];
+      float v[2][HI];
 #pragma unroll
-      for (int q = 0; q < QG; ++q) {
-        float v[HI];
+      for (int u = 0; u < 2; ++u)
 #pragma unroll
-        for (int c = 0; c < HI; c += 16) tmem_ld16(tmem + lane_base + buf * 256 + q * HI + c, v + c);
-        tmem_wait_ld();
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-        for (int h = 0; h < HI; h += 4) {
-          const float4 wv = *reinterpret_cast<const float4*>(&sm.w[q][h]);
-          a0 = fmaf(wv.x, fmaxf(v[h], 0.f), a0);
-          a1 = fmaf(wv.y, fmaxf(v[h + 1], 0.f), a1);
-          a2 = fmaf(wv.z, fmaxf(v[h + 2], 0.f), a2);
-          a3 = fmaf(wv.w, fmaxf(v[h + 3], 0.f), a3);
-        }
-        acc[q] = (a0 + a1) + (a2 + a3);
-      }
+        for (int c = 0; c < HI; c += 16) tmem_ld16(tmem + lane_base + buf * 256 + (qb + u) * HI + c, v[u] + c);
+      tmem_wait_ld();
       before_sync();
       __syncwarp();
       if (lane == 0) bar_arrive(&sm.bar_free[buf]);
-      const int key = i * BM + warp * 32 + lane;
-      if (key < P.n_keys)
+      float acc[2];
 #pragma unroll
-        for (int q = 0; q < QG; ++q)
-          if (q < nq) P.scores[(row0 + q) * P.n_pad + key] = acc[q];
+      for (int u = 0; u < 2; ++u) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int h = 0; h < HI; h += 4) {
+          const float4 wv = *reinterpret_cast<const float4*>(&sm.w[qb + u][h]);
+          a0 = fmaf(wv.x, fmaxf(v[u][h], 0.f), a0);
+          a1 = fmaf(wv.y, fmaxf(v[u][h + 1], 0.f), a1);
+          a2 = fmaf(wv.z, fmaxf(v[u][h + 2], 0.f), a2);
+          a3 = fmaf(wv.w, fmaxf(v[u][h + 3], 0.f), a3);
+        }
+        acc[u] = (a0 + a1) + (a2 + a3);
+      }
+      const int key = i * BM + (warp & 3) * 32 + lane;
+      if (key < P.n_keys) {
+        const float ks = kinv[key];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          if (qb + u < nq) P.scores[(row0 + qb + u) * P.n_pad + key] = acc[u] * ks;
+      }
     }
   }
   before_sync();

@@ -2,10 +2,11 @@
 // indexer_tc.cu).
 //
 // approx score A[i, j] = sum_h w[i,h] * relu(q[i,h,:] . k[j,:]) with every dot product taken on
-// tcgen05 from a two-term bf16 split of both operands (q = qh + ql, k = kh + kl; qh.kh + qh.kl +
-// ql.kh, fp32 accumulate). The select kernel then bounds |A - E| (E: the canonical fp32 score) by
-// eps_i = C * sum_h |w[i,h]| * ||q[i,h,:]|| * max_j ||k[j,:]||, keeps the keys that are certainly in
-// the top-k, drops those certainly out, and rescores only the keys in between in the canonical order.
+// tcgen05 from a two-term fp16 split of both operands after an exact power-of-two scaling of each row
+// (q = qh + ql, k = kh + kl; qh.kh + qh.kl + ql.kh, fp32 accumulate). The select kernel then bounds
+// |A - E| (E: the canonical fp32 score) by eps_i = C * sum_h |w[i,h]| * ||q[i,h,:]|| * max_j ||k[j,:]||,
+// keeps the keys that are certainly in the top-k, drops those certainly out, and rescores only the
+// keys in between in the canonical order.
 #pragma once
 #include <cstddef>
 #include <cstdint>
@@ -28,12 +29,16 @@ struct ApproxArgs {
   const int32_t* positions;
   int32_t ratio;
   uint8_t* kimg;        // workspace: [batch][tiles][TILE_BYTES]
+  float* kinv;          // workspace: [batch][tiles * BM] inverse power-of-two scale of each key row
   float* kmax;          // workspace: [batch] max key norm (zeroed by the launcher)
 };
 
 __host__ __device__ inline int key_tiles(int n_keys) { return (n_keys + BM - 1) / BM; }
 inline size_t kimg_bytes(int batch, int n_keys) {
   return static_cast<size_t>(batch) * key_tiles(n_keys) * TILE_BYTES;
+}
+inline size_t kinv_bytes(int batch, int n_keys) {
+  return static_cast<size_t>(batch) * key_tiles(n_keys) * BM * sizeof(float);
 }
 
 // key image + norms, then the approximate scores (two launches on `stream`)

@@ -32,7 +32,17 @@ constexpr uint32_t idesc_bf16(bool a_mn_major, bool b_mn_major) {
          ((static_cast<uint32_t>(N) >> 3) << 17) | ((static_cast<uint32_t>(M) >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+// instruction descriptor, kind::f16: fp32 accumulate, fp16 A and B, shape M x N
+template <int M, int N>
+constexpr uint32_t idesc_f16(bool a_mn_major, bool b_mn_major) {
+  static_assert(M == 64 || M == 128, "M");
+  static_assert(N % 16 == 0 && N >= 16 && N <= 256, "N");
+  return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((static_cast<uint32_t>(N) >> 3) << 17) | ((static_cast<uint32_t>(M) >> 4) << 24);
+}
+
+// D (fp32, tensor memory) (+)= A . B^T for 16-bit A, B of the kind given by the descriptor
+__device__ __forceinline__ void mma16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
   asm volatile(
       "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),

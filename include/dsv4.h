@@ -203,11 +203,13 @@ typedef struct {
   int32_t window_linear;
   /* scoring method (the selected sets are the same, bit for bit):
    * 1 = every score in the fixed fp32 order above on the FMA pipe;
-   * 2 = tensor-core filter: approximate scores A from a two-term bf16 split of q and k on tcgen05
-   *     (fp32 accumulate), a proven bound |A - score| <= eps = 2^-12 * sum_h |w[h]| * ||q[h,:]|| *
-   *     max_j ||k[j,:]||, and exact fp32 rescoring (the order above) of the keys whose A lies within
-   *     2 eps of the k-th largest A; keys above that band are in the top_k, keys below it are not.
-   *     n_keys <= 16384. With scores_out, the approximate scores are written there.
+   * 2 = tensor-core filter: approximate scores A from a two-term fp16 split of q and k (each row
+   *     scaled by a power of two) on tcgen05 with fp32 accumulation, the bound
+   *     |A - score| <= eps = 2^-14 * sum_h |w[h]| * ||q[h,:]|| * max_j ||k[j,:]|| (the rounding
+   *     analysis gives about 2^-15.7 for finite inputs whose nonzero rows peak within 2^+-86), and
+   *     exact fp32 rescoring (the order above) of the keys whose A lies within 2 eps of the k-th
+   *     largest A; keys above that band are in the top_k, keys below it are not. n_keys <= 16384.
+   *     With scores_out, the approximate scores are written there.
    * 0 = automatic: 2 for prefill-shaped calls (batch * s >= 256, n_keys > top_k, n_keys <= 16384),
    *     else 1. The allocation-free entry point below always uses 1. */
   int32_t mode;

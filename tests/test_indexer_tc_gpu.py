@@ -8,7 +8,7 @@ from oracle import indexer_ref as I
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-EPS_C = 2.0 ** -12
+EPS_C = 2.0 ** -14
 
 
 def _inputs(b, s, n, seed, spread=False):
@@ -94,3 +94,17 @@ def test_mode2_into_window_and_offset(dsv4):
                               window_linear=True, mode=mode)
         outs.append(out.cpu().numpy())
     np.testing.assert_array_equal(outs[1], outs[0])
+
+
+def test_mode2_row_scales_bit_exact(dsv4):
+    """Rows of very different magnitude (2^-40 .. 2^40 per query head and per key): the per-row
+    power-of-two scaling keeps the fp16 split exact up to its rounding; the sets match mode 1."""
+    q, w, keys = _inputs(1, 256, 2000, 55)
+    g = torch.Generator().manual_seed(56)
+    q = q * torch.exp2(torch.randint(-40, 41, (1, 256, 64, 1), generator=g).float())
+    keys = keys * torch.exp2(torch.randint(-40, 41, (1, 2000, 1), generator=g).float())
+    args = (q.to(DEV), w.to(DEV), keys.to(DEV), 200)
+    got = dsv4.indexer_topk(*args, mode=2).cpu().numpy()
+    np.testing.assert_array_equal(got, dsv4.indexer_topk(*args, mode=1).cpu().numpy())
+    ref = I.indexer_topk(q[:, :6].numpy(), w[:, :6].numpy(), keys.numpy(), 200)
+    np.testing.assert_array_equal(got[:, :6], ref)
