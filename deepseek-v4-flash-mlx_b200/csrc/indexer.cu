@@ -606,7 +606,7 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams P) {
 // whose boundary bin is taken whole ends the search early; otherwise after all 32 bits the keys equal
 // to the threshold are taken lowest index first. The taken keys are written in ascending order.
 struct SelRegShared {
-  uint32_t hist[SEL_BINS];
+  alignas(16) uint32_t hist[SEL_BINS];
   uint32_t warp_sum[SEL_THREADS / 32];
   uint32_t total, bin, need;
   int32_t tau_last;
@@ -667,11 +667,16 @@ __device__ __forceinline__ void radix_levels(const uint32_t (&key)[PER], int nv,
   whole = false;
   {
     constexpr int PB = SEL_BINS / SEL_THREADS;
+    static_assert(PB == 8, "two 16-byte reads per thread");
     uint32_t c[PB], tot = 0;
+    {
+      // this thread's 8 bins, highest first, read as two 16-byte vectors
+      const uint4* h4 = reinterpret_cast<const uint4*>(sh.hist + SEL_BINS - PB * (tid + 1));
+      const uint4 lo4 = h4[0], hi4 = h4[1];
+      c[0] = hi4.w; c[1] = hi4.z; c[2] = hi4.y; c[3] = hi4.x;
+      c[4] = lo4.w; c[5] = lo4.z; c[6] = lo4.y; c[7] = lo4.x;
 #pragma unroll
-    for (int e = 0; e < PB; ++e) {
-      c[e] = sh.hist[SEL_BINS - 1 - (tid * PB + e)];
-      tot += c[e];
+      for (int e = 0; e < PB; ++e) tot += c[e];
     }
     const uint32_t before = block_scan_reg(tot, sh);
     if (before < k && k <= before + tot) {
@@ -747,15 +752,19 @@ __device__ __forceinline__ void radix_levels(const uint32_t (&key)[PER], int nv,
 
 
 constexpr int BAND_CAP = 512;  // band keys rescored per round
+constexpr int STAGE_ROWS = 64;  // band key rows staged in shared memory at a time
+constexpr int OUT_STAGE = 2048;  // selections up to this size leave through shared memory
 constexpr float EPS_C = 0x1p-14f;
 
 struct RefineSmem {
   float4 q[HI * DI / 4];   // the query's 64 x 128 indexer q; chunk c of head h at c ^ ((h / 4) % 8)
   float w[HI];
   float wq[HI];
+  float4 krow[STAGE_ROWS][DI / 4];  // band key rows staged for the exact rescoring
   int32_t band_idx[BAND_CAP];
   float band_e[BAND_CAP];
   uint8_t band_take[BAND_CAP];
+  int32_t out_stage[OUT_STAGE];
   float eps;
 };
 
@@ -776,22 +785,98 @@ __device__ __forceinline__ float from_ordered(uint32_t u) {
 // largest / smallest ordered key and the band keys holding their exact scores, for the ordinary
 // selection that follows (returns false). Valid for finite inputs (see the error analysis of the
 // approximate scores).
+// Exact scores of band entries rs.band_idx[0, cnt) into rs.band_e (the canonical fp32 order),
+// STAGE_ROWS key rows at a time staged in shared memory: task = (4 band entries, head quad); the
+// 16 lanes of a quad set form the partial tree. Each thread keeps 4 heads x 4 keys of fmaf chains,
+// so a q chunk serves 4 keys and a key chunk 4 heads. Ends with the block synchronised.
+__device__ __forceinline__ void rescore_band(const float* kb, int cnt, RefineSmem& rs) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int s0 = 0; s0 < cnt; s0 += STAGE_ROWS) {
+    const int rows = min(STAGE_ROWS, cnt - s0);
+    {
+      const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(&rs.krow[0][0]));
+      for (int i = tid; i < rows * (DI / 4); i += SEL_THREADS) {
+        const int r = i >> 5, c = i & 31;
+        cp_async16(dst + static_cast<uint32_t>(i) * 16,
+                   kb + static_cast<int64_t>(rs.band_idx[s0 + r]) * DI + c * 4, true);
+      }
+      asm volatile("cp.async.commit_group;\n" ::);
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    }
+    __syncthreads();
+    const int n_groups = (rows + 3) >> 2;
+    for (int base = warp * 32; base < n_groups * 16; base += SEL_THREADS) {
+      const int task = base + lane;
+      const int grp = task >> 4, quad = task & 15;
+      const bool valid = grp < n_groups;
+      const int m0 = grp * 4;  // within the stage
+      int rr[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) rr[e] = (valid && m0 + e < rows) ? m0 + e : 0;
+      const int h0 = quad * 4, sw = quad & 7;
+      float d[4][4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) d[a][e] = 0.f;
+      if (valid) {
+#pragma unroll 4
+        for (int c = 0; c < DI / 4; ++c) {
+          float4 kv[4], qv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) kv[e] = rs.krow[rr[e]][c];
+#pragma unroll
+          for (int a = 0; a < 4; ++a) qv[a] = rs.q[(h0 + a) * 32 + (c ^ sw)];
+#pragma unroll
+          for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              d[a][e] = __fmaf_rn(qv[a].x, kv[e].x, d[a][e]);
+              d[a][e] = __fmaf_rn(qv[a].y, kv[e].y, d[a][e]);
+              d[a][e] = __fmaf_rn(qv[a].z, kv[e].z, d[a][e]);
+              d[a][e] = __fmaf_rn(qv[a].w, kv[e].w, d[a][e]);
+            }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float part = 0.f;
+#pragma unroll
+        for (int a = 0; a < 4; ++a) part = __fmaf_rn(rs.w[h0 + a], d[a][e] > 0.f ? d[a][e] : 0.f, part);
+        // balanced tree over the 16 partials: pairs (2t, 2t+1) at every level
+        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 1));
+        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 2));
+        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 4));
+        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 8));
+        if (valid && quad == 0 && m0 + e < rows) rs.band_e[s0 + m0 + e] = part;
+      }
+    }
+    __syncthreads();  // krow reuse
+  }
+  __syncthreads();
+}
+
 template <int PER>
 __device__ __forceinline__ bool refine_band(const SelectParams& P, int64_t qrow, int b, int k, uint32_t (&key)[PER],
                                             int nv, int j0, SelRegShared& sh, RefineSmem& rs, int32_t* out) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // the query's q (64 x 128) streams into shared memory while the radix runs
+  {
+    const float* qg = P.q + qrow * (HI * DI);
+    const uint32_t qs = static_cast<uint32_t>(__cvta_generic_to_shared(rs.q));
+    for (int i = tid; i < HI * DI / 4; i += SEL_THREADS) {
+      const int h = i >> 5, c = i & 31;
+      cp_async16(qs + static_cast<uint32_t>(h * 32 + (c ^ ((h >> 2) & 7))) * 16, qg + i * 4, true);
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+  }
+  if (tid < HI) rs.w[tid] = P.w[qrow * HI + tid];
   // bracket [lo, hi] of the k-th largest approximate score: the first two radix levels (20 bits)
   uint32_t pfx, shift, kleft;
   bool whole;
   radix_levels<PER>(key, nv, static_cast<uint32_t>(k), false, sh, pfx, shift, kleft, whole, 2);
   const float lo = from_ordered(pfx), hi = from_ordered(pfx | ((1u << shift) - 1u));
-
-  const float4* qg = reinterpret_cast<const float4*>(P.q + qrow * (HI * DI));
-  for (int i = tid; i < HI * DI / 4; i += SEL_THREADS) {
-    const int h = i >> 5, c = i & 31;
-    rs.q[h * 32 + (c ^ ((h >> 2) & 7))] = __ldg(qg + i);
-  }
-  if (tid < HI) rs.w[tid] = P.w[qrow * HI + tid];
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   __syncthreads();
   {  // |w_h| * ||q_h||: 8 threads per head
     const int h = tid >> 3, part = tid & 7;
@@ -820,13 +905,14 @@ __device__ __forceinline__ bool refine_band(const SelectParams& P, int64_t qrow,
   __syncthreads();
   const float e2 = 2.f * rs.eps;
   const float upper = __fadd_ru(hi, e2), lower = __fsub_rd(lo, e2);
-  uint32_t band = 0, nb = 0, nin = 0;
+  uint32_t band = 0, inm = 0, nb = 0, nin = 0;
 #pragma unroll
   for (int e = 0; e < PER; ++e) {
     if (e < nv) {
       const float a = from_ordered(key[e]);
       if (a > upper) {
         key[e] = 0xffffffffu;
+        inm |= 1u << e;
         ++nin;
       } else if (a < lower) {
         key[e] = 0u;
@@ -836,11 +922,67 @@ __device__ __forceinline__ bool refine_band(const SelectParams& P, int64_t qrow,
       }
     }
   }
-  const uint32_t pos0 = block_scan_reg(nb, sh);
-  const uint32_t n_band = sh.total;
-  const uint32_t in_before = block_scan_reg(nin, sh);
-  const uint32_t n_in = sh.total;
+  // one scan of both counts (band in the low 16 bits, certain in the high 16; each <= 16384)
+  const uint32_t both = block_scan_reg(nb | (nin << 16), sh);
+  const uint32_t pos0 = both & 0xffffu;
+  const uint32_t n_band = sh.total & 0xffffu;
+  const uint32_t n_in = sh.total >> 16;
   const float* kb = P.k + static_cast<int64_t>(b) * P.k_batch_stride * DI;
+  if (n_band <= static_cast<uint32_t>(BAND_CAP)) {
+    // one round; from here on the per-key state is the two bit masks
+    {
+      uint32_t pos = pos0;
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if ((band >> e) & 1u) rs.band_idx[pos++] = j0 + e;
+    }
+    __syncthreads();
+    rescore_band(kb, static_cast<int>(n_band), rs);
+    // take the (k - n_in) best band entries by (score desc, index asc); entries are in ascending key
+    // order, so the index order is the entry order. Warp w ranks entries w, w + 16, ...; its lanes
+    // split the comparisons.
+    const uint32_t need = static_cast<uint32_t>(k) - n_in;
+    for (int m = warp; m < static_cast<int>(n_band); m += SEL_THREADS / 32) {
+      const uint32_t km = ordered_bits(rs.band_e[m]);
+      uint32_t rank = 0;
+      for (int m2 = lane; m2 < static_cast<int>(n_band); m2 += 32) {
+        const uint32_t k2 = ordered_bits(rs.band_e[m2]);
+        rank += (k2 > km) || (k2 == km && m2 < m);
+      }
+      rank = __reduce_add_sync(0xffffffffu, rank);
+      if (lane == 0) rs.band_take[m] = rank < need ? 1 : 0;
+    }
+    __syncthreads();
+    // the taken keys in ascending order (certain ones and the chosen band entries), staged in shared
+    // memory so that the list leaves in coalesced stores
+    uint32_t take = inm;
+    {
+      uint32_t pos = pos0;
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if ((band >> e) & 1u) {
+          if (rs.band_take[pos]) take |= 1u << e;
+          ++pos;
+        }
+    }
+    uint32_t o = block_scan_reg(static_cast<uint32_t>(__popc(take)), sh);
+    const bool staged = k <= OUT_STAGE;
+#pragma unroll
+    for (int e = 0; e < PER; ++e)
+      if ((take >> e) & 1u) {
+        const int32_t v = map_key(P, b, j0 + e);
+        if (staged) rs.out_stage[o] = v;
+        else out[o] = v;
+        ++o;
+      }
+    if (staged) {
+      __syncthreads();
+      for (int r = tid; r < k; r += SEL_THREADS) out[r] = rs.out_stage[r];
+    }
+    return true;
+  }
+  // a wide band (many equal or near-equal scores): rounds of BAND_CAP, the band keys taking their
+  // exact scores, for the ordinary selection that follows over the pinned keys
   for (uint32_t r0 = 0; r0 < n_band; r0 += BAND_CAP) {
     const uint32_t cnt = min(static_cast<uint32_t>(BAND_CAP), n_band - r0);
     {
@@ -853,98 +995,7 @@ __device__ __forceinline__ bool refine_band(const SelectParams& P, int64_t qrow,
         }
     }
     __syncthreads();
-    // exact scores: task = (4 band entries, head quad); the 16 lanes of a quad set form the partial
-    // tree. Each thread keeps 4 heads x 4 keys of fmaf chains, so a q chunk read from shared memory
-    // serves 4 keys and a key chunk 4 heads.
-    const int n_groups = (static_cast<int>(cnt) + 3) >> 2;
-    for (int base = warp * 32; base < n_groups * 16; base += SEL_THREADS) {
-      const int task = base + lane;
-      const int grp = task >> 4, quad = task & 15;
-      const bool valid = grp < n_groups;
-      const int m0 = grp * 4;
-      const float4* kr[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int m = (valid && m0 + e < static_cast<int>(cnt)) ? m0 + e : 0;
-        kr[e] = reinterpret_cast<const float4*>(kb + static_cast<int64_t>(rs.band_idx[m]) * DI);
-      }
-      const int h0 = quad * 4, sw = quad & 7;
-      float d[4][4];
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) d[a][e] = 0.f;
-      if (valid) {
-#pragma unroll 2
-        for (int c = 0; c < DI / 4; ++c) {
-          float4 kv[4], qv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) kv[e] = __ldg(kr[e] + c);
-#pragma unroll
-          for (int a = 0; a < 4; ++a) qv[a] = rs.q[(h0 + a) * 32 + (c ^ sw)];
-#pragma unroll
-          for (int a = 0; a < 4; ++a)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              d[a][e] = __fmaf_rn(qv[a].x, kv[e].x, d[a][e]);
-              d[a][e] = __fmaf_rn(qv[a].y, kv[e].y, d[a][e]);
-              d[a][e] = __fmaf_rn(qv[a].z, kv[e].z, d[a][e]);
-              d[a][e] = __fmaf_rn(qv[a].w, kv[e].w, d[a][e]);
-            }
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float part = 0.f;
-#pragma unroll
-        for (int a = 0; a < 4; ++a) part = __fmaf_rn(rs.w[h0 + a], d[a][e] > 0.f ? d[a][e] : 0.f, part);
-        // balanced tree over the 16 partials: pairs (2t, 2t+1) at every level
-        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 1));
-        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 2));
-        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 4));
-        part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 8));
-        if (valid && quad == 0 && m0 + e < static_cast<int>(cnt)) rs.band_e[m0 + e] = part;
-      }
-    }
-    __syncthreads();
-    if (n_band <= static_cast<uint32_t>(BAND_CAP)) {
-      // one round: take the (k - n_in) best band entries by (score desc, index asc); the entries are
-      // in ascending key order, so the index order is the entry order
-      const uint32_t need = static_cast<uint32_t>(k) - n_in;
-      for (int m = tid; m < static_cast<int>(n_band); m += SEL_THREADS) {
-        const uint32_t km = ordered_bits(rs.band_e[m]);
-        uint32_t rank = 0;
-        for (int m2 = 0; m2 < static_cast<int>(n_band); ++m2) {
-          const uint32_t k2 = ordered_bits(rs.band_e[m2]);
-          rank += (k2 > km) || (k2 == km && m2 < m);
-        }
-        rs.band_take[m] = rank < need ? 1 : 0;
-      }
-      __syncthreads();
-      // write the taken keys in ascending order: certain ones and the chosen band entries
-      uint32_t cnt_t = 0;
-      {
-        uint32_t pos = pos0;
-#pragma unroll
-        for (int e = 0; e < PER; ++e) {
-          const bool bnd = (band >> e) & 1u;
-          cnt_t += (e < nv && key[e] == 0xffffffffu && !bnd) || (bnd && rs.band_take[pos]);
-          pos += bnd;
-        }
-      }
-      uint32_t o = block_scan_reg(cnt_t, sh);
-      {
-        uint32_t pos = pos0;
-#pragma unroll
-        for (int e = 0; e < PER; ++e) {
-          const bool bnd = (band >> e) & 1u;
-          if ((e < nv && key[e] == 0xffffffffu && !bnd) || (bnd && rs.band_take[pos])) out[o++] = map_key(P, b, j0 + e);
-          pos += bnd;
-        }
-      }
-      (void)in_before;
-      return true;
-    }
+    rescore_band(kb, static_cast<int>(cnt), rs);
     {
       uint32_t pos = pos0;
 #pragma unroll
@@ -956,7 +1007,6 @@ __device__ __forceinline__ bool refine_band(const SelectParams& P, int64_t qrow,
     }
     __syncthreads();
   }
-  // a wide band (many equal or near-equal scores): the ordinary selection over the pinned keys
   return false;
 }
 

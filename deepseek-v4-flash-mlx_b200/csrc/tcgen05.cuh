@@ -25,7 +25,7 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t 
 
 // instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, shape M x N
 template <int M, int N>
-constexpr uint32_t idesc_bf16(bool a_mn_major, bool b_mn_major) {
+__host__ __device__ constexpr uint32_t idesc_bf16(bool a_mn_major, bool b_mn_major) {
   static_assert(M == 64 || M == 128, "M");
   static_assert(N % 16 == 0 && N >= 16 && N <= 256, "N");
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
@@ -34,7 +34,7 @@ constexpr uint32_t idesc_bf16(bool a_mn_major, bool b_mn_major) {
 
 // instruction descriptor, kind::f16: fp32 accumulate, fp16 A and B, shape M x N
 template <int M, int N>
-constexpr uint32_t idesc_f16(bool a_mn_major, bool b_mn_major) {
+__host__ __device__ constexpr uint32_t idesc_f16(bool a_mn_major, bool b_mn_major) {
   static_assert(M == 64 || M == 128, "M");
   static_assert(N % 16 == 0 && N >= 16 && N <= 256, "N");
   return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
