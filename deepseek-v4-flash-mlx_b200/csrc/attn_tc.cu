@@ -115,6 +115,12 @@ __device__ __forceinline__ void mma16_ta(uint32_t d_tmem, uint32_t a_tmem, uint6
       "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
 }
 
+// 2^x on the SFU (ex2.approx.ftz: relative error ~2^-22, 2^-inf = +0), for the bf16 probabilities
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void sm_bar() { asm volatile("bar.sync 1, %0;\n" ::"n"(SM_THREADS) : "memory"); }
 __device__ __forceinline__ bool sm_bar_or(bool v) {
   uint32_t r;
@@ -317,23 +323,29 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
 
       // ---------------------------------------------------------- softmax of tile i (warps 4-11)
       if (ok) ok = __all_sync(0xffffffffu, bar_wait_or_abort(&sm.bar_s, i & 1, abort));
-      if (sm_bar_or(!ok)) {
-        ok = false;
-        if (lane == 0) set_abort(sm);
-        break;
-      }
-      after_sync();
       float x[32];
-      tmem_ld16(tmem + lq + COL_S + half * 32, x);
-      tmem_ld16(tmem + lq + COL_S + half * 32 + 16, x + 16);
-      tmem_wait_ld();
       bool grow = false;
+      if (ok) {
+        after_sync();
+        tmem_ld16(tmem + lq + COL_S + half * 32, x);
+        tmem_ld16(tmem + lq + COL_S + half * 32 + 16, x + 16);
+        tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        x[c] = valid ? x[c] * P.scale_log2 : -INFINITY;
-        grow |= x[c] > m[c] + RESCALE_THRESHOLD;
+        for (int c = 0; c < 32; ++c) {
+          x[c] = valid ? x[c] * P.scale_log2 : -INFINITY;
+          grow |= x[c] > m[c] + RESCALE_THRESHOLD;
+        }
       }
-      if (sm_bar_or(grow)) {
+      // one block reduction in the common case; a second only when something is off
+      if (sm_bar_or(grow || !ok)) {
+        if (sm_bar_or(!ok)) {
+          ok = false;
+          if (lane == 0) set_abort(sm);
+          break;
+        }
+        grow = true;
+      }
+      if (grow) {
         // exact tile maximum per head, then m = max(m, tile max); O^T and L rescaled by 2^(m_old - m)
         sm.red[qd][half * 32 + lane] = warp_col_max32(x);
         sm_bar();
@@ -382,7 +394,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int c = c4 * 8 + e;
-            pv[e] = (m[c] == -INFINITY) ? 0.f : exp2f(x[c] - m[c]);
+            pv[e] = (m[c] == -INFINITY) ? 0.f : ex2_approx(x[c] - m[c]);
           }
           const uint4 u = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
                                      pack_bf16x2(pv[6], pv[7]));
