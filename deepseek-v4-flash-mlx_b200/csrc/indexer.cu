@@ -1174,7 +1174,10 @@ int resolve_mode(const dsv4_indexer_params* p) {
   const bool tc_ok = p->heads == idx::HI && p->n_keys <= idx::SEL_THREADS * 32;
   if (p->mode == 2) return tc_ok ? 2 : -1;
   if (p->mode != 0) return -1;
-  return (tc_ok && static_cast<int64_t>(p->batch) * p->s >= 256 && p->n_keys > p->top_k) ? 2 : 1;
+  // prefill-shaped calls, and decode batches large enough that the exact selection's latency per
+  // query is hidden behind the others
+  const bool many = itc::row_kernel(p->s) ? p->batch >= 16 : static_cast<int64_t>(p->batch) * p->s >= 256;
+  return (tc_ok && many && p->n_keys > p->top_k) ? 2 : 1;
 }
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // workspace: [scores rows x n_pad fp32] then, for mode 2, [key tile images] [key scales]
@@ -1184,7 +1187,8 @@ size_t workspace_layout(const dsv4_indexer_params* p, int mode, size_t* off_kimg
   const size_t sc = static_cast<size_t>(static_cast<int64_t>(p->batch) * p->s * n_pad * sizeof(float));
   if (mode != 2) return sc;
   *off_kimg = round_up(sc, 1024);
-  *off_kmax = *off_kimg + itc::kimg_bytes(p->batch, p->n_keys) + itc::kinv_bytes(p->batch, p->n_keys);
+  *off_kmax = *off_kimg;
+  if (!itc::row_kernel(p->s)) *off_kmax += itc::kimg_bytes(p->batch, p->n_keys) + itc::kinv_bytes(p->batch, p->n_keys);
   return *off_kmax + round_up(sizeof(float) * p->batch, 256);
 }
 }  // namespace
@@ -1241,8 +1245,10 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
     A.k_batch_stride = p->k_batch_stride;
     A.positions = p->positions;
     A.ratio = p->ratio;
-    A.kimg = static_cast<uint8_t*>(p->workspace) + off_kimg;
-    A.kinv = reinterpret_cast<float*>(A.kimg + itc::kimg_bytes(p->batch, p->n_keys));
+    if (!itc::row_kernel(p->s)) {
+      A.kimg = static_cast<uint8_t*>(p->workspace) + off_kimg;
+      A.kinv = reinterpret_cast<float*>(A.kimg + itc::kimg_bytes(p->batch, p->n_keys));
+    }
     A.kmax = kmax = reinterpret_cast<float*>(static_cast<uint8_t*>(p->workspace) + off_kmax);
     DSV4_CUDA_CHECK(itc::launch_approx_scores(A, as_stream(stream)));
   }

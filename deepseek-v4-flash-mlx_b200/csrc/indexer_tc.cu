@@ -94,6 +94,22 @@ __device__ __forceinline__ uint32_t key_off(int r, int f) {
   return static_cast<uint32_t>(g * GROUP + r * 128 + ((c ^ (r & 7)) << 4) + (f & 1) * 8);
 }
 
+// max over the CTA's threads (all of them call it), one atomicMax per CTA into *dst (the values
+// are non-negative floats, which order like their bit patterns)
+__device__ __forceinline__ void cta_atomic_max(float v, float* dst) {
+  __shared__ float wmax[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) wmax[warp] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) m = fmaxf(m, wmax[i]);
+    atomicMax(reinterpret_cast<unsigned int*>(dst), __float_as_uint(m));
+  }
+}
+
 // grid (tiles, batch), 128 threads: thread = key row of the tile
 __global__ void __launch_bounds__(BM) key_image_kernel(ApproxArgs P) {
   const int t = blockIdx.x, b = blockIdx.y, r = threadIdx.x;
@@ -127,8 +143,7 @@ __global__ void __launch_bounds__(BM) key_image_kernel(ApproxArgs P) {
     *reinterpret_cast<uint2*>(img + off + SLAB_K) = lo;
   }
   P.kinv[static_cast<int64_t>(b) * tiles * BM + j] = pow2(-sh);
-  // non-negative floats order like their bit patterns
-  if (valid) atomicMax(reinterpret_cast<unsigned int*>(P.kmax + b), __float_as_uint(sqrtf(ss)));
+  cta_atomic_max(valid ? sqrtf(ss) : 0.f, P.kmax + b);
 }
 
 __device__ __forceinline__ int visible(const ApproxArgs& P, int64_t row) {
@@ -175,11 +190,24 @@ __global__ void __launch_bounds__(THREADS, 1) approx_score_kernel(ApproxArgs P) 
   const int T = (nvis + BM - 1) / BM;
   if (T == 0) return;  // block-uniform
 
-  // stage the scaled, split Q: 160 threads = 5 warps, one (query, head) row of 32 float4 per warp
-  for (int r = warp; r < NQ; r += THREADS / 32) {
+  // stage the scaled, split Q: each warp takes (query, head) rows warp, warp + 9, ..; lane = float4
+  // of the row; loads are issued 8 rows ahead of their use
+  constexpr int NW = THREADS / 32;
+  constexpr int QB = 8;
+  for (int r0 = warp; r0 < NQ; r0 += NW * QB) {
+    float4 qv[QB];
+#pragma unroll
+    for (int k = 0; k < QB; ++k) {
+      const int r = r0 + k * NW;
+      qv[k] = (r < NQ && (r >> 6) < nq) ? __ldg(reinterpret_cast<const float4*>(P.q + (row0 * HI + r) * DI) + lane)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < QB; ++k) {
+    const int r = r0 + k * NW;
+    if (r >= NQ) break;
     const int q = r >> 6;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (q < nq) v = __ldg(reinterpret_cast<const float4*>(P.q + (row0 * HI + r) * DI) + lane);
+    const float4 v = qv[k];
     float mx = amax4(v);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -191,6 +219,7 @@ __global__ void __launch_bounds__(THREADS, 1) approx_score_kernel(ApproxArgs P) 
     *reinterpret_cast<uint2*>(sm.qh + off) = hi;
     *reinterpret_cast<uint2*>(sm.ql + off) = lo;
     if (lane == 0) sm.w[q][r & 63] = q < nq ? P.w[(row0 + q) * HI + (r & 63)] * pow2(-sh) : 0.f;
+    }
   }
   if (warp == 0) tmem_alloc<TMEM_COLS>(&sm.tmem_base);
   if (tid == 0) {
@@ -307,11 +336,164 @@ __global__ void __launch_bounds__(THREADS, 1) approx_score_kernel(ApproxArgs P) 
   if (warp == 0) tmem_dealloc<TMEM_COLS>(tmem);
 }
 
+// ---- one query per CTA (decode batches): grid (key tiles, queries), no key image ----------------
+// The CTA scales and splits its query (64 heads x 128) and its 128-key tile (fp32 rows read once)
+// into fp16 hi / lo slabs itself, runs the 24 MMAs (M = 128 keys, N = 64 heads) into 64 TMEM
+// columns, and folds the scores; the maximum key norm of the batch entry is accumulated as in
+// key_image_kernel. About 97 KB of shared memory: two CTAs per SM.
+constexpr int RT_THREADS = 128;
+constexpr int RSLAB_Q = HI * 128;   // 8 KB
+constexpr int RSLAB_K = BM * 128;   // 16 KB
+
+struct RowSmem {
+  alignas(1024) uint8_t qh[2 * RSLAB_Q];
+  alignas(1024) uint8_t ql[2 * RSLAB_Q];
+  alignas(1024) uint8_t kh[2 * RSLAB_K];
+  alignas(1024) uint8_t kl[2 * RSLAB_K];
+  float w[HI];                      // w[h] * 2^-s_qh
+  uint64_t bar;
+  uint32_t tmem_base;
+};
+
+__global__ void __launch_bounds__(RT_THREADS) approx_score_row_kernel(ApproxArgs P) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  RowSmem& sm = *reinterpret_cast<RowSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t = blockIdx.x;
+  const int64_t row = blockIdx.y;
+  const int b = static_cast<int>(row / P.s);
+  const int nvis = visible(P, row);
+  if (t * BM >= nvis) return;  // block-uniform
+
+  // issue every global load first (the key row of this thread, then the query rows of this warp),
+  // so that the two round trips overlap
+  const int j = t * BM + tid;
+  const bool valid = j < P.n_keys;
+  float4 v[DI / 4];
+  {
+    const float4* kr = reinterpret_cast<const float4*>(P.k + (static_cast<int64_t>(b) * P.k_batch_stride + j) * DI);
+#pragma unroll
+    for (int f = 0; f < DI / 4; ++f) v[f] = valid ? __ldg(kr + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  // the query: warp w scales and splits heads w, w+4, ..; lane = float4 of the head's 128 dims
+  constexpr int QH = HI / (RT_THREADS / 32);
+  float4 qv[QH];
+#pragma unroll
+  for (int k = 0; k < QH; ++k)
+    qv[k] = __ldg(reinterpret_cast<const float4*>(P.q + (row * HI + warp + k * (RT_THREADS / 32)) * DI) + lane);
+#pragma unroll
+  for (int k = 0; k < QH; ++k) {
+    const int h = warp + k * (RT_THREADS / 32);
+    float mx = amax4(qv[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int sh = row_shift(mx);
+    uint2 hi, lo;
+    split4(scale4(qv[k], pow2(sh)), &hi, &lo);
+    const uint32_t off = static_cast<uint32_t>((lane >> 4) * RSLAB_Q + h * 128 + ((((lane >> 1) & 7) ^ (h & 7)) << 4) +
+                                               (lane & 1) * 8);
+    *reinterpret_cast<uint2*>(sm.qh + off) = hi;
+    *reinterpret_cast<uint2*>(sm.ql + off) = lo;
+    if (lane == 0) sm.w[h] = P.w[row * HI + h] * pow2(-sh);
+  }
+  // the key tile: thread = key
+  float kinv = 1.f;
+  {
+    float ss = 0.f, mx = 0.f;
+#pragma unroll
+    for (int f = 0; f < DI / 4; ++f) {
+      ss = fmaf(v[f].x, v[f].x, ss);
+      ss = fmaf(v[f].y, v[f].y, ss);
+      ss = fmaf(v[f].z, v[f].z, ss);
+      ss = fmaf(v[f].w, v[f].w, ss);
+      mx = fmaxf(mx, amax4(v[f]));
+    }
+    const int sh = row_shift(mx);
+    const float up = pow2(sh);
+    kinv = pow2(-sh);
+#pragma unroll
+    for (int f = 0; f < DI / 4; ++f) {
+      uint2 hi, lo;
+      split4(scale4(v[f], up), &hi, &lo);
+      const uint32_t off = static_cast<uint32_t>((f >> 4) * RSLAB_K + tid * 128 + ((((f >> 1) & 7) ^ (tid & 7)) << 4) +
+                                                 (f & 1) * 8);
+      *reinterpret_cast<uint2*>(sm.kh + off) = hi;
+      *reinterpret_cast<uint2*>(sm.kl + off) = lo;
+    }
+    cta_atomic_max(valid ? sqrtf(ss) : 0.f, P.kmax + b);
+  }
+  if (warp == 0) tmem_alloc<64>(&sm.tmem_base);
+  if (tid == 0) {
+    bar_init(&sm.bar, 1);
+    bar_init_fence();
+  }
+  fence_async_smem();
+  before_sync();
+  __syncthreads();
+  after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  if (tid == 0) {
+    constexpr uint32_t id = idesc_f16<128, HI>(false, false);
+    const uint32_t qh = smem_u32(sm.qh), ql = smem_u32(sm.ql), kh = smem_u32(sm.kh), kl = smem_u32(sm.kl);
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma16(tmem, sdesc(kl + g * RSLAB_K + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id,
+              (g | kk) ? 1u : 0u);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma16(tmem, sdesc(kh + g * RSLAB_K + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma16(tmem, sdesc(kh + g * RSLAB_K + kk * 32, 16, 1024), sdesc(ql + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
+    }
+    mma_commit(&sm.bar);
+  }
+  const bool ok = __syncthreads_and(bar_wait(&sm.bar, 0));
+  if (ok) {
+    after_sync();
+    float v[HI];
+    const uint32_t lq = static_cast<uint32_t>(warp * 32) << 16;
+#pragma unroll
+    for (int c = 0; c < HI; c += 16) tmem_ld16(tmem + lq + c, v + c);
+    tmem_wait_ld();
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int h = 0; h < HI; h += 4) {
+      const float4 wv = *reinterpret_cast<const float4*>(&sm.w[h]);
+      a0 = fmaf(wv.x, fmaxf(v[h], 0.f), a0);
+      a1 = fmaf(wv.y, fmaxf(v[h + 1], 0.f), a1);
+      a2 = fmaf(wv.z, fmaxf(v[h + 2], 0.f), a2);
+      a3 = fmaf(wv.w, fmaxf(v[h + 3], 0.f), a3);
+    }
+    if (valid) P.scores[row * P.n_pad + j] = ((a0 + a1) + (a2 + a3)) * kinv;
+  } else if (tid == 0) {
+    raise_device_error(DSV4_ERR_WAIT_TIMEOUT);
+  }
+  before_sync();
+  __syncthreads();
+  after_sync();
+  if (warp == 0) tmem_dealloc<64>(tmem);
+}
+
 DSV4_ERROR_READER(indexer_tc)
 
 cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaMemsetAsync(a.kmax, 0, sizeof(float) * a.batch, stream);
   if (e != cudaSuccess) return e;
+  if (row_kernel(a.s)) {
+    const int smem = static_cast<int>(sizeof(RowSmem)) + 1024;
+    static bool rattr = false;
+    if (!rattr) {
+      e = cudaFuncSetAttribute(approx_score_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      rattr = true;
+    }
+    approx_score_row_kernel<<<dim3(key_tiles(a.n_keys), static_cast<unsigned>(static_cast<int64_t>(a.batch) * a.s)),
+                              RT_THREADS, smem, stream>>>(a);
+    return cudaGetLastError();
+  }
   key_image_kernel<<<dim3(key_tiles(a.n_keys), a.batch), BM, 0, stream>>>(a);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;

@@ -37,6 +37,9 @@ __host__ __device__ inline int key_tiles(int n_keys) { return (n_keys + BM - 1) 
 inline size_t kimg_bytes(int batch, int n_keys) {
   return static_cast<size_t>(batch) * key_tiles(n_keys) * TILE_BYTES;
 }
+// fewer than 4 queries per batch entry (decode): one query per CTA, keys split in tiles across CTAs,
+// no key image (kimg / kinv unused)
+inline bool row_kernel(int s) { return s < 4; }
 inline size_t kinv_bytes(int batch, int n_keys) {
   return static_cast<size_t>(batch) * key_tiles(n_keys) * BM * sizeof(float);
 }

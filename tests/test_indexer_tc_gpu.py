@@ -108,3 +108,30 @@ def test_mode2_row_scales_bit_exact(dsv4):
     np.testing.assert_array_equal(got, dsv4.indexer_topk(*args, mode=1).cpu().numpy())
     ref = I.indexer_topk(q[:, :6].numpy(), w[:, :6].numpy(), keys.numpy(), 200)
     np.testing.assert_array_equal(got[:, :6], ref)
+
+
+@pytest.mark.parametrize("b,n,k", [(20, 3000, 512), (64, 2048, 512), (17, 700, 100)])
+def test_mode2_decode_batch_bit_exact(dsv4, b, n, k):
+    """Decode batches (one query per sequence): the one-query-per-CTA tensor-core filter, causal
+    visibility per sequence, block-table output mapping and the window columns, against mode 1 and
+    the oracle."""
+    mod = __import__("importlib").import_module("deepseek-v4-flash-mlx_b200.indexer")
+    q, w, keys = _inputs(b, 1, n, 1000 + b)
+    g = torch.Generator().manual_seed(b)
+    pos = torch.randint(4 * k, 4 * n + 8, (b, 1), generator=g, dtype=torch.int32)   # some see all n keys
+    page = 64
+    pages = (n + page - 1) // page
+    table = torch.stack([torch.randperm(pages, generator=g) for _ in range(b)]).to(torch.int32)
+    outs = []
+    for mode in (1, 2):
+        out = torch.full((b, 1, 128 + k), -7, dtype=torch.int32, device=DEV)
+        mod.indexer_topk_into(out, q.to(DEV), w.to(DEV), keys.to(DEV), k, positions=pos.to(DEV), ratio=4, out_col=128,
+                              out_offset=333, block_table=table.to(DEV), page=page,
+                              win_base=torch.arange(b, dtype=torch.int64, device=DEV) * 128, window=128, mode=mode)
+        outs.append(out.cpu().numpy())
+    np.testing.assert_array_equal(outs[1], outs[0])
+    ref = I.indexer_topk(q.numpy(), w.numpy(), keys.numpy(), k, pos.numpy())          # [b, 1, k] key indices
+    sel = ref[:, 0]
+    mapped = np.where(sel >= 0, table.numpy()[np.arange(b)[:, None], np.maximum(sel, 0) // page] * page
+                      + np.maximum(sel, 0) % page + 333, -1)
+    np.testing.assert_array_equal(np.sort(outs[1][:, 0, 128:], axis=1), np.sort(mapped, axis=1))
