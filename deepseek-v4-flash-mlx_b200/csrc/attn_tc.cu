@@ -61,6 +61,8 @@ struct Smem {
 static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory above the 227 KB a CTA may opt into");
 
 struct Params {
+  int splits;             // CTAs per query; > 1: partials into part (the split-K layout of sparse_attn.cu)
+  float* part;
   const __nv_bfloat16* q;
   const __nv_bfloat16* kv;
   const void* idx;
@@ -170,9 +172,14 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
   // the 128-byte swizzle pattern is anchored to 1024-byte boundaries
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t qi = blockIdx.x;
+  // CTA = (query, split): tiles [tbase, tbase + ntiles) of the query's list
+  const int64_t qi = blockIdx.x / P.splits;
+  const int split = static_cast<int>(blockIdx.x % P.splits);
   const int L = (P.win_base ? P.window : 0) + P.t;
-  const int ntiles = (L + BN - 1) / BN;
+  const int tiles_all = (L + BN - 1) / BN;
+  const int per = (tiles_all + P.splits - 1) / P.splits;
+  const int tbase = split * per;
+  const int ntiles = max(0, min(per, tiles_all - tbase));
 
   if (warp == 0) tmem_alloc<TMEM_COLS>(&sm.tmem_base);
   if (tid == 0) {
@@ -257,7 +264,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
         const int c = wt + W_THREADS * k;
         int32_t v = 0;
         if (k < nown) {
-          const int u = i * BN + (c >> 4);
+          const int u = (tbase + i) * BN + (c >> 4);
           int64_t r = u < L ? list_row(P, qi, u) : -1;
           if (r >= P.n) {
             raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
@@ -293,7 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       }
       before_sync();
       sm_bar();
-      valid = row_valid(P, qi, row, L);
+      valid = row_valid(P, qi, tbase * BN + row, L);
     }
     bool ok = true;
     for (int i = 0; i < ntiles; ++i) {
@@ -404,7 +411,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       fence_async_smem();
       before_sync();
       bar_arrive(&sm.bar_p);
-      valid = row_valid(P, qi, (i + 1) * BN + row, L);
+      valid = row_valid(P, qi, (tbase + i + 1) * BN + row, L);
     }
 
     if (smx) {
@@ -412,7 +419,49 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
         ok = __all_sync(0xffffffffu, bar_wait_or_abort(&sm.bar_fin, 0, abort));
         if (!ok && lane == 0) set_abort(sm);
       }
-      if (ok && !*abort) {
+      if (ok && !*abort && P.splits > 1) {
+        after_sync();
+        // split partial: O unnormalised (relative to m), m and l per head, for the combine kernel;
+        // part [s][splits][64][512] then [s][splits][64][2]
+        const int64_t unit = qi * P.splits + split;
+        float* po = P.part + unit * (HB * D);
+        float* pml = P.part + P.s * P.splits * static_cast<int64_t>(HB * D) + unit * (HB * 2);
+        if (ntiles > 0) {
+#pragma unroll 1
+          for (int mt = 0; mt < 4; ++mt) {
+            const int d = mt * 128 + qd * 32 + lane;
+            float v[32];
+            tmem_ld16(tmem + lq + COL_O + mt * HB + half * 32, v);
+            tmem_ld16(tmem + lq + COL_O + mt * HB + half * 32 + 16, v + 16);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) po[(half * 32 + c) * D + d] = v[c];
+          }
+          if (qd == 0) {
+            float l[32];
+            tmem_ld16(tmem + lq + COL_L + half * 32, l);
+            tmem_ld16(tmem + lq + COL_L + half * 32 + 16, l + 16);
+            tmem_wait_ld();
+            // lane c writes head half*32 + c (selects, no dynamic register indexing)
+            float mv = 0.f, lv = 0.f;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              mv = (c == lane) ? m[c] : mv;
+              lv = (c == lane) ? l[c] : lv;
+            }
+            pml[(half * 32 + lane) * 2 + 0] = mv;
+            pml[(half * 32 + lane) * 2 + 1] = lv;
+          }
+        } else {
+          for (int c = 0; c < 32; ++c)
+#pragma unroll 1
+            for (int mt = 0; mt < 4; ++mt) po[(half * 32 + c) * D + mt * 128 + qd * 32 + lane] = 0.f;
+          if (qd == 0) {
+            pml[(half * 32 + lane) * 2 + 0] = -INFINITY;
+            pml[(half * 32 + lane) * 2 + 1] = 0.f;
+          }
+        }
+      } else if (ok && !*abort) {
         after_sync();
         // epilogue: lane = dim (within the M-tile quadrant), 32 heads per thread
         float inv[32];
@@ -484,9 +533,12 @@ DSV4_ERROR_READER(attn_tc)
 
 using namespace dsv4;
 
-// Internal entry used by dsv4_sparse_attn for prefill shapes (64 heads, bf16 q).
-int dsv4_sparse_attn_tc(const dsv4_sparse_attn_params* p, void* stream) {
+// Internal entry used by dsv4_sparse_attn (64 heads, bf16 q); splits > 1 writes the partials that
+// sparse_attn.cu's combine kernel merges.
+int dsv4_sparse_attn_tc(const dsv4_sparse_attn_params* p, int splits, float* part, void* stream) {
   tc::Params P;
+  P.splits = splits;
+  P.part = part;
   P.q = reinterpret_cast<const __nv_bfloat16*>(p->q);
   P.idx = p->idx;
   P.sink = p->sink;
@@ -514,7 +566,8 @@ int dsv4_sparse_attn_tc(const dsv4_sparse_attn_params* p, void* stream) {
     DSV4_CUDA_CHECK(cudaFuncSetAttribute(tc::attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  tc::attn_tc_kernel<<<static_cast<unsigned>(p->s), tc::THREADS, smem, as_stream(stream)>>>(P);
+  DSV4_CHECK_ARG(splits >= 1 && (splits == 1 || part != nullptr), "dsv4_sparse_attn: split partials need a workspace");
+  tc::attn_tc_kernel<<<static_cast<unsigned>(p->s * splits), tc::THREADS, smem, as_stream(stream)>>>(P);
   DSV4_LAUNCH_CHECK("attn_tc_kernel");
   return DSV4_OK;
 }

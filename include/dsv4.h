@@ -102,10 +102,11 @@ typedef struct {
   int32_t win_stride;
   int32_t window;
   int32_t window_linear;
-  /* kernel choice: 0 = automatic (the tcgen05 kernel for prefill-shaped calls: 64 heads, bf16 q or
-   * the fused q prologue, one CTA per query filling the GPU; the mma.sync split-K kernel otherwise),
-   * 1 = the mma.sync kernel, 2 = the tcgen05 kernel (64 heads and bf16 q or the fused prologue,
-   * else DSV4_ERR_INVALID_ARGUMENT). Both compute the same function; the choice is for tests and
+  /* kernel choice: 0 = automatic (the tcgen05 kernel, 128-row tiles, split-K over tile ranges, for
+   * calls of at least 16 queries with 64 heads and bf16 q or the fused q prologue; the mma.sync
+   * split-K kernel otherwise), 1 = the mma.sync kernel, 2 = the tcgen05 kernel (64 heads and bf16 q
+   * or the fused prologue, else DSV4_ERR_INVALID_ARGUMENT). Both compute the same function (num_splits
+   * counts 64-row tiles for the first, 128-row tiles for the second); the choice is for tests and
    * measurements. */
   int32_t kernel;
 } dsv4_sparse_attn_params;

@@ -146,3 +146,36 @@ def test_tc_rejects_unsupported_shape(dsv4):
                           idx.to(DEV), SCALE, kernel=2)
     with pytest.raises(L.Dsv4Error):
         _sa().sparse_attn(q.to(DEV), kv.to(DEV).bfloat16(), sink.to(DEV), idx.to(DEV), SCALE, kernel=2)  # fp32 q
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 5])
+def test_tc_split_partials_against_oracle(dsv4, splits):
+    """The tcgen05 kernel split over ranges of 128-row tiles (partials merged by the combine kernel),
+    with the implicit decode window (ring order) and the fused inverse rope."""
+    S = _sa()
+    s, n, t = 20, 4000, 512
+    g = torch.Generator().manual_seed(40 + splits)
+    q = _bf16(torch.randn(s, 64, 512, generator=g))
+    kv = _bf16(torch.randn(n, 512, generator=g))
+    sink = torch.randn(64, generator=g)
+    idx = torch.randint(128 * s, n, (s, t), generator=g, dtype=torch.int32)
+    idx[:, 400:] = -1
+    pos = torch.randint(0, 5000, (s,), generator=g, dtype=torch.int32)
+    wb = torch.arange(s, dtype=torch.int64) * 128
+    freqs = importlib.import_module("deepseek-v4-flash-mlx_b200.norm_rope").rope_freqs(64, DEV)
+    out = S.sparse_attn_rope(q.to(DEV).bfloat16(), kv.to(DEV).bfloat16(), sink.to(DEV), idx.to(DEV), SCALE,
+                             pos.to(DEV), freqs, 64, out_dtype=torch.float32, num_splits=splits,
+                             win_base=wb.to(DEV), window=128, kernel=2)
+    # the decode ring order of the window (ref_torch/sparse_attn.py:11-15) and the oracle
+    lists = []
+    for i in range(s):
+        p = int(pos[i])
+        if p >= 127:
+            sp = p % 128
+            win = [int(wb[i]) + (sp + 1 + u if u < 127 - sp else u - (127 - sp)) for u in range(128)]
+        else:
+            win = [int(wb[i]) + u if u <= p else -1 for u in range(128)]
+        lists.append(torch.tensor(win + idx[i].tolist()))
+    ref = SA.sparse_attn(q, kv, sink, torch.stack(lists), SCALE)
+    ref = NR.rope_at(ref, pos, freqs.cpu(), 64, inverse=True)
+    assert_close_bf16(out, ref, what=f"splits={splits}")
