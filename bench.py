@@ -54,6 +54,13 @@ L2_BYTES = 126 * 1024 * 1024
 # kernels of one decode step: q norm/rope, indexer scores, top-k selection, sparse attention, split merge
 LAUNCHES_PER_STEP = 5
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant op, from one
+# ncu capture each on B200: config 2 on this bench's own command (score + select kernels of one
+# step); config 4 on `--kernel-case attn_prefill` (4,096 of the 65,536 queries, every query with
+# 1,152 list entries), scaled by 16 to the step's eight 8,192-query launches.
+TRAFFIC = {"c2": {"indexer_topk": 4331264, "sparse_attn": 2138982},
+           "c4": {"tc::attn_tc_kernel": 16 * 547425536}}
+
 
 def _pkg():
     import importlib
@@ -263,7 +270,12 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--replicas", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-case", default=None, choices=["attn_prefill", "indexer_prefill"],
+                    help="profiling aid: run one prefill kernel alone on a 4096-query slice of config 4 "
+                         "(positions 60000..64095) and print its CUDA-event time; not a bench line")
     args = ap.parse_args()
+    if args.kernel_case:
+        return run_kernel_case(args)
     args.steps_given, args.warmup_given = args.steps is not None, args.warmup is not None
     if args.steps is None:
         args.steps = 2400
@@ -381,12 +393,7 @@ def main():
                 "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
                 "per_kernel_us": {k: round(v["us"], 3) for k, v in kern.items()},
                 "algorithmic_bytes_per_launch": kb["bytes"]}
-    prof = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(prof):
-        try:
-            roofline["traffic"] = json.load(open(prof)).get(args.config, {}).get(top)
-        except Exception:
-            pass
+    roofline["traffic"] = TRAFFIC.get(args.config, {}).get(top)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -491,7 +498,8 @@ def bench_prefill(args, world, rank, local, dev):
     achieved = att_flops / (att_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "kernel": "tc::attn_tc_kernel", "achieved": achieved,
                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                "peak_source": "measured" if "when" in peaks else "fallback", "traffic": None,
+                "peak_source": "measured" if "when" in peaks else "fallback",
+                "traffic": TRAFFIC["c4"]["tc::attn_tc_kernel"] // world,  # this rank's queries
                 "algorithmic_flops_per_launch": att_flops, "phases_ms": phases}
     # e2e: this rank's inputs from pinned host memory, the step, its outputs back
     hx = x.cpu().pin_memory()
@@ -726,6 +734,49 @@ def kernel_times(dsv4, cases, runners, stream, dev, n):
         torch.cuda.synchronize()
         out[name] = {"us": e0.elapsed_time(e1) * 1000.0 / (reps * R), "bytes": nbytes}
     return out
+
+
+def run_kernel_case(args):
+    """One prefill kernel on a 4096-query slice of config 4 (queries at positions 60000..64095,
+    65,536 window rows + 16,384 compressed rows, top-k 1024): the case the profiles under profiles/
+    were captured on. Seeded synthetic inputs; prints one JSON line with the CUDA-event time."""
+    import importlib
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    SA = importlib.import_module(PKG + ".sparse_attn")
+    IX = importlib.import_module(PKG + ".indexer")
+    NRm = importlib.import_module(PKG + ".norm_rope")
+    s, nwin, ncomp, top_k = 4096, 65536, 16384, 1024
+    g = torch.Generator(device=dev).manual_seed(0)
+    pos = torch.arange(60000, 60000 + s, dtype=torch.int32, device=dev)
+    reps = args.steps if args.steps is not None else 3
+    if args.kernel_case == "attn_prefill":
+        q = torch.randn(s, 64, 512, device=dev, generator=g).bfloat16()
+        kvcat = torch.randn(nwin + ncomp, 512, device=dev, generator=g).bfloat16()
+        sink = torch.randn(64, device=dev, generator=g)
+        idx = torch.randint(nwin, nwin + ncomp, (s, top_k), device=dev, generator=g, dtype=torch.int32)
+        freqs = NRm.rope_freqs(64, dev)
+        wb = torch.zeros(1, dtype=torch.int64, device=dev)
+        fn = lambda: SA.sparse_attn_rope(q, kvcat, sink, idx, 512 ** -0.5, pos, freqs, 64, win_base=wb, window=128,
+                                         window_linear=True, kernel=2)
+        work = {"flop": s * 64 * (128 + top_k) * 512 * 4}
+    else:
+        qi = torch.randn(1, s, 64, 128, device=dev, generator=g)
+        wi = torch.randn(1, s, 64, device=dev, generator=g) / 8
+        keys = torch.randn(1, ncomp, 128, device=dev, generator=g)
+        out = torch.empty((1, s, top_k), dtype=torch.int32, device=dev)
+        fn = lambda: IX.indexer_topk_into(out, qi, wi, keys, top_k, positions=pos[None], ratio=4, mode=2)
+        work = {"visible_pairs": int(((pos.long() + 1) // 4).clamp(max=ncomp).sum())}
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    print(json.dumps({"kernel_case": args.kernel_case, "queries": s, "ms_per_call": ms, **work}), flush=True)
 
 
 if __name__ == "__main__":

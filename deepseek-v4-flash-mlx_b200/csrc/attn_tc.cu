@@ -35,9 +35,9 @@ namespace tc {
 using namespace tc5;
 
 constexpr int D = 512, HB = 64, BN = 128;
-constexpr int THREADS = 384;
+constexpr int THREADS = 384;               // 12 warps (3 per SM sub-partition: 168 registers each)
 constexpr int SM_WARP0 = 4;                 // first softmax warp
-constexpr int SM_THREADS = 256;             // softmax warps 4-11
+constexpr int SM_THREADS = 256;             // softmax warps 4-11 (warp w: lane quadrant w % 4)
 constexpr int W_WARP0 = 1, W_THREADS = 352;  // gather workers: warps 1-11
 constexpr int W_CHUNKS = 6;                 // ceil(128 rows x 16 chunks per slab pair / 352)
 constexpr int SLAB_Q = HB * 128;            // 8 KB: one 64-dim slab of Q (64 rows x 128 B)
@@ -52,6 +52,7 @@ struct Smem {
   alignas(1024) uint8_t kv[8 * SLAB_KV];    // 128 KB
   alignas(1024) uint8_t p[BN * 128];        // 16 KB: P^T rows (64 heads x bf16)
   float red[4][HB];                         // per-quadrant column maxima
+  float alpha[HB];                          // rescale factors of a tile that raised m
   uint64_t bar_full[4];                     // slab pair mt of the current tile landed (one arrival per worker)
   uint64_t bar_empty[4];                    // O^T M-tile mt done: slab pair mt free
   uint64_t bar_s, bar_p, bar_fin;           // S^T done / P^T published / everything issued done
@@ -356,18 +357,18 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
         // exact tile maximum per head, then m = max(m, tile max); O^T and L rescaled by 2^(m_old - m)
         sm.red[qd][half * 32 + lane] = warp_col_max32(x);
         sm_bar();
-        float alpha[32];
+        // the rescale factors go to shared memory (every warp of a half writes the same values)
         bool any = false;
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const int hh = half * 32 + c;
           const float tm = fmaxf(fmaxf(sm.red[0][hh], sm.red[1][hh]), fmaxf(sm.red[2][hh], sm.red[3][hh]));
           const float mn = fmaxf(m[c], tm);
-          alpha[c] = (m[c] == -INFINITY) ? 0.f : exp2f(m[c] - mn);
+          if (lane == c) sm.alpha[hh] = (m[c] == -INFINITY) ? 0.f : exp2f(m[c] - mn);
           any |= (mn != m[c]) && (m[c] != -INFINITY);
           m[c] = mn;
         }
-        sm_bar();  // red[] reuse
+        sm_bar();  // red[] reuse; alpha[] written
         if (i > 0 && __any_sync(0xffffffffu, any)) {
           // the previous tile's O^T and L MMAs completed before this tile's S^T (one commit covers all)
 #pragma unroll 1
@@ -377,7 +378,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
             tmem_ld16(tmem + lq + COL_O + mt * HB + half * 32 + 16, v + 16);
             tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) v[c] *= alpha[c];
+            for (int c = 0; c < 32; ++c) v[c] *= sm.alpha[half * 32 + c];
             tmem_st16(tmem + lq + COL_O + mt * HB + half * 32, v);
             tmem_st16(tmem + lq + COL_O + mt * HB + half * 32 + 16, v + 16);
           }
@@ -386,7 +387,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
           tmem_ld16(tmem + lq + COL_L + half * 32 + 16, v + 16);
           tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] *= alpha[c];
+          for (int c = 0; c < 32; ++c) v[c] *= sm.alpha[half * 32 + c];
           tmem_st16(tmem + lq + COL_L + half * 32, v);
           tmem_st16(tmem + lq + COL_L + half * 32 + 16, v + 16);
           tmem_wait_st();
@@ -438,19 +439,21 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
             for (int c = 0; c < 32; ++c) po[(half * 32 + c) * D + d] = v[c];
           }
           if (qd == 0) {
+            // m and l of this half's 32 heads through shared memory (red[0], red[1]: free here)
             float l[32];
             tmem_ld16(tmem + lq + COL_L + half * 32, l);
             tmem_ld16(tmem + lq + COL_L + half * 32 + 16, l + 16);
             tmem_wait_ld();
-            // lane c writes head half*32 + c (selects, no dynamic register indexing)
-            float mv = 0.f, lv = 0.f;
+            if (lane == 0) {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              mv = (c == lane) ? m[c] : mv;
-              lv = (c == lane) ? l[c] : lv;
+              for (int c = 0; c < 32; ++c) {
+                sm.red[0][half * 32 + c] = m[c];
+                sm.red[1][half * 32 + c] = l[c];
+              }
             }
-            pml[(half * 32 + lane) * 2 + 0] = mv;
-            pml[(half * 32 + lane) * 2 + 1] = lv;
+            __syncwarp();
+            pml[(half * 32 + lane) * 2 + 0] = sm.red[0][half * 32 + lane];
+            pml[(half * 32 + lane) * 2 + 1] = sm.red[1][half * 32 + lane];
           }
         } else {
           for (int c = 0; c < 32; ++c)
