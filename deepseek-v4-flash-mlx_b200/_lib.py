@@ -75,7 +75,14 @@ class CompressorDecodeParams(ctypes.Structure):
 
 class LinearParams(ctypes.Structure):
     _fields_ = [("x", vp), ("w", vp), ("w_scale", vp), ("y", vp), ("m", i64), ("n", i32), ("k", i32),
-                ("groups", i32), ("group", i32), ("x_dtype", i32), ("w_dtype", i32), ("y_dtype", i32)]
+                ("groups", i32), ("group", i32), ("x_dtype", i32), ("w_dtype", i32), ("y_dtype", i32),
+                ("workspace", vp), ("workspace_bytes", sz)]
+
+
+class DecodeRowsParams(ctypes.Structure):
+    _fields_ = [("positions", vp), ("win_base", vp), ("block_table", vp), ("win_rows", vp), ("comp_rows", vp),
+                ("key_rows", vp), ("comp_base", i64), ("b", i32), ("window", i32), ("ratio", i32), ("page", i32),
+                ("bt_stride", i32), ("max_comp", i32)]
 
 
 # every symbol include/dsv4.h declares, with its ctypes signature
@@ -97,6 +104,8 @@ SIGNATURES = {
     "dsv4_decode_window_indices": (ctypes.c_int, [i32, i32, vp, vp, vp, i32, vp]),
     "dsv4_compressor_pool": (ctypes.c_int, [ctypes.POINTER(CompressorParams), vp]),
     "dsv4_compressor_decode": (ctypes.c_int, [ctypes.POINTER(CompressorDecodeParams), vp]),
+    "dsv4_decode_rows": (ctypes.c_int, [ctypes.POINTER(DecodeRowsParams), vp]),
+    "dsv4_linear_workspace_size": (sz, [ctypes.POINTER(LinearParams)]),
     "dsv4_linear": (ctypes.c_int, [ctypes.POINTER(LinearParams), vp]),
     "dsv4_cast": (ctypes.c_int, [vp, i32, vp, i32, i64, vp]),
 }

@@ -7,6 +7,7 @@
 // (exact: |q| <= 127), each 64-wide k group is accumulated separately in fp32 and folded into the
 // output with its scale, so the dequantised product is computed without rounding the weights.
 // CTA tile 128 x 128 x 64, 8 warps (2 x 4), warp tile 64 x 32, bf16 mma.sync, 3-stage cp.async.
+#include <algorithm>
 #include "common.cuh"
 
 namespace dsv4 {
@@ -43,6 +44,8 @@ struct Params {
   int64_t m;
   int n, k, groups;
   int y_dtype;
+  int ksplit;               // CTAs along k; > 1: fp32 partials [ksplit][m][groups*n] into part
+  float* part;
 };
 
 template <bool I8>
@@ -100,8 +103,12 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(Params P) {
   const int wm = warp >> 2, wn = warp & 3;  // 2 x 4 warps
   const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM;
   const int n0 = blockIdx.x * BN;
-  const int g = blockIdx.z;
+  const int g = blockIdx.z / P.ksplit;
+  const int split = blockIdx.z % P.ksplit;
   const int KT = P.k / BK;
+  const int per = (KT + P.ksplit - 1) / P.ksplit;
+  const int kt0 = split * per;
+  const int nkt = max(0, min(per, KT - kt0));  // k tiles [kt0, kt0 + nkt) of this CTA
 
   float acc[4][4][4];
   float gacc[4][4][4];  // per-group partial (int8 weights only)
@@ -114,17 +121,18 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(Params P) {
 
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
-    if (s < KT) load_stage<I8>(P, sm, s, m0, n0, s, g);
+    if (s < nkt) load_stage<I8>(P, sm, s, m0, n0, kt0 + s, g);
     asm volatile("cp.async.commit_group;\n" ::);
   }
 
-  for (int kt = 0; kt < KT; ++kt) {
-    const int st = kt % STAGES;
+  for (int it = 0; it < nkt; ++it) {
+    const int kt = kt0 + it;
+    const int st = it % STAGES;
     asm volatile("cp.async.wait_group %0;\n" ::"n"(STAGES - 2));
     __syncthreads();
     {
-      int nk = kt + STAGES - 1;
-      if (nk < KT) load_stage<I8>(P, sm, nk % STAGES, m0, n0, nk, g);
+      int nk = it + STAGES - 1;
+      if (nk < nkt) load_stage<I8>(P, sm, nk % STAGES, m0, n0, kt0 + nk, g);
       asm volatile("cp.async.commit_group;\n" ::);
     }
     uint32_t bsm;
@@ -216,7 +224,10 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(Params P) {
         if (col >= P.n) continue;
         const int64_t off = row * ldy + static_cast<int64_t>(g) * P.n + col;
         float v0 = acc[mt][nt][hf * 2], v1 = acc[mt][nt][hf * 2 + 1];
-        if (P.y_dtype == DSV4_BF16) {
+        if (P.ksplit > 1) {
+          // fp32 partial of this k range (col is even, n is even: 8-byte aligned pairs)
+          *reinterpret_cast<float2*>(P.part + static_cast<int64_t>(split) * P.m * ldy + off) = make_float2(v0, v1);
+        } else if (P.y_dtype == DSV4_BF16) {
           if (col + 1 < P.n)
             *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(P.y) + off) = pack_bf16x2(v0, v1);
           else
@@ -234,10 +245,405 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(Params P) {
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Decode-shaped projections (m <= 64 tokens): the weights are the only traffic that matters, so the
+// CTA streams 128 weight rows x its k range through a cp.async ring and the tokens ride along as
+// the small operand. Swapped roles: the MMA's A (16 rows) is a slice of W, its B (8 columns) eight
+// tokens, D = W x^T. Every lane reads 16 contiguous k of one row and its tokens at the same
+// positions, so the k order inside a 64-wide group is permuted identically in both operands (slot
+// 2q+e / 2q+8+e of k-step j is element 16q + 4j + e / 16q + 4j + 2 + e); the sum is unchanged.
+// int8 weights are widened in registers exactly (|q| <= 128 fits the 8 significant bits of bf16),
+// each group accumulates in fp32 and folds with its scale, as in the tiled kernel.
+namespace sk {
+
+constexpr int ROWS = 128, THREADS = 256, BK = 64;
+
+template <bool I8>
+struct Cfg {
+  static constexpr int NST = I8 ? 5 : 4;
+  static constexpr int ROW_BYTES = BK * (I8 ? 1 : 2);
+};
+
+template <bool I8, int MT>
+struct Smem {
+  alignas(128) uint8_t w[Cfg<I8>::NST][ROWS * Cfg<I8>::ROW_BYTES];
+  alignas(128) uint8_t x[Cfg<I8>::NST][MT * 8 * 128];  // 8*MT tokens x 64 bf16, chunk c at c ^ (t % 8)
+  float scale[I8 ? Cfg<I8>::NST : 1][ROWS];
+};
+
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+
+// two signed bytes of w (bytes 2h, 2h+1) -> bf16x2, exact: 2^23 + (b ^ 0x80) as an fp32 bit pattern,
+// minus 2^23 + 128, is b; an integer of magnitude <= 128 is its own bf16 (the fp32's upper half)
+__device__ __forceinline__ uint32_t s8x2_bf16x2(uint32_t w, int h) {
+  const uint32_t u = w ^ 0x80808080u;
+  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, h ? 0x7442 : 0x7440)) - 8388736.0f;
+  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, h ? 0x7443 : 0x7441)) - 8388736.0f;
+  return __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// fp32 at shared address `a` of the CTA with rank `rank` in this cluster
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t a, int rank) {
+  uint32_t ra;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(ra) : "r"(a), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+__device__ __forceinline__ void store_y(const Params& P, int64_t off, float v) {
+  if (P.y_dtype == DSV4_BF16)
+    reinterpret_cast<__nv_bfloat16*>(P.y)[off] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<float*>(P.y)[off] = v;
+}
+
+template <bool I8, int MT>
+__device__ __forceinline__ void load_w(const Params& P, Smem<I8, MT>& sm, int st, int n0, int kg, int g) {
+  const int tid = threadIdx.x;
+  constexpr int CH = Cfg<I8>::ROW_BYTES / 16;  // 16-byte chunks per weight row
+  const uint8_t* wb = reinterpret_cast<const uint8_t*>(P.w) +
+                      (static_cast<int64_t>(g) * P.n * P.k + static_cast<int64_t>(kg) * BK) * (I8 ? 1 : 2);
+  const uint32_t ws = static_cast<uint32_t>(__cvta_generic_to_shared(sm.w[st]));
+#pragma unroll
+  for (int i = 0; i < ROWS * CH / THREADS; ++i) {
+    const int c = tid + i * THREADS;
+    const int r = c / CH, ch = c % CH;
+    const bool v = n0 + r < P.n;
+    const uint8_t* src = wb + static_cast<int64_t>(v ? n0 + r : 0) * P.k * (I8 ? 1 : 2) + ch * 16;
+    cp_async16(ws + r * Cfg<I8>::ROW_BYTES + ((I8 ? ch : (ch ^ (r & 7))) << 4), src, v);
+  }
+}
+
+template <bool I8, int MT>
+__device__ __forceinline__ void load_x(const Params& P, Smem<I8, MT>& sm, int st, int kg, int g) {
+  const int tid = threadIdx.x;
+  const int64_t ldx = static_cast<int64_t>(P.groups) * P.k;
+  const __nv_bfloat16* xb = P.x + static_cast<int64_t>(g) * P.k + static_cast<int64_t>(kg) * BK;
+  const uint32_t xs = static_cast<uint32_t>(__cvta_generic_to_shared(sm.x[st]));
+  for (int c = tid; c < MT * 8 * 8; c += THREADS) {
+    const int t = c >> 3, ch = c & 7;
+    const bool v = t < P.m;
+    cp_async16(xs + t * 128 + ((ch ^ (t & 7)) << 4), xb + (v ? t : 0) * ldx + ch * 8, v);
+  }
+}
+
+template <bool I8, int MT>
+__device__ __forceinline__ float load_scale(const Params& P, int n0, int kg, int g) {
+  const int r = n0 + static_cast<int>(threadIdx.x);
+  if (threadIdx.x >= ROWS || r >= P.n) return 0.f;
+  return __bfloat162float(__ldg(P.ws + (static_cast<int64_t>(g) * P.n + r) * (P.k / BK) + kg));
+}
+
+template <bool I8, int MT>
+__global__ void __launch_bounds__(THREADS) skinny_kernel(Params P) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem<I8, MT>& sm = *reinterpret_cast<Smem<I8, MT>*>(smem_raw);
+  constexpr int NST = Cfg<I8>::NST;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r = lane >> 2, q = lane & 3;
+  const int n0 = blockIdx.x * ROWS;
+  const int g = blockIdx.z / P.ksplit;
+  const int split = blockIdx.z % P.ksplit;
+  const int KT = P.k / BK;
+  const int per = (KT + P.ksplit - 1) / P.ksplit;
+  const int kt0 = split * per;
+  const int nkt = max(0, min(per, KT - kt0));
+
+  float acc[MT][4], gacc[MT][4];
+#pragma unroll
+  for (int a = 0; a < MT; ++a)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+
+  // the weights and their scales do not depend on the kernel before this one: their first stages
+  // load while it finishes (programmatic dependent launch); the tokens load after pdl_wait()
+#pragma unroll
+  for (int s = 0; s < NST - 1; ++s) {
+    if (s < nkt) {
+      load_w<I8, MT>(P, sm, s, n0, kt0 + s, g);
+      if constexpr (I8)
+        if (tid < ROWS) sm.scale[s][tid] = load_scale<I8, MT>(P, n0, kt0 + s, g);
+    }
+  }
+  pdl_wait();
+#pragma unroll
+  for (int s = 0; s < NST - 1; ++s) {
+    if (s < nkt) load_x<I8, MT>(P, sm, s, kt0 + s, g);
+    asm volatile("cp.async.commit_group;\n" ::);
+  }
+
+  const int wrow = warp * 16 + r;  // this lane's weight rows: wrow, wrow + 8
+  for (int it = 0; it < nkt; ++it) {
+    const int st = it % NST;
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(NST - 2));
+    __syncthreads();
+    const int nk = it + NST - 1;
+    float sc_next = 0.f;
+    if (nk < nkt) {
+      load_w<I8, MT>(P, sm, nk % NST, n0, kt0 + nk, g);
+      load_x<I8, MT>(P, sm, nk % NST, kt0 + nk, g);
+      if constexpr (I8) sc_next = load_scale<I8, MT>(P, n0, kt0 + nk, g);
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+
+    // operands of this lane: 16 k of rows wrow and wrow + 8, 16 k of its tokens
+    const uint32_t wsm = static_cast<uint32_t>(__cvta_generic_to_shared(sm.w[st]));
+    const uint32_t xsm = static_cast<uint32_t>(__cvta_generic_to_shared(sm.x[st]));
+    uint32_t w0[8], w1[8];  // I8: words 0..3 used (4 bytes each); bf16: 8 words of k pairs
+    if constexpr (I8) {
+      const uint4 a = lds128(wsm + wrow * 64 + q * 16), b = lds128(wsm + (wrow + 8) * 64 + q * 16);
+      w0[0] = a.x; w0[1] = a.y; w0[2] = a.z; w0[3] = a.w;
+      w1[0] = b.x; w1[1] = b.y; w1[2] = b.z; w1[3] = b.w;
+    } else {
+      const int r0 = wrow, r1 = wrow + 8;
+      const uint4 a0 = lds128(wsm + r0 * 128 + (((2 * q) ^ (r0 & 7)) << 4));
+      const uint4 a1 = lds128(wsm + r0 * 128 + (((2 * q + 1) ^ (r0 & 7)) << 4));
+      const uint4 b0 = lds128(wsm + r1 * 128 + (((2 * q) ^ (r1 & 7)) << 4));
+      const uint4 b1 = lds128(wsm + r1 * 128 + (((2 * q + 1) ^ (r1 & 7)) << 4));
+      w0[0] = a0.x; w0[1] = a0.y; w0[2] = a0.z; w0[3] = a0.w; w0[4] = a1.x; w0[5] = a1.y; w0[6] = a1.z; w0[7] = a1.w;
+      w1[0] = b0.x; w1[1] = b0.y; w1[2] = b0.z; w1[3] = b0.w; w1[4] = b1.x; w1[5] = b1.y; w1[6] = b1.z; w1[7] = b1.w;
+    }
+    uint32_t xw[MT][8];
+#pragma unroll
+    for (int nt = 0; nt < MT; ++nt) {
+      const int t = nt * 8 + r;
+      const uint4 a = lds128(xsm + t * 128 + (((2 * q) ^ (t & 7)) << 4));
+      const uint4 b = lds128(xsm + t * 128 + (((2 * q + 1) ^ (t & 7)) << 4));
+      xw[nt][0] = a.x; xw[nt][1] = a.y; xw[nt][2] = a.z; xw[nt][3] = a.w;
+      xw[nt][4] = b.x; xw[nt][5] = b.y; xw[nt][6] = b.z; xw[nt][7] = b.w;
+    }
+    if constexpr (I8) {
+#pragma unroll
+      for (int a = 0; a < MT; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) gacc[a][c] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t af[4];
+      if constexpr (I8) {
+        af[0] = s8x2_bf16x2(w0[j], 0);
+        af[1] = s8x2_bf16x2(w1[j], 0);
+        af[2] = s8x2_bf16x2(w0[j], 1);
+        af[3] = s8x2_bf16x2(w1[j], 1);
+      } else {
+        af[0] = w0[2 * j];
+        af[1] = w1[2 * j];
+        af[2] = w0[2 * j + 1];
+        af[3] = w1[2 * j + 1];
+      }
+#pragma unroll
+      for (int nt = 0; nt < MT; ++nt) {
+        if constexpr (I8)
+          mma_bf16(gacc[nt], af, xw[nt][2 * j], xw[nt][2 * j + 1]);
+        else
+          mma_bf16(acc[nt], af, xw[nt][2 * j], xw[nt][2 * j + 1]);
+      }
+    }
+    if constexpr (I8) {
+      const float s0 = sm.scale[st][wrow], s1 = sm.scale[st][wrow + 8];
+#pragma unroll
+      for (int nt = 0; nt < MT; ++nt) {
+        acc[nt][0] = fmaf(gacc[nt][0], s0, acc[nt][0]);
+        acc[nt][1] = fmaf(gacc[nt][1], s0, acc[nt][1]);
+        acc[nt][2] = fmaf(gacc[nt][2], s1, acc[nt][2]);
+        acc[nt][3] = fmaf(gacc[nt][3], s1, acc[nt][3]);
+      }
+      // the slot refilled this iteration was last read in the previous one (before the barrier)
+      if (nk < nkt && tid < ROWS) sm.scale[nk % NST][tid] = sc_next;
+    }
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::);
+  pdl_trigger();
+
+  // D fragment: c0, c1 = (row wrow, tokens 2q, 2q+1 of the tile), c2, c3 = row wrow + 8
+  const int64_t ldy = static_cast<int64_t>(P.groups) * P.n;
+  if (P.ksplit == 1) {
+#pragma unroll
+    for (int nt = 0; nt < MT; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int f = n0 + wrow + hf * 8;
+        if (f >= P.n) continue;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int64_t t = nt * 8 + 2 * q + e;
+          if (t >= P.m) continue;
+          store_y(P, t * ldy + static_cast<int64_t>(g) * P.n + f, acc[nt][hf * 2 + e]);
+        }
+      }
+    return;
+  }
+  // k split over the CTAs of this cluster: each parks its partial tile in shared memory, then CTA
+  // `split` sums rows [split, split + 1) * ROWS / ksplit of all partials in split order (the same
+  // order whichever CTA finishes first) and stores them
+  constexpr int LD = MT * 8 + 1;
+  static_assert(ROWS * LD * 4 <= sizeof(sm.w), "partial tile fits the weight ring");
+  float* red = reinterpret_cast<float*>(sm.w);
+  __syncthreads();  // every warp is done with the ring
+#pragma unroll
+  for (int nt = 0; nt < MT; ++nt)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) red[(wrow + hf * 8) * LD + nt * 8 + 2 * q + e] = acc[nt][hf * 2 + e];
+  cluster_sync();
+  const int rows_per = ROWS / P.ksplit;
+  const uint32_t red_s = static_cast<uint32_t>(__cvta_generic_to_shared(red));
+  for (int i = tid; i < rows_per * MT * 8; i += THREADS) {
+    const int row = split * rows_per + i / (MT * 8), t = i % (MT * 8);
+    const uint32_t off = static_cast<uint32_t>((row * LD + t) * 4);
+    float v = 0.f;
+    for (int r2 = 0; r2 < P.ksplit; ++r2) v += ld_dsmem_f32(red_s + off, r2);
+    const int f = n0 + row;
+    if (f < P.n && t < P.m) store_y(P, static_cast<int64_t>(t) * ldy + static_cast<int64_t>(g) * P.n + f, v);
+  }
+  cluster_sync();  // peers keep their partials until every CTA has read them
+}
+
+}  // namespace sk
+
+// y = sum over the k splits of the partials, in split order (deterministic), converted to y's dtype
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(Params P) {
+  const int64_t total = P.m * static_cast<int64_t>(P.groups) * P.n;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x) * 2;
+  if (i >= total) return;
+  float2 a = *reinterpret_cast<const float2*>(P.part + i);
+  for (int s = 1; s < P.ksplit; ++s) {
+    const float2 b = *reinterpret_cast<const float2*>(P.part + static_cast<int64_t>(s) * total + i);
+    a.x += b.x;
+    a.y += b.y;
+  }
+  if (P.y_dtype == DSV4_BF16)
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(P.y) + i) = pack_bf16x2(a.x, a.y);
+  else
+    *reinterpret_cast<float2*>(reinterpret_cast<float*>(P.y) + i) = a;
+}
+
+// k splits for a call whose output tiles alone leave the GPU idle (decode batches: small m, with
+// n in the hundreds or thousands and k in the thousands): about two CTAs per SM, two k tiles each
+// at least
+// at least, and partials of at most half the weight bytes (w_bytes: 1 for int8, 2 for bf16)
+inline int choose_ksplit(int64_t m, int n, int k, int groups, int w_bytes) {
+  const int64_t tiles = ((n + BN - 1) / BN) * ((m + BM - 1) / BM) * static_cast<int64_t>(groups);
+  const int KT = k / BK;
+  const int64_t want = 2 * static_cast<int64_t>(num_sms());
+  if (tiles >= want || KT < 4) return 1;
+  int64_t sp = (want + tiles - 1) / tiles;
+  sp = std::min<int64_t>(sp, KT / 2);
+  sp = std::min<int64_t>(sp, (static_cast<int64_t>(k) * w_bytes) / (8 * std::max<int64_t>(m, 1)));
+  sp = std::min<int64_t>(sp, 64);
+  if (sp <= 1) return 1;
+  const int per = (KT + static_cast<int>(sp) - 1) / static_cast<int>(sp);
+  return (KT + per - 1) / per;  // no split without k tiles
+}
+
+// token tiles of the decode-shaped kernel: m <= 8 * MT, MT in {1, 2, 4, 8}
+constexpr int SKINNY_MAX_M = 64;
+
+struct Plan {
+  bool skinny;
+  int mt;      // 8-token tiles (skinny kernel)
+  int ksplit;  // CTAs along k
+};
+
+// the decode-shaped kernel splits k over a thread-block cluster (partials summed through distributed
+// shared memory) only when its 128-row tiles leave SMs idle: about two CTAs per SM, a power of two
+// up to 8 CTAs, two k groups per CTA at least
+constexpr int MAX_CLUSTER = 8;
+inline int skinny_ksplit(int n, int k, int groups) {
+  const int64_t tiles = ((n + sk::ROWS - 1) / sk::ROWS) * static_cast<int64_t>(groups);
+  const int KT = k / BK;
+  const int64_t sms = num_sms();
+  if (tiles >= sms || KT < 4) return 1;
+  const int64_t want = std::min<int64_t>((2 * sms + tiles - 1) / tiles, KT / 2);
+  int sp = 1;
+  while (sp * 2 <= want && sp * 2 <= MAX_CLUSTER) sp *= 2;
+  return sp;
+}
+
+inline Plan plan(int64_t m, int n, int k, int groups, bool i8) {
+  Plan pl;
+  const int wb = i8 ? 1 : 2;
+  pl.skinny = m <= SKINNY_MAX_M;
+  pl.mt = m <= 8 ? 1 : m <= 16 ? 2 : m <= 32 ? 4 : 8;
+  pl.ksplit = pl.skinny ? skinny_ksplit(n, k, groups) : choose_ksplit(m, n, k, groups, wb);
+  return pl;
+}
+
 }  // namespace gm
 }  // namespace dsv4
 
 using namespace dsv4;
+
+template <bool I8, int MT>
+static int launch_skinny_mt(const gm::Params& P, void* stream) {
+  static bool set = false;
+  const int smem = sizeof(gm::sk::Smem<I8, MT>);
+  if (!set) {
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(gm::sk::skinny_kernel<I8, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((P.n + gm::sk::ROWS - 1) / gm::sk::ROWS, 1, P.groups * P.ksplit);
+  cfg.blockDim = dim3(gm::sk::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;  // the CTAs of one output tile's k split
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = P.ksplit;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  DSV4_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gm::sk::skinny_kernel<I8, MT>, P));
+  DSV4_LAUNCH_CHECK("skinny_kernel");
+  return DSV4_OK;
+}
+
+template <bool I8>
+static int launch_skinny(const gm::Params& P, int mt, void* stream) {
+  switch (mt) {
+    case 1: return launch_skinny_mt<I8, 1>(P, stream);
+    case 2: return launch_skinny_mt<I8, 2>(P, stream);
+    case 4: return launch_skinny_mt<I8, 4>(P, stream);
+    default: return launch_skinny_mt<I8, 8>(P, stream);
+  }
+}
+
+template <bool I8>
+static int launch_tiled(const gm::Params& P, void* stream) {
+  const int64_t mt = (P.m + gm::BM - 1) / gm::BM;
+  DSV4_CHECK_ARG(mt <= 65535, "dsv4_linear: m too large");
+  static bool set = false;
+  const int smem = sizeof(gm::Smem<I8>);
+  if (!set) {
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(gm::gemm_kernel<I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set = true;
+  }
+  dim3 grid((P.n + gm::BN - 1) / gm::BN, static_cast<unsigned>(mt), P.groups * P.ksplit);
+  gm::gemm_kernel<I8><<<grid, gm::THREADS, smem, as_stream(stream)>>>(P);
+  DSV4_LAUNCH_CHECK("gemm_kernel");
+  return DSV4_OK;
+}
+
+extern "C" size_t dsv4_linear_workspace_size(const dsv4_linear_params* p) {
+  if (!p || p->m <= 0 || p->n <= 0 || p->k <= 0 || p->groups < 1) return 0;
+  const gm::Plan pl = gm::plan(p->m, p->n, p->k, p->groups, p->w_dtype == DSV4_I8);
+  const int sp = pl.ksplit;
+  if (pl.skinny || sp <= 1) return 0;  // the decode-shaped kernel reduces inside its cluster
+  return static_cast<size_t>(sp) * static_cast<size_t>(p->m) * static_cast<size_t>(p->groups) *
+         static_cast<size_t>(p->n) * sizeof(float);
+}
 
 extern "C" int dsv4_linear(const dsv4_linear_params* p, void* stream) {
   DSV4_CHECK_ARG(p && p->x && p->w && p->y, "dsv4_linear: NULL tensor");
@@ -261,26 +667,35 @@ extern "C" int dsv4_linear(const dsv4_linear_params* p, void* stream) {
   P.k = p->k;
   P.groups = p->groups;
   P.y_dtype = p->y_dtype;
-  const int64_t mt = (p->m + gm::BM - 1) / gm::BM;
-  DSV4_CHECK_ARG(mt <= 65535 && p->groups <= 65535, "dsv4_linear: m too large");
-  dim3 grid((p->n + gm::BN - 1) / gm::BN, static_cast<unsigned>(mt), p->groups);
-  if (i8) {
-    static bool set = false;
-    const int smem = sizeof(gm::Smem<true>);
-    if (!set) {
-      DSV4_CUDA_CHECK(cudaFuncSetAttribute(gm::gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      set = true;
+  const gm::Plan pl = gm::plan(p->m, p->n, p->k, p->groups, i8);
+  P.ksplit = pl.skinny ? pl.ksplit : 1;
+  P.part = nullptr;
+  if (!pl.skinny && (p->workspace_bytes > 0 || p->workspace)) {
+    const size_t need = dsv4_linear_workspace_size(p);
+    if (p->workspace_bytes < need || (need > 0 && p->workspace == nullptr)) {
+      set_error("dsv4_linear: workspace of %zu bytes needed, %zu given", need, p->workspace_bytes);
+      return DSV4_ERR_WORKSPACE;
     }
-    gm::gemm_kernel<true><<<grid, gm::THREADS, smem, as_stream(stream)>>>(P);
-  } else {
-    static bool set = false;
-    const int smem = sizeof(gm::Smem<false>);
-    if (!set) {
-      DSV4_CUDA_CHECK(cudaFuncSetAttribute(gm::gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      set = true;
+    if (need > 0) {
+      DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(p->workspace) % 16 == 0, "dsv4_linear: workspace not 16-byte aligned");
+      P.ksplit = pl.ksplit;
+      P.part = reinterpret_cast<float*>(p->workspace);
     }
-    gm::gemm_kernel<false><<<grid, gm::THREADS, smem, as_stream(stream)>>>(P);
   }
-  DSV4_LAUNCH_CHECK("gemm_kernel");
+  DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(p->x) % 16 == 0 && reinterpret_cast<uintptr_t>(p->w) % 16 == 0,
+                 "dsv4_linear: x and W must be 16-byte aligned");
+  DSV4_CHECK_ARG(static_cast<int64_t>(p->groups) * P.ksplit <= 65535, "dsv4_linear: too many groups");
+  int rc;
+  if (pl.skinny)
+    rc = i8 ? launch_skinny<true>(P, pl.mt, stream) : launch_skinny<false>(P, pl.mt, stream);
+  else
+    rc = i8 ? launch_tiled<true>(P, stream) : launch_tiled<false>(P, stream);
+  if (rc != DSV4_OK) return rc;
+  if (!pl.skinny && P.ksplit > 1) {
+    const int64_t pairs = (P.m * static_cast<int64_t>(P.groups) * P.n) / 2;
+    const int64_t blocks = (pairs + 255) / 256;
+    gm::splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(P);
+    DSV4_LAUNCH_CHECK("splitk_reduce_kernel");
+  }
   return DSV4_OK;
 }

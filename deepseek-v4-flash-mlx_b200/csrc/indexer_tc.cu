@@ -477,12 +477,243 @@ __global__ void __launch_bounds__(RT_THREADS) approx_score_row_kernel(ApproxArgs
   if (warp == 0) tmem_dealloc<64>(tmem);
 }
 
+// ---- decode batches, pipelined: a persistent CTA per SM walks a contiguous run of (query, key
+// tile) items. The query (64 heads x 128) is scaled and split once per query it meets; each 128-key
+// tile arrives as one 64 KB bulk copy of the stored fp32 rows (two tiles in flight), is scaled and
+// split by its threads (thread = key, reading its row's 16-byte chunks in an order rotated by the
+// row so that the eight threads of a shared-memory phase hit distinct banks), then 24 MMAs
+// (M = 128 keys, N = 64 heads) and the fold as in approx_score_row_kernel. About 225 KB of shared
+// memory: one CTA per SM.
+constexpr int SQ_THREADS = 128;
+constexpr int RAW_TILE = BM * DI * 4;  // 64 KB
+
+struct SeqSmem {
+  alignas(1024) uint8_t raw[2][RAW_TILE];
+  alignas(1024) uint8_t kh[2 * RSLAB_K];
+  alignas(1024) uint8_t kl[2 * RSLAB_K];
+  alignas(1024) uint8_t qh[2 * RSLAB_Q];
+  alignas(1024) uint8_t ql[2 * RSLAB_Q];
+  float w[HI];
+  uint64_t full[2], mma;
+  uint32_t tmem_base;
+};
+static_assert(sizeof(SeqSmem) + 1024 <= 232448, "shared memory above the 227 KB a CTA may opt into");
+
+// scale and split query `row` into the Q slabs (warp w: heads w, w+4, ..; lane = float4 of a head)
+__device__ __forceinline__ void split_query(const ApproxArgs& P, int64_t row, uint8_t* qh, uint8_t* ql, float* w) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NW = SQ_THREADS / 32, QH = HI / NW;
+  float4 qv[QH];
+#pragma unroll
+  for (int k = 0; k < QH; ++k)
+    qv[k] = __ldg(reinterpret_cast<const float4*>(P.q + (row * HI + warp + k * NW) * DI) + lane);
+#pragma unroll
+  for (int k = 0; k < QH; ++k) {
+    const int h = warp + k * NW;
+    float mx = amax4(qv[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int sh = row_shift(mx);
+    uint2 hi, lo;
+    split4(scale4(qv[k], pow2(sh)), &hi, &lo);
+    const uint32_t off = static_cast<uint32_t>((lane >> 4) * RSLAB_Q + h * 128 + ((((lane >> 1) & 7) ^ (h & 7)) << 4) +
+                                               (lane & 1) * 8);
+    *reinterpret_cast<uint2*>(qh + off) = hi;
+    *reinterpret_cast<uint2*>(ql + off) = lo;
+    if (lane == 0) w[h] = P.w[row * HI + h] * pow2(-sh);
+  }
+}
+
+struct SeqWalk {  // the CTA's items [begin, end): item = query row * tiles + key tile
+  int64_t end;
+  int tiles;
+  __device__ __forceinline__ int64_t next_valid(const ApproxArgs& P, int64_t i) const {
+    for (; i < end; ++i) {
+      const int64_t row = i / tiles;
+      const int t = static_cast<int>(i % tiles);
+      if (t * BM < visible(P, row)) return i;
+    }
+    return end;
+  }
+};
+
+__device__ __forceinline__ void seq_issue(const ApproxArgs& P, SeqSmem& sm, int slot, int64_t item, int tiles) {
+  const int64_t row = item / tiles;
+  const int t = static_cast<int>(item % tiles);
+  const int b = static_cast<int>(row / P.s);
+  const int rows = min(BM, P.n_keys - t * BM);
+  const uint32_t bytes = static_cast<uint32_t>(rows) * DI * 4;
+  bar_expect_tx(&sm.full[slot], bytes);
+  bulk_g2s(sm.raw[slot], P.k + (static_cast<int64_t>(b) * P.k_batch_stride + static_cast<int64_t>(t) * BM) * DI, bytes,
+           &sm.full[slot]);
+}
+
+__global__ void __launch_bounds__(SQ_THREADS) approx_score_seq_kernel(ApproxArgs P, int64_t per) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  SeqSmem& sm = *reinterpret_cast<SeqSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tiles = key_tiles(P.n_keys);
+  const int64_t items = static_cast<int64_t>(P.batch) * P.s * tiles;
+  const int64_t begin = static_cast<int64_t>(blockIdx.x) * per;
+  SeqWalk walk{begin + per < items ? begin + per : items, tiles};
+  if (warp == 0) tmem_alloc<64>(&sm.tmem_base);
+  if (tid == 0) {
+    bar_init(&sm.full[0], 1);
+    bar_init(&sm.full[1], 1);
+    bar_init(&sm.mma, 1);
+    bar_init_fence();
+  }
+  before_sync();
+  __syncthreads();
+  after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  // producer cursor (thread 0): the next valid item to copy; copies issued / consumed
+  int64_t pnext = 0;
+  int issued = 0;
+  if (tid == 0) {
+    pnext = walk.next_valid(P, begin);
+    for (int k = 0; k < 2 && pnext < walk.end; ++k) {
+      seq_issue(P, sm, k, pnext, tiles);
+      ++issued;
+      pnext = walk.next_valid(P, pnext + 1);
+    }
+  }
+  int64_t cur_row = -1;
+  int k = 0;
+  bool ok = true, mma_pending = false;
+  for (int64_t i = walk.next_valid(P, begin); i < walk.end; i = walk.next_valid(P, i + 1), ++k) {
+    const int64_t row = i / tiles;
+    const int t = static_cast<int>(i % tiles);
+    const int b = static_cast<int>(row / P.s);
+    const int slot = k & 1;
+    if (row != cur_row) {  // the previous item's MMAs are done (waited below): the Q slabs are free
+      split_query(P, row, sm.qh, sm.ql, sm.w);
+      cur_row = row;
+    }
+    ok = __syncthreads_and(bar_wait(&sm.full[slot], (k >> 1) & 1));
+    if (!ok) break;
+    // the key tile: thread = key row r, 16-byte chunk c = (f + r) % 32 at step f
+    const int r = tid;
+    const int j = t * BM + r;
+    const bool valid = j < P.n_keys;
+    const uint32_t rowaddr = smem_u32(sm.raw[slot]) + static_cast<uint32_t>(r) * (DI * 4);
+    float4 v[DI / 4];
+#pragma unroll
+    for (int f = 0; f < DI / 4; ++f) {
+      const uint32_t c = static_cast<uint32_t>((f + r) & 31);
+      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                   : "=f"(v[f].x), "=f"(v[f].y), "=f"(v[f].z), "=f"(v[f].w)
+                   : "r"(rowaddr + c * 16));
+    }
+    float ss = 0.f, mx = 0.f;
+#pragma unroll
+    for (int f = 0; f < DI / 4; ++f) {
+      ss = fmaf(v[f].x, v[f].x, ss);
+      ss = fmaf(v[f].y, v[f].y, ss);
+      ss = fmaf(v[f].z, v[f].z, ss);
+      ss = fmaf(v[f].w, v[f].w, ss);
+      mx = fmaxf(mx, amax4(v[f]));
+    }
+    const int sh = valid ? row_shift(mx) : 0;
+    const float up = pow2(sh), kinv = pow2(-sh);
+#pragma unroll
+    for (int f = 0; f < DI / 4; ++f) {
+      const int c = (f + r) & 31;
+      uint2 hi, lo;
+      split4(scale4(v[f], up), &hi, &lo);
+      const uint32_t off = static_cast<uint32_t>((c >> 4) * RSLAB_K + r * 128 + ((((c >> 1) & 7) ^ (r & 7)) << 4) +
+                                                 (c & 1) * 8);
+      *reinterpret_cast<uint2*>(sm.kh + off) = hi;
+      *reinterpret_cast<uint2*>(sm.kl + off) = lo;
+    }
+    cta_atomic_max(valid ? sqrtf(ss) : 0.f, P.kmax + b);  // includes a barrier: raw[slot] is consumed
+    fence_async_smem();
+    before_sync();
+    __syncthreads();
+    after_sync();
+    if (tid == 0) {
+      if (pnext < walk.end) {  // refill the slot just consumed
+        seq_issue(P, sm, slot, pnext, tiles);
+        ++issued;
+        pnext = walk.next_valid(P, pnext + 1);
+      }
+      constexpr uint32_t id = idesc_f16<128, HI>(false, false);
+      const uint32_t qh = smem_u32(sm.qh), ql = smem_u32(sm.ql), kh = smem_u32(sm.kh), kl = smem_u32(sm.kl);
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma16(tmem, sdesc(kl + g * RSLAB_K + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id,
+                (g | kk) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma16(tmem, sdesc(kh + g * RSLAB_K + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma16(tmem, sdesc(kh + g * RSLAB_K + kk * 32, 16, 1024), sdesc(ql + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
+      }
+      mma_commit(&sm.mma);
+    }
+    ok = __syncthreads_and(bar_wait(&sm.mma, k & 1));
+    if (!ok) {
+      mma_pending = true;
+      ++k;  // this item's copy has landed
+      break;
+    }
+    after_sync();
+    float sc[HI];
+    const uint32_t lq = static_cast<uint32_t>(warp * 32) << 16;
+#pragma unroll
+    for (int c = 0; c < HI; c += 16) tmem_ld16(tmem + lq + c, sc + c);
+    tmem_wait_ld();
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int h = 0; h < HI; h += 4) {
+      const float4 wv = *reinterpret_cast<const float4*>(&sm.w[h]);
+      a0 = fmaf(wv.x, fmaxf(sc[h], 0.f), a0);
+      a1 = fmaf(wv.y, fmaxf(sc[h + 1], 0.f), a1);
+      a2 = fmaf(wv.z, fmaxf(sc[h + 2], 0.f), a2);
+      a3 = fmaf(wv.w, fmaxf(sc[h + 3], 0.f), a3);
+    }
+    if (valid) P.scores[row * P.n_pad + j] = ((a0 + a1) + (a2 + a3)) * kinv;
+    before_sync();
+    __syncthreads();  // TMEM read and the K slabs free before the next item's MMAs
+    after_sync();
+  }
+  if (!ok) {
+    if (tid == 0) {
+      raise_device_error(DSV4_ERR_WAIT_TIMEOUT);
+      // let the copies still in flight land before the CTA's shared memory goes away (bounded)
+      for (int kk = k; kk < issued; ++kk) bar_wait(&sm.full[kk & 1], (kk >> 1) & 1);
+      if (mma_pending) bar_wait(&sm.mma, (k - 1) & 1);
+    }
+  }
+  before_sync();
+  __syncthreads();
+  after_sync();
+  if (warp == 0) tmem_dealloc<64>(tmem);
+}
+
 DSV4_ERROR_READER(indexer_tc)
 
 cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaMemsetAsync(a.kmax, 0, sizeof(float) * a.batch, stream);
   if (e != cudaSuccess) return e;
   if (row_kernel(a.s)) {
+    const int64_t items = static_cast<int64_t>(a.batch) * a.s * key_tiles(a.n_keys);
+    if (items >= 2 * static_cast<int64_t>(num_sms())) {  // at least two items per CTA: the pipelined walk
+      const int smem = static_cast<int>(sizeof(SeqSmem)) + 1024;
+      static bool sattr = false;
+      if (!sattr) {
+        e = cudaFuncSetAttribute(approx_score_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        sattr = true;
+      }
+      const int64_t ctas = num_sms();
+      const int64_t per = (items + ctas - 1) / ctas;
+      approx_score_seq_kernel<<<static_cast<unsigned>((items + per - 1) / per), SQ_THREADS, smem, stream>>>(a, per);
+      return cudaGetLastError();
+    }
     const int smem = static_cast<int>(sizeof(RowSmem)) + 1024;
     static bool rattr = false;
     if (!rattr) {

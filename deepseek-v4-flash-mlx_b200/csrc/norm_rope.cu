@@ -8,6 +8,60 @@
 namespace dsv4 {
 namespace nr {
 
+// four consecutive elements as fp32 (16-byte fp32 or 8-byte bf16 access)
+__device__ __forceinline__ float4 load4(const void* p, int64_t i, int dtype) {
+  if (dtype == DSV4_BF16) {
+    const uint2 r = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p) + i);
+    return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u), __uint_as_float(r.y << 16),
+                       __uint_as_float(r.y & 0xFFFF0000u));
+  }
+  return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+}
+__device__ __forceinline__ void store4(void* p, int64_t i, int dtype, float4 v) {
+  if (dtype == DSV4_BF16)
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p) + i) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  else
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i) = v;
+}
+
+// RMSNorm for few rows (decode batches): one CTA per row, the row in registers (VPT groups of 4
+// elements per thread), one block reduction; the CTAs of a handful of rows still fill the GPU's
+// memory pipes, where one warp per row would serialise the row's loads on a few SMs
+template <int VPT>
+__global__ void __launch_bounds__(256) rmsnorm_row_kernel(dsv4_rmsnorm_params p) {
+  __shared__ float part[8];
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * p.dim;
+  float4 v[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = (j * nt + tid) * 4;
+    v[j] = i < p.dim ? load4(p.x, base + i, p.x_dtype) : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss = fmaf(v[j].x, v[j].x, ss);
+    ss = fmaf(v[j].y, v[j].y, ss);
+    ss = fmaf(v[j].z, v[j].z, ss);
+    ss = fmaf(v[j].w, v[j].w, ss);
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) part[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < (nt >> 5); ++w) tot += part[w];
+  const float r = rsqrtf(tot / static_cast<float>(p.dim) + p.eps);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = (j * nt + tid) * 4;
+    if (i >= p.dim) continue;
+    float4 o = make_float4(v[j].x * r, v[j].y * r, v[j].z * r, v[j].w * r);
+    if (p.weight) {
+      const float4 w = load4(p.weight, i, p.w_dtype);
+      o = make_float4(w.x * o.x, w.y * o.y, w.z * o.z, w.w * o.w);
+    }
+    store4(p.out, base + i, p.out_dtype, o);
+  }
+}
+
 // generic RMSNorm, any dim (multiple of 2), one warp per row, two passes over L1-resident data
 __global__ void rmsnorm_kernel(dsv4_rmsnorm_params p) {
   const int lane = threadIdx.x & 31;
@@ -159,6 +213,23 @@ extern "C" int dsv4_rmsnorm(const dsv4_rmsnorm_params* p, void* stream) {
                        (p->weight == nullptr || is_float_dtype(p->w_dtype)),
                    "dsv4_rmsnorm: F32/BF16 only");
   if (p->rows == 0) return DSV4_OK;
+  const auto al = [](const void* q, int dt) { return reinterpret_cast<uintptr_t>(q) % (dt == DSV4_BF16 ? 8 : 16) == 0; };
+  if (p->rows <= 4 * num_sms() && p->dim % 4 == 0 && p->dim >= 128 && p->dim <= 8192 && al(p->x, p->x_dtype) &&
+      al(p->out, p->out_dtype) && (p->weight == nullptr || al(p->weight, p->w_dtype))) {
+    const int threads = p->dim >= 1024 ? 256 : 128;
+    const int vpt = (p->dim / 4 + threads - 1) / threads;  // <= 8
+    const dim3 grid(static_cast<unsigned>(p->rows));
+    if (vpt <= 1)
+      nr::rmsnorm_row_kernel<1><<<grid, threads, 0, as_stream(stream)>>>(*p);
+    else if (vpt <= 2)
+      nr::rmsnorm_row_kernel<2><<<grid, threads, 0, as_stream(stream)>>>(*p);
+    else if (vpt <= 4)
+      nr::rmsnorm_row_kernel<4><<<grid, threads, 0, as_stream(stream)>>>(*p);
+    else
+      nr::rmsnorm_row_kernel<8><<<grid, threads, 0, as_stream(stream)>>>(*p);
+    DSV4_LAUNCH_CHECK("rmsnorm_row_kernel");
+    return DSV4_OK;
+  }
   const int warps = 8;
   int64_t blocks = (p->rows + warps - 1) / warps;
   nr::rmsnorm_kernel<<<static_cast<unsigned>(blocks), warps * 32, 0, as_stream(stream)>>>(*p);

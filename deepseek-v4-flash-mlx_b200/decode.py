@@ -19,6 +19,7 @@ through the block table), sparse attention — whose window tiles, computed from
 while the selection finishes — with the inverse RoPE fused into its epilogue, and the split-K merge;
 q's per-head norm + RoPE runs on a side stream beside the indexer.
 """
+import ctypes
 import math
 
 import torch
@@ -69,6 +70,23 @@ class SparseMLACache:
 
     def fill_window(self, b, positions, rows_bf16):
         self.kv_pool[self.window_rows(b, positions)] = rows_bf16.to(torch.bfloat16)
+
+
+def decode_rows(cache, positions):
+    """Pool rows of one decode step, one launch (dsv4_decode_rows): (win_rows, comp_rows, key_rows),
+    int64 [b] each — this token's window slot, the compressed row the step emits (when
+    (p+1) % ratio == 0) and its indexer key row in k_idx viewed as [batch*max_comp, 128]."""
+    L.require_cuda(positions)
+    b = positions.shape[0]
+    pos = positions.to(torch.int32).contiguous()
+    out = torch.empty((3, b), dtype=torch.int64, device=positions.device)
+    p = L.DecodeRowsParams()
+    p.positions, p.win_base, p.block_table = L.ptr(pos), L.ptr(cache.win_base), L.ptr(cache.block_table)
+    p.win_rows, p.comp_rows, p.key_rows = L.ptr(out[0]), L.ptr(out[1]), L.ptr(out[2])
+    p.comp_base, p.b, p.window, p.ratio, p.page = cache.comp_base, b, cache.window, cache.ratio, cache.page
+    p.bt_stride, p.max_comp = cache.block_table.shape[1], cache.max_comp
+    L.check(L.lib().dsv4_decode_rows(ctypes.byref(p), L.stream_of(positions)))
+    return out[0], out[1], out[2]
 
 
 def attention_index_buffer(batch, window, top_k, device):

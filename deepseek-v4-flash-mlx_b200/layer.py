@@ -22,7 +22,7 @@ import torch
 from . import _lib as L
 from .compressor import compressor_decode_step, compressor_prefill
 from .configs import DIMS, LayerDims
-from .decode import SparseMLACache, decode_attention
+from .decode import SparseMLACache, decode_attention, decode_rows
 from .indexer import indexer_topk_into
 from .mla import QuantWeight, linear, o_grouped, quantize_int8_g64
 from .norm_rope import norm_rope, rmsnorm, rope, rope_freqs
@@ -144,20 +144,17 @@ class DecodeBlock:
         d, W, c = self.dims, self.W, self.cache
         b = x.shape[0]
         pos = positions.to(torch.int32).contiguous()
-        xn = rmsnorm(x, W.attn_norm)
-        qa = rmsnorm(linear(xn, W.wq_a, torch.float32), W.q_a_norm)
+        # the normed activations feed only bf16 projections: rounded to bf16 once, by the norm
+        xn = rmsnorm(x, W.attn_norm, out_dtype=torch.bfloat16)
+        qa = rmsnorm(linear(xn, W.wq_a, torch.float32), W.q_a_norm, out_dtype=torch.bfloat16)
         qraw = linear(qa, W.wq_b, torch.float32).view(b, d.n_heads, d.head_dim)
-        # this token's kv row -> its window ring slot
-        win_rows = (c.win_base + pos.long() % d.window).contiguous()
+        # this token's window slot, and where the compressors emit (when (p+1) % ratio == 0)
+        win_rows, comp_rows, key_rows = decode_rows(c, pos)
         kvp = linear(xn, W.wkv, torch.float32)
         _norm_rope_into(kvp, W.kv_a_norm, pos, self.freqs, c.kv_pool, win_rows, d.rope_dim)
-        # compressor rings: a compressed row / an indexer key is emitted when (p+1) % ratio == 0
-        entry = torch.clamp((pos.long() + 1) // d.ratio - 1, min=0)
-        comp_rows = c.comp_base + c.block_table.long()[self._seq[:b], entry // c.page] * c.page + entry % c.page
         compressor_decode_step(xn, W.c_wkv, W.c_wgate, W.c_ape, W.c_norm, c.ring_kv, c.ring_score, pos, c.kv_pool,
-                               comp_rows.contiguous(), head_dim=d.head_dim, ratio=d.ratio,
+                               comp_rows, head_dim=d.head_dim, ratio=d.ratio,
                                rope_head_dim=d.rope_dim, freqs=self.freqs)
-        key_rows = (self._seq[:b] * c.max_comp + entry).contiguous()
         compressor_decode_step(xn, W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, c.ring_k_idx, c.ring_s_idx, pos,
                                c.k_idx.view(-1, d.idx_dim), key_rows, head_dim=d.idx_dim, ratio=d.ratio,
                                rope_head_dim=d.rope_dim, freqs=self.freqs)

@@ -61,6 +61,9 @@ def _linear_op(x: torch.Tensor, w: torch.Tensor, w_scale: torch.Tensor | None, g
     p.w_scale = L.ptr(w_scale) if w_scale is not None else None
     p.m, p.n, p.k, p.groups, p.group = m, n, k, groups, 64
     p.x_dtype, p.w_dtype, p.y_dtype = L.BF16, L.dtype_code(w), L.dtype_code(y)
+    nbytes = L.lib().dsv4_linear_workspace_size(ctypes.byref(p))
+    ws = L.workspace(nbytes, x.device)
+    p.workspace, p.workspace_bytes = L.ptr(ws), nbytes
     L.check(L.lib().dsv4_linear(ctypes.byref(p), L.stream_of(x)))
     return y
 

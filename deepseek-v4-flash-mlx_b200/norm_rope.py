@@ -63,15 +63,16 @@ def rope_freqs(rope_dim=64, device="cuda", **yarn):
 # ---- custom ops ---------------------------------------------------------------------------------
 
 @torch.library.custom_op("dsv4::rmsnorm", mutates_args=(), device_types="cuda")
-def _rmsnorm_op(x: torch.Tensor, weight: torch.Tensor | None, eps: float) -> torch.Tensor:
+def _rmsnorm_op(x: torch.Tensor, weight: torch.Tensor | None, eps: float,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
     x = x.contiguous()
-    out = torch.empty_like(x)
+    out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
     p = L.RmsNormParams()
     p.x, p.out = L.ptr(x), L.ptr(out)
     p.weight = L.ptr(weight.contiguous()) if weight is not None else None
     p.rows = x.numel() // x.shape[-1] if x.numel() else 0
     p.dim = x.shape[-1]
-    p.x_dtype = p.out_dtype = L.dtype_code(x)
+    p.x_dtype, p.out_dtype = L.dtype_code(x), L.dtype_code(out)
     p.w_dtype = L.dtype_code(weight) if weight is not None else L.F32
     p.eps = eps
     L.check(L.lib().dsv4_rmsnorm(ctypes.byref(p), L.stream_of(x)))
@@ -79,16 +80,17 @@ def _rmsnorm_op(x: torch.Tensor, weight: torch.Tensor | None, eps: float) -> tor
 
 
 @_rmsnorm_op.register_fake
-def _(x, weight, eps):
-    return torch.empty_like(x)
+def _(x, weight, eps, out_dtype=None):
+    return torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
 
 
-def rmsnorm(x, weight, eps=1e-6):
-    """RMSNorm.forward (ref_torch/norm_rope.py:10-16): fp32 math, result in x.dtype."""
+def rmsnorm(x, weight, eps=1e-6, out_dtype=None):
+    """RMSNorm.forward (ref_torch/norm_rope.py:10-16): fp32 math, result in x.dtype (or out_dtype:
+    one rounding of the fp32 result, the operand a bf16 projection consumes)."""
     L.require_cuda(x, weight)
     if weight is not None and weight.dtype not in (torch.float32, torch.bfloat16):
         weight = weight.float()
-    return _rmsnorm_op(x, weight, float(eps))
+    return _rmsnorm_op(x, weight, float(eps), out_dtype)
 
 
 def perhead_norm(q, eps=1e-6):
@@ -107,7 +109,7 @@ def _rope_cis_op(x: torch.Tensor, cis: torch.Tensor, inverse: bool) -> torch.Ten
     p = L.RopeParams()
     p.x, p.out = L.ptr(x), L.ptr(out)
     p.s, p.heads, p.dim, p.rope_dim = rows, heads, x.shape[-1], x.shape[-1]
-    p.x_dtype = p.out_dtype = L.dtype_code(x)
+    p.x_dtype, p.out_dtype = L.dtype_code(x), L.dtype_code(out)
     p.cis, p.cis_rows = L.ptr(table), table.shape[0]
     p.freqs, p.positions, p.pos_offset, p.inverse = None, None, 0, int(inverse)
     L.check(L.lib().dsv4_rope(ctypes.byref(p), L.stream_of(x)))
@@ -140,7 +142,7 @@ def _rope_pos_op(x: torch.Tensor, freqs: torch.Tensor, positions: torch.Tensor, 
     p = L.RopeParams()
     p.x, p.out = L.ptr(x), L.ptr(out)
     p.s, p.heads, p.dim, p.rope_dim = rows, heads, x.shape[-1], rope_dim
-    p.x_dtype = p.out_dtype = L.dtype_code(x)
+    p.x_dtype, p.out_dtype = L.dtype_code(x), L.dtype_code(out)
     p.cis, p.cis_rows = None, 0
     p.freqs, p.positions = L.ptr(freqs), L.ptr(positions)
     p.pos_offset, p.inverse = 0, int(inverse)

@@ -277,6 +277,27 @@ typedef struct {
 } dsv4_compressor_decode_params;
 DSV4_API int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream);
 
+/* ---- decode-step row bookkeeping of the device-resident state (pool of bf16 rows: per-sequence
+ * window rings at win_base[i], then pages of compressed rows from comp_base through block_table;
+ * indexer keys [b, max_comp, 128]). For sequence i at position p = positions[i]:
+ *   win_rows[i]  = win_base[i] + p % window                      (this token's window slot)
+ *   entry        = max((p + 1) / ratio - 1, 0)                   (compressed entry the step emits)
+ *   comp_rows[i] = comp_base + block_table[i*bt_stride + entry/page]*page + entry % page
+ *   key_rows[i]  = i * max_comp + entry
+ * An entry >= max_comp raises DSV4_ERR_INDEX_OUT_OF_RANGE on the device error word (clamped).
+ * Replaces the host-side ring and kvbuf bookkeeping of oracle/v4_fast.py:93-118. */
+typedef struct {
+  const int32_t* positions;   /* [b] */
+  const int64_t* win_base;    /* [b] */
+  const int32_t* block_table; /* [b, bt_stride] */
+  int64_t* win_rows;          /* [b] out */
+  int64_t* comp_rows;         /* [b] out */
+  int64_t* key_rows;          /* [b] out */
+  int64_t comp_base;
+  int32_t b, window, ratio, page, bt_stride, max_comp;
+} dsv4_decode_rows_params;
+DSV4_API int dsv4_decode_rows(const dsv4_decode_rows_params* p, void* stream);
+
 /* ---- a6: projections. y[m, n] = sum_k x[m, k] * W[n, k] (W row-major [n, k] as the reference)
  * W is BF16, or I8 with BF16 scales per (row, group of `group` k). x BF16 or F32, y F32 or BF16.
  * `groups` > 1 runs a grouped projection: x viewed as [m, groups, k], W as [groups, n, k], y as
@@ -289,7 +310,15 @@ typedef struct {
   int64_t m;
   int32_t n, k, groups, group;
   int32_t x_dtype, w_dtype, y_dtype;
+  /* m <= 64 (decode batches) runs a weight-streaming kernel; when its output tiles leave SMs
+   * idle it splits k over a thread-block cluster and sums the partials in shared memory, no
+   * workspace. Larger m with few output tiles and a long k splits k across CTAs and sums fp32
+   * partials from this workspace (dsv4_linear_workspace_size bytes); NULL with 0 bytes runs it
+   * without the split. Both sums run in a fixed order: results are deterministic. */
+  void* workspace;
+  size_t workspace_bytes;
 } dsv4_linear_params;
+DSV4_API size_t dsv4_linear_workspace_size(const dsv4_linear_params* p);
 DSV4_API int dsv4_linear(const dsv4_linear_params* p, void* stream);
 
 /* ---- casts used by the op layer (fp32 <-> bf16) ---- */

@@ -21,6 +21,7 @@ PAIRS = {
     "dsv4_compressor_params": L.CompressorParams,
     "dsv4_compressor_decode_params": L.CompressorDecodeParams,
     "dsv4_linear_params": L.LinearParams,
+    "dsv4_decode_rows_params": L.DecodeRowsParams,
 }
 
 

@@ -91,3 +91,28 @@ def test_decode_runner_graph_and_host_path(dsv4):
     out = r.step_host(h["q"], h["q_idx"], h["w_idx"], h["positions"])
     r.synchronize()
     torch.testing.assert_close(out, ref.cpu(), rtol=0, atol=0)
+
+
+def test_decode_rows_bookkeeping(dsv4):
+    """One launch computes this step's window slot, compressed row and indexer key row for every
+    sequence, as the cache's own host-side formulas; an entry past the cache raises the device
+    error word and is clamped."""
+    D = importlib.import_module("deepseek-v4-flash-mlx_b200.decode")
+    L = importlib.import_module("deepseek-v4-flash-mlx_b200._lib")
+    g = torch.Generator().manual_seed(9)
+    b, max_comp = 6, 700
+    perm = torch.randperm(6 * 11, generator=g)
+    cache = D.SparseMLACache(b, max_comp, page=64, page_order=perm)
+    pos = torch.tensor([0, 1, 2, 3, 4 * max_comp - 1, 1234], dtype=torch.int32)
+    L.device_error()
+    win, comp, key = (t.cpu() for t in D.decode_rows(cache, pos.cuda()))
+    assert L.device_error() == 0
+    entry = torch.clamp((pos.long() + 1) // 4 - 1, min=0)
+    bt = cache.block_table.cpu().long()
+    seq = torch.arange(b)
+    assert torch.equal(win, cache.win_base.cpu() + pos.long() % cache.window)
+    assert torch.equal(comp, cache.comp_base + bt[seq, entry // 64] * 64 + entry % 64)
+    assert torch.equal(key, seq * max_comp + entry)
+    over = torch.tensor([4 * max_comp + 3], dtype=torch.int32)     # entry max_comp: outside the cache
+    D.decode_rows(D.SparseMLACache(1, max_comp), over.cuda())
+    assert L.device_error() == 4

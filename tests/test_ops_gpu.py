@@ -1,4 +1,7 @@
 """Each dsv4 op on the GPU against the CPU oracle (same seeded inputs)."""
+import ctypes
+import importlib
+
 import numpy as np
 import pytest
 import torch
@@ -121,6 +124,23 @@ def test_rmsnorm_and_perhead(dsv4):
     assert rel_rms(out, NR.rmsnorm(xb, w)) < 8e-3
     q = torch.randn(5, 64, 512, generator=g)
     assert rel_rms(dsv4.perhead_norm(q.to(DEV)), NR.perhead_norm(q)) < 1e-6
+
+
+@pytest.mark.parametrize("rows,dim,out_dtype", [(32, 4096, torch.bfloat16), (32, 1024, torch.float32),
+                                                 (3, 4100, torch.float32), (7, 130, torch.bfloat16),
+                                                 (1000, 512, torch.float32), (1, 8192, torch.bfloat16)])
+def test_rmsnorm_row_shapes(dsv4, rows, dim, out_dtype):
+    """Decode-sized batches (one CTA per row, the row in registers) and the one-warp-per-row form
+    (many rows, or a dim that is not a multiple of 4), fp32 input with a bf16 or fp32 result."""
+    g = torch.Generator().manual_seed(rows + dim)
+    x = torch.randn(rows, dim, generator=g) * 2
+    w = torch.randn(dim, generator=g)
+    out = dsv4.rmsnorm(x.to(DEV), w.to(DEV), out_dtype=out_dtype)
+    assert out.dtype == out_dtype
+    ref = NR.rmsnorm(x, w)
+    assert rel_rms(out.float(), ref) < (4e-3 if out_dtype == torch.bfloat16 else 1e-6)
+    if out_dtype == torch.bfloat16:   # one rounding of the fp32 result
+        assert torch.equal(out.cpu(), dsv4.rmsnorm(x.to(DEV), w.to(DEV)).cpu().bfloat16())
 
 
 def test_apply_rotary_emb_table_form(dsv4, golden):
@@ -246,6 +266,44 @@ def test_linear_int8_g64(dsv4):
     qd = type(qw)(qw.q.to(DEV), qw.scale.to(DEV))
     out = dsv4.linear(x.to(DEV).bfloat16(), qd)
     assert rel_rms(out, ref) < 1e-5
+
+
+@pytest.mark.parametrize("m,n,k,groups,quant,split", [
+    (32, 1024, 4096, 1, True, True),      # wq_a at batch 32: 8 output tiles, k split
+    (5, 512, 4096, 1, False, True),       # ragged m, bf16 weights
+    (32, 256, 1600, 4, True, True),       # grouped, k tiles not a multiple of the split
+    (1, 64, 4096, 1, True, True),         # one output tile (the indexer head weights)
+    (40, 19200, 128, 1, True, False),     # 64-token tiles, enough output tiles: no split
+    (12, 19200, 256, 1, False, False),    # 16-token tiles, bf16
+    (100, 256, 4096, 1, False, True),     # the tiled kernel (m > 64) with k split
+])
+def test_linear_split_k_decode_shapes(dsv4, m, n, k, groups, quant, split):
+    """Decode-shaped projections (the weight-streaming kernel for m <= 64), with k split across
+    CTAs and a fixed-order fp32 sum of the partials where the output tiles alone leave SMs idle
+    (`split`): close to the fp64 product and bit-identical from call to call."""
+    L = importlib.import_module("deepseek-v4-flash-mlx_b200._lib")
+    p = L.LinearParams()
+    p.m, p.n, p.k, p.groups, p.w_dtype = m, n, k, groups, L.I8 if quant else L.BF16
+    # m <= 64 sums its k split inside a thread-block cluster (no workspace); the tiled kernel
+    # writes fp32 partials to the workspace
+    assert (L.lib().dsv4_linear_workspace_size(ctypes.byref(p)) > 0) == (split and m > 64)
+    g = torch.Generator().manual_seed(m + n + k)
+    x = _bf16(torch.randn(m, groups * k, generator=g))
+    w = torch.randn(groups * n, k, generator=g) * 0.02
+    if quant:
+        qw = dsv4.quantize_int8_g64(w)
+        wd = M.dequant_int8_g64(qw.q, qw.scale)
+        wdev = type(qw)(qw.q.to(DEV), qw.scale.to(DEV))
+    else:
+        wd = _bf16(w)
+        wdev = wd.to(DEV).bfloat16()
+    ref = torch.einsum("mgk,gnk->mgn", x.double().view(m, groups, k), wd.double().view(groups, n, k)).reshape(m, -1)
+    out = dsv4.linear(x.to(DEV).bfloat16(), wdev, groups=groups)
+    assert rel_rms(out, ref.float()) < 1e-5
+    again = dsv4.linear(x.to(DEV).bfloat16(), wdev, groups=groups)
+    assert torch.equal(out, again)
+    outb = dsv4.linear(x.to(DEV).bfloat16(), wdev, torch.bfloat16, groups=groups)
+    assert rel_rms(outb.float(), ref.float()) < 4e-3
 
 
 # ---------------------------------------------------------------- compressor
