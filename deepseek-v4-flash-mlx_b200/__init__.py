@@ -18,7 +18,7 @@ from .decode import DecodeRunner, SparseMLACache, decode_attention
 from .indexer import indexer_scores, indexer_topk, indexer_topk_into
 from .layer import AttentionWeights, DecodeBlock, make_attention_weights, prefill_layer
 from .prefill import CompressorWeights, ShardedPrefill, sparse_mla_prefill
-from .mla import (N_GROUPS, N_HEADS, HEAD_DIM, O_LORA, ROPE_HD, QuantWeight, kv_proj, linear, o_grouped,
+from .mla import (N_GROUPS, N_HEADS, HEAD_DIM, O_LORA, ROPE_HD, QuantWeight, kv_proj, linear, linear_multi, o_grouped,
                   q_down, q_up, quantize_int8_g64)
 from .norm_rope import (apply_rotary_emb, norm_rope, perhead_norm, precompute_freqs, precompute_freqs_cis,
                         rmsnorm, rope, rope_freqs)
@@ -27,7 +27,7 @@ from .sparse_attn import get_window_topk_idxs, sparse_attn, sparse_attn_rope
 __all__ = [
     "sparse_attn", "sparse_attn_rope", "get_window_topk_idxs", "compressor_prefill", "compressor_decode_step",
     "rmsnorm", "perhead_norm", "apply_rotary_emb", "precompute_freqs", "precompute_freqs_cis", "norm_rope",
-    "rope", "rope_freqs", "indexer_topk", "indexer_scores", "indexer_topk_into", "linear", "q_down", "q_up",
+    "rope", "rope_freqs", "indexer_topk", "indexer_scores", "indexer_topk_into", "linear", "linear_multi", "q_down", "q_up",
     "kv_proj", "o_grouped", "QuantWeight", "quantize_int8_g64", "SparseMLACache", "decode_attention", "DecodeRunner",
     "AttentionWeights", "DecodeBlock", "make_attention_weights", "prefill_layer", "CompressorWeights", "ShardedPrefill",
     "sparse_mla_prefill",

@@ -79,6 +79,18 @@ class LinearParams(ctypes.Structure):
                 ("workspace", vp), ("workspace_bytes", sz)]
 
 
+LINEAR_MULTI_MAX = 8
+
+
+class LinearOut(ctypes.Structure):
+    _fields_ = [("w", vp), ("w_scale", vp), ("y", vp), ("n", i32), ("y_dtype", i32)]
+
+
+class LinearMultiParams(ctypes.Structure):
+    _fields_ = [("x", vp), ("m", i64), ("k", i32), ("group", i32), ("x_dtype", i32), ("w_dtype", i32),
+                ("count", i32), ("outs", LinearOut * LINEAR_MULTI_MAX)]
+
+
 class DecodeRowsParams(ctypes.Structure):
     _fields_ = [("positions", vp), ("win_base", vp), ("block_table", vp), ("win_rows", vp), ("comp_rows", vp),
                 ("key_rows", vp), ("comp_base", i64), ("b", i32), ("window", i32), ("ratio", i32), ("page", i32),
@@ -107,6 +119,7 @@ SIGNATURES = {
     "dsv4_decode_rows": (ctypes.c_int, [ctypes.POINTER(DecodeRowsParams), vp]),
     "dsv4_linear_workspace_size": (sz, [ctypes.POINTER(LinearParams)]),
     "dsv4_linear": (ctypes.c_int, [ctypes.POINTER(LinearParams), vp]),
+    "dsv4_linear_multi": (ctypes.c_int, [ctypes.POINTER(LinearMultiParams), vp]),
     "dsv4_cast": (ctypes.c_int, [vp, i32, vp, i32, i64, vp]),
 }
 

@@ -163,6 +163,108 @@ __global__ void ring_seed_kernel(dsv4_compressor_params p) {
 
 // one decode token per sequence: ring row R + p%R <- (kv, score + ape[p%R]); when (p+1)%R == 0
 // emit the pooled row at position p+1-R and shift rows [R,2R) to [0,R).
+// ratio 4 (the model's): the same step with every thread owning column pairs (c, c+1) of both
+// halves. The ring rows it reads were written by earlier steps and the current token's row stays
+// in registers, so all of a thread's loads go out at once and the only barrier is the norm's
+// reduction (the generic kernel below re-reads the ring it just wrote, behind a barrier, with
+// runtime-sized loops). Same operations in the same order: identical results.
+__device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ void st2(float* p, float2 v) { *reinterpret_cast<float2*>(p) = v; }
+
+template <int NP>
+__global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_decode_params p) {
+  constexpr int R = 4;
+  __shared__ float red[33];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int d = p.head_dim, d2 = 2 * d;
+  const int pos = p.positions[b];
+  const int slot = R + pos % R;
+  float* rk = p.ring_kv + static_cast<int64_t>(b) * 2 * R * d2;
+  float* rs = p.ring_score + static_cast<int64_t>(b) * 2 * R * d2;
+  const float* kin = p.kv + static_cast<int64_t>(b) * d2;
+  const float* sin_ = p.score + static_cast<int64_t>(b) * d2;
+  const float* ape = p.ape + (pos % R) * d2;
+  const bool emit = (pos + 1) % R == 0;
+  float2 nk[NP][2], ns[NP][2];  // this token's kv and score + ape, columns c and d + c
+  float2 K[NP][8], S[NP][8], F[NP][3], G[NP][3];  // pooled inputs; rows 4..6 of the first half (shift)
+#pragma unroll
+  for (int np = 0; np < NP; ++np) {
+    const int c = 2 * (tid + np * THREADS);
+    if (c >= d) continue;
+    nk[np][0] = ld2(kin + c);
+    nk[np][1] = ld2(kin + d + c);
+    const float2 s0 = ld2(sin_ + c), s1 = ld2(sin_ + d + c), a0 = ld2(ape + c), a1 = ld2(ape + d + c);
+    ns[np][0] = make_float2(s0.x + a0.x, s0.y + a0.y);
+    ns[np][1] = make_float2(s1.x + a1.x, s1.y + a1.y);
+    if (emit) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        K[np][r] = ld2(rk + r * d2 + c);
+        S[np][r] = ld2(rs + r * d2 + c);
+      }
+#pragma unroll
+      for (int r = 0; r < R - 1; ++r) {
+        K[np][R + r] = ld2(rk + (R + r) * d2 + d + c);
+        S[np][R + r] = ld2(rs + (R + r) * d2 + d + c);
+        F[np][r] = ld2(rk + (R + r) * d2 + c);
+        G[np][r] = ld2(rs + (R + r) * d2 + c);
+      }
+      K[np][2 * R - 1] = nk[np][1];  // row 2R - 1 is this token's slot
+      S[np][2 * R - 1] = ns[np][1];
+    }
+    // the slot is written in every case (after an emission the ring holds what the generic kernel
+    // leaves: this token's row both in its slot and, shifted, in row R - 1)
+    st2(rk + slot * d2 + c, nk[np][0]);
+    st2(rk + slot * d2 + d + c, nk[np][1]);
+    st2(rs + slot * d2 + c, ns[np][0]);
+    st2(rs + slot * d2 + d + c, ns[np][1]);
+  }
+  if (!emit) return;  // uniform over the CTA
+  float vals[NP][2];
+  float ss = 0.f;
+#pragma unroll
+  for (int np = 0; np < NP; ++np) {
+    const int c = 2 * (tid + np * THREADS);
+    if (c >= d) continue;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float m = e ? S[np][0].y : S[np][0].x;
+#pragma unroll
+      for (int i = 1; i < 2 * R; ++i) m = fmaxf(m, e ? S[np][i].y : S[np][i].x);
+      float den = 0.f, num = 0.f;
+#pragma unroll
+      for (int i = 0; i < 2 * R; ++i) {
+        const float ex = expf((e ? S[np][i].y : S[np][i].x) - m);
+        den += ex;
+        num = fmaf(ex, e ? K[np][i].y : K[np][i].x, num);
+      }
+      vals[np][e] = num / den;
+      ss = fmaf(vals[np][e], vals[np][e], ss);
+    }
+  }
+  ss = block_sum(ss, red);
+  const float rinv = rsqrtf(ss / static_cast<float>(d) + p.eps);
+#pragma unroll
+  for (int np = 0; np < NP; ++np) {
+    const int c = 2 * (tid + np * THREADS);
+    if (c >= d) continue;
+    finish_pair(vals[np][0], vals[np][1], c, d, p.rope_dim, p.norm_w, p.norm_dtype, rinv, p.freqs, pos + 1 - R,
+                p.out, p.out_rows[b], p.out_dtype);
+    // the block's rows become the previous block (rows 0..R-1); this token's row is the last
+#pragma unroll
+    for (int r = 0; r < R - 1; ++r) {
+      st2(rk + r * d2 + c, F[np][r]);
+      st2(rs + r * d2 + c, G[np][r]);
+      st2(rk + r * d2 + d + c, K[np][R + r]);
+      st2(rs + r * d2 + d + c, S[np][R + r]);
+    }
+    st2(rk + (R - 1) * d2 + c, nk[np][0]);
+    st2(rs + (R - 1) * d2 + c, ns[np][0]);
+    st2(rk + (R - 1) * d2 + d + c, nk[np][1]);
+    st2(rs + (R - 1) * d2 + d + c, ns[np][1]);
+  }
+}
+
 __global__ void __launch_bounds__(THREADS) decode_kernel(dsv4_compressor_decode_params p) {
   __shared__ float red[33];
   const int b = blockIdx.x;
@@ -256,7 +358,12 @@ extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, vo
                      p->head_dim <= 4 * cmp::THREADS && p->rope_dim % 2 == 0 && p->rope_dim <= p->head_dim,
                  "dsv4_compressor_decode: bad sizes");
   DSV4_CHECK_DTYPE(p->out_dtype == DSV4_F32 || p->out_dtype == DSV4_BF16, "dsv4_compressor_decode: out dtype");
-  cmp::decode_kernel<<<p->b, cmp::THREADS, 0, as_stream(stream)>>>(*p);
+  if (p->ratio == 4 && p->head_dim <= 2 * cmp::THREADS)
+    cmp::decode_r4_kernel<1><<<p->b, cmp::THREADS, 0, as_stream(stream)>>>(*p);
+  else if (p->ratio == 4)
+    cmp::decode_r4_kernel<2><<<p->b, cmp::THREADS, 0, as_stream(stream)>>>(*p);
+  else
+    cmp::decode_kernel<<<p->b, cmp::THREADS, 0, as_stream(stream)>>>(*p);
   DSV4_LAUNCH_CHECK("compressor decode_kernel");
   return DSV4_OK;
 }

@@ -28,6 +28,15 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
+// d = A.B (no accumulator input)
+__device__ __forceinline__ void mma_bf16_z(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
+}
 __device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
@@ -46,6 +55,16 @@ struct Params {
   int y_dtype;
   int ksplit;               // CTAs along k; > 1: fp32 partials [ksplit][m][groups*n] into part
   float* part;
+  // nprob > 0 (decode-shaped kernel, groups == 1): several projections of the same x in one launch;
+  // projection p owns the 128-row tiles [tile0, tile0 + ceil(n / 128)) of grid.x, and w, ws, y, n,
+  // y_dtype above are replaced by its own
+  int nprob;
+  struct Prob {
+    const void* w;
+    const __nv_bfloat16* ws;
+    void* y;
+    int n, y_dtype, tile0;
+  } prob[DSV4_LINEAR_MULTI_MAX];
 };
 
 template <bool I8>
@@ -342,13 +361,24 @@ __device__ __forceinline__ float load_scale(const Params& P, int n0, int kg, int
 }
 
 template <bool I8, int MT>
-__global__ void __launch_bounds__(THREADS) skinny_kernel(Params P) {
+__global__ void __launch_bounds__(THREADS) skinny_kernel(const __grid_constant__ Params P0) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem<I8, MT>& sm = *reinterpret_cast<Smem<I8, MT>*>(smem_raw);
   constexpr int NST = Cfg<I8>::NST;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r = lane >> 2, q = lane & 3;
-  const int n0 = blockIdx.x * ROWS;
+  Params P = P0;
+  int n0 = blockIdx.x * ROWS;
+  if (P0.nprob > 0) {
+    int pi = 0;
+    while (pi + 1 < P0.nprob && static_cast<int>(blockIdx.x) >= P0.prob[pi + 1].tile0) ++pi;
+    P.w = P0.prob[pi].w;
+    P.ws = P0.prob[pi].ws;
+    P.y = P0.prob[pi].y;
+    P.n = P0.prob[pi].n;
+    P.y_dtype = P0.prob[pi].y_dtype;
+    n0 = (static_cast<int>(blockIdx.x) - P0.prob[pi].tile0) * ROWS;
+  }
   const int g = blockIdx.z / P.ksplit;
   const int split = blockIdx.z % P.ksplit;
   const int KT = P.k / BK;
@@ -364,13 +394,16 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(Params P) {
 
   // the weights and their scales do not depend on the kernel before this one: their first stages
   // load while it finishes (programmatic dependent launch); the tokens load after pdl_wait()
+  float sc0[NST - 1];  // the prologue's scales: all loads in flight at once
 #pragma unroll
-  for (int s = 0; s < NST - 1; ++s) {
-    if (s < nkt) {
-      load_w<I8, MT>(P, sm, s, n0, kt0 + s, g);
-      if constexpr (I8)
-        if (tid < ROWS) sm.scale[s][tid] = load_scale<I8, MT>(P, n0, kt0 + s, g);
-    }
+  for (int s = 0; s < NST - 1; ++s) sc0[s] = (I8 && s < nkt) ? load_scale<I8, MT>(P, n0, kt0 + s, g) : 0.f;
+#pragma unroll
+  for (int s = 0; s < NST - 1; ++s)
+    if (s < nkt) load_w<I8, MT>(P, sm, s, n0, kt0 + s, g);
+  if constexpr (I8) {
+#pragma unroll
+    for (int s = 0; s < NST - 1; ++s)
+      if (s < nkt && tid < ROWS) sm.scale[s][tid] = sc0[s];
   }
   pdl_wait();
 #pragma unroll
@@ -380,6 +413,10 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(Params P) {
   }
 
   const int wrow = warp * 16 + r;  // this lane's weight rows: wrow, wrow + 8
+  // a stage's scale is loaded with its tiles (NST - 1 steps ahead) but parked in shared memory two
+  // steps later, so that no step waits on the load: sc_1, sc_2 are the loads of the last two steps
+  float sc_1 = 0.f, sc_2 = 0.f;
+  static_assert(!I8 || NST >= 4, "the delayed scale store needs four stages");
   for (int it = 0; it < nkt; ++it) {
     const int st = it % NST;
     asm volatile("cp.async.wait_group %0;\n" ::"n"(NST - 2));
@@ -419,12 +456,6 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(Params P) {
       xw[nt][0] = a.x; xw[nt][1] = a.y; xw[nt][2] = a.z; xw[nt][3] = a.w;
       xw[nt][4] = b.x; xw[nt][5] = b.y; xw[nt][6] = b.z; xw[nt][7] = b.w;
     }
-    if constexpr (I8) {
-#pragma unroll
-      for (int a = 0; a < MT; ++a)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) gacc[a][c] = 0.f;
-    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint32_t af[4];
@@ -441,9 +472,12 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(Params P) {
       }
 #pragma unroll
       for (int nt = 0; nt < MT; ++nt) {
-        if constexpr (I8)
-          mma_bf16(gacc[nt], af, xw[nt][2 * j], xw[nt][2 * j + 1]);
-        else
+        if constexpr (I8) {
+          if (j == 0)  // the group's first k step starts its partial from zero
+            mma_bf16_z(gacc[nt], af, xw[nt][0], xw[nt][1]);
+          else
+            mma_bf16(gacc[nt], af, xw[nt][2 * j], xw[nt][2 * j + 1]);
+        } else
           mma_bf16(acc[nt], af, xw[nt][2 * j], xw[nt][2 * j + 1]);
       }
     }
@@ -456,8 +490,11 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(Params P) {
         acc[nt][2] = fmaf(gacc[nt][2], s1, acc[nt][2]);
         acc[nt][3] = fmaf(gacc[nt][3], s1, acc[nt][3]);
       }
-      // the slot refilled this iteration was last read in the previous one (before the barrier)
-      if (nk < nkt && tid < ROWS) sm.scale[nk % NST][tid] = sc_next;
+      // the scale loaded two steps ago, for stage it + NST - 3 (read at step it + NST - 3 >= it + 1,
+      // after the next barrier; its slot was last read at step it - 3)
+      if (it >= 2 && it + NST - 3 < nkt && tid < ROWS) sm.scale[(it + NST - 3) % NST][tid] = sc_2;
+      sc_2 = sc_1;
+      sc_1 = sc_next;
     }
   }
   asm volatile("cp.async.wait_group 0;\n" ::);
@@ -558,8 +595,7 @@ struct Plan {
 // shared memory) only when its 128-row tiles leave SMs idle: about two CTAs per SM, a power of two
 // up to 8 CTAs, two k groups per CTA at least
 constexpr int MAX_CLUSTER = 8;
-inline int skinny_ksplit(int n, int k, int groups) {
-  const int64_t tiles = ((n + sk::ROWS - 1) / sk::ROWS) * static_cast<int64_t>(groups);
+inline int skinny_ksplit_tiles(int64_t tiles, int k) {
   const int KT = k / BK;
   const int64_t sms = num_sms();
   if (tiles >= sms || KT < 4) return 1;
@@ -567,6 +603,9 @@ inline int skinny_ksplit(int n, int k, int groups) {
   int sp = 1;
   while (sp * 2 <= want && sp * 2 <= MAX_CLUSTER) sp *= 2;
   return sp;
+}
+inline int skinny_ksplit(int n, int k, int groups) {
+  return skinny_ksplit_tiles(((n + sk::ROWS - 1) / sk::ROWS) * static_cast<int64_t>(groups), k);
 }
 
 inline Plan plan(int64_t m, int n, int k, int groups, bool i8) {
@@ -592,7 +631,9 @@ static int launch_skinny_mt(const gm::Params& P, void* stream) {
     set = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((P.n + gm::sk::ROWS - 1) / gm::sk::ROWS, 1, P.groups * P.ksplit);
+  const int tiles = P.nprob > 0 ? P.prob[P.nprob - 1].tile0 + (P.prob[P.nprob - 1].n + gm::sk::ROWS - 1) / gm::sk::ROWS
+                                : (P.n + gm::sk::ROWS - 1) / gm::sk::ROWS;
+  cfg.gridDim = dim3(tiles, 1, P.groups * P.ksplit);
   cfg.blockDim = dim3(gm::sk::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = as_stream(stream);
@@ -667,6 +708,7 @@ extern "C" int dsv4_linear(const dsv4_linear_params* p, void* stream) {
   P.k = p->k;
   P.groups = p->groups;
   P.y_dtype = p->y_dtype;
+  P.nprob = 0;
   const gm::Plan pl = gm::plan(p->m, p->n, p->k, p->groups, i8);
   P.ksplit = pl.skinny ? pl.ksplit : 1;
   P.part = nullptr;
@@ -698,4 +740,68 @@ extern "C" int dsv4_linear(const dsv4_linear_params* p, void* stream) {
     DSV4_LAUNCH_CHECK("splitk_reduce_kernel");
   }
   return DSV4_OK;
+}
+
+extern "C" int dsv4_linear_multi(const dsv4_linear_multi_params* p, void* stream) {
+  DSV4_CHECK_ARG(p && p->x && p->count >= 1 && p->count <= DSV4_LINEAR_MULTI_MAX, "dsv4_linear_multi: bad arguments");
+  DSV4_CHECK_ARG(p->m >= 0 && p->k > 0 && p->k % gm::BK == 0, "dsv4_linear_multi: k=%d must be a multiple of 64", p->k);
+  DSV4_CHECK_DTYPE(p->x_dtype == DSV4_BF16, "dsv4_linear_multi: x must be BF16");
+  DSV4_CHECK_DTYPE(p->w_dtype == DSV4_BF16 || p->w_dtype == DSV4_I8, "dsv4_linear_multi: W must be BF16 or I8");
+  const bool i8 = p->w_dtype == DSV4_I8;
+  for (int i = 0; i < p->count; ++i) {
+    const dsv4_linear_out& o = p->outs[i];
+    DSV4_CHECK_ARG(o.w && o.y && o.n > 0 && o.n % 2 == 0, "dsv4_linear_multi: output %d: bad W / y / n", i);
+    DSV4_CHECK_DTYPE(o.y_dtype == DSV4_F32 || o.y_dtype == DSV4_BF16, "dsv4_linear_multi: y must be F32 or BF16");
+    DSV4_CHECK_ARG(!i8 || (o.w_scale != nullptr && p->group == 64),
+                   "dsv4_linear_multi: int8 weights need bf16 scales with group 64");
+    DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(o.w) % 16 == 0, "dsv4_linear_multi: W must be 16-byte aligned");
+  }
+  if (p->m == 0) return DSV4_OK;
+  if (p->m > gm::SKINNY_MAX_M) {  // prefill-sized: one tiled launch per projection
+    for (int i = 0; i < p->count; ++i) {
+      dsv4_linear_params lp = {};
+      lp.x = p->x;
+      lp.w = p->outs[i].w;
+      lp.w_scale = p->outs[i].w_scale;
+      lp.y = p->outs[i].y;
+      lp.m = p->m;
+      lp.n = p->outs[i].n;
+      lp.k = p->k;
+      lp.groups = 1;
+      lp.group = p->group;
+      lp.x_dtype = p->x_dtype;
+      lp.w_dtype = p->w_dtype;
+      lp.y_dtype = p->outs[i].y_dtype;
+      const int rc = dsv4_linear(&lp, stream);
+      if (rc != DSV4_OK) return rc;
+    }
+    return DSV4_OK;
+  }
+  DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(p->x) % 16 == 0, "dsv4_linear_multi: x must be 16-byte aligned");
+  gm::Params P = {};
+  P.x = reinterpret_cast<const __nv_bfloat16*>(p->x);
+  P.m = p->m;
+  P.k = p->k;
+  P.groups = 1;
+  P.nprob = p->count;
+  int tiles = 0;
+  for (int i = 0; i < p->count; ++i) {
+    P.prob[i].w = p->outs[i].w;
+    P.prob[i].ws = reinterpret_cast<const __nv_bfloat16*>(p->outs[i].w_scale);
+    P.prob[i].y = p->outs[i].y;
+    P.prob[i].n = p->outs[i].n;
+    P.prob[i].y_dtype = p->outs[i].y_dtype;
+    P.prob[i].tile0 = tiles;
+    tiles += (p->outs[i].n + gm::sk::ROWS - 1) / gm::sk::ROWS;
+  }
+  // the first projection's fields stand in until the kernel resolves its own
+  P.w = P.prob[0].w;
+  P.ws = P.prob[0].ws;
+  P.y = P.prob[0].y;
+  P.n = P.prob[0].n;
+  P.y_dtype = P.prob[0].y_dtype;
+  P.ksplit = gm::skinny_ksplit_tiles(tiles, p->k);
+  P.part = nullptr;
+  const int mt = p->m <= 8 ? 1 : p->m <= 16 ? 2 : p->m <= 32 ? 4 : 8;
+  return i8 ? launch_skinny<true>(P, mt, stream) : launch_skinny<false>(P, mt, stream);
 }

@@ -479,27 +479,32 @@ __global__ void __launch_bounds__(RT_THREADS) approx_score_row_kernel(ApproxArgs
 
 // ---- decode batches, pipelined: a persistent CTA per SM walks a contiguous run of (query, key
 // tile) items. The query (64 heads x 128) is scaled and split once per query it meets; each 128-key
-// tile arrives as one 64 KB bulk copy of the stored fp32 rows (two tiles in flight), is scaled and
-// split by its threads (thread = key, reading its row's 16-byte chunks in an order rotated by the
-// row so that the eight threads of a shared-memory phase hit distinct banks), then 24 MMAs
-// (M = 128 keys, N = 64 heads) and the fold as in approx_score_row_kernel. About 225 KB of shared
-// memory: one CTA per SM.
-constexpr int SQ_THREADS = 128;
+// tile arrives as one 64 KB bulk copy of the stored fp32 rows (two tiles in flight) and is scaled
+// and split by four threads per key (a quarter of its dims each; the 16-byte chunks are visited in
+// an order rotated by key and quarter so that the eight threads of a shared-memory phase hit
+// distinct banks), then 24 MMAs (M = 128 keys, N = 64 heads) and the fold as in
+// approx_score_row_kernel, by warps 0-3 (one TMEM lane quadrant each) while the other warps
+// already split the next tile. About 226 KB of shared memory: one CTA per SM.
+constexpr int SQ_THREADS = 512;
 constexpr int RAW_TILE = BM * DI * 4;  // 64 KB
 
-struct SeqSmem {
+struct SeqSmem {  // dynamic shared memory (1024-byte aligned slabs)
   alignas(1024) uint8_t raw[2][RAW_TILE];
   alignas(1024) uint8_t kh[2 * RSLAB_K];
   alignas(1024) uint8_t kl[2 * RSLAB_K];
   alignas(1024) uint8_t qh[2 * RSLAB_Q];
   alignas(1024) uint8_t ql[2 * RSLAB_Q];
+};
+struct SeqSmall {  // static shared memory
   float w[HI];
+  float kinv[2][BM];
   uint64_t full[2], mma;
   uint32_t tmem_base;
 };
-static_assert(sizeof(SeqSmem) + 1024 <= 232448, "shared memory above the 227 KB a CTA may opt into");
+static_assert(sizeof(SeqSmem) + 1024 + sizeof(SeqSmall) + 256 <= 232448,
+              "shared memory above the 227 KB a CTA may opt into");
 
-// scale and split query `row` into the Q slabs (warp w: heads w, w+4, ..; lane = float4 of a head)
+// scale and split query `row` into the Q slabs (warp w: heads w, w + NW, ..; lane = float4 of a head)
 __device__ __forceinline__ void split_query(const ApproxArgs& P, int64_t row, uint8_t* qh, uint8_t* ql, float* w) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int NW = SQ_THREADS / 32, QH = HI / NW;
@@ -527,115 +532,133 @@ __device__ __forceinline__ void split_query(const ApproxArgs& P, int64_t row, ui
 struct SeqWalk {  // the CTA's items [begin, end): item = query row * tiles + key tile
   int64_t end;
   int tiles;
-  __device__ __forceinline__ int64_t next_valid(const ApproxArgs& P, int64_t i) const {
+  int64_t vrow = -1;  // the last query row whose visible count was read (one global load per row)
+  int vis = 0;
+  __device__ __forceinline__ int64_t next_valid(const ApproxArgs& P, int64_t i) {
     for (; i < end; ++i) {
       const int64_t row = i / tiles;
       const int t = static_cast<int>(i % tiles);
-      if (t * BM < visible(P, row)) return i;
+      if (row != vrow) {
+        vrow = row;
+        vis = visible(P, row);
+      }
+      if (t * BM < vis) return i;
+      i = (row + 1) * tiles - 1;  // the rest of this row's tiles are not visible either
     }
     return end;
   }
 };
 
-__device__ __forceinline__ void seq_issue(const ApproxArgs& P, SeqSmem& sm, int slot, int64_t item, int tiles) {
+__device__ __forceinline__ void seq_issue(const ApproxArgs& P, SeqSmem& sm, SeqSmall& ss, int slot, int64_t item,
+                                          int tiles) {
   const int64_t row = item / tiles;
   const int t = static_cast<int>(item % tiles);
   const int b = static_cast<int>(row / P.s);
   const int rows = min(BM, P.n_keys - t * BM);
   const uint32_t bytes = static_cast<uint32_t>(rows) * DI * 4;
-  bar_expect_tx(&sm.full[slot], bytes);
+  bar_expect_tx(&ss.full[slot], bytes);
   bulk_g2s(sm.raw[slot], P.k + (static_cast<int64_t>(b) * P.k_batch_stride + static_cast<int64_t>(t) * BM) * DI, bytes,
-           &sm.full[slot]);
+           &ss.full[slot]);
 }
 
 __global__ void __launch_bounds__(SQ_THREADS) approx_score_seq_kernel(ApproxArgs P, int64_t per) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SeqSmem& sm = *reinterpret_cast<SeqSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
-  const int tid = threadIdx.x, warp = tid >> 5;
+  __shared__ SeqSmall sx;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tiles = key_tiles(P.n_keys);
   const int64_t items = static_cast<int64_t>(P.batch) * P.s * tiles;
   const int64_t begin = static_cast<int64_t>(blockIdx.x) * per;
   SeqWalk walk{begin + per < items ? begin + per : items, tiles};
-  if (warp == 0) tmem_alloc<64>(&sm.tmem_base);
+  SeqWalk pwalk = walk;  // the producer's own cursor state
+  if (warp == 0) tmem_alloc<64>(&sx.tmem_base);
   if (tid == 0) {
-    bar_init(&sm.full[0], 1);
-    bar_init(&sm.full[1], 1);
-    bar_init(&sm.mma, 1);
+    bar_init(&sx.full[0], 1);
+    bar_init(&sx.full[1], 1);
+    bar_init(&sx.mma, 1);
     bar_init_fence();
   }
   before_sync();
   __syncthreads();
   after_sync();
-  const uint32_t tmem = sm.tmem_base;
-  // producer cursor (thread 0): the next valid item to copy; copies issued / consumed
+  const uint32_t tmem = sx.tmem_base;
+  // producer cursor (thread 0): the next valid item to copy; copies issued
   int64_t pnext = 0;
   int issued = 0;
   if (tid == 0) {
-    pnext = walk.next_valid(P, begin);
+    pnext = pwalk.next_valid(P, begin);
     for (int k = 0; k < 2 && pnext < walk.end; ++k) {
-      seq_issue(P, sm, k, pnext, tiles);
+      seq_issue(P, sm, sx, k, pnext, tiles);
       ++issued;
-      pnext = walk.next_valid(P, pnext + 1);
+      pnext = pwalk.next_valid(P, pnext + 1);
     }
   }
+  const int kr = tid >> 2, part = tid & 3;  // splitting: key row, quarter of its 128 dims
   int64_t cur_row = -1;
   int k = 0;
   bool ok = true, mma_pending = false;
-  for (int64_t i = walk.next_valid(P, begin); i < walk.end; i = walk.next_valid(P, i + 1), ++k) {
+  for (int64_t i = walk.next_valid(P, begin); i < walk.end; ++k) {
     const int64_t row = i / tiles;
     const int t = static_cast<int>(i % tiles);
     const int b = static_cast<int>(row / P.s);
     const int slot = k & 1;
-    if (row != cur_row) {  // the previous item's MMAs are done (waited below): the Q slabs are free
-      split_query(P, row, sm.qh, sm.ql, sm.w);
+    if (row != cur_row) {
+      // every thread is past the previous item's epilogue (it reads sx.w) and its MMAs are done
+      __syncthreads();
+      split_query(P, row, sm.qh, sm.ql, sx.w);
       cur_row = row;
     }
-    ok = __syncthreads_and(bar_wait(&sm.full[slot], (k >> 1) & 1));
+    ok = __syncthreads_and(bar_wait(&sx.full[slot], (k >> 1) & 1));
     if (!ok) break;
-    // the key tile: thread = key row r, 16-byte chunk c = (f + r) % 32 at step f
-    const int r = tid;
-    const int j = t * BM + r;
+    // the key tile: this thread's 8 chunks c = 8 part + ((f + 2 part + kr) % 8) of key row kr
+    const int j = t * BM + kr;
     const bool valid = j < P.n_keys;
-    const uint32_t rowaddr = smem_u32(sm.raw[slot]) + static_cast<uint32_t>(r) * (DI * 4);
-    float4 v[DI / 4];
+    const uint32_t rowaddr = smem_u32(sm.raw[slot]) + static_cast<uint32_t>(kr) * (DI * 4);
+    float4 v[8];
 #pragma unroll
-    for (int f = 0; f < DI / 4; ++f) {
-      const uint32_t c = static_cast<uint32_t>((f + r) & 31);
+    for (int f = 0; f < 8; ++f) {
+      const uint32_t c = static_cast<uint32_t>(8 * part + ((f + 2 * part + kr) & 7));
       asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
                    : "=f"(v[f].x), "=f"(v[f].y), "=f"(v[f].z), "=f"(v[f].w)
                    : "r"(rowaddr + c * 16));
     }
     float ss = 0.f, mx = 0.f;
 #pragma unroll
-    for (int f = 0; f < DI / 4; ++f) {
+    for (int f = 0; f < 8; ++f) {
       ss = fmaf(v[f].x, v[f].x, ss);
       ss = fmaf(v[f].y, v[f].y, ss);
       ss = fmaf(v[f].z, v[f].z, ss);
       ss = fmaf(v[f].w, v[f].w, ss);
       mx = fmaxf(mx, amax4(v[f]));
     }
+    // the four quarters of a key are lanes 4r'..4r'+3 of one warp
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
     const int sh = valid ? row_shift(mx) : 0;
-    const float up = pow2(sh), kinv = pow2(-sh);
+    const float up = pow2(sh);
 #pragma unroll
-    for (int f = 0; f < DI / 4; ++f) {
-      const int c = (f + r) & 31;
+    for (int f = 0; f < 8; ++f) {
+      const int c = 8 * part + ((f + 2 * part + kr) & 7);
       uint2 hi, lo;
       split4(scale4(v[f], up), &hi, &lo);
-      const uint32_t off = static_cast<uint32_t>((c >> 4) * RSLAB_K + r * 128 + ((((c >> 1) & 7) ^ (r & 7)) << 4) +
+      const uint32_t off = static_cast<uint32_t>((c >> 4) * RSLAB_K + kr * 128 + ((((c >> 1) & 7) ^ (kr & 7)) << 4) +
                                                  (c & 1) * 8);
       *reinterpret_cast<uint2*>(sm.kh + off) = hi;
       *reinterpret_cast<uint2*>(sm.kl + off) = lo;
     }
-    cta_atomic_max(valid ? sqrtf(ss) : 0.f, P.kmax + b);  // includes a barrier: raw[slot] is consumed
+    if (part == 0) sx.kinv[slot][kr] = pow2(-sh);
+    cta_atomic_max((valid && part == 0) ? sqrtf(ss) : 0.f, P.kmax + b);  // its barrier: raw[slot] consumed
     fence_async_smem();
     before_sync();
     __syncthreads();
     after_sync();
     if (tid == 0) {
       if (pnext < walk.end) {  // refill the slot just consumed
-        seq_issue(P, sm, slot, pnext, tiles);
+        seq_issue(P, sm, sx, slot, pnext, tiles);
         ++issued;
-        pnext = walk.next_valid(P, pnext + 1);
+        pnext = pwalk.next_valid(P, pnext + 1);
       }
       constexpr uint32_t id = idesc_f16<128, HI>(false, false);
       const uint32_t qh = smem_u32(sm.qh), ql = smem_u32(sm.ql), kh = smem_u32(sm.kh), kl = smem_u32(sm.kl);
@@ -652,40 +675,46 @@ __global__ void __launch_bounds__(SQ_THREADS) approx_score_seq_kernel(ApproxArgs
         for (int kk = 0; kk < 4; ++kk)
           mma16(tmem, sdesc(kh + g * RSLAB_K + kk * 32, 16, 1024), sdesc(ql + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
       }
-      mma_commit(&sm.mma);
+      mma_commit(&sx.mma);
     }
-    ok = __syncthreads_and(bar_wait(&sm.mma, k & 1));
+    // every thread waits for the MMAs: then the K slabs are free for the next tile's split
+    ok = __syncthreads_and(bar_wait(&sx.mma, k & 1));
     if (!ok) {
       mma_pending = true;
       ++k;  // this item's copy has landed
       break;
     }
     after_sync();
-    float sc[HI];
-    const uint32_t lq = static_cast<uint32_t>(warp * 32) << 16;
+    if (warp < 4) {  // the fold: thread = key (TMEM lane)
+      const int key = warp * 32 + lane;
+      const uint32_t lq = static_cast<uint32_t>(warp * 32) << 16;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
-    for (int c = 0; c < HI; c += 16) tmem_ld16(tmem + lq + c, sc + c);
-    tmem_wait_ld();
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (int c = 0; c < HI; c += 16) {
+        float sc[16];
+        tmem_ld16(tmem + lq + c, sc);
+        tmem_wait_ld();
 #pragma unroll
-    for (int h = 0; h < HI; h += 4) {
-      const float4 wv = *reinterpret_cast<const float4*>(&sm.w[h]);
-      a0 = fmaf(wv.x, fmaxf(sc[h], 0.f), a0);
-      a1 = fmaf(wv.y, fmaxf(sc[h + 1], 0.f), a1);
-      a2 = fmaf(wv.z, fmaxf(sc[h + 2], 0.f), a2);
-      a3 = fmaf(wv.w, fmaxf(sc[h + 3], 0.f), a3);
+        for (int h = 0; h < 16; h += 4) {
+          const float4 wv = *reinterpret_cast<const float4*>(&sx.w[c + h]);
+          a0 = fmaf(wv.x, fmaxf(sc[h], 0.f), a0);
+          a1 = fmaf(wv.y, fmaxf(sc[h + 1], 0.f), a1);
+          a2 = fmaf(wv.z, fmaxf(sc[h + 2], 0.f), a2);
+          a3 = fmaf(wv.w, fmaxf(sc[h + 3], 0.f), a3);
+        }
+      }
+      const int jj = t * BM + key;
+      if (jj < P.n_keys) P.scores[row * P.n_pad + jj] = ((a0 + a1) + (a2 + a3)) * sx.kinv[slot][key];
+      before_sync();  // these TMEM reads precede the next item's MMAs (issued after its barrier)
     }
-    if (valid) P.scores[row * P.n_pad + j] = ((a0 + a1) + (a2 + a3)) * kinv;
-    before_sync();
-    __syncthreads();  // TMEM read and the K slabs free before the next item's MMAs
-    after_sync();
+    i = walk.next_valid(P, i + 1);
   }
   if (!ok) {
     if (tid == 0) {
       raise_device_error(DSV4_ERR_WAIT_TIMEOUT);
       // let the copies still in flight land before the CTA's shared memory goes away (bounded)
-      for (int kk = k; kk < issued; ++kk) bar_wait(&sm.full[kk & 1], (kk >> 1) & 1);
-      if (mma_pending) bar_wait(&sm.mma, (k - 1) & 1);
+      for (int kk = k; kk < issued; ++kk) bar_wait(&sx.full[kk & 1], (kk >> 1) & 1);
+      if (mma_pending) bar_wait(&sx.mma, (k - 1) & 1);
     }
   }
   before_sync();

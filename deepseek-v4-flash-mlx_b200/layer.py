@@ -24,7 +24,7 @@ from .compressor import compressor_decode_step, compressor_prefill
 from .configs import DIMS, LayerDims
 from .decode import SparseMLACache, decode_attention, decode_rows
 from .indexer import indexer_topk_into
-from .mla import QuantWeight, linear, o_grouped, quantize_int8_g64
+from .mla import QuantWeight, linear, linear_multi, o_grouped, quantize_int8_g64
 from .norm_rope import norm_rope, rmsnorm, rope, rope_freqs
 from .sparse_attn import sparse_attn_rope
 
@@ -144,22 +144,24 @@ class DecodeBlock:
         d, W, c = self.dims, self.W, self.cache
         b = x.shape[0]
         pos = positions.to(torch.int32).contiguous()
-        # the normed activations feed only bf16 projections: rounded to bf16 once, by the norm
+        # the normed activations feed only bf16 projections: rounded to bf16 once, by the norm; the
+        # seven projections of xn run as one launch, the two of qa as another
         xn = rmsnorm(x, W.attn_norm, out_dtype=torch.bfloat16)
-        qa = rmsnorm(linear(xn, W.wq_a, torch.float32), W.q_a_norm, out_dtype=torch.bfloat16)
-        qraw = linear(qa, W.wq_b, torch.float32).view(b, d.n_heads, d.head_dim)
+        qa_p, kvp, c_kv, c_sc, w_idx, i_kv, i_sc = linear_multi(
+            xn, [W.wq_a, W.wkv, W.c_wkv, W.c_wgate, W.i_wproj, W.i_wkv, W.i_wgate], torch.float32)
+        qa = rmsnorm(qa_p, W.q_a_norm, out_dtype=torch.bfloat16)
+        qraw, qi = linear_multi(qa, [W.wq_b, W.i_wq], torch.float32)
+        qraw = qraw.view(b, d.n_heads, d.head_dim)
         # this token's window slot, and where the compressors emit (when (p+1) % ratio == 0)
         win_rows, comp_rows, key_rows = decode_rows(c, pos)
-        kvp = linear(xn, W.wkv, torch.float32)
         _norm_rope_into(kvp, W.kv_a_norm, pos, self.freqs, c.kv_pool, win_rows, d.rope_dim)
         compressor_decode_step(xn, W.c_wkv, W.c_wgate, W.c_ape, W.c_norm, c.ring_kv, c.ring_score, pos, c.kv_pool,
                                comp_rows, head_dim=d.head_dim, ratio=d.ratio,
-                               rope_head_dim=d.rope_dim, freqs=self.freqs)
+                               rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(c_kv, c_sc))
         compressor_decode_step(xn, W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, c.ring_k_idx, c.ring_s_idx, pos,
                                c.k_idx.view(-1, d.idx_dim), key_rows, head_dim=d.idx_dim, ratio=d.ratio,
-                               rope_head_dim=d.rope_dim, freqs=self.freqs)
-        q_idx = rope(linear(qa, W.i_wq, torch.float32).view(b, d.idx_heads, d.idx_dim), pos, self.freqs, d.rope_dim)
-        w_idx = linear(xn, W.i_wproj, torch.float32)
+                               rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(i_kv, i_sc))
+        q_idx = rope(qi.view(b, d.idx_heads, d.idx_dim), pos, self.freqs, d.rope_dim)
         o = decode_attention(c, qraw, q_idx, w_idx, W.sinks, pos, self.top_k, freqs=self.freqs)
         return o_grouped(o.reshape(b, -1), W.wo_a, W.wo_b)
 

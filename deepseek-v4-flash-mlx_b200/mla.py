@@ -86,6 +86,46 @@ def linear(x, W, out_dtype=torch.float32, groups=1):
     return _linear_op(x, W.contiguous(), None, int(groups), out_dtype)
 
 
+@torch.library.custom_op("dsv4::linear_multi", mutates_args=(), device_types="cuda")
+def _linear_multi_op(x: torch.Tensor, ws: list[torch.Tensor], scales: list[torch.Tensor],
+                     out_dtype: torch.dtype) -> list[torch.Tensor]:
+    xb = _as_bf16(x)
+    k = ws[0].shape[1]
+    lead = x.shape[:-1]
+    m = xb.numel() // k
+    ys = [torch.empty((*lead, w.shape[0]), dtype=out_dtype, device=x.device) for w in ws]
+    p = L.LinearMultiParams()
+    p.x, p.m, p.k, p.group, p.count = L.ptr(xb), m, k, 64, len(ws)
+    p.x_dtype, p.w_dtype = L.BF16, L.dtype_code(ws[0])
+    for i, (w, y) in enumerate(zip(ws, ys)):
+        o = p.outs[i]
+        o.w, o.y, o.n, o.y_dtype = L.ptr(w), L.ptr(y), w.shape[0], L.dtype_code(y)
+        o.w_scale = L.ptr(scales[i]) if scales else None
+    L.check(L.lib().dsv4_linear_multi(ctypes.byref(p), L.stream_of(x)))
+    return ys
+
+
+@_linear_multi_op.register_fake
+def _(x, ws, scales, out_dtype):
+    return [x.new_empty((*x.shape[:-1], w.shape[0]), dtype=out_dtype) for w in ws]
+
+
+def linear_multi(x, Ws, out_dtype=torch.float32):
+    """[x @ W.T for W in Ws] in one launch (up to 8 projections of the same x, all bf16 or all
+    QuantWeight, same input width): the decode block's projections that read the same activations."""
+    if not 1 <= len(Ws) <= L.LINEAR_MULTI_MAX:
+        raise ValueError(f"linear_multi takes 1..{L.LINEAR_MULTI_MAX} weights")
+    quant = isinstance(Ws[0], QuantWeight)
+    if any(isinstance(W, QuantWeight) != quant for W in Ws):
+        raise ValueError("linear_multi: mixed weight kinds")
+    if quant:
+        L.require_cuda(x, *[W.q for W in Ws])
+        return _linear_multi_op(x, [W.q for W in Ws], [W.scale for W in Ws], out_dtype)
+    L.require_cuda(x, *Ws)
+    return _linear_multi_op(x, [(W if W.dtype == torch.bfloat16 else _as_bf16(W)).contiguous() for W in Ws], [],
+                            out_dtype)
+
+
 def q_down(x, wq_a, out_dtype=torch.float32):
     """x [..., dim] -> q_lora [..., q_lora_rank] (v4mlx/mla.py:21)."""
     return linear(x, wq_a, out_dtype)

@@ -321,6 +321,26 @@ typedef struct {
 DSV4_API size_t dsv4_linear_workspace_size(const dsv4_linear_params* p);
 DSV4_API int dsv4_linear(const dsv4_linear_params* p, void* stream);
 
+/* Several projections of the same x in one launch (the decode block's q_down, kv_proj, the two
+ * compressors' projections and the indexer head weights all read the normed hidden states): output
+ * i is y_i[m, n_i] = x[m, k] . W_i[n_i, k]^T, each W_i as in dsv4_linear (groups 1), one weight
+ * dtype for all. m <= 64 runs them as one grid of the weight-streaming kernel; larger m runs one
+ * dsv4_linear per output. Fuses the projections of v4mlx/mla.py:16-42 that share their input. */
+#define DSV4_LINEAR_MULTI_MAX 8
+typedef struct {
+  const void* w;          /* [n, k] */
+  const void* w_scale;    /* [n, k/64] BF16 when w_dtype == I8 */
+  void* y;                /* [m, n] y_dtype */
+  int32_t n, y_dtype;
+} dsv4_linear_out;
+typedef struct {
+  const void* x;          /* [m, k] BF16 */
+  int64_t m;
+  int32_t k, group, x_dtype, w_dtype, count;
+  dsv4_linear_out outs[DSV4_LINEAR_MULTI_MAX];
+} dsv4_linear_multi_params;
+DSV4_API int dsv4_linear_multi(const dsv4_linear_multi_params* p, void* stream);
+
 /* ---- casts used by the op layer (fp32 <-> bf16) ---- */
 DSV4_API int dsv4_cast(const void* x, int32_t x_dtype, void* y, int32_t y_dtype, int64_t numel, void* stream);
 

@@ -22,6 +22,8 @@ PAIRS = {
     "dsv4_compressor_decode_params": L.CompressorDecodeParams,
     "dsv4_linear_params": L.LinearParams,
     "dsv4_decode_rows_params": L.DecodeRowsParams,
+    "dsv4_linear_out": L.LinearOut,
+    "dsv4_linear_multi_params": L.LinearMultiParams,
 }
 
 

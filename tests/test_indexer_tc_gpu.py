@@ -43,6 +43,8 @@ def test_approx_scores_within_bound(dsv4, spread):
     (2, 260, 1000, 64, False),
     (1, 256, 16384, 1024, True),
     (1, 257, 777, 100, False),
+    (12, 2, 3000, 512, True),     # two queries per batch entry: the per-sequence walk, causal
+    (40, 1, 9000, 512, False),    # decode batch, a walk that crosses queries inside a CTA
 ])
 def test_mode2_selection_bit_exact(dsv4, b, s, n, k, causal):
     q, w, keys = _inputs(b, s, n, b * 31 + s + n)

@@ -306,6 +306,31 @@ def test_linear_split_k_decode_shapes(dsv4, m, n, k, groups, quant, split):
     assert rel_rms(outb.float(), ref.float()) < 4e-3
 
 
+@pytest.mark.parametrize("m,quant", [(32, True), (7, False), (64, True), (100, True)])
+def test_linear_multi_matches_separate_projections(dsv4, m, quant):
+    """Several projections of one x in one launch (ragged n, a tile shared by none): each output
+    close to the fp64 product and to its own dsv4.linear; m > 64 runs one tiled call per output."""
+    g = torch.Generator().manual_seed(m)
+    k = 1024
+    ns = [1024, 512, 64, 256, 130]
+    x = _bf16(torch.randn(m, k, generator=g))
+    Ws, ref = [], []
+    for n in ns:
+        w = torch.randn(n, k, generator=g) * 0.02
+        if quant:
+            qw = dsv4.quantize_int8_g64(w)
+            ref.append(x.double() @ M.dequant_int8_g64(qw.q, qw.scale).double().T)
+            Ws.append(type(qw)(qw.q.to(DEV), qw.scale.to(DEV)))
+        else:
+            ref.append(x.double() @ _bf16(w).double().T)
+            Ws.append(w.to(DEV).bfloat16())
+    outs = dsv4.linear_multi(x.to(DEV).bfloat16(), Ws)
+    for o, r, W in zip(outs, ref, Ws):
+        assert o.shape == r.shape
+        assert rel_rms(o, r.float()) < 1e-5
+        assert rel_rms(o, dsv4.linear(x.to(DEV).bfloat16(), W)) < 1e-6
+
+
 # ---------------------------------------------------------------- compressor
 def test_compressor_prefill_golden_inputs(dsv4, golden):
     wkv, wgate, ape, nw = (torch.from_numpy(golden[k]) for k in ("cmp_wkv", "cmp_wgate", "cmp_ape", "cmp_nw"))
@@ -320,6 +345,36 @@ def test_compressor_prefill_golden_inputs(dsv4, golden):
         assert_close_bf16(gst["score"], st["score"], 1e-4, 1e-5, what="state score")
         # and against the reference itself (fp32 operands): bf16 operand rounding only
         assert_close_bf16(out, torch.from_numpy(golden[f"cmp{s}_rows"]), what=f"cmp{s} vs ref")
+
+
+@pytest.mark.parametrize("hd,b", [(128, 3), (512, 5), (1024, 2)])
+def test_compressor_decode_state_and_rows(dsv4, hd, b):
+    """Eight decode steps of b sequences at staggered positions from a random ring: every emitted
+    row and the whole ring state after each step against the oracle's ring step."""
+    g = torch.Generator().manual_seed(hd + b)
+    d2 = 2 * hd
+    rk = torch.randn(b, 8, d2, generator=g)
+    rs = torch.randn(b, 8, d2, generator=g)
+    ape = torch.randn(4, d2, generator=g) * 0.1
+    nw = torch.rand(hd, generator=g) + 0.5
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    grk, grs = rk.clone().to(DEV), rs.clone().to(DEV)
+    pos0 = torch.tensor([100 + 3 * i for i in range(b)], dtype=torch.int32)
+    pool = torch.zeros(b * 8, hd, device=DEV)
+    for step in range(8):
+        pos = pos0 + step
+        kv = torch.randn(b, d2, generator=g)
+        sc = torch.randn(b, d2, generator=g)
+        rows = torch.arange(b) * 8 + step
+        dsv4.compressor_decode_step(kv.to(DEV), None, None, ape.to(DEV), nw.to(DEV), grk, grs,
+                                    pos.to(DEV), pool, rows.to(DEV), head_dim=hd, freqs=f.to(DEV),
+                                    proj=(kv.to(DEV), sc.to(DEV)))
+        for i in range(b):
+            ref = C.decode_ring_step(rk[i], rs[i], kv[i], sc[i], ape, nw, int(pos[i]), f)
+            if ref is not None:
+                assert_close_bf16(pool[rows[i]], ref, 2e-3, 1e-4, what=f"hd={hd} seq {i} step {step}")
+        torch.testing.assert_close(grk.cpu(), rk, rtol=0, atol=0)
+        torch.testing.assert_close(grs.cpu(), rs, rtol=1e-6, atol=1e-6)
 
 
 def test_compressor_decode_ring(dsv4):
