@@ -56,7 +56,15 @@ class IndexerParams(ctypes.Structure):
                 ("out_stride", i32), ("out_col", i32), ("out_offset", i64),
                 ("block_table", vp), ("table_stride", i32), ("page", i32),
                 ("workspace", vp), ("workspace_bytes", sz), ("win_base", vp), ("window", i32),
-                ("window_linear", i32), ("mode", i32)]
+                ("window_linear", i32), ("mode", i32), ("key_image", vp), ("key_inv", vp), ("key_norm_max", vp)]
+
+
+KEY_TILE_BYTES = 65536
+
+
+class KeyImageParams(ctypes.Structure):
+    _fields_ = [("k", vp), ("batch", i32), ("n_keys", i32), ("k_batch_stride", i64), ("image", vp), ("inv", vp),
+                ("norm_max", vp)]
 
 
 class CompressorParams(ctypes.Structure):
@@ -70,7 +78,8 @@ class CompressorDecodeParams(ctypes.Structure):
     _fields_ = [("kv", vp), ("score", vp), ("ape", vp), ("norm_w", vp), ("ring_kv", vp),
                 ("ring_score", vp), ("positions", vp), ("out", vp), ("out_rows", vp),
                 ("b", i32), ("head_dim", i32), ("ratio", i32), ("rope_dim", i32),
-                ("norm_dtype", i32), ("out_dtype", i32), ("eps", f32), ("freqs", vp)]
+                ("norm_dtype", i32), ("out_dtype", i32), ("eps", f32), ("freqs", vp),
+                ("key_image", vp), ("key_inv", vp), ("key_norm_max", vp), ("image_stride", i64)]
 
 
 class LinearParams(ctypes.Structure):
@@ -117,6 +126,7 @@ SIGNATURES = {
     "dsv4_compressor_pool": (ctypes.c_int, [ctypes.POINTER(CompressorParams), vp]),
     "dsv4_compressor_decode": (ctypes.c_int, [ctypes.POINTER(CompressorDecodeParams), vp]),
     "dsv4_decode_rows": (ctypes.c_int, [ctypes.POINTER(DecodeRowsParams), vp]),
+    "dsv4_indexer_key_image": (ctypes.c_int, [ctypes.POINTER(KeyImageParams), vp]),
     "dsv4_linear_workspace_size": (sz, [ctypes.POINTER(LinearParams)]),
     "dsv4_linear": (ctypes.c_int, [ctypes.POINTER(LinearParams), vp]),
     "dsv4_linear_multi": (ctypes.c_int, [ctypes.POINTER(LinearMultiParams), vp]),

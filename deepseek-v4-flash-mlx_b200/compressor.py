@@ -69,11 +69,13 @@ def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_h
 
 def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, positions, out, out_rows,
                            head_dim=512, ratio=4, rope_head_dim=64, freqs=None, eps=1e-6,
-                           proj=None):
+                           proj=None, key_image=None):
     """One decode token per sequence (oracle/decode_engine.py:96-105): write this token's kv / score
     into the device ring; sequences whose position p has (p+1) % ratio == 0 emit a pooled, normed,
     roped row into out[out_rows[b]] and shift the ring. x [b, dim]; positions int32 [b].
-    `proj` may pass precomputed projections (kv, score) [b, 2*head_dim] fp32."""
+    `proj` may pass precomputed projections (kv, score) [b, 2*head_dim] fp32. `key_image`
+    (image, inv, norm_max, keys_per_entry) also adds each emitted indexer key (out viewed as
+    [entries * keys_per_entry, 128] fp32) to a decode cache's key image."""
     L.require_cuda(x, ring_kv, ring_score, positions, out, out_rows)
     if proj is None:
         kvp = linear(x, wkv, torch.float32)
@@ -93,4 +95,7 @@ def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, posi
     p.out_dtype = L.dtype_code(out)
     p.eps = eps
     p.freqs = L.ptr(freqs)
+    if key_image is not None:
+        img, inv, nmax, stride = key_image
+        p.key_image, p.key_inv, p.key_norm_max, p.image_stride = L.ptr(img), L.ptr(inv), L.ptr(nmax), int(stride)
     L.check(L.lib().dsv4_compressor_decode(ctypes.byref(p), L.stream_of(x)))

@@ -73,6 +73,8 @@ def make_decode_case(batch, ctx, top_k=512, seeds=None, device="cuda", page=64, 
         cache.fill_window(b, torch.arange(dims.window, device=device), win.to(device))
         qs.append(q), qis.append(q_idx), ws.append(w)
         comp_h.append(comp), win_h.append(win), keys_h.append(keys)
+    if str(device).startswith("cuda"):
+        cache.refresh_key_image()
     positions = torch.full((batch,), ctx - 1, dtype=torch.int32)
     host = dict(q=torch.stack(qs), q_idx=torch.stack(qis), w_idx=torch.stack(ws), sink=sink, positions=positions,
                 k_idx=torch.stack(keys_h))

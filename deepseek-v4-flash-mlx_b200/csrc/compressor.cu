@@ -10,6 +10,7 @@
 // scattered into a paged pool through out_rows. One CTA per compressed row, 256 threads, two
 // dims per thread. The decode kernel keeps the per-sequence ring [2*ratio, 2d] on the device.
 #include "common.cuh"
+#include "key_image.cuh"
 
 namespace dsv4 {
 namespace cmp {
@@ -31,8 +32,24 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return red[32];
 }
 
-// normalise, rope and store two adjacent dims (c, c+1) of one compressed row
-__device__ __forceinline__ void finish_pair(float v0, float v1, int c, int d, int rope_dim,
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_max(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_max(t);
+    if (threadIdx.x == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// normalise, rope and store two adjacent dims (c, c+1) of one compressed row; the stored values
+// (before the cast) are left in v0, v1
+__device__ __forceinline__ void finish_pair(float& v0, float& v1, int c, int d, int rope_dim,
                                             const void* norm_w, int norm_dtype, float rinv,
                                             const float* freqs, int pos, void* out, int64_t orow,
                                             int out_dtype) {
@@ -171,6 +188,37 @@ __global__ void ring_seed_kernel(dsv4_compressor_params p) {
 __device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
 __device__ __forceinline__ void st2(float* p, float2 v) { *reinterpret_cast<float2*>(p) = v; }
 
+// the emitted row (indexer key, head_dim 128 = 64 pairs held by threads 0..63, fp32 values as
+// stored) added to the key image: scaled and split as dsv4_indexer_key_image does it, its inverse
+// scale, and the entry's norm maximum raised
+template <int NP>
+__device__ __forceinline__ void append_key_image(const dsv4_compressor_decode_params& p, const float (&vals)[NP][2],
+                                                 float* red) {
+  const int tid = threadIdx.x;
+  const bool mine = 2 * tid < p.head_dim;
+  const float v0 = mine ? vals[0][0] : 0.f, v1 = mine ? vals[0][1] : 0.f;
+  const float mx = block_max(fmaxf(fabsf(v0), fabsf(v1)), red);
+  const float ss = block_sum(fmaf(v1, v1, v0 * v0), red);
+  const int64_t orow = p.out_rows[blockIdx.x];
+  const int64_t seq = orow / p.image_stride, j = orow % p.image_stride;
+  const int64_t tiles = (p.image_stride + 127) / 128;
+  const int sh = itc::row_shift(mx);
+  if (mine) {
+    uint32_t hi, lo;
+    const float up = itc::pow2(sh);
+    itc::split2(v0 * up, v1 * up, &hi, &lo);
+    const int c = 2 * tid;
+    uint8_t* img = p.key_image + (seq * tiles + j / 128) * itc::IMG_TILE_BYTES;
+    const uint32_t off = itc::key_off(static_cast<int>(j % 128), c >> 2) + ((c >> 1) & 1) * 4;
+    *reinterpret_cast<uint32_t*>(img + off) = hi;
+    *reinterpret_cast<uint32_t*>(img + off + itc::IMG_SLAB_K) = lo;
+  }
+  if (tid == 0) {
+    p.key_inv[seq * tiles * 128 + j] = itc::pow2(-sh);
+    atomicMax(reinterpret_cast<unsigned int*>(p.key_norm_max + seq), __float_as_uint(sqrtf(ss)));
+  }
+}
+
 template <int NP>
 __global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_decode_params p) {
   constexpr int R = 4;
@@ -263,6 +311,7 @@ __global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_deco
     st2(rk + (R - 1) * d2 + d + c, nk[np][1]);
     st2(rs + (R - 1) * d2 + d + c, ns[np][1]);
   }
+  if (p.key_image) append_key_image<NP>(p, vals, red);
 }
 
 __global__ void __launch_bounds__(THREADS) decode_kernel(dsv4_compressor_decode_params p) {
@@ -358,6 +407,11 @@ extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, vo
                      p->head_dim <= 4 * cmp::THREADS && p->rope_dim % 2 == 0 && p->rope_dim <= p->head_dim,
                  "dsv4_compressor_decode: bad sizes");
   DSV4_CHECK_DTYPE(p->out_dtype == DSV4_F32 || p->out_dtype == DSV4_BF16, "dsv4_compressor_decode: out dtype");
+  DSV4_CHECK_ARG(p->key_image == nullptr || (p->key_inv && p->key_norm_max && p->image_stride > 0 && p->ratio == 4 &&
+                                              p->head_dim == 128 && p->out_dtype == DSV4_F32 &&
+                                              reinterpret_cast<uintptr_t>(p->key_image) % 16 == 0),
+                 "dsv4_compressor_decode: a key image needs ratio 4, head_dim 128, fp32 out, inv, norm_max, "
+                 "image_stride and a 16-byte aligned image");
   if (p->ratio == 4 && p->head_dim <= 2 * cmp::THREADS)
     cmp::decode_r4_kernel<1><<<p->b, cmp::THREADS, 0, as_stream(stream)>>>(*p);
   else if (p->ratio == 4)

@@ -12,6 +12,7 @@
 // order-preserving 32-bit image; the top_k visible keys are written in ascending key order,
 // padded with -1. The reference attends to all visible compressed rows (oracle/decode_engine.py
 // :112-114); with top_k >= visible rows this selection returns exactly that list.
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -1185,7 +1186,10 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 size_t workspace_layout(const dsv4_indexer_params* p, int mode, size_t* off_kimg, size_t* off_kmax) {
   const int64_t n_pad = (p->n_keys + 3) / 4 * 4;
   const size_t sc = static_cast<size_t>(static_cast<int64_t>(p->batch) * p->s * n_pad * sizeof(float));
-  if (mode != 2) return sc;
+  if (mode != 2 || p->key_image != nullptr) {  // a cache-kept image brings its own scales and norms
+    *off_kimg = *off_kmax = sc;
+    return sc;
+  }
   *off_kimg = round_up(sc, 1024);
   *off_kmax = *off_kimg;
   if (!itc::row_kernel(p->s)) *off_kmax += itc::kimg_bytes(p->batch, p->n_keys) + itc::kinv_bytes(p->batch, p->n_keys);
@@ -1220,6 +1224,13 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
                  "dsv4_indexer_topk: window columns need positions and out_col >= window");
   const int64_t rows = static_cast<int64_t>(p->batch) * p->s;
   DSV4_CHECK_ARG(rows <= 2147483647LL, "dsv4_indexer_topk: too many queries");
+  DSV4_CHECK_ARG((p->key_image == nullptr) == (p->key_inv == nullptr) &&
+                     (p->key_image == nullptr) == (p->key_norm_max == nullptr),
+                 "dsv4_indexer_topk: key_image, key_inv and key_norm_max go together");
+  DSV4_CHECK_ARG(p->key_image == nullptr || p->k_batch_stride >= p->n_keys,
+                 "dsv4_indexer_topk: a key image needs k_batch_stride >= n_keys");
+  DSV4_CHECK_ARG(p->key_image == nullptr || reinterpret_cast<uintptr_t>(p->key_image) % 16 == 0,
+                 "dsv4_indexer_topk: key image must be 16-byte aligned");
   const int mode = resolve_mode(p);
   DSV4_CHECK_ARG(mode > 0, "dsv4_indexer_topk: mode %d unavailable (mode 2 needs n_keys <= %d)", p->mode,
                  idx::SEL_THREADS * 32);
@@ -1245,11 +1256,20 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
     A.k_batch_stride = p->k_batch_stride;
     A.positions = p->positions;
     A.ratio = p->ratio;
-    if (!itc::row_kernel(p->s)) {
-      A.kimg = static_cast<uint8_t*>(p->workspace) + off_kimg;
-      A.kinv = reinterpret_cast<float*>(A.kimg + itc::kimg_bytes(p->batch, p->n_keys));
+    if (p->key_image) {
+      A.kimg = const_cast<uint8_t*>(p->key_image);
+      A.kinv = const_cast<float*>(p->key_inv);
+      A.kmax = kmax = const_cast<float*>(p->key_norm_max);
+      A.img_tiles = itc::key_tiles(static_cast<int>(std::min<int64_t>(p->k_batch_stride, 1 << 30)));
+      A.img_ready = 1;
+    } else {
+      if (!itc::row_kernel(p->s)) {
+        A.kimg = static_cast<uint8_t*>(p->workspace) + off_kimg;
+        A.kinv = reinterpret_cast<float*>(A.kimg + itc::kimg_bytes(p->batch, p->n_keys));
+      }
+      A.kmax = kmax = reinterpret_cast<float*>(static_cast<uint8_t*>(p->workspace) + off_kmax);
+      A.img_tiles = itc::key_tiles(p->n_keys);
     }
-    A.kmax = kmax = reinterpret_cast<float*>(static_cast<uint8_t*>(p->workspace) + off_kmax);
     DSV4_CUDA_CHECK(itc::launch_approx_scores(A, as_stream(stream)));
   }
 
@@ -1296,6 +1316,28 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
     L.eps_c = idx::EPS_C;
   }
   DSV4_CUDA_CHECK(idx::launch_select(L, static_cast<unsigned>(rows), as_stream(stream)));
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_indexer_key_image(const dsv4_key_image_params* p, void* stream) {
+  DSV4_CHECK_ARG(p && p->k && p->image && p->inv && p->norm_max, "dsv4_indexer_key_image: NULL tensor");
+  DSV4_CHECK_ARG(p->batch > 0 && p->n_keys >= 0 && p->k_batch_stride >= p->n_keys && p->k_batch_stride < (1 << 30),
+                 "dsv4_indexer_key_image: bad sizes");
+  DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(p->image) % 16 == 0, "dsv4_indexer_key_image: image not 16-byte aligned");
+  itc::ApproxArgs A = {};
+  A.k = p->k;
+  A.batch = p->batch;
+  A.n_keys = p->n_keys;
+  A.k_batch_stride = p->k_batch_stride;
+  A.kimg = p->image;
+  A.kinv = p->inv;
+  A.kmax = p->norm_max;
+  A.img_tiles = itc::key_tiles(static_cast<int>(p->k_batch_stride));
+  if (p->n_keys == 0) {
+    DSV4_CUDA_CHECK(cudaMemsetAsync(p->norm_max, 0, sizeof(float) * p->batch, as_stream(stream)));
+    return DSV4_OK;
+  }
+  DSV4_CUDA_CHECK(itc::launch_key_image(A, as_stream(stream)));
   return DSV4_OK;
 }
 

@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "indexer_tc.cuh"
+#include "key_image.cuh"
 #include "tcgen05.cuh"
 
 namespace dsv4 {
@@ -37,7 +38,7 @@ constexpr int THREADS = (EPI_WARPS + 1) * 32;  // + the producer warp
 constexpr int SLAB_Q = NQ * 128;        // 32 KB: 256 (query, head) rows x 64 fp16 dims
 constexpr int SLAB_K = BM * 128;        // 16 KB: 128 keys x 64 fp16 dims
 constexpr int GROUP = 2 * SLAB_K;       // 32 KB: hi + lo slab of one dim group of a tile
-static_assert(TILE_BYTES == 2 * GROUP, "tile image");
+static_assert(TILE_BYTES == 2 * GROUP && GROUP == IMG_GROUP && SLAB_K == IMG_SLAB_K, "tile image");
 constexpr int TMEM_COLS = 512;
 constexpr int NSLOT = 3;                // slab-group copies in flight: 3 x 32 KB next to the 128 KB of Q
 
@@ -53,46 +54,6 @@ struct Smem {
 };
 
 static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory above the 227 KB a CTA may opt into");
-
-// exponent s (|s| <= 100) with max_abs * 2^s in [2^14, 2^15); 0 for a zero row
-__device__ __forceinline__ int row_shift(float max_abs) {
-  if (!(max_abs > 0.f)) return 0;
-  int adj = 0;
-  if (max_abs < 0x1p-100f) {
-    max_abs *= 0x1p64f;
-    adj = 64;
-  }
-  const int e = static_cast<int>((__float_as_uint(max_abs) >> 23) & 0xff) - 127 - adj;  // floor(log2)
-  const int s = 14 - e;
-  return s < -100 ? -100 : (s > 100 ? 100 : s);
-}
-__device__ __forceinline__ float pow2(int s) { return __uint_as_float(static_cast<uint32_t>(s + 127) << 23); }
-
-__device__ __forceinline__ uint32_t pack2h(__half a, __half b) {
-  return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
-}
-// 4 fp32 (already scaled) -> (hi, lo) as two 8-byte groups of 4 fp16
-__device__ __forceinline__ void split4(float4 v, uint2* hi, uint2* lo) {
-  const __half h0 = __float2half_rn(v.x), h1 = __float2half_rn(v.y);
-  const __half h2 = __float2half_rn(v.z), h3 = __float2half_rn(v.w);
-  const __half l0 = __float2half_rn(v.x - __half2float(h0));
-  const __half l1 = __float2half_rn(v.y - __half2float(h1));
-  const __half l2 = __float2half_rn(v.z - __half2float(h2));
-  const __half l3 = __float2half_rn(v.w - __half2float(h3));
-  *hi = make_uint2(pack2h(h0, h1), pack2h(h2, h3));
-  *lo = make_uint2(pack2h(l0, l1), pack2h(l2, l3));
-}
-__device__ __forceinline__ float4 scale4(float4 v, float f) {
-  return make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
-}
-__device__ __forceinline__ float amax4(float4 v) {
-  return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-}
-// byte offset of float4 f (dims 4f..4f+3) of row r inside a tile image's slab group layout
-__device__ __forceinline__ uint32_t key_off(int r, int f) {
-  const int g = f >> 4, c = (f >> 1) & 7;
-  return static_cast<uint32_t>(g * GROUP + r * 128 + ((c ^ (r & 7)) << 4) + (f & 1) * 8);
-}
 
 // max over the CTA's threads (all of them call it), one atomicMax per CTA into *dst (the values
 // are non-negative floats, which order like their bit patterns)
@@ -114,7 +75,7 @@ __device__ __forceinline__ void cta_atomic_max(float v, float* dst) {
 __global__ void __launch_bounds__(BM) key_image_kernel(ApproxArgs P) {
   const int t = blockIdx.x, b = blockIdx.y, r = threadIdx.x;
   const int j = t * BM + r;
-  const int tiles = key_tiles(P.n_keys);
+  const int tiles = P.img_tiles;
   uint8_t* img = P.kimg + (static_cast<int64_t>(b) * tiles + t) * TILE_BYTES;
   const float4* kr = reinterpret_cast<const float4*>(P.k + (static_cast<int64_t>(b) * P.k_batch_stride + j) * DI);
   const bool valid = j < P.n_keys;
@@ -240,7 +201,7 @@ __global__ void __launch_bounds__(THREADS, 1) approx_score_kernel(ApproxArgs P) 
   after_sync();
   const uint32_t tmem = sm.tmem_base;
   const volatile int* abort = &sm.abort;
-  const int tiles = key_tiles(P.n_keys);
+  const int tiles = P.img_tiles;  // image stride per batch entry
 
   if (warp == EPI_WARPS) {
     if (lane == 0) {
@@ -505,9 +466,10 @@ static_assert(sizeof(SeqSmem) + 1024 + sizeof(SeqSmall) + 256 <= 232448,
               "shared memory above the 227 KB a CTA may opt into");
 
 // scale and split query `row` into the Q slabs (warp w: heads w, w + NW, ..; lane = float4 of a head)
+template <int NT>
 __device__ __forceinline__ void split_query(const ApproxArgs& P, int64_t row, uint8_t* qh, uint8_t* ql, float* w) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int NW = SQ_THREADS / 32, QH = HI / NW;
+  constexpr int NW = NT / 32, QH = HI / NW;
   float4 qv[QH];
 #pragma unroll
   for (int k = 0; k < QH; ++k)
@@ -605,7 +567,7 @@ __global__ void __launch_bounds__(SQ_THREADS) approx_score_seq_kernel(ApproxArgs
     if (row != cur_row) {
       // every thread is past the previous item's epilogue (it reads sx.w) and its MMAs are done
       __syncthreads();
-      split_query(P, row, sm.qh, sm.ql, sx.w);
+      split_query<SQ_THREADS>(P, row, sm.qh, sm.ql, sx.w);
       cur_row = row;
     }
     ok = __syncthreads_and(bar_wait(&sx.full[slot], (k >> 1) & 1));
@@ -723,11 +685,186 @@ __global__ void __launch_bounds__(SQ_THREADS) approx_score_seq_kernel(ApproxArgs
   if (warp == 0) tmem_dealloc<64>(tmem);
 }
 
+// ---- decode batches over a cache-kept key image: the persistent walk of approx_score_seq_kernel
+// without the split. Each visible 128-key tile's 64 KB image lands by one bulk copy (three in
+// flight), then 24 MMAs and the fold (thread = key, inverse scale from the cache). About 225 KB of
+// shared memory: one CTA per SM.
+constexpr int IM_THREADS = 128;
+constexpr int IM_SLOTS = 3;
+
+struct ImgSmem {  // dynamic shared memory
+  alignas(1024) uint8_t img[IM_SLOTS][TILE_BYTES];
+  alignas(1024) uint8_t qh[2 * RSLAB_Q];
+  alignas(1024) uint8_t ql[2 * RSLAB_Q];
+};
+struct ImgSmall {  // static shared memory
+  float w[HI];
+  uint64_t full[IM_SLOTS], mma;
+  uint32_t tmem_base;
+};
+static_assert(sizeof(ImgSmem) + 1024 + sizeof(ImgSmall) + 256 <= 232448,
+              "shared memory above the 227 KB a CTA may opt into");
+
+__device__ __forceinline__ void img_issue(const ApproxArgs& P, ImgSmem& sm, ImgSmall& sx, int slot, int64_t item,
+                                          int tiles) {
+  const int64_t row = item / tiles;
+  const int t = static_cast<int>(item % tiles);
+  const int b = static_cast<int>(row / P.s);
+  bar_expect_tx(&sx.full[slot], TILE_BYTES);
+  bulk_g2s(sm.img[slot], P.kimg + (static_cast<int64_t>(b) * P.img_tiles + t) * TILE_BYTES, TILE_BYTES, &sx.full[slot]);
+}
+
+__global__ void __launch_bounds__(IM_THREADS) approx_score_img_kernel(ApproxArgs P, int64_t per) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  ImgSmem& sm = *reinterpret_cast<ImgSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
+  __shared__ ImgSmall sx;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tiles = key_tiles(P.n_keys);
+  const int64_t items = static_cast<int64_t>(P.batch) * P.s * tiles;
+  const int64_t begin = static_cast<int64_t>(blockIdx.x) * per;
+  SeqWalk walk{begin + per < items ? begin + per : items, tiles};
+  SeqWalk pwalk = walk;  // the producer's own cursor state
+  if (warp == 0) tmem_alloc<64>(&sx.tmem_base);
+  if (tid == 0) {
+    for (int k = 0; k < IM_SLOTS; ++k) bar_init(&sx.full[k], 1);
+    bar_init(&sx.mma, 1);
+    bar_init_fence();
+  }
+  before_sync();
+  __syncthreads();
+  after_sync();
+  const uint32_t tmem = sx.tmem_base;
+  int64_t pnext = 0;
+  int issued = 0;
+  if (tid == 0) {
+    pnext = pwalk.next_valid(P, begin);
+    for (int k = 0; k < IM_SLOTS && pnext < walk.end; ++k) {
+      img_issue(P, sm, sx, k, pnext, tiles);
+      ++issued;
+      pnext = pwalk.next_valid(P, pnext + 1);
+    }
+  }
+  int64_t cur_row = -1;
+  int k = 0;
+  bool ok = true, mma_pending = false;
+  for (int64_t i = walk.next_valid(P, begin); i < walk.end; ++k) {
+    const int64_t row = i / tiles;
+    const int t = static_cast<int>(i % tiles);
+    const int b = static_cast<int>(row / P.s);
+    const int slot = k % IM_SLOTS;
+    if (row != cur_row) {  // the previous item's MMAs are done (waited below): the Q slabs are free
+      __syncthreads();
+      split_query<IM_THREADS>(P, row, sm.qh, sm.ql, sx.w);
+      fence_async_smem();
+      cur_row = row;
+    }
+    const int j = t * BM + tid;
+    const float ki = j < P.n_keys ? __ldg(P.kinv + static_cast<int64_t>(b) * P.img_tiles * BM + j) : 0.f;
+    before_sync();
+    __syncthreads();  // the Q slabs written; the previous item's TMEM reads done
+    after_sync();
+    int ok0 = 1;
+    if (tid == 0) {
+      ok0 = bar_wait(&sx.full[slot], (k / IM_SLOTS) & 1);
+      if (ok0) {
+        after_sync();
+        constexpr uint32_t id = idesc_f16<128, HI>(false, false);
+        const uint32_t qh = smem_u32(sm.qh), ql = smem_u32(sm.ql), kb = smem_u32(sm.img[slot]);
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const uint32_t kh = kb + g * GROUP, kl = kh + SLAB_K;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma16(tmem, sdesc(kl + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id,
+                  (g | kk) ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma16(tmem, sdesc(kh + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma16(tmem, sdesc(kh + kk * 32, 16, 1024), sdesc(ql + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
+        }
+        mma_commit(&sx.mma);
+      }
+    }
+    ok = __syncthreads_and(ok0);
+    if (!ok) break;
+    ok = __syncthreads_and(bar_wait(&sx.mma, k & 1));
+    if (!ok) {
+      mma_pending = true;
+      ++k;  // this item's copy has landed
+      break;
+    }
+    after_sync();
+    if (tid == 0 && pnext < walk.end) {  // the MMAs have read the slot: refill it
+      img_issue(P, sm, sx, slot, pnext, tiles);
+      ++issued;
+      pnext = pwalk.next_valid(P, pnext + 1);
+    }
+    {  // the fold: thread = key (TMEM lane)
+      const uint32_t lq = static_cast<uint32_t>(warp * 32) << 16;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+      for (int c = 0; c < HI; c += 16) {
+        float sc[16];
+        tmem_ld16(tmem + lq + c, sc);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < 16; h += 4) {
+          const float4 wv = *reinterpret_cast<const float4*>(&sx.w[c + h]);
+          a0 = fmaf(wv.x, fmaxf(sc[h], 0.f), a0);
+          a1 = fmaf(wv.y, fmaxf(sc[h + 1], 0.f), a1);
+          a2 = fmaf(wv.z, fmaxf(sc[h + 2], 0.f), a2);
+          a3 = fmaf(wv.w, fmaxf(sc[h + 3], 0.f), a3);
+        }
+      }
+      if (j < P.n_keys) P.scores[row * P.n_pad + j] = ((a0 + a1) + (a2 + a3)) * ki;
+    }
+    i = walk.next_valid(P, i + 1);
+  }
+  if (!ok) {
+    if (tid == 0) {
+      raise_device_error(DSV4_ERR_WAIT_TIMEOUT);
+      // let the copies still in flight land before the CTA's shared memory goes away (bounded)
+      for (int kk = k; kk < issued; ++kk) bar_wait(&sx.full[kk % IM_SLOTS], (kk / IM_SLOTS) & 1);
+      if (mma_pending) bar_wait(&sx.mma, (k - 1) & 1);
+    }
+  }
+  before_sync();
+  __syncthreads();
+  after_sync();
+  if (warp == 0) tmem_dealloc<64>(tmem);
+}
+
 DSV4_ERROR_READER(indexer_tc)
 
-cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream) {
+cudaError_t launch_key_image(const ApproxArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaMemsetAsync(a.kmax, 0, sizeof(float) * a.batch, stream);
   if (e != cudaSuccess) return e;
+  key_image_kernel<<<dim3(key_tiles(a.n_keys), a.batch), BM, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
+  if (a.img_ready && row_kernel(a.s)) {  // decode over a cache-kept image: the walk without the split
+    const int smem = static_cast<int>(sizeof(ImgSmem)) + 1024;
+    static bool iattr = false;
+    if (!iattr) {
+      e = cudaFuncSetAttribute(approx_score_img_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      iattr = true;
+    }
+    const int64_t items = static_cast<int64_t>(a.batch) * a.s * key_tiles(a.n_keys);
+    const int64_t ctas = num_sms();
+    const int64_t per = (items + ctas - 1) / ctas;
+    approx_score_img_kernel<<<static_cast<unsigned>((items + per - 1) / per), IM_THREADS, smem, stream>>>(a, per);
+    return cudaGetLastError();
+  }
+  if (!a.img_ready) {
+    e = cudaMemsetAsync(a.kmax, 0, sizeof(float) * a.batch, stream);
+    if (e != cudaSuccess) return e;
+  }
   if (row_kernel(a.s)) {
     const int64_t items = static_cast<int64_t>(a.batch) * a.s * key_tiles(a.n_keys);
     if (items >= 2 * static_cast<int64_t>(num_sms())) {  // at least two items per CTA: the pipelined walk
@@ -754,8 +891,10 @@ cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream) {
                               RT_THREADS, smem, stream>>>(a);
     return cudaGetLastError();
   }
-  key_image_kernel<<<dim3(key_tiles(a.n_keys), a.batch), BM, 0, stream>>>(a);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (!a.img_ready) {
+    key_image_kernel<<<dim3(key_tiles(a.n_keys), a.batch), BM, 0, stream>>>(a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;
   static bool attr = false;
   if (!attr) {

@@ -28,9 +28,11 @@ struct ApproxArgs {
   int64_t k_batch_stride;
   const int32_t* positions;
   int32_t ratio;
-  uint8_t* kimg;        // workspace: [batch][tiles][TILE_BYTES]
-  float* kinv;          // workspace: [batch][tiles * BM] inverse power-of-two scale of each key row
-  float* kmax;          // workspace: [batch] max key norm (zeroed by the launcher)
+  uint8_t* kimg;        // [batch][img_tiles][TILE_BYTES]: workspace, or a decode cache's image
+  float* kinv;          // [batch][img_tiles * BM] inverse power-of-two scale of each key row
+  float* kmax;          // [batch] max key norm (zeroed by the launcher unless img_ready)
+  int32_t img_tiles;    // tiles per batch entry in kimg / kinv
+  int32_t img_ready;    // kimg / kinv / kmax already hold every visible key (a decode cache's image)
 };
 
 __host__ __device__ inline int key_tiles(int n_keys) { return (n_keys + BM - 1) / BM; }
@@ -44,8 +46,10 @@ inline size_t kinv_bytes(int batch, int n_keys) {
   return static_cast<size_t>(batch) * key_tiles(n_keys) * BM * sizeof(float);
 }
 
-// key image + norms, then the approximate scores (two launches on `stream`)
+// key image + norms (unless img_ready), then the approximate scores
 cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream);
+// key image + norms of keys [0, n_keys) of every batch entry into kimg / kinv / kmax (kmax zeroed)
+cudaError_t launch_key_image(const ApproxArgs& a, cudaStream_t stream);
 
 }  // namespace itc
 }  // namespace dsv4

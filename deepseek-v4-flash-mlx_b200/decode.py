@@ -25,7 +25,7 @@ import math
 import torch
 
 from . import _lib as L
-from .indexer import indexer_topk_into
+from .indexer import build_key_image, indexer_topk_into, key_image_buffers
 from .norm_rope import norm_rope, rope_freqs
 from .sparse_attn import sparse_attn_rope
 
@@ -45,6 +45,9 @@ class SparseMLACache:
             page_order = torch.arange(n_pages, dtype=torch.int32)
         self.block_table = page_order.to(torch.int32).reshape(batch, self.pages_per_seq).to(device)
         self.k_idx = torch.zeros((batch, max_comp, idx_dim), dtype=torch.float32, device=device)
+        # the indexer keys' split form for the tensor-core filter, kept current with k_idx
+        self.key_image = key_image_buffers(batch, max_comp, device)
+        self.image_stale = False
         self.ring_kv = torch.zeros((batch, 2 * ratio, 2 * head_dim), dtype=torch.float32, device=device)
         self.ring_score = torch.full((batch, 2 * ratio, 2 * head_dim), float("-inf"), dtype=torch.float32,
                                      device=device)
@@ -67,6 +70,12 @@ class SparseMLACache:
         j = torch.arange(n, device=rows_bf16.device)
         self.kv_pool[self.comp_rows(b, j)] = rows_bf16.to(torch.bfloat16)
         self.k_idx[b, :n] = keys_f32
+        self.image_stale = True
+
+    def refresh_key_image(self):
+        """Rebuild the key image from k_idx (after host-side fills; decode steps keep it current)."""
+        build_key_image(self.k_idx, self.key_image)
+        self.image_stale = False
 
     def fill_window(self, b, positions, rows_bf16):
         self.kv_pool[self.window_rows(b, positions)] = rows_bf16.to(torch.bfloat16)
@@ -115,9 +124,12 @@ def decode_attention(cache, q, q_idx, w_idx, sink, positions, top_k=512, scale=N
     with torch.cuda.stream(side):          # q's norm + rope runs beside the indexer
         qr = norm_rope(q, positions, freqs, weight=None)
     idx = idx_buf if idx_buf is not None else attention_index_buffer(b, cache.window, top_k, q.device)
+    if cache.image_stale:
+        cache.refresh_key_image()
     indexer_topk_into(idx.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
                       cache.k_idx, top_k, positions.view(b, 1), cache.ratio, out_col=0,
-                      out_offset=cache.comp_base, block_table=cache.block_table, page=cache.page)
+                      out_offset=cache.comp_base, block_table=cache.block_table, page=cache.page,
+                      key_image=cache.key_image)
     main.wait_stream(side)
     qr.record_stream(main)
     return sparse_attn_rope(qr, cache.kv_pool, sink, idx, scale, positions, freqs, 64, out_dtype,

@@ -14,7 +14,7 @@ from . import _lib as L
 
 
 def _params(q, w, k, out, top_k, positions, ratio, out_col, out_offset, block_table, page, scores_out,
-            win_base=None, window=0, window_linear=False, mode=0):
+            win_base=None, window=0, window_linear=False, mode=0, key_image=None):
     b, s, h, di = q.shape
     p = L.IndexerParams()
     p.q, p.w, p.k, p.out = L.ptr(q), L.ptr(w), L.ptr(k), L.ptr(out)
@@ -31,7 +31,32 @@ def _params(q, w, k, out, top_k, positions, ratio, out_col, out_offset, block_ta
     p.window = window
     p.window_linear = int(window_linear)
     p.mode = mode
+    if key_image is not None:
+        img, inv, nmax = key_image
+        p.key_image, p.key_inv, p.key_norm_max = L.ptr(img), L.ptr(inv), L.ptr(nmax)
     return p
+
+
+def key_image_buffers(batch, max_keys, device):
+    """Zeroed buffers of a decode cache's key image for `max_keys` keys per batch entry:
+    (image uint8 [batch * tiles * 64 KB], inverse scales fp32 [batch, tiles * 128], norm max fp32 [batch])."""
+    tiles = (max_keys + 127) // 128
+    img = torch.zeros(batch * tiles * L.KEY_TILE_BYTES, dtype=torch.uint8, device=device)
+    return img, torch.zeros(batch, tiles * 128, dtype=torch.float32, device=device), \
+        torch.zeros(batch, dtype=torch.float32, device=device)
+
+
+def build_key_image(k_idx, key_image, n_keys=None):
+    """(Re)build the key image (dsv4_indexer_key_image) of keys [0, n_keys) of every batch entry of
+    k_idx [batch, max_keys, 128] fp32 into the buffers of key_image_buffers."""
+    L.require_cuda(k_idx)
+    img, inv, nmax = key_image
+    b, stride = k_idx.shape[0], k_idx.shape[1]
+    p = L.KeyImageParams()
+    p.k, p.batch, p.n_keys, p.k_batch_stride = L.ptr(k_idx), b, stride if n_keys is None else int(n_keys), stride
+    p.image, p.inv, p.norm_max = L.ptr(img), L.ptr(inv), L.ptr(nmax)
+    L.check(L.lib().dsv4_indexer_key_image(ctypes.byref(p), L.stream_of(k_idx)))
+    return key_image
 
 
 def _run(p, device, stream_ref):
@@ -95,17 +120,20 @@ def indexer_scores(q_idx, w, k_idx, positions=None, ratio=4, mode=1):
 
 
 def indexer_topk_into(out, q_idx, w, k_idx, top_k, positions=None, ratio=4, out_col=0, out_offset=0,
-                      block_table=None, page=0, win_base=None, window=0, window_linear=False, mode=0):
+                      block_table=None, page=0, win_base=None, window=0, window_linear=False, mode=0,
+                      key_image=None):
     """Write the selection into columns [out_col, out_col+top_k) of an existing int32 index buffer
     out [b, s, T], mapping key j to pool row out_offset + j, or through a block table
     (block_table[b, j // page] * page + j % page + out_offset). Used by the decode and prefill
     pipelines to build the attention index list without a copy. With `win_base` (int64 [b]) the
     window rows of each query also go to columns [out_col - window, out_col): the decode ring order
-    at positions[b], or with window_linear the prefill rows win_base + max(0, p-window+1) .. p."""
+    at positions[b], or with window_linear the prefill rows win_base + max(0, p-window+1) .. p.
+    `key_image` (the buffers of key_image_buffers, kept current for k_idx) lets the tensor-core
+    filter read the keys' split form instead of splitting them on every call."""
     q_idx, w, k_idx, positions, _ = _prep(q_idx, w, k_idx, positions)
     if out.dtype != torch.int32 or not out.is_contiguous():
         raise TypeError("indexer_topk_into: out must be a contiguous int32 tensor")
     p = _params(q_idx, w, k_idx, out, int(top_k), positions, int(ratio), int(out_col), int(out_offset),
-                block_table, int(page), None, win_base, int(window), window_linear, int(mode))
+                block_table, int(page), None, win_base, int(window), window_linear, int(mode), key_image)
     _run(p, q_idx.device, q_idx)
     return out

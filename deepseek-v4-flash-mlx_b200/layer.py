@@ -160,7 +160,8 @@ class DecodeBlock:
                                rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(c_kv, c_sc))
         compressor_decode_step(xn, W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, c.ring_k_idx, c.ring_s_idx, pos,
                                c.k_idx.view(-1, d.idx_dim), key_rows, head_dim=d.idx_dim, ratio=d.ratio,
-                               rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(i_kv, i_sc))
+                               rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(i_kv, i_sc),
+                               key_image=(*c.key_image, c.max_comp))
         q_idx = rope(qi.view(b, d.idx_heads, d.idx_dim), pos, self.freqs, d.rope_dim)
         o = decode_attention(c, qraw, q_idx, w_idx, W.sinks, pos, self.top_k, freqs=self.freqs)
         return o_grouped(o.reshape(b, -1), W.wo_a, W.wo_b)

@@ -211,10 +211,34 @@ typedef struct {
    *     exact fp32 rescoring (the order above) of the keys whose A lies within 2 eps of the k-th
    *     largest A; keys above that band are in the top_k, keys below it are not. n_keys <= 16384.
    *     With scores_out, the approximate scores are written there.
-   * 0 = automatic: 2 for prefill-shaped calls (batch * s >= 256, n_keys > top_k, n_keys <= 16384),
-   *     else 1. The allocation-free entry point below always uses 1. */
+   * 0 = automatic: 2 for prefill-shaped calls (batch * s >= 256) and decode batches (batch >= 16),
+   *     when n_keys > top_k and n_keys <= 16384, else 1. The allocation-free entry point below
+   *     always uses 1. */
   int32_t mode;
+  /* optional, mode 2: the keys' tile image kept by a decode cache (dsv4_indexer_key_image, and the
+   * compressor decode step for the keys it appends): the filter reads it instead of splitting the
+   * keys on every call. All three or none; k_batch_stride keys per batch entry in the image. */
+  const uint8_t* key_image;
+  const float* key_inv;
+  const float* key_norm_max;
 } dsv4_indexer_params;
+
+/* The decode cache's form of the indexer keys for the tensor-core filter: per batch entry,
+ * ceil(k_batch_stride / 128) tiles of DSV4_KEY_TILE_BYTES (the scaled fp16 hi / lo split of 128 keys,
+ * laid out as the MMA reads it), one inverse power-of-two scale per key ([batch, tiles * 128] fp32),
+ * and a running maximum key norm per entry (an upper bound for the filter's error bound). This call
+ * (re)builds keys [0, n_keys) of every entry and sets the norm maximum over them; keys a compressor
+ * decode step appends later are added by that step (dsv4_compressor_decode_params). */
+#define DSV4_KEY_TILE_BYTES 65536
+typedef struct {
+  const float* k;         /* [batch, k_batch_stride, 128] */
+  int32_t batch, n_keys;
+  int64_t k_batch_stride;
+  uint8_t* image;         /* [batch, ceil(k_batch_stride / 128), DSV4_KEY_TILE_BYTES] */
+  float* inv;             /* [batch, ceil(k_batch_stride / 128) * 128] */
+  float* norm_max;        /* [batch] */
+} dsv4_key_image_params;
+DSV4_API int dsv4_indexer_key_image(const dsv4_key_image_params* p, void* stream);
 
 DSV4_API size_t dsv4_indexer_topk_workspace_size(const dsv4_indexer_params* p);
 DSV4_API int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream);
@@ -274,6 +298,13 @@ typedef struct {
   int32_t norm_dtype, out_dtype;
   float eps;
   const float* freqs;
+  /* optional (indexer keys: head_dim 128, fp32 out): also add each emitted row to a key image
+   * (dsv4_key_image_params layout) as key j = out_rows[b] % image_stride of entry
+   * out_rows[b] / image_stride, and raise that entry's norm maximum. NULL = off. */
+  uint8_t* key_image;
+  float* key_inv;
+  float* key_norm_max;
+  int64_t image_stride;
 } dsv4_compressor_decode_params;
 DSV4_API int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream);
 

@@ -24,6 +24,7 @@ PAIRS = {
     "dsv4_decode_rows_params": L.DecodeRowsParams,
     "dsv4_linear_out": L.LinearOut,
     "dsv4_linear_multi_params": L.LinearMultiParams,
+    "dsv4_key_image_params": L.KeyImageParams,
 }
 
 

@@ -55,6 +55,14 @@ def test_mode2_selection_bit_exact(dsv4, b, s, n, k, causal):
     got2 = dsv4.indexer_topk(*args, mode=2).cpu().numpy()
     got1 = dsv4.indexer_topk(*args, mode=1).cpu().numpy()
     np.testing.assert_array_equal(got2, got1)
+    # the same filter reading a key image built once (as a decode cache keeps it)
+    mod = __import__("importlib").import_module("deepseek-v4-flash-mlx_b200.indexer")
+    kd = keys.to(DEV)
+    image = mod.build_key_image(kd, mod.key_image_buffers(b, n, DEV))
+    outi = torch.full((b, s, k), -7, dtype=torch.int32, device=DEV)
+    mod.indexer_topk_into(outi, q.to(DEV), w.to(DEV), kd, k, positions=None if pos is None else pos.to(DEV), ratio=4,
+                          mode=2, key_image=image)
+    np.testing.assert_array_equal(outi.cpu().numpy(), got1)
     rows = range(s) if s * n <= 300 * 2000 else range(0, s, 16)
     ref = I.indexer_topk(q[:, list(rows)].numpy(), w[:, list(rows)].numpy(), keys.numpy(), k,
                          None if pos is None else pos[:, list(rows)].numpy())
@@ -125,13 +133,16 @@ def test_mode2_decode_batch_bit_exact(dsv4, b, n, k):
     pages = (n + page - 1) // page
     table = torch.stack([torch.randperm(pages, generator=g) for _ in range(b)]).to(torch.int32)
     outs = []
-    for mode in (1, 2):
+    image = mod.build_key_image(keys.to(DEV), mod.key_image_buffers(b, n, DEV))
+    for mode, kimg in ((1, None), (2, None), (2, image)):
         out = torch.full((b, 1, 128 + k), -7, dtype=torch.int32, device=DEV)
         mod.indexer_topk_into(out, q.to(DEV), w.to(DEV), keys.to(DEV), k, positions=pos.to(DEV), ratio=4, out_col=128,
                               out_offset=333, block_table=table.to(DEV), page=page,
-                              win_base=torch.arange(b, dtype=torch.int64, device=DEV) * 128, window=128, mode=mode)
+                              win_base=torch.arange(b, dtype=torch.int64, device=DEV) * 128, window=128, mode=mode,
+                              key_image=kimg)
         outs.append(out.cpu().numpy())
     np.testing.assert_array_equal(outs[1], outs[0])
+    np.testing.assert_array_equal(outs[2], outs[0])   # the filter reading a kept key image
     ref = I.indexer_topk(q.numpy(), w.numpy(), keys.numpy(), k, pos.numpy())          # [b, 1, k] key indices
     sel = ref[:, 0]
     mapped = np.where(sel >= 0, table.numpy()[np.arange(b)[:, None], np.maximum(sel, 0) // page] * page

@@ -82,3 +82,40 @@ def test_decode_block_config5(quant):
     # keys come from bf16 GEMM operands on the GPU (fp32 in the oracle): bf16-level tolerance
     assert_close_bf16(cache.k_idx.cpu(), state["k_idx"], what="indexer keys after step")
     assert_close_bf16(cache.ring_kv.cpu(), state["ring_kv"], what="compressor ring")
+    # the key image the step kept current (the emitted key appended by the compressor) is the one a
+    # full rebuild from the keys gives, byte for byte; its norm maximum still bounds every key
+    IX = importlib.import_module(PKG + ".indexer")
+    img, inv, nmax = cache.key_image
+    fresh = IX.build_key_image(cache.k_idx, IX.key_image_buffers(b, cache.max_comp, "cuda"))
+    assert torch.equal(img, fresh[0])
+    assert torch.equal(inv, fresh[1])
+    assert (nmax >= fresh[2] * (1 - 1e-6)).all()
+
+
+def test_decode_block_steps_keep_key_image():
+    """Eight decode steps (two block closings per sequence): the incrementally kept key image
+    matches a rebuild, and the indexer reading it selects what the split-every-call path selects."""
+    Lm = _layer()
+    C = importlib.import_module(PKG + ".configs")
+    IX = importlib.import_module(PKG + ".indexer")
+    b, ctx = 4, 2048
+    case = C.make_decode_case(b, ctx, 512, seeds=[400 + i for i in range(b)])
+    W = Lm.make_attention_weights(4, quant=True).to("cuda")
+    blk = Lm.DecodeBlock(W, b, ctx + 16, top_k=512, cache=case.cache)
+    g = torch.Generator().manual_seed(6)
+    for step in range(8):  # rewrites entries near the end of the cache (positions below its capacity)
+        pos = torch.tensor([ctx - 40 + step + i for i in range(b)], dtype=torch.int32).cuda()
+        blk.step(torch.randn(b, 4096, generator=g).cuda(), pos)
+    c = case.cache
+    fresh = IX.build_key_image(c.k_idx, IX.key_image_buffers(b, c.max_comp, "cuda"))
+    assert torch.equal(c.key_image[0], fresh[0])
+    assert torch.equal(c.key_image[1], fresh[1])
+    q = torch.randn(b, 1, 64, 128, generator=g).cuda()
+    w = (torch.randn(b, 1, 64, generator=g) / 8).cuda()
+    pos = torch.full((b, 1), ctx + 4, dtype=torch.int32).cuda()
+    outs = []
+    for kimg, mode in ((c.key_image, 2), (None, 2), (None, 1)):
+        out = torch.full((b, 1, 256), -7, dtype=torch.int32, device="cuda")
+        IX.indexer_topk_into(out, q, w, c.k_idx, 256, positions=pos, ratio=4, mode=mode, key_image=kimg)
+        outs.append(out.cpu())
+    assert torch.equal(outs[0], outs[2]) and torch.equal(outs[1], outs[2])
