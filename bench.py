@@ -270,9 +270,10 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--replicas", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", default=None, choices=["attn_prefill", "indexer_prefill"],
+    ap.add_argument("--kernel-case", default=None, choices=["attn_prefill", "indexer_prefill", "block_decode"],
                     help="profiling aid: run one prefill kernel alone on a 4096-query slice of config 4 "
-                         "(positions 60000..64095) and print its CUDA-event time; not a bench line")
+                         "(positions 60000..64095), or config 5's block step eagerly inside an NVTX range "
+                         "(block_decode), and print its CUDA-event time; not a bench line")
     args = ap.parse_args()
     if args.kernel_case:
         return run_kernel_case(args)
@@ -746,6 +747,8 @@ def run_kernel_case(args):
     SA = importlib.import_module(PKG + ".sparse_attn")
     IX = importlib.import_module(PKG + ".indexer")
     NRm = importlib.import_module(PKG + ".norm_rope")
+    if args.kernel_case == "block_decode":
+        return run_block_case(args, dev)
     s, nwin, ncomp, top_k = 4096, 65536, 16384, 1024
     g = torch.Generator(device=dev).manual_seed(0)
     pos = torch.arange(60000, 60000 + s, dtype=torch.int32, device=dev)
@@ -777,6 +780,36 @@ def run_kernel_case(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
     print(json.dumps({"kernel_case": args.kernel_case, "queries": s, "ms_per_call": ms, **work}), flush=True)
+
+
+def run_block_case(args, dev):
+    """Config 5's block step (batch 32, 16384-token contexts, int8-g64 weights) launched eagerly:
+    three warm-up steps, then `--steps` (default 2) steps inside the NVTX range "step", so that a
+    profiler can take exactly those launches (`ncu --nvtx --nvtx-include "step/"`)."""
+    import importlib
+    Lm = importlib.import_module(PKG + ".layer")
+    C = importlib.import_module(PKG + ".configs")
+    cfgd = CONFIGS["c5"]
+    B, ctx, top_k = cfgd["batch"], cfgd["ctx"], cfgd["top_k"]
+    W = Lm.make_attention_weights(3, quant=True).to(dev)
+    case = C.make_decode_case(B, ctx, top_k, seeds=[cfgd["seeds"](0, i) for i in range(B)], device=dev)
+    blk = Lm.DecodeBlock(W, B, ctx, top_k=top_k, cache=case.cache)
+    x = torch.randn(B, 4096, generator=torch.Generator().manual_seed(3)).to(dev)
+    pos = torch.full((B,), ctx - 1, dtype=torch.int32, device=dev)
+    for _ in range(3):
+        blk.step(x, pos)
+    torch.cuda.synchronize()
+    reps = args.steps if args.steps is not None else 2
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("step")
+    e0.record()
+    for _ in range(reps):
+        out = blk.step(x, pos)
+    e1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": "block_decode", "batch": B, "ctx": ctx, "eager_ms_per_step": e0.elapsed_time(e1) / reps,
+                      "checksum": float(out.abs().sum())}), flush=True)
 
 
 if __name__ == "__main__":

@@ -87,6 +87,8 @@ __device__ __forceinline__ float pool8(const float* kv8, const float* sc8) {
 }
 
 __global__ void __launch_bounds__(THREADS) pool_kernel(dsv4_compressor_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
   __shared__ float red[33];
   const int groups = p.s / p.ratio;
   const int64_t rowid = blockIdx.x;  // b * groups + g
@@ -147,6 +149,8 @@ __global__ void __launch_bounds__(THREADS) pool_kernel(dsv4_compressor_params p)
 // decode hand-off ring (ref_torch/compressor.py:67-74; seeding as oracle/decode_engine.py:91-95):
 // rows [0, R) = last full block (kv, score+ape), rows [R, R+rem) = remainder, rest 0 / -inf.
 __global__ void ring_seed_kernel(dsv4_compressor_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
   const int b = blockIdx.y;
   const int slot = blockIdx.x;  // 0 .. 2R-1
   const int R = p.ratio, d2 = 2 * p.head_dim;
@@ -221,6 +225,8 @@ __device__ __forceinline__ void append_key_image(const dsv4_compressor_decode_pa
 
 template <int NP>
 __global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_decode_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
   constexpr int R = 4;
   __shared__ float red[33];
   const int b = blockIdx.x, tid = threadIdx.x;
@@ -315,6 +321,8 @@ __global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_deco
 }
 
 __global__ void __launch_bounds__(THREADS) decode_kernel(dsv4_compressor_decode_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
   __shared__ float red[33];
   const int b = blockIdx.x;
   const int R = p.ratio, d = p.head_dim, d2 = 2 * d;
@@ -387,13 +395,12 @@ extern "C" int dsv4_compressor_pool(const dsv4_compressor_params* p, void* strea
                    "dsv4_compressor_pool: norm dtype");
   const int groups = p->s / p->ratio;
   if (groups > 0) {
-    cmp::pool_kernel<<<static_cast<unsigned>(static_cast<int64_t>(p->b) * groups), cmp::THREADS, 0,
-                       as_stream(stream)>>>(*p);
+    DSV4_CUDA_CHECK(launch_pdl(cmp::pool_kernel, dim3(static_cast<unsigned>(static_cast<int64_t>(p->b) * groups)), dim3(cmp::THREADS), 0, as_stream(stream), *p));
     DSV4_LAUNCH_CHECK("compressor pool_kernel");
   }
   if (p->ring_kv && p->ring_score) {
     dim3 g(2 * p->ratio, p->b);
-    cmp::ring_seed_kernel<<<g, 256, 0, as_stream(stream)>>>(*p);
+    DSV4_CUDA_CHECK(launch_pdl(cmp::ring_seed_kernel, dim3(g), dim3(256), 0, as_stream(stream), *p));
     DSV4_LAUNCH_CHECK("compressor ring_seed_kernel");
   }
   return DSV4_OK;
@@ -413,11 +420,11 @@ extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, vo
                  "dsv4_compressor_decode: a key image needs ratio 4, head_dim 128, fp32 out, inv, norm_max, "
                  "image_stride and a 16-byte aligned image");
   if (p->ratio == 4 && p->head_dim <= 2 * cmp::THREADS)
-    cmp::decode_r4_kernel<1><<<p->b, cmp::THREADS, 0, as_stream(stream)>>>(*p);
+    DSV4_CUDA_CHECK(launch_pdl(cmp::decode_r4_kernel<1>, dim3(p->b), dim3(cmp::THREADS), 0, as_stream(stream), *p));
   else if (p->ratio == 4)
-    cmp::decode_r4_kernel<2><<<p->b, cmp::THREADS, 0, as_stream(stream)>>>(*p);
+    DSV4_CUDA_CHECK(launch_pdl(cmp::decode_r4_kernel<2>, dim3(p->b), dim3(cmp::THREADS), 0, as_stream(stream), *p));
   else
-    cmp::decode_kernel<<<p->b, cmp::THREADS, 0, as_stream(stream)>>>(*p);
+    DSV4_CUDA_CHECK(launch_pdl(cmp::decode_kernel, dim3(p->b), dim3(cmp::THREADS), 0, as_stream(stream), *p));
   DSV4_LAUNCH_CHECK("compressor decode_kernel");
   return DSV4_OK;
 }

@@ -275,11 +275,17 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(Params P) {
 // each group accumulates in fp32 and folds with its scale, as in the tiled kernel.
 namespace sk {
 
-constexpr int ROWS = 128, THREADS = 256, BK = 64;
+// RW m16 row tiles per warp: the CTA's 128 weight rows are 8 warps x 16 rows (RW = 1) or 4 warps x
+// 32 rows (RW = 2, the tokens' fragments then serve two row tiles)
+constexpr int ROWS = 128, BK = 64;
+template <int RW>
+constexpr int threads_for() {
+  return (ROWS / (16 * RW)) * 32;
+}
 
 template <bool I8>
 struct Cfg {
-  static constexpr int NST = I8 ? 5 : 4;
+  static constexpr int NST = I8 ? 8 : 4;
   static constexpr int ROW_BYTES = BK * (I8 ? 1 : 2);
 };
 
@@ -297,12 +303,15 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
 }
 
 // two signed bytes of w (bytes 2h, 2h+1) -> bf16x2, exact: 2^23 + (b ^ 0x80) as an fp32 bit pattern,
-// minus 2^23 + 128, is b; an integer of magnitude <= 128 is its own bf16 (the fp32's upper half)
-__device__ __forceinline__ uint32_t s8x2_bf16x2(uint32_t w, int h) {
-  const uint32_t u = w ^ 0x80808080u;
-  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, h ? 0x7442 : 0x7440)) - 8388736.0f;
-  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, h ? 0x7443 : 0x7441)) - 8388736.0f;
-  return __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+// minus 2^23 + 128, is b (both subtractions in one packed f32x2 add); an integer of magnitude
+// <= 128 is its own bf16 (the fp32's upper half)
+__device__ __forceinline__ uint32_t s8x2_bf16x2(uint32_t u, int h) {  // u = w ^ 0x80808080
+  const uint32_t f0 = __byte_perm(u, 0x4B000000u, h ? 0x7442 : 0x7440);
+  const uint32_t f1 = __byte_perm(u, 0x4B000000u, h ? 0x7443 : 0x7441);
+  const uint64_t m = 0xCB000080CB000080ull;  // (-(2^23 + 128), -(2^23 + 128))
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"((static_cast<uint64_t>(f1) << 32) | f0), "l"(m));
+  return __byte_perm(static_cast<uint32_t>(d), static_cast<uint32_t>(d >> 32), 0x7632);
 }
 
 __device__ __forceinline__ void cluster_sync() {
@@ -323,7 +332,7 @@ __device__ __forceinline__ void store_y(const Params& P, int64_t off, float v) {
     reinterpret_cast<float*>(P.y)[off] = v;
 }
 
-template <bool I8, int MT>
+template <bool I8, int MT, int NT>
 __device__ __forceinline__ void load_w(const Params& P, Smem<I8, MT>& sm, int st, int n0, int kg, int g) {
   const int tid = threadIdx.x;
   constexpr int CH = Cfg<I8>::ROW_BYTES / 16;  // 16-byte chunks per weight row
@@ -331,8 +340,8 @@ __device__ __forceinline__ void load_w(const Params& P, Smem<I8, MT>& sm, int st
                       (static_cast<int64_t>(g) * P.n * P.k + static_cast<int64_t>(kg) * BK) * (I8 ? 1 : 2);
   const uint32_t ws = static_cast<uint32_t>(__cvta_generic_to_shared(sm.w[st]));
 #pragma unroll
-  for (int i = 0; i < ROWS * CH / THREADS; ++i) {
-    const int c = tid + i * THREADS;
+  for (int i = 0; i < ROWS * CH / NT; ++i) {
+    const int c = tid + i * NT;
     const int r = c / CH, ch = c % CH;
     const bool v = n0 + r < P.n;
     const uint8_t* src = wb + static_cast<int64_t>(v ? n0 + r : 0) * P.k * (I8 ? 1 : 2) + ch * 16;
@@ -340,31 +349,31 @@ __device__ __forceinline__ void load_w(const Params& P, Smem<I8, MT>& sm, int st
   }
 }
 
-template <bool I8, int MT>
+template <bool I8, int MT, int NT>
 __device__ __forceinline__ void load_x(const Params& P, Smem<I8, MT>& sm, int st, int kg, int g) {
   const int tid = threadIdx.x;
   const int64_t ldx = static_cast<int64_t>(P.groups) * P.k;
   const __nv_bfloat16* xb = P.x + static_cast<int64_t>(g) * P.k + static_cast<int64_t>(kg) * BK;
   const uint32_t xs = static_cast<uint32_t>(__cvta_generic_to_shared(sm.x[st]));
-  for (int c = tid; c < MT * 8 * 8; c += THREADS) {
+  for (int c = tid; c < MT * 8 * 8; c += NT) {
     const int t = c >> 3, ch = c & 7;
     const bool v = t < P.m;
     cp_async16(xs + t * 128 + ((ch ^ (t & 7)) << 4), xb + (v ? t : 0) * ldx + ch * 8, v);
   }
 }
 
-template <bool I8, int MT>
 __device__ __forceinline__ float load_scale(const Params& P, int n0, int kg, int g) {
   const int r = n0 + static_cast<int>(threadIdx.x);
   if (threadIdx.x >= ROWS || r >= P.n) return 0.f;
   return __bfloat162float(__ldg(P.ws + (static_cast<int64_t>(g) * P.n + r) * (P.k / BK) + kg));
 }
 
-template <bool I8, int MT>
-__global__ void __launch_bounds__(THREADS) skinny_kernel(const __grid_constant__ Params P0) {
+template <bool I8, int MT, int RW>
+__global__ void __launch_bounds__(threads_for<RW>()) skinny_kernel(const __grid_constant__ Params P0) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem<I8, MT>& sm = *reinterpret_cast<Smem<I8, MT>*>(smem_raw);
   constexpr int NST = Cfg<I8>::NST;
+  constexpr int NT = threads_for<RW>();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r = lane >> 2, q = lane & 3;
   Params P = P0;
@@ -386,33 +395,37 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(const __grid_constant__
   const int kt0 = split * per;
   const int nkt = max(0, min(per, KT - kt0));
 
-  float acc[MT][4], gacc[MT][4];
+  float acc[RW][MT][4], gacc[RW][MT][4];
 #pragma unroll
-  for (int a = 0; a < MT; ++a)
+  for (int i = 0; i < RW; ++i)
 #pragma unroll
-    for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+    for (int a = 0; a < MT; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[i][a][c] = 0.f;
 
   // the weights and their scales do not depend on the kernel before this one: their first stages
   // load while it finishes (programmatic dependent launch); the tokens load after pdl_wait()
   float sc0[NST - 1];  // the prologue's scales: all loads in flight at once
 #pragma unroll
-  for (int s = 0; s < NST - 1; ++s) sc0[s] = (I8 && s < nkt) ? load_scale<I8, MT>(P, n0, kt0 + s, g) : 0.f;
+  for (int s = 0; s < NST - 1; ++s) sc0[s] = (I8 && s < nkt) ? load_scale(P, n0, kt0 + s, g) : 0.f;
 #pragma unroll
   for (int s = 0; s < NST - 1; ++s)
-    if (s < nkt) load_w<I8, MT>(P, sm, s, n0, kt0 + s, g);
+    if (s < nkt) load_w<I8, MT, NT>(P, sm, s, n0, kt0 + s, g);
+  pdl_wait();
+#pragma unroll
+  for (int s = 0; s < NST - 1; ++s) {
+    if (s < nkt) load_x<I8, MT, NT>(P, sm, s, kt0 + s, g);
+    asm volatile("cp.async.commit_group;\n" ::);
+  }
+  // the scales are parked only now, so that their loads overlap the tokens' (the first step's
+  // barrier orders these stores before any read)
   if constexpr (I8) {
 #pragma unroll
     for (int s = 0; s < NST - 1; ++s)
       if (s < nkt && tid < ROWS) sm.scale[s][tid] = sc0[s];
   }
-  pdl_wait();
-#pragma unroll
-  for (int s = 0; s < NST - 1; ++s) {
-    if (s < nkt) load_x<I8, MT>(P, sm, s, kt0 + s, g);
-    asm volatile("cp.async.commit_group;\n" ::);
-  }
 
-  const int wrow = warp * 16 + r;  // this lane's weight rows: wrow, wrow + 8
+  const int wrow = warp * 16 * RW + r;  // this lane's weight rows: wrow + 16 i + {0, 8}
   // a stage's scale is loaded with its tiles (NST - 1 steps ahead) but parked in shared memory two
   // steps later, so that no step waits on the load: sc_1, sc_2 are the loads of the last two steps
   float sc_1 = 0.f, sc_2 = 0.f;
@@ -424,29 +437,15 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(const __grid_constant__
     const int nk = it + NST - 1;
     float sc_next = 0.f;
     if (nk < nkt) {
-      load_w<I8, MT>(P, sm, nk % NST, n0, kt0 + nk, g);
-      load_x<I8, MT>(P, sm, nk % NST, kt0 + nk, g);
-      if constexpr (I8) sc_next = load_scale<I8, MT>(P, n0, kt0 + nk, g);
+      load_w<I8, MT, NT>(P, sm, nk % NST, n0, kt0 + nk, g);
+      load_x<I8, MT, NT>(P, sm, nk % NST, kt0 + nk, g);
+      if constexpr (I8) sc_next = load_scale(P, n0, kt0 + nk, g);
     }
     asm volatile("cp.async.commit_group;\n" ::);
 
-    // operands of this lane: 16 k of rows wrow and wrow + 8, 16 k of its tokens
     const uint32_t wsm = static_cast<uint32_t>(__cvta_generic_to_shared(sm.w[st]));
     const uint32_t xsm = static_cast<uint32_t>(__cvta_generic_to_shared(sm.x[st]));
-    uint32_t w0[8], w1[8];  // I8: words 0..3 used (4 bytes each); bf16: 8 words of k pairs
-    if constexpr (I8) {
-      const uint4 a = lds128(wsm + wrow * 64 + q * 16), b = lds128(wsm + (wrow + 8) * 64 + q * 16);
-      w0[0] = a.x; w0[1] = a.y; w0[2] = a.z; w0[3] = a.w;
-      w1[0] = b.x; w1[1] = b.y; w1[2] = b.z; w1[3] = b.w;
-    } else {
-      const int r0 = wrow, r1 = wrow + 8;
-      const uint4 a0 = lds128(wsm + r0 * 128 + (((2 * q) ^ (r0 & 7)) << 4));
-      const uint4 a1 = lds128(wsm + r0 * 128 + (((2 * q + 1) ^ (r0 & 7)) << 4));
-      const uint4 b0 = lds128(wsm + r1 * 128 + (((2 * q) ^ (r1 & 7)) << 4));
-      const uint4 b1 = lds128(wsm + r1 * 128 + (((2 * q + 1) ^ (r1 & 7)) << 4));
-      w0[0] = a0.x; w0[1] = a0.y; w0[2] = a0.z; w0[3] = a0.w; w0[4] = a1.x; w0[5] = a1.y; w0[6] = a1.z; w0[7] = a1.w;
-      w1[0] = b0.x; w1[1] = b0.y; w1[2] = b0.z; w1[3] = b0.w; w1[4] = b1.x; w1[5] = b1.y; w1[6] = b1.z; w1[7] = b1.w;
-    }
+    // the tokens' operands: 16 k of each of this lane's tokens
     uint32_t xw[MT][8];
 #pragma unroll
     for (int nt = 0; nt < MT; ++nt) {
@@ -457,39 +456,60 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(const __grid_constant__
       xw[nt][4] = b.x; xw[nt][5] = b.y; xw[nt][6] = b.z; xw[nt][7] = b.w;
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t af[4];
+    for (int i = 0; i < RW; ++i) {
+      // 16 k of rows wrow + 16 i and wrow + 16 i + 8
+      const int r0 = wrow + 16 * i, r1 = r0 + 8;
+      uint32_t w0[8], w1[8];  // I8: words 0..3 (4 bytes each, biased by 0x80); bf16: 8 words of k pairs
       if constexpr (I8) {
-        af[0] = s8x2_bf16x2(w0[j], 0);
-        af[1] = s8x2_bf16x2(w1[j], 0);
-        af[2] = s8x2_bf16x2(w0[j], 1);
-        af[3] = s8x2_bf16x2(w1[j], 1);
+        const uint4 a = lds128(wsm + r0 * 64 + q * 16), b = lds128(wsm + r1 * 64 + q * 16);
+        w0[0] = a.x ^ 0x80808080u; w0[1] = a.y ^ 0x80808080u; w0[2] = a.z ^ 0x80808080u; w0[3] = a.w ^ 0x80808080u;
+        w1[0] = b.x ^ 0x80808080u; w1[1] = b.y ^ 0x80808080u; w1[2] = b.z ^ 0x80808080u; w1[3] = b.w ^ 0x80808080u;
       } else {
-        af[0] = w0[2 * j];
-        af[1] = w1[2 * j];
-        af[2] = w0[2 * j + 1];
-        af[3] = w1[2 * j + 1];
+        const uint4 a0 = lds128(wsm + r0 * 128 + (((2 * q) ^ (r0 & 7)) << 4));
+        const uint4 a1 = lds128(wsm + r0 * 128 + (((2 * q + 1) ^ (r0 & 7)) << 4));
+        const uint4 b0 = lds128(wsm + r1 * 128 + (((2 * q) ^ (r1 & 7)) << 4));
+        const uint4 b1 = lds128(wsm + r1 * 128 + (((2 * q + 1) ^ (r1 & 7)) << 4));
+        w0[0] = a0.x; w0[1] = a0.y; w0[2] = a0.z; w0[3] = a0.w; w0[4] = a1.x; w0[5] = a1.y; w0[6] = a1.z; w0[7] = a1.w;
+        w1[0] = b0.x; w1[1] = b0.y; w1[2] = b0.z; w1[3] = b0.w; w1[4] = b1.x; w1[5] = b1.y; w1[6] = b1.z; w1[7] = b1.w;
       }
 #pragma unroll
-      for (int nt = 0; nt < MT; ++nt) {
+      for (int j = 0; j < 4; ++j) {
+        uint32_t af[4];
         if constexpr (I8) {
-          if (j == 0)  // the group's first k step starts its partial from zero
-            mma_bf16_z(gacc[nt], af, xw[nt][0], xw[nt][1]);
-          else
-            mma_bf16(gacc[nt], af, xw[nt][2 * j], xw[nt][2 * j + 1]);
-        } else
-          mma_bf16(acc[nt], af, xw[nt][2 * j], xw[nt][2 * j + 1]);
+          af[0] = s8x2_bf16x2(w0[j], 0);
+          af[1] = s8x2_bf16x2(w1[j], 0);
+          af[2] = s8x2_bf16x2(w0[j], 1);
+          af[3] = s8x2_bf16x2(w1[j], 1);
+        } else {
+          af[0] = w0[2 * j];
+          af[1] = w1[2 * j];
+          af[2] = w0[2 * j + 1];
+          af[3] = w1[2 * j + 1];
+        }
+#pragma unroll
+        for (int nt = 0; nt < MT; ++nt) {
+          if constexpr (I8) {
+            if (j == 0)  // the group's first k step starts its partial from zero
+              mma_bf16_z(gacc[i][nt], af, xw[nt][0], xw[nt][1]);
+            else
+              mma_bf16(gacc[i][nt], af, xw[nt][2 * j], xw[nt][2 * j + 1]);
+          } else {
+            mma_bf16(acc[i][nt], af, xw[nt][2 * j], xw[nt][2 * j + 1]);
+          }
+        }
+      }
+      if constexpr (I8) {
+        const float s0 = sm.scale[st][r0], s1 = sm.scale[st][r1];
+#pragma unroll
+        for (int nt = 0; nt < MT; ++nt) {
+          acc[i][nt][0] = fmaf(gacc[i][nt][0], s0, acc[i][nt][0]);
+          acc[i][nt][1] = fmaf(gacc[i][nt][1], s0, acc[i][nt][1]);
+          acc[i][nt][2] = fmaf(gacc[i][nt][2], s1, acc[i][nt][2]);
+          acc[i][nt][3] = fmaf(gacc[i][nt][3], s1, acc[i][nt][3]);
+        }
       }
     }
     if constexpr (I8) {
-      const float s0 = sm.scale[st][wrow], s1 = sm.scale[st][wrow + 8];
-#pragma unroll
-      for (int nt = 0; nt < MT; ++nt) {
-        acc[nt][0] = fmaf(gacc[nt][0], s0, acc[nt][0]);
-        acc[nt][1] = fmaf(gacc[nt][1], s0, acc[nt][1]);
-        acc[nt][2] = fmaf(gacc[nt][2], s1, acc[nt][2]);
-        acc[nt][3] = fmaf(gacc[nt][3], s1, acc[nt][3]);
-      }
       // the scale loaded two steps ago, for stage it + NST - 3 (read at step it + NST - 3 >= it + 1,
       // after the next barrier; its slot was last read at step it - 3)
       if (it >= 2 && it + NST - 3 < nkt && tid < ROWS) sm.scale[(it + NST - 3) % NST][tid] = sc_2;
@@ -500,22 +520,24 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(const __grid_constant__
   asm volatile("cp.async.wait_group 0;\n" ::);
   pdl_trigger();
 
-  // D fragment: c0, c1 = (row wrow, tokens 2q, 2q+1 of the tile), c2, c3 = row wrow + 8
+  // D fragment: c0, c1 = (row wrow + 16 i, tokens 2q, 2q+1 of the tile), c2, c3 = row + 8
   const int64_t ldy = static_cast<int64_t>(P.groups) * P.n;
   if (P.ksplit == 1) {
 #pragma unroll
-    for (int nt = 0; nt < MT; ++nt)
+    for (int i = 0; i < RW; ++i)
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int f = n0 + wrow + hf * 8;
-        if (f >= P.n) continue;
+      for (int nt = 0; nt < MT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int64_t t = nt * 8 + 2 * q + e;
-          if (t >= P.m) continue;
-          store_y(P, t * ldy + static_cast<int64_t>(g) * P.n + f, acc[nt][hf * 2 + e]);
+        for (int hf = 0; hf < 2; ++hf) {
+          const int f = n0 + wrow + 16 * i + hf * 8;
+          if (f >= P.n) continue;
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int64_t t = nt * 8 + 2 * q + e;
+            if (t >= P.m) continue;
+            store_y(P, t * ldy + static_cast<int64_t>(g) * P.n + f, acc[i][nt][hf * 2 + e]);
+          }
         }
-      }
     return;
   }
   // k split over the CTAs of this cluster: each parks its partial tile in shared memory, then CTA
@@ -526,16 +548,19 @@ __global__ void __launch_bounds__(THREADS) skinny_kernel(const __grid_constant__
   float* red = reinterpret_cast<float*>(sm.w);
   __syncthreads();  // every warp is done with the ring
 #pragma unroll
-  for (int nt = 0; nt < MT; ++nt)
+  for (int i = 0; i < RW; ++i)
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf)
+    for (int nt = 0; nt < MT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) red[(wrow + hf * 8) * LD + nt * 8 + 2 * q + e] = acc[nt][hf * 2 + e];
+      for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          red[(wrow + 16 * i + hf * 8) * LD + nt * 8 + 2 * q + e] = acc[i][nt][hf * 2 + e];
   cluster_sync();
   const int rows_per = ROWS / P.ksplit;
   const uint32_t red_s = static_cast<uint32_t>(__cvta_generic_to_shared(red));
-  for (int i = tid; i < rows_per * MT * 8; i += THREADS) {
-    const int row = split * rows_per + i / (MT * 8), t = i % (MT * 8);
+  for (int i = tid; i < rows_per * MT * 8; i += NT) {
+    const int row = split * rows_per + i / (MT * 8), t = i % (MT * 8);  // a warp reads 128 B of a peer
     const uint32_t off = static_cast<uint32_t>((row * LD + t) * 4);
     float v = 0.f;
     for (int r2 = 0; r2 < P.ksplit; ++r2) v += ld_dsmem_f32(red_s + off, r2);
@@ -624,17 +649,20 @@ using namespace dsv4;
 
 template <bool I8, int MT>
 static int launch_skinny_mt(const gm::Params& P, void* stream) {
+  // int8 weights: 32 rows per warp (the tokens' fragments serve two row tiles); bf16: 16
+  constexpr int RW = I8 ? 2 : 1;
+  const auto kern = gm::sk::skinny_kernel<I8, MT, RW>;
   static bool set = false;
   const int smem = sizeof(gm::sk::Smem<I8, MT>);
   if (!set) {
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(gm::sk::skinny_kernel<I8, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    DSV4_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     set = true;
   }
   cudaLaunchConfig_t cfg = {};
   const int tiles = P.nprob > 0 ? P.prob[P.nprob - 1].tile0 + (P.prob[P.nprob - 1].n + gm::sk::ROWS - 1) / gm::sk::ROWS
                                 : (P.n + gm::sk::ROWS - 1) / gm::sk::ROWS;
   cfg.gridDim = dim3(tiles, 1, P.groups * P.ksplit);
-  cfg.blockDim = dim3(gm::sk::THREADS);
+  cfg.blockDim = dim3(gm::sk::threads_for<RW>());
   cfg.dynamicSmemBytes = smem;
   cfg.stream = as_stream(stream);
   cudaLaunchAttribute attr[2];
@@ -646,7 +674,7 @@ static int launch_skinny_mt(const gm::Params& P, void* stream) {
   attr[1].val.clusterDim.z = P.ksplit;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  DSV4_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gm::sk::skinny_kernel<I8, MT>, P));
+  DSV4_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, P));
   DSV4_LAUNCH_CHECK("skinny_kernel");
   return DSV4_OK;
 }

@@ -29,6 +29,8 @@ __device__ __forceinline__ void store4(void* p, int64_t i, int dtype, float4 v) 
 // memory pipes, where one warp per row would serialise the row's loads on a few SMs
 template <int VPT>
 __global__ void __launch_bounds__(256) rmsnorm_row_kernel(dsv4_rmsnorm_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
   __shared__ float part[8];
   const int tid = threadIdx.x, nt = blockDim.x;
   const int64_t base = static_cast<int64_t>(blockIdx.x) * p.dim;
@@ -64,6 +66,8 @@ __global__ void __launch_bounds__(256) rmsnorm_row_kernel(dsv4_rmsnorm_params p)
 
 // generic RMSNorm, any dim (multiple of 2), one warp per row, two passes over L1-resident data
 __global__ void rmsnorm_kernel(dsv4_rmsnorm_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= p.rows) return;
@@ -83,6 +87,8 @@ __global__ void rmsnorm_kernel(dsv4_rmsnorm_params p) {
 }
 
 __global__ void rope_kernel(dsv4_rope_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
   const int half = p.rope_dim / 2;
   const int64_t total = p.s * p.heads * half;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
@@ -110,6 +116,8 @@ __global__ void rope_kernel(dsv4_rope_params p) {
 
 // also copies the non-rope part when out != x
 __global__ void copy_nonrope_kernel(dsv4_rope_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
   const int keep = p.dim - p.rope_dim;
   const int64_t total = p.s * p.heads * keep;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
@@ -123,6 +131,8 @@ __global__ void copy_nonrope_kernel(dsv4_rope_params p) {
 // fused norm + rope + cast for rows of DIM (compile-time) elements: one warp per (row, head).
 template <int DIM>
 __global__ void norm_rope_kernel(dsv4_norm_rope_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
   constexpr int PER = DIM / 32;  // contiguous elements per lane
   const int lane = threadIdx.x & 31;
   const int64_t unit = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -220,19 +230,19 @@ extern "C" int dsv4_rmsnorm(const dsv4_rmsnorm_params* p, void* stream) {
     const int vpt = (p->dim / 4 + threads - 1) / threads;  // <= 8
     const dim3 grid(static_cast<unsigned>(p->rows));
     if (vpt <= 1)
-      nr::rmsnorm_row_kernel<1><<<grid, threads, 0, as_stream(stream)>>>(*p);
+      DSV4_CUDA_CHECK(launch_pdl(nr::rmsnorm_row_kernel<1>, dim3(grid), dim3(threads), 0, as_stream(stream), *p));
     else if (vpt <= 2)
-      nr::rmsnorm_row_kernel<2><<<grid, threads, 0, as_stream(stream)>>>(*p);
+      DSV4_CUDA_CHECK(launch_pdl(nr::rmsnorm_row_kernel<2>, dim3(grid), dim3(threads), 0, as_stream(stream), *p));
     else if (vpt <= 4)
-      nr::rmsnorm_row_kernel<4><<<grid, threads, 0, as_stream(stream)>>>(*p);
+      DSV4_CUDA_CHECK(launch_pdl(nr::rmsnorm_row_kernel<4>, dim3(grid), dim3(threads), 0, as_stream(stream), *p));
     else
-      nr::rmsnorm_row_kernel<8><<<grid, threads, 0, as_stream(stream)>>>(*p);
+      DSV4_CUDA_CHECK(launch_pdl(nr::rmsnorm_row_kernel<8>, dim3(grid), dim3(threads), 0, as_stream(stream), *p));
     DSV4_LAUNCH_CHECK("rmsnorm_row_kernel");
     return DSV4_OK;
   }
   const int warps = 8;
   int64_t blocks = (p->rows + warps - 1) / warps;
-  nr::rmsnorm_kernel<<<static_cast<unsigned>(blocks), warps * 32, 0, as_stream(stream)>>>(*p);
+  DSV4_CUDA_CHECK(launch_pdl(nr::rmsnorm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(warps * 32), 0, as_stream(stream), *p));
   DSV4_LAUNCH_CHECK("rmsnorm_kernel");
   return DSV4_OK;
 }
@@ -249,10 +259,10 @@ extern "C" int dsv4_rope(const dsv4_rope_params* p, void* stream) {
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 16 * num_sms()) blocks = 16 * num_sms();
   if (p->out != p->x && p->dim > p->rope_dim) {
-    nr::copy_nonrope_kernel<<<blocks, 256, 0, as_stream(stream)>>>(*p);
+    DSV4_CUDA_CHECK(launch_pdl(nr::copy_nonrope_kernel, dim3(blocks), dim3(256), 0, as_stream(stream), *p));
     DSV4_LAUNCH_CHECK("copy_nonrope_kernel");
   }
-  nr::rope_kernel<<<blocks, 256, 0, as_stream(stream)>>>(*p);
+  DSV4_CUDA_CHECK(launch_pdl(nr::rope_kernel, dim3(blocks), dim3(256), 0, as_stream(stream), *p));
   DSV4_LAUNCH_CHECK("rope_kernel");
   return DSV4_OK;
 }
@@ -271,13 +281,13 @@ extern "C" int dsv4_norm_rope(const dsv4_norm_rope_params* p, void* stream) {
   const unsigned blocks = static_cast<unsigned>((units + warps - 1) / warps);
   switch (p->dim) {
     case 512:
-      nr::norm_rope_kernel<512><<<blocks, warps * 32, 0, as_stream(stream)>>>(*p);
+      DSV4_CUDA_CHECK(launch_pdl(nr::norm_rope_kernel<512>, dim3(blocks), dim3(warps * 32), 0, as_stream(stream), *p));
       break;
     case 256:
-      nr::norm_rope_kernel<256><<<blocks, warps * 32, 0, as_stream(stream)>>>(*p);
+      DSV4_CUDA_CHECK(launch_pdl(nr::norm_rope_kernel<256>, dim3(blocks), dim3(warps * 32), 0, as_stream(stream), *p));
       break;
     case 128:
-      nr::norm_rope_kernel<128><<<blocks, warps * 32, 0, as_stream(stream)>>>(*p);
+      DSV4_CUDA_CHECK(launch_pdl(nr::norm_rope_kernel<128>, dim3(blocks), dim3(warps * 32), 0, as_stream(stream), *p));
       break;
     default:
       set_error("dsv4_norm_rope: dim %d unsupported (128/256/512)", p->dim);
