@@ -150,11 +150,13 @@ def _side_stream(device):
 class DecodeRunner:
     """CUDA-graph-backed decode attention for a fixed batch: the serving-loop entry point.
 
-    The first call captures `decode_attention` on static device buffers into a CUDA graph (the
+    The first call captures `decode_attention` on static device buffers into CUDA graphs (the
     reference's per-token path is a Python loop of library calls, oracle/v4_fast.py:82-122; here one
-    graph launch replays the five kernels). `step_device` replays with inputs already on the device;
-    `step_host` copies this token's inputs from pinned host memory, replays, and copies the output
-    back to pinned host memory, all ordered on the runner's stream.
+    graph launch replays the kernels). `step_device` replays with inputs already on the device.
+    `step_host` runs a second graph that also holds the step's copies: this token's inputs from one
+    pinned host block to the device (one copy: q, q_idx, w_idx and positions sit at fixed offsets of
+    both blocks), the kernels, and the output back to pinned host memory, so a step is one launch.
+    Callers that write their inputs straight into `host_inputs()` skip the host-side staging copy.
     """
 
     def __init__(self, cache, sink, top_k=512, device="cuda", out_dtype=torch.bfloat16, stream=None):
@@ -162,22 +164,30 @@ class DecodeRunner:
         b = cache.batch
         dev = torch.device(device)
         self.sink = sink.float().contiguous().to(dev)
-        self.q = torch.zeros((b, 64, cache.head_dim), dtype=torch.float32, device=dev)
-        self.q_idx = torch.zeros((b, 64, 128), dtype=torch.float32, device=dev)
-        self.w_idx = torch.zeros((b, 64), dtype=torch.float32, device=dev)
-        self.positions = torch.zeros((b,), dtype=torch.int32, device=dev)
+        shapes = [((b, 64, cache.head_dim), torch.float32), ((b, 64, 128), torch.float32), ((b, 64), torch.float32),
+                  ((b,), torch.int32)]
+        offs, total = [], 0
+        for shape, dt in shapes:  # 256-byte aligned fields of one block
+            offs.append(total)
+            total += -(-math.prod(shape) * torch.empty((), dtype=dt).element_size() // 256) * 256
+        self._in_bytes = total
+        self.d_in = torch.zeros(total, dtype=torch.uint8, device=dev)
+        self.h_in = torch.zeros(total, dtype=torch.uint8).pin_memory()
+
+        def views(buf):
+            return [buf[o:o + math.prod(sh) * torch.empty((), dtype=dt).element_size()].view(dt).view(sh)
+                    for o, (sh, dt) in zip(offs, shapes)]
+        self.q, self.q_idx, self.w_idx, self.positions = views(self.d_in)
+        self.h_q, self.h_qi, self.h_w, self.h_pos = views(self.h_in)
         self.idx = attention_index_buffer(b, cache.window, top_k, dev)
         self.freqs = rope_freqs(64, dev)
         self.out_dtype = out_dtype
         self.out = None
         self.graph = None
+        self.graph_host = None
         self.stream = stream or torch.cuda.Stream(dev)
-        self.h_q = torch.zeros(self.q.shape, dtype=torch.float32).pin_memory()
-        self.h_qi = torch.zeros(self.q_idx.shape, dtype=torch.float32).pin_memory()
-        self.h_w = torch.zeros(self.w_idx.shape, dtype=torch.float32).pin_memory()
-        self.h_pos = torch.zeros(self.positions.shape, dtype=torch.int32).pin_memory()
         self.h_out = None
-        self._h2d_done = None
+        self._done = None
 
     def _body(self):
         return decode_attention(self.cache, self.q, self.q_idx, self.w_idx, self.sink, self.positions, self.top_k,
@@ -191,6 +201,16 @@ class DecodeRunner:
         with torch.cuda.graph(self.graph, stream=self.stream):
             self.out = self._body()
         self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.graph_host = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph_host, stream=self.stream):
+            self.d_in.copy_(self.h_in, non_blocking=True)
+            out = self._body()
+            self.h_out.copy_(out, non_blocking=True)
+        self.out_host_graph = out
+
+    def host_inputs(self):
+        """The pinned host views (q, q_idx, w_idx, positions) that `step_host` copies from."""
+        return self.h_q, self.h_qi, self.h_w, self.h_pos
 
     def step_device(self):
         if self.graph is None:
@@ -201,31 +221,28 @@ class DecodeRunner:
         return self.out
 
     def step_host(self, q, q_idx, w_idx, positions):
-        """Host tensors in, host tensor out, ordered on the runner's stream. Pinned inputs are copied
-        directly; other host tensors are staged through pinned buffers (waiting for the previous
-        step's copies first). The returned pinned output is valid after `synchronize()` and until
-        the next step."""
+        """Host tensors in, host tensor out, as one graph launch on the runner's stream (input copy,
+        kernels, output copy). Inputs that are not the `host_inputs()` views are first copied into
+        them (after the previous step has finished with them). The returned pinned output is valid
+        after `synchronize()` and until the next step."""
         if self.graph is None:
             self.capture()
         srcs = (q, q_idx, w_idx, positions)
-        if not all(t.is_pinned() for t in srcs):
-            if self._h2d_done is not None:
-                self._h2d_done.synchronize()
-            for dst, src in zip((self.h_q, self.h_qi, self.h_w, self.h_pos), srcs):
+        mine = (self.h_q, self.h_qi, self.h_w, self.h_pos)
+        if not all(a.data_ptr() == b.data_ptr() and a.shape == b.shape for a, b in zip(srcs, mine)):
+            if self._done is not None:
+                self._done.synchronize()
+            for dst, src in zip(mine, srcs):
                 dst.copy_(src)
-            srcs = (self.h_q, self.h_qi, self.h_w, self.h_pos)
         with torch.cuda.stream(self.stream):
-            for dst, src in zip((self.q, self.q_idx, self.w_idx, self.positions), srcs):
-                dst.copy_(src, non_blocking=True)
-            if self._h2d_done is None:
-                self._h2d_done = torch.cuda.Event()
-            self._h2d_done.record(self.stream)
-            self.graph.replay()
-            self.h_out.copy_(self.out, non_blocking=True)
+            self.graph_host.replay()
+            if self._done is None:
+                self._done = torch.cuda.Event()
+            self._done.record(self.stream)
         return self.h_out
 
     def h2d_bytes(self):
-        return sum(t.numel() * t.element_size() for t in (self.q, self.q_idx, self.w_idx, self.positions))
+        return self._in_bytes
 
     def d2h_bytes(self):
         return self.out.numel() * self.out.element_size() if self.out is not None else 0

@@ -88,7 +88,15 @@ def test_decode_runner_graph_and_host_path(dsv4):
                                 out_dtype=torch.float32)
     torch.testing.assert_close(dev_out, ref, rtol=0, atol=0)
     h = case.host
-    out = r.step_host(h["q"], h["q_idx"], h["w_idx"], h["positions"])
+    out = r.step_host(h["q"], h["q_idx"], h["w_idx"], h["positions"])   # staged through host_inputs()
+    r.synchronize()
+    torch.testing.assert_close(out, ref.cpu(), rtol=0, atol=0)
+    # the zero-copy path: inputs written straight into the runner's pinned block
+    r.synchronize()
+    out.zero_()
+    for dst, key in zip(r.host_inputs(), ("q", "q_idx", "w_idx", "positions")):
+        dst.copy_(h[key])
+    out = r.step_host(*r.host_inputs())
     r.synchronize()
     torch.testing.assert_close(out, ref.cpu(), rtol=0, atol=0)
 
