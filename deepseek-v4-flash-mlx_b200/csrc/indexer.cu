@@ -23,14 +23,14 @@ namespace idx {
 
 constexpr int DI = 128;         // indexer head dim
 constexpr int HI = 64;          // indexer heads
-constexpr int KT = 32;          // keys per score CTA (decode)
+constexpr int KT = 64;          // keys per score CTA (decode)
 constexpr int THREADS = 256;
 
 struct ScoreSmem {
-  alignas(16) float q[HI * DI];   // swizzled 16-byte chunks
-  alignas(16) float k[KT * DI];
+  alignas(16) float q[HI * DI];   // [head][dim], 16-byte chunk c of row r at c ^ ((r / 4) % 8)
+  alignas(16) float k[KT * DI];   // [key][dim], the same swizzle
   float w[HI];
-  float red[4][KT];
+  float red[THREADS / 32][KT];    // tree level 0 per warp and key
 };
 
 __device__ __forceinline__ int swz_chunk(int r, int c) { return c ^ ((r >> 2) & 7); }
@@ -58,13 +58,13 @@ __device__ __forceinline__ int visible_keys(const int32_t* positions, int64_t qr
   return nv < n_keys ? (nv < 0 ? 0 : nv) : n_keys;
 }
 
-// grid: (batch*s, key tiles of KT = 32). 256 threads: thread = (head quad hq, key pair jq);
-// lane = hq_lo<<3 | jq_lo, warp = hq_hi<<1 | jq_hi, so a thread owns heads 4*hq..4*hq+3 and keys
-// 2*jq, 2*jq+1 of the tile. Two keys per thread (rather than four) doubles the threads of a decode
-// query (8192 keys -> 256 CTAs) so that each SM holds enough warps to hide FMA and shared-memory
-// latency; the fp32 operation order per (head, key) is unchanged.
-__device__ __forceinline__ int swz_pair(int r, int c) { return c ^ ((r >> 1) & 7); }
-
+// grid: (batch*s, key tiles of KT = 64). 256 threads: thread = (head quad hq, key quad kq) with
+// lane = (hq & 1) << 4 | kq, warp = hq >> 1: a thread owns heads 4hq..4hq+3 and keys 4kq..4kq+3 of
+// the tile, 16 accumulators. A 4-dim step loads 4 q chunks (two distinct per warp: shared-memory
+// broadcasts) and 4 key chunks for 64 FMAs, so the step is bound by the FMA pipe rather than by
+// shared-memory bandwidth. Per (head, key) the dot product is one sequential fmaf chain over the
+// 128 dims; the thread's four heads fold (ascending) into the partial P[hq] of the canonical order,
+// whose balanced tree is level 0 across lane bit 4 and levels 1-3 across warps.
 __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
   extern __shared__ __align__(16) uint8_t score_smem[];
   ScoreSmem& sm = *reinterpret_cast<ScoreSmem*>(score_smem);
@@ -82,79 +82,71 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
   const uint32_t qs = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
   const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(sm.k));
   for (int c = tid; c < HI * DI / 4; c += THREADS) {
-    int r = c >> 5, ch = c & 31;
-    cp_async16(qs + (r * 32 + swz_pair(r, ch)) * 16, qg + r * DI + ch * 4, true);
+    const int r = c >> 5, ch = c & 31;
+    cp_async16(qs + (r * 32 + swz_chunk(r, ch)) * 16, qg + r * DI + ch * 4, true);
   }
   for (int c = tid; c < KT * DI / 4; c += THREADS) {
-    int r = c >> 5, ch = c & 31;
-    bool valid = (j0 + r) < nvis;
+    const int r = c >> 5, ch = c & 31;
+    const bool valid = (j0 + r) < nvis;
     const float* src = kg + static_cast<int64_t>(valid ? j0 + r : 0) * DI + ch * 4;
-    cp_async16(ks + (r * 32 + swz_pair(r, ch)) * 16, src, valid);
+    cp_async16(ks + (r * 32 + swz_chunk(r, ch)) * 16, src, valid);
   }
   asm volatile("cp.async.commit_group;\n" ::);
   if (tid < HI) sm.w[tid] = P.w[qrow * HI + tid];
   asm volatile("cp.async.wait_group 0;\n" ::);
   __syncthreads();
 
-  const int hq = ((warp >> 1) << 2) | (lane >> 3);
-  const int jq = ((warp & 1) << 3) | (lane & 7);
-  float acc[4][2];
+  const int hq = (warp << 1) | (lane >> 4), kq = lane & 15;
+  float acc[4][4];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int c = 0; c < 2; ++c) acc[a][c] = 0.f;
-
-#pragma unroll 4
+    for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+#pragma unroll 2
   for (int ch = 0; ch < DI / 4; ++ch) {
-    float4 qv[4], kv[2];
+    float4 qv[4], kv[4];
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
-      int r = hq * 4 + a;
-      qv[a] = *reinterpret_cast<const float4*>(&sm.q[(r * 32 + swz_pair(r, ch)) * 4]);
+      const int r = hq * 4 + a;
+      qv[a] = *reinterpret_cast<const float4*>(&sm.q[(r * 32 + swz_chunk(r, ch)) * 4]);
     }
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      int r = jq * 2 + c;
-      kv[c] = *reinterpret_cast<const float4*>(&sm.k[(r * 32 + swz_pair(r, ch)) * 4]);
+    for (int c = 0; c < 4; ++c) {
+      const int r = kq * 4 + c;
+      kv[c] = *reinterpret_cast<const float4*>(&sm.k[(r * 32 + swz_chunk(r, ch)) * 4]);
     }
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         acc[a][c] = __fmaf_rn(qv[a].x, kv[c].x, acc[a][c]);
         acc[a][c] = __fmaf_rn(qv[a].y, kv[c].y, acc[a][c]);
         acc[a][c] = __fmaf_rn(qv[a].z, kv[c].z, acc[a][c]);
         acc[a][c] = __fmaf_rn(qv[a].w, kv[c].w, acc[a][c]);
       }
   }
-  // fold this thread's four heads (ascending) per key
-  float part[2];
+  // P[hq] per key: the thread's four heads, ascending; tree level 0 across hq bit 0 (lane bit 4)
+  float part[4];
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
+  for (int c = 0; c < 4; ++c) {
     float p = 0.f;
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
-      float d = acc[a][c];
-      float r = d > 0.f ? d : 0.f;
-      p = __fmaf_rn(sm.w[hq * 4 + a], r, p);
+      const float d = acc[a][c];
+      p = __fmaf_rn(sm.w[hq * 4 + a], d > 0.f ? d : 0.f, p);
     }
-    part[c] = p;
+    part[c] = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 16));
   }
-  // tree levels 0 and 1 over hq bits 0,1 (lane bits 3,4)
+  if (lane < 16) {
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    part[c] = __fadd_rn(part[c], __shfl_xor_sync(0xffffffffu, part[c], 8));
-    part[c] = __fadd_rn(part[c], __shfl_xor_sync(0xffffffffu, part[c], 16));
-  }
-  // levels 2 and 3 over hq bits 2,3 (warp bits 1,2)
-  if ((lane >> 3) == 0) {
-#pragma unroll
-    for (int c = 0; c < 2; ++c) sm.red[warp >> 1][jq * 2 + c] = part[c];
+    for (int c = 0; c < 4; ++c) sm.red[warp][kq * 4 + c] = part[c];
   }
   __syncthreads();
-  if (tid < KT) {
+  if (tid < KT) {  // levels 1-3: hq bits 1-3 are the warp's bits 0-2
     const int j = j0 + tid;
-    float v = __fadd_rn(__fadd_rn(sm.red[0][tid], sm.red[1][tid]), __fadd_rn(sm.red[2][tid], sm.red[3][tid]));
+    const float l1a = __fadd_rn(sm.red[0][tid], sm.red[1][tid]), l1b = __fadd_rn(sm.red[2][tid], sm.red[3][tid]);
+    const float l1c = __fadd_rn(sm.red[4][tid], sm.red[5][tid]), l1d = __fadd_rn(sm.red[6][tid], sm.red[7][tid]);
+    const float v = __fadd_rn(__fadd_rn(l1a, l1b), __fadd_rn(l1c, l1d));
     if (j < nvis) P.scores[qrow * P.n_pad + j] = v;
   }
 }
@@ -400,6 +392,33 @@ __device__ __forceinline__ int32_t map_key(const SelectParams& P, int b, int j) 
   return static_cast<int32_t>(row + P.out_offset);
 }
 
+// map_key for the PER contiguous keys j0 .. j0 + PER - 1 of one thread: with pages of at least PER
+// keys they lie on at most two pages, whose table entries are read once up front (the writes of the
+// selection then need no dependent global loads)
+struct KeyMap {
+  int64_t off0 = 0, off1 = 0;  // pool row - key index on the first / second page, + out_offset
+  int split = 0x7fffffff;      // first key index on the second page
+  bool direct;                 // false: map through map_key
+  __device__ __forceinline__ KeyMap(const SelectParams& P, int b, int j0, int per) {
+    direct = P.block_table == nullptr || P.page >= per;
+    if (P.block_table == nullptr) {
+      off0 = off1 = P.out_offset;
+    } else if (direct) {
+      const int last = max(0, P.table_stride - 1);
+      const int pg0 = min(j0 / P.page, last);
+      const int pg1 = min((j0 + per - 1) / P.page, last);
+      const int32_t* t = P.block_table + static_cast<int64_t>(b) * P.table_stride;
+      off0 = (static_cast<int64_t>(__ldg(t + pg0)) - pg0) * P.page + P.out_offset;
+      off1 = (static_cast<int64_t>(__ldg(t + pg1)) - pg1) * P.page + P.out_offset;
+      split = (pg0 + 1) * P.page;
+    }
+  }
+  __device__ __forceinline__ int32_t map(const SelectParams& P, int b, int j) const {
+    if (!direct) return map_key(P, b, j);
+    return static_cast<int32_t>(j + (j < split ? off0 : off1));
+  }
+};
+
 struct SelShared {
   uint32_t hist[SEL_BINS];
   uint32_t warp_sum[SEL_THREADS / 32];
@@ -611,6 +630,7 @@ struct SelRegShared {
   uint32_t warp_sum[SEL_THREADS / 32];
   uint32_t total, bin, need;
   int32_t tau_last;
+  uint32_t ncand, tau_key;
 };
 
 __device__ __forceinline__ uint32_t block_scan_reg(uint32_t v, SelRegShared& sh) {
@@ -859,7 +879,8 @@ __device__ __forceinline__ void rescore_band(const float* kb, int cnt, RefineSme
 
 template <int PER>
 __device__ __forceinline__ bool refine_band(const SelectParams& P, int64_t qrow, int b, int k, uint32_t (&key)[PER],
-                                            int nv, int j0, SelRegShared& sh, RefineSmem& rs, int32_t* out) {
+                                            int nv, int j0, SelRegShared& sh, RefineSmem& rs, int32_t* out,
+                                            const KeyMap& km) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // the query's q (64 x 128) streams into shared memory while the radix runs
   {
@@ -971,7 +992,7 @@ __device__ __forceinline__ bool refine_band(const SelectParams& P, int64_t qrow,
 #pragma unroll
     for (int e = 0; e < PER; ++e)
       if ((take >> e) & 1u) {
-        const int32_t v = map_key(P, b, j0 + e);
+        const int32_t v = km.map(P, b, j0 + e);
         if (staged) rs.out_stage[o] = v;
         else out[o] = v;
         ++o;
@@ -1017,23 +1038,16 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
   extern __shared__ __align__(16) uint8_t sel_dyn[];
   pdl_trigger();
   pdl_wait();
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x;
   const int64_t qrow = blockIdx.x;
   const int b = static_cast<int>(qrow / P.s);
-  const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
-  int32_t* out = P.out + qrow * P.out_stride + P.out_col;
-  const int k = P.top_k;
-
-  if (P.win_base != nullptr)
-    for (int c = tid; c < P.window; c += SEL_THREADS) out[c - P.window] = window_row(P, b, P.positions[qrow], c);
-  if (nvis <= k) {
-    for (int r = tid; r < k; r += SEL_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
-    return;
-  }
   const int j0 = tid * PER;
+  // the scores and the block table entries load before the visible count is known (the three
+  // global reads overlap): reads stay inside the row's n_pad entries, and keys at or past the
+  // visible count are never counted
   const float* sc = P.scores + qrow * P.n_pad + j0;
   uint32_t key[PER];
-  if ((P.n_pad & 3) == 0 && j0 + PER <= nvis) {
+  if ((P.n_pad & 3) == 0 && j0 + PER <= P.n_pad) {
 #pragma unroll
     for (int e = 0; e < PER; e += 4) {
       const float4 v = __ldcg(reinterpret_cast<const float4*>(sc + e));
@@ -1044,19 +1058,66 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
     }
   } else {
 #pragma unroll
-    for (int e = 0; e < PER; ++e) key[e] = (j0 + e < nvis) ? ordered_bits(__ldcg(sc + e)) : 0u;
+    for (int e = 0; e < PER; ++e) key[e] = (j0 + e < P.n_pad) ? ordered_bits(__ldcg(sc + e)) : 0u;
+  }
+  const KeyMap km(P, b, j0, PER);
+  if (tid == 0) sh.ncand = 0;  // ordered before its use by the radix level's barriers
+  const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
+  int32_t* out = P.out + qrow * P.out_stride + P.out_col;
+  const int k = P.top_k;
+
+  if (P.win_base != nullptr)
+    for (int c = tid; c < P.window; c += SEL_THREADS) out[c - P.window] = window_row(P, b, P.positions[qrow], c);
+  if (nvis <= k) {
+    for (int r = tid; r < k; r += SEL_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
+    return;
   }
   // number of valid keys of this thread (the rest are padding and never counted)
   const int nv = max(0, min(PER, nvis - j0));
   if constexpr (REFINE) {
-    if (refine_band<PER>(P, qrow, b, k, key, nv, j0, sh, *reinterpret_cast<RefineSmem*>(sel_dyn), out)) return;
+    if (refine_band<PER>(P, qrow, b, k, key, nv, j0, sh, *reinterpret_cast<RefineSmem*>(sel_dyn), out, km)) return;
   }
   uint32_t prefix, kleft, shift;
   bool whole;
-  radix_levels<PER>(key, nv, static_cast<uint32_t>(k), true, sh, prefix, shift, kleft, whole);
-  // keys equal to the full 32-bit prefix (shift == 0, not whole): the kleft lowest indices
   int32_t tau_last = 0x7fffffff;
+  // The top 12 bits first. When the boundary bin holds at most SEL_THREADS keys (the usual case:
+  // ~n / 4096 keys per bin), its keys are ranked directly by (key desc, index asc) instead of
+  // histogramming the lower bits: the kleft-th of them is the threshold (key, index).
+  radix_levels<PER>(key, nv, static_cast<uint32_t>(k), true, sh, prefix, shift, kleft, whole, 1);
+  bool ranked = false;
   if (!whole) {
+    uint64_t* cand = reinterpret_cast<uint64_t*>(sh.hist);  // the histogram is free after the level
+    const uint32_t top = prefix >> shift;
+#pragma unroll
+    for (int e = 0; e < PER; ++e)
+      if (e < nv && (key[e] >> shift) == top) {
+        const uint32_t slot = atomicAdd(&sh.ncand, 1u);
+        if (slot < SEL_THREADS)
+          cand[slot] = (static_cast<uint64_t>(key[e]) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(j0 + e));
+      }
+    __syncthreads();
+    const uint32_t nc = sh.ncand;
+    if (nc <= SEL_THREADS) {
+      if (tid < static_cast<int>(nc)) {
+        const uint64_t v = cand[tid];
+        uint32_t rank = 0;
+        for (uint32_t m = 0; m < nc; ++m) rank += cand[m] > v;
+        if (rank == kleft - 1) {
+          sh.tau_key = static_cast<uint32_t>(v >> 32);
+          sh.tau_last = static_cast<int32_t>(~static_cast<uint32_t>(v));
+        }
+      }
+      __syncthreads();
+      prefix = sh.tau_key;
+      tau_last = sh.tau_last;
+      shift = 0;
+      ranked = true;
+    } else {  // a crowded bin (many equal or near-equal scores): the remaining radix levels
+      radix_levels<PER>(key, nv, static_cast<uint32_t>(k), true, sh, prefix, shift, kleft, whole);
+    }
+  }
+  // keys equal to the full 32-bit prefix (shift == 0, not whole): the kleft lowest indices
+  if (!whole && !ranked) {
     uint32_t ne = 0;
 #pragma unroll
     for (int e = 0; e < PER; ++e) ne += (e < nv && key[e] == prefix);
@@ -1072,17 +1133,17 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
   }
   // take: (key >> shift) above the prefix, or equal to it and (whole, or index <= tau_last)
   const uint32_t hi = prefix >> shift;
-  uint32_t cnt = 0;
+  uint32_t take = 0;
 #pragma unroll
   for (int e = 0; e < PER; ++e) {
     const uint32_t kh = key[e] >> shift;
-    cnt += (e < nv) && (kh > hi || (kh == hi && (whole || j0 + e <= tau_last)));
+    take |= static_cast<uint32_t>((e < nv) && (kh > hi || (kh == hi && (whole || j0 + e <= tau_last)))) << e;
   }
-  uint32_t pos = block_scan_reg(cnt, sh);
-#pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const uint32_t kh = key[e] >> shift;
-    if ((e < nv) && (kh > hi || (kh == hi && (whole || j0 + e <= tau_last)))) out[pos++] = map_key(P, b, j0 + e);
+  uint32_t pos = block_scan_reg(static_cast<uint32_t>(__popc(take)), sh);
+  while (take) {  // the taken keys in ascending order
+    const int e = __ffs(take) - 1;
+    take &= take - 1;
+    out[pos++] = km.map(P, b, j0 + e);
   }
 }
 

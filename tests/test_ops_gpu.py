@@ -240,6 +240,13 @@ def test_indexer_heavy_ties_fallback(dsv4):
     got2 = dsv4.indexer_topk(q.to(DEV), w.to(DEV), keys2.to(DEV), 512).cpu().numpy()
     ref2 = I.indexer_topk(q.numpy(), w.numpy(), keys2.numpy(), 512)
     np.testing.assert_array_equal(got2, ref2)
+    # 450 near-identical keys: one 12-bit bin of 450 (at most the CTA's 512 threads), ranked directly
+    keys3 = keys[:, :450].clone()
+    keys3[0] = keys[0, :1] + 1e-4 * torch.randn(450, 128, generator=torch.Generator().manual_seed(2))
+    keys3[0, 300:310] = keys3[0, 100:110]                   # exact ties inside the ranked bin
+    got3 = dsv4.indexer_topk(q.to(DEV), w.to(DEV), keys3.to(DEV), 200).cpu().numpy()
+    ref3 = I.indexer_topk(q.numpy(), w.numpy(), keys3.numpy(), 200)
+    np.testing.assert_array_equal(got3, ref3)
 
 
 # ---------------------------------------------------------------- projections
