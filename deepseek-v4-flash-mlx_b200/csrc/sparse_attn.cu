@@ -95,7 +95,30 @@ struct Params {
   int rope_dim;
   const int64_t* win_base;  // implicit window (NULL: the list is idx alone)
   int win_stride, window, window_linear;
+  int cluster;  // 1: the splits of a query are one thread-block cluster and merge through DSMEM
 };
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t a, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float dsmem_f32(uint32_t a, int rank) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(dsmem_addr(a, rank)) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 dsmem_f32x4(uint32_t a, int rank) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(dsmem_addr(a, rank))
+               : "memory");
+  return v;
+}
 
 // logical list length of a query: implicit window rows followed by the explicit indices
 __device__ __forceinline__ int list_len(const Params& P) { return (P.win_base ? P.window : 0) + P.t; }
@@ -459,6 +482,70 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_kernel(Params P) {
       }
     }
   __syncthreads();
+  if (P.cluster) {
+    // The query's splits are this cluster: each CTA parks (m, l) beside its unnormalised O, then
+    // CTA `split` merges heads [split * nh, +nh) over all splits exactly as combine_kernel does
+    // (weights by a warp with lane = split, the dims in split order) and writes them out.
+    if (tid < HB) {
+      sm.red_max[0][tid] = sm.m_run[cur][tid];
+      sm.red_sum[0][tid] = sm.l_run[tid];
+    }
+    cluster_sync_all();
+    const int nh = (HB + P.splits - 1) / P.splits;
+    const int hb0 = split * nh, hb1 = min(min(HB, heads_here), hb0 + nh);
+    float* wbuf = &sm.red_max[1][0];  // [nh][splits], at most 64 + splits floats
+    const uint32_t m_s = static_cast<uint32_t>(__cvta_generic_to_shared(&sm.red_max[0][0]));
+    const uint32_t l_s = static_cast<uint32_t>(__cvta_generic_to_shared(&sm.red_sum[0][0]));
+    for (int j = warp; j < hb1 - hb0; j += THREADS / 32) {
+      const int hh = hb0 + j;
+      float m = -INFINITY, l = 0.f;
+      if (lane < P.splits) {
+        m = dsmem_f32(m_s + hh * 4, lane);
+        l = dsmem_f32(l_s + hh * 4, lane);
+      }
+      const float M = warp_max(m);
+      const float w = (m == -INFINITY) ? 0.f : exp2f(m - M);
+      if (lane < P.splits) wbuf[j * P.splits + lane] = w;
+      const float L = warp_sum(w * l);
+      if (lane == 0)
+        sm.alpha[hh] = (M == -INFINITY) ? __int_as_float(0x7fc00000) : 1.f / (L + exp2f(P.sink[h0 + hh] * LOG2E - M));
+    }
+    __syncthreads();
+    const bool rope = P.rope_freqs != nullptr;
+    const int pos = rope ? P.positions[qi] : 0;
+    const uint32_t os_s = static_cast<uint32_t>(__cvta_generic_to_shared(os));
+#pragma unroll 1
+    for (int c = tid; c < (hb1 - hb0) * (D / 4); c += THREADS) {
+      const int j = c / (D / 4), hh = hb0 + j, d = (c % (D / 4)) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < P.splits; ++sp) {
+        const float4 v = dsmem_f32x4(os_s + (hh * OSTRIDE + d) * 4, sp);
+        const float w = wbuf[j * P.splits + sp];
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+      const float inv = sm.alpha[hh];
+      float4 v = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+      if (rope && d >= D - P.rope_dim) {
+        const int f0 = (d - (D - P.rope_dim)) >> 1;
+        float c0, s0, c1, s1;
+        rope_cos_sin(pos, P.rope_freqs[f0], &c0, &s0);
+        rope_cos_sin(pos, P.rope_freqs[f0 + 1], &c1, &s1);
+        rotate_pair(v.x, v.y, c0, s0, true, &v.x, &v.y);
+        rotate_pair(v.z, v.w, c1, s1, true, &v.z, &v.w);
+      }
+      const int64_t off = ((qi * P.h) + h0 + hh) * D + d;
+      if (P.out_dtype == DSV4_BF16)
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(P.out) + off) =
+            make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+      else
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.out) + off) = v;
+    }
+    cluster_sync_all();  // the peers keep their partials until every CTA of the cluster has read them
+    return;
+  }
   if (final_out) {
     const bool rope = P.rope_freqs != nullptr;
     const int pos = rope ? P.positions[qi] : 0;
@@ -616,7 +703,40 @@ static bool tc_shape_ok(const dsv4_sparse_attn_params* p) {
 struct AttnPlan {
   bool tc;
   int splits;
+  bool cluster;  // mma.sync kernel: the splits of a query merge inside a cluster (no partials in HBM)
 };
+
+// whether `splits` CTAs of the mma.sync kernel (one per SM by shared memory) can run as one cluster
+// on this GPU; asked once per size
+static bool cluster_fits(int splits) {
+  static int known[17] = {0};  // 0 unknown, 1 yes, -1 no
+  if (splits < 2 || splits > 16) return false;
+  if (known[splits] != 0) return known[splits] > 0;
+  const int smem = static_cast<int>(sizeof(sa::Smem));
+  bool ok = cudaFuncSetAttribute(sa::sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
+            cudaSuccess;
+  if (ok && splits > 8)
+    ok = cudaFuncSetAttribute(sa::sparse_attn_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+         cudaSuccess;
+  int nclusters = 0;
+  if (ok) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(splits, 1, 1);
+    cfg.blockDim = dim3(sa::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ok = cudaOccupancyMaxActiveClusters(&nclusters, sa::sparse_attn_kernel, &cfg) == cudaSuccess && nclusters > 0;
+  }
+  (void)cudaGetLastError();  // a refused query leaves no sticky error
+  known[splits] = ok ? 1 : -1;
+  return ok;
+}
 static int tc_splits(const dsv4_sparse_attn_params* p) {
   const int len = (p->win_base ? p->window : 0) + p->t;
   const int tiles = (len + 127) / 128;
@@ -640,14 +760,16 @@ static int tc_splits(const dsv4_sparse_attn_params* p) {
 constexpr int64_t TC_MIN_QUERIES = 16;
 static AttnPlan plan_attention(const dsv4_sparse_attn_params* p) {
   const bool tc = p->kernel == 2 || (p->kernel == 0 && tc_shape_ok(p) && p->s >= TC_MIN_QUERIES);
-  if (tc && tc_shape_ok(p)) return {true, tc_splits(p)};
-  return {false, sa::choose_splits(p)};
+  if (tc && tc_shape_ok(p)) return {true, tc_splits(p), false};
+  const int sp = sa::choose_splits(p);
+  return {false, sp, sp > 1 && cluster_fits(sp)};
 }
 
 // workspace: [split partials (O, m, l)] [bf16 q after the fused norm/rope pre-pass]
 static size_t partial_bytes(const dsv4_sparse_attn_params* p) {
-  const int splits = plan_attention(p).splits;
-  if (splits <= 1) return 0;
+  const AttnPlan pl = plan_attention(p);
+  const int splits = pl.splits;
+  if (splits <= 1 || pl.cluster) return 0;
   const int hblocks = (p->h + sa::HB - 1) / sa::HB;
   const int64_t units = p->s * hblocks * splits;
   return static_cast<size_t>(units) * (sa::HB * sa::D + sa::HB * 2) * sizeof(float);
@@ -695,6 +817,7 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
   P.hblocks = (p->h + sa::HB - 1) / sa::HB;
   const AttnPlan plan = plan_attention(p);
   P.splits = plan.splits;
+  P.cluster = plan.cluster ? 1 : 0;
   P.q_dtype = p->q_dtype;
   P.idx_dtype = p->idx_dtype;
   P.out_dtype = p->out_dtype;
@@ -712,7 +835,7 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
     set_error("dsv4_sparse_attn: workspace of %zu bytes needed, %zu given", need, p->workspace_bytes);
     return DSV4_ERR_WORKSPACE;
   }
-  if (P.splits > 1) P.part = reinterpret_cast<float*>(p->workspace);
+  if (P.splits > 1 && !P.cluster) P.part = reinterpret_cast<float*>(p->workspace);
   if (p->q_norm_rope) {
     // weightless per-head norm + rope of q into bf16 scratch, then attention reads it
     void* qn = static_cast<char*>(p->workspace) + (partial_bytes(p) + 255) / 256 * 256;
@@ -752,6 +875,24 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
     attr_set = true;
   }
   dim3 grid(static_cast<unsigned>(P.s * P.splits), P.hblocks);
+  if (P.cluster) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(sa::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;  // the splits of one query
+    attr[1].val.clusterDim.x = P.splits;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    DSV4_CUDA_CHECK(cudaLaunchKernelEx(&cfg, sa::sparse_attn_kernel, P));
+    return DSV4_OK;
+  }
   DSV4_CUDA_CHECK(launch_pdl(sa::sparse_attn_kernel, grid, dim3(sa::THREADS), smem, as_stream(stream), P));
   if (P.splits > 1) {
     dim3 g2(static_cast<unsigned>(P.s * P.hblocks), sa::HB);
