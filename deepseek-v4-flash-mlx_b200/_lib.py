@@ -46,7 +46,7 @@ class RopeParams(ctypes.Structure):
 class NormRopeParams(ctypes.Structure):
     _fields_ = [("x", vp), ("weight", vp), ("out", vp), ("out_rows", vp), ("rows", i64),
                 ("heads", i32), ("dim", i32), ("rope_dim", i32), ("x_dtype", i32), ("w_dtype", i32),
-                ("out_dtype", i32), ("eps", f32), ("freqs", vp), ("positions", vp)]
+                ("out_dtype", i32), ("eps", f32), ("freqs", vp), ("positions", vp), ("act_quant", i32)]
 
 
 class IndexerParams(ctypes.Structure):
@@ -71,7 +71,7 @@ class CompressorParams(ctypes.Structure):
     _fields_ = [("kv", vp), ("score", vp), ("ape", vp), ("norm_w", vp), ("out", vp), ("out_rows", vp),
                 ("b", i32), ("s", i32), ("head_dim", i32), ("ratio", i32), ("rope_dim", i32),
                 ("norm_dtype", i32), ("out_dtype", i32), ("eps", f32), ("freqs", vp), ("pos0", i32),
-                ("ring_kv", vp), ("ring_score", vp)]
+                ("ring_kv", vp), ("ring_score", vp), ("act_quant", i32)]
 
 
 class CompressorDecodeParams(ctypes.Structure):
@@ -79,7 +79,8 @@ class CompressorDecodeParams(ctypes.Structure):
                 ("ring_score", vp), ("positions", vp), ("out", vp), ("out_rows", vp),
                 ("b", i32), ("head_dim", i32), ("ratio", i32), ("rope_dim", i32),
                 ("norm_dtype", i32), ("out_dtype", i32), ("eps", f32), ("freqs", vp),
-                ("key_image", vp), ("key_inv", vp), ("key_norm_max", vp), ("image_stride", i64)]
+                ("key_image", vp), ("key_inv", vp), ("key_norm_max", vp), ("image_stride", i64),
+                ("act_quant", i32)]
 
 
 class LinearParams(ctypes.Structure):

@@ -16,7 +16,7 @@ from .norm_rope import rope_freqs
 
 
 def _pool(kv, score, ape, norm_w, out, head_dim, ratio, rope_dim, freqs, ring_kv=None, ring_score=None,
-          out_rows=None, pos0=0, eps=1e-6):
+          out_rows=None, pos0=0, eps=1e-6, act_quant=False):
     b, s = kv.shape[0], kv.shape[1]
     p = L.CompressorParams()
     p.kv, p.score, p.ape = L.ptr(kv), L.ptr(score), L.ptr(ape)
@@ -30,19 +30,21 @@ def _pool(kv, score, ape, norm_w, out, head_dim, ratio, rope_dim, freqs, ring_kv
     p.freqs, p.pos0 = L.ptr(freqs), pos0
     p.ring_kv = L.ptr(ring_kv) if ring_kv is not None else None
     p.ring_score = L.ptr(ring_score) if ring_score is not None else None
+    p.act_quant = int(act_quant)
     L.check(L.lib().dsv4_compressor_pool(ctypes.byref(p), L.stream_of(kv)))
 
 
 def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_head_dim=64,
                        base=160000.0, original_seq_len=65536, factor=16, beta_fast=32, beta_slow=1,
-                       out_dtype=torch.float32, pos0=0):
+                       out_dtype=torch.float32, pos0=0, act_quant=False):
     """x [b, s, dim] -> (kv [b, s//ratio, head_dim] post-rope, state).
 
     state: "kv" / "score" = the last full block's kv and score+ape [b, ratio, 2*head_dim] (when
     s >= ratio), "kv_rem" = the remainder rows, and "ring_kv" / "ring_score" [b, 2*ratio, 2*head_dim]
     the device ring that `compressor_decode_step` continues from (ref_torch/compressor.py:67-74).
     `pos0` is the position of x's first token (a slice of a longer sequence): row g is roped at
-    pos0 + ratio*g."""
+    pos0 + ratio*g. `act_quant`: the fp8-e4m3 act-quant simulation of each row's nope dims (the
+    reference's default for the main compressor, v4mlx/compressor.py:60-62)."""
     L.require_cuda(x, wkv, wgate, ape, norm_w)
     b, s, _ = x.shape
     d2 = 2 * head_dim
@@ -56,7 +58,7 @@ def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_h
     ring_score = torch.empty_like(ring_kv)
     nw = norm_w if norm_w.dtype in (torch.float32, torch.bfloat16) else norm_w.float()
     _pool(kv, score, ape.float().contiguous(), nw.contiguous(), out, head_dim, ratio, rope_head_dim, freqs,
-          ring_kv, ring_score, pos0=pos0)
+          ring_kv, ring_score, pos0=pos0, act_quant=act_quant)
     cutoff = s - s % ratio
     state = {"ring_kv": ring_kv, "ring_score": ring_score}
     if cutoff >= ratio:
@@ -69,13 +71,14 @@ def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_h
 
 def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, positions, out, out_rows,
                            head_dim=512, ratio=4, rope_head_dim=64, freqs=None, eps=1e-6,
-                           proj=None, key_image=None):
+                           proj=None, key_image=None, act_quant=False):
     """One decode token per sequence (oracle/decode_engine.py:96-105): write this token's kv / score
     into the device ring; sequences whose position p has (p+1) % ratio == 0 emit a pooled, normed,
     roped row into out[out_rows[b]] and shift the ring. x [b, dim]; positions int32 [b].
     `proj` may pass precomputed projections (kv, score) [b, 2*head_dim] fp32. `key_image`
     (image, inv, norm_max, keys_per_entry) also adds each emitted indexer key (out viewed as
-    [entries * keys_per_entry, 128] fp32) to a decode cache's key image."""
+    [entries * keys_per_entry, 128] fp32) to a decode cache's key image. `act_quant`: the fp8-e4m3
+    act-quant simulation of the emitted row's nope dims (oracle/decode_engine.py:105)."""
     L.require_cuda(x, ring_kv, ring_score, positions, out, out_rows)
     if proj is None:
         kvp = linear(x, wkv, torch.float32)
@@ -95,6 +98,7 @@ def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, posi
     p.out_dtype = L.dtype_code(out)
     p.eps = eps
     p.freqs = L.ptr(freqs)
+    p.act_quant = int(act_quant)
     if key_image is not None:
         img, inv, nmax, stride = key_image
         p.key_image, p.key_inv, p.key_norm_max, p.image_stride = L.ptr(img), L.ptr(inv), L.ptr(nmax), int(stride)

@@ -2,6 +2,8 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <cstdarg>
@@ -136,6 +138,20 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// fp8-e4m3 round trip of y = x * 2^-e (nearest even, saturating at 448), times 2^e: exact in fp32
+// and in bf16, since e4m3 keeps 4 significant bits
+__device__ __forceinline__ float fp8_round_pow2(float x, int e) {
+  const float y = fminf(fmaxf(x * __uint_as_float(static_cast<uint32_t>(127 - e) << 23), -448.f), 448.f);
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3), __NV_E4M3);
+  return __half2float(__half(h)) * __uint_as_float(static_cast<uint32_t>(127 + e) << 23);
+}
+// the act-quant block scale exponent: ceil(log2(max(amax, 1e-4) / 448)), from the bits of the
+// (correctly rounded) fp32 quotient
+__device__ __forceinline__ int act_quant_exp(float amax) {
+  const uint32_t b = __float_as_uint(fmaxf(amax, 1e-4f) / 448.f);
+  return static_cast<int>((b >> 23) & 0xff) - 127 + ((b & 0x7fffff) != 0 ? 1 : 0);
 }
 
 // rope angle as the reference forms it: fp32 product of the position and the frequency

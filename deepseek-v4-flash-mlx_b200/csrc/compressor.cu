@@ -52,7 +52,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 __device__ __forceinline__ void finish_pair(float& v0, float& v1, int c, int d, int rope_dim,
                                             const void* norm_w, int norm_dtype, float rinv,
                                             const float* freqs, int pos, void* out, int64_t orow,
-                                            int out_dtype) {
+                                            int out_dtype, int act_quant) {
   v0 = v0 * rinv;
   v1 = v1 * rinv;
   if (norm_w) {
@@ -63,6 +63,13 @@ __device__ __forceinline__ void finish_pair(float& v0, float& v1, int c, int d, 
     float cs, sn;
     rope_cos_sin(pos, freqs[(c - (d - rope_dim)) >> 1], &cs, &sn);
     rotate_pair(v0, v1, cs, sn, false, &v0, &v1);
+  }
+  // fp8 act-quant simulation of the nope dims: a 64-dim block is the 32 pairs of one warp (the
+  // condition is warp-uniform)
+  if (act_quant && c < d - rope_dim) {
+    const int ex = act_quant_exp(warp_max(fmaxf(fabsf(v0), fabsf(v1))));
+    v0 = fp8_round_pow2(v0, ex);
+    v1 = fp8_round_pow2(v1, ex);
   }
   const int64_t off = orow * d + c;
   if (out_dtype == DSV4_BF16)
@@ -143,7 +150,7 @@ __global__ void __launch_bounds__(THREADS) pool_kernel(dsv4_compressor_params p)
   npairs = 0;
   for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++npairs)
     finish_pair(vals[npairs][0], vals[npairs][1], c, d, p.rope_dim, p.norm_w, p.norm_dtype, rinv,
-                p.freqs, p.pos0 + R * g, p.out, orow, p.out_dtype);
+                p.freqs, p.pos0 + R * g, p.out, orow, p.out_dtype, p.act_quant);
 }
 
 // decode hand-off ring (ref_torch/compressor.py:67-74; seeding as oracle/decode_engine.py:91-95):
@@ -303,7 +310,7 @@ __global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_deco
     const int c = 2 * (tid + np * THREADS);
     if (c >= d) continue;
     finish_pair(vals[np][0], vals[np][1], c, d, p.rope_dim, p.norm_w, p.norm_dtype, rinv, p.freqs, pos + 1 - R,
-                p.out, p.out_rows[b], p.out_dtype);
+                p.out, p.out_rows[b], p.out_dtype, p.act_quant);
     // the block's rows become the previous block (rows 0..R-1); this token's row is the last
 #pragma unroll
     for (int r = 0; r < R - 1; ++r) {
@@ -371,7 +378,7 @@ __global__ void __launch_bounds__(THREADS) decode_kernel(dsv4_compressor_decode_
   np = 0;
   for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++np)
     finish_pair(vals[np][0], vals[np][1], c, d, p.rope_dim, p.norm_w, p.norm_dtype, rinv, p.freqs,
-                pos + 1 - R, p.out, p.out_rows[b], p.out_dtype);
+                pos + 1 - R, p.out, p.out_rows[b], p.out_dtype, p.act_quant);
   for (int c = threadIdx.x; c < d2; c += blockDim.x)
     for (int r = 0; r < R; ++r) {
       rk[r * d2 + c] = rk[(R + r) * d2 + c];
@@ -385,6 +392,9 @@ __global__ void __launch_bounds__(THREADS) decode_kernel(dsv4_compressor_decode_
 using namespace dsv4;
 
 extern "C" int dsv4_compressor_pool(const dsv4_compressor_params* p, void* stream) {
+  DSV4_CHECK_ARG(p == nullptr || p->act_quant == 0 ||
+                     (p->act_quant == 1 && p->head_dim % 64 == 0 && (p->head_dim - p->rope_dim) % 64 == 0),
+                 "dsv4_compressor_pool: act_quant needs head_dim and head_dim - rope_dim multiples of 64");
   DSV4_CHECK_ARG(p && p->kv && p->score && p->ape && p->out && p->freqs, "dsv4_compressor_pool: NULL tensor");
   DSV4_CHECK_ARG(p->b > 0 && p->s >= 0 && p->ratio > 0 && p->ratio <= 8, "dsv4_compressor_pool: bad sizes");
   DSV4_CHECK_ARG(p->head_dim % 2 == 0 && p->head_dim <= 4 * cmp::THREADS && p->head_dim >= p->rope_dim &&
@@ -407,6 +417,9 @@ extern "C" int dsv4_compressor_pool(const dsv4_compressor_params* p, void* strea
 }
 
 extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream) {
+  DSV4_CHECK_ARG(p == nullptr || p->act_quant == 0 ||
+                     (p->act_quant == 1 && p->head_dim % 64 == 0 && (p->head_dim - p->rope_dim) % 64 == 0),
+                 "dsv4_compressor_decode: act_quant needs head_dim and head_dim - rope_dim multiples of 64");
   DSV4_CHECK_ARG(p && p->kv && p->score && p->ape && p->ring_kv && p->ring_score && p->positions &&
                      p->out && p->out_rows && p->freqs,
                  "dsv4_compressor_decode: NULL tensor");

@@ -189,6 +189,20 @@ __global__ void norm_rope_kernel(dsv4_norm_rope_params p) {
       }
     }
   }
+  if (p.act_quant) {  // fp8 act-quant simulation of the nope dims in blocks of 64 (64 / PER lanes)
+    constexpr int LPB = 64 / PER;
+    static_assert(64 % PER == 0, "a block spans whole lanes");
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) amax = fmaxf(amax, fabsf(v[e]));
+#pragma unroll
+    for (int o = 1; o < LPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane * PER < DIM - p.rope_dim) {
+      const int ex = act_quant_exp(amax);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) v[e] = fp8_round_pow2(v[e], ex);
+    }
+  }
   int64_t dst;
   if (p.out_rows) {
     dst = (p.out_rows[row] * p.heads + head) * DIM + lane * PER;
@@ -268,6 +282,9 @@ extern "C" int dsv4_rope(const dsv4_rope_params* p, void* stream) {
 }
 
 extern "C" int dsv4_norm_rope(const dsv4_norm_rope_params* p, void* stream) {
+  DSV4_CHECK_ARG(p == nullptr || p->act_quant == 0 ||
+                     (p->act_quant == 1 && p->dim >= 128 && (p->dim - p->rope_dim) % 64 == 0),
+                 "dsv4_norm_rope: act_quant needs (dim - rope_dim) a multiple of 64");
   DSV4_CHECK_ARG(p && p->x && p->out && p->freqs && p->positions && p->rows >= 0 && p->heads > 0,
                  "dsv4_norm_rope: bad arguments");
   DSV4_CHECK_ARG(p->rope_dim > 0 && p->rope_dim % 2 == 0 && p->rope_dim <= p->dim,

@@ -89,9 +89,11 @@ def make_attention_weights(seed, dims: LayerDims = DIMS, quant=False):
     )
 
 
-def prefill_layer(x, W: AttentionWeights, top_k=512, dims: LayerDims = DIMS, return_aux=False):
+def prefill_layer(x, W: AttentionWeights, top_k=512, dims: LayerDims = DIMS, return_aux=False, act_quant=False):
     """x [s, dim] (one sequence from position 0) -> out [s, dim] fp32 (and the int32 index list
-    [s, window + top_k] plus intermediates with return_aux)."""
+    [s, window + top_k] plus intermediates with return_aux). `act_quant`: the fp8 act-quant
+    simulation of the cached kv rows and compressed rows (oracle/decode_engine.py:82,
+    v4mlx/compressor.py:60-62)."""
     L.require_cuda(x)
     s = x.shape[0]
     dev = x.device
@@ -103,9 +105,11 @@ def prefill_layer(x, W: AttentionWeights, top_k=512, dims: LayerDims = DIMS, ret
     q = norm_rope(qraw, pos, freqs, weight=None, rope_dim=dims.rope_dim)                  # bf16
     n_comp = s // dims.ratio
     kvcat = torch.empty((s + n_comp, dims.head_dim), dtype=torch.bfloat16, device=dev)
-    kvcat[:s] = norm_rope(linear(xn, W.wkv, torch.float32), pos, freqs, weight=W.kv_a_norm, rope_dim=dims.rope_dim)
+    kvcat[:s] = norm_rope(linear(xn, W.wkv, torch.float32), pos, freqs, weight=W.kv_a_norm, rope_dim=dims.rope_dim,
+                          act_quant=act_quant)
     comp, _ = compressor_prefill(xn[None], W.c_wkv, W.c_wgate, W.c_ape, W.c_norm, head_dim=dims.head_dim,
-                                 ratio=dims.ratio, rope_head_dim=dims.rope_dim, out_dtype=torch.bfloat16)
+                                 ratio=dims.ratio, rope_head_dim=dims.rope_dim, out_dtype=torch.bfloat16,
+                                 act_quant=act_quant)
     kvcat[s:] = comp[0]
     k_idx, _ = compressor_prefill(xn[None], W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, head_dim=dims.idx_dim,
                                   ratio=dims.ratio, rope_head_dim=dims.rope_dim, out_dtype=torch.float32)
@@ -129,8 +133,9 @@ class DecodeBlock:
     (config 5): `step(x, positions)` runs the whole attention block for one token per sequence."""
 
     def __init__(self, W: AttentionWeights, batch, max_ctx, top_k=512, dims: LayerDims = DIMS, device="cuda",
-                 page=64, cache=None):
+                 page=64, cache=None, act_quant=False):
         self.W, self.dims, self.top_k = W, dims, top_k
+        self.act_quant = act_quant  # the fp8 act-quant simulation of cached rows (oracle/decode_engine.py:82, 105)
         self.cache = cache if cache is not None else SparseMLACache(
             batch, max_ctx // dims.ratio, window=dims.window, head_dim=dims.head_dim, idx_dim=dims.idx_dim,
             ratio=dims.ratio, page=page, device=device)
@@ -154,10 +159,10 @@ class DecodeBlock:
         qraw = qraw.view(b, d.n_heads, d.head_dim)
         # this token's window slot, and where the compressors emit (when (p+1) % ratio == 0)
         win_rows, comp_rows, key_rows = decode_rows(c, pos)
-        _norm_rope_into(kvp, W.kv_a_norm, pos, self.freqs, c.kv_pool, win_rows, d.rope_dim)
+        _norm_rope_into(kvp, W.kv_a_norm, pos, self.freqs, c.kv_pool, win_rows, d.rope_dim, self.act_quant)
         compressor_decode_step(xn, W.c_wkv, W.c_wgate, W.c_ape, W.c_norm, c.ring_kv, c.ring_score, pos, c.kv_pool,
                                comp_rows, head_dim=d.head_dim, ratio=d.ratio,
-                               rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(c_kv, c_sc))
+                               rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(c_kv, c_sc), act_quant=self.act_quant)
         compressor_decode_step(xn, W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, c.ring_k_idx, c.ring_s_idx, pos,
                                c.k_idx.view(-1, d.idx_dim), key_rows, head_dim=d.idx_dim, ratio=d.ratio,
                                rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(i_kv, i_sc),
@@ -167,7 +172,7 @@ class DecodeBlock:
         return o_grouped(o.reshape(b, -1), W.wo_a, W.wo_b)
 
 
-def _norm_rope_into(x, weight, positions, freqs, pool, rows, rope_dim):
+def _norm_rope_into(x, weight, positions, freqs, pool, rows, rope_dim, act_quant=False):
     """RMSNorm(weight) + RoPE of x [b, dim] written as bf16 into pool rows `rows` (int64 [b])."""
     p = L.NormRopeParams()
     p.x, p.weight, p.out, p.out_rows = L.ptr(x), L.ptr(weight), L.ptr(pool), L.ptr(rows)
@@ -175,6 +180,7 @@ def _norm_rope_into(x, weight, positions, freqs, pool, rows, rope_dim):
     p.x_dtype, p.w_dtype, p.out_dtype = L.dtype_code(x), L.dtype_code(weight), L.BF16
     p.eps = 1e-6
     p.freqs, p.positions = L.ptr(freqs), L.ptr(positions)
+    p.act_quant = int(act_quant)
     L.check(L.lib().dsv4_norm_rope(ctypes_byref(p), L.stream_of(x)))
 
 

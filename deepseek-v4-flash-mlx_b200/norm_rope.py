@@ -164,7 +164,8 @@ def rope(x, positions, freqs, rope_dim=64, inverse=False):
 
 @torch.library.custom_op("dsv4::norm_rope", mutates_args=(), device_types="cuda")
 def _norm_rope_op(x: torch.Tensor, weight: torch.Tensor | None, freqs: torch.Tensor,
-                  positions: torch.Tensor, rope_dim: int, eps: float, out_dtype: torch.dtype) -> torch.Tensor:
+                  positions: torch.Tensor, rope_dim: int, eps: float, out_dtype: torch.dtype,
+                  act_quant: bool = False) -> torch.Tensor:
     x = x.contiguous()
     out = torch.empty(x.shape, dtype=out_dtype, device=x.device)
     rows = positions.numel()
@@ -177,19 +178,22 @@ def _norm_rope_op(x: torch.Tensor, weight: torch.Tensor | None, freqs: torch.Ten
     p.w_dtype = L.dtype_code(weight) if weight is not None else L.F32
     p.eps = eps
     p.freqs, p.positions = L.ptr(freqs), L.ptr(positions)
+    p.act_quant = int(act_quant)
     L.check(L.lib().dsv4_norm_rope(ctypes.byref(p), L.stream_of(x)))
     return out
 
 
 @_norm_rope_op.register_fake
-def _(x, weight, freqs, positions, rope_dim, eps, out_dtype):
+def _(x, weight, freqs, positions, rope_dim, eps, out_dtype, act_quant=False):
     return torch.empty(x.shape, dtype=out_dtype, device=x.device)
 
 
-def norm_rope(x, positions, freqs, weight=None, rope_dim=64, eps=1e-6, out_dtype=torch.bfloat16):
+def norm_rope(x, positions, freqs, weight=None, rope_dim=64, eps=1e-6, out_dtype=torch.bfloat16, act_quant=False):
     """Fused RMSNorm (weight given) or weightless per-head norm (weight None) over the last dim,
     then RoPE of its last rope_dim dims at `positions` (one per leading row), then a cast.
-    This is the q / kv chain of oracle/decode_engine.py:77-81 and oracle/v4_fast.py:87-91."""
+    This is the q / kv chain of oracle/decode_engine.py:77-81 and oracle/v4_fast.py:87-91.
+    `act_quant`: the fp8-e4m3 act-quant simulation of the kv row's nope dims (blocks of 64,
+    power-of-two scales) that the reference applies before caching (oracle/decode_engine.py:82)."""
     L.require_cuda(x, positions, freqs, weight)
     return _norm_rope_op(x, weight, freqs.float().contiguous(), positions.to(torch.int32).contiguous(),
-                         int(rope_dim), float(eps), out_dtype)
+                         int(rope_dim), float(eps), out_dtype, bool(act_quant))

@@ -162,6 +162,11 @@ typedef struct {
   float eps;
   const float* freqs;     /* [rope_dim/2] */
   const int32_t* positions; /* [rows] */
+  /* 1: the act-quant simulation of the cached rows (oracle/decode_engine.py:52-54, 82, 105;
+   * v4mlx/compressor.py:11-20, 60-62): dims [0, dim - rope_dim) are rounded to fp8-e4m3 (nearest
+   * even, saturating) in blocks of 64 with a power-of-two scale 2^ceil(log2(max(amax, 1e-4) / 448)),
+   * after the norm and rope, before the store. (dim - rope_dim) must be a multiple of 64. 0: off. */
+  int32_t act_quant;
 } dsv4_norm_rope_params;
 DSV4_API int dsv4_norm_rope(const dsv4_norm_rope_params* p, void* stream);
 
@@ -281,6 +286,11 @@ typedef struct {
    * for kv (0) and score+ape (-inf) seeded from the last full block and the remainder */
   float* ring_kv;
   float* ring_score;
+  /* 1: the act-quant simulation of the cached rows (oracle/decode_engine.py:52-54, 82, 105;
+   * v4mlx/compressor.py:11-20, 60-62): dims [0, dim - rope_dim) are rounded to fp8-e4m3 (nearest
+   * even, saturating) in blocks of 64 with a power-of-two scale 2^ceil(log2(max(amax, 1e-4) / 448)),
+   * after the norm and rope, before the store. (dim - rope_dim) must be a multiple of 64. 0: off. */
+  int32_t act_quant;
 } dsv4_compressor_params;
 DSV4_API int dsv4_compressor_pool(const dsv4_compressor_params* p, void* stream);
 
@@ -305,6 +315,11 @@ typedef struct {
   float* key_inv;
   float* key_norm_max;
   int64_t image_stride;
+  /* 1: the act-quant simulation of the cached rows (oracle/decode_engine.py:52-54, 82, 105;
+   * v4mlx/compressor.py:11-20, 60-62): dims [0, dim - rope_dim) are rounded to fp8-e4m3 (nearest
+   * even, saturating) in blocks of 64 with a power-of-two scale 2^ceil(log2(max(amax, 1e-4) / 448)),
+   * after the norm and rope, before the store. (dim - rope_dim) must be a multiple of 64. 0: off. */
+  int32_t act_quant;
 } dsv4_compressor_decode_params;
 DSV4_API int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream);
 

@@ -54,7 +54,7 @@ def _w(v):
 
 
 def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=512, idx_heads=64, idx_dim=128,
-                      rope_dim=64, groups=8, indexer_inputs=None):
+                      rope_dim=64, groups=8, indexer_inputs=None, act_quant=False):
     """fp32 restatement of oracle/decode_engine.py:75-119 plus the indexer selection.
     indexer_inputs=(q_idx, w_idx, k_idx) lets a test score the selection on given inputs.
     Returns (out [s, dim], idx [s, window + top_k], o [s, heads, head_dim])."""
@@ -70,6 +70,10 @@ def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=5
     kv = rope_at(rmsnorm(xn @ _w(W.wkv).T, W.kv_a_norm), pos, f, rope_dim)
     comp, _ = compressor_prefill(xn[None], _w(W.c_wkv), _w(W.c_wgate), W.c_ape, W.c_norm, head_dim=head_dim,
                                  ratio=ratio, rope_head_dim=rope_dim)
+    if act_quant:  # oracle/decode_engine.py:82 (kv rows) and the compressor's sim (v4mlx/compressor.py:60-62)
+        from .quant_ref import act_quant_rows
+        kv = act_quant_rows(kv, rope_dim)
+        comp = act_quant_rows(comp, rope_dim)
     if indexer_inputs is None:
         k_idx, _ = compressor_prefill(xn[None], _w(W.i_wkv), _w(W.i_wgate), W.i_ape, W.i_norm, head_dim=idx_dim,
                                       ratio=ratio, rope_head_dim=rope_dim)
@@ -92,10 +96,13 @@ def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=5
 
 
 def decode_block_ref(state, W, x, positions, top_k=512, window=128, ratio=4, heads=64, head_dim=512, idx_heads=64,
-                     idx_dim=128, rope_dim=64, groups=8):
+                     idx_dim=128, rope_dim=64, groups=8, act_quant=False):
     """One decode token per sequence on host copies of the cache (oracle/v4_fast.py:82-122,
     oracle/decode_engine.py:96-105). `state` = dict(pool, win_base, comp_rows(b, j), k_idx, ring_kv, ring_score,
-    ring_k, ring_s) and is updated in place. Returns out [b, dim]."""
+    ring_k, ring_s) and is updated in place. Returns out [b, dim]. With act_quant the token's kv row and
+    the emitted compressed rows take the fp8 act-quant simulation on their nope dims before they are
+    cached (oracle/decode_engine.py:82, 105)."""
+    from .quant_ref import act_quant_rows
     from .compressor_ref import decode_ring_step
     from .mla_ref import o_grouped
     from .norm_rope_ref import precompute_freqs, rmsnorm
@@ -112,10 +119,14 @@ def decode_block_ref(state, W, x, positions, top_k=512, window=128, ratio=4, hea
     for i in range(b):
         p = int(positions[i])
         row = rope_at(kvp[i][None], torch.tensor([p]), f, rope_dim)[0]
+        if act_quant:
+            row = act_quant_rows(row, rope_dim)
         state["pool"][int(state["win_base"][i]) + p % window] = row.to(torch.bfloat16).float()
         emitted = decode_ring_step(state["ring_kv"][i], state["ring_score"][i], ckv[i], cgt[i], W.c_ape, W.c_norm, p, f,
                                    ratio, rope_dim)
         if emitted is not None:
+            if act_quant:
+                emitted = act_quant_rows(emitted, rope_dim)
             e = (p + 1) // ratio - 1
             state["pool"][int(state["comp_rows"](i, torch.tensor(e)))] = emitted.to(torch.bfloat16).float()
         key = decode_ring_step(state["ring_k"][i], state["ring_s"][i], ikv[i], igt[i], W.i_ape, W.i_norm, p, f, ratio,

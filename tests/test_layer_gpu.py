@@ -92,6 +92,37 @@ def test_decode_block_config5(quant):
     assert (nmax >= fresh[2] * (1 - 1e-6)).all()
 
 
+def test_decode_block_act_quant():
+    """The block step with the reference's fp8 act-quant simulation of the cached kv and compressed
+    rows (oracle/decode_engine.py:82, 105) against the oracle doing the same."""
+    Lm = _layer()
+    C = importlib.import_module(PKG + ".configs")
+    b, ctx = 2, 1024
+    case = C.make_decode_case(b, ctx, 512, seeds=[310, 311])
+    W = Lm.make_attention_weights(5, quant=True)
+    cache = case.cache
+    g = torch.Generator().manual_seed(7)
+    cache.ring_kv.copy_(torch.randn(cache.ring_kv.shape, generator=g))
+    cache.ring_score.copy_(torch.randn(cache.ring_score.shape, generator=g))
+    pos = torch.tensor([ctx - 1, ctx - 2], dtype=torch.int32)
+    x = torch.randn(b, 4096, generator=g)
+    pool, win_base, comp_rows = C.decode_case_host_pool(case)
+    state = dict(pool=pool.float(), win_base=win_base, comp_rows=comp_rows, k_idx=cache.k_idx.cpu().clone(),
+                 ring_kv=cache.ring_kv.cpu().clone(), ring_score=cache.ring_score.cpu().clone(),
+                 ring_k=cache.ring_k_idx.cpu().clone(), ring_s=cache.ring_s_idx.cpu().clone())
+    blk = Lm.DecodeBlock(W.to("cuda"), b, ctx, top_k=512, cache=cache, act_quant=True)
+    out = blk.step(x.cuda(), pos.cuda())
+    ref = LR.decode_block_ref(state, W, x, pos, top_k=512, act_quant=True)
+    rr = rel_rms(out, ref)
+    assert rr <= BLOCK_REL, f"decode block (act quant) rel_rms={rr:.3e}"
+    # the rows this step cached carry fp8 values on their nope dims: at most 16 distinct magnitudes
+    # per 64-dim block once the block scale is divided out (e4m3 has 3 mantissa bits and 16 binades)
+    win_row = cache.kv_pool[int(cache.win_base[0]) + (ctx - 1) % 128].float().cpu()
+    blk0 = win_row[:64]
+    e = int(torch.ceil(torch.log2(blk0.abs().max().clamp(min=1e-4) / 448)))
+    assert torch.equal(blk0, (blk0 / 2.0 ** e).to(torch.float8_e4m3fn).float() * 2.0 ** e)
+
+
 def test_decode_block_steps_keep_key_image():
     """Eight decode steps (two block closings per sequence): the incrementally kept key image
     matches a rebuild, and the indexer reading it selects what the split-every-call path selects."""

@@ -384,6 +384,52 @@ def test_compressor_decode_state_and_rows(dsv4, hd, b):
         torch.testing.assert_close(grs.cpu(), rs, rtol=1e-6, atol=1e-6)
 
 
+def test_norm_rope_act_quant(dsv4):
+    """The kv row's fp8 act-quant simulation fused into the norm + rope kernel: the quantised output
+    is the oracle's act-quant of the unquantised output (bit for bit, fp32 and bf16 outputs)."""
+    from oracle import quant_ref as Q
+    g = torch.Generator().manual_seed(31)
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1).to(DEV)
+    kv = (torch.randn(9, 512, generator=g) * torch.exp2(torch.randint(-12, 8, (9, 1), generator=g).float())).to(DEV)
+    w = (torch.rand(512, generator=g) + 0.5).to(DEV)
+    pos = torch.tensor([0, 1, 7, 100, 4095, 32767, 5, 6, 65535], dtype=torch.int32, device=DEV)
+    plain = dsv4.norm_rope(kv, pos, f, weight=w, out_dtype=torch.float32)
+    quant = dsv4.norm_rope(kv, pos, f, weight=w, out_dtype=torch.float32, act_quant=True)
+    ref = Q.act_quant_rows(plain.cpu())
+    np.testing.assert_array_equal(quant.cpu().numpy().view(np.uint32), ref.numpy().view(np.uint32))
+    qb = dsv4.norm_rope(kv, pos, f, weight=w, out_dtype=torch.bfloat16, act_quant=True).float().cpu()
+    assert torch.equal(qb[:, :448], ref[:, :448])      # fp8 values times powers of two are exact in bf16
+    assert torch.equal(qb[:, 448:], ref[:, 448:].bfloat16().float())   # the rope dims: one bf16 rounding
+
+
+def test_compressor_act_quant(dsv4):
+    """Prefill rows and decode-emitted rows with the fp8 act-quant simulation of their nope dims:
+    the oracle's act-quant of the same kernels' unquantised rows."""
+    from oracle import quant_ref as Q
+    g = torch.Generator().manual_seed(32)
+    x = torch.randn(2, 24, 256, generator=g)
+    wkv = torch.randn(1024, 256, generator=g) * 0.05
+    wgate = torch.randn(1024, 256, generator=g) * 0.05
+    ape = torch.randn(4, 1024, generator=g) * 0.1
+    nw = torch.rand(512, generator=g) + 0.5
+    args = (x.to(DEV), wkv.to(DEV).bfloat16(), wgate.to(DEV).bfloat16(), ape.to(DEV), nw.to(DEV))
+    plain, st0 = dsv4.compressor_prefill(*args)
+    quant, st1 = dsv4.compressor_prefill(*args, act_quant=True)
+    np.testing.assert_array_equal(quant.cpu().numpy().view(np.uint32), Q.act_quant_rows(plain.cpu()).numpy().view(np.uint32))
+    # decode: identical rings, one emission each
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1).to(DEV)
+    kvp, scp = torch.randn(2, 1024, generator=g).to(DEV), torch.randn(2, 1024, generator=g).to(DEV)
+    outs = []
+    for aq in (False, True):
+        rk, rs = st0["ring_kv"].clone(), st0["ring_score"].clone()
+        pool = torch.zeros(2, 512, device=DEV)
+        dsv4.compressor_decode_step(kvp, None, None, ape.to(DEV), nw.to(DEV), rk, rs,
+                                    torch.tensor([27, 27], dtype=torch.int32, device=DEV), pool,
+                                    torch.tensor([0, 1], device=DEV), freqs=f, proj=(kvp, scp), act_quant=aq)
+        outs.append(pool.cpu())
+    np.testing.assert_array_equal(outs[1].numpy().view(np.uint32), Q.act_quant_rows(outs[0]).numpy().view(np.uint32))
+
+
 def test_compressor_decode_ring(dsv4):
     g = torch.Generator().manual_seed(8)
     dim, s0 = 128, 13

@@ -68,3 +68,17 @@ def test_decode_ring_continues_prefill(golden):
         row = C.decode_ring_step(rk[0], rs[0], kvp[0, p], scp[0, p], ape, nw, p, f)
         assert (row is None) == (p != 19)
     np.testing.assert_allclose(row.numpy(), full[0, 4].numpy(), rtol=1e-4, atol=1e-5)
+
+
+def _qat_golden():
+    import os
+    return np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "qat_golden.npz"))
+
+
+def test_act_quant_matches_reference():
+    """The fp8-e4m3 act-quant oracle against the reference's own `aq` (oracle/decode_engine.py:52-54)
+    on rows spanning 1e-6..1e3, an all-zero block and a block of exact powers of two: bit for bit."""
+    from oracle import quant_ref as Q
+    g = _qat_golden()
+    got = Q.act_quant_sim(g["aq_x"])
+    np.testing.assert_array_equal(got.view(np.uint32), g["aq_y"].view(np.uint32))
