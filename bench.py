@@ -270,7 +270,7 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--replicas", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", default=None, choices=["attn_prefill", "indexer_prefill", "block_decode"],
+    ap.add_argument("--kernel-case", default=None, choices=["attn_prefill", "indexer_prefill", "block_decode", "hc"],
                     help="profiling aid: run one prefill kernel alone on a 4096-query slice of config 4 "
                          "(positions 60000..64095), or config 5's block step eagerly inside an NVTX range "
                          "(block_decode), and print its CUDA-event time; not a bench line")
@@ -752,6 +752,8 @@ def run_kernel_case(args):
     NRm = importlib.import_module(PKG + ".norm_rope")
     if args.kernel_case == "block_decode":
         return run_block_case(args, dev)
+    if args.kernel_case == "hc":
+        return run_hc_case(args, dev)
     s, nwin, ncomp, top_k = 4096, 65536, 16384, 1024
     g = torch.Generator(device=dev).manual_seed(0)
     pos = torch.arange(60000, 60000 + s, dtype=torch.int32, device=dev)
@@ -783,6 +785,54 @@ def run_kernel_case(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
     print(json.dumps({"kernel_case": args.kernel_case, "queries": s, "ms_per_call": ms, **work}), flush=True)
+
+
+def run_hc_case(args, dev):
+    """The hyper-connection kernels around the block (dim 4096, hc 4): hc_pre with the block's
+    RMSNorm fused (bf16 output) and hc_post, at config 5's decode batch (32 tokens; x and the
+    weights stay in L2 between calls) and at a 4096-token prefill slice (x 268 MB, above L2), each
+    timed as one replay of a CUDA graph of `--steps` calls (default 20).
+    Algorithmic bytes per call: hc_pre reads x (16 dim B per token) and fn once (1.5 MB), writes the
+    bf16 norm (2 dim B per token) and post / comb; hc_post reads x and the residual (20 dim B per
+    token) and writes 16 dim B per token."""
+    import importlib
+    H = importlib.import_module(PKG + ".hc")
+    dim = 4096
+    g = torch.Generator(device=dev).manual_seed(0)
+    fn_w = torch.randn(24, 4 * dim, device=dev, generator=g) * 0.02
+    scale = torch.rand(3, device=dev, generator=g) + 0.5
+    base = torch.randn(24, device=dev, generator=g) * 0.1
+    nw = (torch.rand(dim, device=dev, generator=g) + 0.5).bfloat16()
+    reps = args.steps if args.steps is not None else 20
+    res = {}
+    for tokens in (CONFIGS["c5"]["batch"], 4096):
+        x = torch.randn(tokens, 4, dim, device=dev, generator=g)
+        att = torch.randn(tokens, dim, device=dev, generator=g)
+        _, post, comb, _ = H.hc_pre(x, fn_w, scale, base, norm_w=nw)
+        cases = {
+            "hc_pre_norm": (lambda: H._hc_call(x, fn_w, scale, base, 0, nw, want_y=False),
+                            tokens * (16 * dim + 2 * dim + 80) + fn_w.numel() * 4),
+            "hc_post": (lambda: H.hc_post(att, x, post, comb), tokens * (36 * dim + 80)),
+        }
+        for name, (fn, nbytes) in cases.items():
+            # `reps` calls captured in one CUDA graph: the device time without the host's launch gaps
+            fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(reps):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / reps * 1000
+            res[f"{name}_t{tokens}"] = {"us_per_call": round(us, 2), "alg_bytes": nbytes,
+                                        "gbs": round(nbytes / us / 1000, 1)}
+    print(json.dumps({"kernel_case": "hc", "dim": dim, **res}), flush=True)
 
 
 def run_block_case(args, dev):

@@ -89,6 +89,13 @@ class LinearParams(ctypes.Structure):
                 ("workspace", vp), ("workspace_bytes", sz)]
 
 
+class HcParams(ctypes.Structure):
+    _fields_ = [("x", vp), ("fn", vp), ("scale", vp), ("base", vp), ("y", vp), ("post", vp), ("comb", vp),
+                ("norm_w", vp), ("y_norm", vp), ("workspace", vp), ("workspace_bytes", ctypes.c_size_t), ("rows", i64), ("hc", i32), ("dim", i32), ("sinkhorn_iters", i32),
+                ("head", i32), ("norm_dtype", i32), ("y_norm_dtype", i32), ("norm_eps", f32), ("hc_eps", f32),
+                ("y_norm_eps", f32)]
+
+
 LINEAR_MULTI_MAX = 8
 
 
@@ -127,6 +134,9 @@ SIGNATURES = {
     "dsv4_compressor_pool": (ctypes.c_int, [ctypes.POINTER(CompressorParams), vp]),
     "dsv4_compressor_decode": (ctypes.c_int, [ctypes.POINTER(CompressorDecodeParams), vp]),
     "dsv4_decode_rows": (ctypes.c_int, [ctypes.POINTER(DecodeRowsParams), vp]),
+    "dsv4_hc_pre": (ctypes.c_int, [ctypes.POINTER(HcParams), vp]),
+    "dsv4_hc_workspace_size": (ctypes.c_size_t, [i64, i32, i32, i32]),
+    "dsv4_hc_post": (ctypes.c_int, [vp, vp, vp, vp, vp, i64, i32, i32, vp]),
     "dsv4_indexer_key_image": (ctypes.c_int, [ctypes.POINTER(KeyImageParams), vp]),
     "dsv4_linear_workspace_size": (sz, [ctypes.POINTER(LinearParams)]),
     "dsv4_linear": (ctypes.c_int, [ctypes.POINTER(LinearParams), vp]),

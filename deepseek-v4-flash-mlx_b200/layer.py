@@ -23,6 +23,7 @@ from . import _lib as L
 from .compressor import compressor_decode_step, compressor_prefill
 from .configs import DIMS, LayerDims
 from .decode import SparseMLACache, decode_attention, decode_rows
+from .hc import hc_post, hc_pre
 from .indexer import indexer_topk_into
 from .mla import QuantWeight, linear, linear_multi, o_grouped, quantize_int8_g64
 from .norm_rope import norm_rope, rmsnorm, rope, rope_freqs
@@ -146,12 +147,22 @@ class DecodeBlock:
 
     def step(self, x, positions):
         """x [b, dim] fp32/bf16, positions int32 [b] (position of this token) -> out [b, dim] fp32."""
+        # the normed activations feed only bf16 projections: rounded to bf16 once, by the norm
+        return self._attend(rmsnorm(x, self.W.attn_norm, out_dtype=torch.bfloat16), positions)
+
+    def step_hc(self, x, positions, hc_fn, hc_scale, hc_base, sinkhorn_iters=20, hc_eps=1e-6):
+        """The block inside its hyper-connections (the decode layer's hc_pre -> attn_norm -> attention
+        -> hc_post, oracle/v4_fast.py:85-86, 122): x [b, hc, dim] fp32 residual copies -> [b, hc, dim].
+        hc_pre and the attention norm run as one kernel (bf16 output for the projections)."""
+        _, post, comb, xn = hc_pre(x, hc_fn, hc_scale, hc_base, sinkhorn_iters=sinkhorn_iters, hc_eps=hc_eps,
+                                   norm_w=self.W.attn_norm)
+        return hc_post(self._attend(xn, positions), x, post, comb)
+
+    def _attend(self, xn, positions):
         d, W, c = self.dims, self.W, self.cache
-        b = x.shape[0]
+        b = xn.shape[0]
         pos = positions.to(torch.int32).contiguous()
-        # the normed activations feed only bf16 projections: rounded to bf16 once, by the norm; the
-        # seven projections of xn run as one launch, the two of qa as another
-        xn = rmsnorm(x, W.attn_norm, out_dtype=torch.bfloat16)
+        # the seven projections of xn run as one launch, the two of qa as another
         qa_p, kvp, c_kv, c_sc, w_idx, i_kv, i_sc = linear_multi(
             xn, [W.wq_a, W.wkv, W.c_wkv, W.c_wgate, W.i_wproj, W.i_wkv, W.i_wgate], torch.float32)
         qa = rmsnorm(qa_p, W.q_a_norm, out_dtype=torch.bfloat16)

@@ -387,6 +387,41 @@ typedef struct {
 } dsv4_linear_multi_params;
 DSV4_API int dsv4_linear_multi(const dsv4_linear_multi_params* p, void* stream);
 
+/* ---- hyper-connections around the attention block (ref_torch/hc.py:18-80) -----------------------
+ * hc_pre (head == 0): x [rows, hc, dim] fp32 (the hc = 4 residual copies of a token) ->
+ *   mixes = (x . fn^T) * rsqrt(mean(x^2) + norm_eps), fn [(2 + hc) * hc, hc * dim];
+ *   pre = sigmoid(mixes[0:hc] * scale[0] + base[0:hc]) + hc_eps, post = 2 sigmoid(mixes[hc:2hc] *
+ *   scale[1] + base[hc:2hc]), comb = Sinkhorn(mixes[2hc:] * scale[2] + base[2hc:]) [hc, hc] (row
+ *   softmax + hc_eps, column normalise, then sinkhorn_iters - 1 rounds of row and column
+ *   normalisation, each dividing by the sum + hc_eps), y[d] = sum_k pre[k] x[k, d].
+ * hc_head (head == 1): fn [hc, hc * dim], scale [1]: pre only, y as above (ParallelHead.hc_head).
+ * Optional in the same launch: y_norm = RMSNorm(y) * norm_w (the attention block's first norm;
+ * eps y_norm_eps) in y_norm_dtype. hc == 4, dim a multiple of 4 and at most 4096. Two launches: the
+ * split-K mixes into the workspace, then the split, y and the norm, one CTA per token. */
+typedef struct {
+  const float* x;
+  const float* fn;
+  const float* scale;
+  const float* base;
+  float* y;               /* [rows, dim] or NULL */
+  float* post;            /* [rows, hc] (hc_pre) */
+  float* comb;            /* [rows, hc, hc] (hc_pre) */
+  const void* norm_w;     /* [dim] norm_dtype, or NULL (no weight) */
+  void* y_norm;           /* [rows, dim] y_norm_dtype, or NULL */
+  void* workspace;        /* the split-K partial mixes; dsv4_hc_workspace_size bytes */
+  size_t workspace_bytes;
+  int64_t rows;
+  int32_t hc, dim, sinkhorn_iters, head;
+  int32_t norm_dtype, y_norm_dtype;
+  float norm_eps, hc_eps, y_norm_eps;
+} dsv4_hc_params;
+DSV4_API int dsv4_hc_pre(const dsv4_hc_params* p, void* stream);
+DSV4_API size_t dsv4_hc_workspace_size(int64_t rows, int32_t hc, int32_t dim, int32_t head);
+/* hc_post: out[row, j, d] = post[row, j] x[row, d] + sum_i comb[row, i, j] residual[row, i, d];
+ * x [rows, dim], residual [rows, hc, dim], all fp32 (Block.hc_post). */
+DSV4_API int dsv4_hc_post(const float* x, const float* residual, const float* post, const float* comb, float* out,
+                          int64_t rows, int32_t hc, int32_t dim, void* stream);
+
 /* ---- casts used by the op layer (fp32 <-> bf16) ---- */
 DSV4_API int dsv4_cast(const void* x, int32_t x_dtype, void* y, int32_t y_dtype, int64_t numel, void* stream);
 

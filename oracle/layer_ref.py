@@ -137,3 +137,14 @@ def decode_block_ref(state, W, x, positions, top_k=512, window=128, ratio=4, hea
     o = decode_attention_ref(state["pool"], state["win_base"], state["comp_rows"], state["k_idx"], qraw, q_idx, w_idx,
                              W.sinks, positions, top_k, f, window=window, ratio=ratio, scale=head_dim ** -0.5)
     return o_grouped(o.reshape(b, -1), _w(W.wo_a), _w(W.wo_b), groups=groups)
+
+
+def decode_block_hc_ref(state, W, x, positions, hc_fn, hc_scale, hc_base, **kw):
+    """The block inside its hyper-connections (oracle/v4_fast.py:85, 122): x [b, hc, dim] ->
+    hc_post(block(hc_pre(x)), x) [b, hc, dim], in float64 for the mixes (hc_ref) and the block's
+    own oracle in between. Returns (out, post, comb) as torch float32 / float64."""
+    from . import hc_ref as H
+    y, post, comb = H.hc_pre(x.numpy(), hc_fn.numpy(), hc_scale.numpy(), hc_base.numpy())
+    att = decode_block_ref(state, W, torch.from_numpy(y).float(), positions, **kw)
+    out = H.hc_post(att.double().numpy(), x.numpy(), post, comb)
+    return torch.from_numpy(out), post, comb

@@ -25,6 +25,7 @@ PAIRS = {
     "dsv4_linear_out": L.LinearOut,
     "dsv4_linear_multi_params": L.LinearMultiParams,
     "dsv4_key_image_params": L.KeyImageParams,
+    "dsv4_hc_params": L.HcParams,
 }
 
 

@@ -123,6 +123,39 @@ def test_decode_block_act_quant():
     assert torch.equal(blk0, (blk0 / 2.0 ** e).to(torch.float8_e4m3fn).float() * 2.0 ** e)
 
 
+def test_decode_block_hc():
+    """The block step inside hc_pre / hc_post (oracle/v4_fast.py:85, 122), with hc_pre and the
+    attention norm fused in one kernel, against the oracle chain. The residual term
+    sum_i comb[i, j] x[i] is removed from both sides before the block tolerance is applied, so the
+    check sees the attention output's share."""
+    from oracle import hc_ref as H
+    Lm = _layer()
+    C = importlib.import_module(PKG + ".configs")
+    b, ctx = 2, 1024
+    case = C.make_decode_case(b, ctx, 512, seeds=[320, 321])
+    W = Lm.make_attention_weights(6, quant=True)
+    cache = case.cache
+    g = torch.Generator().manual_seed(8)
+    cache.ring_kv.copy_(torch.randn(cache.ring_kv.shape, generator=g))
+    cache.ring_score.copy_(torch.randn(cache.ring_score.shape, generator=g))
+    pos = torch.tensor([ctx - 1, ctx - 2], dtype=torch.int32)
+    x = torch.randn(b, 4, 4096, generator=g)
+    hc_fn = torch.randn(24, 4 * 4096, generator=g) * 0.02
+    hc_scale, hc_base = torch.rand(3, generator=g) + 0.5, torch.randn(24, generator=g) * 0.1
+    pool, win_base, comp_rows = C.decode_case_host_pool(case)
+    state = dict(pool=pool.float(), win_base=win_base, comp_rows=comp_rows, k_idx=cache.k_idx.cpu().clone(),
+                 ring_kv=cache.ring_kv.cpu().clone(), ring_score=cache.ring_score.cpu().clone(),
+                 ring_k=cache.ring_k_idx.cpu().clone(), ring_s=cache.ring_s_idx.cpu().clone())
+    blk = Lm.DecodeBlock(W.to("cuda"), b, ctx, top_k=512, cache=cache)
+    out = blk.step_hc(x.cuda(), pos.cuda(), hc_fn.cuda(), hc_scale.cuda(), hc_base.cuda())
+    assert out.shape == (b, 4, 4096) and out.dtype == torch.float32
+    ref, post, comb = LR.decode_block_hc_ref(state, W, x, pos, hc_fn, hc_scale, hc_base, top_k=512)
+    resid = torch.from_numpy(H.hc_post(np.zeros((b, 4096)), x.numpy(), np.zeros((b, 4)), comb))
+    rr = rel_rms(out.double().cpu() - resid, ref - resid)
+    assert rr <= BLOCK_REL, f"decode block (hc) rel_rms={rr:.3e}"
+    assert_close_bf16(cache.kv_pool.float().cpu(), state["pool"], what="pool after hc step")
+
+
 def test_decode_block_steps_keep_key_image():
     """Eight decode steps (two block closings per sequence): the incrementally kept key image
     matches a rebuild, and the indexer reading it selects what the split-every-call path selects."""

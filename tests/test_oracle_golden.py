@@ -82,3 +82,20 @@ def test_act_quant_matches_reference():
     g = _qat_golden()
     got = Q.act_quant_sim(g["aq_x"])
     np.testing.assert_array_equal(got.view(np.uint32), g["aq_y"].view(np.uint32))
+
+
+def test_hc_matches_reference():
+    """hc_pre / hc_post / hc_head oracle against the reference's ref_torch/hc.py outputs."""
+    from oracle import hc_ref as H
+    g = _qat_golden()
+    y, post, comb = H.hc_pre(g["hc_x"], g["hc_fn"], g["hc_scale"], g["hc_base"])
+    np.testing.assert_allclose(y, g["hc_y"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(post, g["hc_post"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(comb, g["hc_comb"], rtol=1e-5, atol=1e-6)
+    # the Sinkhorn result is doubly stochastic to within its eps terms
+    np.testing.assert_allclose(comb.sum(-2), 1.0, atol=1e-4)
+    np.testing.assert_allclose(comb.sum(-1), 1.0, atol=1e-4)
+    out = H.hc_post(g["hc_att"], g["hc_x"], g["hc_post"], g["hc_comb"])
+    np.testing.assert_allclose(out, g["hc_post_y"], rtol=1e-5, atol=1e-5)
+    yh = H.hc_head(g["hc_x"], g["hc_head_fn"], g["hc_head_scale"], g["hc_head_base"])
+    np.testing.assert_allclose(yh, g["hc_head_y"], rtol=1e-5, atol=1e-6)
