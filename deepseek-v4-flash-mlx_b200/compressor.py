@@ -36,7 +36,7 @@ def _pool(kv, score, ape, norm_w, out, head_dim, ratio, rope_dim, freqs, ring_kv
 
 def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_head_dim=64,
                        base=160000.0, original_seq_len=65536, factor=16, beta_fast=32, beta_slow=1,
-                       out_dtype=torch.float32, pos0=0, act_quant=False):
+                       out_dtype=torch.float32, pos0=0, act_quant=False, rotate=False):
     """x [b, s, dim] -> (kv [b, s//ratio, head_dim] post-rope, state).
 
     state: "kv" / "score" = the last full block's kv and score+ape [b, ratio, 2*head_dim] (when
@@ -44,7 +44,9 @@ def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_h
     the device ring that `compressor_decode_step` continues from (ref_torch/compressor.py:67-74).
     `pos0` is the position of x's first token (a slice of a longer sequence): row g is roped at
     pos0 + ratio*g. `act_quant`: the fp8-e4m3 act-quant simulation of each row's nope dims (the
-    reference's default for the main compressor, v4mlx/compressor.py:60-62)."""
+    reference's default for the main compressor, v4mlx/compressor.py:60-62). `rotate` (head_dim
+    128, the indexer compressor; v4mlx/compressor.py:57-59): instead, every dim of each row is
+    rotated by the normalised Walsh-Hadamard transform and rounded to fp4-e2m1 in blocks of 32."""
     L.require_cuda(x, wkv, wgate, ape, norm_w)
     b, s, _ = x.shape
     d2 = 2 * head_dim
@@ -58,7 +60,7 @@ def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_h
     ring_score = torch.empty_like(ring_kv)
     nw = norm_w if norm_w.dtype in (torch.float32, torch.bfloat16) else norm_w.float()
     _pool(kv, score, ape.float().contiguous(), nw.contiguous(), out, head_dim, ratio, rope_head_dim, freqs,
-          ring_kv, ring_score, pos0=pos0, act_quant=act_quant)
+          ring_kv, ring_score, pos0=pos0, act_quant=2 if rotate else act_quant)
     cutoff = s - s % ratio
     state = {"ring_kv": ring_kv, "ring_score": ring_score}
     if cutoff >= ratio:
@@ -71,14 +73,15 @@ def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_h
 
 def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, positions, out, out_rows,
                            head_dim=512, ratio=4, rope_head_dim=64, freqs=None, eps=1e-6,
-                           proj=None, key_image=None, act_quant=False):
+                           proj=None, key_image=None, act_quant=False, rotate=False):
     """One decode token per sequence (oracle/decode_engine.py:96-105): write this token's kv / score
     into the device ring; sequences whose position p has (p+1) % ratio == 0 emit a pooled, normed,
     roped row into out[out_rows[b]] and shift the ring. x [b, dim]; positions int32 [b].
     `proj` may pass precomputed projections (kv, score) [b, 2*head_dim] fp32. `key_image`
     (image, inv, norm_max, keys_per_entry) also adds each emitted indexer key (out viewed as
     [entries * keys_per_entry, 128] fp32) to a decode cache's key image. `act_quant`: the fp8-e4m3
-    act-quant simulation of the emitted row's nope dims (oracle/decode_engine.py:105)."""
+    act-quant simulation of the emitted row's nope dims (oracle/decode_engine.py:105). `rotate`
+    (head_dim 128): the Hadamard + fp4-e2m1 key simulation of `compressor_prefill(rotate=True)`."""
     L.require_cuda(x, ring_kv, ring_score, positions, out, out_rows)
     if proj is None:
         kvp = linear(x, wkv, torch.float32)
@@ -98,7 +101,7 @@ def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, posi
     p.out_dtype = L.dtype_code(out)
     p.eps = eps
     p.freqs = L.ptr(freqs)
-    p.act_quant = int(act_quant)
+    p.act_quant = 2 if rotate else int(act_quant)
     if key_image is not None:
         img, inv, nmax, stride = key_image
         p.key_image, p.key_inv, p.key_norm_max, p.image_stride = L.ptr(img), L.ptr(inv), L.ptr(nmax), int(stride)

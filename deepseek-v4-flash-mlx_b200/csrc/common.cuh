@@ -154,6 +154,20 @@ __device__ __forceinline__ int act_quant_exp(float amax) {
   return static_cast<int>((b >> 23) & 0xff) - 127 + ((b & 0x7fffff) != 0 ? 1 : 0);
 }
 
+// nearest fp4-e2m1 value (ties to the even mantissa) of y, |y| <= 6: the format holds 0, 0.5, 1,
+// 1.5, 2, 3, 4, 6, i.e. spacing 0.5 below 2, 1 in [2, 4) and 2 in [4, 6]; every step is exact
+__device__ __forceinline__ float e2m1_round(float y) {
+  const float a = fabsf(y);
+  const float q = a < 2.f ? rintf(2.f * a) * 0.5f : (a < 4.f ? rintf(a) : 2.f * rintf(0.5f * a));
+  return copysignf(q, y);
+}
+// the fp4 block scale exponent: ceil(log2(max(amax, 6 * 2^-126) / 6)), from the bits of the
+// (correctly rounded) fp32 quotient; in [-126, 126] for finite amax
+__device__ __forceinline__ int fp4_exp(float amax) {
+  const uint32_t b = __float_as_uint(fmaxf(amax, __uint_as_float(0x01C00000u)) / 6.f);
+  return static_cast<int>((b >> 23) & 0xff) - 127 + ((b & 0x7fffff) != 0 ? 1 : 0);
+}
+
 // rope angle as the reference forms it: fp32 product of the position and the frequency
 // (torch.outer in fp32, ref_torch/norm_rope.py:48-50), then cos/sin of that fp32 angle.
 __device__ __forceinline__ void rope_cos_sin(int pos, float freq, float* c, float* s) {

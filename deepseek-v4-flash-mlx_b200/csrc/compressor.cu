@@ -47,8 +47,68 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return red[32];
 }
 
+__device__ __forceinline__ void store_pair(float v0, float v1, int c, int d, void* out, int64_t orow, int out_dtype) {
+  const int64_t off = orow * d + c;
+  if (out_dtype == DSV4_BF16)
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(out) + off) = pack_bf16x2(v0, v1);
+  else
+    *reinterpret_cast<float2*>(reinterpret_cast<float*>(out) + off) = make_float2(v0, v1);
+}
+
+// The indexer compressor's key simulation (act_quant mode 2; v4mlx/compressor.py:57-59 with
+// v4mlx/qat.py:8-31) on a 128-dim row held as pairs (2 tid, 2 tid + 1) by threads 0..63: the
+// normalised Walsh-Hadamard transform (width-1 butterflies in the thread, widths 2..32 across lanes,
+// width 64 across the two warps through `xch`, then float32(128^-0.5)), and the fp4-e2m1 round
+// trip per 32-dim block (16 lanes). Every thread of the CTA calls it (one barrier).
+__device__ __forceinline__ void hadamard_fp4_128(float& v0, float& v1, float* xch) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const bool mine = tid < 64;
+  const float a = v0 + v1, b = v0 - v1;
+  v0 = a;
+  v1 = b;
+#pragma unroll
+  for (int o = 1; o <= 16; o <<= 1) {
+    const float p0 = __shfl_xor_sync(0xffffffffu, v0, o), p1 = __shfl_xor_sync(0xffffffffu, v1, o);
+    if (lane & o) {
+      v0 = p0 - v0;
+      v1 = p1 - v1;
+    } else {
+      v0 = v0 + p0;
+      v1 = v1 + p1;
+    }
+  }
+  if (mine) {
+    xch[2 * tid] = v0;
+    xch[2 * tid + 1] = v1;
+  }
+  __syncthreads();
+  if (mine) {
+    const float p0 = xch[2 * (tid ^ 32)], p1 = xch[2 * (tid ^ 32) + 1];
+    if (tid & 32) {
+      v0 = p0 - v0;
+      v1 = p1 - v1;
+    } else {
+      v0 = v0 + p0;
+      v1 = v1 + p1;
+    }
+    v0 *= 0.08838834764831845f;  // float32(128^-0.5)
+    v1 *= 0.08838834764831845f;
+  }
+  float m = fmaxf(fabsf(v0), fabsf(v1));
+#pragma unroll
+  for (int o = 1; o <= 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (mine) {
+    const int e = fp4_exp(m);
+    const float dn = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+    const float up = __uint_as_float(static_cast<uint32_t>(127 + e) << 23);
+    v0 = e2m1_round(fminf(fmaxf(v0 * dn, -6.f), 6.f)) * up;
+    v1 = e2m1_round(fminf(fmaxf(v1 * dn, -6.f), 6.f)) * up;
+  }
+}
+
 // normalise, rope and store two adjacent dims (c, c+1) of one compressed row; the stored values
-// (before the cast) are left in v0, v1
+// (before the cast) are left in v0, v1. In act_quant mode 2 the pair is left unstored for
+// hadamard_fp4_128 and store_pair.
 __device__ __forceinline__ void finish_pair(float& v0, float& v1, int c, int d, int rope_dim,
                                             const void* norm_w, int norm_dtype, float rinv,
                                             const float* freqs, int pos, void* out, int64_t orow,
@@ -66,16 +126,13 @@ __device__ __forceinline__ void finish_pair(float& v0, float& v1, int c, int d, 
   }
   // fp8 act-quant simulation of the nope dims: a 64-dim block is the 32 pairs of one warp (the
   // condition is warp-uniform)
-  if (act_quant && c < d - rope_dim) {
+  if (act_quant == 1 && c < d - rope_dim) {
     const int ex = act_quant_exp(warp_max(fmaxf(fabsf(v0), fabsf(v1))));
     v0 = fp8_round_pow2(v0, ex);
     v1 = fp8_round_pow2(v1, ex);
   }
-  const int64_t off = orow * d + c;
-  if (out_dtype == DSV4_BF16)
-    *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(out) + off) = pack_bf16x2(v0, v1);
-  else
-    *reinterpret_cast<float2*>(reinterpret_cast<float*>(out) + off) = make_float2(v0, v1);
+  if (act_quant == 2) return;
+  store_pair(v0, v1, c, d, out, orow, out_dtype);
 }
 
 // softmax over 8 slots (max-subtracted, as torch.softmax) and the weighted sum
@@ -151,6 +208,11 @@ __global__ void __launch_bounds__(THREADS) pool_kernel(dsv4_compressor_params p)
   for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++npairs)
     finish_pair(vals[npairs][0], vals[npairs][1], c, d, p.rope_dim, p.norm_w, p.norm_dtype, rinv,
                 p.freqs, p.pos0 + R * g, p.out, orow, p.out_dtype, p.act_quant);
+  if (p.act_quant == 2) {  // head_dim 128: threads 0..63 hold the row (uniform over the CTA)
+    __shared__ float xch[128];
+    hadamard_fp4_128(vals[0][0], vals[0][1], xch);
+    if (threadIdx.x < 64) store_pair(vals[0][0], vals[0][1], 2 * threadIdx.x, d, p.out, orow, p.out_dtype);
+  }
 }
 
 // decode hand-off ring (ref_torch/compressor.py:67-74; seeding as oracle/decode_engine.py:91-95):
@@ -324,6 +386,11 @@ __global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_deco
     st2(rk + (R - 1) * d2 + d + c, nk[np][1]);
     st2(rs + (R - 1) * d2 + d + c, ns[np][1]);
   }
+  if (p.act_quant == 2) {  // head_dim 128: threads 0..63 hold the row (uniform over the CTA)
+    __shared__ float xch[128];
+    hadamard_fp4_128(vals[0][0], vals[0][1], xch);
+    if (tid < 64) store_pair(vals[0][0], vals[0][1], 2 * tid, d, p.out, p.out_rows[b], p.out_dtype);
+  }
   if (p.key_image) append_key_image<NP>(p, vals, red);
 }
 
@@ -379,6 +446,12 @@ __global__ void __launch_bounds__(THREADS) decode_kernel(dsv4_compressor_decode_
   for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++np)
     finish_pair(vals[np][0], vals[np][1], c, d, p.rope_dim, p.norm_w, p.norm_dtype, rinv, p.freqs,
                 pos + 1 - R, p.out, p.out_rows[b], p.out_dtype, p.act_quant);
+  if (p.act_quant == 2) {  // head_dim 128: threads 0..63 hold the row (uniform over the CTA)
+    __shared__ float xch[128];
+    hadamard_fp4_128(vals[0][0], vals[0][1], xch);
+    if (threadIdx.x < 64)
+      store_pair(vals[0][0], vals[0][1], 2 * threadIdx.x, d, p.out, p.out_rows[b], p.out_dtype);
+  }
   for (int c = threadIdx.x; c < d2; c += blockDim.x)
     for (int r = 0; r < R; ++r) {
       rk[r * d2 + c] = rk[(R + r) * d2 + c];
@@ -393,8 +466,10 @@ using namespace dsv4;
 
 extern "C" int dsv4_compressor_pool(const dsv4_compressor_params* p, void* stream) {
   DSV4_CHECK_ARG(p == nullptr || p->act_quant == 0 ||
-                     (p->act_quant == 1 && p->head_dim % 64 == 0 && (p->head_dim - p->rope_dim) % 64 == 0),
-                 "dsv4_compressor_pool: act_quant needs head_dim and head_dim - rope_dim multiples of 64");
+                     (p->act_quant == 1 && p->head_dim % 64 == 0 && (p->head_dim - p->rope_dim) % 64 == 0) ||
+                     (p->act_quant == 2 && p->head_dim == 128),
+                 "dsv4_compressor_pool: act_quant 1 needs head_dim and head_dim - rope_dim multiples of 64, "
+                 "act_quant 2 (Hadamard + fp4) head_dim 128");
   DSV4_CHECK_ARG(p && p->kv && p->score && p->ape && p->out && p->freqs, "dsv4_compressor_pool: NULL tensor");
   DSV4_CHECK_ARG(p->b > 0 && p->s >= 0 && p->ratio > 0 && p->ratio <= 8, "dsv4_compressor_pool: bad sizes");
   DSV4_CHECK_ARG(p->head_dim % 2 == 0 && p->head_dim <= 4 * cmp::THREADS && p->head_dim >= p->rope_dim &&
@@ -418,8 +493,10 @@ extern "C" int dsv4_compressor_pool(const dsv4_compressor_params* p, void* strea
 
 extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream) {
   DSV4_CHECK_ARG(p == nullptr || p->act_quant == 0 ||
-                     (p->act_quant == 1 && p->head_dim % 64 == 0 && (p->head_dim - p->rope_dim) % 64 == 0),
-                 "dsv4_compressor_decode: act_quant needs head_dim and head_dim - rope_dim multiples of 64");
+                     (p->act_quant == 1 && p->head_dim % 64 == 0 && (p->head_dim - p->rope_dim) % 64 == 0) ||
+                     (p->act_quant == 2 && p->head_dim == 128),
+                 "dsv4_compressor_decode: act_quant 1 needs head_dim and head_dim - rope_dim multiples of 64, "
+                 "act_quant 2 (Hadamard + fp4) head_dim 128");
   DSV4_CHECK_ARG(p && p->kv && p->score && p->ape && p->ring_kv && p->ring_score && p->positions &&
                      p->out && p->out_rows && p->freqs,
                  "dsv4_compressor_decode: NULL tensor");

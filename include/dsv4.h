@@ -289,7 +289,12 @@ typedef struct {
   /* 1: the act-quant simulation of the cached rows (oracle/decode_engine.py:52-54, 82, 105;
    * v4mlx/compressor.py:11-20, 60-62): dims [0, dim - rope_dim) are rounded to fp8-e4m3 (nearest
    * even, saturating) in blocks of 64 with a power-of-two scale 2^ceil(log2(max(amax, 1e-4) / 448)),
-   * after the norm and rope, before the store. (dim - rope_dim) must be a multiple of 64. 0: off. */
+   * after the norm and rope, before the store. (dim - rope_dim) must be a multiple of 64.
+   * 2: the indexer compressor's key simulation (compressor_prefill(..., rotate=True),
+   * v4mlx/compressor.py:57-59, v4mlx/qat.py:8-31), head_dim 128: after the norm and rope the whole
+   * row is rotated by the normalised Walsh-Hadamard transform (Sylvester order, fp32 butterflies,
+   * then * fp32(128^-0.5)) and rounded to fp4-e2m1 (nearest even) in blocks of 32 with a scale
+   * 2^ceil(log2(max(amax, 6 * 2^-126) / 6)). 0: off. */
   int32_t act_quant;
 } dsv4_compressor_params;
 DSV4_API int dsv4_compressor_pool(const dsv4_compressor_params* p, void* stream);
@@ -318,7 +323,9 @@ typedef struct {
   /* 1: the act-quant simulation of the cached rows (oracle/decode_engine.py:52-54, 82, 105;
    * v4mlx/compressor.py:11-20, 60-62): dims [0, dim - rope_dim) are rounded to fp8-e4m3 (nearest
    * even, saturating) in blocks of 64 with a power-of-two scale 2^ceil(log2(max(amax, 1e-4) / 448)),
-   * after the norm and rope, before the store. (dim - rope_dim) must be a multiple of 64. 0: off. */
+   * after the norm and rope, before the store. (dim - rope_dim) must be a multiple of 64.
+   * 2: the Hadamard + fp4-e2m1 key simulation of dsv4_compressor_params.act_quant (head_dim 128),
+   * also applied to the row added to the key image. 0: off. */
   int32_t act_quant;
 } dsv4_compressor_decode_params;
 DSV4_API int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream);

@@ -430,6 +430,48 @@ def test_compressor_act_quant(dsv4):
     np.testing.assert_array_equal(outs[1].numpy().view(np.uint32), Q.act_quant_rows(outs[0]).numpy().view(np.uint32))
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_compressor_rotate(dsv4, out_dtype):
+    """The indexer compressor's Hadamard + fp4-e2m1 key simulation (v4mlx/compressor.py:57-59):
+    prefill rows and decode-emitted rows equal the oracle's rotation and round trip of the same
+    kernels' plain rows, bit for bit (bf16 output: after one more rounding of both)."""
+    from oracle import quant_ref as Q
+    g = torch.Generator().manual_seed(33)
+    x = torch.randn(2, 40, 256, generator=g)
+    wkv = torch.randn(256, 256, generator=g) * 0.05
+    wgate = torch.randn(256, 256, generator=g) * 0.05
+    ape = torch.randn(4, 256, generator=g) * 0.1
+    nw = torch.rand(128, generator=g) + 0.5
+    args = (x.to(DEV), wkv.to(DEV).bfloat16(), wgate.to(DEV).bfloat16(), ape.to(DEV), nw.to(DEV))
+    plain, st0 = dsv4.compressor_prefill(*args, head_dim=128)
+    rot, _ = dsv4.compressor_prefill(*args, head_dim=128, rotate=True, out_dtype=out_dtype)
+    want = Q.rotate_quant_rows(plain.cpu())
+    if out_dtype == torch.float32:
+        np.testing.assert_array_equal(rot.cpu().numpy().view(np.uint32), want.numpy().view(np.uint32))
+    else:
+        assert torch.equal(rot.cpu(), want.to(torch.bfloat16))
+    # the rows hold fp4 values times a power of two per 32-dim block
+    blk = want.reshape(-1, 32).double()
+    scale = 2.0 ** torch.from_numpy(Q.fp4_exp(Q.hadamard_rotate(plain.cpu().numpy()).reshape(-1, 32).__abs__().max(-1, keepdims=True))).double()
+    assert set((blk / scale).abs().unique().tolist()) <= {0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0}
+    # decode: identical rings, one emission each (ratio-4 kernel, key image kept in step)
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1).to(DEV)
+    kvp, scp = torch.randn(2, 256, generator=g).to(DEV), torch.randn(2, 256, generator=g).to(DEV)
+    outs = []
+    for rotate in (False, True):
+        rk, rs = st0["ring_kv"].clone(), st0["ring_score"].clone()
+        pool = torch.zeros(2, 128, device=DEV)
+        dsv4.compressor_decode_step(kvp, None, None, ape.to(DEV), nw.to(DEV), rk, rs,
+                                    torch.tensor([43, 43], dtype=torch.int32, device=DEV), pool,
+                                    torch.tensor([0, 1], device=DEV), head_dim=128, freqs=f, proj=(kvp, scp),
+                                    rotate=rotate)
+        outs.append(pool.cpu())
+    np.testing.assert_array_equal(outs[1].numpy().view(np.uint32), Q.rotate_quant_rows(outs[0]).numpy().view(np.uint32))
+    with pytest.raises(RuntimeError):
+        dsv4.compressor_prefill(*args[:3], torch.randn(4, 1024, device=DEV), torch.rand(512, device=DEV) + 0.5,
+                                rotate=True)
+
+
 def test_compressor_decode_ring(dsv4):
     g = torch.Generator().manual_seed(8)
     dim, s0 = 128, 13

@@ -99,3 +99,29 @@ def test_hc_matches_reference():
     np.testing.assert_allclose(out, g["hc_post_y"], rtol=1e-5, atol=1e-5)
     yh = H.hc_head(g["hc_x"], g["hc_head_fn"], g["hc_head_scale"], g["hc_head_base"])
     np.testing.assert_allclose(yh, g["hc_head_y"], rtol=1e-5, atol=1e-6)
+
+
+def test_hadamard_fp4_matches_reference():
+    """The indexer-key simulation (v4mlx/qat.py:8-31) against the reference's own outputs, bit for
+    bit: the float32 Hadamard rotation and the fp4-e2m1 block round trip."""
+    from oracle import quant_ref as Q
+    g = _qat_golden()
+    had = Q.hadamard_rotate(g["fp4_x"])
+    np.testing.assert_array_equal(had.view(np.uint32), g["had_y"].view(np.uint32))
+    q = Q.fp4_act_quant(had)
+    np.testing.assert_array_equal(q.view(np.uint32), g["fp4_y"].view(np.uint32))
+    # every value is an e2m1 value times its block's power-of-two scale
+    blk = q.reshape(-1, 32)
+    e = Q.fp4_exp(np.abs(had.reshape(-1, 32)).max(-1, keepdims=True))
+    grid = {0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0}
+    assert set(np.abs(blk / np.exp2(e.astype(np.float64))).ravel().tolist()) <= grid
+
+
+def test_e2m1_round_ties_and_edges():
+    """e2m1 rounding on the tie points and the range ends (planted against a table of the format)."""
+    from oracle import quant_ref as Q
+    x = np.array([0.0, -0.0, 0.2, 0.25, 0.26, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 5.01, 6.0, -1.25, -5.0], np.float32)
+    want = np.array([0.0, -0.0, 0.0, 0.0, 0.5, 1.0, 1.0, 2.0, 2.0, 4.0, 4.0, 6.0, 6.0, -1.0, -4.0], np.float32)
+    got = Q._e2m1_round(x)
+    np.testing.assert_array_equal(got, want)
+    assert np.signbit(got[1]) and np.signbit(Q._e2m1_round(np.float32(-0.2)))
