@@ -14,10 +14,10 @@ There is no CPU path: the ops raise on CPU tensors and when libdsv4.so is missin
 """
 from . import _lib
 from .compressor import compressor_decode_step, compressor_prefill
-from .decode import DecodeRunner, SparseMLACache, decode_attention
+from .decode import DecodeRunner, SparseMLACache, decode_attention, window_attention
 from .hc import hc_head, hc_post, hc_pre
 from .indexer import indexer_scores, indexer_topk, indexer_topk_into
-from .layer import AttentionWeights, DecodeBlock, make_attention_weights, prefill_layer
+from .layer import AttentionWeights, DecodeBlock, layer_rope_freqs, make_attention_weights, prefill_layer
 from .prefill import CompressorWeights, ShardedPrefill, sparse_mla_prefill
 from .mla import (N_GROUPS, N_HEADS, HEAD_DIM, O_LORA, ROPE_HD, QuantWeight, kv_proj, linear, linear_multi, o_grouped,
                   q_down, q_up, quantize_int8_g64)
@@ -31,7 +31,7 @@ __all__ = [
     "rope", "rope_freqs", "indexer_topk", "indexer_scores", "indexer_topk_into", "linear", "linear_multi", "q_down", "q_up",
     "kv_proj", "o_grouped", "QuantWeight", "quantize_int8_g64", "SparseMLACache", "decode_attention", "DecodeRunner",
     "AttentionWeights", "DecodeBlock", "make_attention_weights", "prefill_layer", "CompressorWeights", "ShardedPrefill",
-    "sparse_mla_prefill", "hc_pre", "hc_post", "hc_head",
+    "sparse_mla_prefill", "hc_pre", "hc_post", "hc_head", "window_attention", "layer_rope_freqs",
 ]
 
 

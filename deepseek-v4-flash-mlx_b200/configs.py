@@ -30,6 +30,15 @@ class LayerDims:
 
 DIMS = LayerDims()
 
+# Ratios whose layers attend over the sliding window alone: ratio 0 (the dense-attention layers, RoPE
+# base 10000 without YaRN) and ratio 128, which the reference engine runs with neither a compressor
+# ring nor compressed rows (oracle/v4_fast.py:42-43, 114; oracle/decode_engine.py:17, 47, 112).
+WINDOW_ONLY_RATIOS = (0, 128)
+
+
+def window_only(dims: LayerDims) -> bool:
+    return dims.ratio in WINDOW_ONLY_RATIOS
+
 
 @dataclass
 class DecodeCase:

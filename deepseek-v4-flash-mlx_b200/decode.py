@@ -27,7 +27,7 @@ import torch
 from . import _lib as L
 from .indexer import build_key_image, indexer_topk_into, key_image_buffers
 from .norm_rope import norm_rope, rope_freqs
-from .sparse_attn import sparse_attn_rope
+from .sparse_attn import sparse_attn_decode, sparse_attn_rope
 
 
 class SparseMLACache:
@@ -44,10 +44,17 @@ class SparseMLACache:
         if page_order is None:
             page_order = torch.arange(n_pages, dtype=torch.int32)
         self.block_table = page_order.to(torch.int32).reshape(batch, self.pages_per_seq).to(device)
+        self.image_stale = False
+        # max_comp == 0: a window-only layer (ratio 0, and the ratio-128 layers, which the reference
+        # runs with neither a compressor ring nor compressed rows, oracle/v4_fast.py:42-43, 114)
+        self.compressed = max_comp > 0
+        if not self.compressed:
+            self.k_idx = self.key_image = None
+            self.ring_kv = self.ring_score = self.ring_k_idx = self.ring_s_idx = None
+            return
         self.k_idx = torch.zeros((batch, max_comp, idx_dim), dtype=torch.float32, device=device)
         # the indexer keys' split form for the tensor-core filter, kept current with k_idx
         self.key_image = key_image_buffers(batch, max_comp, device)
-        self.image_stale = False
         self.ring_kv = torch.zeros((batch, 2 * ratio, 2 * head_dim), dtype=torch.float32, device=device)
         self.ring_score = torch.full((batch, 2 * ratio, 2 * head_dim), float("-inf"), dtype=torch.float32,
                                      device=device)
@@ -134,6 +141,27 @@ def decode_attention(cache, q, q_idx, w_idx, sink, positions, top_k=512, scale=N
     qr.record_stream(main)
     return sparse_attn_rope(qr, cache.kv_pool, sink, idx, scale, positions, freqs, 64, out_dtype,
                             win_base=cache.win_base, window=cache.window)
+
+
+def window_attention(cache, q, sink, positions, scale=None, freqs=None, idx_buf=None, out_dtype=torch.bfloat16):
+    """Decode attention of a window-only layer: one token per sequence over its window ring alone
+    (the ratio-0 and ratio-128 layers, oracle/v4_fast.py:110-119 with nvis = 0; the list is the
+    window rows in ring order, ref_torch/sparse_attn.py:11-13). q [b, 64, 512] raw (before the
+    per-head norm), sink [64], positions int32 [b] -> o [b, 64, 512] after the inverse RoPE.
+
+    The window rows are an explicit list (dsv4_decode_window_indices), so the attention waits for
+    the kernels before it (this token's row is written just before) before it reads any row."""
+    L.require_cuda(q, sink, positions)
+    b = q.shape[0]
+    if scale is None:
+        scale = cache.head_dim ** -0.5
+    if freqs is None:
+        freqs = rope_freqs(64, q.device)
+    positions = positions.to(torch.int32).contiguous()
+    idx = idx_buf if idx_buf is not None else torch.empty((b, cache.window), dtype=torch.int32, device=q.device)
+    L.check(L.lib().dsv4_decode_window_indices(b, cache.window, L.ptr(positions), L.ptr(cache.win_base), L.ptr(idx),
+                                               idx.shape[-1], L.stream_of(q)))
+    return sparse_attn_decode(q, cache.kv_pool, sink, idx, scale, positions, freqs, 64, out_dtype=out_dtype)
 
 
 _side_streams = {}

@@ -13,6 +13,12 @@ Decode follows oracle/v4_fast.py:82-122: the token's kv row goes into its window
 compressor rings emit a compressed row (and an indexer key) every 4th token, then decode attention
 over the device-resident cache and the grouped output projection. Weights may be bf16 or
 8-bit grouped (`QuantWeight`, config 5).
+
+Window-only layers (`dims.ratio` 0 or 128): the reference compresses only at ratio 4; its ratio-128
+layers keep no compressor ring and no compressed rows, and ratio-0 layers none either
+(oracle/v4_fast.py:42-43, 114; oracle/decode_engine.py:87, 112). Their list is the window alone, and
+the RoPE table is YaRN(160000, 16, 65536) for ratio 128 and the plain base-10000 table for ratio 0
+(oracle/decode_engine.py:47, 73).
 """
 import math
 from dataclasses import dataclass, fields
@@ -21,13 +27,13 @@ import torch
 
 from . import _lib as L
 from .compressor import compressor_decode_step, compressor_prefill
-from .configs import DIMS, LayerDims
-from .decode import SparseMLACache, decode_attention, decode_rows
+from .configs import DIMS, LayerDims, window_only
+from .decode import SparseMLACache, decode_attention, decode_rows, window_attention
 from .hc import hc_post, hc_pre
 from .indexer import indexer_topk_into
 from .mla import QuantWeight, linear, linear_multi, o_grouped, quantize_int8_g64
-from .norm_rope import norm_rope, rmsnorm, rope, rope_freqs
-from .sparse_attn import sparse_attn_rope
+from .norm_rope import ROPE_PLAIN, norm_rope, rmsnorm, rope, rope_freqs
+from .sparse_attn import get_window_topk_idxs, sparse_attn_rope
 
 
 @dataclass
@@ -98,12 +104,23 @@ def prefill_layer(x, W: AttentionWeights, top_k=512, dims: LayerDims = DIMS, ret
     L.require_cuda(x)
     s = x.shape[0]
     dev = x.device
-    freqs = rope_freqs(dims.rope_dim, dev)
+    freqs = layer_rope_freqs(dims, dev)
     pos = torch.arange(s, dtype=torch.int32, device=dev)
     xn = rmsnorm(x, W.attn_norm)
     qa = rmsnorm(linear(xn, W.wq_a, torch.float32), W.q_a_norm)
     qraw = linear(qa, W.wq_b, torch.float32).view(s, dims.n_heads, dims.head_dim)
     q = norm_rope(qraw, pos, freqs, weight=None, rope_dim=dims.rope_dim)                  # bf16
+    if window_only(dims):
+        # the window alone (oracle/decode_engine.py:111-114 with nvis = 0): query t attends to rows
+        # max(0, t-127)..t, the list of ref_torch/sparse_attn.py:15-18 as an explicit index tensor
+        kv = norm_rope(linear(xn, W.wkv, torch.float32), pos, freqs, weight=W.kv_a_norm, rope_dim=dims.rope_dim,
+                       act_quant=act_quant)
+        idx = get_window_topk_idxs(dims.window, 1, s, 0, device=dev)[0]
+        o = sparse_attn_rope(q, kv, W.sinks, idx, dims.head_dim ** -0.5, pos, freqs, dims.rope_dim)
+        out = o_grouped(o.reshape(s, -1), W.wo_a, W.wo_b)
+        if return_aux:
+            return out, dict(idx=idx, o=o, kvcat=kv, q=q)
+        return out
     n_comp = s // dims.ratio
     kvcat = torch.empty((s + n_comp, dims.head_dim), dtype=torch.bfloat16, device=dev)
     kvcat[:s] = norm_rope(linear(xn, W.wkv, torch.float32), pos, freqs, weight=W.kv_a_norm, rope_dim=dims.rope_dim,
@@ -137,10 +154,13 @@ class DecodeBlock:
                  page=64, cache=None, act_quant=False):
         self.W, self.dims, self.top_k = W, dims, top_k
         self.act_quant = act_quant  # the fp8 act-quant simulation of cached rows (oracle/decode_engine.py:82, 105)
+        self.window_only = window_only(dims)
         self.cache = cache if cache is not None else SparseMLACache(
-            batch, max_ctx // dims.ratio, window=dims.window, head_dim=dims.head_dim, idx_dim=dims.idx_dim,
-            ratio=dims.ratio, page=page, device=device)
-        self.freqs = rope_freqs(dims.rope_dim, device)
+            batch, 0 if self.window_only else max_ctx // dims.ratio, window=dims.window, head_dim=dims.head_dim,
+            idx_dim=dims.idx_dim, ratio=dims.ratio, page=page, device=device)
+        if self.window_only and self.cache.compressed:
+            raise ValueError("DecodeBlock: a window-only layer (ratio 0 or 128) takes a cache without compressed rows")
+        self.freqs = layer_rope_freqs(dims, device)
         self.batch = batch
         b = torch.arange(batch, device=device)
         self._seq = b
@@ -162,6 +182,16 @@ class DecodeBlock:
         d, W, c = self.dims, self.W, self.cache
         b = xn.shape[0]
         pos = positions.to(torch.int32).contiguous()
+        if self.window_only:
+            # oracle/v4_fast.py:87-92, 110-119 without the ring (w.r4 false): q and kv projections,
+            # this token's row into its window slot, attention over the window ring
+            qa_p, kvp = linear_multi(xn, [W.wq_a, W.wkv], torch.float32)
+            qa = rmsnorm(qa_p, W.q_a_norm, out_dtype=torch.bfloat16)
+            qraw = linear(qa, W.wq_b, torch.float32).view(b, d.n_heads, d.head_dim)
+            win_rows, _, _ = decode_rows(c, pos)
+            _norm_rope_into(kvp, W.kv_a_norm, pos, self.freqs, c.kv_pool, win_rows, d.rope_dim, self.act_quant)
+            o = window_attention(c, qraw, W.sinks, pos, freqs=self.freqs)
+            return o_grouped(o.reshape(b, -1), W.wo_a, W.wo_b)
         # the seven projections of xn run as one launch, the two of qa as another
         qa_p, kvp, c_kv, c_sc, w_idx, i_kv, i_sc = linear_multi(
             xn, [W.wq_a, W.wkv, W.c_wkv, W.c_wgate, W.i_wproj, W.i_wkv, W.i_wgate], torch.float32)
@@ -181,6 +211,14 @@ class DecodeBlock:
         q_idx = rope(qi.view(b, d.idx_heads, d.idx_dim), pos, self.freqs, d.rope_dim)
         o = decode_attention(c, qraw, q_idx, w_idx, W.sinks, pos, self.top_k, freqs=self.freqs)
         return o_grouped(o.reshape(b, -1), W.wo_a, W.wo_b)
+
+
+def layer_rope_freqs(dims: LayerDims, device):
+    """RoPE table of a layer: plain base 10000 for ratio 0, YaRN(160000, 16, 65536) otherwise
+    (oracle/decode_engine.py:47, 73; oracle/v4_fast.py:83)."""
+    if dims.ratio == 0:
+        return rope_freqs(dims.rope_dim, device, **ROPE_PLAIN)
+    return rope_freqs(dims.rope_dim, device)
 
 
 def _norm_rope_into(x, weight, positions, freqs, pool, rows, rope_dim, act_quant=False):

@@ -338,6 +338,8 @@ DSV4_API int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void
  *   comp_rows[i] = comp_base + block_table[i*bt_stride + entry/page]*page + entry % page
  *   key_rows[i]  = i * max_comp + entry
  * An entry >= max_comp raises DSV4_ERR_INDEX_OUT_OF_RANGE on the device error word (clamped).
+ * max_comp == 0 is a window-only cache (the ratio-0 and ratio-128 layers, which keep no compressed
+ * rows, oracle/v4_fast.py:42-43, 114): comp_rows and key_rows are -1 and block_table may be NULL.
  * Replaces the host-side ring and kvbuf bookkeeping of oracle/v4_fast.py:93-118. */
 typedef struct {
   const int32_t* positions;   /* [b] */

@@ -4,7 +4,8 @@ decode_attention_ref restates the per-token attention of oracle/v4_fast.py:83-11
 oracle/step12_glue.py ATTN_NEW): q per-head norm + rope, the window rows in ring order
 (ref_torch/sparse_attn.py:11-13), the compressed rows chosen by the indexer (which, with top_k at
 least the visible count, is the reference's "all visible rows" list, oracle/v4_fast.py:114-117),
-sparse attention, inverse rope of the output.
+sparse attention, inverse rope of the output. window_attention_ref is the same for the window-only
+layers (ratio 0 and 128), whose list holds the window rows alone (oracle/decode_engine.py:112).
 """
 import torch
 
@@ -45,6 +46,36 @@ def decode_attention_ref(kv_pool, win_base, comp_rows, k_idx, q, q_idx, w_idx, s
     return (out, torch.stack(all_idx)) if return_indices else out
 
 
+def window_attention_ref(kv_pool, win_base, q, sink, positions, freqs, window=128, scale=512 ** -0.5):
+    """Decode attention of a window-only layer (ratio 0 or 128): oracle/v4_fast.py:110-119 with
+    nvis = 0, i.e. q per-head norm + rope, the window rows alone in ring order, sparse attention,
+    inverse rope of the output. kv_pool [rows, 512], win_base [b], q [b, 64, 512] -> o [b, 64, 512]."""
+    pool = kv_pool.float()
+    outs = []
+    for b in range(q.shape[0]):
+        p = int(positions[b])
+        qn = rope_at(perhead_norm(q[b].float())[None], torch.tensor([p]), freqs)[0]
+        rows = [int(win_base[b]) + s if s >= 0 else -1 for s in window_slots(p, window)]
+        o = sparse_attn(qn[None], pool, sink, torch.tensor([rows], dtype=torch.int64), scale)[0]
+        outs.append(rope_at(o[None], torch.tensor([p]), freqs, inverse=True)[0])
+    return torch.stack(outs)
+
+
+def layer_freqs(ratio, rope_dim=64):
+    """The layer's RoPE table (oracle/decode_engine.py:47, 73): base 10000 without YaRN at ratio 0,
+    YaRN(160000, factor 16, original 65536, beta 32/1) for the compressed-table layers (ratio 4, 128)."""
+    from .norm_rope_ref import precompute_freqs
+    if ratio == 0:
+        return precompute_freqs(rope_dim, 0, 0, 10000.0, 40, 32, 1)
+    return precompute_freqs(rope_dim, 0, 65536, 160000.0, 16, 32, 1)
+
+
+def is_window_only(ratio):
+    """The reference compresses only at ratio 4 (oracle/v4_fast.py:42: "ring/comp ONLY at ratio 4");
+    ratio-0 and ratio-128 layers attend over the window alone (oracle/decode_engine.py:112)."""
+    return ratio in (0, 128)
+
+
 # ---------------------------------------------------------------------------- full block
 def _w(v):
     """fp32 value of a weight (bf16 tensor or an 8-bit grouped weight)."""
@@ -60,14 +91,25 @@ def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=5
     Returns (out [s, dim], idx [s, window + top_k], o [s, heads, head_dim])."""
     from .compressor_ref import compressor_prefill
     from .mla_ref import o_grouped
-    from .norm_rope_ref import precompute_freqs, rmsnorm
+    from .norm_rope_ref import rmsnorm
     s = x.shape[0]
-    f = precompute_freqs(rope_dim, 0, 65536, 160000.0, 16, 32, 1)
+    f = layer_freqs(ratio, rope_dim)
     pos = torch.arange(s)
     xn = rmsnorm(x.float(), W.attn_norm)
     qa = rmsnorm(xn @ _w(W.wq_a).T, W.q_a_norm)
     q = rope_at(perhead_norm((qa @ _w(W.wq_b).T).reshape(s, heads, head_dim)), pos, f, rope_dim)
     kv = rope_at(rmsnorm(xn @ _w(W.wkv).T, W.kv_a_norm), pos, f, rope_dim)
+    win = torch.stack([torch.tensor([max(0, t - window + 1) + c if max(0, t - window + 1) + c <= t else -1
+                                     for c in range(window)]) for t in range(s)])
+    if is_window_only(ratio):
+        # oracle/decode_engine.py:108-116 with nvis = 0: the window rows alone (widx)
+        if act_quant:
+            from .quant_ref import act_quant_rows
+            kv = act_quant_rows(kv, rope_dim)
+        idx = win[:, :min(s, window)]
+        o = sparse_attn_chunked(q, kv, W.sinks, idx, head_dim ** -0.5)
+        o = rope_at(o, pos, f, rope_dim, inverse=True)
+        return o_grouped(o.reshape(s, -1), _w(W.wo_a), _w(W.wo_b), groups=groups), idx, o
     comp, _ = compressor_prefill(xn[None], _w(W.c_wkv), _w(W.c_wgate), W.c_ape, W.c_norm, head_dim=head_dim,
                                  ratio=ratio, rope_head_dim=rope_dim)
     if act_quant:  # oracle/decode_engine.py:82 (kv rows) and the compressor's sim (v4mlx/compressor.py:60-62)
@@ -85,8 +127,6 @@ def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=5
     sel = I.indexer_topk(q_idx.numpy()[None], w_idx.numpy()[None], k_idx.numpy()[None], top_k,
                          positions=pos.numpy()[None], ratio=ratio)[0]
     sel_t = torch.from_numpy(sel.astype("int64"))
-    win = torch.stack([torch.tensor([max(0, t - window + 1) + c if max(0, t - window + 1) + c <= t else -1
-                                     for c in range(window)]) for t in range(s)])
     idx = torch.cat([win, torch.where(sel_t >= 0, sel_t + s, sel_t)], 1)
     kvcat = torch.cat([kv, comp[0]], 0)
     o = sparse_attn_chunked(q, kvcat, W.sinks, idx, head_dim ** -0.5)
@@ -105,13 +145,24 @@ def decode_block_ref(state, W, x, positions, top_k=512, window=128, ratio=4, hea
     from .quant_ref import act_quant_rows
     from .compressor_ref import decode_ring_step
     from .mla_ref import o_grouped
-    from .norm_rope_ref import precompute_freqs, rmsnorm
-    f = precompute_freqs(rope_dim, 0, 65536, 160000.0, 16, 32, 1)
+    from .norm_rope_ref import rmsnorm
+    f = layer_freqs(ratio, rope_dim)
     b = x.shape[0]
     xn = rmsnorm(x.float(), W.attn_norm)
     qa = rmsnorm(xn @ _w(W.wq_a).T, W.q_a_norm)
     qraw = (qa @ _w(W.wq_b).T).reshape(b, heads, head_dim)
     kvp = rmsnorm(xn @ _w(W.wkv).T, W.kv_a_norm)
+    if is_window_only(ratio):
+        # oracle/v4_fast.py:87-96, 110-122 without the ring (w.r4 false): state = dict(pool, win_base)
+        for i in range(b):
+            p = int(positions[i])
+            row = rope_at(kvp[i][None], torch.tensor([p]), f, rope_dim)[0]
+            if act_quant:
+                row = act_quant_rows(row, rope_dim)
+            state["pool"][int(state["win_base"][i]) + p % window] = row.to(torch.bfloat16).float()
+        o = window_attention_ref(state["pool"], state["win_base"], qraw, W.sinks, positions, f, window=window,
+                                 scale=head_dim ** -0.5)
+        return o_grouped(o.reshape(b, -1), _w(W.wo_a), _w(W.wo_b), groups=groups)
     ckv, cgt = xn @ _w(W.c_wkv).T, xn @ _w(W.c_wgate).T
     ikv, igt = xn @ _w(W.i_wkv).T, xn @ _w(W.i_wgate).T
     q_idx = (qa @ _w(W.i_wq).T).reshape(b, idx_heads, idx_dim)
