@@ -1,6 +1,6 @@
 """Benchmark of the sparse-MLA decode path (BASELINE config 2 by default).
 
-python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dsv4|reference] [--config c2|c3]
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dsv4|reference] [--config c2|c3|c4|c5|c5w]
 
 A step is one decode token of the measured path — per-head norm + RoPE of q, the window index list,
 the lightning-indexer scores + top-k over the compressed keys, sparse attention over the 640
@@ -34,7 +34,8 @@ METRIC = "sparse-MLA decode tok/s at 32K ctx (indexer + top-k + sparse attention
 METRICS = {"c2": METRIC,
            "c3": "sparse-MLA batched decode tok/s (indexer + top-k + sparse attention + RoPE)",
            "c4": "sparse-MLA prefill tok/s at 64K ctx (compressors + indexer top-k + sparse attention)",
-           "c5": "full attention block decode tok/s (projections + compressor + indexer + sparse MLA + o_proj)"}
+           "c5": "full attention block decode tok/s (projections + compressor + indexer + sparse MLA + o_proj)",
+           "c5w": "window-only (ratio-128) attention block decode tok/s (projections + window attention + o_proj)"}
 CONFIGS = {
     "c2": dict(batch=1, ctx=32768, top_k=512, seeds=lambda r, i: 1 + 7919 * r, strong=False,
                workload="config2: decode, batch 1, 32768-token context (8192 compressed + 128 window rows), "
@@ -49,6 +50,10 @@ CONFIGS = {
     "c5": dict(batch=32, ctx=16384, top_k=512, seeds=lambda r, i: 3 + i, strong=True,
                workload="config5: full attention block decode, global batch 32 split across GPUs, 16384-token "
                         "contexts, int8-g64 weights (bf16 scales), top-k 512"),
+    "c5w": dict(batch=32, ctx=16384, top_k=0, seeds=lambda r, i: 3 + i, strong=True,
+                workload="config5 block at a ratio-128 layer (window-only attention, as the reference runs "
+                         "ratio-128 layers): global batch 32 split across GPUs, 16384-token contexts, 128-row "
+                         "window rings, int8-g64 weights (bf16 scales)"),
 }
 L2_BYTES = 126 * 1024 * 1024
 # kernels of one decode step: q norm/rope, indexer scores, top-k selection, sparse attention, split merge
@@ -162,6 +167,8 @@ def cpu_reference(cfg_name, samples, threads=None):
         return _cpu_prefill(samples, threads)
     if cfg_name == "c5":
         return _cpu_block(samples, threads)
+    if cfg_name == "c5w":
+        return _cpu_block_window(samples, threads)
     batch = min(cfgd["batch"], samples)
     case = C.make_decode_case(batch, cfgd["ctx"], cfgd["top_k"], seeds=[cfgd["seeds"](0, i) for i in range(batch)],
                               device="cpu", shuffle_pages=True)
@@ -211,6 +218,24 @@ def _cpu_prefill(nq, threads):
     return 1.0 / (t_comp + t_q), threads, (f"oracle port: compressors over 4096 tokens ({t_comp * 4096:.2f} s) + "
                                           f"indexer/attention for {nq} queries at position 32K, the sequence's "
                                           f"average ({t_q * nq:.2f} s)")
+
+
+def _cpu_block_window(nseq, threads):
+    """Window-only (ratio-128) block per-token CPU cost: the oracle decode block without compression."""
+    import importlib
+    from oracle import layer_ref as LR
+    Lm = importlib.import_module(PKG + ".layer")
+    C = importlib.import_module(PKG + ".configs")
+    W = Lm.make_attention_weights(3, dims=C.LayerDims(ratio=128), quant=True)
+    g = torch.Generator().manual_seed(3)
+    state = dict(pool=torch.randn(nseq * 128, 512, generator=g).to(torch.bfloat16).float(),
+                 win_base=torch.arange(nseq) * 128)
+    x = torch.randn(nseq, 4096, generator=g)
+    pos = torch.full((nseq,), 16383, dtype=torch.int32)
+    t0 = time.perf_counter()
+    LR.decode_block_ref(state, W, x, pos, ratio=128)
+    dt = time.perf_counter() - t0
+    return nseq / dt, threads, f"{nseq} token(s) of the window-only (ratio-128) block through the CPU oracle ({dt:.2f} s)"
 
 
 def _cpu_block(nseq, threads):
@@ -299,6 +324,8 @@ def main():
         return bench_prefill(args, world, rank, local, dev)
     if args.config == "c5":
         return bench_block(args, world, rank, local, dev)
+    if args.config == "c5w":
+        return bench_block_window(args, world, rank, local, dev)
     batch, ctx, top_k = cfgd["batch"], cfgd["ctx"], cfgd["top_k"]
     if cfgd.get("strong"):
         batch = max(1, batch // world)
@@ -683,6 +710,111 @@ def bench_block(args, world, rank, local, dev):
                         "d2h_bytes_per_step": ho.numel() * 4, "path": "host hidden states -> block graph -> host"},
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
         print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def bench_block_window(args, world, rank, local, dev):
+    """The config-5 block at a window-only (ratio-128) layer: one step = projections, this token's kv
+    row into its window ring, attention over the 128-row window, grouped output projection, for one
+    token of each sequence (global batch 32 split over the ranks), int8-g64 weights, one CUDA graph
+    per replica. A replica's weights and rings (~114 MB) fit in L2, so the steps rotate over three
+    replicas: a step's inputs were last touched two steps (~228 MB of other data) earlier."""
+    import importlib
+    Lm = importlib.import_module(PKG + ".layer")
+    C = importlib.import_module(PKG + ".configs")
+    M = importlib.import_module(PKG + ".mla")
+    cfgd = CONFIGS["c5w"]
+    dims = C.LayerDims(ratio=128)
+    B, ctx = max(1, cfgd["batch"] // world), cfgd["ctx"]
+    steps = args.steps if args.steps_given else 300
+    warmup = max(3, args.warmup if args.warmup_given else 30)
+    R = 3
+    stream = torch.cuda.Stream(dev)
+    blocks, graphs, xs, outs, Ws = [], [], [], [], []
+    for r in range(R):
+        W = Lm.make_attention_weights(3 + 7 * r, dims=dims, quant=True).to(dev)
+        blk = Lm.DecodeBlock(W, B, ctx, dims=dims, device=dev)
+        g = torch.Generator().manual_seed(cfgd["seeds"](rank, rank * B) + 104729 * r)
+        blk.cache.kv_pool.copy_(torch.randn(blk.cache.kv_pool.shape, generator=g).to(torch.bfloat16))
+        x = torch.randn(B, 4096, generator=g).to(dev)
+        pos = torch.full((B,), ctx - 1, dtype=torch.int32, device=dev)
+        with torch.cuda.stream(stream):
+            blk.step(x, pos)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            out = blk.step(x, pos)
+        blocks.append(blk), graphs.append(graph), xs.append(x), outs.append(out), Ws.append(W)
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            graphs[i % R].replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.05)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            graphs[i % R].replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = _barrier_max(e0.elapsed_time(e1), world, dev) / steps
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    # e2e: this token's hidden states from pinned host memory, the graph, the block output back
+    hx = [x.cpu().pin_memory() for x in xs]
+    ho = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            r = i % R
+            xs[r].copy_(hx[r], non_blocking=True)
+            graphs[r].replay()
+            ho[r].copy_(outs[r], non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ems = _barrier_max(f0.elapsed_time(f1), world, dev) / steps
+    # algorithmic HBM bytes of one step: the five matrices the step reads, once, and the window rows
+    W = Ws[0]
+    wbytes = 0
+    for name in ("wq_a", "wq_b", "wkv", "wo_a", "wo_b"):
+        w = getattr(W, name)
+        wbytes += (w.q.numel() + w.scale.numel() * 2) if isinstance(w, M.QuantWeight) else w.numel() * w.element_size()
+    step_bytes = wbytes + B * 128 * 1024
+    peak, peak_kind = _peaks()
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "whole block step", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                "algorithmic_bytes_per_launch": step_bytes}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, desc = cpu_reference("c5w", 4)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
+    if rank == 0:
+        line = {"metric": METRICS["c5w"], "value": cfgd["batch"] / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+                "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": cfgd["workload"], "global_batch": cfgd["batch"], "ctx": ctx,
+                           "parallelism": f"batch-split x{world} (no collective)" if world > 1 else "single GPU",
+                           "l2": f"{R} replicas of {step_bytes / 2**20:.0f} MiB rotated (> L2 between uses)",
+                           "cuda_graph": True},
+                "gpu_launches": None,
+                "e2e": {"value": cfgd["batch"] / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": hx[0].numel() * 4,
+                        "d2h_bytes_per_step": ho[0].numel() * 4, "path": "host hidden states -> block graph -> host"},
+                "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    del graphs
     if world > 1:
         torch.distributed.destroy_process_group()
 

@@ -104,7 +104,7 @@ __device__ __forceinline__ bool bar_wait_or_abort(uint64_t* bar, uint32_t parity
   }
 }
 
-// bulk copy global -> shared (no multicast), completion counted in bytes on `bar`;
+// bulk copy global -> this CTA's shared memory only, completion counted in bytes on `bar`;
 // both addresses 16-byte aligned, bytes a multiple of 16
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
