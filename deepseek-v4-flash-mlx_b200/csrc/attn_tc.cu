@@ -564,11 +564,8 @@ int dsv4_sparse_attn_tc(const dsv4_sparse_attn_params* p, int splits, float* par
   DSV4_CHECK_ARG((reinterpret_cast<uintptr_t>(p->kv) & 15) == 0, "dsv4_sparse_attn: kv must be 16-byte aligned");
   P.kv = reinterpret_cast<const __nv_bfloat16*>(p->kv);
   const int smem = static_cast<int>(sizeof(tc::Smem)) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(tc::attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  DSV4_CUDA_CHECK(set_smem_once(attr, tc::attn_tc_kernel, smem));
   DSV4_CHECK_ARG(splits >= 1 && (splits == 1 || part != nullptr), "dsv4_sparse_attn: split partials need a workspace");
   tc::attn_tc_kernel<<<static_cast<unsigned>(p->s * splits), tc::THREADS, smem, as_stream(stream)>>>(P);
   DSV4_LAUNCH_CHECK("attn_tc_kernel");

@@ -6,6 +6,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -78,15 +79,46 @@ cudaError_t read_all_error_words(int* first);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// SM count of the current device (looked up once per device ordinal below 64)
 inline int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const bool slot = dev >= 0 && dev < 64;
+  int n = slot ? cached[dev].load(std::memory_order_relaxed) : 0;
+  if (n <= 0) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (n <= 0) n = 148;
+    if (slot) cached[dev].store(n, std::memory_order_relaxed);
   }
   return n;
+}
+
+// Kernel attributes set with cudaFuncSetAttribute belong to the current device, so a process that
+// drives several GPUs must set them on each one. A `PerDeviceOnce` runs its setter once per device
+// ordinal (below 64; other ordinals on every call) and remembers only a success.
+class PerDeviceOnce {
+ public:
+  template <typename F>
+  cudaError_t operator()(F&& set) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t{1} << dev) : 0;
+    if (bit != 0 && (done_.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+    e = set();
+    if (e == cudaSuccess && bit != 0) done_.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+  }
+
+ private:
+  std::atomic<uint64_t> done_{0};
+};
+
+// a kernel's dynamic shared-memory limit, set once per device through `once`
+template <typename K>
+inline cudaError_t set_smem_once(PerDeviceOnce& once, K kernel, int bytes) {
+  return once([&] { return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); });
 }
 
 // ---- element access by runtime dtype ------------------------------------------------------

@@ -652,12 +652,9 @@ static int launch_skinny_mt(const gm::Params& P, void* stream) {
   // int8 weights: 32 rows per warp (the tokens' fragments serve two row tiles); bf16: 16
   constexpr int RW = I8 ? 2 : 1;
   const auto kern = gm::sk::skinny_kernel<I8, MT, RW>;
-  static bool set = false;
+  static PerDeviceOnce set;
   const int smem = sizeof(gm::sk::Smem<I8, MT>);
-  if (!set) {
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    set = true;
-  }
+  DSV4_CUDA_CHECK(set_smem_once(set, kern, smem));
   cudaLaunchConfig_t cfg = {};
   const int tiles = P.nprob > 0 ? P.prob[P.nprob - 1].tile0 + (P.prob[P.nprob - 1].n + gm::sk::ROWS - 1) / gm::sk::ROWS
                                 : (P.n + gm::sk::ROWS - 1) / gm::sk::ROWS;
@@ -693,12 +690,9 @@ template <bool I8>
 static int launch_tiled(const gm::Params& P, void* stream) {
   const int64_t mt = (P.m + gm::BM - 1) / gm::BM;
   DSV4_CHECK_ARG(mt <= 65535, "dsv4_linear: m too large");
-  static bool set = false;
+  static PerDeviceOnce set;
   const int smem = sizeof(gm::Smem<I8>);
-  if (!set) {
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(gm::gemm_kernel<I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    set = true;
-  }
+  DSV4_CUDA_CHECK(set_smem_once(set, gm::gemm_kernel<I8>, smem));
   dim3 grid((P.n + gm::BN - 1) / gm::BN, static_cast<unsigned>(mt), P.groups * P.ksplit);
   gm::gemm_kernel<I8><<<grid, gm::THREADS, smem, as_stream(stream)>>>(P);
   DSV4_LAUNCH_CHECK("gemm_kernel");

@@ -1167,23 +1167,15 @@ __global__ void decode_window_kernel(int32_t batch, int32_t window, const int32_
 // the query-tiled kernel when a batch row holds many queries (prefill), else one CTA per query
 inline cudaError_t launch_scores(const ScoreParams& S, cudaStream_t st) {
   if (S.s >= TQ) {
-    static bool attr = false;
-    if (!attr) {
-      const cudaError_t e = cudaFuncSetAttribute(score_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 sizeof(TiledSmem));
-      if (e != cudaSuccess) return e;
-      attr = true;
-    }
+    static PerDeviceOnce attr;
+    const cudaError_t e = set_smem_once(attr, score_tiled_kernel, static_cast<int>(sizeof(TiledSmem)));
+    if (e != cudaSuccess) return e;
     const dim3 g((S.n_keys + TK - 1) / TK, (S.s + TQ - 1) / TQ, S.batch);
     return launch_pdl(score_tiled_kernel, g, dim3(THREADS), sizeof(TiledSmem), st, S);
   }
-  static bool attr1 = false;
-  if (!attr1) {
-    const cudaError_t e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               sizeof(ScoreSmem));
-    if (e != cudaSuccess) return e;
-    attr1 = true;
-  }
+  static PerDeviceOnce attr1;
+  const cudaError_t e = set_smem_once(attr1, score_kernel, static_cast<int>(sizeof(ScoreSmem)));
+  if (e != cudaSuccess) return e;
   const dim3 g(static_cast<unsigned>(static_cast<int64_t>(S.batch) * S.s), (S.n_keys + KT - 1) / KT);
   return launch_pdl(score_kernel, g, dim3(THREADS), sizeof(ScoreSmem), st, S);
 }
@@ -1193,15 +1185,16 @@ inline cudaError_t launch_select(const SelectParams& L, unsigned rows, cudaStrea
   const dim3 g(rows), blk(SEL_THREADS);
   if (L.refine) {
     constexpr size_t rsm = sizeof(RefineSmem);
-    static bool rattr = false;
-    if (!rattr) {
+    static PerDeviceOnce rattr;
+    const cudaError_t e = rattr([&] {
       for (auto fn : {select_reg_kernel<4, true>, select_reg_kernel<8, true>, select_reg_kernel<16, true>,
                       select_reg_kernel<32, true>}) {
-        const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(rsm));
-        if (e != cudaSuccess) return e;
+        const cudaError_t r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(rsm));
+        if (r != cudaSuccess) return r;
       }
-      rattr = true;
-    }
+      return cudaSuccess;
+    });
+    if (e != cudaSuccess) return e;
     if (L.n_keys <= SEL_THREADS * 4) return launch_pdl(select_reg_kernel<4, true>, g, blk, rsm, st, L);
     if (L.n_keys <= SEL_THREADS * 8) return launch_pdl(select_reg_kernel<8, true>, g, blk, rsm, st, L);
     if (L.n_keys <= SEL_THREADS * 16) return launch_pdl(select_reg_kernel<16, true>, g, blk, rsm, st, L);
@@ -1211,13 +1204,9 @@ inline cudaError_t launch_select(const SelectParams& L, unsigned rows, cudaStrea
   if (L.n_keys <= SEL_THREADS * 8) return launch_pdl(select_reg_kernel<8, false>, g, blk, 0, st, L);
   if (L.n_keys <= SEL_THREADS * 16) return launch_pdl(select_reg_kernel<16, false>, g, blk, 0, st, L);
   if (L.n_keys <= SEL_THREADS * 32) return launch_pdl(select_reg_kernel<32, false>, g, blk, 0, st, L);
-  static bool attr = false;
-  if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               SEL_MAX_KEYS * 4);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  const cudaError_t e = set_smem_once(attr, select_kernel, SEL_MAX_KEYS * 4);
+  if (e != cudaSuccess) return e;
   return launch_pdl(select_kernel, g, blk, static_cast<size_t>(L.n_keys) * 4, st, L);
 }
 
@@ -1491,12 +1480,8 @@ extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* str
   S.k_batch_stride = p->k_batch_stride;
   S.positions = p->positions;
   S.ratio = p->ratio;
-  static bool score_attr = false;
-  if (!score_attr) {
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(idx::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         sizeof(idx::ScoreSmem)));
-    score_attr = true;
-  }
+  static PerDeviceOnce score_attr;
+  DSV4_CUDA_CHECK(set_smem_once(score_attr, idx::score_kernel, static_cast<int>(sizeof(idx::ScoreSmem))));
   dim3 g1(static_cast<unsigned>(rows), (p->n_keys + idx::KT - 1) / idx::KT);
   idx::score_kernel<<<g1, idx::THREADS, sizeof(idx::ScoreSmem), as_stream(stream)>>>(S);
   DSV4_LAUNCH_CHECK("indexer score_kernel (noalloc)");

@@ -849,12 +849,9 @@ cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaSuccess;
   if (a.img_ready && row_kernel(a.s)) {  // decode over a cache-kept image: the walk without the split
     const int smem = static_cast<int>(sizeof(ImgSmem)) + 1024;
-    static bool iattr = false;
-    if (!iattr) {
-      e = cudaFuncSetAttribute(approx_score_img_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return e;
-      iattr = true;
-    }
+    static PerDeviceOnce iattr;
+    e = set_smem_once(iattr, approx_score_img_kernel, smem);
+    if (e != cudaSuccess) return e;
     const int64_t items = static_cast<int64_t>(a.batch) * a.s * key_tiles(a.n_keys);
     const int64_t ctas = num_sms();
     const int64_t per = (items + ctas - 1) / ctas;
@@ -869,24 +866,18 @@ cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream) {
     const int64_t items = static_cast<int64_t>(a.batch) * a.s * key_tiles(a.n_keys);
     if (items >= 2 * static_cast<int64_t>(num_sms())) {  // at least two items per CTA: the pipelined walk
       const int smem = static_cast<int>(sizeof(SeqSmem)) + 1024;
-      static bool sattr = false;
-      if (!sattr) {
-        e = cudaFuncSetAttribute(approx_score_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        sattr = true;
-      }
+      static PerDeviceOnce sattr;
+      e = set_smem_once(sattr, approx_score_seq_kernel, smem);
+      if (e != cudaSuccess) return e;
       const int64_t ctas = num_sms();
       const int64_t per = (items + ctas - 1) / ctas;
       approx_score_seq_kernel<<<static_cast<unsigned>((items + per - 1) / per), SQ_THREADS, smem, stream>>>(a, per);
       return cudaGetLastError();
     }
     const int smem = static_cast<int>(sizeof(RowSmem)) + 1024;
-    static bool rattr = false;
-    if (!rattr) {
-      e = cudaFuncSetAttribute(approx_score_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return e;
-      rattr = true;
-    }
+    static PerDeviceOnce rattr;
+    e = set_smem_once(rattr, approx_score_row_kernel, smem);
+    if (e != cudaSuccess) return e;
     approx_score_row_kernel<<<dim3(key_tiles(a.n_keys), static_cast<unsigned>(static_cast<int64_t>(a.batch) * a.s)),
                               RT_THREADS, smem, stream>>>(a);
     return cudaGetLastError();
@@ -896,12 +887,9 @@ cudaError_t launch_approx_scores(const ApproxArgs& a, cudaStream_t stream) {
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    e = cudaFuncSetAttribute(approx_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  e = set_smem_once(attr, approx_score_kernel, smem);
+  if (e != cudaSuccess) return e;
   const int64_t groups = static_cast<int64_t>(a.batch) * ((a.s + QG - 1) / QG);
   approx_score_kernel<<<static_cast<unsigned>(groups), THREADS, smem, stream>>>(a);
   return cudaGetLastError();

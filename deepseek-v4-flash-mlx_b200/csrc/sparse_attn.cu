@@ -709,9 +709,16 @@ struct AttnPlan {
 // whether `splits` CTAs of the mma.sync kernel (one per SM by shared memory) can run as one cluster
 // on this GPU; asked once per size
 static bool cluster_fits(int splits) {
-  static int known[17] = {0};  // 0 unknown, 1 yes, -1 no
+  // per device ordinal (the attributes set here are per device): 0 unknown, 1 yes, -1 no
+  static std::atomic<int> known[64][17];
   if (splits < 2 || splits > 16) return false;
-  if (known[splits] != 0) return known[splits] > 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  const int k = known[dev][splits].load(std::memory_order_relaxed);
+  if (k != 0) return k > 0;
   const int smem = static_cast<int>(sizeof(sa::Smem));
   bool ok = cudaFuncSetAttribute(sa::sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
             cudaSuccess;
@@ -734,7 +741,7 @@ static bool cluster_fits(int splits) {
     ok = cudaOccupancyMaxActiveClusters(&nclusters, sa::sparse_attn_kernel, &cfg) == cudaSuccess && nclusters > 0;
   }
   (void)cudaGetLastError();  // a refused query leaves no sticky error
-  known[splits] = ok ? 1 : -1;
+  known[dev][splits].store(ok ? 1 : -1, std::memory_order_relaxed);
   return ok;
 }
 static int tc_splits(const dsv4_sparse_attn_params* p) {
@@ -868,12 +875,9 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
     DSV4_CUDA_CHECK(launch_pdl(sa::combine_kernel, g2, dim3(128), 0, as_stream(stream), P));
     return DSV4_OK;
   }
-  static bool attr_set = false;
+  static PerDeviceOnce attr_set;
   const int smem = static_cast<int>(sizeof(sa::Smem));
-  if (!attr_set) {
-    DSV4_CUDA_CHECK(cudaFuncSetAttribute(sa::sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set = true;
-  }
+  DSV4_CUDA_CHECK(set_smem_once(attr_set, sa::sparse_attn_kernel, smem));
   dim3 grid(static_cast<unsigned>(P.s * P.splits), P.hblocks);
   if (P.cluster) {
     cudaLaunchConfig_t cfg = {};

@@ -53,3 +53,33 @@ def test_sharded_prefill_equals_single_gpu():
         p.join(timeout=120)
     assert all(ok for _, ok, _ in res), res
     assert sum(n for _, _, n in res) == 4096
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_one_process_two_devices():
+    """Kernel attributes (shared-memory limits, non-portable cluster sizes) are per device: one
+    process that runs the attention kernels and the indexer on GPU 0 and then on GPU 1 gets the
+    same results on both."""
+    dsv4 = importlib.import_module(PKG)
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(20, 64, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(3000, 512, generator=g).to(torch.bfloat16)
+    sink = torch.randn(64, generator=g)
+    idx = torch.randint(0, 3000, (20, 640), generator=g, dtype=torch.int32)
+    q1 = q[:1]
+    qi = torch.randn(1, 256, 64, 128, generator=g)
+    wi = torch.randn(1, 256, 64, generator=g) / 8
+    keys = torch.randn(1, 2000, 128, generator=g)
+    res = []
+    for d in (0, 1):
+        dev = torch.device("cuda", d)
+        with torch.cuda.device(dev):
+            r = [dsv4.sparse_attn(q.to(dev), kv.to(dev), sink.to(dev), idx.to(dev), 512 ** -0.5, kernel=k).cpu()
+                 for k in (1, 2)]
+            # one query: the mma.sync kernel's splits run as one (non-portable, 10-CTA) cluster
+            r.append(dsv4.sparse_attn(q1.to(dev), kv.to(dev), sink.to(dev), idx[:1].to(dev), 512 ** -0.5).cpu())
+            r.append(dsv4.indexer_topk(qi.to(dev), wi.to(dev), keys.to(dev), 256, mode=2).cpu())
+            torch.cuda.synchronize(dev)
+        res.append(r)
+    for a, b in zip(*res):
+        assert torch.equal(a, b)
