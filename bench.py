@@ -295,10 +295,12 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--replicas", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", default=None, choices=["attn_prefill", "indexer_prefill", "block_decode", "hc"],
+    ap.add_argument("--kernel-case", default=None,
+                    choices=["attn_prefill", "indexer_prefill", "block_decode", "block_decode_window", "hc"],
                     help="profiling aid: run one prefill kernel alone on a 4096-query slice of config 4 "
                          "(positions 60000..64095), or config 5's block step eagerly inside an NVTX range "
-                         "(block_decode), and print its CUDA-event time; not a bench line")
+                         "(block_decode; block_decode_window: the same block at a ratio-128 layer), and print its "
+                         "CUDA-event time; not a bench line")
     args = ap.parse_args()
     if args.kernel_case:
         return run_kernel_case(args)
@@ -882,7 +884,7 @@ def run_kernel_case(args):
     SA = importlib.import_module(PKG + ".sparse_attn")
     IX = importlib.import_module(PKG + ".indexer")
     NRm = importlib.import_module(PKG + ".norm_rope")
-    if args.kernel_case == "block_decode":
+    if args.kernel_case in ("block_decode", "block_decode_window"):
         return run_block_case(args, dev)
     if args.kernel_case == "hc":
         return run_hc_case(args, dev)
@@ -970,15 +972,23 @@ def run_hc_case(args, dev):
 def run_block_case(args, dev):
     """Config 5's block step (batch 32, 16384-token contexts, int8-g64 weights) launched eagerly:
     three warm-up steps, then `--steps` (default 2) steps inside the NVTX range "step", so that a
-    profiler can take exactly those launches (`ncu --nvtx --nvtx-include "step/"`)."""
+    profiler can take exactly those launches (`ncu --nvtx --nvtx-include "step/"`). With
+    `block_decode_window` the block is a ratio-128 (window-only) layer's."""
     import importlib
     Lm = importlib.import_module(PKG + ".layer")
     C = importlib.import_module(PKG + ".configs")
     cfgd = CONFIGS["c5"]
     B, ctx, top_k = cfgd["batch"], cfgd["ctx"], cfgd["top_k"]
-    W = Lm.make_attention_weights(3, quant=True).to(dev)
-    case = C.make_decode_case(B, ctx, top_k, seeds=[cfgd["seeds"](0, i) for i in range(B)], device=dev)
-    blk = Lm.DecodeBlock(W, B, ctx, top_k=top_k, cache=case.cache)
+    if args.kernel_case == "block_decode_window":
+        dims = C.LayerDims(ratio=128)
+        W = Lm.make_attention_weights(3, dims=dims, quant=True).to(dev)
+        blk = Lm.DecodeBlock(W, B, ctx, dims=dims, device=dev)
+        blk.cache.kv_pool.copy_(torch.randn(blk.cache.kv_pool.shape, generator=torch.Generator().manual_seed(3))
+                                .to(torch.bfloat16))
+    else:
+        W = Lm.make_attention_weights(3, quant=True).to(dev)
+        case = C.make_decode_case(B, ctx, top_k, seeds=[cfgd["seeds"](0, i) for i in range(B)], device=dev)
+        blk = Lm.DecodeBlock(W, B, ctx, top_k=top_k, cache=case.cache)
     x = torch.randn(B, 4096, generator=torch.Generator().manual_seed(3)).to(dev)
     pos = torch.full((B,), ctx - 1, dtype=torch.int32, device=dev)
     for _ in range(3):
@@ -993,7 +1003,7 @@ def run_block_case(args, dev):
     e1.record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
-    print(json.dumps({"kernel_case": "block_decode", "batch": B, "ctx": ctx, "eager_ms_per_step": e0.elapsed_time(e1) / reps,
+    print(json.dumps({"kernel_case": args.kernel_case, "batch": B, "ctx": ctx, "eager_ms_per_step": e0.elapsed_time(e1) / reps,
                       "checksum": float(out.abs().sum())}), flush=True)
 
 

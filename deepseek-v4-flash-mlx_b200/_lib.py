@@ -119,6 +119,7 @@ SIGNATURES = {
     "dsv4_last_error": (ctypes.c_char_p, []),
     "dsv4_abi_version": (ctypes.c_int, []),
     "dsv4_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), vp]),
+    "dsv4_selftest_wait_timeout": (ctypes.c_int, [vp]),
     "dsv4_sparse_attn_workspace_size": (sz, [ctypes.POINTER(SparseAttnParams)]),
     "dsv4_sparse_attn": (ctypes.c_int, [ctypes.POINTER(SparseAttnParams), vp]),
     "dsv4_window_topk_idxs": (ctypes.c_int, [i32, i32, i32, i32, vp, vp]),

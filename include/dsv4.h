@@ -63,6 +63,11 @@ DSV4_API int dsv4_abi_version(void);
 /* Reads (and clears) the device error word of the current device after synchronising `stream`.
  * *code receives 0 or a dsv4_status raised by a kernel (index out of range, wait timeout). */
 DSV4_API int dsv4_device_error(int* code, void* stream);
+/* Self-test of the failure path (no counterpart in the reference, which has no kernels): one kernel
+ * waits, with the same bounded wait the tcgen05 kernels use (1 s of %globaltimer), on an mbarrier
+ * that nothing arrives on; it records DSV4_ERR_WAIT_TIMEOUT on the device error word and returns.
+ * dsv4_device_error then reports the timeout, and the context stays usable. */
+DSV4_API int dsv4_selftest_wait_timeout(void* stream);
 
 /* ---- a1: sparse attention --------------------------------------------------------------------
  * o[i,h,:] = sum_t p[i,h,t] kv[idx[i,t],:] / (sum_t p[i,h,t] + exp(sink[h] - m[i,h]))

@@ -58,3 +58,46 @@ def test_cache_all_gather_two_ranks():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: True, 1: True}
+
+
+def _lost_rank_worker(rank, world, port, q):
+    """Rank 1 joins, then leaves between steps (nothing of it in flight); rank 0 then runs the cache
+    exchange and must get an error from the short process-group timeout or the closed connection,
+    not wait for ever."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()  # the item is in the pipe before the process goes
+        os._exit(0)  # leaves without the exchange and without tearing the group down
+    t0 = time.perf_counter()
+    try:
+        sp = P.ShardedPrefill()
+        comp = torch.zeros(8, 4, dtype=torch.bfloat16)
+        keys = torch.zeros(8, 3)
+        sp.gather_cache(comp, keys, 16)
+        q.put((rank, "no error"))
+    except Exception as e:  # the collective fails: a timeout or a closed peer connection
+        q.put((rank, f"error after {time.perf_counter() - t0:.1f} s: {type(e).__name__}"))
+    finally:
+        q.close()
+        q.join_thread()
+        os._exit(0)
+
+
+def test_lost_rank_ends_exchange_with_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_lost_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1] == "left"
+    assert res[0].startswith("error after"), res[0]
+    assert float(res[0].split()[2]) < 60, res[0]
