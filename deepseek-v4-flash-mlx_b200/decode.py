@@ -62,6 +62,53 @@ class SparseMLACache:
         self.ring_s_idx = torch.full((batch, 2 * ratio, 2 * idx_dim), float("-inf"), dtype=torch.float32,
                                      device=device)
 
+    # ---- checkpoint / resume (the reference copies its per-layer state with clone_states,
+    # oracle/v4_fast.py:150-159, and copy.deepcopy, oracle/decode_engine.py:167) ----
+    _STATE = ("kv_pool", "win_base", "block_table", "k_idx", "key_image", "ring_kv", "ring_score", "ring_k_idx",
+              "ring_s_idx")
+
+    def state_dict(self):
+        """The whole decode state as tensors (on the cache's device), for torch.save; the key image
+        is saved as its three buffers."""
+        st = {}
+        for name in self._STATE:
+            v = getattr(self, name)
+            if name == "key_image" and v is not None:
+                for i, t in enumerate(v):
+                    st[f"key_image.{i}"] = t
+            elif v is not None:
+                st[name] = v
+        st["meta"] = torch.tensor([self.batch, self.max_comp, self.window, self.head_dim, self.ratio, self.page,
+                                   int(self.image_stale)], dtype=torch.int64)
+        return st
+
+    def load_state_dict(self, st):
+        """Restore a state_dict into this cache (same shapes; copied into the existing buffers, so
+        CUDA graphs captured on this cache stay valid)."""
+        meta = st["meta"].tolist()
+        if meta[:6] != [self.batch, self.max_comp, self.window, self.head_dim, self.ratio, self.page]:
+            raise ValueError(f"SparseMLACache.load_state_dict: saved layout {meta[:6]} differs from this cache's")
+        for name in self._STATE:
+            v = getattr(self, name)
+            if name == "key_image" and v is not None:
+                for i, t in enumerate(v):
+                    t.copy_(st[f"key_image.{i}"])
+            elif v is not None:
+                v.copy_(st[name])
+        self.image_stale = bool(meta[6])
+
+    def clone(self):
+        """An independent copy of the decode state (new buffers on the same device)."""
+        c = object.__new__(SparseMLACache)
+        c.__dict__.update(self.__dict__)
+        for name in self._STATE:
+            v = getattr(self, name)
+            if name == "key_image" and v is not None:
+                c.key_image = tuple(t.clone() for t in v)
+            elif v is not None:
+                setattr(c, name, v.clone())
+        return c
+
     # ---- address helpers (host side) ----
     def comp_rows(self, b, j):
         """Pool rows of compressed entries j (tensor) of sequence b."""
