@@ -56,8 +56,6 @@ CONFIGS = {
                          "window rings, int8-g64 weights (bf16 scales)"),
 }
 L2_BYTES = 126 * 1024 * 1024
-# kernels of one decode step: q norm/rope, indexer scores, top-k selection, sparse attention, split merge
-LAUNCHES_PER_STEP = 5
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant op, from one
 # ncu capture each on B200: config 2 on this bench's own command (score + select kernels of one
@@ -444,7 +442,7 @@ def main():
                            "l2": f"inputs rotate over {R} replicas x {footprint / 2**20:.1f} MiB = "
                                  f"{R * footprint / 2**20:.0f} MiB > L2 (126 MB)",
                            "cuda_graph": True},
-                "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+                "gpu_launches": decode_launches_per_step(runners[0]) * args.steps,
                 "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -819,6 +817,24 @@ def bench_block_window(args, world, rank, local, dev):
     del graphs
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def decode_launches_per_step(runner):
+    """Kernels one decode step launches: q's norm + RoPE, the indexer's scores (or its tensor-core
+    filter), the top-k selection, sparse attention, and the split merge when the attention plan
+    writes split partials. The plan writes them exactly when its workspace is non-zero; splits merged
+    inside a thread-block cluster need none."""
+    import ctypes
+    import importlib
+    L = importlib.import_module(PKG + "._lib")
+    SA = importlib.import_module(PKG + ".sparse_attn")
+    c = runner.cache
+    qr = torch.empty((c.batch, 64, c.head_dim), dtype=torch.bfloat16, device=runner.idx.device)
+    out = torch.empty(qr.shape, dtype=runner.out_dtype, device=qr.device)
+    p = SA._attn_params(qr, c.kv_pool, runner.sink, runner.idx, out, c.head_dim ** -0.5, runner.freqs,
+                        runner.positions, 64, win_base=c.win_base, window=c.window)
+    merge = L.lib().dsv4_sparse_attn_workspace_size(ctypes.byref(p)) > 0
+    return 4 + int(merge)
 
 
 def kernel_times(dsv4, cases, runners, stream, dev, n):
