@@ -114,6 +114,20 @@ class ClockSampler:
             self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
 
+    def sample_while(self, event, period=0.001):
+        """Sample on the calling thread, every `period` seconds, until `event` (the CUDA event that
+        ends the timed region) has completed: a timed region shorter than the thread's 10 ms period
+        still gets samples while the GPU works through the queued steps."""
+        if not self.ok:
+            return
+        while not event.query():
+            try:
+                self.samples.append((time.perf_counter(), self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM),
+                                     self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)))
+            except Exception:
+                pass
+            time.sleep(period)
+
     def stop(self):
         if self.ok:
             self._stop.set()
@@ -378,6 +392,7 @@ def main():
     e0.record(stream)
     run_steps(args.steps)
     e1.record(stream)
+    sampler.sample_while(e1)
     torch.cuda.synchronize()
     t1 = time.perf_counter()
     if world > 1:
@@ -511,6 +526,7 @@ def bench_prefill(args, world, rank, local, dev):
     for _ in range(steps):
         step()
     e1.record()
+    sampler.sample_while(e1)
     torch.cuda.synchronize()
     t1 = time.perf_counter()
     if world > 1:
@@ -661,6 +677,7 @@ def bench_block(args, world, rank, local, dev):
         for _ in range(steps):
             graph.replay()
     e1.record(stream)
+    sampler.sample_while(e1)
     torch.cuda.synchronize()
     t1 = time.perf_counter()
     if world > 1:
@@ -763,6 +780,7 @@ def bench_block_window(args, world, rank, local, dev):
         for i in range(steps):
             graphs[i % R].replay()
     e1.record(stream)
+    sampler.sample_while(e1)
     torch.cuda.synchronize()
     t1 = time.perf_counter()
     if world > 1:
