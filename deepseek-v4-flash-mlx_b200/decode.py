@@ -235,6 +235,9 @@ class DecodeRunner:
     """
 
     def __init__(self, cache, sink, top_k=512, device="cuda", out_dtype=torch.bfloat16, stream=None):
+        if not cache.compressed:
+            raise ValueError("DecodeRunner runs the compressed layer's step (indexer + sparse attention); a window-only "
+                             "cache (ratio 0 or 128) is stepped by DecodeBlock or window_attention")
         self.cache, self.top_k = cache, top_k
         b = cache.batch
         dev = torch.device(device)

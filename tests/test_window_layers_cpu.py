@@ -77,3 +77,9 @@ def test_decode_rows_window_only_validation(dsv4):
     p.b = 0
     p.window = 128
     assert lib.dsv4_decode_rows(ctypes.byref(p), None) == 0  # empty batch: nothing launched
+
+
+def test_decode_runner_refuses_window_only_cache():
+    D = importlib.import_module(PKG + ".decode")
+    with pytest.raises(ValueError, match="window-only"):
+        D.DecodeRunner(D.SparseMLACache(2, 0, device="cpu"), torch.zeros(64), device="cpu")
