@@ -164,40 +164,84 @@ def _barrier_max(x, world, device):
 
 
 # ------------------------------------------------------------------------------ CPU reference leg
-def cpu_reference(cfg_name, samples, threads=None):
-    """Time the oracle port (torch fp32 + the C indexer restatement) on the host cores for a bounded
-    sample of the config's workload; returns (tok/s, cores, description)."""
-    from oracle import layer_ref as LR
-    from oracle import norm_rope_ref as NR
-    cfgd = CONFIGS[cfg_name]
+CPU_MIN_SECONDS = 10.0  # timed CPU work per reported number (a bounded sample of the workload)
+
+
+def _cpu_threads(threads=None):
     threads = threads or os.cpu_count()
     torch.set_num_threads(threads)
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    return threads
+
+
+def cpu_workload(cfg_name, samples):
+    """Set up, once, a bounded sample of the config's workload for the CPU oracle (torch fp32 + the
+    C indexer restatement). Returns (run, desc): run() performs one timed repetition and returns
+    (tokens, seconds) of it."""
+    from oracle import layer_ref as LR
+    from oracle import norm_rope_ref as NR
+    if cfg_name == "c4":
+        return _cpu_prefill(samples)
+    if cfg_name == "c5":
+        return _cpu_block(samples)
+    if cfg_name == "c5w":
+        return _cpu_block_window(samples)
+    cfgd = CONFIGS[cfg_name]
     C = __import__("importlib").import_module(PKG + ".configs")
     f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
-    if cfg_name == "c4":
-        return _cpu_prefill(samples, threads)
-    if cfg_name == "c5":
-        return _cpu_block(samples, threads)
-    if cfg_name == "c5w":
-        return _cpu_block_window(samples, threads)
     batch = min(cfgd["batch"], samples)
     case = C.make_decode_case(batch, cfgd["ctx"], cfgd["top_k"], seeds=[cfgd["seeds"](0, i) for i in range(batch)],
                               device="cpu", shuffle_pages=True)
     pool, win_base, comp_rows = C.decode_case_host_pool(case)
     h = case.host
-    LR.decode_attention_ref(pool, win_base, comp_rows, h["k_idx"][:1], h["q"][:1], h["q_idx"][:1], h["w_idx"][:1],
-                            h["sink"], h["positions"][:1], cfgd["top_k"], f)  # warm-up
-    t0 = time.perf_counter()
-    LR.decode_attention_ref(pool, win_base, comp_rows, h["k_idx"], h["q"], h["q_idx"], h["w_idx"], h["sink"],
-                            h["positions"], cfgd["top_k"], f)
-    dt = time.perf_counter() - t0
-    return batch / dt, threads, f"{batch} decode token(s) of {cfg_name} through the CPU oracle ({dt:.2f} s)"
+
+    def run():
+        t0 = time.perf_counter()
+        LR.decode_attention_ref(pool, win_base, comp_rows, h["k_idx"], h["q"], h["q_idx"], h["w_idx"], h["sink"],
+                                h["positions"], cfgd["top_k"], f)
+        return batch, time.perf_counter() - t0
+    return run, f"{batch} decode token(s) of {cfg_name} per repetition through the CPU oracle"
 
 
-def _cpu_prefill(nq, threads):
+def cpu_sample_size(cfg_name):
+    """Tokens per repetition of the CPU sample: the block configs run their batch of 32 per call (the
+    weights are read once per call, as a CPU implementation would), config 4 runs 64 queries, the
+    attention-only decode configs one sequence (their oracle loops over sequences anyway)."""
+    return {"c4": 64, "c5": 32, "c5w": 32}.get(cfg_name, 1)
+
+
+def _dequantized(W):
+    """The attention weights with every 8-bit grouped matrix dequantised to fp32 once, so that the
+    CPU oracle's timed repetitions do not repeat the dequantisation."""
+    from dataclasses import fields
+    from oracle.layer_ref import _w
+    return W.__class__(**{f.name: _w(getattr(W, f.name)) if hasattr(getattr(W, f.name), "scale")
+                          else getattr(W, f.name) for f in fields(W)})
+
+
+def timed_rate(run, min_seconds=CPU_MIN_SECONDS):
+    """Repeat run() until at least min_seconds of timed work; returns (tok/s, repetitions, seconds)."""
+    tok = sec = 0.0
+    reps = 0
+    while sec < min_seconds or reps == 0:
+        t, dt = run()
+        tok, sec, reps = tok + t, sec + dt, reps + 1
+    return tok / sec, reps, sec
+
+
+def cpu_reference(cfg_name, samples, threads=None, min_seconds=CPU_MIN_SECONDS):
+    """Time the oracle port on the host cores: one warm-up repetition, then repetitions of the
+    config's bounded sample until at least min_seconds of timed work; returns (tok/s, cores, description)."""
+    threads = _cpu_threads(threads)
+    run, desc = cpu_workload(cfg_name, samples)
+    run()
+    v, reps, sec = timed_rate(run, min_seconds)
+    return v, threads, f"{desc}; {reps} repetitions, {sec:.1f} s of timed CPU work, {threads} threads"
+
+
+def _cpu_prefill(nq):
     """Config 4 per-token CPU cost: the two compressors over a 4096-token slice (per token), plus
-    the indexer over 16384 keys and attention over 1152 rows for nq queries at the end of the
+    the indexer over 16384 keys and attention over 1152 rows for nq queries in the middle of the
     65536-token sequence (per query)."""
     import importlib
     from oracle import compressor_ref as CR
@@ -208,10 +252,6 @@ def _cpu_prefill(nq, threads):
     W = Lm.make_attention_weights(2)
     g = torch.Generator().manual_seed(2)
     xs = torch.randn(4096, 4096, generator=g)
-    t0 = time.perf_counter()
-    CR.compressor_prefill(xs[None], W.c_wkv.float(), W.c_wgate.float(), W.c_ape, W.c_norm)
-    CR.compressor_prefill(xs[None], W.i_wkv.float(), W.i_wgate.float(), W.i_ape, W.i_norm, head_dim=128)
-    t_comp = (time.perf_counter() - t0) / 4096
     s = 65536
     keys = torch.randn(16384, 128, generator=g)
     qi = torch.randn(nq, 64, 128, generator=g)
@@ -220,43 +260,54 @@ def _cpu_prefill(nq, threads):
     kvcat = torch.randn(s + 16384, 512, generator=g).to(torch.bfloat16).float()
     f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
     pos = np.arange(s // 2 - nq, s // 2)   # mid-sequence queries: the average visible key count
-    t0 = time.perf_counter()
-    sel = I.indexer_topk(qi.numpy()[None], wi.numpy()[None], keys.numpy()[None], 1024, positions=pos[None], ratio=4)[0]
     win = np.stack([np.arange(t - 127, t + 1) for t in pos])
-    idx = torch.from_numpy(np.concatenate([win, sel + s], 1).astype(np.int64))
-    o = SA.sparse_attn_chunked(q, kvcat, W.sinks, idx, 512 ** -0.5, chunk=16)
-    NR.rope_at(o, torch.from_numpy(pos), f, inverse=True)
-    t_q = (time.perf_counter() - t0) / nq
-    return 1.0 / (t_comp + t_q), threads, (f"oracle port: compressors over 4096 tokens ({t_comp * 4096:.2f} s) + "
-                                          f"indexer/attention for {nq} queries at position 32K, the sequence's "
-                                          f"average ({t_q * nq:.2f} s)")
+
+    def run():
+        t0 = time.perf_counter()
+        CR.compressor_prefill(xs[None], W.c_wkv.float(), W.c_wgate.float(), W.c_ape, W.c_norm)
+        CR.compressor_prefill(xs[None], W.i_wkv.float(), W.i_wgate.float(), W.i_ape, W.i_norm, head_dim=128)
+        t_comp = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        sel = I.indexer_topk(qi.numpy()[None], wi.numpy()[None], keys.numpy()[None], 1024, positions=pos[None],
+                             ratio=4)[0]
+        idx = torch.from_numpy(np.concatenate([win, sel + s], 1).astype(np.int64))
+        o = SA.sparse_attn_chunked(q, kvcat, W.sinks, idx, 512 ** -0.5, chunk=16)
+        NR.rope_at(o, torch.from_numpy(pos), f, inverse=True)
+        t_q = time.perf_counter() - t0
+        per_token = t_comp / 4096 + t_q / nq   # seconds of one prefill token: its compressor share + one query
+        return (t_comp + t_q) / per_token, t_comp + t_q
+    return run, (f"oracle port, per repetition: compressors over 4096 tokens + indexer/attention for {nq} queries at "
+                 f"position 32K (the sequence's average), combined per token")
 
 
-def _cpu_block_window(nseq, threads):
+def _cpu_block_window(nseq):
     """Window-only (ratio-128) block per-token CPU cost: the oracle decode block without compression."""
     import importlib
     from oracle import layer_ref as LR
     Lm = importlib.import_module(PKG + ".layer")
     C = importlib.import_module(PKG + ".configs")
-    W = Lm.make_attention_weights(3, dims=C.LayerDims(ratio=128), quant=True)
+    W = _dequantized(Lm.make_attention_weights(3, dims=C.LayerDims(ratio=128), quant=True))
     g = torch.Generator().manual_seed(3)
     state = dict(pool=torch.randn(nseq * 128, 512, generator=g).to(torch.bfloat16).float(),
                  win_base=torch.arange(nseq) * 128)
     x = torch.randn(nseq, 4096, generator=g)
     pos = torch.full((nseq,), 16383, dtype=torch.int32)
-    t0 = time.perf_counter()
-    LR.decode_block_ref(state, W, x, pos, ratio=128)
-    dt = time.perf_counter() - t0
-    return nseq / dt, threads, f"{nseq} token(s) of the window-only (ratio-128) block through the CPU oracle ({dt:.2f} s)"
+
+    def run():
+        t0 = time.perf_counter()
+        LR.decode_block_ref(state, W, x, pos, ratio=128)
+        return nseq, time.perf_counter() - t0
+    return run, f"{nseq} token(s) of the window-only (ratio-128) block per repetition through the CPU oracle"
 
 
-def _cpu_block(nseq, threads):
-    """Config 5 per-token CPU cost: the oracle decode block (dequantised int8 weights in fp32)."""
+def _cpu_block(nseq):
+    """Config 5 per-token CPU cost: the oracle decode block (dequantised int8 weights in fp32). Each
+    repetition steps the same token again (same work; the state it writes is overwritten)."""
     import importlib
     from oracle import layer_ref as LR
     Lm = importlib.import_module(PKG + ".layer")
     C = importlib.import_module(PKG + ".configs")
-    W = Lm.make_attention_weights(3, quant=True)
+    W = _dequantized(Lm.make_attention_weights(3, quant=True))
     case = C.make_decode_case(nseq, 16384, 512, seeds=[3 + i for i in range(nseq)], device="cpu")
     pool, win_base, comp_rows = C.decode_case_host_pool(case)
     c = case.cache
@@ -265,33 +316,43 @@ def _cpu_block(nseq, threads):
                  ring_s=c.ring_s_idx.clone())
     x = torch.randn(nseq, 4096, generator=torch.Generator().manual_seed(3))
     pos = torch.full((nseq,), 16383, dtype=torch.int32)
-    t0 = time.perf_counter()
-    LR.decode_block_ref(state, W, x, pos, top_k=512)
-    dt = time.perf_counter() - t0
-    return nseq / dt, threads, f"{nseq} token(s) of the config-5 block through the CPU oracle ({dt:.2f} s)"
+
+    def run():
+        t0 = time.perf_counter()
+        LR.decode_block_ref(state, W, x, pos, top_k=512)
+        return nseq, time.perf_counter() - t0
+    return run, f"{nseq} token(s) of the config-5 block per repetition through the CPU oracle"
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU implementation of the path (its ref_torch code as
+    restated in oracle/, since the reference cannot be installed as a package) on all host cores,
+    on this config's workload. Rank 0 alone runs it; each step is a bounded sample of at least
+    CPU_MIN_SECONDS of timed work."""
     world, rank, _ = _dist()
     if rank != 0:
         return
     cfgd = CONFIGS[args.config]
-    per_step = []
-    n_tok = 64 if args.config == "c4" else 1
-    for _ in range(max(1, args.warmup // 100)):
-        cpu_reference(args.config, n_tok)
+    threads = _cpu_threads()
+    run, desc = cpu_workload(args.config, cpu_sample_size(args.config))
+    warm = max(1, min(args.warmup, 3))
+    for _ in range(warm):
+        run()
+    per_step, reps_total, sec_total = [], 0, 0.0
     for _ in range(min(args.steps, 3)):
-        v, cores, desc = cpu_reference(args.config, n_tok)
+        v, reps, sec = timed_rate(run)
         per_step.append(v)
+        reps_total, sec_total = reps_total + reps, sec_total + sec
     v = statistics.median(per_step)
+    desc = f"{desc}; {reps_total} repetitions over {len(per_step)} steps, {sec_total:.1f} s of timed CPU work"
     line = {"impl": "reference", "metric": METRICS[args.config],
-            "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": len(per_step), "warmup": args.warmup,
+            "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": len(per_step), "warmup": warm,
             "ms_per_step": 1000.0 * (cfgd["ctx"] if args.config == "c4" else cfgd["batch"]) / v,
             "higher_is_better": True, "scaling": "strong" if cfgd.get("strong") or args.config == "c4" else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfgd["workload"], "global_batch": cfgd["batch"], "ctx": cfgd["ctx"],
                        "parallelism": "cpu"},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
                              "sample": desc + "; the reference's ref_torch path restated in oracle/"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -580,7 +641,7 @@ def bench_prefill(args, world, rank, local, dev):
     ems = _barrier_max(f0.elapsed_time(f1), world, dev) / steps
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, desc = cpu_reference("c4", 64)
+        v, cores, desc = cpu_reference("c4", cpu_sample_size("c4"))
         cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
     if rank == 0:
         line = {"metric": METRICS["c4"], "value": s / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
@@ -713,7 +774,7 @@ def bench_block(args, world, rank, local, dev):
                 "algorithmic_bytes_per_launch": step_bytes}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, desc = cpu_reference("c5", 1)
+        v, cores, desc = cpu_reference("c5", cpu_sample_size("c5"))
         cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
     if rank == 0:
         line = {"metric": METRICS["c5"], "value": cfgd["batch"] / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
@@ -817,7 +878,7 @@ def bench_block_window(args, world, rank, local, dev):
                 "algorithmic_bytes_per_launch": step_bytes}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, desc = cpu_reference("c5w", 4)
+        v, cores, desc = cpu_reference("c5w", cpu_sample_size("c5w"))
         cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
     if rank == 0:
         line = {"metric": METRICS["c5w"], "value": cfgd["batch"] / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
