@@ -134,6 +134,32 @@ class SparseMLACache:
     def fill_window(self, b, positions, rows_bf16):
         self.kv_pool[self.window_rows(b, positions)] = rows_bf16.to(torch.bfloat16)
 
+    def load_prefill(self, b, window_rows, comp_rows=None, keys=None, ring=None, key_ring=None):
+        """Seed sequence b's decode state from a prefill of its first s tokens (positions 0..s-1),
+        the state the reference's prefill leaves for its decode steps (oracle/decode_engine.py:86-95):
+        window_rows [s, head_dim] are the tokens' kv rows (the last min(s, window) of them go to
+        their ring slots p % window); comp_rows [n, head_dim] and keys [n, idx_dim] are the
+        compressed entries 0..n-1 and their indexer keys; ring / key_ring = (ring_kv, ring_score)
+        [1 or b, 2*ratio, 2*dim] are the compressors' rings after the prefill (compressor_prefill's
+        state["ring_kv"], state["ring_score"]). The next decode token is at position s."""
+        s = window_rows.shape[0]
+        lo = max(0, s - self.window)
+        pos = torch.arange(lo, s, device=self.kv_pool.device)
+        self.fill_window(b, pos, window_rows[lo:s])
+        if not self.compressed:
+            return
+        n = comp_rows.shape[0] if comp_rows is not None else 0
+        if n > self.max_comp:
+            raise ValueError(f"SparseMLACache.load_prefill: {n} compressed rows exceed the cache's {self.max_comp}")
+        if n:
+            self.fill_compressed(b, comp_rows, keys)
+        if ring is not None:
+            self.ring_kv[b].copy_(ring[0].reshape(self.ring_kv[b].shape))
+            self.ring_score[b].copy_(ring[1].reshape(self.ring_score[b].shape))
+        if key_ring is not None:
+            self.ring_k_idx[b].copy_(key_ring[0].reshape(self.ring_k_idx[b].shape))
+            self.ring_s_idx[b].copy_(key_ring[1].reshape(self.ring_s_idx[b].shape))
+
 
 def decode_rows(cache, positions):
     """Pool rows of one decode step, one launch (dsv4_decode_rows): (win_rows, comp_rows, key_rows),

@@ -100,7 +100,9 @@ def prefill_layer(x, W: AttentionWeights, top_k=512, dims: LayerDims = DIMS, ret
     """x [s, dim] (one sequence from position 0) -> out [s, dim] fp32 (and the int32 index list
     [s, window + top_k] plus intermediates with return_aux). `act_quant`: the fp8 act-quant
     simulation of the cached kv rows and compressed rows (oracle/decode_engine.py:82,
-    v4mlx/compressor.py:60-62)."""
+    v4mlx/compressor.py:60-62). The aux dict also carries the state a decode continues from
+    (kv rows and compressed rows in `kvcat`, keys in `k_idx`, the compressors' rings in `ring` and
+    `key_ring`): `DecodeBlock.load_prefill` takes it."""
     L.require_cuda(x)
     s = x.shape[0]
     dev = x.device
@@ -125,12 +127,12 @@ def prefill_layer(x, W: AttentionWeights, top_k=512, dims: LayerDims = DIMS, ret
     kvcat = torch.empty((s + n_comp, dims.head_dim), dtype=torch.bfloat16, device=dev)
     kvcat[:s] = norm_rope(linear(xn, W.wkv, torch.float32), pos, freqs, weight=W.kv_a_norm, rope_dim=dims.rope_dim,
                           act_quant=act_quant)
-    comp, _ = compressor_prefill(xn[None], W.c_wkv, W.c_wgate, W.c_ape, W.c_norm, head_dim=dims.head_dim,
-                                 ratio=dims.ratio, rope_head_dim=dims.rope_dim, out_dtype=torch.bfloat16,
-                                 act_quant=act_quant)
+    comp, cstate = compressor_prefill(xn[None], W.c_wkv, W.c_wgate, W.c_ape, W.c_norm, head_dim=dims.head_dim,
+                                      ratio=dims.ratio, rope_head_dim=dims.rope_dim, out_dtype=torch.bfloat16,
+                                      act_quant=act_quant)
     kvcat[s:] = comp[0]
-    k_idx, _ = compressor_prefill(xn[None], W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, head_dim=dims.idx_dim,
-                                  ratio=dims.ratio, rope_head_dim=dims.rope_dim, out_dtype=torch.float32)
+    k_idx, kstate = compressor_prefill(xn[None], W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, head_dim=dims.idx_dim,
+                                       ratio=dims.ratio, rope_head_dim=dims.rope_dim, out_dtype=torch.float32)
     q_idx = rope(linear(qa, W.i_wq, torch.float32).view(s, dims.idx_heads, dims.idx_dim), pos, freqs,
                  dims.rope_dim)
     w_idx = linear(xn, W.i_wproj, torch.float32)
@@ -142,7 +144,9 @@ def prefill_layer(x, W: AttentionWeights, top_k=512, dims: LayerDims = DIMS, ret
     o = sparse_attn_rope(q, kvcat, W.sinks, idx[0], dims.head_dim ** -0.5, pos, freqs, dims.rope_dim)
     out = o_grouped(o.reshape(s, -1), W.wo_a, W.wo_b)
     if return_aux:
-        return out, dict(idx=idx[0], o=o, q_idx=q_idx, w_idx=w_idx, k_idx=k_idx, kvcat=kvcat, q=q)
+        return out, dict(idx=idx[0], o=o, q_idx=q_idx, w_idx=w_idx, k_idx=k_idx, kvcat=kvcat, q=q,
+                         ring=(cstate["ring_kv"], cstate["ring_score"]),
+                         key_ring=(kstate["ring_kv"], kstate["ring_score"]))
     return out
 
 
@@ -164,6 +168,18 @@ class DecodeBlock:
         self.batch = batch
         b = torch.arange(batch, device=device)
         self._seq = b
+
+    def load_prefill(self, b, aux):
+        """Continue sequence b from a `prefill_layer(..., return_aux=True)` of its first s tokens
+        (same weights and dims): its window rows, compressed rows, indexer keys and compressor rings
+        go into the cache, as the reference's prefill leaves its layer state for the decode steps
+        (oracle/decode_engine.py:86-95). The next `step` for b is at position s."""
+        s = aux["q"].shape[0]
+        if self.window_only:
+            self.cache.load_prefill(b, aux["kvcat"][:s])
+            return
+        self.cache.load_prefill(b, aux["kvcat"][:s], aux["kvcat"][s:], aux["k_idx"].reshape(-1, self.dims.idx_dim),
+                                ring=aux["ring"], key_ring=aux["key_ring"])
 
     def step(self, x, positions):
         """x [b, dim] fp32/bf16, positions int32 [b] (position of this token) -> out [b, dim] fp32."""

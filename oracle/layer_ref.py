@@ -85,10 +85,13 @@ def _w(v):
 
 
 def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=512, idx_heads=64, idx_dim=128,
-                      rope_dim=64, groups=8, indexer_inputs=None, act_quant=False):
+                      rope_dim=64, groups=8, indexer_inputs=None, act_quant=False, return_state=False):
     """fp32 restatement of oracle/decode_engine.py:75-119 plus the indexer selection.
     indexer_inputs=(q_idx, w_idx, k_idx) lets a test score the selection on given inputs.
-    Returns (out [s, dim], idx [s, window + top_k], o [s, heads, head_dim])."""
+    Returns (out [s, dim], idx [s, window + top_k], o [s, heads, head_dim]); with return_state also
+    the state the reference's prefill leaves for its decode steps (oracle/decode_engine.py:86-95):
+    dict(kv [s, head_dim] rows, comp [s//ratio, head_dim] rows, k_idx keys, ring / key_ring =
+    (ring_kv, ring_score) [1, 2*ratio, 2*dim] seeded from the compressors' projections)."""
     from .compressor_ref import compressor_prefill
     from .mla_ref import o_grouped
     from .norm_rope_ref import rmsnorm
@@ -109,7 +112,8 @@ def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=5
         idx = win[:, :min(s, window)]
         o = sparse_attn_chunked(q, kv, W.sinks, idx, head_dim ** -0.5)
         o = rope_at(o, pos, f, rope_dim, inverse=True)
-        return o_grouped(o.reshape(s, -1), _w(W.wo_a), _w(W.wo_b), groups=groups), idx, o
+        res = (o_grouped(o.reshape(s, -1), _w(W.wo_a), _w(W.wo_b), groups=groups), idx, o)
+        return (*res, dict(kv=kv)) if return_state else res
     comp, _ = compressor_prefill(xn[None], _w(W.c_wkv), _w(W.c_wgate), W.c_ape, W.c_norm, head_dim=head_dim,
                                  ratio=ratio, rope_head_dim=rope_dim)
     if act_quant:  # oracle/decode_engine.py:82 (kv rows) and the compressor's sim (v4mlx/compressor.py:60-62)
@@ -132,7 +136,12 @@ def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=5
     o = sparse_attn_chunked(q, kvcat, W.sinks, idx, head_dim ** -0.5)
     o = rope_at(o, pos, f, rope_dim, inverse=True)
     out = o_grouped(o.reshape(s, -1), _w(W.wo_a), _w(W.wo_b), groups=groups)
-    return out, idx, o
+    if not return_state:
+        return out, idx, o
+    from .compressor_ref import ring_from_prefill
+    ring = ring_from_prefill((xn @ _w(W.c_wkv).T)[None], (xn @ _w(W.c_wgate).T)[None], W.c_ape, s, ratio)
+    key_ring = ring_from_prefill((xn @ _w(W.i_wkv).T)[None], (xn @ _w(W.i_wgate).T)[None], W.i_ape, s, ratio)
+    return out, idx, o, dict(kv=kv, comp=comp[0], k_idx=k_idx, ring=ring, key_ring=key_ring)
 
 
 def decode_block_ref(state, W, x, positions, top_k=512, window=128, ratio=4, heads=64, head_dim=512, idx_heads=64,
