@@ -178,6 +178,9 @@ class DecodeBlock:
         if self.window_only:
             self.cache.load_prefill(b, aux["kvcat"][:s])
             return
+        if "ring" not in aux:
+            raise ValueError("DecodeBlock.load_prefill: the prefill state comes from a window-only layer, this block "
+                             "compresses (its dims.ratio is 4)")
         self.cache.load_prefill(b, aux["kvcat"][:s], aux["kvcat"][s:], aux["k_idx"].reshape(-1, self.dims.idx_dim),
                                 ring=aux["ring"], key_ring=aux["key_ring"])
 

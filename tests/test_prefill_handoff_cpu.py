@@ -66,3 +66,13 @@ def test_load_prefill_places_rows_keys_and_rings():
     assert torch.equal(c.ring_kv[0], torch.zeros(8, 1024))  # the other sequence is untouched
     with pytest.raises(ValueError):
         c.load_prefill(0, rows, torch.zeros(101, 512), torch.zeros(101, 128))
+
+
+def test_block_load_prefill_rejects_a_window_only_state():
+    Lm = importlib.import_module(PKG + ".layer")
+    C = importlib.import_module(PKG + ".configs")
+    dims = C.LayerDims(dim=256, q_lora=128)
+    blk = Lm.DecodeBlock(Lm.make_attention_weights(0, dims=dims), 1, 256, dims=dims, device="cpu")
+    aux = dict(q=torch.zeros(10, 64, 512), kvcat=torch.zeros(10, 512))   # what a window-only prefill returns
+    with pytest.raises(ValueError, match="window-only"):
+        blk.load_prefill(0, aux)
