@@ -1,4 +1,6 @@
 """The canonical-order indexer oracle (C) on the CPU: scores, selection rule, ties, padding."""
+from fractions import Fraction
+
 import numpy as np
 
 from oracle import indexer_ref as I
@@ -59,3 +61,49 @@ def test_causal_visibility_per_query():
         sc = I.scores(q[0, i], w[0, i], k[0, :nv])
         np.testing.assert_array_equal(out[0, i], I.select(sc, 4))
         assert out[0, i].max() < nv
+
+
+def _round_f32(x):
+    """The float32 nearest to the rational x, ties to the even significand (IEEE round-to-nearest)."""
+    c = np.float32(float(x))  # within one ulp of the answer (float64 then float32 may round twice)
+    best = None
+    for cand in (np.nextafter(c, np.float32(-np.inf)), c, np.nextafter(c, np.float32(np.inf))):
+        d = abs(Fraction(float(cand)) - x)
+        even = (int(np.array(cand, dtype=np.float32).view(np.uint32)) & 1) == 0
+        if best is None or d < best[0] or (d == best[0] and even):
+            best = (d, cand)
+    return np.float32(best[1])
+
+
+def _fmaf(a, b, c):
+    return _round_f32(Fraction(float(a)) * Fraction(float(b)) + Fraction(float(c)))
+
+
+def _score_exact(q, w, k, fused=True):
+    """The documented canonical order, with each fmaf rounded once from its exact value (fused), or
+    as a rounded product then a rounded sum (not fused)."""
+    step = _fmaf if fused else (lambda a, b, c: np.float32(np.float32(a * b) + c))
+    part = []
+    for m in range(16):
+        p = np.float32(0.0)
+        for h in range(4 * m, 4 * m + 4):
+            d = np.float32(0.0)
+            for i in range(128):
+                d = step(q[h, i], k[i], d)
+            p = step(w[h], d if d > 0 else np.float32(0.0), p)
+        part.append(p)
+    while len(part) > 1:
+        part = [np.float32(part[2 * t] + part[2 * t + 1]) for t in range(len(part) // 2)]
+    return part[0]
+
+
+def test_c_oracle_is_the_canonical_fma_order():
+    """The C oracle (which the GPU score kernels match bit for bit) against an independent Python
+    restatement of its documented order with exactly rounded fmaf: equal bit for bit, and different
+    from the same order without fused multiply-adds (so the comparison can tell them apart)."""
+    q, w, k = _rand(4, 5)
+    got = I.scores(q, w, k)
+    fused = np.array([_score_exact(q, w, k[j]) for j in range(4)], dtype=np.float32)
+    plain = np.array([_score_exact(q, w, k[j], fused=False) for j in range(4)], dtype=np.float32)
+    np.testing.assert_array_equal(got.view(np.uint32), fused.view(np.uint32))
+    assert (plain.view(np.uint32) != fused.view(np.uint32)).any()
