@@ -1,0 +1,68 @@
+"""Generate tests/golden/mla_golden.npz from the reference's own v4mlx/mla.py on seeded inputs.
+
+Run where a checkout of the reference project is available:
+    python tests/golden/make_mla_golden.py <reference checkout>
+The module imports mlx, which is absent here (no Apple GPU). Its projection functions use only `@`,
+`.T`, `reshape`, `.square()`, `mean`, `mx.rsqrt` and `mx.stack`, so they run unchanged on numpy
+arrays given a small stand-in for `mlx.core` that provides those two functions. The module's shape
+constants (heads, head dim, groups, o_lora) are read when a function runs, so they are set to small
+values for small fixtures; the code path is the reference's own. Recorded (inputs included):
+q_down, q_up, perhead_norm, kv_proj and o_grouped (v4mlx/mla.py:16-56).
+"""
+import os
+import sys
+import types
+
+import numpy as np
+
+OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "mla_golden.npz")
+
+
+class _Array(np.ndarray):
+    """numpy array with the one array method the module calls that numpy lacks."""
+
+    def square(self):
+        return np.square(self)
+
+
+def _install_mlx_stand_in():
+    core = types.ModuleType("mlx.core")
+    core.rsqrt = lambda x: (1.0 / np.sqrt(x)).astype(np.float32)
+    core.stack = np.stack
+    pkg = types.ModuleType("mlx")
+    pkg.core = core
+    sys.modules["mlx"], sys.modules["mlx.core"] = pkg, core
+
+
+def main(ref_root):
+    _install_mlx_stand_in()
+    sys.path.insert(0, ref_root)
+    from v4mlx import mla as M
+
+    M.N_HEADS, M.HEAD_DIM, M.N_GROUPS, M.O_LORA = 8, 32, 8, 16
+    rng = np.random.default_rng(20)
+
+    def arr(*shape, scale=1.0):
+        return (rng.standard_normal(shape) * scale).astype(np.float32).view(_Array)
+
+    dim, q_lora, s = 64, 32, 3
+    x = arr(s, dim)
+    wq_a, wq_b = arr(q_lora, dim, scale=0.1), arr(M.N_HEADS * M.HEAD_DIM, q_lora, scale=0.1)
+    wkv = arr(M.HEAD_DIM, dim, scale=0.1)
+    o = arr(s, M.N_HEADS * M.HEAD_DIM)
+    wo_a = arr(M.N_GROUPS * M.O_LORA, M.N_HEADS * M.HEAD_DIM // M.N_GROUPS, scale=0.1)
+    wo_b = arr(dim, M.N_GROUPS * M.O_LORA, scale=0.1)
+    qa = M.q_down(x, wq_a)
+    qraw = M.q_up(qa, wq_b)
+    g = dict(mla_x=x, mla_wq_a=wq_a, mla_wq_b=wq_b, mla_wkv=wkv, mla_o=o, mla_wo_a=wo_a, mla_wo_b=wo_b,
+             mla_q_down=qa, mla_q_up=qraw, mla_perhead_norm=M.perhead_norm(qraw), mla_kv_proj=M.kv_proj(x, wkv),
+             mla_o_grouped=M.o_grouped(o, wo_a, wo_b),
+             mla_shape=np.array([M.N_HEADS, M.HEAD_DIM, M.N_GROUPS, M.O_LORA], dtype=np.int64))
+    np.savez_compressed(OUT, **{k: np.asarray(v) for k, v in g.items()})
+    print("wrote", OUT, sorted(g))
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_mla_golden.py <reference checkout>")
+    main(sys.argv[1])

@@ -125,3 +125,26 @@ def test_e2m1_round_ties_and_edges():
     got = Q._e2m1_round(x)
     np.testing.assert_array_equal(got, want)
     assert np.signbit(got[1]) and np.signbit(Q._e2m1_round(np.float32(-0.2)))
+
+
+def test_mla_projections_match_reference():
+    """oracle/mla_ref.py and the per-head norm against the reference's own v4mlx/mla.py functions
+    (run on numpy arrays with a stand-in for mlx.core, at reduced shapes; tests/golden/make_mla_golden.py)."""
+    import os
+
+    import torch
+
+    from oracle import mla_ref as M
+    from oracle.norm_rope_ref import perhead_norm
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mla_golden.npz"))
+    heads, head_dim, groups, _ = (int(v) for v in g["mla_shape"])
+    t = {k: torch.from_numpy(g[k]) for k in g.files}
+    tol = dict(rtol=1e-5, atol=1e-6)  # fp32 matmuls, summed in a different order than numpy's
+    qa = M.linear(t["mla_x"], t["mla_wq_a"])
+    np.testing.assert_allclose(qa.numpy(), g["mla_q_down"], **tol)
+    q = M.q_up(t["mla_q_down"], t["mla_wq_b"], heads=heads, head_dim=head_dim)
+    np.testing.assert_allclose(q.numpy(), g["mla_q_up"], **tol)
+    np.testing.assert_allclose(perhead_norm(t["mla_q_up"]).numpy(), g["mla_perhead_norm"], **tol)
+    np.testing.assert_allclose(M.linear(t["mla_x"], t["mla_wkv"]).numpy(), g["mla_kv_proj"], **tol)
+    out = M.o_grouped(t["mla_o"], t["mla_wo_a"], t["mla_wo_b"], groups=groups)
+    np.testing.assert_allclose(out.numpy(), g["mla_o_grouped"], **tol)
