@@ -1,4 +1,5 @@
-"""Generate tests/golden/mla_golden.npz from the reference's own v4mlx/mla.py on seeded inputs.
+"""Generate tests/golden/mla_golden.npz from the reference's own v4mlx/mla.py and v4mlx/sparse_attn.py
+on seeded inputs.
 
 Run where a checkout of the reference project is available:
     python tests/golden/make_mla_golden.py <reference checkout>
@@ -7,7 +8,9 @@ The module imports mlx, which is absent here (no Apple GPU). Its projection func
 arrays given a small stand-in for `mlx.core` that provides those two functions. The module's shape
 constants (heads, head dim, groups, o_lora) are read when a function runs, so they are set to small
 values for small fixtures; the code path is the reference's own. Recorded (inputs included):
-q_down, q_up, perhead_norm, kv_proj and o_grouped (v4mlx/mla.py:16-56).
+q_down, q_up, perhead_norm, kv_proj and o_grouped (v4mlx/mla.py:16-56); the MLX twin of sparse
+attention and of the prefill window list (v4mlx/sparse_attn.py:16-39), which need `arange`,
+`maximum`, `where`, `einsum`, `exp` and `inf` from the stand-in.
 """
 import os
 import sys
@@ -29,6 +32,8 @@ def _install_mlx_stand_in():
     core = types.ModuleType("mlx.core")
     core.rsqrt = lambda x: (1.0 / np.sqrt(x)).astype(np.float32)
     core.stack = np.stack
+    core.arange, core.maximum, core.where, core.einsum, core.exp = np.arange, np.maximum, np.where, np.einsum, np.exp
+    core.inf = np.float32(np.inf)
     pkg = types.ModuleType("mlx")
     pkg.core = core
     sys.modules["mlx"], sys.modules["mlx.core"] = pkg, core
@@ -58,6 +63,16 @@ def main(ref_root):
              mla_q_down=qa, mla_q_up=qraw, mla_perhead_norm=M.perhead_norm(qraw), mla_kv_proj=M.kv_proj(x, wkv),
              mla_o_grouped=M.o_grouped(o, wo_a, wo_b),
              mla_shape=np.array([M.N_HEADS, M.HEAD_DIM, M.N_GROUPS, M.O_LORA], dtype=np.int64))
+    from v4mlx import sparse_attn as SA
+    n, sq, t = 200, 5, 48
+    sq_q, sq_kv = rng.standard_normal((sq, 16, 512)).astype(np.float32), rng.standard_normal((n, 512)).astype(np.float32)
+    sink = rng.standard_normal(16).astype(np.float32)
+    idx = rng.integers(0, n, (sq, t))
+    idx[0, 3:9] = -1
+    idx[2, ::4] = -1
+    g.update(mlxsa_q=sq_q, mlxsa_kv=sq_kv, mlxsa_sink=sink, mlxsa_idx=idx,
+             mlxsa_out=SA.sparse_attn(sq_q, sq_kv, sink, idx, np.float32(512 ** -0.5)),
+             mlxsa_win_20_8=SA.get_window_topk_idxs(8, 20), mlxsa_win_5_128=SA.get_window_topk_idxs(128, 5))
     np.savez_compressed(OUT, **{k: np.asarray(v) for k, v in g.items()})
     print("wrote", OUT, sorted(g))
 

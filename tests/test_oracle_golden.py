@@ -148,3 +148,20 @@ def test_mla_projections_match_reference():
     np.testing.assert_allclose(M.linear(t["mla_x"], t["mla_wkv"]).numpy(), g["mla_kv_proj"], **tol)
     out = M.o_grouped(t["mla_o"], t["mla_wo_a"], t["mla_wo_b"], groups=groups)
     np.testing.assert_allclose(out.numpy(), g["mla_o_grouped"], **tol)
+
+
+def test_sparse_attn_matches_reference_mlx_twin():
+    """The oracle's sparse attention and prefill window list against the reference's MLX twin
+    (v4mlx/sparse_attn.py, run on numpy with a stand-in for mlx.core; tests/golden/make_mla_golden.py):
+    the two reference forms and the oracle agree."""
+    import os
+
+    import torch
+
+    from oracle import sparse_attn_ref as SA
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mla_golden.npz"))
+    out = SA.sparse_attn(torch.from_numpy(g["mlxsa_q"]), torch.from_numpy(g["mlxsa_kv"]),
+                         torch.from_numpy(g["mlxsa_sink"]), torch.from_numpy(g["mlxsa_idx"]), 512 ** -0.5)
+    np.testing.assert_allclose(out.numpy(), g["mlxsa_out"], rtol=2e-5, atol=2e-6)
+    for key, (w, s) in (("mlxsa_win_20_8", (8, 20)), ("mlxsa_win_5_128", (128, 5))):
+        np.testing.assert_array_equal(SA.get_window_topk_idxs(w, 1, s, 0)[0].numpy(), g[key])
