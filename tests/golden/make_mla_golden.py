@@ -10,7 +10,10 @@ constants (heads, head dim, groups, o_lora) are read when a function runs, so th
 values for small fixtures; the code path is the reference's own. Recorded (inputs included):
 q_down, q_up, perhead_norm, kv_proj and o_grouped (v4mlx/mla.py:16-56); the MLX twin of sparse
 attention and of the prefill window list (v4mlx/sparse_attn.py:16-39), which need `arange`,
-`maximum`, `where`, `einsum`, `exp` and `inf` from the stand-in.
+`maximum`, `where`, `einsum`, `exp` and `inf` from the stand-in; and the MLX twin of the compressor
+(v4mlx/compressor.py:32-63) without and with its fp8 simulation, and as the indexer-key compressor
+with `rotate`, for which the stand-in also gives `float32`, `full`, `array`, `concatenate`, `clip`,
+`cos`, `sin` and a softmax along one axis.
 """
 import os
 import sys
@@ -34,6 +37,16 @@ def _install_mlx_stand_in():
     core.stack = np.stack
     core.arange, core.maximum, core.where, core.einsum, core.exp = np.arange, np.maximum, np.where, np.einsum, np.exp
     core.inf = np.float32(np.inf)
+    core.float32, core.clip, core.cos, core.sin = np.float32, np.clip, np.cos, np.sin
+
+    def wrap(fn):  # results keep the array method the reference code calls (`.square()`)
+        return lambda *a, **k: np.asarray(fn(*a, **k)).view(_Array)
+
+    def softmax(a, axis):
+        e = np.exp(a - a.max(axis=axis, keepdims=True))
+        return e / e.sum(axis=axis, keepdims=True)
+    core.full, core.array, core.concatenate, core.softmax = (wrap(np.full), wrap(np.asarray),
+                                                             wrap(np.concatenate), wrap(softmax))
     pkg = types.ModuleType("mlx")
     pkg.core = core
     sys.modules["mlx"], sys.modules["mlx.core"] = pkg, core
@@ -73,6 +86,21 @@ def main(ref_root):
     g.update(mlxsa_q=sq_q, mlxsa_kv=sq_kv, mlxsa_sink=sink, mlxsa_idx=idx,
              mlxsa_out=SA.sparse_attn(sq_q, sq_kv, sink, idx, np.float32(512 ** -0.5)),
              mlxsa_win_20_8=SA.get_window_topk_idxs(8, 20), mlxsa_win_5_128=SA.get_window_topk_idxs(128, 5))
+    from v4mlx import compressor as CMP
+    dim_c = 48
+    cx = rng.standard_normal((1, 18, dim_c)).astype(np.float32).view(_Array)  # 4 full blocks, remainder 2
+    for hd, tag in ((512, "cmp"), (128, "icmp")):
+        wkv = (rng.standard_normal((2 * hd, dim_c)) * 0.1).astype(np.float32)
+        wgate = (rng.standard_normal((2 * hd, dim_c)) * 0.1).astype(np.float32)
+        ape = (rng.standard_normal((4, 2 * hd)) * 0.1).astype(np.float32)
+        nw = (rng.random(hd) + 0.5).astype(np.float32)
+        g.update({f"mlx{tag}_x": cx, f"mlx{tag}_wkv": wkv, f"mlx{tag}_wgate": wgate, f"mlx{tag}_ape": ape,
+                  f"mlx{tag}_nw": nw,
+                  f"mlx{tag}_rows": CMP.compressor_prefill(cx, wkv, wgate, ape, nw, head_dim=hd, apply_sim=False)})
+        if hd == 512:
+            g["mlxcmp_rows_sim"] = CMP.compressor_prefill(cx, wkv, wgate, ape, nw, head_dim=hd, apply_sim=True)
+        else:
+            g["mlxicmp_rows_rotate"] = CMP.compressor_prefill(cx, wkv, wgate, ape, nw, head_dim=hd, rotate=True)
     np.savez_compressed(OUT, **{k: np.asarray(v) for k, v in g.items()})
     print("wrote", OUT, sorted(g))
 

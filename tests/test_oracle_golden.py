@@ -165,3 +165,27 @@ def test_sparse_attn_matches_reference_mlx_twin():
     np.testing.assert_allclose(out.numpy(), g["mlxsa_out"], rtol=2e-5, atol=2e-6)
     for key, (w, s) in (("mlxsa_win_20_8", (8, 20)), ("mlxsa_win_5_128", (128, 5))):
         np.testing.assert_array_equal(SA.get_window_topk_idxs(w, 1, s, 0)[0].numpy(), g[key])
+
+
+def test_compressor_matches_reference_mlx_twin():
+    """The oracle's compressor against the reference's MLX twin (v4mlx/compressor.py, run on numpy
+    with a stand-in for mlx.core; tests/golden/make_mla_golden.py): the rows before any simulation
+    to fp32 accuracy, and the twin's fp8 (main compressor) and Hadamard + fp4 (indexer compressor,
+    `rotate`) rows equal bit for bit to the oracle's simulations applied to the twin's own rows, which
+    pins where the twin applies them (after the norm and RoPE; fp8 on the nope dims only)."""
+    import os
+
+    import torch
+
+    from oracle import compressor_ref as CR
+    from oracle import quant_ref as Q
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mla_golden.npz"))
+    for tag, hd in (("cmp", 512), ("icmp", 128)):
+        t = {k: torch.from_numpy(g[f"mlx{tag}_{k}"]) for k in ("x", "wkv", "wgate", "ape", "nw")}
+        rows, _ = CR.compressor_prefill(t["x"], t["wkv"], t["wgate"], t["ape"], t["nw"], head_dim=hd)
+        np.testing.assert_allclose(rows.numpy(), g[f"mlx{tag}_rows"], rtol=1e-4, atol=2e-5)
+    twin = torch.from_numpy(g["mlxcmp_rows"])
+    sim = Q.act_quant_rows(twin, 64).numpy()
+    np.testing.assert_array_equal(sim.view(np.uint32), g["mlxcmp_rows_sim"].view(np.uint32))
+    rot = Q.rotate_quant_rows(torch.from_numpy(g["mlxicmp_rows"])).numpy()
+    np.testing.assert_array_equal(rot.view(np.uint32), g["mlxicmp_rows_rotate"].astype(np.float32).view(np.uint32))
