@@ -13,7 +13,8 @@ attention and of the prefill window list (v4mlx/sparse_attn.py:16-39), which nee
 `maximum`, `where`, `einsum`, `exp` and `inf` from the stand-in; and the MLX twin of the compressor
 (v4mlx/compressor.py:32-63) without and with its fp8 simulation, and as the indexer-key compressor
 with `rotate`, for which the stand-in also gives `float32`, `full`, `array`, `concatenate`, `clip`,
-`cos`, `sin` and a softmax along one axis.
+`cos`, `sin` and a softmax along one axis; and the MLX twin of the hyper-connections
+(v4mlx/hc.py: hc_pre, hc_post, hc_head), which adds `sigmoid` and `sum`.
 """
 import os
 import sys
@@ -47,6 +48,8 @@ def _install_mlx_stand_in():
         return e / e.sum(axis=axis, keepdims=True)
     core.full, core.array, core.concatenate, core.softmax = (wrap(np.full), wrap(np.asarray),
                                                              wrap(np.concatenate), wrap(softmax))
+    core.sigmoid = wrap(lambda a: 1.0 / (1.0 + np.exp(-a)))
+    core.sum = wrap(np.sum)
     pkg = types.ModuleType("mlx")
     pkg.core = core
     sys.modules["mlx"], sys.modules["mlx.core"] = pkg, core
@@ -101,6 +104,18 @@ def main(ref_root):
             g["mlxcmp_rows_sim"] = CMP.compressor_prefill(cx, wkv, wgate, ape, nw, head_dim=hd, apply_sim=True)
         else:
             g["mlxicmp_rows_rotate"] = CMP.compressor_prefill(cx, wkv, wgate, ape, nw, head_dim=hd, rotate=True)
+    from v4mlx import hc as HC
+    hdim = 32
+    hx = rng.standard_normal((1, 3, 4, hdim)).astype(np.float32).view(_Array)
+    hfn = (rng.standard_normal((24, 4 * hdim)) * 0.05).astype(np.float32)
+    hscale = (rng.random(3) + 0.5).astype(np.float32)
+    hbase = (rng.standard_normal(24) * 0.1).astype(np.float32)
+    y, post, comb = HC.hc_pre(hx, hfn, hscale, hbase)
+    att = rng.standard_normal((1, 3, hdim)).astype(np.float32).view(_Array)
+    head_fn = (rng.standard_normal((4, 4 * hdim)) * 0.05).astype(np.float32)
+    g.update(mlxhc_x=hx, mlxhc_fn=hfn, mlxhc_scale=hscale, mlxhc_base=hbase, mlxhc_y=y, mlxhc_post=post,
+             mlxhc_comb=comb, mlxhc_att=att, mlxhc_post_y=HC.hc_post(att, hx, post, comb), mlxhc_head_fn=head_fn,
+             mlxhc_head_y=HC.hc_head(hx, head_fn, hscale[:1], hbase[:4]))
     np.savez_compressed(OUT, **{k: np.asarray(v) for k, v in g.items()})
     print("wrote", OUT, sorted(g))
 

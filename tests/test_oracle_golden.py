@@ -189,3 +189,21 @@ def test_compressor_matches_reference_mlx_twin():
     np.testing.assert_array_equal(sim.view(np.uint32), g["mlxcmp_rows_sim"].view(np.uint32))
     rot = Q.rotate_quant_rows(torch.from_numpy(g["mlxicmp_rows"])).numpy()
     np.testing.assert_array_equal(rot.view(np.uint32), g["mlxicmp_rows_rotate"].astype(np.float32).view(np.uint32))
+
+
+def test_hyper_connections_match_reference_mlx_twin():
+    """The float64 hyper-connection oracle against the reference's MLX twin (v4mlx/hc.py, run in
+    float32 on numpy with a stand-in for mlx.core; tests/golden/make_mla_golden.py)."""
+    import os
+
+    from oracle import hc_ref as H
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mla_golden.npz"))
+    tol = dict(rtol=2e-5, atol=2e-6)  # the twin runs in float32, the oracle in float64
+    y, post, comb = H.hc_pre(g["mlxhc_x"], g["mlxhc_fn"], g["mlxhc_scale"], g["mlxhc_base"])
+    np.testing.assert_allclose(y, g["mlxhc_y"], **tol)
+    np.testing.assert_allclose(post, g["mlxhc_post"], **tol)
+    np.testing.assert_allclose(comb, g["mlxhc_comb"], **tol)
+    np.testing.assert_allclose(H.hc_post(g["mlxhc_att"], g["mlxhc_x"], g["mlxhc_post"], g["mlxhc_comb"]),
+                               g["mlxhc_post_y"], **tol)
+    yh = H.hc_head(g["mlxhc_x"], g["mlxhc_head_fn"], g["mlxhc_scale"][:1], g["mlxhc_base"][:4])
+    np.testing.assert_allclose(yh, g["mlxhc_head_y"], **tol)
