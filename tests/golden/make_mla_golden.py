@@ -14,7 +14,9 @@ attention and of the prefill window list (v4mlx/sparse_attn.py:16-39), which nee
 (v4mlx/compressor.py:32-63) without and with its fp8 simulation, and as the indexer-key compressor
 with `rotate`, for which the stand-in also gives `float32`, `full`, `array`, `concatenate`, `clip`,
 `cos`, `sin` and a softmax along one axis; and the MLX twin of the hyper-connections
-(v4mlx/hc.py: hc_pre, hc_post, hc_head), which adds `sigmoid` and `sum`.
+(v4mlx/hc.py: hc_pre, hc_post, hc_head), which adds `sigmoid` and `sum`; and the MLX twin of the
+norm and RoPE (v4mlx/norm_rope.py: precompute_freqs, the cos/sin rotation forward and inverse,
+rmsnorm).
 """
 import os
 import sys
@@ -116,6 +118,18 @@ def main(ref_root):
     g.update(mlxhc_x=hx, mlxhc_fn=hfn, mlxhc_scale=hscale, mlxhc_base=hbase, mlxhc_y=y, mlxhc_post=post,
              mlxhc_comb=comb, mlxhc_att=att, mlxhc_post_y=HC.hc_post(att, hx, post, comb), mlxhc_head_fn=head_fn,
              mlxhc_head_y=HC.hc_head(hx, head_fn, hscale[:1], hbase[:4]))
+    from v4mlx import norm_rope as NRM
+    cos, sin = NRM.rope_cos_sin(64, 16, 65536, 160000.0, 16, 32, 1)
+    rx3 = rng.standard_normal((1, 16, 64)).astype(np.float32).view(_Array)
+    rx4 = rng.standard_normal((1, 16, 4, 64)).astype(np.float32).view(_Array)
+    nx = rng.standard_normal((3, 512)).astype(np.float32).view(_Array)
+    nwt = (rng.standard_normal(512) * 0.1 + 1).astype(np.float32)
+    g.update(mlxnr_freqs_yarn=NRM.precompute_freqs(64, 65536, 160000.0, 16, 32, 1),
+             mlxnr_freqs_plain=NRM.precompute_freqs(64, 0, 10000.0, 40, 32, 1),
+             mlxnr_x3=rx3, mlxnr_x4=rx4, mlxnr_x3_fwd=NRM.apply_rotary_emb(rx3, cos, sin),
+             mlxnr_x3_inv=NRM.apply_rotary_emb(rx3, cos, sin, inverse=True),
+             mlxnr_x4_fwd=NRM.apply_rotary_emb(rx4, cos, sin), mlxnr_nx=nx, mlxnr_nw=nwt,
+             mlxnr_rms=NRM.rmsnorm(nx, nwt))
     np.savez_compressed(OUT, **{k: np.asarray(v) for k, v in g.items()})
     print("wrote", OUT, sorted(g))
 

@@ -207,3 +207,27 @@ def test_hyper_connections_match_reference_mlx_twin():
                                g["mlxhc_post_y"], **tol)
     yh = H.hc_head(g["mlxhc_x"], g["mlxhc_head_fn"], g["mlxhc_scale"][:1], g["mlxhc_base"][:4])
     np.testing.assert_allclose(yh, g["mlxhc_head_y"], **tol)
+
+
+def test_norm_rope_match_reference_mlx_twin():
+    """The oracle's YaRN tables, RoPE (forward and inverse, with and without a head axis) and RMSNorm
+    against the reference's MLX twin (v4mlx/norm_rope.py on numpy with a stand-in for mlx.core,
+    whose cos/sin tables are float32 where ref_torch builds complex64 ones)."""
+    import os
+
+    import torch
+
+    from oracle import norm_rope_ref as NR
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mla_golden.npz"))
+    fy = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    np.testing.assert_allclose(fy.numpy(), g["mlxnr_freqs_yarn"], rtol=1e-6)
+    np.testing.assert_allclose(NR.precompute_freqs(64, 0, 0, 10000.0, 40, 32, 1).numpy(), g["mlxnr_freqs_plain"],
+                               rtol=1e-6)
+    pos = torch.arange(16)
+    tol = dict(rtol=1e-5, atol=1e-5)
+    x3, x4 = torch.from_numpy(g["mlxnr_x3"]), torch.from_numpy(g["mlxnr_x4"])
+    np.testing.assert_allclose(NR.rope_at(x3[0], pos, fy).numpy(), g["mlxnr_x3_fwd"][0], **tol)
+    np.testing.assert_allclose(NR.rope_at(x3[0], pos, fy, inverse=True).numpy(), g["mlxnr_x3_inv"][0], **tol)
+    np.testing.assert_allclose(NR.rope_at(x4[0], pos, fy).numpy(), g["mlxnr_x4_fwd"][0], **tol)
+    rms = NR.rmsnorm(torch.from_numpy(g["mlxnr_nx"]), torch.from_numpy(g["mlxnr_nw"]))
+    np.testing.assert_allclose(rms.numpy(), g["mlxnr_rms"], rtol=1e-5, atol=1e-6)
