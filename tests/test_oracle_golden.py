@@ -231,3 +231,37 @@ def test_norm_rope_match_reference_mlx_twin():
     np.testing.assert_allclose(NR.rope_at(x4[0], pos, fy).numpy(), g["mlxnr_x4_fwd"][0], **tol)
     rms = NR.rmsnorm(torch.from_numpy(g["mlxnr_nx"]), torch.from_numpy(g["mlxnr_nw"]))
     np.testing.assert_allclose(rms.numpy(), g["mlxnr_rms"], rtol=1e-5, atol=1e-6)
+
+
+def test_decode_ring_matches_reference_code():
+    """The oracle's decode ring step against the reference's own inline ring code
+    (oracle/decode_engine.py:96-105, run from the file's syntax tree; tests/golden/make_ring_golden.py):
+    the ring after every step, the emitted rows before the fp8 simulation, and the simulation of the
+    reference's own rows equal to its final rows bit for bit (emission at (p+1) % 4 == 0, RoPE at p-3,
+    fp8 on the nope dims after the norm and RoPE)."""
+    import os
+
+    import torch
+
+    from oracle import compressor_ref as CR
+    from oracle import norm_rope_ref as NR
+    from oracle import quant_ref as Q
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ring_golden.npz"))
+    t = {k: torch.from_numpy(g[f"ring_{k}"]) for k in ("wkv", "wgate", "ape", "nw")}
+    rk, rs = torch.from_numpy(g["ring_kv0"]).clone(), torch.from_numpy(g["ring_sc0"]).clone()
+    f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
+    emitted = 0
+    for i, p in enumerate(g["ring_pos"]):
+        x = torch.from_numpy(g["ring_x"][i])
+        row = CR.decode_ring_step(rk, rs, x @ t["wkv"].T, x @ t["wgate"].T, t["ape"], t["nw"], int(p), f)
+        np.testing.assert_allclose(rk.numpy(), g["ring_kvs"][i], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(rs.numpy(), g["ring_scs"][i], rtol=1e-5, atol=1e-6)
+        raw = g["ring_raw_rows"][i]
+        if np.isnan(raw).all():
+            assert row is None, p
+            continue
+        emitted += 1
+        np.testing.assert_allclose(row.numpy(), raw, rtol=1e-4, atol=1e-5)
+        sim = Q.act_quant_rows(torch.from_numpy(raw), 64).numpy()
+        np.testing.assert_array_equal(sim.view(np.uint32), g["ring_q_rows"][i].view(np.uint32))
+    assert emitted == 2
