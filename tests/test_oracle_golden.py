@@ -265,3 +265,32 @@ def test_decode_ring_matches_reference_code():
         sim = Q.act_quant_rows(torch.from_numpy(raw), 64).numpy()
         np.testing.assert_array_equal(sim.view(np.uint32), g["ring_q_rows"][i].view(np.uint32))
     assert emitted == 2
+
+
+def test_decode_attention_matches_reference_code():
+    """The oracle's decode attention (window rows in ring order + every visible compressed row) and
+    its window-only attention against the reference's own inline decode attention
+    (oracle/v4_fast.py:108-119 run from the file's syntax tree with the MLX twins on numpy;
+    tests/golden/make_decode_attention_golden.py): a wrapped window with 75 visible rows, a partial
+    window, and a layer without compression."""
+    import os
+
+    import torch
+
+    from oracle import layer_ref as LR
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "decode_attention_golden.npz"))
+    f = LR.layer_freqs(4)
+    for tag in ("r4", "r4p", "w"):
+        winr, comp = torch.from_numpy(g[f"da_{tag}_winr"]), torch.from_numpy(g[f"da_{tag}_comp"])
+        q = torch.from_numpy(g[f"da_{tag}_qraw"])[None]
+        sink, pos = torch.from_numpy(g[f"da_{tag}_sinks"]), torch.tensor([int(g[f"da_{tag}_p"])])
+        pool, win_base = torch.cat([winr, comp]), torch.zeros(1, dtype=torch.int64)
+        if bool(g[f"da_{tag}_r4"]):
+            rng = np.random.default_rng(0)   # the indexer inputs do not matter: top_k covers every visible row
+            k_idx = torch.from_numpy(rng.standard_normal((1, comp.shape[0], 128)).astype(np.float32))
+            q_idx = torch.from_numpy(rng.standard_normal((1, 64, 128)).astype(np.float32))
+            w_idx = torch.from_numpy(rng.standard_normal((1, 64)).astype(np.float32))
+            o = LR.decode_attention_ref(pool, win_base, lambda b, j: 128 + j, k_idx, q, q_idx, w_idx, sink, pos, 512, f)
+        else:
+            o = LR.window_attention_ref(pool, win_base, q, sink, pos, f)
+        np.testing.assert_allclose(o[0].numpy(), g[f"da_{tag}_o"], rtol=1e-4, atol=2e-5, err_msg=tag)
