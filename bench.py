@@ -1,29 +1,43 @@
-"""Benchmark of the sparse-MLA decode path (BASELINE config 2 by default).
+"""Benchmark of the B200 sparse-MLA attention path.
 
-python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dsv4|reference] [--config c2|c3|c4|c5|c5w]
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dsv4|reference] [--config all|c2|c3|c4|c5|c5w]
 
-A step is one decode token of the measured path — per-head norm + RoPE of q, the window index list,
-the lightning-indexer scores + top-k over the compressed keys, sparse attention over the 640
-gathered rows with the inverse RoPE fused — for every sequence of the config's batch (config 2:
-batch 1 against a 32768-token context; config 3: batch 64 against 8192-token contexts).
+The default run (`--config all`) prints ONE JSON line: the headline, config 2 (decode of one token
+against a 32768-token context), with configs 3, 4 and 5 measured in the same process under
+`"configs"`, each entry carrying its own value, ms_per_step, roofline, clocks, e2e and CPU baseline:
 
-Timing: `value` replays the step's CUDA graph with inputs resident in HBM, rotating over R replicas
-of the whole state (R * footprint > 2 x L2, so no step finds its inputs in L2); K steps are
-bracketed by a barrier + synchronize and timed with CUDA events, max over ranks. `e2e` runs the
-same K steps through the public DecodeRunner.step_host: pinned host inputs copied in, the graph,
-the output copied out, every step. N > 1: each rank runs its own replica set (decode batches split
-across GPUs with no collective; weak scaling).
+  c2  one decode token (batch 1, 32K context): the per-head norm + RoPE of q, the lightning-indexer
+      scores + top-k 512 over 8192 compressed keys, sparse attention over the 128 window + 512
+      selected rows with the inverse RoPE fused. Does not shard: N GPUs run N replicas (weak).
+  c3  one decode token of each of 64 sequences (8K contexts): the same kernels, batched. The
+      batch is split across the N GPUs with no collective (strong scaling).
+  c4  prefill of 65,536 tokens: the KV and indexer-key compressors, the indexer top-k 1024
+      (causal), sparse attention over 128 + 1024 rows. Query-sharded across N GPUs with one NCCL
+      all-gather of the compressed rows and keys (strong).
+  c5  the full attention block decode of 32 sequences (16K contexts, int8-g64 weights): RMSNorm,
+      projections, RoPE, compressor ring, indexer, sparse MLA, grouped output projection. Batch
+      split across the N GPUs with no collective (strong).
+
+Timing: a step is one decode token (c2, c3, c5: one CUDA graph launch per step; a decode loop
+cannot batch successive tokens of a sequence into one launch) or one whole prefill (c4). Inputs
+resident in HBM, larger than L2 between uses (the decode steps rotate over replicas of the whole
+state). W untimed warm-up steps, then `repeats` regions of exactly K steps, each bracketed by a
+barrier + synchronize and timed with CUDA events on the launching stream, max over ranks; the
+reported ms_per_step is the median region / K. `e2e` is the same K steps through the public host
+API (pinned host inputs copied in, the step, the result copied out, every step). SM clocks and
+throttle reasons are sampled through NVML during the timed regions (reading only).
 """
 import argparse
+import ctypes
+import gc
 import json
-
-import numpy as np
 import os
 import statistics
 import sys
 import threading
 import time
 
+import numpy as np
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -43,7 +57,7 @@ CONFIGS = {
     "c3": dict(batch=64, ctx=8192, top_k=512, seeds=lambda r, i: 100 + i, strong=True,
                workload="config3: batched decode, global batch 64 split across GPUs, 8192-token contexts "
                         "(2048 compressed + 128 window rows each), top-k 512"),
-    "c4": dict(batch=1, ctx=65536, top_k=1024, seeds=lambda r, i: 2,
+    "c4": dict(batch=1, ctx=65536, top_k=1024, seeds=lambda r, i: 2, strong=True,
                workload="config4: long prefill, 65536 tokens: KV + indexer-key compressors (16384 rows), indexer "
                         "top-k 1024 causal, sparse attention over 128 window + 1024 rows; query-sharded with an NCCL "
                         "all-gather of compressed KV and keys"),
@@ -55,7 +69,18 @@ CONFIGS = {
                          "ratio-128 layers): global batch 32 split across GPUs, 16384-token contexts, 128-row "
                          "window rings, int8-g64 weights (bf16 scales)"),
 }
+ALL = ("c2", "c3", "c4", "c5")
+# steps of a sub-config region when the headline's K is larger (c4 steps are whole prefills)
+SUB_STEPS = {"c2": 200, "c3": 100, "c4": 5, "c5": 100, "c5w": 100}
+REPEATS = {"c2": 15, "c3": 9, "c4": 3, "c5": 9, "c5w": 9}
 L2_BYTES = 126 * 1024 * 1024
+L2_NOTE = {
+    "c2": "inputs > L2 between uses: steps rotate over replicas of the whole decode state (> 2x L2 in total)",
+    "c3": "inputs > L2 between uses: steps rotate over replicas of the whole decode state (> 2x L2 in total)",
+    "c4": "inputs (~7 GB) larger than L2",
+    "c5": "weights + caches read per step (~230 MB) larger than L2",
+    "c5w": "steps rotate over 3 replicas of weights + windows (> 2x L2 between uses)",
+}
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant op, from one
 # ncu capture each on B200: config 2 on this bench's own command (score + select kernels of one
@@ -70,13 +95,39 @@ def _pkg():
     return importlib.import_module(PKG)
 
 
+def _mod(name):
+    import importlib
+    return importlib.import_module(PKG + "." + name)
+
+
 def _peaks():
+    """(hbm GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, source)."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return (float(p["hbm_gbs"]), float(p["bf16_tflops"]),
+                float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured")
     except Exception:
-        return 6650.0, "fallback"
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def config_dict(name, world):
+    """The workload description shared by both arms (the reference arm prints the same dict)."""
+    c = CONFIGS[name]
+    if name == "c2":
+        par = f"replicas x{world} (batch 1 does not shard)" if world > 1 else "single GPU"
+        gb = world
+    elif name == "c4":
+        par = f"query-sharded x{world} (zig-zag) + NCCL all-gather of compressed KV and keys" if world > 1 \
+            else "single GPU"
+        gb = 1
+    else:
+        par = f"batch-split x{world} (no collective)" if world > 1 else "single GPU"
+        gb = c["batch"]
+    d = {"workload": c["workload"], "global_batch": gb, "ctx": c["ctx"], "parallelism": par, "l2": L2_NOTE[name]}
+    if c["top_k"]:
+        d["top_k"] = c["top_k"]
+    return d
 
 
 class ClockSampler:
@@ -87,7 +138,7 @@ class ClockSampler:
 
     def __init__(self, device_index):
         self.samples, self.reasons, self.ok = [], set(), False
-        self.window = None
+        self.windows = []
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -133,8 +184,11 @@ class ClockSampler:
             self._stop.set()
             self.t.join()
 
-    def summary(self, t0, t1):
-        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+    def summary(self, t0=None, t1=None, windows=None):
+        """Median SM clock and the union of throttle reasons over the samples inside the timed
+        windows ([(t0, t1)], or the single window t0..t1); all samples if none fell inside."""
+        windows = windows if windows is not None else [(t0, t1)]
+        inside = [s for s in self.samples if any(a <= s[0] <= b for a, b in windows)]
         use = inside or self.samples
         reasons = set()
         for _, _, r in use:
@@ -163,8 +217,127 @@ def _barrier_max(x, world, device):
     return t.item()
 
 
+def _barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+class Env:
+    """Per-process run context: ranks, device, step counts of the headline."""
+
+    def __init__(self, args, world, rank, local, dev):
+        self.args, self.world, self.rank, self.local, self.dev = args, world, rank, local, dev
+
+    def steps_for(self, name, headline):
+        a = self.args
+        if headline and a.steps_given:
+            return a.steps
+        if a.steps_given:
+            return min(a.steps, SUB_STEPS[name]) if name == "c4" else a.steps
+        return SUB_STEPS[name]
+
+    def warmup_for(self, name, headline):
+        a = self.args
+        w = a.warmup if a.warmup_given else (3 if name == "c4" else 20)
+        return max(3, w)
+
+    def repeats_for(self, name):
+        return self.args.repeats or REPEATS[name]
+
+
+def timed_regions(env, stream, run_k, k, repeats, sampler):
+    """`repeats` regions of exactly k steps each: barrier + synchronize, CUDA events on `stream`
+    around run_k(k), synchronize + barrier; per-region ms as the max over ranks. Returns
+    (list of ms, wall windows for the clock summary)."""
+    out, windows = [], []
+    for _ in range(repeats):
+        _barrier(env.world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record(stream)
+        run_k(k)
+        e1.record(stream)
+        sampler.sample_while(e1)
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        _barrier(env.world)
+        out.append(_barrier_max(e0.elapsed_time(e1), env.world, env.dev))
+        windows.append((t0, t1))
+    return out, windows
+
+
+def timing_summary(ms_list, k):
+    return {"repeats": len(ms_list), "steps_per_region": k,
+            "region_ms": [round(m, 4) for m in ms_list],
+            "ms_per_step_min": min(ms_list) / k, "ms_per_step_max": max(ms_list) / k}
+
+
+# ------------------------------------------------------------------------------ graph launch counts
+_cuda_drv = None
+
+
+def _drv():
+    global _cuda_drv
+    if _cuda_drv is None:
+        _cuda_drv = ctypes.CDLL("libcuda.so.1")
+    return _cuda_drv
+
+
+def graph_kernel_nodes(graph):
+    """(kernel nodes, of which this library's) in a captured torch CUDAGraph (keep_graph=True), read
+    through the driver API: cuGraphGetNodes / cuGraphNodeGetType and, for the names, the kernel
+    node's function (cuGraphKernelNodeGetParams, cuFuncGetName). Returns (None, None) when the
+    driver does not answer."""
+    try:
+        d = _drv()
+        g = ctypes.c_void_p(graph.raw_cuda_graph())
+        n = ctypes.c_size_t(0)
+        if d.cuGraphGetNodes(g, None, ctypes.byref(n)) != 0:
+            return None, None
+        nodes = (ctypes.c_void_p * n.value)()
+        if d.cuGraphGetNodes(g, nodes, ctypes.byref(n)) != 0:
+            return None, None
+        kernels, ours = 0, 0
+
+        class KParams(ctypes.Structure):  # CUDA_KERNEL_NODE_PARAMS_v2
+            _fields_ = [("func", ctypes.c_void_p), ("gx", ctypes.c_uint), ("gy", ctypes.c_uint),
+                        ("gz", ctypes.c_uint), ("bx", ctypes.c_uint), ("by", ctypes.c_uint), ("bz", ctypes.c_uint),
+                        ("smem", ctypes.c_uint), ("params", ctypes.c_void_p), ("extra", ctypes.c_void_p),
+                        ("kern", ctypes.c_void_p), ("ctx", ctypes.c_void_p)]
+        named = 0
+        for i in range(n.value):
+            t = ctypes.c_int(-1)
+            d.cuGraphNodeGetType(ctypes.c_void_p(nodes[i]), ctypes.byref(t))
+            if t.value != 0:   # CU_GRAPH_NODE_TYPE_KERNEL
+                continue
+            kernels += 1
+            kp = KParams()
+            name = ctypes.c_char_p()
+            try:
+                if d.cuGraphKernelNodeGetParams_v2(ctypes.c_void_p(nodes[i]), ctypes.byref(kp)) == 0 and kp.func and \
+                        d.cuFuncGetName(ctypes.byref(name), ctypes.c_void_p(kp.func)) == 0 and name.value:
+                    named += 1
+                    if name.value.startswith(b"_ZN4dsv4"):   # every kernel of libdsv4.so is in namespace dsv4
+                        ours += 1
+            except Exception:
+                pass
+        return kernels, (ours if named == kernels else None)
+    except Exception:
+        return None, None
+
+
+def _count_launches(graph, steps_per_graph=1):
+    k, ours = graph_kernel_nodes(graph)
+    if k is None:
+        return None
+    per = (ours if ours is not None else k) / steps_per_graph
+    return per
+
+
 # ------------------------------------------------------------------------------ CPU reference leg
 CPU_MIN_SECONDS = 10.0  # timed CPU work per reported number (a bounded sample of the workload)
+CPU_SUB_SECONDS = 5.0   # the same for the configs reported beside the headline
 
 
 def _cpu_threads(threads=None):
@@ -187,10 +360,10 @@ def cpu_workload(cfg_name, samples):
     if cfg_name == "c5w":
         return _cpu_block_window(samples)
     cfgd = CONFIGS[cfg_name]
-    C = __import__("importlib").import_module(PKG + ".configs")
+    C = _mod("configs")
     f = NR.precompute_freqs(64, 0, 65536, 160000.0, 16, 32, 1)
-    batch = min(cfgd["batch"], samples)
-    case = C.make_decode_case(batch, cfgd["ctx"], cfgd["top_k"], seeds=[cfgd["seeds"](0, i) for i in range(batch)],
+    batch = samples
+    case = C.make_decode_case(batch, cfgd["ctx"], cfgd["top_k"], seeds=[cfgd["seeds"](i, i) for i in range(batch)],
                               device="cpu", shuffle_pages=True)
     pool, win_base, comp_rows = C.decode_case_host_pool(case)
     h = case.host
@@ -203,11 +376,12 @@ def cpu_workload(cfg_name, samples):
     return run, f"{batch} decode token(s) of {cfg_name} per repetition through the CPU oracle"
 
 
-def cpu_sample_size(cfg_name):
-    """Tokens per repetition of the CPU sample: the block configs run their batch of 32 per call (the
-    weights are read once per call, as a CPU implementation would), config 4 runs 64 queries, the
-    attention-only decode configs one sequence (their oracle loops over sequences anyway)."""
-    return {"c4": 64, "c5": 32, "c5w": 32}.get(cfg_name, 1)
+def cpu_sample_size(cfg_name, world=1):
+    """Tokens per repetition of the CPU sample: config 2 runs the arm's global batch (one sequence
+    per GPU replica), the block configs their batch of 32 per call (the weights are read once per
+    call, as a CPU implementation would), config 4 runs 64 queries, config 3 two sequences (the
+    oracle loops over sequences, so tok/s does not depend on the sample's batch)."""
+    return {"c2": world, "c3": 2, "c4": 64, "c5": 32, "c5w": 32}[cfg_name]
 
 
 def _dequantized(W):
@@ -239,16 +413,23 @@ def cpu_reference(cfg_name, samples, threads=None, min_seconds=CPU_MIN_SECONDS):
     return v, threads, f"{desc}; {reps} repetitions, {sec:.1f} s of timed CPU work, {threads} threads"
 
 
+def _cpu_baseline(env, name, headline):
+    if env.rank != 0 or env.world != 1 or env.args.no_cpu_baseline:
+        return None
+    v, cores, desc = cpu_reference(name, cpu_sample_size(name), min_seconds=CPU_MIN_SECONDS if headline
+                                   else CPU_SUB_SECONDS)
+    return {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
+
+
 def _cpu_prefill(nq):
     """Config 4 per-token CPU cost: the two compressors over a 4096-token slice (per token), plus
     the indexer over 16384 keys and attention over 1152 rows for nq queries in the middle of the
     65536-token sequence (per query)."""
-    import importlib
     from oracle import compressor_ref as CR
     from oracle import indexer_ref as I
     from oracle import norm_rope_ref as NR
     from oracle import sparse_attn_ref as SA
-    Lm = importlib.import_module(PKG + ".layer")
+    Lm = _mod("layer")
     W = Lm.make_attention_weights(2)
     g = torch.Generator().manual_seed(2)
     xs = torch.randn(4096, 4096, generator=g)
@@ -282,10 +463,8 @@ def _cpu_prefill(nq):
 
 def _cpu_block_window(nseq):
     """Window-only (ratio-128) block per-token CPU cost: the oracle decode block without compression."""
-    import importlib
     from oracle import layer_ref as LR
-    Lm = importlib.import_module(PKG + ".layer")
-    C = importlib.import_module(PKG + ".configs")
+    Lm, C = _mod("layer"), _mod("configs")
     W = _dequantized(Lm.make_attention_weights(3, dims=C.LayerDims(ratio=128), quant=True))
     g = torch.Generator().manual_seed(3)
     state = dict(pool=torch.randn(nseq * 128, 512, generator=g).to(torch.bfloat16).float(),
@@ -303,10 +482,8 @@ def _cpu_block_window(nseq):
 def _cpu_block(nseq):
     """Config 5 per-token CPU cost: the oracle decode block (dequantised int8 weights in fp32). Each
     repetition steps the same token again (same work; the state it writes is overwritten)."""
-    import importlib
     from oracle import layer_ref as LR
-    Lm = importlib.import_module(PKG + ".layer")
-    C = importlib.import_module(PKG + ".configs")
+    Lm, C = _mod("layer"), _mod("configs")
     W = _dequantized(Lm.make_attention_weights(3, quant=True))
     case = C.make_decode_case(nseq, 16384, 512, seeds=[3 + i for i in range(nseq)], device="cpu")
     pool, win_base, comp_rows = C.decode_case_host_pool(case)
@@ -324,146 +501,106 @@ def _cpu_block(nseq):
     return run, f"{nseq} token(s) of the config-5 block per repetition through the CPU oracle"
 
 
-def run_reference(args):
-    """The reference arm: the reference's own CPU implementation of the path (its ref_torch code as
-    restated in oracle/, since the reference cannot be installed as a package) on all host cores,
-    on this config's workload. Rank 0 alone runs it; each step is a bounded sample of at least
-    CPU_MIN_SECONDS of timed work."""
-    world, rank, _ = _dist()
-    if rank != 0:
-        return
-    cfgd = CONFIGS[args.config]
+def _tokens_per_step(name, world):
+    c = CONFIGS[name]
+    if name == "c2":
+        return world
+    if name == "c4":
+        return c["ctx"]
+    return c["batch"]
+
+
+def reference_line(name, steps, warmup, world, per_step_seconds):
+    """One config through the reference's CPU path (its ref_torch code as restated in oracle/) on all
+    host cores: `warmup` untimed repetitions, then `steps` timed steps, each a bounded sample of at
+    least per_step_seconds of CPU work."""
     threads = _cpu_threads()
-    run, desc = cpu_workload(args.config, cpu_sample_size(args.config))
-    warm = max(1, min(args.warmup, 3))
-    for _ in range(warm):
+    run, desc = cpu_workload(name, cpu_sample_size(name, world))
+    for _ in range(max(1, warmup)):
         run()
     per_step, reps_total, sec_total = [], 0, 0.0
-    for _ in range(min(args.steps, 3)):
-        v, reps, sec = timed_rate(run)
+    for _ in range(steps):
+        v, reps, sec = timed_rate(run, per_step_seconds)
         per_step.append(v)
         reps_total, sec_total = reps_total + reps, sec_total + sec
     v = statistics.median(per_step)
-    desc = f"{desc}; {reps_total} repetitions over {len(per_step)} steps, {sec_total:.1f} s of timed CPU work"
-    line = {"impl": "reference", "metric": METRICS[args.config],
-            "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": len(per_step), "warmup": warm,
-            "ms_per_step": 1000.0 * (cfgd["ctx"] if args.config == "c4" else cfgd["batch"]) / v,
-            "higher_is_better": True, "scaling": "strong" if cfgd.get("strong") or args.config == "c4" else "weak",
+    desc = f"{desc}; {reps_total} repetitions over {steps} steps, {sec_total:.1f} s of timed CPU work"
+    return {"impl": "reference", "metric": METRICS[name],
+            "value": v, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": max(1, warmup),
+            "ms_per_step": 1000.0 * _tokens_per_step(name, world) / v,
+            "higher_is_better": True, "scaling": "weak" if name == "c2" else "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": cfgd["workload"], "global_batch": cfgd["batch"], "ctx": cfgd["ctx"],
-                       "parallelism": "cpu"},
+            "config": config_dict(name, world),
+            "execution": f"CPU, {threads} host threads (rank 0 of {world})",
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
                              "sample": desc + "; the reference's ref_torch path restated in oracle/"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
 
 
-# ------------------------------------------------------------------------------ GPU leg
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=None)
-    ap.add_argument("--warmup", type=int, default=None)
-    ap.add_argument("--impl", default="dsv4", choices=["dsv4", "reference"])
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
-    ap.add_argument("--replicas", type=int, default=0)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", default=None,
-                    choices=["attn_prefill", "indexer_prefill", "block_decode", "block_decode_window", "hc"],
-                    help="profiling aid: run one prefill kernel alone on a 4096-query slice of config 4 "
-                         "(positions 60000..64095), or config 5's block step eagerly inside an NVTX range "
-                         "(block_decode; block_decode_window: the same block at a ratio-128 layer), and print its "
-                         "CUDA-event time; not a bench line")
-    args = ap.parse_args()
-    if args.kernel_case:
-        return run_kernel_case(args)
-    args.steps_given, args.warmup_given = args.steps is not None, args.warmup is not None
-    if args.steps is None:
-        args.steps = 2400
-    if args.warmup is None:
-        args.warmup = 240
-    if args.impl == "reference":
-        return run_reference(args)
+def run_reference(args):
+    """The reference arm: the reference's own CPU implementation of the path (its ref_torch code as
+    restated in oracle/, since the reference cannot be installed as a package) on all host cores,
+    on the same configs (same `config` dicts) as the GPU arm at this N. Rank 0 alone runs it. The
+    headline runs K timed steps, each a bounded sample sized so the whole run stays within a few
+    minutes; the other configs get one bounded sample each under "configs"."""
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    names = ALL if args.config == "all" else (args.config,)
+    per_step = min(CPU_MIN_SECONDS, max(0.5, 90.0 / args.steps))
+    head = reference_line(names[0], args.steps, min(args.warmup, 3), world, per_step)
+    if len(names) > 1:
+        head["configs"] = {n: reference_line(n, 1, 1, world, CPU_SUB_SECONDS) for n in names[1:]}
+    print(json.dumps(head), flush=True)
 
-    world, rank, local = _dist()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    dsv4 = _pkg()
-    C = __import__("importlib").import_module(PKG + ".configs")
-    cfgd = CONFIGS[args.config]
-    if args.config == "c4":
-        return bench_prefill(args, world, rank, local, dev)
-    if args.config == "c5":
-        return bench_block(args, world, rank, local, dev)
-    if args.config == "c5w":
-        return bench_block_window(args, world, rank, local, dev)
+
+# ------------------------------------------------------------------------------ configs 2 and 3 (decode attention)
+def bench_decode(env, name, headline):
+    """Configs 2 and 3: a step is one decode token of every sequence of this rank's batch, one CUDA
+    graph launch (q's norm + RoPE, indexer scores + top-k, sparse attention + inverse RoPE)."""
+    dsv4, C = _pkg(), _mod("configs")
+    cfgd = CONFIGS[name]
+    world, rank, dev = env.world, env.rank, env.dev
+    K, W, reps = env.steps_for(name, headline), env.warmup_for(name, headline), env.repeats_for(name)
     batch, ctx, top_k = cfgd["batch"], cfgd["ctx"], cfgd["top_k"]
     if cfgd.get("strong"):
         batch = max(1, batch // world)
-
-    # ---- replicas of the whole decode state, rotating so that no step starts with warm L2
     seed_of = (lambda i: cfgd["seeds"](rank, rank * batch + i)) if cfgd.get("strong") else (lambda i: cfgd["seeds"](rank, i))
     probe = C.make_decode_case(batch, ctx, top_k, seeds=[seed_of(i) for i in range(batch)], device=dev)
     c = probe.cache
-    footprint = (c.kv_pool.numel() * 2 + c.k_idx.numel() * 4 + c.block_table.numel() * 4)
-    R = args.replicas or max(2, -(-2 * L2_BYTES // footprint) + 1)
+    footprint = (c.kv_pool.numel() * 2 + c.k_idx.numel() * 4 + c.block_table.numel() * 4 +
+                 sum(t.numel() * t.element_size() for t in c.key_image))
+    R = env.args.replicas or max(2, -(-2 * L2_BYTES // footprint) + 1)
     cases = [probe] + [C.make_decode_case(batch, ctx, top_k, seeds=[seed_of(i) + 104729 * r for i in range(batch)],
                                           device=dev)
                        for r in range(1, R)]
     runners = []
+    stream = torch.cuda.Stream(dev)
     for cs in cases:
-        r = dsv4.DecodeRunner(cs.cache, cs.sink, top_k, device=dev)
+        r = dsv4.DecodeRunner(cs.cache, cs.sink, top_k, device=dev, q_dtype=torch.bfloat16, stream=stream,
+                              keep_graph=True)
         r.q.copy_(cs.q), r.q_idx.copy_(cs.q_idx), r.w_idx.copy_(cs.w_idx), r.positions.copy_(cs.positions)
         r.capture()
         runners.append(r)
-    stream = runners[0].stream
-    for r in runners[1:]:
-        r.stream = stream
     torch.cuda.synchronize()
+    cursor = [0]
 
-    # ---- one graph holding R steps (one per replica): a replay = R decode tokens
-    big = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(big, stream=stream):
-        for r in runners:
-            r._body()
-    torch.cuda.synchronize()
-
-    def run_steps(k):
-        full, rest = divmod(k, R)
+    def run_k(k):  # one graph launch per decode step, rotating over the replicas
         with torch.cuda.stream(stream):
-            for _ in range(full):
-                big.replay()
-            for i in range(rest):
-                runners[i].graph.replay()
+            for _ in range(k):
+                runners[cursor[0] % R].graph.replay()
+                cursor[0] += 1
 
-    run_steps(max(args.warmup, 3))
+    run_k(W)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(env.local)
     sampler.start()
     time.sleep(0.05)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.perf_counter()
-    e0.record(stream)
-    run_steps(args.steps)
-    e1.record(stream)
-    sampler.sample_while(e1)
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
-    if world > 1:
-        torch.distributed.barrier()
-    ms = e0.elapsed_time(e1)
-    ms = _barrier_max(ms, world, dev)
+    ms_list, windows = timed_regions(env, stream, run_k, K, reps, sampler)
     sampler.stop()
-    clocks = sampler.summary(t0, t1)
-    ms_per_step = ms / args.steps
-    value = world * batch * args.steps / (ms / 1000.0)
+    clocks = sampler.summary(windows=windows)
+    ms_per_step = statistics.median(ms_list) / K
+    value = world * batch / (ms_per_step / 1000.0)
 
     # ---- e2e through the public host API: each step copies the token's inputs from pinned host
     # memory (the runner's host_inputs(), written once per replica here as a serving loop writes
@@ -473,73 +610,113 @@ def main():
         for dst, key in zip(r.host_inputs(), ("q", "q_idx", "w_idx", "positions")):
             dst.copy_(cs.host[key])
         hin.append(r.host_inputs())
-    for i in range(min(R, 4)):
-        runners[i].step_host(*hin[i])
+    ecur = [0]
+
+    def run_host(k):
+        for _ in range(k):
+            i = ecur[0] % R
+            runners[i].step_host(*hin[i])
+            ecur[0] += 1
+
+    run_host(min(R, 4))
     torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for s in range(args.steps):
-        i = s % R
-        runners[i].step_host(*hin[i])
-    f1.record(stream)
-    torch.cuda.synchronize()
-    ems = _barrier_max(f0.elapsed_time(f1), world, dev)
-    e2e = {"value": world * batch * args.steps / (ems / 1000.0), "unit": "tok/s",
+    ems_list, _ = timed_regions(env, stream, run_host, K, reps, _NoSampler())
+    ems = statistics.median(ems_list) / K
+    e2e = {"value": world * batch / (ems / 1000.0), "unit": "tok/s", "ms_per_step": ems,
            "h2d_bytes_per_step": runners[0].h2d_bytes(), "d2h_bytes_per_step": runners[0].d2h_bytes(),
-           "path": "DecodeRunner.step_host (pinned host in/out, copies and kernels in one CUDA graph)"}
+           "path": "DecodeRunner.step_host (pinned host in/out, copies and kernels in one CUDA graph; q in bf16)"}
 
     # ---- dominant-kernel timing: each kernel of the step, alone, over the replica rotation
-    kern = kernel_times(dsv4, cases, runners, stream, dev, min(args.steps, 4 * R))
-    peak, peak_kind = _peaks()
+    kern = kernel_times(cases, runners, stream, min(max(K, 20), 4 * R))
+    hbm, _, _, peak_kind = _peaks()
     top = max(kern, key=lambda k: kern[k]["us"])
     kb = kern[top]
     achieved = kb["bytes"] / (kb["us"] * 1e-6) / 1e9
-    roofline = {"bound": "hbm", "kernel": top, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+    roofline = {"bound": "hbm", "kernel": top, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_source": peak_kind,
+                "traffic": TRAFFIC.get(name, {}).get(top),
                 "per_kernel_us": {k: round(v["us"], 3) for k, v in kern.items()},
                 "algorithmic_bytes_per_launch": kb["bytes"]}
-    roofline["traffic"] = TRAFFIC.get(args.config, {}).get(top)
+    launches = _count_launches(runners[0].graph)
+    line = {"metric": METRICS[name], "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if cfgd.get("strong") else "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": config_dict(name, world),
+            "timing": dict(timing_summary(ms_list, K), replicas=R, replica_mib=round(footprint / 2**20, 1),
+                           graph="one CUDA graph launch per decode step"),
+            "gpu_launches": None if launches is None else int(round(launches * K)),
+            "gpu_launches_per_step": launches,
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": _cpu_baseline(env, name, headline), "clocks": clocks}
+    for r in runners:
+        r.release()
+    return line
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, desc = cpu_reference(args.config, 1 if args.config == "c2" else 2)
-        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
 
-    if rank == 0:
-        line = {"metric": METRICS[args.config],
-                "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": ms_per_step, "higher_is_better": True,
-                "scaling": "strong" if cfgd.get("strong") else "weak", "vs_baseline": None,
-                "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": cfgd["workload"], "global_batch": batch * world, "ctx": ctx, "top_k": top_k,
-                           "parallelism": f"batch-split x{world} (no collective)" if world > 1 else "single GPU",
-                           "l2": f"inputs rotate over {R} replicas x {footprint / 2**20:.1f} MiB = "
-                                 f"{R * footprint / 2**20:.0f} MiB > L2 (126 MB)",
-                           "cuda_graph": True},
-                "gpu_launches": decode_launches_per_step(runners[0]) * args.steps,
-                "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
+class _NoSampler:
+    def sample_while(self, event, period=0.001):
+        return
+
+
+def kernel_times(cases, runners, stream, n):
+    """Average duration of each op of the step, launched alone n times over the replica rotation
+    inside a CUDA graph and timed with CUDA events on the launching stream."""
+    SA, IX, NRm = _mod("sparse_attn"), _mod("indexer"), _mod("norm_rope")
+    R = len(cases)
+    b = cases[0].cache.batch
+    top_k = runners[0].top_k
+    freqs = runners[0].freqs
+    qn = [NRm.norm_rope(r.q, r.positions, freqs) for r in runners]
+    torch.cuda.synchronize()
+    nvis = [min((int(c.host["positions"][i]) + 1) // 4, c.cache.max_comp) for c in cases[:1] for i in range(b)]
+    n_keys = sum(nvis)
+    funcs = {
+        # score + select (which also writes the window rows): k_idx read once, indices written
+        "indexer_topk": (lambda i: IX.indexer_topk_into(runners[i].idx.view(b, 1, -1), runners[i].q_idx.view(b, 1, 64, 128),
+                                                        runners[i].w_idx.view(b, 1, 64), cases[i].cache.k_idx, top_k,
+                                                        runners[i].positions.view(b, 1), 4, out_col=0,
+                                                        out_offset=cases[i].cache.comp_base,
+                                                        block_table=cases[i].cache.block_table, page=cases[i].cache.page,
+                                                        key_image=cases[i].cache.key_image),
+                         n_keys * 128 * 4 + b * (64 * 128 * 4 + 64 * 4 + top_k * 4)),
+        # attention (+ split merge): gathered rows, normed q in, o out, indices
+        "sparse_attn": (lambda i: SA.sparse_attn_rope(qn[i], cases[i].cache.kv_pool, cases[i].sink, runners[i].idx,
+                                                      512 ** -0.5, runners[i].positions, freqs, 64,
+                                                      win_base=cases[i].cache.win_base, window=128),
+                        b * ((128 + top_k) * 512 * 2 + top_k * 4 + 64 * 512 * 2 * 2)),
+    }
+    out = {}
+    for name, (fn, nbytes) in funcs.items():
+        with torch.cuda.stream(stream):
+            fn(0)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(R):
+                fn(i)
+        reps = max(1, n // R)
+        with torch.cuda.stream(stream):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        out[name] = {"us": e0.elapsed_time(e1) * 1000.0 / (reps * R), "bytes": nbytes}
+        del g
+    return out
 
 
 # ------------------------------------------------------------------------------ config 4 (long prefill)
-def _phase_events(n):
-    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
-
-
-def bench_prefill(args, world, rank, local, dev):
+def bench_prefill(env, name, headline):
     """Config 4: one step = the sparse-MLA prefill core over 65536 tokens (strong scaling: the
-    same sequence split over the ranks; the compressed cache is all-gathered)."""
-    import importlib
-    P = importlib.import_module(PKG + ".prefill")
-    Lm = importlib.import_module(PKG + ".layer")
+    same sequence split over the ranks by query; the compressed cache is all-gathered)."""
+    P, Lm = _mod("prefill"), _mod("layer")
     cfgd = CONFIGS["c4"]
+    world, rank, dev = env.world, env.rank, env.dev
     s, top_k = cfgd["ctx"], cfgd["top_k"]
-    steps = args.steps if args.steps_given else 5
-    warmup = max(3, args.warmup if args.warmup_given else 3)
+    K, Wm, reps = env.steps_for("c4", headline), env.warmup_for("c4", headline), env.repeats_for("c4")
     W = Lm.make_attention_weights(2).to(dev)
     cw = P.CompressorWeights.from_attention_weights(W)
     g = torch.Generator(device=dev).manual_seed(2)
@@ -551,10 +728,10 @@ def bench_prefill(args, world, rank, local, dev):
     sharded = P.ShardedPrefill() if world > 1 else None
     ranges = P.zigzag_ranges(s, world, rank) if world > 1 else [(0, s)]
     g0, g1 = P.block_range(s // 4, world, rank)
-    phases = {"compress": 0.0, "gather": 0.0, "indexer+attention": 0.0}
+    stream = torch.cuda.current_stream(dev)
 
     def step(record=False):
-        ev = _phase_events(4) if record else None
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
         if ev:
             ev[0].record()
         comp_l, keys_l = P.compress_range(x, cw, g0, g1)
@@ -572,43 +749,36 @@ def bench_prefill(args, world, rank, local, dev):
             ev[3].record()
         return outs, ev
 
-    for _ in range(warmup):
-        step()
+    def run_k(k):
+        for _ in range(k):
+            step()
+
+    run_k(Wm)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(env.local)
     sampler.start()
     time.sleep(0.05)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.perf_counter()
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
-    sampler.sample_while(e1)
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
-    if world > 1:
-        torch.distributed.barrier()
-    ms = _barrier_max(e0.elapsed_time(e1), world, dev) / steps
+    ms_list, windows = timed_regions(env, stream, run_k, K, reps, sampler)
     sampler.stop()
-    clocks = sampler.summary(t0, t1)
+    clocks = sampler.summary(windows=windows)
+    ms = statistics.median(ms_list) / K
+    _barrier(world)
     _, ev = step(record=True)
     torch.cuda.synchronize()
     phases = {"compress": ev[0].elapsed_time(ev[1]), "gather": ev[1].elapsed_time(ev[2]),
               "indexer+attention": ev[2].elapsed_time(ev[3])}
+    phases = {k: _barrier_max(v, world, dev) for k, v in phases.items()}
     # attention-only timing on this rank's queries for the tensor roofline (indices precomputed)
     att_ms, att_flops = _prefill_attention_time(P, x, q, qi, wi, kv, W, cw, ranges, s, top_k, dev)
-    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
-        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {"bf16_tflops": 1590.0}
+    att_ms = _barrier_max(att_ms, world, dev)
+    _, burst, sustained, src = _peaks()
     achieved = att_flops / (att_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "kernel": "tc::attn_tc_kernel", "achieved": achieved,
-                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                "peak_source": "measured" if "when" in peaks else "fallback",
+                "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
+                "peak_source": f"{src} (bf16 sustained: the kernel runs for ~{att_ms:.0f} ms back to back)",
+                "frac_of_burst": achieved / burst,
                 "traffic": TRAFFIC["c4"]["tc::attn_tc_kernel"] // world,  # this rank's queries
-                "algorithmic_flops_per_launch": att_flops, "phases_ms": phases}
+                "algorithmic_flops_per_launch": att_flops, "attention_ms": att_ms, "phases_ms": phases}
     # e2e: this rank's inputs from pinned host memory, the step, its outputs back
     hx = x.cpu().pin_memory()
     hq = [q[a:b].cpu().pin_memory() for a, b in ranges]
@@ -616,56 +786,42 @@ def bench_prefill(args, world, rank, local, dev):
     hw = [wi[a:b].cpu().pin_memory() for a, b in ranges]
     hkv = kv.cpu().pin_memory()
     ho = [torch.empty((b - a, 64, 512), dtype=torch.bfloat16).pin_memory() for a, b in ranges]
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    h2d = d2h = 0
-    for _ in range(steps):
-        x.copy_(hx, non_blocking=True)
-        kv.copy_(hkv, non_blocking=True)
-        h2d = hx.numel() * 2 + hkv.numel() * 2
-        for i, (a, b) in enumerate(ranges):
-            q[a:b].copy_(hq[i], non_blocking=True)
-            qi[a:b].copy_(hqi[i], non_blocking=True)
-            wi[a:b].copy_(hw[i], non_blocking=True)
-            h2d += hq[i].numel() * 2 + hqi[i].numel() * 4 + hw[i].numel() * 4
-        outs, _ = step()
-        d2h = 0
-        for i, o in enumerate(outs):
-            ho[i].copy_(o, non_blocking=True)
-            d2h += o.numel() * 2
-    f1.record()
-    torch.cuda.synchronize()
-    ems = _barrier_max(f0.elapsed_time(f1), world, dev) / steps
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, desc = cpu_reference("c4", cpu_sample_size("c4"))
-        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
-    if rank == 0:
-        line = {"metric": METRICS["c4"], "value": s / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
-                "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": cfgd["workload"], "global_batch": 1, "seq_len": s, "top_k": top_k,
-                           "parallelism": f"query-sharded x{world} (zig-zag) + NCCL all-gather" if world > 1
-                           else "single GPU", "l2": "inputs (~7 GB) larger than L2"},
-                "gpu_launches": None,
-                "e2e": {"value": s / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h, "path": "host inputs -> prefill core -> host outputs"},
-                "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    io = {"h2d": 0, "d2h": 0}
+
+    def run_host(k):
+        for _ in range(k):
+            x.copy_(hx, non_blocking=True)
+            kv.copy_(hkv, non_blocking=True)
+            h2d = hx.numel() * 2 + hkv.numel() * 2
+            for i, (a, b) in enumerate(ranges):
+                q[a:b].copy_(hq[i], non_blocking=True)
+                qi[a:b].copy_(hqi[i], non_blocking=True)
+                wi[a:b].copy_(hw[i], non_blocking=True)
+                h2d += hq[i].numel() * 2 + hqi[i].numel() * 4 + hw[i].numel() * 4
+            outs, _ = step()
+            d2h = 0
+            for i, o in enumerate(outs):
+                ho[i].copy_(o, non_blocking=True)
+                d2h += o.numel() * 2
+            io["h2d"], io["d2h"] = h2d, d2h
+
+    ems_list, _ = timed_regions(env, stream, run_host, K, 1, _NoSampler())
+    ems = ems_list[0] / K
+    line = {"metric": METRICS["c4"], "value": s / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+            "steps": K, "warmup": Wm, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config_dict("c4", world),
+            "timing": dict(timing_summary(ms_list, K), graph="eager launches (chunks of 8192 queries)"),
+            "gpu_launches": None,
+            "e2e": {"value": s / (ems / 1000.0), "unit": "tok/s", "ms_per_step": ems, "h2d_bytes_per_step": io["h2d"],
+                    "d2h_bytes_per_step": io["d2h"], "path": "host inputs -> prefill core -> host outputs"},
+            "roofline": roofline, "cpu_baseline": _cpu_baseline(env, "c4", headline), "clocks": clocks}
+    return line
 
 
 def _prefill_attention_time(P, x, q, qi, wi, kv, W, cw, ranges, s, top_k, dev):
     """CUDA-event time of the sparse attention kernels alone over this rank's queries (index lists
     built beforehand). FLOPs = sum over queries of 64 heads x valid rows x 512 x 4 (QK^T and PV)."""
-    import importlib
-    IX = importlib.import_module(PKG + ".indexer")
-    SA = importlib.import_module(PKG + ".sparse_attn")
-    NRm = importlib.import_module(PKG + ".norm_rope")
+    IX, SA, NRm = _mod("indexer"), _mod("sparse_attn"), _mod("norm_rope")
     comp, keys = P.compress_range(x, cw, 0, s // 4)
     kvcat = torch.cat([kv, comp])
     freqs = NRm.rope_freqs(64, dev)
@@ -697,288 +853,172 @@ def _prefill_attention_time(P, x, q, qi, wi, kv, W, cw, ranges, s, top_k, dev):
 
 
 # ------------------------------------------------------------------------------ config 5 (decode block)
-def bench_block(args, world, rank, local, dev):
-    """Config 5: one step = the whole attention block for one token of each sequence (global batch
-    32 split over the ranks), int8-g64 weights, captured in a CUDA graph."""
-    import importlib
-    Lm = importlib.import_module(PKG + ".layer")
-    C = importlib.import_module(PKG + ".configs")
-    M = importlib.import_module(PKG + ".mla")
-    cfgd = CONFIGS["c5"]
-    B, ctx, top_k = max(1, cfgd["batch"] // world), cfgd["ctx"], cfgd["top_k"]
-    steps = args.steps if args.steps_given else 200
-    warmup = max(3, args.warmup if args.warmup_given else 20)
-    W = Lm.make_attention_weights(3, quant=True).to(dev)
-    case = C.make_decode_case(B, ctx, top_k, seeds=[cfgd["seeds"](rank, rank * B + i) for i in range(B)], device=dev)
-    blk = Lm.DecodeBlock(W, B, ctx, top_k=top_k, cache=case.cache)
-    g = torch.Generator().manual_seed(3 + rank)
-    x = torch.randn(B, 4096, generator=g).to(dev)
-    pos = torch.full((B,), ctx - 1, dtype=torch.int32, device=dev)
-    stream = torch.cuda.Stream(dev)
-    with torch.cuda.stream(stream):
-        blk.step(x, pos)
-    stream.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        out = blk.step(x, pos)
-    with torch.cuda.stream(stream):
-        for _ in range(warmup):
-            graph.replay()
-    torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.05)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.perf_counter()
-    e0.record(stream)
-    with torch.cuda.stream(stream):
-        for _ in range(steps):
-            graph.replay()
-    e1.record(stream)
-    sampler.sample_while(e1)
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
-    if world > 1:
-        torch.distributed.barrier()
-    ms = _barrier_max(e0.elapsed_time(e1), world, dev) / steps
-    sampler.stop()
-    clocks = sampler.summary(t0, t1)
-    # e2e: this token's hidden states from pinned host memory, the graph, the block output back
-    hx = x.cpu().pin_memory()
-    ho = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    with torch.cuda.stream(stream):
-        for _ in range(steps):
-            x.copy_(hx, non_blocking=True)
-            graph.replay()
-            ho.copy_(out, non_blocking=True)
-    f1.record(stream)
-    torch.cuda.synchronize()
-    ems = _barrier_max(f0.elapsed_time(f1), world, dev) / steps
-    # algorithmic HBM bytes of one step: every weight once, the visible indexer keys, the gathered rows
+def _step_bytes_block(W, B, ctx, top_k, max_comp, names):
+    M = _mod("mla")
     wbytes = 0
-    for name in Lm.MATRICES:
-        w = getattr(W, name)
+    for n in names:
+        w = getattr(W, n)
         wbytes += (w.q.numel() + w.scale.numel() * 2) if isinstance(w, M.QuantWeight) else w.numel() * w.element_size()
-    nvis = min(ctx // 4, case.cache.max_comp)
-    step_bytes = wbytes + B * (nvis * 128 * 4 + (128 + top_k) * 1024)
-    peak, peak_kind = _peaks()
-    achieved = step_bytes / (ms * 1e-3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "whole block step", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
-                "algorithmic_bytes_per_launch": step_bytes}
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, desc = cpu_reference("c5", cpu_sample_size("c5"))
-        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
-    if rank == 0:
-        line = {"metric": METRICS["c5"], "value": cfgd["batch"] / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
-                "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": cfgd["workload"], "global_batch": cfgd["batch"], "ctx": ctx, "top_k": top_k,
-                           "parallelism": f"batch-split x{world} (no collective)" if world > 1 else "single GPU",
-                           "l2": f"weights + caches {step_bytes / 2**20:.0f} MiB per step > L2", "cuda_graph": True},
-                "gpu_launches": None,
-                "e2e": {"value": cfgd["batch"] / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": hx.numel() * 4,
-                        "d2h_bytes_per_step": ho.numel() * 4, "path": "host hidden states -> block graph -> host"},
-                "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    nvis = min(ctx // 4, max_comp)
+    return wbytes + B * (nvis * 128 * 4 + (128 + top_k) * 1024) if top_k else wbytes + B * 128 * 1024
 
 
-def bench_block_window(args, world, rank, local, dev):
-    """The config-5 block at a window-only (ratio-128) layer: one step = projections, this token's kv
-    row into its window ring, attention over the 128-row window, grouped output projection, for one
-    token of each sequence (global batch 32 split over the ranks), int8-g64 weights, one CUDA graph
-    per replica. A replica's weights and rings (~114 MB) fit in L2, so the steps rotate over three
-    replicas: a step's inputs were last touched two steps (~228 MB of other data) earlier."""
-    import importlib
-    Lm = importlib.import_module(PKG + ".layer")
-    C = importlib.import_module(PKG + ".configs")
-    M = importlib.import_module(PKG + ".mla")
-    cfgd = CONFIGS["c5w"]
-    dims = C.LayerDims(ratio=128)
-    B, ctx = max(1, cfgd["batch"] // world), cfgd["ctx"]
-    steps = args.steps if args.steps_given else 300
-    warmup = max(3, args.warmup if args.warmup_given else 30)
-    R = 3
+def bench_block(env, name, headline):
+    """Config 5 (and 5w): one step = the whole attention block for one token of each sequence
+    (global batch 32 split over the ranks), int8-g64 weights, one CUDA graph per step. Config 5w is
+    the block of a ratio-128 (window-only) layer."""
+    Lm, C = _mod("layer"), _mod("configs")
+    cfgd = CONFIGS[name]
+    world, rank, dev = env.world, env.rank, env.dev
+    K, Wm, reps = env.steps_for(name, headline), env.warmup_for(name, headline), env.repeats_for(name)
+    B, ctx, top_k = max(1, cfgd["batch"] // world), cfgd["ctx"], cfgd["top_k"]
+    window_only = name == "c5w"
     stream = torch.cuda.Stream(dev)
+    R = 3 if window_only else 1   # a window-only replica fits in L2: rotate three
     blocks, graphs, xs, outs, Ws = [], [], [], [], []
     for r in range(R):
-        W = Lm.make_attention_weights(3 + 7 * r, dims=dims, quant=True).to(dev)
-        blk = Lm.DecodeBlock(W, B, ctx, dims=dims, device=dev)
-        g = torch.Generator().manual_seed(cfgd["seeds"](rank, rank * B) + 104729 * r)
-        blk.cache.kv_pool.copy_(torch.randn(blk.cache.kv_pool.shape, generator=g).to(torch.bfloat16))
+        if window_only:
+            dims = C.LayerDims(ratio=128)
+            W = Lm.make_attention_weights(3 + 7 * r, dims=dims, quant=True).to(dev)
+            blk = Lm.DecodeBlock(W, B, ctx, dims=dims, device=dev)
+            g = torch.Generator().manual_seed(cfgd["seeds"](rank, rank * B) + 104729 * r)
+            blk.cache.kv_pool.copy_(torch.randn(blk.cache.kv_pool.shape, generator=g).to(torch.bfloat16))
+        else:
+            W = Lm.make_attention_weights(3, quant=True).to(dev)
+            case = C.make_decode_case(B, ctx, top_k, seeds=[cfgd["seeds"](rank, rank * B + i) for i in range(B)],
+                                      device=dev)
+            blk = Lm.DecodeBlock(W, B, ctx, top_k=top_k, cache=case.cache)
+            g = torch.Generator().manual_seed(3 + rank)
         x = torch.randn(B, 4096, generator=g).to(dev)
         pos = torch.full((B,), ctx - 1, dtype=torch.int32, device=dev)
         with torch.cuda.stream(stream):
             blk.step(x, pos)
         stream.synchronize()
-        graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph(keep_graph=True)
         with torch.cuda.graph(graph, stream=stream):
             out = blk.step(x, pos)
         blocks.append(blk), graphs.append(graph), xs.append(x), outs.append(out), Ws.append(W)
-    with torch.cuda.stream(stream):
-        for i in range(warmup):
-            graphs[i % R].replay()
+    cursor = [0]
+
+    def run_k(k):
+        with torch.cuda.stream(stream):
+            for _ in range(k):
+                graphs[cursor[0] % R].replay()
+                cursor[0] += 1
+
+    run_k(Wm)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(env.local)
     sampler.start()
     time.sleep(0.05)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.perf_counter()
-    e0.record(stream)
-    with torch.cuda.stream(stream):
-        for i in range(steps):
-            graphs[i % R].replay()
-    e1.record(stream)
-    sampler.sample_while(e1)
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
-    if world > 1:
-        torch.distributed.barrier()
-    ms = _barrier_max(e0.elapsed_time(e1), world, dev) / steps
+    ms_list, windows = timed_regions(env, stream, run_k, K, reps, sampler)
     sampler.stop()
-    clocks = sampler.summary(t0, t1)
+    clocks = sampler.summary(windows=windows)
+    ms = statistics.median(ms_list) / K
     # e2e: this token's hidden states from pinned host memory, the graph, the block output back
     hx = [x.cpu().pin_memory() for x in xs]
     ho = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    with torch.cuda.stream(stream):
-        for i in range(steps):
-            r = i % R
-            xs[r].copy_(hx[r], non_blocking=True)
-            graphs[r].replay()
-            ho[r].copy_(outs[r], non_blocking=True)
-    f1.record(stream)
-    torch.cuda.synchronize()
-    ems = _barrier_max(f0.elapsed_time(f1), world, dev) / steps
-    # algorithmic HBM bytes of one step: the five matrices the step reads, once, and the window rows
-    W = Ws[0]
-    wbytes = 0
-    for name in ("wq_a", "wq_b", "wkv", "wo_a", "wo_b"):
-        w = getattr(W, name)
-        wbytes += (w.q.numel() + w.scale.numel() * 2) if isinstance(w, M.QuantWeight) else w.numel() * w.element_size()
-    step_bytes = wbytes + B * 128 * 1024
-    peak, peak_kind = _peaks()
+    ecur = [0]
+
+    def run_host(k):
+        with torch.cuda.stream(stream):
+            for _ in range(k):
+                r = ecur[0] % R
+                xs[r].copy_(hx[r], non_blocking=True)
+                graphs[r].replay()
+                ho[r].copy_(outs[r], non_blocking=True)
+                ecur[0] += 1
+
+    run_host(3)
+    ems_list, _ = timed_regions(env, stream, run_host, K, reps, _NoSampler())
+    ems = statistics.median(ems_list) / K
+    names = ("wq_a", "wq_b", "wkv", "wo_a", "wo_b") if window_only else Lm.MATRICES
+    max_comp = 0 if window_only else blocks[0].cache.max_comp
+    step_bytes = _step_bytes_block(Ws[0], B, ctx, top_k, max_comp, names)
+    hbm, _, _, peak_kind = _peaks()
     achieved = step_bytes / (ms * 1e-3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "whole block step", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+    roofline = {"bound": "hbm", "kernel": "whole block step", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_source": peak_kind, "traffic": None,
                 "algorithmic_bytes_per_launch": step_bytes}
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, desc = cpu_reference("c5w", cpu_sample_size("c5w"))
-        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
-    if rank == 0:
-        line = {"metric": METRICS["c5w"], "value": cfgd["batch"] / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
-                "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": cfgd["workload"], "global_batch": cfgd["batch"], "ctx": ctx,
-                           "parallelism": f"batch-split x{world} (no collective)" if world > 1 else "single GPU",
-                           "l2": f"{R} replicas of {step_bytes / 2**20:.0f} MiB rotated (> L2 between uses)",
-                           "cuda_graph": True},
-                "gpu_launches": None,
-                "e2e": {"value": cfgd["batch"] / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": hx[0].numel() * 4,
-                        "d2h_bytes_per_step": ho[0].numel() * 4, "path": "host hidden states -> block graph -> host"},
-                "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks}
-        print(json.dumps(line), flush=True)
+    launches = _count_launches(graphs[0])
+    line = {"metric": METRICS[name], "value": cfgd["batch"] / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+            "steps": K, "warmup": Wm, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config_dict(name, world),
+            "timing": dict(timing_summary(ms_list, K), replicas=R, graph="one CUDA graph launch per decode step"),
+            "gpu_launches": None if launches is None else int(round(launches * K)),
+            "gpu_launches_per_step": launches,
+            "e2e": {"value": cfgd["batch"] / (ems / 1000.0), "unit": "tok/s", "ms_per_step": ems,
+                    "h2d_bytes_per_step": hx[0].numel() * 4, "d2h_bytes_per_step": ho[0].numel() * 4,
+                    "path": "host hidden states -> block graph -> host"},
+            "roofline": roofline, "cpu_baseline": _cpu_baseline(env, name, headline), "clocks": clocks}
     del graphs
+    return line
+
+
+BENCH = {"c2": bench_decode, "c3": bench_decode, "c4": bench_prefill, "c5": bench_block, "c5w": bench_block}
+
+
+# ------------------------------------------------------------------------------ GPU leg
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--repeats", type=int, default=0, help="timed regions of K steps per config (median reported)")
+    ap.add_argument("--impl", default="dsv4", choices=["dsv4", "reference"])
+    ap.add_argument("--config", default="all", choices=["all"] + sorted(CONFIGS))
+    ap.add_argument("--replicas", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-case", default=None,
+                    choices=["attn_prefill", "indexer_prefill", "block_decode", "block_decode_window", "hc"],
+                    help="profiling aid: run one prefill kernel alone on a 4096-query slice of config 4 "
+                         "(positions 60000..64095), or config 5's block step eagerly inside an NVTX range "
+                         "(block_decode; block_decode_window: the same block at a ratio-128 layer), and print its "
+                         "CUDA-event time; not a bench line")
+    args = ap.parse_args()
+    if args.kernel_case:
+        return run_kernel_case(args)
+    args.steps_given, args.warmup_given = args.steps is not None, args.warmup is not None
+    if args.steps is None:
+        args.steps = SUB_STEPS["c2"] if args.config == "all" else SUB_STEPS[args.config]
+    if args.warmup is None:
+        args.warmup = 20
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    _pkg()
+    env = Env(args, world, rank, local, dev)
+    names = ALL if args.config == "all" else (args.config,)
+    results = {}
+    for i, name in enumerate(names):
+        results[name] = BENCH[name](env, name, i == 0)
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    head = results[names[0]]
+    if len(names) > 1:
+        head["configs"] = {n: results[n] for n in names[1:]}
+    if rank == 0:
+        print(json.dumps(head), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
         torch.distributed.destroy_process_group()
-
-
-def decode_launches_per_step(runner):
-    """Kernels one decode step launches: q's norm + RoPE, the indexer's scores (or its tensor-core
-    filter), the top-k selection, sparse attention, and the split merge when the attention plan
-    writes split partials. The plan writes them exactly when its workspace is non-zero; splits merged
-    inside a thread-block cluster need none."""
-    import ctypes
-    import importlib
-    L = importlib.import_module(PKG + "._lib")
-    SA = importlib.import_module(PKG + ".sparse_attn")
-    c = runner.cache
-    qr = torch.empty((c.batch, 64, c.head_dim), dtype=torch.bfloat16, device=runner.idx.device)
-    out = torch.empty(qr.shape, dtype=runner.out_dtype, device=qr.device)
-    p = SA._attn_params(qr, c.kv_pool, runner.sink, runner.idx, out, c.head_dim ** -0.5, runner.freqs,
-                        runner.positions, 64, win_base=c.win_base, window=c.window)
-    merge = L.lib().dsv4_sparse_attn_workspace_size(ctypes.byref(p)) > 0
-    return 4 + int(merge)
-
-
-def kernel_times(dsv4, cases, runners, stream, dev, n):
-    """Average duration of each kernel of the step, launched alone n times over the replica
-    rotation inside a CUDA graph and timed with CUDA events on the launching stream."""
-    import importlib
-    L = importlib.import_module(PKG + "._lib")
-    SA = importlib.import_module(PKG + ".sparse_attn")
-    IX = importlib.import_module(PKG + ".indexer")
-    R = len(cases)
-    b = cases[0].cache.batch
-    top_k = runners[0].top_k
-    freqs = runners[0].freqs
-    NRm = importlib.import_module(PKG + ".norm_rope")
-    qn = [NRm.norm_rope(r.q, r.positions, freqs) for r in runners]
-    torch.cuda.synchronize()
-    nvis = [min((int(c.host["positions"][i]) + 1) // 4, c.cache.max_comp) for c in cases[:1] for i in range(b)]
-    n_keys = sum(nvis)
-    funcs = {
-        # score + select (which also writes the window rows): k_idx read once, indices written
-        "indexer_topk": (lambda i: IX.indexer_topk_into(runners[i].idx.view(b, 1, -1), runners[i].q_idx.view(b, 1, 64, 128),
-                                                        runners[i].w_idx.view(b, 1, 64), cases[i].cache.k_idx, top_k,
-                                                        runners[i].positions.view(b, 1), 4, out_col=0,
-                                                        out_offset=cases[i].cache.comp_base,
-                                                        block_table=cases[i].cache.block_table, page=cases[i].cache.page),
-                         n_keys * 128 * 4 + b * (64 * 128 * 4 + 64 * 4 + top_k * 4)),
-        # attention (+ split merge): gathered rows, normed q in, o out, indices
-        "sparse_attn": (lambda i: SA.sparse_attn_rope(qn[i], cases[i].cache.kv_pool, cases[i].sink, runners[i].idx,
-                                                      512 ** -0.5, runners[i].positions, freqs, 64,
-                                                      win_base=cases[i].cache.win_base, window=128),
-                        b * ((128 + top_k) * 512 * 2 + top_k * 4 + 64 * 512 * 2 * 2)),
-    }
-    out = {}
-    for name, (fn, nbytes) in funcs.items():
-        with torch.cuda.stream(stream):
-            fn(0)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for i in range(R):
-                fn(i)
-        reps = max(1, n // R)
-        with torch.cuda.stream(stream):
-            g.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        with torch.cuda.stream(stream):
-            for _ in range(reps):
-                g.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        out[name] = {"us": e0.elapsed_time(e1) * 1000.0 / (reps * R), "bytes": nbytes}
-    return out
 
 
 def run_kernel_case(args):
     """One prefill kernel on a 4096-query slice of config 4 (queries at positions 60000..64095,
     65,536 window rows + 16,384 compressed rows, top-k 1024): the case the profiles under profiles/
     were captured on. Seeded synthetic inputs; prints one JSON line with the CUDA-event time."""
-    import importlib
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    SA = importlib.import_module(PKG + ".sparse_attn")
-    IX = importlib.import_module(PKG + ".indexer")
-    NRm = importlib.import_module(PKG + ".norm_rope")
+    SA, IX, NRm = _mod("sparse_attn"), _mod("indexer"), _mod("norm_rope")
     if args.kernel_case in ("block_decode", "block_decode_window"):
         return run_block_case(args, dev)
     if args.kernel_case == "hc":
@@ -1024,8 +1064,7 @@ def run_hc_case(args, dev):
     Algorithmic bytes per call: hc_pre reads x (16 dim B per token) and fn once (1.5 MB), writes the
     bf16 norm (2 dim B per token) and post / comb; hc_post reads x and the residual (20 dim B per
     token) and writes 16 dim B per token."""
-    import importlib
-    H = importlib.import_module(PKG + ".hc")
+    H = _mod("hc")
     dim = 4096
     g = torch.Generator(device=dev).manual_seed(0)
     fn_w = torch.randn(24, 4 * dim, device=dev, generator=g) * 0.02
@@ -1069,9 +1108,7 @@ def run_block_case(args, dev):
     three warm-up steps, then `--steps` (default 2) steps inside the NVTX range "step", so that a
     profiler can take exactly those launches (`ncu --nvtx --nvtx-include "step/"`). With
     `block_decode_window` the block is a ratio-128 (window-only) layer's."""
-    import importlib
-    Lm = importlib.import_module(PKG + ".layer")
-    C = importlib.import_module(PKG + ".configs")
+    Lm, C = _mod("layer"), _mod("configs")
     cfgd = CONFIGS["c5"]
     B, ctx, top_k = cfgd["batch"], cfgd["ctx"], cfgd["top_k"]
     if args.kernel_case == "block_decode_window":

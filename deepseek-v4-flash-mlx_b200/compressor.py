@@ -11,7 +11,7 @@ import ctypes
 import torch
 
 from . import _lib as L
-from .mla import linear
+from .mla import QuantWeight, linear
 from .norm_rope import rope_freqs
 
 
@@ -34,11 +34,55 @@ def _pool(kv, score, ape, norm_w, out, head_dim, ratio, rope_dim, freqs, ring_kv
     L.check(L.lib().dsv4_compressor_pool(ctypes.byref(p), L.stream_of(kv)))
 
 
+def _w_parts(W):
+    """(tensor, scale or None) of a weight: bf16 / fp32 tensor, or QuantWeight's int8 values + scales."""
+    if isinstance(W, QuantWeight):
+        return W.q, W.scale
+    return W, None
+
+
+def _w_join(w, scale):
+    return QuantWeight(w, scale) if scale is not None else w
+
+
+@torch.library.custom_op("dsv4::compressor_prefill", mutates_args=(), device_types="cuda")
+def _compressor_prefill_op(x: torch.Tensor, wkv: torch.Tensor, wkv_scale: torch.Tensor | None, wgate: torch.Tensor,
+                           wgate_scale: torch.Tensor | None, ape: torch.Tensor, norm_w: torch.Tensor, head_dim: int,
+                           ratio: int, rope_head_dim: int, base: float, original_seq_len: int, factor: float,
+                           beta_fast: float, beta_slow: float, out_dtype: torch.dtype, pos0: int,
+                           act_quant: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    b, s, _ = x.shape
+    d2 = 2 * head_dim
+    kv = linear(x, _w_join(wkv, wkv_scale), torch.float32)
+    score = linear(x, _w_join(wgate, wgate_scale), torch.float32)
+    freqs = rope_freqs(rope_head_dim, x.device, original_seq_len=original_seq_len, base=base, factor=factor,
+                       beta_fast=beta_fast, beta_slow=beta_slow)
+    out = torch.empty((b, s // ratio, head_dim), dtype=out_dtype, device=x.device)
+    ring_kv = torch.empty((b, 2 * ratio, d2), dtype=torch.float32, device=x.device)
+    ring_score = torch.empty_like(ring_kv)
+    nw = norm_w if norm_w.dtype in (torch.float32, torch.bfloat16) else norm_w.float()
+    _pool(kv, score, ape.float().contiguous(), nw.contiguous(), out, head_dim, ratio, rope_head_dim, freqs,
+          ring_kv, ring_score, pos0=pos0, act_quant=act_quant)
+    cutoff = s - s % ratio
+    return out, ring_kv, ring_score, kv[:, cutoff:].clone()
+
+
+@_compressor_prefill_op.register_fake
+def _(x, wkv, wkv_scale, wgate, wgate_scale, ape, norm_w, head_dim, ratio, rope_head_dim, base, original_seq_len,
+      factor, beta_fast, beta_slow, out_dtype, pos0, act_quant):
+    b, s, _ = x.shape
+    ring = x.new_empty((b, 2 * ratio, 2 * head_dim), dtype=torch.float32)
+    return (x.new_empty((b, s // ratio, head_dim), dtype=out_dtype), ring, torch.empty_like(ring),
+            x.new_empty((b, s % ratio, 2 * head_dim), dtype=torch.float32))
+
+
 def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_head_dim=64,
                        base=160000.0, original_seq_len=65536, factor=16, beta_fast=32, beta_slow=1,
                        out_dtype=torch.float32, pos0=0, act_quant=False, rotate=False):
     """x [b, s, dim] -> (kv [b, s//ratio, head_dim] post-rope, state).
 
+    The reference signature (ref_torch/compressor.py:21) over the custom op `dsv4::compressor_prefill`
+    (opaque to torch.compile / FakeTensor tracing; weights bf16, fp32, or QuantWeight).
     state: "kv" / "score" = the last full block's kv and score+ape [b, ratio, 2*head_dim] (when
     s >= ratio), "kv_rem" = the remainder rows, and "ring_kv" / "ring_score" [b, 2*ratio, 2*head_dim]
     the device ring that `compressor_decode_step` continues from (ref_torch/compressor.py:67-74).
@@ -47,51 +91,42 @@ def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_h
     reference's default for the main compressor, v4mlx/compressor.py:60-62). `rotate` (head_dim
     128, the indexer compressor; v4mlx/compressor.py:57-59): instead, every dim of each row is
     rotated by the normalised Walsh-Hadamard transform and rounded to fp4-e2m1 in blocks of 32."""
-    L.require_cuda(x, wkv, wgate, ape, norm_w)
-    b, s, _ = x.shape
-    d2 = 2 * head_dim
-    kv = linear(x, wkv, torch.float32)
-    score = linear(x, wgate, torch.float32)
-    freqs = rope_freqs(rope_head_dim, x.device, original_seq_len=original_seq_len, base=base, factor=factor,
-                       beta_fast=beta_fast, beta_slow=beta_slow)
-    groups = s // ratio
-    out = torch.empty((b, groups, head_dim), dtype=out_dtype, device=x.device)
-    ring_kv = torch.empty((b, 2 * ratio, d2), dtype=torch.float32, device=x.device)
-    ring_score = torch.empty_like(ring_kv)
-    nw = norm_w if norm_w.dtype in (torch.float32, torch.bfloat16) else norm_w.float()
-    _pool(kv, score, ape.float().contiguous(), nw.contiguous(), out, head_dim, ratio, rope_head_dim, freqs,
-          ring_kv, ring_score, pos0=pos0, act_quant=2 if rotate else act_quant)
-    cutoff = s - s % ratio
+    wkv_t, wkv_s = _w_parts(wkv)
+    wg_t, wg_s = _w_parts(wgate)
+    L.require_cuda(x, wkv_t, wg_t, ape, norm_w)
+    s = x.shape[1]
+    out, ring_kv, ring_score, rem = _compressor_prefill_op(
+        x, wkv_t, wkv_s, wg_t, wg_s, ape, norm_w, int(head_dim), int(ratio), int(rope_head_dim), float(base),
+        int(original_seq_len), float(factor), float(beta_fast), float(beta_slow), out_dtype, int(pos0),
+        2 if rotate else int(act_quant))
     state = {"ring_kv": ring_kv, "ring_score": ring_score}
-    if cutoff >= ratio:
+    if s - s % ratio >= ratio:
         state["kv"] = ring_kv[:, :ratio]
         state["score"] = ring_score[:, :ratio]
     if s % ratio:
-        state["kv_rem"] = kv[:, cutoff:]
+        state["kv_rem"] = rem
     return out, state
 
 
-def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, positions, out, out_rows,
-                           head_dim=512, ratio=4, rope_head_dim=64, freqs=None, eps=1e-6,
-                           proj=None, key_image=None, act_quant=False, rotate=False):
-    """One decode token per sequence (oracle/decode_engine.py:96-105): write this token's kv / score
-    into the device ring; sequences whose position p has (p+1) % ratio == 0 emit a pooled, normed,
-    roped row into out[out_rows[b]] and shift the ring. x [b, dim]; positions int32 [b].
-    `proj` may pass precomputed projections (kv, score) [b, 2*head_dim] fp32. `key_image`
-    (image, inv, norm_max, keys_per_entry) also adds each emitted indexer key (out viewed as
-    [entries * keys_per_entry, 128] fp32) to a decode cache's key image. `act_quant`: the fp8-e4m3
-    act-quant simulation of the emitted row's nope dims (oracle/decode_engine.py:105). `rotate`
-    (head_dim 128): the Hadamard + fp4-e2m1 key simulation of `compressor_prefill(rotate=True)`."""
-    L.require_cuda(x, ring_kv, ring_score, positions, out, out_rows)
-    if proj is None:
-        kvp = linear(x, wkv, torch.float32)
-        scp = linear(x, wgate, torch.float32)
+@torch.library.custom_op("dsv4::compressor_decode_step",
+                         mutates_args=("ring_kv", "ring_score", "out", "key_image", "key_inv", "key_norm_max"),
+                         device_types="cuda")
+def _compressor_decode_op(x: torch.Tensor, wkv: torch.Tensor, wkv_scale: torch.Tensor | None, wgate: torch.Tensor,
+                          wgate_scale: torch.Tensor | None, ape: torch.Tensor, norm_w: torch.Tensor | None,
+                          ring_kv: torch.Tensor, ring_score: torch.Tensor, positions: torch.Tensor,
+                          out: torch.Tensor, out_rows: torch.Tensor, head_dim: int, ratio: int, rope_head_dim: int,
+                          freqs: torch.Tensor, eps: float, proj_kv: torch.Tensor | None,
+                          proj_score: torch.Tensor | None, key_image: torch.Tensor | None,
+                          key_inv: torch.Tensor | None, key_norm_max: torch.Tensor | None, image_stride: int,
+                          act_quant: int) -> None:
+    if proj_kv is None:
+        kvp = linear(x, _w_join(wkv, wkv_scale), torch.float32)
+        scp = linear(x, _w_join(wgate, wgate_scale), torch.float32)
     else:
-        kvp, scp = proj
-    if freqs is None:
-        freqs = rope_freqs(rope_head_dim, x.device)
+        kvp, scp = proj_kv, proj_score
+    kvp, scp = kvp.contiguous(), scp.contiguous()
     p = L.CompressorDecodeParams()
-    p.kv, p.score, p.ape = L.ptr(kvp.contiguous()), L.ptr(scp.contiguous()), L.ptr(ape)
+    p.kv, p.score, p.ape = L.ptr(kvp), L.ptr(scp), L.ptr(ape)
     p.norm_w = L.ptr(norm_w) if norm_w is not None else None
     p.ring_kv, p.ring_score = L.ptr(ring_kv), L.ptr(ring_score)
     p.positions = L.ptr(positions)
@@ -101,8 +136,39 @@ def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, posi
     p.out_dtype = L.dtype_code(out)
     p.eps = eps
     p.freqs = L.ptr(freqs)
-    p.act_quant = 2 if rotate else int(act_quant)
+    p.act_quant = act_quant
     if key_image is not None:
-        img, inv, nmax, stride = key_image
-        p.key_image, p.key_inv, p.key_norm_max, p.image_stride = L.ptr(img), L.ptr(inv), L.ptr(nmax), int(stride)
+        p.key_image, p.key_inv, p.key_norm_max = L.ptr(key_image), L.ptr(key_inv), L.ptr(key_norm_max)
+        p.image_stride = image_stride
     L.check(L.lib().dsv4_compressor_decode(ctypes.byref(p), L.stream_of(x)))
+
+
+@_compressor_decode_op.register_fake
+def _(x, wkv, wkv_scale, wgate, wgate_scale, ape, norm_w, ring_kv, ring_score, positions, out, out_rows, head_dim,
+      ratio, rope_head_dim, freqs, eps, proj_kv, proj_score, key_image, key_inv, key_norm_max, image_stride,
+      act_quant):
+    return None
+
+
+def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, positions, out, out_rows,
+                           head_dim=512, ratio=4, rope_head_dim=64, freqs=None, eps=1e-6,
+                           proj=None, key_image=None, act_quant=False, rotate=False):
+    """One decode token per sequence (oracle/decode_engine.py:96-105): write this token's kv / score
+    into the device ring; sequences whose position p has (p+1) % ratio == 0 emit a pooled, normed,
+    roped row into out[out_rows[b]] and shift the ring. x [b, dim]; positions int32 [b].
+    The custom op `dsv4::compressor_decode_step` (it mutates the ring, `out` and the key image).
+    `proj` may pass precomputed projections (kv, score) [b, 2*head_dim] fp32. `key_image`
+    (image, inv, norm_max, keys_per_entry) also adds each emitted indexer key (out viewed as
+    [entries * keys_per_entry, 128] fp32) to a decode cache's key image. `act_quant`: the fp8-e4m3
+    act-quant simulation of the emitted row's nope dims (oracle/decode_engine.py:105). `rotate`
+    (head_dim 128): the Hadamard + fp4-e2m1 key simulation of `compressor_prefill(rotate=True)`."""
+    wkv_t, wkv_s = _w_parts(wkv)
+    wg_t, wg_s = _w_parts(wgate)
+    L.require_cuda(x, ring_kv, ring_score, positions, out, out_rows)
+    if freqs is None:
+        freqs = rope_freqs(rope_head_dim, x.device)
+    pk, ps = proj if proj is not None else (None, None)
+    img, inv, nmax, stride = key_image if key_image is not None else (None, None, None, 0)
+    _compressor_decode_op(x, wkv_t, wkv_s, wg_t, wg_s, ape, norm_w, ring_kv, ring_score, positions, out, out_rows,
+                          int(head_dim), int(ratio), int(rope_head_dim), freqs, float(eps), pk, ps, img, inv, nmax,
+                          int(stride), 2 if rotate else int(act_quant))

@@ -1414,8 +1414,37 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kMaxDevices] = {};
+unsigned long long g_noalloc_ctx[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device, looked up once per device.
+// Unique id of the current CUDA context (cuCtxGetCurrent + cuCtxGetId, reached through the
+// runtime's driver entry points so that the library needs no link to libcuda), 0 if unavailable.
+// Ids are never reused within a process, so a context recreated after cudaDeviceReset (where the
+// library's device image, and with it the scratch array, may load at another address) differs.
+unsigned long long current_context_id() {
+  using GetCurrent = int (*)(void**);
+  using GetId = int (*)(void*, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {  // called with g_noalloc_mu held
+    looked_up = true;
+    cudaDriverEntryPointQueryResult q1, q2;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", reinterpret_cast<void**>(&get_current), 12000,
+                                         cudaEnableDefault, &q1) != cudaSuccess || q1 != cudaDriverEntryPointSuccess)
+      get_current = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", reinterpret_cast<void**>(&get_id), 12000,
+                                         cudaEnableDefault, &q2) != cudaSuccess || q2 != cudaDriverEntryPointSuccess)
+      get_id = nullptr;
+    cudaGetLastError();
+  }
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != 0 || ctx == nullptr || get_id(ctx, &id) != 0) return 0;
+  return id;
+}
+
+// Device address of the scratch array on the current device: looked up at the first call on each
+// device (with that device current), and again only when the device's context has changed.
 int noalloc_scratch(float** out) {
   int dev = 0;
   DSV4_CUDA_CHECK(cudaGetDevice(&dev));
@@ -1424,10 +1453,12 @@ int noalloc_scratch(float** out) {
     return DSV4_ERR_INVALID_ARGUMENT;
   }
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  const unsigned long long ctx = current_context_id();
+  if (g_noalloc_ptr[dev] == nullptr || ctx != g_noalloc_ctx[dev]) {
     void* ptr = nullptr;
     DSV4_CUDA_CHECK(cudaGetSymbolAddress(&ptr, g_noalloc_scores));
     g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return DSV4_OK;
@@ -1439,6 +1470,10 @@ extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* str
   DSV4_CHECK_ARG(p->q && p->w && p->k && p->out, "dsv4_indexer_topk_noalloc: NULL tensor");
   DSV4_CHECK_ARG(p->workspace == nullptr && p->scores_out == nullptr,
                  "dsv4_indexer_topk_noalloc: workspace and scores_out must be NULL (the scratch is built in)");
+  DSV4_CHECK_ARG(p->mode >= 0 && p->mode <= 2, "dsv4_indexer_topk_noalloc: mode %d unknown (0, 1 or 2)", p->mode);
+  DSV4_CHECK_ARG((p->key_image == nullptr) == (p->key_inv == nullptr) &&
+                     (p->key_image == nullptr) == (p->key_norm_max == nullptr),
+                 "dsv4_indexer_topk_noalloc: key_image, key_inv and key_norm_max go together");
   DSV4_CHECK_ARG(p->heads == idx::HI, "dsv4_indexer_topk_noalloc: %d heads unsupported (64 only)", p->heads);
   DSV4_CHECK_ARG(p->batch > 0 && p->s > 0 && p->n_keys > 0 && p->top_k > 0,
                  "dsv4_indexer_topk_noalloc: bad sizes");

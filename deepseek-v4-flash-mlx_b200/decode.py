@@ -153,12 +153,20 @@ class SparseMLACache:
             raise ValueError(f"SparseMLACache.load_prefill: {n} compressed rows exceed the cache's {self.max_comp}")
         if n:
             self.fill_compressed(b, comp_rows, keys)
+        # an omitted ring starts from the compressor's initial state (kv 0, scores -inf), never from
+        # what a previous sequence left in slot b
         if ring is not None:
             self.ring_kv[b].copy_(ring[0].reshape(self.ring_kv[b].shape))
             self.ring_score[b].copy_(ring[1].reshape(self.ring_score[b].shape))
+        else:
+            self.ring_kv[b].zero_()
+            self.ring_score[b].fill_(float("-inf"))
         if key_ring is not None:
             self.ring_k_idx[b].copy_(key_ring[0].reshape(self.ring_k_idx[b].shape))
             self.ring_s_idx[b].copy_(key_ring[1].reshape(self.ring_s_idx[b].shape))
+        else:
+            self.ring_k_idx[b].zero_()
+            self.ring_s_idx[b].fill_(float("-inf"))
 
 
 def decode_rows(cache, positions):
@@ -184,9 +192,38 @@ def attention_index_buffer(batch, window, top_k, device):
     return torch.empty((batch, top_k), dtype=torch.int32, device=device)
 
 
+@torch.library.custom_op("dsv4::decode_attention", mutates_args=("idx_buf",), device_types="cuda")
+def _decode_attention_op(kv_pool: torch.Tensor, k_idx: torch.Tensor, block_table: torch.Tensor,
+                         win_base: torch.Tensor, key_image: torch.Tensor | None, key_inv: torch.Tensor | None,
+                         key_norm_max: torch.Tensor | None, q: torch.Tensor, q_idx: torch.Tensor, w_idx: torch.Tensor,
+                         sink: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor, idx_buf: torch.Tensor,
+                         top_k: int, scale: float, window: int, ratio: int, page: int, comp_base: int,
+                         out_dtype: torch.dtype) -> torch.Tensor:
+    b = q.shape[0]
+    main = torch.cuda.current_stream(q.device)
+    side = _side_stream(q.device)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):          # q's norm + rope runs beside the indexer
+        qr = norm_rope(q, positions, freqs, weight=None)
+    image = (key_image, key_inv, key_norm_max) if key_image is not None else None
+    indexer_topk_into(idx_buf.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
+                      k_idx, top_k, positions.view(b, 1), ratio, out_col=0, out_offset=comp_base,
+                      block_table=block_table, page=page, key_image=image)
+    main.wait_stream(side)
+    qr.record_stream(main)
+    return sparse_attn_rope(qr, kv_pool, sink, idx_buf, scale, positions, freqs, 64, out_dtype,
+                            win_base=win_base, window=window)
+
+
+@_decode_attention_op.register_fake
+def _(kv_pool, k_idx, block_table, win_base, key_image, key_inv, key_norm_max, q, q_idx, w_idx, sink, positions, freqs,
+      idx_buf, top_k, scale, window, ratio, page, comp_base, out_dtype):
+    return q.new_empty(q.shape, dtype=out_dtype)
+
+
 def decode_attention(cache, q, q_idx, w_idx, sink, positions, top_k=512, scale=None, freqs=None, idx_buf=None,
                      out_dtype=torch.bfloat16):
-    """One decode token per sequence.
+    """One decode token per sequence, through the custom op `dsv4::decode_attention`.
 
     q [b, 64, 512] raw (before the per-head norm), q_idx [b, 64, 128] fp32, w_idx [b, 64] fp32,
     sink [64] fp32, positions int32 [b] (position p of the new token). Returns o [b, 64, 512] after
@@ -198,22 +235,16 @@ def decode_attention(cache, q, q_idx, w_idx, sink, positions, top_k=512, scale=N
     if freqs is None:
         freqs = rope_freqs(64, q.device)
     positions = positions.to(torch.int32).contiguous()
-    main = torch.cuda.current_stream(q.device)
-    side = _side_stream(q.device)
-    side.wait_stream(main)
-    with torch.cuda.stream(side):          # q's norm + rope runs beside the indexer
-        qr = norm_rope(q, positions, freqs, weight=None)
     idx = idx_buf if idx_buf is not None else attention_index_buffer(b, cache.window, top_k, q.device)
     if cache.image_stale:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("decode_attention: the cache's key image is stale inside a stream capture (the full "
+                               "rebuild would replay every step); call cache.refresh_key_image() before capturing")
         cache.refresh_key_image()
-    indexer_topk_into(idx.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
-                      cache.k_idx, top_k, positions.view(b, 1), cache.ratio, out_col=0,
-                      out_offset=cache.comp_base, block_table=cache.block_table, page=cache.page,
-                      key_image=cache.key_image)
-    main.wait_stream(side)
-    qr.record_stream(main)
-    return sparse_attn_rope(qr, cache.kv_pool, sink, idx, scale, positions, freqs, 64, out_dtype,
-                            win_base=cache.win_base, window=cache.window)
+    img, inv, nmax = cache.key_image if cache.key_image is not None else (None, None, None)
+    return _decode_attention_op(cache.kv_pool, cache.k_idx, cache.block_table, cache.win_base, img, inv, nmax, q,
+                                q_idx, w_idx, sink, positions, freqs, idx, int(top_k), float(scale),
+                                int(cache.window), int(cache.ratio), int(cache.page), int(cache.comp_base), out_dtype)
 
 
 def window_attention(cache, q, sink, positions, scale=None, freqs=None, idx_buf=None, out_dtype=torch.bfloat16):
@@ -260,7 +291,13 @@ class DecodeRunner:
     Callers that write their inputs straight into `host_inputs()` skip the host-side staging copy.
     """
 
-    def __init__(self, cache, sink, top_k=512, device="cuda", out_dtype=torch.bfloat16, stream=None):
+    def __init__(self, cache, sink, top_k=512, device="cuda", out_dtype=torch.bfloat16, stream=None,
+                 q_dtype=torch.float32, keep_graph=False):
+        """`q_dtype`: the dtype of q in the input block (float32, or bfloat16 to halve its copy: the
+        kernels round the normed q to bf16 either way, but the per-head norm then reads bf16 values).
+        `keep_graph`: keep the captured cudaGraph_t (for inspection of its nodes)."""
+        if q_dtype not in (torch.float32, torch.bfloat16):
+            raise TypeError("DecodeRunner: q_dtype must be float32 or bfloat16")
         if not cache.compressed:
             raise ValueError("DecodeRunner runs the compressed layer's step (indexer + sparse attention); a window-only "
                              "cache (ratio 0 or 128) is stepped by DecodeBlock or window_attention")
@@ -268,7 +305,8 @@ class DecodeRunner:
         b = cache.batch
         dev = torch.device(device)
         self.sink = sink.float().contiguous().to(dev)
-        shapes = [((b, 64, cache.head_dim), torch.float32), ((b, 64, 128), torch.float32), ((b, 64), torch.float32),
+        self.keep_graph = keep_graph
+        shapes = [((b, 64, cache.head_dim), q_dtype), ((b, 64, 128), torch.float32), ((b, 64), torch.float32),
                   ((b,), torch.int32)]
         offs, total = [], 0
         for shape, dt in shapes:  # 256-byte aligned fields of one block
@@ -299,9 +337,11 @@ class DecodeRunner:
 
     def capture(self):
         with torch.cuda.stream(self.stream):
+            if self.cache.image_stale:   # rebuilt here, never inside the captured step
+                self.cache.refresh_key_image()
             self._body()  # warm up allocations and one-time attributes outside capture
         self.stream.synchronize()
-        self.graph = torch.cuda.CUDAGraph()
+        self.graph = torch.cuda.CUDAGraph(keep_graph=self.keep_graph)
         with torch.cuda.graph(self.graph, stream=self.stream):
             self.out = self._body()
         self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
@@ -353,3 +393,9 @@ class DecodeRunner:
 
     def synchronize(self):
         self.stream.synchronize()
+
+    def release(self):
+        """Drop the captured graphs (their memory returns to torch's graph pool)."""
+        self.stream.synchronize()
+        self.graph = self.graph_host = None
+        self.out = self.out_host_graph = None

@@ -257,12 +257,15 @@ DSV4_API int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream);
  * a host engine that hands out all GPU memory from its own pool and forbids other allocations, a
  * plugin invoked inside a step that must not synchronise (cudaMalloc and cudaFree can), or code that
  * runs while someone else's stream capture is open. It has no counterpart in the reference.
- * Same parameters and results as dsv4_indexer_topk; `workspace` and `scores_out` must be NULL. The
- * score scratch is a fixed device array inside the library of DSV4_INDEXER_NOALLOC_MAX_SCORES floats
+ * Same parameters and results as dsv4_indexer_topk; `workspace` and `scores_out` must be NULL. Every
+ * valid `mode` (0, 1, 2) gives the same selection, and this path always computes it from the exact
+ * fp32 scores (mode 1): it ignores key_image / key_inv / key_norm_max, which must still be all set or
+ * all NULL. The score scratch is a fixed device array inside the library of DSV4_INDEXER_NOALLOC_MAX_SCORES floats
  * (4 MiB), present on every GPU that loads the library until the process exits; requests with
  * batch * s * round_up(n_keys, 4) above that are rejected with DSV4_ERR_WORKSPACE. The first call on a
  * device looks up that array's device address (cudaGetSymbolAddress) with the device current, so make
- * it before any stream capture. All calls share the one array: calls that overlap on the GPU (on
+ * it before any stream capture; the address is looked up again if the device's context changes (after
+ * cudaDeviceReset), so make the first call after a reset outside a capture too. All calls share the one array: calls that overlap on the GPU (on
  * different streams, or on one stream from different host threads without ordering) race. */
 #define DSV4_INDEXER_NOALLOC_MAX_SCORES (1 << 20)
 DSV4_API int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* stream);

@@ -16,8 +16,10 @@ def overlap_transform(t, ratio, d, fill):
 
 
 def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_head_dim=64,
-                       base=160000.0, original_seq_len=65536, factor=16, beta_fast=32, beta_slow=1):
-    """ref_torch/compressor.py:21-50 -> (rows [b, s//ratio, head_dim], state)."""
+                       base=160000.0, original_seq_len=65536, factor=16, beta_fast=32, beta_slow=1, pos0=0):
+    """ref_torch/compressor.py:21-50 -> (rows [b, s//ratio, head_dim], state). `pos0` (test aid, 0 in
+    the reference): x is a slice of a longer sequence starting at position pos0, so row g is roped at
+    pos0 + ratio * g (the angles t * freq do not depend on the table's length)."""
     b, s, _ = x.shape
     x = x.float()
     kv = x @ wkv.float().T
@@ -37,7 +39,8 @@ def compressor_prefill(x, wkv, wgate, ape, norm_w, head_dim=512, ratio=4, rope_h
     sc = overlap_transform(sc, ratio, head_dim, float("-inf"))
     rows = (kv * sc.softmax(dim=2)).sum(dim=2)
     rows = rmsnorm(rows, norm_w.float())
-    cis = precompute_freqs_cis(rope_head_dim, s, original_seq_len, base, factor, beta_fast, beta_slow)[:cut:ratio]
+    cis = precompute_freqs_cis(rope_head_dim, pos0 + s, original_seq_len, base, factor, beta_fast,
+                               beta_slow)[pos0:pos0 + cut:ratio]
     rd = rope_head_dim
     rows = torch.cat([rows[..., :-rd], apply_rotary_emb(rows[..., -rd:], cis)], -1)
     return rows, state

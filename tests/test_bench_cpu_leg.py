@@ -24,3 +24,14 @@ def test_dequantized_weights_equal_the_oracles():
         got = getattr(Wd, name)
         assert got.dtype == torch.float32 and torch.equal(got, _w(getattr(W, name))), name
     assert torch.equal(Wd.sinks, W.sinks)
+
+
+def test_reference_arm_prints_the_gpu_arms_config():
+    """The reference arm's line carries the GPU arm's config dict at the same N (config 2 at N=2: two
+    replica sequences), and exactly K timed steps."""
+    line = bench.reference_line("c2", steps=2, warmup=1, world=2, per_step_seconds=0.01)
+    assert line["config"] == bench.config_dict("c2", 2)
+    assert line["config"]["global_batch"] == 2 and line["steps"] == 2 and line["impl"] == "reference"
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
+    for name in ("c3", "c4", "c5"):
+        assert bench.config_dict(name, 8)["global_batch"] == (1 if name == "c4" else bench.CONFIGS[name]["batch"])

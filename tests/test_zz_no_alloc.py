@@ -42,23 +42,53 @@ def _params(q, w, k, pos, out, top_k, ws=None):
     return p
 
 
+def _decode_layout(p, b, n, page=64, window=128, out_col=128, seed=0):
+    """A decode engine's call: keys mapped through a shuffled block table into pool rows after each
+    sequence's window ring, the window rows written to the first `window` columns."""
+    g = torch.Generator().manual_seed(seed)
+    pages = (n + page - 1) // page
+    table = torch.randperm(b * pages, generator=g).to(torch.int32).reshape(b, pages).cuda()
+    win_base = (torch.arange(b, dtype=torch.int64) * window).cuda()
+    p.block_table, p.table_stride, p.page = table.data_ptr(), pages, page
+    p.out_col, p.out_offset = out_col, b * window
+    p.win_base, p.window, p.window_linear = win_base.data_ptr(), window, 0
+    return table, win_base
+
+
+CASES = [  # (batch, queries per row, keys, top_k, seed, mode of the allocating call, decode layout)
+    (2, 3, 3000, 512, 21, 0, False),
+    (1, 2, 8192, 512, 22, 0, False),
+    (1, 128, 4096, 512, 23, 1, False),  # s >= 64: the allocating call takes the query-tiled score kernel
+    (3, 1, 2048, 512, 24, 0, True),     # block table, window columns, out_col > 0
+]
+
+
 def test_noalloc_indexer_matches_allocating_entry_point():
     lib = L.load()
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    for call, (b, s, n, top_k, seed) in enumerate([(2, 3, 3000, 512, 21), (1, 2, 8192, 512, 22)]):
+    for call, (b, s, n, top_k, seed, mode, decode) in enumerate(CASES):
         q, w, k, pos = _inputs(b, s, n, seed)
-        ref = torch.full((b, s, top_k), -7, dtype=torch.int32, device="cuda")
+        width = top_k + (128 if decode else 0)
+        ref = torch.full((b, s, width), -7, dtype=torch.int32, device="cuda")
         p_ref = _params(q, w, k, pos, ref, top_k)
-        ws = torch.empty(lib.dsv4_indexer_topk_workspace_size(ctypes.byref(p_ref)), dtype=torch.uint8,
+        p_ref.mode = mode
+        keep = _decode_layout(p_ref, b, n, seed=seed) if decode else None
+        ws = torch.empty(max(1, lib.dsv4_indexer_topk_workspace_size(ctypes.byref(p_ref))), dtype=torch.uint8,
                          device="cuda")
-        p_ref = _params(q, w, k, pos, ref, top_k, ws)
+        p_ref.workspace, p_ref.workspace_bytes = ws.data_ptr(), ws.numel()
         assert lib.dsv4_indexer_topk(ctypes.byref(p_ref), stream) == 0, lib.dsv4_last_error()
-        got = torch.full((b, s, top_k), -7, dtype=torch.int32, device="cuda")
-        p = _params(q, w, k, pos, got, top_k)
-        assert lib.dsv4_indexer_topk_noalloc(ctypes.byref(p), stream) == 0, lib.dsv4_last_error()
-        torch.cuda.synchronize()
-        assert torch.equal(got, ref), f"call {call}: allocation-free selection differs"
-        assert (got >= -1).all()
+        for rep in range(2):   # two calls in a row on the shared scratch
+            got = torch.full((b, s, width), -7, dtype=torch.int32, device="cuda")
+            p = _params(q, w, k, pos, got, top_k)
+            if decode:
+                p.block_table, p.table_stride, p.page = p_ref.block_table, p_ref.table_stride, p_ref.page
+                p.out_col, p.out_offset = p_ref.out_col, p_ref.out_offset
+                p.win_base, p.window, p.window_linear = p_ref.win_base, p_ref.window, 0
+            assert lib.dsv4_indexer_topk_noalloc(ctypes.byref(p), stream) == 0, lib.dsv4_last_error()
+            torch.cuda.synchronize()
+            assert torch.equal(got, ref), f"case {call} call {rep}: allocation-free selection differs"
+            assert (got >= -1).all()
+        del keep
 
 
 def test_noalloc_indexer_rejects_oversized_requests():
@@ -73,3 +103,10 @@ def test_noalloc_indexer_rejects_oversized_requests():
     ws = torch.empty(16, dtype=torch.uint8, device="cuda")
     p2 = _params(q, w, k, pos, out, 8, ws)
     assert lib.dsv4_indexer_topk_noalloc(ctypes.byref(p2), None) == 1   # workspace must be NULL
+    p3 = _params(q, w, k, pos, out, 8)
+    p3.mode = 3                                                          # unknown mode, as the allocating call
+    assert lib.dsv4_indexer_topk_noalloc(ctypes.byref(p3), None) == 1
+    p4 = _params(q, w, k, pos, out, 8)
+    p4.key_image = k.data_ptr()                                          # half of the key-image triple
+    assert lib.dsv4_indexer_topk_noalloc(ctypes.byref(p4), None) == 1
+    assert b"go together" in lib.dsv4_last_error()
