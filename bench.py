@@ -591,7 +591,7 @@ def bench_decode(env, name, headline):
                 runners[cursor[0] % R].graph.replay()
                 cursor[0] += 1
 
-    run_k(W)
+    run_k(max(W, 2 * R))   # at least W, and every replica's graph replayed (uploaded) before timing
     torch.cuda.synchronize()
     sampler = ClockSampler(env.local)
     sampler.start()
@@ -618,7 +618,7 @@ def bench_decode(env, name, headline):
             runners[i].step_host(*hin[i])
             ecur[0] += 1
 
-    run_host(min(R, 4))
+    run_host(R)
     torch.cuda.synchronize()
     ems_list, _ = timed_regions(env, stream, run_host, K, reps, _NoSampler())
     ems = statistics.median(ems_list) / K
@@ -906,7 +906,7 @@ def bench_block(env, name, headline):
                 graphs[cursor[0] % R].replay()
                 cursor[0] += 1
 
-    run_k(Wm)
+    run_k(max(Wm, 2 * R))
     torch.cuda.synchronize()
     sampler = ClockSampler(env.local)
     sampler.start()

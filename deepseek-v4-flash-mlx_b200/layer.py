@@ -184,10 +184,12 @@ class DecodeBlock:
         self.cache.load_prefill(b, aux["kvcat"][:s], aux["kvcat"][s:], aux["k_idx"].reshape(-1, self.dims.idx_dim),
                                 ring=aux["ring"], key_ring=aux["key_ring"])
 
-    def step(self, x, positions):
-        """x [b, dim] fp32/bf16, positions int32 [b] (position of this token) -> out [b, dim] fp32."""
+    def step(self, x, positions, aux=None):
+        """x [b, dim] fp32/bf16, positions int32 [b] (position of this token) -> out [b, dim] fp32.
+        `aux` (a dict, for verification) receives the indexer's inputs ("q_idx" after RoPE, "w_idx")
+        and the selected pool rows ("idx") of a compressed layer's step."""
         # the normed activations feed only bf16 projections: rounded to bf16 once, by the norm
-        return self._attend(rmsnorm(x, self.W.attn_norm, out_dtype=torch.bfloat16), positions)
+        return self._attend(rmsnorm(x, self.W.attn_norm, out_dtype=torch.bfloat16), positions, aux)
 
     def step_hc(self, x, positions, hc_fn, hc_scale, hc_base, sinkhorn_iters=20, hc_eps=1e-6):
         """The block inside its hyper-connections (the decode layer's hc_pre -> attn_norm -> attention
@@ -197,7 +199,7 @@ class DecodeBlock:
                                    norm_w=self.W.attn_norm)
         return hc_post(self._attend(xn, positions), x, post, comb)
 
-    def _attend(self, xn, positions):
+    def _attend(self, xn, positions, aux=None):
         d, W, c = self.dims, self.W, self.cache
         b = xn.shape[0]
         pos = positions.to(torch.int32).contiguous()
@@ -228,7 +230,11 @@ class DecodeBlock:
                                rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(i_kv, i_sc),
                                key_image=(*c.key_image, c.max_comp))
         q_idx = rope(qi.view(b, d.idx_heads, d.idx_dim), pos, self.freqs, d.rope_dim)
-        o = decode_attention(c, qraw, q_idx, w_idx, W.sinks, pos, self.top_k, freqs=self.freqs)
+        idx_buf = None
+        if aux is not None:
+            idx_buf = torch.empty((b, self.top_k), dtype=torch.int32, device=xn.device)
+            aux.update(q_idx=q_idx, w_idx=w_idx, idx=idx_buf)
+        o = decode_attention(c, qraw, q_idx, w_idx, W.sinks, pos, self.top_k, freqs=self.freqs, idx_buf=idx_buf)
         return o_grouped(o.reshape(b, -1), W.wo_a, W.wo_b)
 
 

@@ -145,12 +145,14 @@ def prefill_layer_ref(x, W, top_k=512, window=128, ratio=4, heads=64, head_dim=5
 
 
 def decode_block_ref(state, W, x, positions, top_k=512, window=128, ratio=4, heads=64, head_dim=512, idx_heads=64,
-                     idx_dim=128, rope_dim=64, groups=8, act_quant=False):
+                     idx_dim=128, rope_dim=64, groups=8, act_quant=False, indexer_inputs=None, aux=None):
     """One decode token per sequence on host copies of the cache (oracle/v4_fast.py:82-122,
     oracle/decode_engine.py:96-105). `state` = dict(pool, win_base, comp_rows(b, j), k_idx, ring_kv, ring_score,
     ring_k, ring_s) and is updated in place. Returns out [b, dim]. With act_quant the token's kv row and
     the emitted compressed rows take the fp8 act-quant simulation on their nope dims before they are
-    cached (oracle/decode_engine.py:82, 105)."""
+    cached (oracle/decode_engine.py:82, 105). indexer_inputs=(q_idx after RoPE [b, 64, 128], w_idx [b, 64],
+    k_idx [b, n, 128]) lets a test select on given indexer inputs (the rest of the block stays the
+    oracle's); `aux` (a dict) receives the attention index lists under "idx"."""
     from .quant_ref import act_quant_rows
     from .compressor_ref import decode_ring_step
     from .mla_ref import o_grouped
@@ -194,8 +196,14 @@ def decode_block_ref(state, W, x, positions, top_k=512, window=128, ratio=4, hea
         if key is not None:
             state["k_idx"][i, (p + 1) // ratio - 1] = key
         q_idx[i] = rope_at(q_idx[i][None], torch.tensor([p]), f, rope_dim)[0]
-    o = decode_attention_ref(state["pool"], state["win_base"], state["comp_rows"], state["k_idx"], qraw, q_idx, w_idx,
-                             W.sinks, positions, top_k, f, window=window, ratio=ratio, scale=head_dim ** -0.5)
+    keys = state["k_idx"]
+    if indexer_inputs is not None:
+        q_idx, w_idx, keys = indexer_inputs
+    o, idx = decode_attention_ref(state["pool"], state["win_base"], state["comp_rows"], keys, qraw, q_idx, w_idx,
+                                  W.sinks, positions, top_k, f, window=window, ratio=ratio, scale=head_dim ** -0.5,
+                                  return_indices=True)
+    if aux is not None:
+        aux["idx"] = idx
     return o_grouped(o.reshape(b, -1), _w(W.wo_a), _w(W.wo_b), groups=groups)
 
 
