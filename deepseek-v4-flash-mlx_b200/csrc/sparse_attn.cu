@@ -693,6 +693,9 @@ DSV4_ERROR_READER(sparse_attn)
 using namespace dsv4;
 
 int dsv4_sparse_attn_tc(const dsv4_sparse_attn_params* p, int splits, float* part, void* stream);
+int dsv4_sparse_attn_hg(const dsv4_sparse_attn_params* p, int splits, void* stream);
+int dsv4_hg_splits(const dsv4_sparse_attn_params* p);
+bool dsv4_hg_cluster_fits(int splits);
 
 // tcgen05 kernel: 64 heads, bf16 q (or the fused prologue, which writes bf16 q), 128-row tiles,
 // one CTA per (query, split). The plan (kernel and split count) is made in one place, for the
@@ -704,6 +707,7 @@ struct AttnPlan {
   bool tc;
   int splits;
   bool cluster;  // mma.sync kernel: the splits of a query merge inside a cluster (no partials in HBM)
+  bool hg;       // the head-group decode kernel (16 heads per CTA, row splits merged in a cluster)
 };
 
 // whether `splits` CTAs of the mma.sync kernel (one per SM by shared memory) can run as one cluster
@@ -767,16 +771,21 @@ static int tc_splits(const dsv4_sparse_attn_params* p) {
 constexpr int64_t TC_MIN_QUERIES = 16;
 static AttnPlan plan_attention(const dsv4_sparse_attn_params* p) {
   const bool tc = p->kernel == 2 || (p->kernel == 0 && tc_shape_ok(p) && p->s >= TC_MIN_QUERIES);
-  if (tc && tc_shape_ok(p)) return {true, tc_splits(p), false};
+  if (tc && tc_shape_ok(p)) return {true, tc_splits(p), false, false};
+  // decode-sized calls: the head-group kernel, when its row splits fit in one cluster
+  if (p->kernel == 3 || (p->kernel == 0 && p->s < TC_MIN_QUERIES)) {
+    const int sp = dsv4_hg_splits(p);
+    if (dsv4_hg_cluster_fits(sp)) return {false, sp, sp > 1, true};
+  }
   const int sp = sa::choose_splits(p);
-  return {false, sp, sp > 1 && cluster_fits(sp)};
+  return {false, sp, sp > 1 && cluster_fits(sp), false};
 }
 
 // workspace: [split partials (O, m, l)] [bf16 q after the fused norm/rope pre-pass]
 static size_t partial_bytes(const dsv4_sparse_attn_params* p) {
   const AttnPlan pl = plan_attention(p);
   const int splits = pl.splits;
-  if (splits <= 1 || pl.cluster) return 0;
+  if (splits <= 1 || pl.cluster || pl.hg) return 0;
   const int hblocks = (p->h + sa::HB - 1) / sa::HB;
   const int64_t units = p->s * hblocks * splits;
   return static_cast<size_t>(units) * (sa::HB * sa::D + sa::HB * 2) * sizeof(float);
@@ -785,7 +794,7 @@ static size_t partial_bytes(const dsv4_sparse_attn_params* p) {
 extern "C" size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p) {
   if (!p || p->s <= 0 || p->h <= 0 || (p->t <= 0 && p->win_base == nullptr)) return 0;
   size_t bytes = (partial_bytes(p) + 255) / 256 * 256;
-  if (p->q_norm_rope) bytes += static_cast<size_t>(p->s) * p->h * p->d * 2;
+  if (p->q_norm_rope && !plan_attention(p).hg) bytes += static_cast<size_t>(p->s) * p->h * p->d * 2;
   return bytes;
 }
 
@@ -808,7 +817,7 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
   DSV4_CHECK_ARG(!p->q_norm_rope || p->rope_freqs != nullptr,
                  "dsv4_sparse_attn: the fused q norm/rope needs rope_freqs, positions and rope_dim");
   DSV4_CHECK_ARG(p->s * 64 < (int64_t)INT32_MAX, "dsv4_sparse_attn: too many queries per call");
-  DSV4_CHECK_ARG(p->kernel >= 0 && p->kernel <= 2 && (p->kernel != 2 || tc_shape_ok(p)),
+  DSV4_CHECK_ARG(p->kernel >= 0 && p->kernel <= 3 && (p->kernel != 2 || tc_shape_ok(p)),
                  "dsv4_sparse_attn: kernel %d unavailable for h=%d q_dtype=%d", p->kernel, p->h, p->q_dtype);
   if (p->s == 0) return DSV4_OK;
   sa::Params P;
@@ -842,6 +851,7 @@ extern "C" int dsv4_sparse_attn(const dsv4_sparse_attn_params* p, void* stream) 
     set_error("dsv4_sparse_attn: workspace of %zu bytes needed, %zu given", need, p->workspace_bytes);
     return DSV4_ERR_WORKSPACE;
   }
+  if (plan.hg) return dsv4_sparse_attn_hg(p, plan.splits, stream);  // q prologue fused in the kernel
   if (P.splits > 1 && !P.cluster) P.part = reinterpret_cast<float*>(p->workspace);
   if (p->q_norm_rope) {
     // weightless per-head norm + rope of q into bf16 scratch, then attention reads it

@@ -17,7 +17,8 @@ HBM and is addressed by index:
 launch, the indexer scores, the top-k selection straight into the attention index list (mapped
 through the block table), sparse attention — whose window tiles, computed from the positions, run
 while the selection finishes — with the inverse RoPE fused into its epilogue, and the split-K merge;
-q's per-head norm + RoPE runs on a side stream beside the indexer.
+q's per-head norm + RoPE is fused into the attention kernel for decode-sized batches (below 16
+sequences), else it runs on a side stream beside the indexer.
 """
 import ctypes
 import math
@@ -27,7 +28,11 @@ import torch
 from . import _lib as L
 from .indexer import build_key_image, indexer_topk_into, key_image_buffers
 from .norm_rope import norm_rope, rope_freqs
-from .sparse_attn import sparse_attn_decode, sparse_attn_rope
+from .sparse_attn import _sparse_attn_op, sparse_attn_decode, sparse_attn_rope
+
+# below this batch the decode step fuses q's norm + RoPE into the attention kernel (the head-group
+# kernel's prologue); from it on the norm runs on a side stream beside the indexer
+FUSED_Q_MAX_BATCH = 16
 
 
 class SparseMLACache:
@@ -200,12 +205,20 @@ def _decode_attention_op(kv_pool: torch.Tensor, k_idx: torch.Tensor, block_table
                          top_k: int, scale: float, window: int, ratio: int, page: int, comp_base: int,
                          out_dtype: torch.dtype) -> torch.Tensor:
     b = q.shape[0]
+    image = (key_image, key_inv, key_norm_max) if key_image is not None else None
+    if b < FUSED_Q_MAX_BATCH:
+        # decode-sized batches: one stream, three kernels chained by programmatic dependent launch
+        # (scores, selection, attention); q's norm + RoPE is fused into the attention kernel
+        indexer_topk_into(idx_buf.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
+                          k_idx, top_k, positions.view(b, 1), ratio, out_col=0, out_offset=comp_base,
+                          block_table=block_table, page=page, key_image=image)
+        return _sparse_attn_op(q, kv_pool, sink, idx_buf, float(scale), out_dtype, freqs, positions, 64, 0, True,
+                               1e-6, win_base, int(window), False, 0)
     main = torch.cuda.current_stream(q.device)
     side = _side_stream(q.device)
     side.wait_stream(main)
     with torch.cuda.stream(side):          # q's norm + rope runs beside the indexer
         qr = norm_rope(q, positions, freqs, weight=None)
-    image = (key_image, key_inv, key_norm_max) if key_image is not None else None
     indexer_topk_into(idx_buf.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
                       k_idx, top_k, positions.view(b, 1), ratio, out_col=0, out_offset=comp_base,
                       block_table=block_table, page=page, key_image=image)

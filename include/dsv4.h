@@ -108,11 +108,14 @@ typedef struct {
   int32_t window;
   int32_t window_linear;
   /* kernel choice: 0 = automatic (the tcgen05 kernel, 128-row tiles, split-K over tile ranges, for
-   * calls of at least 16 queries with 64 heads and bf16 q or the fused q prologue; the mma.sync
-   * split-K kernel otherwise), 1 = the mma.sync kernel, 2 = the tcgen05 kernel (64 heads and bf16 q
-   * or the fused prologue, else DSV4_ERR_INVALID_ARGUMENT). Both compute the same function (num_splits
-   * counts 64-row tiles for the first, 128-row tiles for the second); the choice is for tests and
-   * measurements. */
+   * calls of at least 16 queries with 64 heads and bf16 q or the fused q prologue; below 16 queries
+   * the head-group kernel, else the mma.sync split-K kernel), 1 = the mma.sync kernel (64 heads per
+   * CTA), 2 = the tcgen05 kernel (64 heads and bf16 q or the fused prologue, else
+   * DSV4_ERR_INVALID_ARGUMENT), 3 = the head-group decode kernel (16 heads per CTA, the 64-row tiles of
+   * a query split over up to 16 CTAs that merge as one thread-block cluster; the q prologue fused in
+   * the kernel; falls back to 1 where such a cluster cannot be scheduled). All compute the same
+   * function (num_splits counts 64-row tiles for 1 and 3, 128-row tiles for 2); the choice is for
+   * tests and measurements. */
   int32_t kernel;
 } dsv4_sparse_attn_params;
 
