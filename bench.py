@@ -629,7 +629,7 @@ def bench_decode(env, name, headline):
     # ---- dominant-kernel timing: each kernel of the step, alone, over the replica rotation
     kern = kernel_times(cases, runners, stream, min(max(K, 20), 4 * R))
     hbm, _, _, peak_kind = _peaks()
-    top = max(kern, key=lambda k: kern[k]["us"])
+    top = max((k for k in kern if not k.startswith("alt:")), key=lambda k: kern[k]["us"])
     kb = kern[top]
     achieved = kb["bytes"] / (kb["us"] * 1e-6) / 1e9
     roofline = {"bound": "hbm", "kernel": top, "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -684,6 +684,14 @@ def kernel_times(cases, runners, stream, n):
                                                       win_base=cases[i].cache.win_base, window=128),
                         b * ((128 + top_k) * 512 * 2 + top_k * 4 + 64 * 512 * 2 * 2)),
     }
+    # the tensor-core filter + exact band (mode 2) on the same call, for comparison (not in the step)
+    funcs["alt:indexer_topk_mode2"] = (
+        lambda i: IX.indexer_topk_into(runners[i].idx.view(b, 1, -1), runners[i].q_idx.view(b, 1, 64, 128),
+                                       runners[i].w_idx.view(b, 1, 64), cases[i].cache.k_idx, top_k,
+                                       runners[i].positions.view(b, 1), 4, out_col=0,
+                                       out_offset=cases[i].cache.comp_base, block_table=cases[i].cache.block_table,
+                                       page=cases[i].cache.page, key_image=cases[i].cache.key_image, mode=2),
+        funcs["indexer_topk"][1])
     out = {}
     for name, (fn, nbytes) in funcs.items():
         with torch.cuda.stream(stream):

@@ -309,17 +309,25 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
     if (tile + 1 < tile_end) gather_tile(P, sm, buf ^ 1, qi, (tile + 1) * BN, t_end);
     const uint32_t kv_s = static_cast<uint32_t>(__cvta_generic_to_shared(sm.kv[buf]));
 
-    // ---- S = Q K^T: warp w takes gathered rows [8w, 8w + 8), all 16 heads, K = 512 ----
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-    for (int kc = 0; kc < D / 16; kc += 2) {
-      uint32_t b[4], a0[4], a1[4];
-      ldsm_x4(kv_s + swz(warp * 8 + (lane & 7), kc * 2 + (lane >> 3), ROW_BYTES), b[0], b[1], b[2], b[3]);
-      ldsm_x4(q_s + swz(lane & 15, kc * 2 + (lane >> 4), ROW_BYTES), a0[0], a0[1], a0[2], a0[3]);
-      ldsm_x4(q_s + swz(lane & 15, kc * 2 + 2 + (lane >> 4), ROW_BYTES), a1[0], a1[1], a1[2], a1[3]);
-      mma_bf16(s, a0[0], a0[1], a0[2], a0[3], b[0], b[1]);
-      mma_bf16(s, a1[0], a1[1], a1[2], a1[3], b[2], b[3]);
+    // ---- S = Q K^T: warp w takes gathered rows [8w, 8w + 8), all 16 heads, K = 512; four
+    // accumulators (k steps mod 4) keep four independent MMA chains in flight ----
+    float sacc[4][4] = {};
+#pragma unroll 2
+    for (int kc = 0; kc < D / 16; kc += 4) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int k0 = kc + 2 * half;
+        uint32_t b[4], a0[4], a1[4];
+        ldsm_x4(kv_s + swz(warp * 8 + (lane & 7), k0 * 2 + (lane >> 3), ROW_BYTES), b[0], b[1], b[2], b[3]);
+        ldsm_x4(q_s + swz(lane & 15, k0 * 2 + (lane >> 4), ROW_BYTES), a0[0], a0[1], a0[2], a0[3]);
+        ldsm_x4(q_s + swz(lane & 15, k0 * 2 + 2 + (lane >> 4), ROW_BYTES), a1[0], a1[1], a1[2], a1[3]);
+        mma_bf16(sacc[2 * half], a0[0], a0[1], a0[2], a0[3], b[0], b[1]);
+        mma_bf16(sacc[2 * half + 1], a1[0], a1[1], a1[2], a1[3], b[2], b[3]);
+      }
     }
+    float s[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) s[c] = (sacc[0][c] + sacc[1][c]) + (sacc[2][c] + sacc[3][c]);
     // s[0..1]: head lane/4, rows 8w + 2(lane%4) + {0,1}; s[2..3]: head lane/4 + 8
     const int rbase = warp * 8 + (lane & 3) * 2;
     const bool v0 = sm.rowidx[buf][rbase] >= 0, v1 = sm.rowidx[buf][rbase + 1] >= 0;
@@ -457,15 +465,21 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
   const int f0 = split * chunk, f1 = min(NF4, f0 + chunk);
   for (int f = f0 + tid; f < f1; f += THREADS) {
     const int hh = f / (D / 4), d = (f % (D / 4)) * 4;
+    // every split's partial is requested before the first is used (the peer loads overlap)
+    float4 v[MAX_SPLITS];
+#pragma unroll
+    for (int sp = 0; sp < MAX_SPLITS; ++sp)
+      if (sp < S) v[sp] = dsmem_f32x4(os_s + (hh * OSTRIDE + d) * 4, sp);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp = 0; sp < S; ++sp) {
-      const float4 v = dsmem_f32x4(os_s + (hh * OSTRIDE + d) * 4, sp);
-      const float w = sm.wts[hh][sp];
-      acc.x = fmaf(w, v.x, acc.x);
-      acc.y = fmaf(w, v.y, acc.y);
-      acc.z = fmaf(w, v.z, acc.z);
-      acc.w = fmaf(w, v.w, acc.w);
-    }
+#pragma unroll
+    for (int sp = 0; sp < MAX_SPLITS; ++sp)
+      if (sp < S) {
+        const float w = sm.wts[hh][sp];
+        acc.x = fmaf(w, v[sp].x, acc.x);
+        acc.y = fmaf(w, v[sp].y, acc.y);
+        acc.z = fmaf(w, v[sp].z, acc.z);
+        acc.w = fmaf(w, v[sp].w, acc.w);
+      }
     const float iv = sm.inv[hh];
     write_out(P, qi, h0, hh, d, make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv), pos);
   }

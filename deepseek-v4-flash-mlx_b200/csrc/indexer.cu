@@ -81,20 +81,24 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
   const float* kg = P.k + static_cast<int64_t>(b) * P.k_batch_stride * DI;
   const uint32_t qs = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
   const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(sm.k));
-  for (int c = tid; c < HI * DI / 4; c += THREADS) {
-    const int r = c >> 5, ch = c & 31;
-    cp_async16(qs + (r * 32 + swz_chunk(r, ch)) * 16, qg + r * DI + ch * 4, true);
+  // four stages of 32 dims (eight 16-byte chunks of every q and key row; the swizzle keeps a
+  // stage's chunks within its group of eight), so the dot products start on the first 32 dims
+  // while the rest are in flight
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    for (int c = tid; c < HI * 8; c += THREADS) {
+      const int r = c >> 3, ch = g * 8 + (c & 7);
+      cp_async16(qs + (r * 32 + swz_chunk(r, ch)) * 16, qg + r * DI + ch * 4, true);
+    }
+    for (int c = tid; c < KT * 8; c += THREADS) {
+      const int r = c >> 3, ch = g * 8 + (c & 7);
+      const bool valid = (j0 + r) < nvis;
+      const float* src = kg + static_cast<int64_t>(valid ? j0 + r : 0) * DI + ch * 4;
+      cp_async16(ks + (r * 32 + swz_chunk(r, ch)) * 16, src, valid);
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
   }
-  for (int c = tid; c < KT * DI / 4; c += THREADS) {
-    const int r = c >> 5, ch = c & 31;
-    const bool valid = (j0 + r) < nvis;
-    const float* src = kg + static_cast<int64_t>(valid ? j0 + r : 0) * DI + ch * 4;
-    cp_async16(ks + (r * 32 + swz_chunk(r, ch)) * 16, src, valid);
-  }
-  asm volatile("cp.async.commit_group;\n" ::);
   if (tid < HI) sm.w[tid] = P.w[qrow * HI + tid];
-  asm volatile("cp.async.wait_group 0;\n" ::);
-  __syncthreads();
 
   const int hq = (warp << 1) | (lane >> 4), kq = lane & 15;
   float acc[4][4];
@@ -104,6 +108,15 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
     for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
 #pragma unroll 2
   for (int ch = 0; ch < DI / 4; ++ch) {
+    if ((ch & 7) == 0) {  // stage ch / 8 has landed (and w, before the first)
+      switch (ch >> 3) {
+        case 0: asm volatile("cp.async.wait_group 3;\n" ::); break;
+        case 1: asm volatile("cp.async.wait_group 2;\n" ::); break;
+        case 2: asm volatile("cp.async.wait_group 1;\n" ::); break;
+        default: asm volatile("cp.async.wait_group 0;\n" ::); break;
+      }
+      __syncthreads();
+    }
     float4 qv[4], kv[4];
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
@@ -1147,6 +1160,214 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
   }
 }
 
+// ---- selection for decode-sized calls (few query rows): one 1024-thread CTA per row ----------
+// The keys' order-preserving images are binned linearly over [min, max] of the visible keys (a
+// shift of key - min into 12 bits) instead of by their top 12 bits: the top bits of fp32 scores
+// put most keys of a row into a handful of bins (3 mantissa bits per binade), while the linear bins
+// leave a few keys in the boundary bin, which are then ranked directly by (key desc, index asc).
+// A boundary bin with more than LIN_CAND keys narrows the range to that bin and bins again; a range
+// of one value (equal scores) takes its kleft lowest indices. Same set as the oracle's sort, written
+// in ascending key order.
+constexpr int LIN_THREADS = 1024;
+constexpr int LIN_BINS = 4096;
+constexpr int LIN_CAND = 1024;
+constexpr int LIN_MAX_ROWS = 32;     // rows per call served by this kernel
+
+struct LinShared {
+  alignas(16) uint32_t hist[LIN_BINS];
+  unsigned long long cand[LIN_CAND];
+  uint32_t wa[LIN_THREADS / 32], wb[LIN_THREADS / 32];
+  uint32_t bin, kleft, count, ncand;
+  unsigned long long thr;
+  int32_t tau_idx;
+};
+
+// exclusive prefix sum over the 1024 threads (2 barriers, plus one before the scratch is reused)
+__device__ __forceinline__ uint32_t lin_scan(uint32_t v, LinShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) sh.wa[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t w = sh.wa[lane];
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    sh.wb[lane] = wi - w;
+  }
+  __syncthreads();
+  return sh.wb[warp] + incl - v;
+}
+
+template <int PER>
+__global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P) {
+  __shared__ LinShared sh;
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t qrow = blockIdx.x;
+  const int b = static_cast<int>(qrow / P.s);
+  const int j0 = tid * PER;
+  const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
+  const float* sc = P.scores + qrow * P.n_pad + j0;
+  uint32_t key[PER];
+  if ((P.n_pad & 3) == 0 && j0 + PER <= P.n_pad) {
+#pragma unroll
+    for (int e = 0; e < PER; e += 4) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(sc + e));
+      key[e] = ordered_bits(v.x);
+      key[e + 1] = ordered_bits(v.y);
+      key[e + 2] = ordered_bits(v.z);
+      key[e + 3] = ordered_bits(v.w);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < PER; ++e) key[e] = (j0 + e < P.n_pad) ? ordered_bits(__ldcg(sc + e)) : 0u;
+  }
+  const KeyMap km(P, b, j0, PER);
+  int32_t* out = P.out + qrow * P.out_stride + P.out_col;
+  const uint32_t k = static_cast<uint32_t>(P.top_k);
+  if (P.win_base != nullptr)
+    for (int c = tid; c < P.window; c += LIN_THREADS) out[c - P.window] = window_row(P, b, P.positions[qrow], c);
+  if (nvis <= P.top_k) {
+    for (int r = tid; r < P.top_k; r += LIN_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
+    return;
+  }
+  const int nv = max(0, min(PER, nvis - j0));  // this thread's visible keys; the rest never count
+
+  // min and max of the visible keys
+  uint32_t mn = 0xffffffffu, mx = 0u;
+#pragma unroll
+  for (int e = 0; e < PER; ++e)
+    if (e < nv) {
+      mn = min(mn, key[e]);
+      mx = max(mx, key[e]);
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if (lane == 0) {
+    sh.wa[warp] = mn;
+    sh.wb[warp] = mx;
+  }
+#pragma unroll
+  for (int i = tid; i < LIN_BINS; i += LIN_THREADS) sh.hist[i] = 0;
+  __syncthreads();
+  uint32_t lo = 0xffffffffu, hi = 0u;
+#pragma unroll 8
+  for (int w = 0; w < LIN_THREADS / 32; ++w) {
+    lo = min(lo, sh.wa[w]);
+    hi = max(hi, sh.wb[w]);
+  }
+  uint32_t kleft = k;
+  unsigned long long thr = 0;   // (key << 32) | ~index of the k-th largest: take every key >= it
+  bool found = false;
+  // each pass narrows [lo, hi] to the boundary bin (a 4096th of the range or less); at most 4 passes
+  // reach a single value
+  for (int pass = 0; pass < 4 && !found && lo != hi; ++pass) {
+    const uint32_t range = hi - lo;
+    const int bits = 32 - __clz(range);
+    const int shift = bits > 12 ? bits - 12 : 0;   // (key - lo) >> shift < 4096
+    if (pass > 0) {
+      __syncthreads();   // every thread is done with the previous pass's histogram
+#pragma unroll
+      for (int i = tid; i < LIN_BINS; i += LIN_THREADS) sh.hist[i] = 0;
+      __syncthreads();
+    }
+#pragma unroll
+    for (int e = 0; e < PER; ++e)
+      if (e < nv && key[e] >= lo && key[e] <= hi) atomicAdd(&sh.hist[(key[e] - lo) >> shift], 1u);
+    __syncthreads();
+    // boundary bin: thread t owns bins 4095 - 4t .. 4092 - 4t (highest first)
+    const uint4 h4 = *reinterpret_cast<const uint4*>(&sh.hist[LIN_BINS - 4 * (tid + 1)]);
+    const uint32_t c[4] = {h4.w, h4.z, h4.y, h4.x};
+    const uint32_t tot = c[0] + c[1] + c[2] + c[3];
+    const uint32_t before = lin_scan(tot, sh);
+    if (before < kleft && kleft <= before + tot) {
+      uint32_t run = before;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (run + c[e] >= kleft) {
+          sh.bin = LIN_BINS - 1 - (4 * tid + e);
+          sh.kleft = kleft - run;
+          sh.count = c[e];
+          break;
+        }
+        run += c[e];
+      }
+    }
+    if (tid == 0) sh.ncand = 0;
+    __syncthreads();
+    const uint32_t bin = sh.bin, cnt = sh.count;
+    kleft = sh.kleft;
+    const uint32_t blo = lo + (bin << shift);
+    const uint32_t bhi = static_cast<uint32_t>(
+        min(static_cast<unsigned long long>(hi), static_cast<unsigned long long>(blo) + ((1ull << shift) - 1ull)));
+    if (cnt <= LIN_CAND) {
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if (e < nv && key[e] >= blo && key[e] <= bhi) {
+          const uint32_t slot = atomicAdd(&sh.ncand, 1u);
+          sh.cand[slot] = (static_cast<unsigned long long>(key[e]) << 32) |
+                          static_cast<uint32_t>(~static_cast<uint32_t>(j0 + e));
+        }
+      __syncthreads();
+      if (tid < static_cast<int>(cnt)) {
+        const unsigned long long v = sh.cand[tid];
+        uint32_t rank = 0;
+        for (uint32_t m = 0; m < cnt; ++m) rank += sh.cand[m] > v;
+        if (rank == kleft - 1) sh.thr = v;
+      }
+      __syncthreads();
+      thr = sh.thr;
+      found = true;
+    } else {
+      lo = blo;
+      hi = bhi;
+    }
+  }
+  if (!found) {
+    // [lo, hi] is one value: every key above it is taken and the kleft lowest indices equal to it
+    uint32_t ne = 0;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) ne += (e < nv && key[e] == lo);
+    __syncthreads();
+    const uint32_t before = lin_scan(ne, sh);
+    if (before < kleft && kleft <= before + ne) {
+      uint32_t seen = before;
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        if (e < nv && key[e] == lo && ++seen == kleft) sh.tau_idx = j0 + e;
+    }
+    __syncthreads();
+    thr = (static_cast<unsigned long long>(lo) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(sh.tau_idx));
+  }
+  uint32_t take = 0;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const unsigned long long v =
+        (static_cast<unsigned long long>(key[e]) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(j0 + e));
+    take |= static_cast<uint32_t>(e < nv && v >= thr) << e;
+  }
+  __syncthreads();   // the scan scratch is free
+  uint32_t pos = lin_scan(static_cast<uint32_t>(__popc(take)), sh);
+  while (take) {  // the taken keys in ascending order
+    const int e = __ffs(take) - 1;
+    take &= take - 1;
+    out[pos++] = km.map(P, b, j0 + e);
+  }
+}
+
 __global__ void decode_window_kernel(int32_t batch, int32_t window, const int32_t* positions,
                                      const int64_t* win_base, int32_t* out, int32_t out_stride) {
   const int b = blockIdx.x;
@@ -1183,6 +1404,12 @@ inline cudaError_t launch_scores(const ScoreParams& S, cudaStream_t st) {
 // the register-resident kernel up to 16384 visible keys, the shared-memory one above
 inline cudaError_t launch_select(const SelectParams& L, unsigned rows, cudaStream_t st) {
   const dim3 g(rows), blk(SEL_THREADS);
+  if (!L.refine && rows <= static_cast<unsigned>(LIN_MAX_ROWS) && L.n_keys <= LIN_THREADS * 16) {
+    const dim3 lb(LIN_THREADS);
+    if (L.n_keys <= LIN_THREADS * 4) return launch_pdl(select_lin_kernel<4>, g, lb, 0, st, L);
+    if (L.n_keys <= LIN_THREADS * 8) return launch_pdl(select_lin_kernel<8>, g, lb, 0, st, L);
+    return launch_pdl(select_lin_kernel<16>, g, lb, 0, st, L);
+  }
   if (L.refine) {
     constexpr size_t rsm = sizeof(RefineSmem);
     static PerDeviceOnce rattr;
