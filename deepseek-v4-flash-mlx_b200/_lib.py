@@ -28,7 +28,7 @@ class SparseAttnParams(ctypes.Structure):
                 ("rope_freqs", vp), ("positions", vp), ("rope_dim", i32), ("num_splits", i32),
                 ("workspace", vp), ("workspace_bytes", sz), ("q_norm_rope", i32), ("q_eps", f32),
                 ("win_base", vp), ("win_stride", i32), ("window", i32), ("window_linear", i32),
-                ("kernel", i32)]
+                ("kernel", i32), ("pre_wait", i32)]
 
 
 class RmsNormParams(ctypes.Structure):

@@ -6,8 +6,8 @@
 //   * heads: 16 per CTA (the MMA M dimension), h / 16 head groups;
 //   * rows: the query's list [window | selected] in 64-row tiles, split over up to 16 CTAs.
 // The row splits of one (query, head group) run as one thread-block cluster and merge their
-// unnormalised partials (O, m, l) through distributed shared memory: with 16 heads a CTA reads
-// 16 x 512 x 4 B / splits of partial O from each peer, a quarter of what a 64-head CTA would read.
+// unnormalised partials (O, m, l) through distributed shared memory: each split finalises a slice of
+// the 16 x 512 outputs, reading every split's partial of it (and their m, l) in one round of peer loads.
 //
 // Per CTA: q of its 16 heads is staged as bf16 (with the fused prologue: the weightless per-head
 // RMS norm and the RoPE of the last rope_dim dims, in the arithmetic of the norm_rope kernel), the
@@ -15,8 +15,10 @@
 // bf16 mma.sync m16n8k16 with fp32 accumulation, the softmax is online in the exp2 domain. The
 // sink enters only the denominator and an all-masked query yields NaN, as in the reference.
 //
-// Programmatic dependent launch: the kernel waits for the previous kernel before it reads any
-// global memory (q, the window rows and the selected indices are all written earlier in a step).
+// Programmatic dependent launch: by default the kernel waits for the previous kernel before it
+// reads any global memory. With pre_wait (the decode step: scores, selection, attention, where the
+// score kernel waits for all earlier work before the other two launch) it stages q and computes the
+// window tiles while the selection runs, and waits only before it reads the selected indices.
 #include "common.cuh"
 
 namespace dsv4 {
@@ -40,9 +42,10 @@ struct Smem {
   float m_run[HG];
   float l_run[HG];
   float alpha[HG];
-  float wts[HG][MAX_SPLITS];
   float inv[HG];
+  float rope_c[32], rope_s[32];  // cos / sin of the query position times each rope pair's frequency
   int32_t rowidx[2][BN];
+  float2 ml[HG];                 // (m, l) per head, read by the cluster merge
 };
 static_assert(sizeof(float) * HG * OSTRIDE <= 2 * BN * ROW_BYTES, "partial O fits in the kv buffers");
 
@@ -63,6 +66,7 @@ struct Params {
   float q_eps;
   const int64_t* win_base;
   int win_stride, window, window_linear;
+  int pre_wait;
 };
 
 __device__ __forceinline__ uint32_t swz(int r, int c, int row_bytes) {
@@ -108,6 +112,11 @@ __device__ __forceinline__ float dsmem_f32(uint32_t a, int rank) {
   asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(dsmem_addr(a, rank)) : "memory");
   return v;
 }
+__device__ __forceinline__ float2 dsmem_f32x2(uint32_t a, int rank) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0,%1}, [%2];\n" : "=f"(v.x), "=f"(v.y) : "r"(dsmem_addr(a, rank)) : "memory");
+  return v;
+}
 __device__ __forceinline__ float4 dsmem_f32x4(uint32_t a, int rank) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];\n"
@@ -118,6 +127,11 @@ __device__ __forceinline__ float4 dsmem_f32x4(uint32_t a, int rank) {
 }
 
 __device__ __forceinline__ int list_len(const Params& P) { return (P.win_base ? P.window : 0) + P.t; }
+
+// whether tile `tile` holds explicit indices (written by the kernel launched before this one)
+__device__ __forceinline__ bool tile_needs_idx(const Params& P, int tile) {
+  return P.win_base == nullptr || (tile + 1) * BN > P.window;
+}
 
 // pool row of logical entry u of query qi (-1 = masked): implicit window rows, then idx
 __device__ __forceinline__ int64_t list_row(const Params& P, int64_t qi, int u) {
@@ -143,123 +157,141 @@ __device__ __forceinline__ int64_t list_row(const Params& P, int64_t qi, int u) 
   return __ldg(reinterpret_cast<const int32_t*>(P.idx) + qi * P.t + u);
 }
 
-// gather rows [t0, t0 + BN) of the list into buffer `buf`: thread = (16-byte chunk, 16 rows)
-__device__ __forceinline__ void gather_tile(const Params& P, Smem& sm, int buf, int64_t qi, int t0, int t_end) {
-  const int tid = threadIdx.x;
-  constexpr int RPT = BN / (THREADS / 64);  // 16 rows per thread
-  const int chunk = tid & 63, r0 = tid >> 6;
-  int32_t rows[RPT];
-#pragma unroll
-  for (int i = 0; i < RPT; ++i) {
-    const int t = t0 + r0 + i * (THREADS / 64);
+// pool rows of list entries [t0, t0 + BN) into sm.rowidx[buf]: thread r < 64 takes entry t0 + r
+// (-1 masked; an index past the pool is recorded in the device error word and masked)
+__device__ __forceinline__ void load_rows(const Params& P, Smem& sm, int buf, int64_t qi, int t0, int t_end) {
+  const int r = threadIdx.x;
+  if (r < BN) {
+    const int t = t0 + r;
     int64_t v = t < t_end ? list_row(P, qi, t) : -1;
     if (v >= P.n) {
-      if (chunk == 0) raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
+      raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
       v = -1;
     }
-    rows[i] = static_cast<int32_t>(v < 0 ? -1 : v);
+    sm.rowidx[buf][r] = static_cast<int32_t>(v < 0 ? -1 : v);
   }
+}
+
+// the gather of buffer `buf` (its rows in sm.rowidx[buf], after a barrier): thread = (16-byte chunk,
+// 16 rows); masked rows are zero-filled
+__device__ __forceinline__ void issue_tile(const Params& P, Smem& sm, int buf) {
+  const int tid = threadIdx.x;
+  const int chunk = tid & 63, r0 = tid >> 6;
   const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(sm.kv[buf]));
 #pragma unroll
-  for (int i = 0; i < RPT; ++i) {
+  for (int i = 0; i < BN / (THREADS / 64); ++i) {
     const int rr = r0 + i * (THREADS / 64);
-    const bool valid = rows[i] >= 0;
-    cp_async16(base + swz(rr, chunk, ROW_BYTES), P.kv + static_cast<int64_t>(valid ? rows[i] : 0) * D + chunk * 8,
+    const int32_t row = sm.rowidx[buf][rr];
+    const bool valid = row >= 0;
+    cp_async16(base + swz(rr, chunk, ROW_BYTES), P.kv + static_cast<int64_t>(valid ? row : 0) * D + chunk * 8,
                valid);
-    if (chunk == 0) sm.rowidx[buf][rr] = rows[i];
   }
   cp_async_commit();
 }
 
-// q of heads [h0, h0 + 16) of query qi as bf16 in sm.q. With the fused prologue each warp takes two
-// heads, a lane 16 consecutive dims: sum of squares (lane-sequential fmaf, then the warp butterfly),
-// x * rsqrt(ss / 512 + eps), RoPE of the last rope_dim dims at positions[qi] (the norm_rope kernel's
-// arithmetic, so both give the same bf16 q).
-__device__ __forceinline__ void stage_q(const Params& P, Smem& sm, int64_t qi, int h0) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t qbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
-  if (!P.q_norm_rope && P.q_dtype == DSV4_BF16) {
-    const __nv_bfloat16* qg = reinterpret_cast<const __nv_bfloat16*>(P.q) + (qi * P.h + h0) * D;
+constexpr int QPER = D / 32;               // q dims per lane
+constexpr int QHPW = HG / (THREADS / 32);  // q heads per warp
+
+// q of heads [h0, h0 + 16) of query qi. bf16 q goes straight to sm.q by cp.async (its own commit
+// group), each warp copying the two heads it later finishes; fp32 q is loaded into registers.
+__device__ __forceinline__ void load_q(const Params& P, Smem& sm, int64_t qi, int h0, float (&v)[QHPW][QPER]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (P.q_dtype == DSV4_BF16) {
+    const uint32_t qbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
 #pragma unroll
-    for (int c = tid; c < HG * 64; c += THREADS) {
-      const int hh = c >> 6, ch = c & 63;
-      cp_async16(qbase + swz(hh, ch, ROW_BYTES), qg + hh * D + ch * 8, true);
+    for (int j = 0; j < QHPW; ++j) {
+      const int hh = warp * QHPW + j;
+      const __nv_bfloat16* qg = reinterpret_cast<const __nv_bfloat16*>(P.q) + (qi * P.h + h0 + hh) * D;
+#pragma unroll
+      for (int c = lane; c < 64; c += 32) cp_async16(qbase + swz(hh, c, ROW_BYTES), qg + c * 8, true);
     }
     cp_async_commit();
     return;
   }
-  constexpr int PER = D / 32;  // 16
 #pragma unroll
-  for (int j = 0; j < HG / (THREADS / 32); ++j) {
-    const int hh = warp * (HG / (THREADS / 32)) + j;
-    const int64_t src = (qi * P.h + h0 + hh) * D + lane * PER;
-    float v[PER];
-    if (P.q_dtype == DSV4_BF16) {
-      const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(P.q) + src;
+  for (int j = 0; j < QHPW; ++j) {
+    const float* x = reinterpret_cast<const float*>(P.q) + (qi * P.h + h0 + warp * QHPW + j) * D + lane * QPER;
 #pragma unroll
-      for (int e = 0; e < PER; e += 8) {
-        const uint4 u = *reinterpret_cast<const uint4*>(x + e);
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+    for (int e = 0; e < QPER; e += 4) {
+      const float4 f = *reinterpret_cast<const float4*>(x + e);
+      v[j][e] = f.x;
+      v[j][e + 1] = f.y;
+      v[j][e + 2] = f.z;
+      v[j][e + 3] = f.w;
+    }
+  }
+}
+
+// the rest of q's staging (after the barrier that publishes the RoPE table, with the bf16 copy's
+// group complete): with the fused prologue the weightless per-head RMS norm (lane-sequential fmaf
+// sum of squares, the warp butterfly, x * rsqrt(ss / 512 + eps)) and the RoPE of the last rope_dim
+// dims, in the norm_rope kernel's arithmetic, so both give the same bf16 q; the bf16 rows then
+// (over)write sm.q, each warp its own two heads
+__device__ __forceinline__ void finish_q(const Params& P, Smem& sm, float (&v)[QHPW][QPER]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (!P.q_norm_rope && P.q_dtype == DSV4_BF16) return;  // staged as it is
+  const uint32_t qbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
+  if (P.q_dtype == DSV4_BF16) {  // this warp's copies have landed (wait_group + syncwarp by the caller)
+#pragma unroll
+    for (int j = 0; j < QHPW; ++j) {
+      const int hh = warp * QHPW + j;
+#pragma unroll
+      for (int e = 0; e < QPER; e += 8) {
+        uint32_t r0, r1, r2, r3;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                     : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                     : "r"(qbase + swz(hh, (lane * QPER + e) >> 3, ROW_BYTES)));
+        const uint32_t w[4] = {r0, r1, r2, r3};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const float2 f = __bfloat1622float2(h2[k]);
-          v[e + 2 * k] = f.x;
-          v[e + 2 * k + 1] = f.y;
+          v[j][e + 2 * k] = __uint_as_float(w[k] << 16);
+          v[j][e + 2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
         }
       }
-    } else {
-      const float* x = reinterpret_cast<const float*>(P.q) + src;
-#pragma unroll
-      for (int e = 0; e < PER; e += 4) {
-        const float4 f = *reinterpret_cast<const float4*>(x + e);
-        v[e] = f.x;
-        v[e + 1] = f.y;
-        v[e + 2] = f.z;
-        v[e + 3] = f.w;
-      }
     }
+    __syncwarp();  // every lane has read its chunks before any lane overwrites them
+  }
+  const int rope_lo = D - P.rope_dim;
+#pragma unroll
+  for (int j = 0; j < QHPW; ++j) {
     if (P.q_norm_rope) {
       float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < PER; ++e) ss = fmaf(v[e], v[e], ss);
+      for (int e = 0; e < QPER; ++e) ss = fmaf(v[j][e], v[j][e], ss);
       ss = warp_sum(ss);
       const float r = rsqrtf(ss / static_cast<float>(D) + P.q_eps);
 #pragma unroll
-      for (int e = 0; e < PER; ++e) v[e] = v[e] * r;
-      const int rope_lo = D - P.rope_dim;
-      if (lane * PER + PER > rope_lo) {
-        const int pos = P.positions[qi];
+      for (int e = 0; e < QPER; ++e) v[j][e] = v[j][e] * r;
+      if (lane * QPER + QPER > rope_lo) {
 #pragma unroll
-        for (int e = 0; e < PER; e += 2) {
-          const int d = lane * PER + e;
+        for (int e = 0; e < QPER; e += 2) {
+          const int d = lane * QPER + e;
           if (d >= rope_lo) {
-            float c, s;
-            rope_cos_sin(pos, P.rope_freqs[(d - rope_lo) >> 1], &c, &s);
-            rotate_pair(v[e], v[e + 1], c, s, false, &v[e], &v[e + 1]);
+            const int f = (d - rope_lo) >> 1;
+            rotate_pair(v[j][e], v[j][e + 1], sm.rope_c[f], sm.rope_s[f], false, &v[j][e], &v[j][e + 1]);
           }
         }
       }
     }
+    const int hh = warp * QHPW + j;
 #pragma unroll
-    for (int e = 0; e < PER; e += 8) {
-      const int ch = (lane * PER + e) >> 3;
+    for (int e = 0; e < QPER; e += 8) {
+      const int ch = (lane * QPER + e) >> 3;
       asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(qbase + swz(hh, ch, ROW_BYTES)),
-                   "r"(pack_bf16x2(v[e], v[e + 1])), "r"(pack_bf16x2(v[e + 2], v[e + 3])),
-                   "r"(pack_bf16x2(v[e + 4], v[e + 5])), "r"(pack_bf16x2(v[e + 6], v[e + 7])));
+                   "r"(pack_bf16x2(v[j][e], v[j][e + 1])), "r"(pack_bf16x2(v[j][e + 2], v[j][e + 3])),
+                   "r"(pack_bf16x2(v[j][e + 4], v[j][e + 5])), "r"(pack_bf16x2(v[j][e + 6], v[j][e + 7])));
     }
   }
 }
 
 // final value of output element (head hh, dims d..d+3), after the normalisation: inverse RoPE on
-// the rope dims, then the store
-__device__ __forceinline__ void write_out(const Params& P, int64_t qi, int h0, int hh, int d, float4 v, int pos) {
+// the rope dims (angles from the shared table), then the store
+__device__ __forceinline__ void write_out(const Params& P, const Smem& sm, int64_t qi, int h0, int hh, int d,
+                                          float4 v) {
   if (P.rope_freqs != nullptr && d >= D - P.rope_dim) {
     const int f0 = (d - (D - P.rope_dim)) >> 1;
-    float c0, s0, c1, s1;
-    rope_cos_sin(pos, P.rope_freqs[f0], &c0, &s0);
-    rope_cos_sin(pos, P.rope_freqs[f0 + 1], &c1, &s1);
-    rotate_pair(v.x, v.y, c0, s0, true, &v.x, &v.y);
-    rotate_pair(v.z, v.w, c1, s1, true, &v.z, &v.w);
+    rotate_pair(v.x, v.y, sm.rope_c[f0], sm.rope_s[f0], true, &v.x, &v.y);
+    rotate_pair(v.z, v.w, sm.rope_c[f0 + 1], sm.rope_s[f0 + 1], true, &v.z, &v.w);
   }
   const int64_t off = (qi * P.h + h0 + hh) * D + d;
   if (P.out_dtype == DSV4_BF16)
@@ -285,14 +317,39 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
   const int tile_end = min(ntiles, tile_begin + per);
 
   pdl_trigger();
-  pdl_wait();  // q, the window rows and the selected indices come from earlier kernels of the step
-
-  if (tile_begin < tile_end) gather_tile(P, sm, 0, qi, tile_begin * BN, t_end);
-  stage_q(P, sm, qi, h0);
+  // Without pre_wait every read follows the wait. With it (the caller's guarantee that only idx can
+  // still be in flight), q, the RoPE angles and the window rows are read while the kernel before this
+  // one finishes, and a CTA whose tiles are all window rows computes them too; reading idx waits first.
+  bool waited = false;
+  if (!P.pre_wait) {
+    pdl_wait();
+    waited = true;
+  }
+  float qv[QHPW][QPER];
+  load_q(P, sm, qi, h0, qv);
+  if (warp == 2 && P.rope_freqs != nullptr && lane < P.rope_dim / 2)  // angles of the rope pairs
+    rope_cos_sin(P.positions[qi], P.rope_freqs[lane], &sm.rope_c[lane], &sm.rope_s[lane]);
+  const bool first_idx = tile_begin < tile_end && tile_needs_idx(P, tile_begin);
+  if (tile_begin < tile_end && !first_idx) load_rows(P, sm, 0, qi, tile_begin * BN, t_end);  // window rows
   if (tid < HG) {
     sm.m_run[tid] = -INFINITY;
     sm.l_run[tid] = 0.f;
   }
+  __syncthreads();  // the RoPE table (and a window tile's rows) are in shared memory
+  // q's norm and RoPE before the tile's copies are issued: shared-memory accesses queued behind a
+  // tile's worth of copies would wait for them
+  cp_async_wait<0>();  // the bf16 q copies (this warp's heads)
+  __syncwarp();
+  finish_q(P, sm, qv);
+  if (first_idx) {  // rows from idx: after the dependency wait
+    if (!waited) {
+      pdl_wait();
+      waited = true;
+    }
+    load_rows(P, sm, 0, qi, tile_begin * BN, t_end);
+    __syncthreads();
+  }
+  if (tile_begin < tile_end) issue_tile(P, sm, 0);
   float o[8][4];
 #pragma unroll
   for (int a = 0; a < 8; ++a)
@@ -306,7 +363,14 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
     const int buf = (tile - tile_begin) & 1;
     cp_async_wait<0>();
     __syncthreads();  // tile `buf` (and q) landed; the previous tile's PV is done with buffer buf ^ 1
-    if (tile + 1 < tile_end) gather_tile(P, sm, buf ^ 1, qi, (tile + 1) * BN, t_end);
+    const bool has_next = tile + 1 < tile_end;
+    if (has_next) {  // the next tile's rows now; its copies after the next barrier
+      if (!waited && tile_needs_idx(P, tile + 1)) {
+        pdl_wait();
+        waited = true;
+      }
+      load_rows(P, sm, buf ^ 1, qi, (tile + 1) * BN, t_end);
+    }
     const uint32_t kv_s = static_cast<uint32_t>(__cvta_generic_to_shared(sm.kv[buf]));
 
     // ---- S = Q K^T: warp w takes gathered rows [8w, 8w + 8), all 16 heads, K = 512; four
@@ -345,6 +409,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
       sm.red_max[warp][hB] = mx1;
     }
     __syncthreads();
+    if (has_next) issue_tile(P, sm, buf ^ 1);
     float mA = sm.m_run[hA], mB = sm.m_run[hB];
 #pragma unroll
     for (int w = 0; w < THREADS / 32; ++w) {
@@ -409,8 +474,9 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
   }
   cp_async_wait<0>();
   __syncthreads();  // every warp is done with the kv buffers: they hold the partial O from here
+  if (!waited) pdl_wait();  // global writes only once the kernel before has completed
 
-  // ---- partial O (unnormalised) -> shared memory fp32 [16][OSTRIDE] ----
+  // ---- partial O (unnormalised) -> shared memory fp32 [16][OSTRIDE], (m, l) per head ----
   float* os = reinterpret_cast<float*>(sm.kv[0]);
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt) {
@@ -418,7 +484,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
     *reinterpret_cast<float2*>(os + hA * OSTRIDE + d) = make_float2(o[nt][0], o[nt][1]);
     *reinterpret_cast<float2*>(os + hB * OSTRIDE + d) = make_float2(o[nt][2], o[nt][3]);
   }
-  const int pos = P.positions != nullptr ? P.positions[qi] : 0;
+  if (tid < HG) sm.ml[tid] = make_float2(sm.m_run[tid], sm.l_run[tid]);
   const int S = P.splits;
   if (S == 1) {
     if (tid < HG) {
@@ -432,56 +498,47 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
       const int hh = c / (D / 4), d = (c % (D / 4)) * 4;
       const float4 a = *reinterpret_cast<const float4*>(os + hh * OSTRIDE + d);
       const float iv = sm.inv[hh];
-      write_out(P, qi, h0, hh, d, make_float4(a.x * iv, a.y * iv, a.z * iv, a.w * iv), pos);
+      write_out(P, sm, qi, h0, hh, d, make_float4(a.x * iv, a.y * iv, a.z * iv, a.w * iv));
     }
     return;
   }
-  // ---- cluster merge: weights per (head, split), then this CTA's slice of the 16 x 512 outputs ----
+  // ---- cluster merge: this CTA's slice of the 16 x 512 outputs; every thread requests, in one
+  // round of peer loads, the splits' partials of its four outputs and their (m, l), then weighs
+  // them itself (w_s = e^(m_s - M), 1 / (sum_s w_s l_s + e^(sink - M))) ----
   cluster_sync_all();  // every split's partial O, m and l are in its shared memory
-  const uint32_t m_s = static_cast<uint32_t>(__cvta_generic_to_shared(&sm.m_run[0]));
-  const uint32_t l_s = static_cast<uint32_t>(__cvta_generic_to_shared(&sm.l_run[0]));
-  if (warp < HG / 2) {  // warp w: heads 2w, 2w + 1 (lanes 0-15 and 16-31), lane % 16 = split
-    const int hh = warp * 2 + (lane >> 4), sp = lane & 15;
-    float m = -INFINITY, l = 0.f;
-    if (sp < S) {
-      m = dsmem_f32(m_s + hh * 4, sp);
-      l = dsmem_f32(l_s + hh * 4, sp);
-    }
-    float M = m;
-#pragma unroll
-    for (int off = 8; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    const float w = m == -INFINITY ? 0.f : exp2f(m - M);
-    float L = w * l;
-#pragma unroll
-    for (int off = 8; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    if (sp < S) sm.wts[hh][sp] = w;
-    if (sp == 0)
-      sm.inv[hh] = M == -INFINITY ? __int_as_float(0x7fc00000) : 1.f / (L + exp2f(P.sink[h0 + hh] * LOG2E - M));
-  }
-  __syncthreads();
   const uint32_t os_s = static_cast<uint32_t>(__cvta_generic_to_shared(os));
+  const uint32_t ml_s = static_cast<uint32_t>(__cvta_generic_to_shared(&sm.ml[0]));
   constexpr int NF4 = HG * (D / 4);  // 2048 float4 outputs per (query, head group)
   const int chunk = (NF4 + S - 1) / S;
   const int f0 = split * chunk, f1 = min(NF4, f0 + chunk);
   for (int f = f0 + tid; f < f1; f += THREADS) {
     const int hh = f / (D / 4), d = (f % (D / 4)) * 4;
-    // every split's partial is requested before the first is used (the peer loads overlap)
     float4 v[MAX_SPLITS];
-#pragma unroll
-    for (int sp = 0; sp < MAX_SPLITS; ++sp)
-      if (sp < S) v[sp] = dsmem_f32x4(os_s + (hh * OSTRIDE + d) * 4, sp);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float2 ml[MAX_SPLITS];
 #pragma unroll
     for (int sp = 0; sp < MAX_SPLITS; ++sp)
       if (sp < S) {
-        const float w = sm.wts[hh][sp];
+        v[sp] = dsmem_f32x4(os_s + (hh * OSTRIDE + d) * 4, sp);
+        ml[sp] = dsmem_f32x2(ml_s + hh * 8, sp);
+      }
+    float M = -INFINITY;
+#pragma unroll
+    for (int sp = 0; sp < MAX_SPLITS; ++sp)
+      if (sp < S) M = fmaxf(M, ml[sp].x);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < MAX_SPLITS; ++sp)
+      if (sp < S) {
+        const float w = ml[sp].x == -INFINITY ? 0.f : exp2f(ml[sp].x - M);
+        L += w * ml[sp].y;
         acc.x = fmaf(w, v[sp].x, acc.x);
         acc.y = fmaf(w, v[sp].y, acc.y);
         acc.z = fmaf(w, v[sp].z, acc.z);
         acc.w = fmaf(w, v[sp].w, acc.w);
       }
-    const float iv = sm.inv[hh];
-    write_out(P, qi, h0, hh, d, make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv), pos);
+    const float iv = M == -INFINITY ? __int_as_float(0x7fc00000) : 1.f / (L + exp2f(P.sink[h0 + hh] * LOG2E - M));
+    write_out(P, sm, qi, h0, hh, d, make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv));
   }
   cluster_sync_all();  // the peers keep their partials until every CTA of the cluster has read them
 }
@@ -574,6 +631,7 @@ int dsv4_sparse_attn_hg(const dsv4_sparse_attn_params* p, int splits, void* stre
   P.win_stride = p->win_stride;
   P.window = p->win_base ? p->window : 0;
   P.window_linear = p->window_linear;
+  P.pre_wait = p->pre_wait;
   static PerDeviceOnce attr;
   const int smem = static_cast<int>(sizeof(hg::Smem));
   DSV4_CUDA_CHECK(set_smem_once(attr, hg::decode_attn_kernel, smem));

@@ -68,8 +68,11 @@ __device__ __forceinline__ int visible_keys(const int32_t* positions, int64_t qr
 __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
   extern __shared__ __align__(16) uint8_t score_smem[];
   ScoreSmem& sm = *reinterpret_cast<ScoreSmem*>(score_smem);
-  pdl_trigger();
+  // wait first, then let the next kernel launch: the kernels launched after the scores (the
+  // selection, then a decode attention that stages q and the window rows before its own wait) find
+  // everything written before the scores complete
   pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t qrow = blockIdx.x;
   const int b = static_cast<int>(qrow / P.s);
@@ -190,8 +193,11 @@ __device__ __forceinline__ void add4x4(float (&dst)[4][4], const float (&a)[4][4
 __global__ void __launch_bounds__(THREADS, 1) score_tiled_kernel(ScoreParams P) {
   extern __shared__ __align__(16) uint8_t tiled_smem[];
   TiledSmem& sm = *reinterpret_cast<TiledSmem*>(tiled_smem);
-  pdl_trigger();
+  // wait first, then let the next kernel launch: the kernels launched after the scores (the
+  // selection, then a decode attention that stages q and the window rows before its own wait) find
+  // everything written before the scores complete
   pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.z;
   const int t0 = blockIdx.y * TQ;
@@ -1168,7 +1174,7 @@ __global__ void __launch_bounds__(SEL_THREADS) select_reg_kernel(SelectParams P)
 // A boundary bin with more than LIN_CAND keys narrows the range to that bin and bins again; a range
 // of one value (equal scores) takes its kleft lowest indices. Same set as the oracle's sort, written
 // in ascending key order.
-constexpr int LIN_THREADS = 1024;
+constexpr int LIN_THREADS = 512;     // threads of the selection CTA (16 to 32 warps both work)
 constexpr int LIN_BINS = 4096;
 constexpr int LIN_CAND = 1024;
 constexpr int LIN_MAX_ROWS = 32;     // rows per call served by this kernel
@@ -1176,7 +1182,7 @@ constexpr int LIN_MAX_ROWS = 32;     // rows per call served by this kernel
 struct LinShared {
   alignas(16) uint32_t hist[LIN_BINS];
   unsigned long long cand[LIN_CAND];
-  uint32_t wa[LIN_THREADS / 32], wb[LIN_THREADS / 32];
+  uint32_t wa[32], wb[32];
   uint32_t bin, kleft, count, ncand;
   unsigned long long thr;
   int32_t tau_idx;
@@ -1194,7 +1200,7 @@ __device__ __forceinline__ uint32_t lin_scan(uint32_t v, LinShared& sh) {
   if (lane == 31) sh.wa[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    const uint32_t w = sh.wa[lane];
+    const uint32_t w = lane < LIN_THREADS / 32 ? sh.wa[lane] : 0u;
     uint32_t wi = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -1263,11 +1269,13 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
 #pragma unroll
   for (int i = tid; i < LIN_BINS; i += LIN_THREADS) sh.hist[i] = 0;
   __syncthreads();
-  uint32_t lo = 0xffffffffu, hi = 0u;
-#pragma unroll 8
-  for (int w = 0; w < LIN_THREADS / 32; ++w) {
-    lo = min(lo, sh.wa[w]);
-    hi = max(hi, sh.wb[w]);
+  // every warp folds the per-warp partials itself (lane w takes warp w's), no second barrier
+  uint32_t lo = lane < LIN_THREADS / 32 ? sh.wa[lane] : 0xffffffffu;
+  uint32_t hi = lane < LIN_THREADS / 32 ? sh.wb[lane] : 0u;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
   }
   uint32_t kleft = k;
   unsigned long long thr = 0;   // (key << 32) | ~index of the k-th largest: take every key >= it
@@ -1288,17 +1296,26 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
     for (int e = 0; e < PER; ++e)
       if (e < nv && key[e] >= lo && key[e] <= hi) atomicAdd(&sh.hist[(key[e] - lo) >> shift], 1u);
     __syncthreads();
-    // boundary bin: thread t owns bins 4095 - 4t .. 4092 - 4t (highest first)
-    const uint4 h4 = *reinterpret_cast<const uint4*>(&sh.hist[LIN_BINS - 4 * (tid + 1)]);
-    const uint32_t c[4] = {h4.w, h4.z, h4.y, h4.x};
-    const uint32_t tot = c[0] + c[1] + c[2] + c[3];
+    // boundary bin: thread t owns the BPT bins below LIN_BINS - BPT t (highest first)
+    constexpr int BPT = LIN_BINS / LIN_THREADS;
+    uint32_t c[BPT], tot = 0;
+#pragma unroll
+    for (int q4 = 0; q4 < BPT / 4; ++q4) {
+      const uint4 h4 = *reinterpret_cast<const uint4*>(&sh.hist[LIN_BINS - BPT * (tid + 1) + 4 * (BPT / 4 - 1 - q4)]);
+      c[4 * q4] = h4.w;
+      c[4 * q4 + 1] = h4.z;
+      c[4 * q4 + 2] = h4.y;
+      c[4 * q4 + 3] = h4.x;
+    }
+#pragma unroll
+    for (int e = 0; e < BPT; ++e) tot += c[e];
     const uint32_t before = lin_scan(tot, sh);
     if (before < kleft && kleft <= before + tot) {
       uint32_t run = before;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < BPT; ++e) {
         if (run + c[e] >= kleft) {
-          sh.bin = LIN_BINS - 1 - (4 * tid + e);
+          sh.bin = LIN_BINS - 1 - (BPT * tid + e);
           sh.kleft = kleft - run;
           sh.count = c[e];
           break;
@@ -1322,8 +1339,8 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
                           static_cast<uint32_t>(~static_cast<uint32_t>(j0 + e));
         }
       __syncthreads();
-      if (tid < static_cast<int>(cnt)) {
-        const unsigned long long v = sh.cand[tid];
+      for (int i = tid; i < static_cast<int>(cnt); i += LIN_THREADS) {
+        const unsigned long long v = sh.cand[i];
         uint32_t rank = 0;
         for (uint32_t m = 0; m < cnt; ++m) rank += sh.cand[m] > v;
         if (rank == kleft - 1) sh.thr = v;
@@ -1404,11 +1421,12 @@ inline cudaError_t launch_scores(const ScoreParams& S, cudaStream_t st) {
 // the register-resident kernel up to 16384 visible keys, the shared-memory one above
 inline cudaError_t launch_select(const SelectParams& L, unsigned rows, cudaStream_t st) {
   const dim3 g(rows), blk(SEL_THREADS);
-  if (!L.refine && rows <= static_cast<unsigned>(LIN_MAX_ROWS) && L.n_keys <= LIN_THREADS * 16) {
+  if (!L.refine && rows <= static_cast<unsigned>(LIN_MAX_ROWS) && L.n_keys <= LIN_THREADS * 32) {
     const dim3 lb(LIN_THREADS);
     if (L.n_keys <= LIN_THREADS * 4) return launch_pdl(select_lin_kernel<4>, g, lb, 0, st, L);
     if (L.n_keys <= LIN_THREADS * 8) return launch_pdl(select_lin_kernel<8>, g, lb, 0, st, L);
-    return launch_pdl(select_lin_kernel<16>, g, lb, 0, st, L);
+    if (L.n_keys <= LIN_THREADS * 16) return launch_pdl(select_lin_kernel<16>, g, lb, 0, st, L);
+    return launch_pdl(select_lin_kernel<32>, g, lb, 0, st, L);
   }
   if (L.refine) {
     constexpr size_t rsm = sizeof(RefineSmem);

@@ -212,8 +212,10 @@ def _decode_attention_op(kv_pool: torch.Tensor, k_idx: torch.Tensor, block_table
         indexer_topk_into(idx_buf.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
                           k_idx, top_k, positions.view(b, 1), ratio, out_col=0, out_offset=comp_base,
                           block_table=block_table, page=page, key_image=image)
+        # the score kernel waits for all earlier work before the selection and the attention launch,
+        # so the attention may stage q and its window tiles before its own wait (pre_wait)
         return _sparse_attn_op(q, kv_pool, sink, idx_buf, float(scale), out_dtype, freqs, positions, 64, 0, True,
-                               1e-6, win_base, int(window), False, 0)
+                               1e-6, win_base, int(window), False, 0, True)
     main = torch.cuda.current_stream(q.device)
     side = _side_stream(q.device)
     side.wait_stream(main)

@@ -12,7 +12,8 @@ from . import _lib as L
 
 
 def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_dim=0, num_splits=0,
-                 q_norm_rope=False, q_eps=1e-6, win_base=None, window=0, window_linear=False, kernel=0):
+                 q_norm_rope=False, q_eps=1e-6, win_base=None, window=0, window_linear=False, kernel=0,
+                 pre_wait=False):
     p = L.SparseAttnParams()
     p.q, p.kv, p.sink, p.idx, p.out = L.ptr(q), L.ptr(kv), L.ptr(sink), L.ptr(idx), L.ptr(out)
     p.s, p.n, p.h, p.d, p.t = q.shape[0], kv.shape[0], q.shape[1], q.shape[2], idx.shape[-1]
@@ -29,6 +30,7 @@ def _attn_params(q, kv, sink, idx, out, scale, freqs=None, positions=None, rope_
     p.window = window
     p.window_linear = int(window_linear)
     p.kernel = kernel
+    p.pre_wait = int(pre_wait)
     return p
 
 
@@ -37,7 +39,8 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
                     scale: float, out_dtype: torch.dtype, rope_freqs: torch.Tensor | None,
                     positions: torch.Tensor | None, rope_dim: int, num_splits: int,
                     q_norm_rope: bool = False, q_eps: float = 1e-6, win_base: torch.Tensor | None = None,
-                    window: int = 0, window_linear: bool = False, kernel: int = 0) -> torch.Tensor:
+                    window: int = 0, window_linear: bool = False, kernel: int = 0,
+                    pre_wait: bool = False) -> torch.Tensor:
     q = q.contiguous()
     kv = kv.contiguous()
     if kv.dtype != torch.bfloat16:
@@ -48,7 +51,7 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
     idx = topk_idxs.contiguous()
     out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
     p = _attn_params(q, kv, sink, idx, out, scale, rope_freqs, positions, rope_dim, num_splits, q_norm_rope, q_eps,
-                     win_base, window, window_linear, kernel)
+                     win_base, window, window_linear, kernel, pre_wait)
     nbytes = L.lib().dsv4_sparse_attn_workspace_size(ctypes.byref(p))
     ws = L.workspace(nbytes, q.device)
     p.workspace, p.workspace_bytes = L.ptr(ws), nbytes
@@ -58,7 +61,7 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
 
 @_sparse_attn_op.register_fake
 def _(q, kv, attn_sink, topk_idxs, scale, out_dtype, rope_freqs, positions, rope_dim, num_splits, q_norm_rope=False,
-      q_eps=1e-6, win_base=None, window=0, window_linear=False, kernel=0):
+      q_eps=1e-6, win_base=None, window=0, window_linear=False, kernel=0, pre_wait=False):
     return torch.empty(q.shape, dtype=out_dtype, device=q.device)
 
 

@@ -117,6 +117,12 @@ typedef struct {
    * function (num_splits counts 64-row tiles for 1 and 3, 128-row tiles for 2); the choice is for
    * tests and measurements. */
   int32_t kernel;
+  /* 1: the caller guarantees that no kernel still running when this one launches writes q,
+   * positions, win_base or the implicit window's pool rows (only idx may come from the kernel launched
+   * just before, e.g. the indexer's selection after its score kernel, which waits for all earlier work
+   * before it lets later kernels launch); the head-group kernel then stages q and computes its window
+   * tiles before the programmatic-dependency wait. 0: every read follows the wait. */
+  int32_t pre_wait;
 } dsv4_sparse_attn_params;
 
 DSV4_API size_t dsv4_sparse_attn_workspace_size(const dsv4_sparse_attn_params* p);
