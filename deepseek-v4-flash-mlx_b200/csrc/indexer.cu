@@ -65,14 +65,7 @@ __device__ __forceinline__ int visible_keys(const int32_t* positions, int64_t qr
 // shared-memory bandwidth. Per (head, key) the dot product is one sequential fmaf chain over the
 // 128 dims; the thread's four heads fold (ascending) into the partial P[hq] of the canonical order,
 // whose balanced tree is level 0 across lane bit 4 and levels 1-3 across warps.
-__global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
-  extern __shared__ __align__(16) uint8_t score_smem[];
-  ScoreSmem& sm = *reinterpret_cast<ScoreSmem*>(score_smem);
-  // wait first, then let the next kernel launch: the kernels launched after the scores (the
-  // selection, then a decode attention that stages q and the window rows before its own wait) find
-  // everything written before the scores complete
-  pdl_wait();
-  pdl_trigger();
+__device__ __forceinline__ void score_tile(const ScoreParams& P, ScoreSmem& sm) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t qrow = blockIdx.x;
   const int b = static_cast<int>(qrow / P.s);
@@ -165,6 +158,16 @@ __global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
     const float v = __fadd_rn(__fadd_rn(l1a, l1b), __fadd_rn(l1c, l1d));
     if (j < nvis) P.scores[qrow * P.n_pad + j] = v;
   }
+}
+
+__global__ void __launch_bounds__(THREADS) score_kernel(ScoreParams P) {
+  extern __shared__ __align__(16) uint8_t score_smem[];
+  // wait first, then let the next kernel launch: the kernels launched after the scores (the
+  // selection, then a decode attention that stages q and the window rows before its own wait) find
+  // everything written before the scores complete
+  pdl_wait();
+  pdl_trigger();
+  score_tile(P, *reinterpret_cast<ScoreSmem*>(score_smem));
 }
 
 // Query-tiled scores for prefill: one CTA per (64 queries, 64 keys) of one batch row, skipping tiles
@@ -1188,7 +1191,8 @@ struct LinShared {
   int32_t tau_idx;
 };
 
-// exclusive prefix sum over the 1024 threads (2 barriers, plus one before the scratch is reused)
+// exclusive prefix sum over the NT threads (2 barriers, plus one before the scratch is reused)
+template <int NT>
 __device__ __forceinline__ uint32_t lin_scan(uint32_t v, LinShared& sh) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t incl = v;
@@ -1200,7 +1204,7 @@ __device__ __forceinline__ uint32_t lin_scan(uint32_t v, LinShared& sh) {
   if (lane == 31) sh.wa[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    const uint32_t w = lane < LIN_THREADS / 32 ? sh.wa[lane] : 0u;
+    const uint32_t w = lane < NT / 32 ? sh.wa[lane] : 0u;
     uint32_t wi = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -1213,13 +1217,10 @@ __device__ __forceinline__ uint32_t lin_scan(uint32_t v, LinShared& sh) {
   return sh.wb[warp] + incl - v;
 }
 
-template <int PER>
-__global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P) {
-  __shared__ LinShared sh;
-  pdl_trigger();
-  pdl_wait();
+// the selection of query row qrow by the NT threads of a CTA, PER keys per thread
+template <int PER, int NT>
+__device__ __forceinline__ void select_lin_row(const SelectParams& P, int64_t qrow, LinShared& sh) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t qrow = blockIdx.x;
   const int b = static_cast<int>(qrow / P.s);
   const int j0 = tid * PER;
   const int nvis = visible_keys(P.positions, qrow, P.ratio, P.n_keys);
@@ -1242,9 +1243,9 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
   int32_t* out = P.out + qrow * P.out_stride + P.out_col;
   const uint32_t k = static_cast<uint32_t>(P.top_k);
   if (P.win_base != nullptr)
-    for (int c = tid; c < P.window; c += LIN_THREADS) out[c - P.window] = window_row(P, b, P.positions[qrow], c);
+    for (int c = tid; c < P.window; c += NT) out[c - P.window] = window_row(P, b, P.positions[qrow], c);
   if (nvis <= P.top_k) {
-    for (int r = tid; r < P.top_k; r += LIN_THREADS) out[r] = r < nvis ? map_key(P, b, r) : -1;
+    for (int r = tid; r < P.top_k; r += NT) out[r] = r < nvis ? map_key(P, b, r) : -1;
     return;
   }
   const int nv = max(0, min(PER, nvis - j0));  // this thread's visible keys; the rest never count
@@ -1267,11 +1268,11 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
     sh.wb[warp] = mx;
   }
 #pragma unroll
-  for (int i = tid; i < LIN_BINS; i += LIN_THREADS) sh.hist[i] = 0;
+  for (int i = tid; i < LIN_BINS; i += NT) sh.hist[i] = 0;
   __syncthreads();
   // every warp folds the per-warp partials itself (lane w takes warp w's), no second barrier
-  uint32_t lo = lane < LIN_THREADS / 32 ? sh.wa[lane] : 0xffffffffu;
-  uint32_t hi = lane < LIN_THREADS / 32 ? sh.wb[lane] : 0u;
+  uint32_t lo = lane < NT / 32 ? sh.wa[lane] : 0xffffffffu;
+  uint32_t hi = lane < NT / 32 ? sh.wb[lane] : 0u;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
@@ -1289,7 +1290,7 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
     if (pass > 0) {
       __syncthreads();   // every thread is done with the previous pass's histogram
 #pragma unroll
-      for (int i = tid; i < LIN_BINS; i += LIN_THREADS) sh.hist[i] = 0;
+      for (int i = tid; i < LIN_BINS; i += NT) sh.hist[i] = 0;
       __syncthreads();
     }
 #pragma unroll
@@ -1297,7 +1298,7 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
       if (e < nv && key[e] >= lo && key[e] <= hi) atomicAdd(&sh.hist[(key[e] - lo) >> shift], 1u);
     __syncthreads();
     // boundary bin: thread t owns the BPT bins below LIN_BINS - BPT t (highest first)
-    constexpr int BPT = LIN_BINS / LIN_THREADS;
+    constexpr int BPT = LIN_BINS / NT;
     uint32_t c[BPT], tot = 0;
 #pragma unroll
     for (int q4 = 0; q4 < BPT / 4; ++q4) {
@@ -1309,7 +1310,7 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
     }
 #pragma unroll
     for (int e = 0; e < BPT; ++e) tot += c[e];
-    const uint32_t before = lin_scan(tot, sh);
+    const uint32_t before = lin_scan<NT>(tot, sh);
     if (before < kleft && kleft <= before + tot) {
       uint32_t run = before;
 #pragma unroll
@@ -1339,7 +1340,7 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
                           static_cast<uint32_t>(~static_cast<uint32_t>(j0 + e));
         }
       __syncthreads();
-      for (int i = tid; i < static_cast<int>(cnt); i += LIN_THREADS) {
+      for (int i = tid; i < static_cast<int>(cnt); i += NT) {
         const unsigned long long v = sh.cand[i];
         uint32_t rank = 0;
         for (uint32_t m = 0; m < cnt; ++m) rank += sh.cand[m] > v;
@@ -1359,7 +1360,7 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
 #pragma unroll
     for (int e = 0; e < PER; ++e) ne += (e < nv && key[e] == lo);
     __syncthreads();
-    const uint32_t before = lin_scan(ne, sh);
+    const uint32_t before = lin_scan<NT>(ne, sh);
     if (before < kleft && kleft <= before + ne) {
       uint32_t seen = before;
 #pragma unroll
@@ -1377,12 +1378,20 @@ __global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P)
     take |= static_cast<uint32_t>(e < nv && v >= thr) << e;
   }
   __syncthreads();   // the scan scratch is free
-  uint32_t pos = lin_scan(static_cast<uint32_t>(__popc(take)), sh);
+  uint32_t pos = lin_scan<NT>(static_cast<uint32_t>(__popc(take)), sh);
   while (take) {  // the taken keys in ascending order
     const int e = __ffs(take) - 1;
     take &= take - 1;
     out[pos++] = km.map(P, b, j0 + e);
   }
+}
+
+template <int PER>
+__global__ void __launch_bounds__(LIN_THREADS) select_lin_kernel(SelectParams P) {
+  __shared__ LinShared sh;
+  pdl_trigger();
+  pdl_wait();
+  select_lin_row<PER, LIN_THREADS>(P, blockIdx.x, sh);
 }
 
 __global__ void decode_window_kernel(int32_t batch, int32_t window, const int32_t* positions,
@@ -1580,8 +1589,6 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
   S.k_batch_stride = p->k_batch_stride;
   S.positions = p->positions;
   S.ratio = p->ratio;
-  if (mode == 1) DSV4_CUDA_CHECK(idx::launch_scores(S, as_stream(stream)));
-
   idx::SelectParams L = {};
   L.scores = scores;
   L.out = p->out;
@@ -1610,6 +1617,7 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
     L.kmax = kmax;
     L.eps_c = idx::EPS_C;
   }
+  if (mode == 1) DSV4_CUDA_CHECK(idx::launch_scores(S, as_stream(stream)));
   DSV4_CUDA_CHECK(idx::launch_select(L, static_cast<unsigned>(rows), as_stream(stream)));
   return DSV4_OK;
 }
