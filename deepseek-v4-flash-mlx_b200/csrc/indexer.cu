@@ -23,14 +23,17 @@ namespace idx {
 
 constexpr int DI = 128;         // indexer head dim
 constexpr int HI = 64;          // indexer heads
-constexpr int KT = 64;          // keys per score CTA (decode)
+// keys per score CTA (decode): 56, so that 8192 keys take 147 CTAs, one per SM of the 148; the
+// thread layout covers 64 key slots, the last eight of which are zero-filled and never stored
+constexpr int KT = 56;
+constexpr int KT_SLOTS = 64;
 constexpr int THREADS = 256;
 
 struct ScoreSmem {
-  alignas(16) float q[HI * DI];   // [head][dim], 16-byte chunk c of row r at c ^ ((r / 4) % 8)
-  alignas(16) float k[KT * DI];   // [key][dim], the same swizzle
+  alignas(16) float q[HI * DI];        // [head][dim], 16-byte chunk c of row r at c ^ ((r / 4) % 8)
+  alignas(16) float k[KT_SLOTS * DI];  // [key][dim], the same swizzle
   float w[HI];
-  float red[THREADS / 32][KT];    // tree level 0 per warp and key
+  float red[THREADS / 32][KT_SLOTS];   // tree level 0 per warp and key
 };
 
 __device__ __forceinline__ int swz_chunk(int r, int c) { return c ^ ((r >> 2) & 7); }
@@ -58,7 +61,7 @@ __device__ __forceinline__ int visible_keys(const int32_t* positions, int64_t qr
   return nv < n_keys ? (nv < 0 ? 0 : nv) : n_keys;
 }
 
-// grid: (batch*s, key tiles of KT = 64). 256 threads: thread = (head quad hq, key quad kq) with
+// grid: (batch*s, key tiles of KT = 56). 256 threads: thread = (head quad hq, key quad kq) with
 // lane = (hq & 1) << 4 | kq, warp = hq >> 1: a thread owns heads 4hq..4hq+3 and keys 4kq..4kq+3 of
 // the tile, 16 accumulators. A 4-dim step loads 4 q chunks (two distinct per warp: shared-memory
 // broadcasts) and 4 key chunks for 64 FMAs, so the step is bound by the FMA pipe rather than by
@@ -86,9 +89,9 @@ __device__ __forceinline__ void score_tile(const ScoreParams& P, ScoreSmem& sm) 
       const int r = c >> 3, ch = g * 8 + (c & 7);
       cp_async16(qs + (r * 32 + swz_chunk(r, ch)) * 16, qg + r * DI + ch * 4, true);
     }
-    for (int c = tid; c < KT * 8; c += THREADS) {
+    for (int c = tid; c < KT_SLOTS * 8; c += THREADS) {
       const int r = c >> 3, ch = g * 8 + (c & 7);
-      const bool valid = (j0 + r) < nvis;
+      const bool valid = r < KT && (j0 + r) < nvis;
       const float* src = kg + static_cast<int64_t>(valid ? j0 + r : 0) * DI + ch * 4;
       cp_async16(ks + (r * 32 + swz_chunk(r, ch)) * 16, src, valid);
     }
