@@ -692,6 +692,13 @@ def kernel_times(cases, runners, stream, n):
                                        out_offset=cases[i].cache.comp_base, block_table=cases[i].cache.block_table,
                                        page=cases[i].cache.page, key_image=cases[i].cache.key_image, mode=2),
         funcs["indexer_topk"][1])
+    # the other attention kernels on the same call (kernel 1: 64-head mma.sync, 2: tcgen05, 3: head groups)
+    for kern_id in (1, 2, 3):
+        funcs[f"alt:sparse_attn_kernel{kern_id}"] = (
+            (lambda k: lambda i: SA.sparse_attn_rope(qn[i], cases[i].cache.kv_pool, cases[i].sink, runners[i].idx,
+                                                     512 ** -0.5, runners[i].positions, freqs, 64,
+                                                     win_base=cases[i].cache.win_base, window=128, kernel=k))(kern_id),
+            funcs["sparse_attn"][1])
     out = {}
     for name, (fn, nbytes) in funcs.items():
         with torch.cuda.stream(stream):
