@@ -68,6 +68,15 @@ __global__ void cast_kernel(const void* x, int32_t xd, void* y, int32_t yd, int6
     store_from_float(y, i, yd, load_as_float(x, i, xd));
 }
 
+// 16-byte copy by the SMs (either side may be pinned host memory, reached over the bus through its
+// unified address); under programmatic dependent launch it waits for the previous kernel first
+__global__ void copy16_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t n16) {
+  pdl_wait();
+  pdl_trigger();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
 }  // namespace dsv4
 
 using namespace dsv4;
@@ -132,6 +141,20 @@ int dsv4_window_topk_idxs(int32_t window, int32_t bsz, int32_t seqlen, int32_t s
   if (blocks > 4096) blocks = 4096;
   window_idx_kernel<<<blocks, 256, 0, as_stream(stream)>>>(window, bsz, seqlen, start_pos, cols, out);
   DSV4_LAUNCH_CHECK("window_idx_kernel");
+  return DSV4_OK;
+}
+
+int dsv4_copy(void* dst, const void* src, size_t bytes, void* stream) {
+  DSV4_CHECK_ARG(dst && src, "dsv4_copy: NULL pointer");
+  DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(dst) % 16 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+                     bytes % 16 == 0,
+                 "dsv4_copy: addresses and size must be multiples of 16 bytes");
+  if (bytes == 0) return DSV4_OK;
+  const int64_t n16 = static_cast<int64_t>(bytes / 16);
+  int blocks = static_cast<int>((n16 + 255) / 256);
+  if (blocks > 2 * num_sms()) blocks = 2 * num_sms();
+  DSV4_CUDA_CHECK(launch_pdl(copy16_kernel, dim3(blocks), dim3(256), 0, as_stream(stream),
+                             reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n16));
   return DSV4_OK;
 }
 

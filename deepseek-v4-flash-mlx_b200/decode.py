@@ -301,8 +301,9 @@ class DecodeRunner:
     reference's per-token path is a Python loop of library calls, oracle/v4_fast.py:82-122; here one
     graph launch replays the kernels). `step_device` replays with inputs already on the device.
     `step_host` runs a second graph that also holds the step's copies: this token's inputs from one
-    pinned host block to the device (one copy: q, q_idx, w_idx and positions sit at fixed offsets of
-    both blocks), the kernels, and the output back to pinned host memory, so a step is one launch.
+    pinned host block to the device (one copy kernel: q, q_idx, w_idx and positions sit at fixed
+    offsets of both blocks), the kernels, and the output back to pinned host memory (a second copy
+    kernel), so a step is one launch.
     Callers that write their inputs straight into `host_inputs()` skip the host-side staging copy.
     """
 
@@ -362,9 +363,11 @@ class DecodeRunner:
         self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
         self.graph_host = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph_host, stream=self.stream):
-            self.d_in.copy_(self.h_in, non_blocking=True)
+            # the step's inputs and output cross the bus by kernel loads / stores of the pinned
+            # blocks (dsv4_copy), not copy-engine transfers: tens of KB, latency-bound
+            L.copy_(self.d_in, self.h_in)
             out = self._body()
-            self.h_out.copy_(out, non_blocking=True)
+            L.copy_(self.h_out, out)
         self.out_host_graph = out
 
     def host_inputs(self):

@@ -451,6 +451,15 @@ DSV4_API int dsv4_hc_post(const float* x, const float* residual, const float* po
 /* ---- casts used by the op layer (fp32 <-> bf16) ---- */
 DSV4_API int dsv4_cast(const void* x, int32_t x_dtype, void* y, int32_t y_dtype, int64_t numel, void* stream);
 
+/* ---- copy by a kernel, for the serving loop's host <-> device staging (no reference counterpart:
+ * the reference uploads its host-built buffers with MLX array constructors, oracle/v4_fast.py:108-118).
+ * dst and src are device or pinned (cudaHostAlloc'd) host memory, addressed by their unified pointers;
+ * both 16-byte aligned, bytes a multiple of 16. A pinned buffer read or written this way moves over the
+ * bus as the SMs load or store it, which for the tens of KB of a decode step's inputs and outputs costs
+ * less than a copy-engine transfer. Ordered in the stream like any kernel (programmatic dependent
+ * launch: it waits for the kernel before it). */
+DSV4_API int dsv4_copy(void* dst, const void* src, size_t bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -124,3 +124,18 @@ def test_decode_rows_bookkeeping(dsv4):
     over = torch.tensor([4 * max_comp + 3], dtype=torch.int32)     # entry max_comp: outside the cache
     D.decode_rows(D.SparseMLACache(1, max_comp), over.cuda())
     assert L.device_error() == 4
+
+
+def test_copy_kernel_between_pinned_host_and_device(dsv4):
+    """dsv4_copy moves bytes between pinned host memory and the device by kernel loads and stores
+    (the serving step's staging); misaligned sizes are refused."""
+    L = importlib.import_module("deepseek-v4-flash-mlx_b200._lib")
+    src = torch.arange(100_000, dtype=torch.int32).pin_memory()
+    dev = torch.empty(100_000, dtype=torch.int32, device="cuda")
+    back = torch.zeros(100_000, dtype=torch.int32).pin_memory()
+    L.copy_(dev, src)
+    L.copy_(back, dev)
+    torch.cuda.synchronize()
+    assert torch.equal(dev.cpu(), src) and torch.equal(back, src)
+    with pytest.raises(L.Dsv4Error):
+        L.copy_(dev[:3], src[:3])     # 12 bytes: not a multiple of 16
