@@ -29,11 +29,13 @@ constexpr int KT = 56;
 constexpr int KT_SLOTS = 64;
 constexpr int THREADS = 256;
 
+constexpr int SROW = DI + 4;   // padded row (floats): the 16 keys a half-warp reads hit distinct banks
+
 struct ScoreSmem {
-  alignas(16) float q[HI * DI];        // [head][dim], 16-byte chunk c of row r at c ^ ((r / 4) % 8)
-  alignas(16) float k[KT_SLOTS * DI];  // [key][dim], the same swizzle
-  float w[HI];
-  float red[THREADS / 32][KT_SLOTS];   // tree level 0 per warp and key
+  alignas(16) float q[HI * SROW];        // [head][dim]
+  alignas(16) float k[KT_SLOTS * SROW];  // [key slot][dim]
+  alignas(16) float w[HI];
+  float red[THREADS / 32][KT_SLOTS];     // tree level 0 per warp and key slot
 };
 
 __device__ __forceinline__ int swz_chunk(int r, int c) { return c ^ ((r >> 2) & 7); }
@@ -61,9 +63,10 @@ __device__ __forceinline__ int visible_keys(const int32_t* positions, int64_t qr
   return nv < n_keys ? (nv < 0 ? 0 : nv) : n_keys;
 }
 
-// grid: (batch*s, key tiles of KT = 56). 256 threads: thread = (head quad hq, key quad kq) with
-// lane = (hq & 1) << 4 | kq, warp = hq >> 1: a thread owns heads 4hq..4hq+3 and keys 4kq..4kq+3 of
-// the tile, 16 accumulators. A 4-dim step loads 4 q chunks (two distinct per warp: shared-memory
+// grid: (batch*s, key tiles of KT = 56). 256 threads: thread = (head quad hq, key lane kq) with
+// lane = (hq & 1) << 4 | kq, warp = hq >> 1: a thread owns heads 4hq..4hq+3 and key slots kq, kq+16,
+// kq+32, kq+48 of the tile, 16 accumulators; q and key rows are padded to 132 floats, so a half-warp's
+// 16 keys read distinct banks. A 4-dim step loads 4 q chunks (two distinct per warp: shared-memory
 // broadcasts) and 4 key chunks for 64 FMAs, so the step is bound by the FMA pipe rather than by
 // shared-memory bandwidth. Per (head, key) the dot product is one sequential fmaf chain over the
 // 128 dims; the thread's four heads fold (ascending) into the partial P[hq] of the canonical order,
@@ -80,62 +83,73 @@ __device__ __forceinline__ void score_tile(const ScoreParams& P, ScoreSmem& sm) 
   const float* kg = P.k + static_cast<int64_t>(b) * P.k_batch_stride * DI;
   const uint32_t qs = static_cast<uint32_t>(__cvta_generic_to_shared(sm.q));
   const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(sm.k));
-  // four stages of 32 dims (eight 16-byte chunks of every q and key row; the swizzle keeps a
-  // stage's chunks within its group of eight), so the dot products start on the first 32 dims
-  // while the rest are in flight
+  // four stages of 32 dims (eight 16-byte chunks of every q and key row), so the dot products
+  // start on the first 32 dims while the rest are in flight
+  // the head weights ride in the first group (a plain load would hold the thread until it lands)
+  if (tid < HI / 4)
+    cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(sm.w)) + tid * 16, P.w + qrow * HI + tid * 4, true);
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     for (int c = tid; c < HI * 8; c += THREADS) {
       const int r = c >> 3, ch = g * 8 + (c & 7);
-      cp_async16(qs + (r * 32 + swz_chunk(r, ch)) * 16, qg + r * DI + ch * 4, true);
+      cp_async16(qs + (r * SROW + ch * 4) * 4, qg + r * DI + ch * 4, true);
     }
     for (int c = tid; c < KT_SLOTS * 8; c += THREADS) {
       const int r = c >> 3, ch = g * 8 + (c & 7);
       const bool valid = r < KT && (j0 + r) < nvis;
       const float* src = kg + static_cast<int64_t>(valid ? j0 + r : 0) * DI + ch * 4;
-      cp_async16(ks + (r * 32 + swz_chunk(r, ch)) * 16, src, valid);
+      cp_async16(ks + (r * SROW + ch * 4) * 4, src, valid);
     }
     asm volatile("cp.async.commit_group;\n" ::);
   }
-  if (tid < HI) sm.w[tid] = P.w[qrow * HI + tid];
 
+  // thread: heads 4 hq .. 4 hq + 3, key slots kq, kq + 16, kq + 32, kq + 48
   const int hq = (warp << 1) | (lane >> 4), kq = lane & 15;
+  const float* qrow_s = sm.q + hq * 4 * SROW;
+  const float* krow_s = sm.k + kq * SROW;
   float acc[4][4];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+  // (loops kept rolled: a kernel of a few microseconds runs on SMs whose instruction caches are
+  // cold, and straight-line code would be fetched line by line)
+#pragma unroll 1
+  for (int g = 0; g < 4; ++g) {
+    switch (g) {  // stage g has landed (with w in the first group)
+      case 0: asm volatile("cp.async.wait_group 3;\n" ::); break;
+      case 1: asm volatile("cp.async.wait_group 2;\n" ::); break;
+      case 2: asm volatile("cp.async.wait_group 1;\n" ::); break;
+      default: asm volatile("cp.async.wait_group 0;\n" ::); break;
+    }
+    __syncthreads();
 #pragma unroll 2
-  for (int ch = 0; ch < DI / 4; ++ch) {
-    if ((ch & 7) == 0) {  // stage ch / 8 has landed (and w, before the first)
-      switch (ch >> 3) {
-        case 0: asm volatile("cp.async.wait_group 3;\n" ::); break;
-        case 1: asm volatile("cp.async.wait_group 2;\n" ::); break;
-        case 2: asm volatile("cp.async.wait_group 1;\n" ::); break;
-        default: asm volatile("cp.async.wait_group 0;\n" ::); break;
-      }
-      __syncthreads();
+    for (int st = 0; st < 8; ++st) {
+      const int d = (g * 8 + st) * 4;
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) qv[a] = *reinterpret_cast<const float4*>(qrow_s + a * SROW + d);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) kv[c] = *reinterpret_cast<const float4*>(krow_s + c * 16 * SROW + d);
+      // dimension-major: x of all 16 (head, key) pairs, then y, z, w; every pair's chain still
+      // runs over the dims in ascending order
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][c] = __fmaf_rn(qv[a].x, kv[c].x, acc[a][c]);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][c] = __fmaf_rn(qv[a].y, kv[c].y, acc[a][c]);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][c] = __fmaf_rn(qv[a].z, kv[c].z, acc[a][c]);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][c] = __fmaf_rn(qv[a].w, kv[c].w, acc[a][c]);
     }
-    float4 qv[4], kv[4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a) {
-      const int r = hq * 4 + a;
-      qv[a] = *reinterpret_cast<const float4*>(&sm.q[(r * 32 + swz_chunk(r, ch)) * 4]);
-    }
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int r = kq * 4 + c;
-      kv[c] = *reinterpret_cast<const float4*>(&sm.k[(r * 32 + swz_chunk(r, ch)) * 4]);
-    }
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        acc[a][c] = __fmaf_rn(qv[a].x, kv[c].x, acc[a][c]);
-        acc[a][c] = __fmaf_rn(qv[a].y, kv[c].y, acc[a][c]);
-        acc[a][c] = __fmaf_rn(qv[a].z, kv[c].z, acc[a][c]);
-        acc[a][c] = __fmaf_rn(qv[a].w, kv[c].w, acc[a][c]);
-      }
   }
   // P[hq] per key: the thread's four heads, ascending; tree level 0 across hq bit 0 (lane bit 4)
   float part[4];
@@ -151,7 +165,7 @@ __device__ __forceinline__ void score_tile(const ScoreParams& P, ScoreSmem& sm) 
   }
   if (lane < 16) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) sm.red[warp][kq * 4 + c] = part[c];
+    for (int c = 0; c < 4; ++c) sm.red[warp][kq + 16 * c] = part[c];
   }
   __syncthreads();
   if (tid < KT) {  // levels 1-3: hq bits 1-3 are the warp's bits 0-2
@@ -1515,6 +1529,9 @@ extern "C" int dsv4_indexer_topk(const dsv4_indexer_params* p, void* stream) {
   DSV4_CHECK_ARG(p != nullptr, "dsv4_indexer_topk: params is NULL");
   DSV4_CHECK_ARG(p->q && p->w && p->k && p->out, "dsv4_indexer_topk: NULL tensor");
   DSV4_CHECK_ARG(p->heads == idx::HI, "dsv4_indexer_topk: %d heads unsupported (64 only)", p->heads);
+  DSV4_CHECK_ARG((reinterpret_cast<uintptr_t>(p->q) | reinterpret_cast<uintptr_t>(p->w) |
+                  reinterpret_cast<uintptr_t>(p->k)) % 16 == 0,
+                 "dsv4_indexer_topk: q, w and k must be 16-byte aligned");
   DSV4_CHECK_ARG(p->batch > 0 && p->s > 0 && p->n_keys > 0 && p->top_k > 0,
                  "dsv4_indexer_topk: bad sizes");
   DSV4_CHECK_ARG(p->n_keys <= idx::SEL_MAX_KEYS, "dsv4_indexer_topk: n_keys %d above %d", p->n_keys,
@@ -1731,6 +1748,9 @@ extern "C" int dsv4_indexer_topk_noalloc(const dsv4_indexer_params* p, void* str
                      (p->key_image == nullptr) == (p->key_norm_max == nullptr),
                  "dsv4_indexer_topk_noalloc: key_image, key_inv and key_norm_max go together");
   DSV4_CHECK_ARG(p->heads == idx::HI, "dsv4_indexer_topk_noalloc: %d heads unsupported (64 only)", p->heads);
+  DSV4_CHECK_ARG((reinterpret_cast<uintptr_t>(p->q) | reinterpret_cast<uintptr_t>(p->w) |
+                  reinterpret_cast<uintptr_t>(p->k)) % 16 == 0,
+                 "dsv4_indexer_topk_noalloc: q, w and k must be 16-byte aligned");
   DSV4_CHECK_ARG(p->batch > 0 && p->s > 0 && p->n_keys > 0 && p->top_k > 0,
                  "dsv4_indexer_topk_noalloc: bad sizes");
   DSV4_CHECK_ARG(p->n_keys <= idx::SEL_MAX_KEYS, "dsv4_indexer_topk_noalloc: n_keys %d above %d", p->n_keys,
