@@ -86,7 +86,7 @@ class CompressorDecodeParams(ctypes.Structure):
 class LinearParams(ctypes.Structure):
     _fields_ = [("x", vp), ("w", vp), ("w_scale", vp), ("y", vp), ("m", i64), ("n", i32), ("k", i32),
                 ("groups", i32), ("group", i32), ("x_dtype", i32), ("w_dtype", i32), ("y_dtype", i32),
-                ("workspace", vp), ("workspace_bytes", sz)]
+                ("workspace", vp), ("workspace_bytes", sz), ("kernel", i32)]
 
 
 class HcParams(ctypes.Structure):
@@ -105,7 +105,7 @@ class LinearOut(ctypes.Structure):
 
 class LinearMultiParams(ctypes.Structure):
     _fields_ = [("x", vp), ("m", i64), ("k", i32), ("group", i32), ("x_dtype", i32), ("w_dtype", i32),
-                ("count", i32), ("outs", LinearOut * LINEAR_MULTI_MAX)]
+                ("count", i32), ("outs", LinearOut * LINEAR_MULTI_MAX), ("kernel", i32)]
 
 
 class DecodeRowsParams(ctypes.Structure):

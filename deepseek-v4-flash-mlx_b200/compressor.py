@@ -11,7 +11,7 @@ import ctypes
 import torch
 
 from . import _lib as L
-from .mla import QuantWeight, linear
+from .mla import QuantWeight, linear, linear_multi
 from .norm_rope import rope_freqs
 
 
@@ -53,8 +53,11 @@ def _compressor_prefill_op(x: torch.Tensor, wkv: torch.Tensor, wkv_scale: torch.
                            act_quant: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     b, s, _ = x.shape
     d2 = 2 * head_dim
-    kv = linear(x, _w_join(wkv, wkv_scale), torch.float32)
-    score = linear(x, _w_join(wgate, wgate_scale), torch.float32)
+    if b * s > 64 and wkv_scale is None and wgate_scale is None:
+        kv, score = linear_multi(x, [wkv, wgate], torch.float32)  # one tcgen05 launch, x read once
+    else:
+        kv = linear(x, _w_join(wkv, wkv_scale), torch.float32)
+        score = linear(x, _w_join(wgate, wgate_scale), torch.float32)
     freqs = rope_freqs(rope_head_dim, x.device, original_seq_len=original_seq_len, base=base, factor=factor,
                        beta_fast=beta_fast, beta_slow=beta_slow)
     out = torch.empty((b, s // ratio, head_dim), dtype=out_dtype, device=x.device)

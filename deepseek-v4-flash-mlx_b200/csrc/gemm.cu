@@ -647,6 +647,19 @@ inline Plan plan(int64_t m, int n, int k, int groups, bool i8) {
 
 using namespace dsv4;
 
+namespace dsv4 {
+int gemm_tc_launch(const void* x, int64_t m, int k, int groups, const void* const* w, void* const* y, const int* n,
+                   const int* y_dtype, int nprob, void* stream);
+}  // namespace dsv4
+
+// The tcgen05 kernel for kernel == 2, and for kernel == 0 with bf16 weights and m above the
+// weight-streaming range. The choice depends on m only through that bound, so the rows of a
+// prefill computed in slices (one per rank) are bit-identical to the same rows computed whole.
+static bool use_tcgen05(int kernel, bool i8, int64_t m) {
+  if (kernel == 2) return true;
+  return kernel == 0 && !i8 && m > gm::SKINNY_MAX_M;
+}
+
 template <bool I8, int MT>
 static int launch_skinny_mt(const gm::Params& P, void* stream) {
   // int8 weights: 32 rows per warp (the tokens' fragments serve two row tiles); bf16: 16
@@ -701,6 +714,7 @@ static int launch_tiled(const gm::Params& P, void* stream) {
 
 extern "C" size_t dsv4_linear_workspace_size(const dsv4_linear_params* p) {
   if (!p || p->m <= 0 || p->n <= 0 || p->k <= 0 || p->groups < 1) return 0;
+  if (use_tcgen05(p->kernel, p->w_dtype == DSV4_I8, p->m)) return 0;
   const gm::Plan pl = gm::plan(p->m, p->n, p->k, p->groups, p->w_dtype == DSV4_I8);
   const int sp = pl.ksplit;
   if (pl.skinny || sp <= 1) return 0;  // the decode-shaped kernel reduces inside its cluster
@@ -719,7 +733,16 @@ extern "C" int dsv4_linear(const dsv4_linear_params* p, void* stream) {
   const bool i8 = p->w_dtype == DSV4_I8;
   DSV4_CHECK_ARG(!i8 || (p->w_scale != nullptr && p->group == 64),
                  "dsv4_linear: int8 weights need bf16 scales with group 64");
+  DSV4_CHECK_ARG(p->kernel >= 0 && p->kernel <= 2, "dsv4_linear: kernel=%d must be 0, 1 or 2", p->kernel);
+  DSV4_CHECK_ARG(p->kernel != 2 || !i8, "dsv4_linear: the tcgen05 kernel (2) takes bf16 weights");
   if (p->m == 0) return DSV4_OK;
+  DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(p->x) % 16 == 0 && reinterpret_cast<uintptr_t>(p->w) % 16 == 0,
+                 "dsv4_linear: x and W must be 16-byte aligned");
+  if (use_tcgen05(p->kernel, i8, p->m)) {
+    const void* w = p->w;
+    void* y = p->y;
+    return gemm_tc_launch(p->x, p->m, p->k, p->groups, &w, &y, &p->n, &p->y_dtype, 1, stream);
+  }
   gm::Params P;
   P.x = reinterpret_cast<const __nv_bfloat16*>(p->x);
   P.w = p->w;
@@ -746,8 +769,6 @@ extern "C" int dsv4_linear(const dsv4_linear_params* p, void* stream) {
       P.part = reinterpret_cast<float*>(p->workspace);
     }
   }
-  DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(p->x) % 16 == 0 && reinterpret_cast<uintptr_t>(p->w) % 16 == 0,
-                 "dsv4_linear: x and W must be 16-byte aligned");
   DSV4_CHECK_ARG(static_cast<int64_t>(p->groups) * P.ksplit <= 65535, "dsv4_linear: too many groups");
   int rc;
   if (pl.skinny)
@@ -778,7 +799,23 @@ extern "C" int dsv4_linear_multi(const dsv4_linear_multi_params* p, void* stream
                    "dsv4_linear_multi: int8 weights need bf16 scales with group 64");
     DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(o.w) % 16 == 0, "dsv4_linear_multi: W must be 16-byte aligned");
   }
+  DSV4_CHECK_ARG(p->kernel >= 0 && p->kernel <= 2, "dsv4_linear_multi: kernel=%d must be 0, 1 or 2", p->kernel);
+  DSV4_CHECK_ARG(p->kernel != 2 || !i8, "dsv4_linear_multi: the tcgen05 kernel (2) takes bf16 weights");
   if (p->m == 0) return DSV4_OK;
+  DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(p->x) % 16 == 0, "dsv4_linear_multi: x must be 16-byte aligned");
+  {
+    int n[DSV4_LINEAR_MULTI_MAX], yd[DSV4_LINEAR_MULTI_MAX];
+    const void* w[DSV4_LINEAR_MULTI_MAX];
+    void* y[DSV4_LINEAR_MULTI_MAX];
+    for (int i = 0; i < p->count; ++i) {
+      n[i] = p->outs[i].n;
+      yd[i] = p->outs[i].y_dtype;
+      w[i] = p->outs[i].w;
+      y[i] = p->outs[i].y;
+    }
+    if (use_tcgen05(p->kernel, i8, p->m))  // all projections in one launch
+      return gemm_tc_launch(p->x, p->m, p->k, 1, w, y, n, yd, p->count, stream);
+  }
   if (p->m > gm::SKINNY_MAX_M) {  // prefill-sized: one tiled launch per projection
     for (int i = 0; i < p->count; ++i) {
       dsv4_linear_params lp = {};
@@ -794,12 +831,12 @@ extern "C" int dsv4_linear_multi(const dsv4_linear_multi_params* p, void* stream
       lp.x_dtype = p->x_dtype;
       lp.w_dtype = p->w_dtype;
       lp.y_dtype = p->outs[i].y_dtype;
+      lp.kernel = 1;
       const int rc = dsv4_linear(&lp, stream);
       if (rc != DSV4_OK) return rc;
     }
     return DSV4_OK;
   }
-  DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(p->x) % 16 == 0, "dsv4_linear_multi: x must be 16-byte aligned");
   gm::Params P = {};
   P.x = reinterpret_cast<const __nv_bfloat16*>(p->x);
   P.m = p->m;

@@ -389,6 +389,13 @@ typedef struct {
    * without the split. Both sums run in a fixed order: results are deterministic. */
   void* workspace;
   size_t workspace_bytes;
+  /* kernel choice (a choice of implementation, not of result beyond fp32 summation order):
+   * 0 = automatic: bf16 weights with m > 64 run the tcgen05 kernel (TMA-fed, fp32 accumulator in
+   * tensor memory, persistent grid, no workspace; a row's result does not depend on m), everything
+   * else the kernels below; 1 = the mma.sync kernels (weight-streaming for m <= 64,
+   * tiled above); 2 = the tcgen05 kernel for any m (bf16 weights only, else
+   * DSV4_ERR_INVALID_ARGUMENT). */
+  int32_t kernel;
 } dsv4_linear_params;
 DSV4_API size_t dsv4_linear_workspace_size(const dsv4_linear_params* p);
 DSV4_API int dsv4_linear(const dsv4_linear_params* p, void* stream);
@@ -396,8 +403,8 @@ DSV4_API int dsv4_linear(const dsv4_linear_params* p, void* stream);
 /* Several projections of the same x in one launch (the decode block's q_down, kv_proj, the two
  * compressors' projections and the indexer head weights all read the normed hidden states): output
  * i is y_i[m, n_i] = x[m, k] . W_i[n_i, k]^T, each W_i as in dsv4_linear (groups 1), one weight
- * dtype for all. m <= 64 runs them as one grid of the weight-streaming kernel; larger m runs one
- * dsv4_linear per output. Fuses the projections of v4mlx/mla.py:16-42 that share their input. */
+ * dtype for all. m <= 64 runs them as one grid of the weight-streaming kernel; larger m runs them
+ * as one tcgen05 launch (bf16 weights) or one dsv4_linear per output. Fuses the projections of v4mlx/mla.py:16-42 that share their input. */
 #define DSV4_LINEAR_MULTI_MAX 8
 typedef struct {
   const void* w;          /* [n, k] */
@@ -410,6 +417,9 @@ typedef struct {
   int64_t m;
   int32_t k, group, x_dtype, w_dtype, count;
   dsv4_linear_out outs[DSV4_LINEAR_MULTI_MAX];
+  /* as dsv4_linear_params.kernel; for m > 64 the tcgen05 kernel runs all outputs in one launch,
+   * so the CTAs working on one token tile at the same time share it through L2 */
+  int32_t kernel;
 } dsv4_linear_multi_params;
 DSV4_API int dsv4_linear_multi(const dsv4_linear_multi_params* p, void* stream);
 

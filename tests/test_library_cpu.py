@@ -51,6 +51,12 @@ def test_argument_validation_without_gpu(dsv4):
     lp.m, lp.n, lp.k, lp.groups, lp.x_dtype, lp.w_dtype = 4, 8, 100, 1, 1, 1
     assert lib.dsv4_linear(ctypes.byref(lp), None) == 1
     assert b"multiple of 64" in lib.dsv4_last_error()
+    lp.m, lp.k, lp.kernel = 0, 128, 3  # kernel choices are 0, 1, 2
+    assert lib.dsv4_linear(ctypes.byref(lp), None) == 1
+    assert b"kernel=3" in lib.dsv4_last_error()
+    lp.kernel, lp.w_dtype, lp.w_scale, lp.group = 2, L.I8, ctypes.c_void_p(16), 64
+    assert lib.dsv4_linear(ctypes.byref(lp), None) == 1  # the tcgen05 kernel takes bf16 weights
+    assert b"bf16 weights" in lib.dsv4_last_error()
 
 
 def test_ops_refuse_cpu_tensors(dsv4):

@@ -282,7 +282,7 @@ def test_linear_int8_g64(dsv4):
     (1, 64, 4096, 1, True, True),         # one output tile (the indexer head weights)
     (40, 19200, 128, 1, True, False),     # 64-token tiles, enough output tiles: no split
     (12, 19200, 256, 1, False, False),    # 16-token tiles, bf16
-    (100, 256, 4096, 1, False, True),     # the tiled kernel (m > 64) with k split
+    (100, 256, 4096, 1, True, True),      # the tiled kernel (m > 64, int8) with k split
 ])
 def test_linear_split_k_decode_shapes(dsv4, m, n, k, groups, quant, split):
     """Decode-shaped projections (the weight-streaming kernel for m <= 64), with k split across
