@@ -985,9 +985,12 @@ def main():
     ap.add_argument("--replicas", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-case", default=None,
-                    choices=["attn_prefill", "indexer_prefill", "block_decode", "block_decode_window", "hc"],
+                    choices=["attn_prefill", "indexer_prefill", "compressor_prefill", "gemm_prefill",
+                             "block_decode", "block_decode_window", "hc"],
                     help="profiling aid: run one prefill kernel alone on a 4096-query slice of config 4 "
-                         "(positions 60000..64095), or config 5's block step eagerly inside an NVTX range "
+                         "(positions 60000..64095), the two compressors on a 16384-token slice "
+                         "(compressor_prefill), the projection GEMM's two kernels on prefill shapes "
+                         "(gemm_prefill), or config 5's block step eagerly inside an NVTX range "
                          "(block_decode; block_decode_window: the same block at a ratio-128 layer), and print its "
                          "CUDA-event time; not a bench line")
     args = ap.parse_args()
@@ -1038,6 +1041,10 @@ def run_kernel_case(args):
         return run_block_case(args, dev)
     if args.kernel_case == "hc":
         return run_hc_case(args, dev)
+    if args.kernel_case == "compressor_prefill":
+        return run_compressor_case(args, dev)
+    if args.kernel_case == "gemm_prefill":
+        return run_gemm_case(args, dev)
     s, nwin, ncomp, top_k = 4096, 65536, 16384, 1024
     g = torch.Generator(device=dev).manual_seed(0)
     pos = torch.arange(60000, 60000 + s, dtype=torch.int32, device=dev)
@@ -1069,6 +1076,88 @@ def run_kernel_case(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
     print(json.dumps({"kernel_case": args.kernel_case, "queries": s, "ms_per_call": ms, **work}), flush=True)
+
+
+def run_compressor_case(args, dev):
+    """The two compressors of config 4 on 16,384 tokens (x [16384, 4096] bf16, 128 MB, above L2):
+    per compressor the projection pair (x wkv^T, x wgate^T in one tcgen05 launch, fp32 out) and the
+    pooling kernel (softmax over 8 slots, RMSNorm, RoPE, the cache rounding), each timed with CUDA
+    events over `--steps` calls. Prints one JSON line; not a bench line."""
+    mla, C = _mod("mla"), _mod("compressor")
+    NRm = _mod("norm_rope")
+    s, dim = 16384, 4096
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(s, dim, device=dev, generator=g).bfloat16()
+    reps = args.steps if args.steps is not None else 3
+    freqs = NRm.rope_freqs(64, dev)
+    res = {}
+    for tag, hd, aq, odt in (("main", 512, 1, torch.bfloat16), ("indexer", 128, 2, torch.float32)):
+        ws = [(torch.randn(2 * hd, dim, device=dev, generator=g) * 0.02).bfloat16() for _ in range(2)]
+        ape = torch.randn(4, 2 * hd, device=dev, generator=g) * 0.1
+        nw = torch.ones(hd, device=dev)
+        kv, sc = mla.linear_multi(x, ws, torch.float32)
+        out = torch.empty(1, s // 4, hd, dtype=odt, device=dev)
+        proj = lambda: mla.linear_multi(x, ws, torch.float32)
+        pool = lambda: C._pool(kv[None], sc[None], ape, nw, out, hd, 4, 64, freqs, pos0=0, act_quant=aq)
+        for name, fn in (("proj", proj), ("pool", pool)):
+            fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            if name == "proj":
+                res[f"{tag}_proj"] = {"ms": ms, "tflops": 2 * 2 * s * 2 * hd * dim / ms / 1e9}
+            else:
+                nbytes = 2 * kv.numel() * 4 + out.numel() * out.element_size()
+                res[f"{tag}_pool"] = {"ms": ms, "gbs": nbytes / ms / 1e6, "bytes": nbytes}
+    print(json.dumps({"kernel_case": "compressor_prefill", "tokens": s, **res}), flush=True)
+
+
+def run_gemm_case(args, dev):
+    """dsv4_linear on prefill shapes (bf16 x and W, fp32 y) with the tcgen05 kernel (kernel 2) and
+    the mma.sync kernel (kernel 1): median CUDA-event time of `--steps` calls (default 10) after 3
+    warm-up calls. Shapes: config 4's compressor projection over all 65,536 tokens and its indexer
+    twin, an 8,192-token chunk, q_up's width on 4,096 tokens, and config 1's 512 tokens."""
+    import ctypes
+    L = _mod("_lib")
+    reps = args.steps if args.steps is not None else 10
+    g = torch.Generator(device=dev).manual_seed(0)
+    rows = []
+    for m, n, k in ((65536, 1024, 4096), (65536, 256, 4096), (8192, 1024, 4096), (4096, 32768, 1024),
+                    (512, 1024, 4096)):
+        x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+        w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+        y = torch.empty(m, n, device=dev)
+        for kern in (2, 1):
+            p = L.LinearParams()
+            p.x, p.w, p.y = L.ptr(x), L.ptr(w), L.ptr(y)
+            p.m, p.n, p.k, p.groups, p.group = m, n, k, 1, 64
+            p.x_dtype, p.w_dtype, p.y_dtype, p.kernel = L.BF16, L.BF16, L.F32, kern
+            nb = L.lib().dsv4_linear_workspace_size(ctypes.byref(p))
+            ws = torch.empty(max(nb, 16), dtype=torch.uint8, device=dev)
+            p.workspace, p.workspace_bytes = L.ptr(ws), nb
+            st = L.stream_of(x)
+            fn = lambda: L.check(L.lib().dsv4_linear(ctypes.byref(p), st))
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            ms = sorted(ts)[len(ts) // 2]
+            rows.append({"m": m, "n": n, "k": k, "kernel": "tcgen05" if kern == 2 else "mma.sync", "ms": ms,
+                         "tflops": 2 * m * n * k / ms / 1e9})
+        del x, w, y
+    print(json.dumps({"kernel_case": "gemm_prefill", "calls": rows}), flush=True)
 
 
 def run_hc_case(args, dev):

@@ -7,8 +7,10 @@
 //   pooled[c] = sum_slot softmax_slot(score) * kv
 // then RMSNorm(norm_w), RoPE of the last rope_dim dims at position ratio*g (+pos0), and one
 // 128-bit vectorised store per thread into the cache (bf16) or a plain fp32 output; rows can be
-// scattered into a paged pool through out_rows. One CTA per compressed row, 256 threads, two
-// dims per thread. The decode kernel keeps the per-sequence ring [2*ratio, 2d] on the device.
+// scattered into a paged pool through out_rows. One CTA per compressed row, one thread per two
+// dims (up to 256 threads, whole warps). The decode kernel keeps the per-sequence ring [2*ratio, 2d] on the device.
+#include <algorithm>
+
 #include "common.cuh"
 #include "key_image.cuh"
 
@@ -150,6 +152,8 @@ __device__ __forceinline__ float pool8(const float* kv8, const float* sc8) {
   return num / den;
 }
 
+// One CTA per compressed row; blockDim = the row's pairs of dims rounded up to whole warps (at
+// most THREADS), so a 128-dim row (the indexer compressor) runs 64 threads, none idle.
 __global__ void __launch_bounds__(THREADS) pool_kernel(dsv4_compressor_params p) {
   pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
   pdl_trigger();
@@ -165,7 +169,7 @@ __global__ void __launch_bounds__(THREADS) pool_kernel(dsv4_compressor_params p)
   float vals[2][2];  // up to 2 pairs per thread (d <= 1024)
   float ss = 0.f;
   int npairs = 0;
-  for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++npairs) {
+  for (int c = threadIdx.x * 2; c < d; c += blockDim.x * 2, ++npairs) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       float kv8[16], sc8[16];
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(THREADS) pool_kernel(dsv4_compressor_params p)
   const float rinv = rsqrtf(ss / static_cast<float>(d) + p.eps);
   const int64_t orow = p.out_rows ? p.out_rows[rowid] : rowid;
   npairs = 0;
-  for (int c = threadIdx.x * 2; c < d; c += THREADS * 2, ++npairs)
+  for (int c = threadIdx.x * 2; c < d; c += blockDim.x * 2, ++npairs)
     finish_pair(vals[npairs][0], vals[npairs][1], c, d, p.rope_dim, p.norm_w, p.norm_dtype, rinv,
                 p.freqs, p.pos0 + R * g, p.out, orow, p.out_dtype, p.act_quant);
   if (p.act_quant == 2) {  // head_dim 128: threads 0..63 hold the row (uniform over the CTA)
@@ -480,7 +484,10 @@ extern "C" int dsv4_compressor_pool(const dsv4_compressor_params* p, void* strea
                    "dsv4_compressor_pool: norm dtype");
   const int groups = p->s / p->ratio;
   if (groups > 0) {
-    DSV4_CUDA_CHECK(launch_pdl(cmp::pool_kernel, dim3(static_cast<unsigned>(static_cast<int64_t>(p->b) * groups)), dim3(cmp::THREADS), 0, as_stream(stream), *p));
+    // one thread per pair of dims, whole warps, at most THREADS (2 pairs a thread above 512 dims)
+    const int threads = std::min(cmp::THREADS, (p->head_dim / 2 + 31) / 32 * 32);
+    const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(p->b) * groups));
+    DSV4_CUDA_CHECK(launch_pdl(cmp::pool_kernel, grid, dim3(threads), 0, as_stream(stream), *p));
     DSV4_LAUNCH_CHECK("compressor pool_kernel");
   }
   if (p->ring_kv && p->ring_score) {

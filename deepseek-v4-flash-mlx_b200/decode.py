@@ -28,7 +28,7 @@ import torch
 from . import _lib as L
 from .indexer import build_key_image, indexer_topk_into, key_image_buffers
 from .norm_rope import norm_rope, rope_freqs
-from .sparse_attn import _sparse_attn_op, sparse_attn_decode, sparse_attn_rope
+from .sparse_attn import sparse_attn_decode, sparse_attn_into, sparse_attn_rope
 
 # below this batch the decode step fuses q's norm + RoPE into the attention kernel (the head-group
 # kernel's prologue); from it on the norm runs on a side stream beside the indexer
@@ -207,15 +207,9 @@ def _decode_attention_op(kv_pool: torch.Tensor, k_idx: torch.Tensor, block_table
     b = q.shape[0]
     image = (key_image, key_inv, key_norm_max) if key_image is not None else None
     if b < FUSED_Q_MAX_BATCH:
-        # decode-sized batches: one stream, three kernels chained by programmatic dependent launch
-        # (scores, selection, attention); q's norm + RoPE is fused into the attention kernel
-        indexer_topk_into(idx_buf.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
-                          k_idx, top_k, positions.view(b, 1), ratio, out_col=0, out_offset=comp_base,
-                          block_table=block_table, page=page, key_image=image)
-        # the score kernel waits for all earlier work before the selection and the attention launch,
-        # so the attention may stage q and its window tiles before its own wait (pre_wait)
-        return _sparse_attn_op(q, kv_pool, sink, idx_buf, float(scale), out_dtype, freqs, positions, 64, 0, True,
-                               1e-6, win_base, int(window), False, 0, True)
+        out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
+        return _fused_decode_into(out, kv_pool, k_idx, block_table, win_base, image, q, q_idx, w_idx, sink, positions,
+                                  freqs, idx_buf, top_k, scale, window, ratio, page, comp_base)
     main = torch.cuda.current_stream(q.device)
     side = _side_stream(q.device)
     side.wait_stream(main)
@@ -228,6 +222,21 @@ def _decode_attention_op(kv_pool: torch.Tensor, k_idx: torch.Tensor, block_table
     qr.record_stream(main)
     return sparse_attn_rope(qr, kv_pool, sink, idx_buf, scale, positions, freqs, 64, out_dtype,
                             win_base=win_base, window=window)
+
+
+def _fused_decode_into(out, kv_pool, k_idx, block_table, win_base, image, q, q_idx, w_idx, sink, positions, freqs,
+                       idx_buf, top_k, scale, window, ratio, page, comp_base):
+    """Decode-sized batches: one stream, three kernels chained by programmatic dependent launch
+    (scores, selection, attention); q's norm + RoPE is fused into the attention kernel, which
+    stores o into `out` (device memory, or a pinned host block)."""
+    b = q.shape[0]
+    indexer_topk_into(idx_buf.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
+                      k_idx, top_k, positions.view(b, 1), ratio, out_col=0, out_offset=comp_base,
+                      block_table=block_table, page=page, key_image=image)
+    # the score kernel waits for all earlier work before the selection and the attention launch,
+    # so the attention may stage q and its window tiles before its own wait (pre_wait)
+    return sparse_attn_into(out, q, kv_pool, sink, idx_buf, float(scale), freqs, positions, 64, 0, True, 1e-6,
+                            win_base, int(window), False, 0, True)
 
 
 @_decode_attention_op.register_fake
@@ -351,6 +360,13 @@ class DecodeRunner:
         return decode_attention(self.cache, self.q, self.q_idx, self.w_idx, self.sink, self.positions, self.top_k,
                                 freqs=self.freqs, idx_buf=self.idx, out_dtype=self.out_dtype)
 
+    def _body_into(self, out):
+        c = self.cache
+        image = c.key_image if c.key_image is not None else None
+        return _fused_decode_into(out, c.kv_pool, c.k_idx, c.block_table, c.win_base, image, self.q, self.q_idx,
+                                  self.w_idx, self.sink, self.positions, self.freqs, self.idx, self.top_k,
+                                  c.head_dim ** -0.5, c.window, c.ratio, c.page, c.comp_base)
+
     def capture(self):
         with torch.cuda.stream(self.stream):
             if self.cache.image_stale:   # rebuilt here, never inside the captured step
@@ -364,10 +380,15 @@ class DecodeRunner:
         self.graph_host = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph_host, stream=self.stream):
             # the step's inputs and output cross the bus by kernel loads / stores of the pinned
-            # blocks (dsv4_copy), not copy-engine transfers: tens of KB, latency-bound
+            # blocks, not copy-engine transfers: tens of KB, latency-bound. The inputs by one copy
+            # kernel (dsv4_copy); at decode-sized batches the attention kernel stores o into the
+            # pinned output itself, else a second copy kernel brings it back.
             L.copy_(self.d_in, self.h_in)
-            out = self._body()
-            L.copy_(self.h_out, out)
+            if self.cache.batch < FUSED_Q_MAX_BATCH:
+                out = self._body_into(self.h_out)
+            else:
+                out = self._body()
+                L.copy_(self.h_out, out)
         self.out_host_graph = out
 
     def host_inputs(self):

@@ -41,6 +41,18 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
                     q_norm_rope: bool = False, q_eps: float = 1e-6, win_base: torch.Tensor | None = None,
                     window: int = 0, window_linear: bool = False, kernel: int = 0,
                     pre_wait: bool = False) -> torch.Tensor:
+    out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
+    sparse_attn_into(out, q, kv, attn_sink, topk_idxs, scale, rope_freqs, positions, rope_dim, num_splits, q_norm_rope,
+                     q_eps, win_base, window, window_linear, kernel, pre_wait)
+    return out
+
+
+def sparse_attn_into(out, q, kv, attn_sink, topk_idxs, scale, rope_freqs=None, positions=None, rope_dim=0,
+                     num_splits=0, q_norm_rope=False, q_eps=1e-6, win_base=None, window=0, window_linear=False,
+                     kernel=0, pre_wait=False):
+    """The body of `dsv4::sparse_attn` into a caller-owned `out` (q's shape, bf16 or fp32). `out`
+    may be pinned host memory (a unified-address pointer): the kernel then stores the result over
+    the bus itself, which a decode step captured with its host copies uses to skip the copy back."""
     q = q.contiguous()
     kv = kv.contiguous()
     if kv.dtype != torch.bfloat16:
@@ -49,7 +61,6 @@ def _sparse_attn_op(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor, 
         kv = kv16
     sink = attn_sink.float().contiguous()
     idx = topk_idxs.contiguous()
-    out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
     p = _attn_params(q, kv, sink, idx, out, scale, rope_freqs, positions, rope_dim, num_splits, q_norm_rope, q_eps,
                      win_base, window, window_linear, kernel, pre_wait)
     nbytes = L.lib().dsv4_sparse_attn_workspace_size(ctypes.byref(p))
