@@ -144,6 +144,7 @@ SIGNATURES = {
     "dsv4_linear_multi": (ctypes.c_int, [ctypes.POINTER(LinearMultiParams), vp]),
     "dsv4_cast": (ctypes.c_int, [vp, i32, vp, i32, i64, vp]),
     "dsv4_copy": (ctypes.c_int, [vp, vp, sz, vp]),
+    "dsv4_copy_beside": (ctypes.c_int, [vp, vp, sz, vp]),
 }
 
 _lib = None
@@ -216,6 +217,16 @@ def device_error(stream=None):
     s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream if stream is None else stream)
     check(lib().dsv4_device_error(ctypes.byref(code), s))
     return code.value
+
+
+def copy_beside_(dst, src, stream=None):
+    """dst <- src as `copy_`, overlapped with the kernel launched before it (dsv4_copy_beside)."""
+    nbytes = src.numel() * src.element_size()
+    if dst.numel() * dst.element_size() != nbytes or not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("dsv4 copy_beside_: contiguous tensors of the same size in bytes")
+    s = stream if stream is not None else ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    check(lib().dsv4_copy_beside(ptr(dst), ptr(src), nbytes, s))
+    return dst
 
 
 def copy_(dst, src, stream=None):

@@ -77,6 +77,17 @@ __global__ void copy16_kernel(const uint4* __restrict__ src, uint4* __restrict__
     dst[i] = src[i];
 }
 
+// The copy of dsv4_copy_beside: it runs while the kernel launched before it finishes (no wait
+// first), makes its stores visible device-wide and only then lets the next kernel launch, and waits
+// for the kernel before it at the end, so that the next kernel's wait covers both.
+__global__ void copy16_beside_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t n16) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+  __threadfence();
+  pdl_trigger();
+  pdl_wait();
+}
+
 }  // namespace dsv4
 
 using namespace dsv4;
@@ -154,6 +165,20 @@ int dsv4_copy(void* dst, const void* src, size_t bytes, void* stream) {
   int blocks = static_cast<int>((n16 + 255) / 256);
   if (blocks > 2 * num_sms()) blocks = 2 * num_sms();
   DSV4_CUDA_CHECK(launch_pdl(copy16_kernel, dim3(blocks), dim3(256), 0, as_stream(stream),
+                             reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n16));
+  return DSV4_OK;
+}
+
+int dsv4_copy_beside(void* dst, const void* src, size_t bytes, void* stream) {
+  DSV4_CHECK_ARG(dst && src, "dsv4_copy_beside: NULL pointer");
+  DSV4_CHECK_ARG(reinterpret_cast<uintptr_t>(dst) % 16 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+                     bytes % 16 == 0,
+                 "dsv4_copy_beside: addresses and size must be multiples of 16 bytes");
+  if (bytes == 0) return DSV4_OK;
+  const int64_t n16 = static_cast<int64_t>(bytes / 16);
+  int blocks = static_cast<int>((n16 + 255) / 256);
+  if (blocks > 2 * num_sms()) blocks = 2 * num_sms();
+  DSV4_CUDA_CHECK(launch_pdl(copy16_beside_kernel, dim3(blocks), dim3(256), 0, as_stream(stream),
                              reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n16));
   return DSV4_OK;
 }

@@ -225,14 +225,17 @@ def _decode_attention_op(kv_pool: torch.Tensor, k_idx: torch.Tensor, block_table
 
 
 def _fused_decode_into(out, kv_pool, k_idx, block_table, win_base, image, q, q_idx, w_idx, sink, positions, freqs,
-                       idx_buf, top_k, scale, window, ratio, page, comp_base):
+                       idx_buf, top_k, scale, window, ratio, page, comp_base, before_attention=None):
     """Decode-sized batches: one stream, three kernels chained by programmatic dependent launch
     (scores, selection, attention); q's norm + RoPE is fused into the attention kernel, which
-    stores o into `out` (device memory, or a pinned host block)."""
+    stores o into `out` (device memory, or a pinned host block). `before_attention` (optional)
+    launches work between the selection and the attention (the host step's copy of q)."""
     b = q.shape[0]
     indexer_topk_into(idx_buf.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
                       k_idx, top_k, positions.view(b, 1), ratio, out_col=0, out_offset=comp_base,
                       block_table=block_table, page=page, key_image=image)
+    if before_attention is not None:
+        before_attention()
     # the score kernel waits for all earlier work before the selection and the attention launch,
     # so the attention may stage q and its window tiles before its own wait (pre_wait)
     return sparse_attn_into(out, q, kv_pool, sink, idx_buf, float(scale), freqs, positions, 64, 0, True, 1e-6,
@@ -338,6 +341,7 @@ class DecodeRunner:
             offs.append(total)
             total += -(-math.prod(shape) * torch.empty((), dtype=dt).element_size() // 256) * 256
         self._in_bytes = total
+        self._q_bytes = offs[1]  # q's field, padded to 256 bytes
         self.d_in = torch.zeros(total, dtype=torch.uint8, device=dev)
         self.h_in = torch.zeros(total, dtype=torch.uint8).pin_memory()
 
@@ -360,12 +364,12 @@ class DecodeRunner:
         return decode_attention(self.cache, self.q, self.q_idx, self.w_idx, self.sink, self.positions, self.top_k,
                                 freqs=self.freqs, idx_buf=self.idx, out_dtype=self.out_dtype)
 
-    def _body_into(self, out):
+    def _body_into(self, out, before_attention=None):
         c = self.cache
         image = c.key_image if c.key_image is not None else None
         return _fused_decode_into(out, c.kv_pool, c.k_idx, c.block_table, c.win_base, image, self.q, self.q_idx,
                                   self.w_idx, self.sink, self.positions, self.freqs, self.idx, self.top_k,
-                                  c.head_dim ** -0.5, c.window, c.ratio, c.page, c.comp_base)
+                                  c.head_dim ** -0.5, c.window, c.ratio, c.page, c.comp_base, before_attention)
 
     def capture(self):
         with torch.cuda.stream(self.stream):
@@ -383,10 +387,16 @@ class DecodeRunner:
             # blocks, not copy-engine transfers: tens of KB, latency-bound. The inputs by one copy
             # kernel (dsv4_copy); at decode-sized batches the attention kernel stores o into the
             # pinned output itself, else a second copy kernel brings it back.
-            L.copy_(self.d_in, self.h_in)
             if self.cache.batch < FUSED_Q_MAX_BATCH:
-                out = self._body_into(self.h_out)
+                # q (the block's first field) is read only by the attention: its copy runs beside
+                # the top-k selection (dsv4_copy_beside), so only q_idx, w_idx and the positions
+                # cross the bus before the scores
+                nq = self._q_bytes
+                L.copy_(self.d_in[nq:], self.h_in[nq:])
+                out = self._body_into(self.h_out,
+                                      before_attention=lambda: L.copy_beside_(self.d_in[:nq], self.h_in[:nq]))
             else:
+                L.copy_(self.d_in, self.h_in)
                 out = self._body()
                 L.copy_(self.h_out, out)
         self.out_host_graph = out

@@ -469,6 +469,12 @@ DSV4_API int dsv4_cast(const void* x, int32_t x_dtype, void* y, int32_t y_dtype,
  * less than a copy-engine transfer. Ordered in the stream like any kernel (programmatic dependent
  * launch: it waits for the kernel before it). */
 DSV4_API int dsv4_copy(void* dst, const void* src, size_t bytes, void* stream);
+/* As dsv4_copy, but overlapped with the kernel launched before it on the stream (programmatic
+ * dependent launch): the copy starts without waiting for that kernel, lets the next kernel launch
+ * only once its own stores are visible, and waits for that kernel before it completes, so the next
+ * kernel's dependency wait covers both. The kernel before must neither read nor write dst or src.
+ * A decode step uses it to bring q in beside the top-k selection (no reference counterpart). */
+DSV4_API int dsv4_copy_beside(void* dst, const void* src, size_t bytes, void* stream);
 
 #ifdef __cplusplus
 }
