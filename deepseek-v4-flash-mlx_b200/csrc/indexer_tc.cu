@@ -470,10 +470,13 @@ template <int NT>
 __device__ __forceinline__ void split_query(const ApproxArgs& P, int64_t row, uint8_t* qh, uint8_t* ql, float* w) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int NW = NT / 32, QH = HI / NW;
+  static_assert(QH <= 32, "one head weight per lane");
   float4 qv[QH];
 #pragma unroll
   for (int k = 0; k < QH; ++k)
     qv[k] = __ldg(reinterpret_cast<const float4*>(P.q + (row * HI + warp + k * NW) * DI) + lane);
+  // the warp's head weights with the rows (lane k: head warp + k NW), not one dependent load per head
+  const float wl = lane < QH ? __ldg(P.w + row * HI + warp + lane * NW) : 0.f;
 #pragma unroll
   for (int k = 0; k < QH; ++k) {
     const int h = warp + k * NW;
@@ -487,7 +490,8 @@ __device__ __forceinline__ void split_query(const ApproxArgs& P, int64_t row, ui
                                                (lane & 1) * 8);
     *reinterpret_cast<uint2*>(qh + off) = hi;
     *reinterpret_cast<uint2*>(ql + off) = lo;
-    if (lane == 0) w[h] = P.w[row * HI + h] * pow2(-sh);
+    const float wk = __shfl_sync(0xffffffffu, wl, k);
+    if (lane == 0) w[h] = wk * pow2(-sh);
   }
 }
 
@@ -685,12 +689,21 @@ __global__ void __launch_bounds__(SQ_THREADS) approx_score_seq_kernel(ApproxArgs
   if (warp == 0) tmem_dealloc<64>(tmem);
 }
 
-// ---- decode batches over a cache-kept key image: the persistent walk of approx_score_seq_kernel
-// without the split. Each visible 128-key tile's 64 KB image lands by one bulk copy (three in
-// flight), then 24 MMAs and the fold (thread = key, inverse scale from the cache). About 225 KB of
-// shared memory: one CTA per SM.
-constexpr int IM_THREADS = 128;
+// ---- decode batches over a cache-kept key image: a persistent CTA per SM walks a contiguous run of
+// (query, key tile) items, warp-specialised. Warp 4 (one lane) streams each visible 128-key tile's
+// 64 KB image by one bulk copy into a ring of three slots and issues the item's 24 MMAs (M = 128
+// keys, N = 64 heads) into one of two 64-column TMEM accumulators; warps 0-3 (thread = key = TMEM
+// lane) fold item k - 1 while the MMAs of item k run, and scale and split every query they meet into
+// the Q slabs. The next query's loads are issued one item ahead, and the first query's before the
+// first image copies (behind 28 MB of image copies they waited ~5 us). About 225 KB of shared
+// memory: one CTA per SM.
+constexpr int IM_FOLD = 128;              // fold warps 0-3
+constexpr int IM_MMA_WARP = IM_FOLD / 32;  // warp 4: MMAs
+constexpr int IM_COPY_WARP = IM_MMA_WARP + 1;  // warp 5: image copies (a copy's issue may wait for the
+                                               // bulk-copy unit, which must not hold up the MMAs)
+constexpr int IM_THREADS = IM_FOLD + 64;
 constexpr int IM_SLOTS = 3;
+constexpr int IM_QH = HI / (IM_FOLD / 32);  // heads per fold warp in the query split
 
 struct ImgSmem {  // dynamic shared memory
   alignas(1024) uint8_t img[IM_SLOTS][TILE_BYTES];
@@ -699,8 +712,11 @@ struct ImgSmem {  // dynamic shared memory
 };
 struct ImgSmall {  // static shared memory
   float w[HI];
-  uint64_t full[IM_SLOTS], mma;
+  uint64_t full[IM_SLOTS], slot_free[IM_SLOTS];  // tile landed / its MMAs done
+  uint64_t acc_full[2], acc_free[2];            // accumulator written / folded
+  uint64_t q_ready, fin;                        // Q slabs of the next query split / every MMA done
   uint32_t tmem_base;
+  int abort;
 };
 static_assert(sizeof(ImgSmem) + 1024 + sizeof(ImgSmall) + 256 <= 232448,
               "shared memory above the 227 KB a CTA may opt into");
@@ -714,100 +730,187 @@ __device__ __forceinline__ void img_issue(const ApproxArgs& P, ImgSmem& sm, ImgS
   bulk_g2s(sm.img[slot], P.kimg + (static_cast<int64_t>(b) * P.img_tiles + t) * TILE_BYTES, TILE_BYTES, &sx.full[slot]);
 }
 
-__global__ void __launch_bounds__(IM_THREADS) approx_score_img_kernel(ApproxArgs P, int64_t per) {
+__device__ __forceinline__ void img_set_abort(ImgSmall& sx) {
+  if (!*reinterpret_cast<volatile int*>(&sx.abort)) {
+    *reinterpret_cast<volatile int*>(&sx.abort) = 1;
+    raise_device_error(DSV4_ERR_WAIT_TIMEOUT);
+  }
+}
+
+// the fold warps' own barrier; returns true when every fold thread passed true
+__device__ __forceinline__ bool fold_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.and.pred q, 1, %2, p;\nselp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(IM_FOLD)
+      : "memory");
+  return r != 0;
+}
+
+// query `row` (64 heads x 128 fp32) into registers: fold warp w holds heads w, w + 4, .., and lane k
+// the weight of head w + 4 k
+__device__ __forceinline__ void img_query_load(const ApproxArgs& P, int64_t row, float4 (&qv)[IM_QH], float& wl) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < IM_QH; ++k)
+    qv[k] = __ldg(reinterpret_cast<const float4*>(P.q + (row * HI + warp + k * (IM_FOLD / 32)) * DI) + lane);
+  wl = lane < IM_QH ? __ldg(P.w + row * HI + warp + lane * (IM_FOLD / 32)) : 0.f;
+}
+// scale and split the loaded query into the Q slabs and the scaled head weights (as split_query)
+__device__ __forceinline__ void img_query_store(const float4 (&qv)[IM_QH], float wl, uint8_t* qh, uint8_t* ql,
+                                                float* w) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < IM_QH; ++k) {
+    const int h = warp + k * (IM_FOLD / 32);
+    float mx = amax4(qv[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int sh = row_shift(mx);
+    uint2 hi, lo;
+    split4(scale4(qv[k], pow2(sh)), &hi, &lo);
+    const uint32_t off = static_cast<uint32_t>((lane >> 4) * RSLAB_Q + h * 128 + ((((lane >> 1) & 7) ^ (h & 7)) << 4) +
+                                               (lane & 1) * 8);
+    *reinterpret_cast<uint2*>(qh + off) = hi;
+    *reinterpret_cast<uint2*>(ql + off) = lo;
+    const float wk = __shfl_sync(0xffffffffu, wl, k);
+    if (lane == 0) w[h] = wk * pow2(-sh);
+  }
+}
+
+__global__ void __launch_bounds__(IM_THREADS, 1) approx_score_img_kernel(ApproxArgs P, int64_t per) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   ImgSmem& sm = *reinterpret_cast<ImgSmem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
   __shared__ ImgSmall sx;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tiles = key_tiles(P.n_keys);
   const int64_t items = static_cast<int64_t>(P.batch) * P.s * tiles;
   const int64_t begin = static_cast<int64_t>(blockIdx.x) * per;
-  SeqWalk walk{begin + per < items ? begin + per : items, tiles};
-  SeqWalk pwalk = walk;  // the producer's own cursor state
-  if (warp == 0) tmem_alloc<64>(&sx.tmem_base);
+  const int64_t end = begin + per < items ? begin + per : items;
+  if (warp == 0) tmem_alloc<128>(&sx.tmem_base);
   if (tid == 0) {
-    for (int k = 0; k < IM_SLOTS; ++k) bar_init(&sx.full[k], 1);
-    bar_init(&sx.mma, 1);
+    for (int k = 0; k < IM_SLOTS; ++k) {
+      bar_init(&sx.full[k], 1);
+      bar_init(&sx.slot_free[k], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      bar_init(&sx.acc_full[a], 1);
+      bar_init(&sx.acc_free[a], IM_FOLD / 32);
+    }
+    bar_init(&sx.q_ready, 1);
+    bar_init(&sx.fin, 1);
+    sx.abort = 0;
     bar_init_fence();
   }
+  SeqWalk walk{end, tiles};
+  const int64_t i0 = walk.next_valid(P, begin);
+  float4 qv[IM_QH];
+  float wl = 0.f;
+  if (warp < IM_FOLD / 32 && i0 < end) img_query_load(P, i0 / tiles, qv, wl);  // ahead of the image copies
   before_sync();
   __syncthreads();
   after_sync();
   const uint32_t tmem = sx.tmem_base;
-  int64_t pnext = 0;
-  int issued = 0;
-  if (tid == 0) {
-    pnext = pwalk.next_valid(P, begin);
-    for (int k = 0; k < IM_SLOTS && pnext < walk.end; ++k) {
-      img_issue(P, sm, sx, k, pnext, tiles);
-      ++issued;
-      pnext = pwalk.next_valid(P, pnext + 1);
+  const volatile int* abort = &sx.abort;
+
+  if (warp == IM_COPY_WARP) {
+    // ---------------------------------------------------------------- image copies (one lane)
+    if (lane == 0) {
+      SeqWalk pw{end, tiles};
+      int issued = 0;
+      bool ok = true;
+      for (int64_t p = i0; p < end; p = pw.next_valid(P, p + 1), ++issued) {
+        const int slot = issued % IM_SLOTS;
+        // the slot's previous tile (item issued - IM_SLOTS) has been read by its MMAs
+        if (issued >= IM_SLOTS &&
+            !(ok = bar_wait_or_abort(&sx.slot_free[slot], ((issued - IM_SLOTS) / IM_SLOTS) & 1, abort)))
+          break;
+        img_issue(P, sm, sx, slot, p, tiles);
+      }
+      if (!ok) img_set_abort(sx);
+      // the copies issued land before the CTA's shared memory goes away (bounded; immediate when
+      // the MMAs consumed them)
+      for (int kk = issued - IM_SLOTS > 0 ? issued - IM_SLOTS : 0; kk < issued; ++kk)
+        bar_wait(&sx.full[kk % IM_SLOTS], (kk / IM_SLOTS) & 1);
     }
-  }
-  int64_t cur_row = -1;
-  int k = 0;
-  bool ok = true, mma_pending = false;
-  for (int64_t i = walk.next_valid(P, begin); i < walk.end; ++k) {
-    const int64_t row = i / tiles;
-    const int t = static_cast<int>(i % tiles);
-    const int b = static_cast<int>(row / P.s);
-    const int slot = k % IM_SLOTS;
-    if (row != cur_row) {  // the previous item's MMAs are done (waited below): the Q slabs are free
-      __syncthreads();
-      split_query<IM_THREADS>(P, row, sm.qh, sm.ql, sx.w);
-      fence_async_smem();
-      cur_row = row;
-    }
-    const int j = t * BM + tid;
-    const float ki = j < P.n_keys ? __ldg(P.kinv + static_cast<int64_t>(b) * P.img_tiles * BM + j) : 0.f;
-    before_sync();
-    __syncthreads();  // the Q slabs written; the previous item's TMEM reads done
-    after_sync();
-    int ok0 = 1;
-    if (tid == 0) {
-      ok0 = bar_wait(&sx.full[slot], (k / IM_SLOTS) & 1);
-      if (ok0) {
+  } else if (warp == IM_MMA_WARP) {
+    // ---------------------------------------------------------------- MMAs (one lane)
+    if (lane == 0) {
+      int k = 0, rc = 0;
+      bool ok = true;
+      int64_t prev_row = -1;
+      for (int64_t i = i0; i < end; i = walk.next_valid(P, i + 1), ++k) {
+        const int64_t row = i / tiles;
+        const int slot = k % IM_SLOTS, a = k & 1;
+        if (row != prev_row) {  // the fold warps have split this query into the Q slabs
+          if (!(ok = bar_wait_or_abort(&sx.q_ready, rc & 1, abort))) break;
+          ++rc;
+          prev_row = row;
+        }
+        if (!(ok = bar_wait_or_abort(&sx.acc_free[a], ((k >> 1) & 1) ^ 1, abort))) break;
+        if (!(ok = bar_wait_or_abort(&sx.full[slot], (k / IM_SLOTS) & 1, abort))) break;
         after_sync();
         constexpr uint32_t id = idesc_f16<128, HI>(false, false);
+        const uint32_t d = tmem + a * HI;
         const uint32_t qh = smem_u32(sm.qh), ql = smem_u32(sm.ql), kb = smem_u32(sm.img[slot]);
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
           const uint32_t kh = kb + g * GROUP, kl = kh + SLAB_K;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma16(tmem, sdesc(kl + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id,
-                  (g | kk) ? 1u : 0u);
+            mma16(d, sdesc(kl + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id, (g | kk) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma16(tmem, sdesc(kh + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
+            mma16(d, sdesc(kh + kk * 32, 16, 1024), sdesc(qh + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma16(tmem, sdesc(kh + kk * 32, 16, 1024), sdesc(ql + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
+            mma16(d, sdesc(kh + kk * 32, 16, 1024), sdesc(ql + g * RSLAB_Q + kk * 32, 16, 1024), id, 1u);
         }
-        mma_commit(&sx.mma);
+        mma_commit(&sx.acc_full[a]);
+        mma_commit(&sx.slot_free[slot]);
       }
+      mma_commit(&sx.fin);  // every MMA issued (also on abort) is done before the CTA winds down
+      bar_wait(&sx.fin, 0);
+      if (!ok) img_set_abort(sx);
     }
-    ok = __syncthreads_and(ok0);
-    if (!ok) break;
-    ok = __syncthreads_and(bar_wait(&sx.mma, k & 1));
-    if (!ok) {
-      mma_pending = true;
-      ++k;  // this item's copy has landed
-      break;
-    }
-    after_sync();
-    if (tid == 0 && pnext < walk.end) {  // the MMAs have read the slot: refill it
-      img_issue(P, sm, sx, slot, pnext, tiles);
-      ++issued;
-      pnext = pwalk.next_valid(P, pnext + 1);
-    }
-    {  // the fold: thread = key (TMEM lane)
-      const uint32_t lq = static_cast<uint32_t>(warp * 32) << 16;
+  } else {
+    // ---------------------------------------------------------------- fold warps 0-3 (thread = key)
+    const uint32_t lq = static_cast<uint32_t>(warp * 32) << 16;
+    int64_t prev_row = -1;
+    int k = 0;
+    for (int64_t i = i0; i < end; ++k) {
+      const int64_t row = i / tiles;
+      const int t = static_cast<int>(i % tiles);
+      const int b = static_cast<int>(row / P.s);
+      const int a = k & 1;
+      const int64_t inext = walk.next_valid(P, i + 1);
+      if (row != prev_row) {
+        // item k - 1 (the previous query's last) is folded by every fold warp and its MMAs are done:
+        // the Q slabs and the head weights are free
+        if (prev_row >= 0) fold_bar_and(true);
+        img_query_store(qv, wl, sm.qh, sm.ql, sx.w);
+        fence_async_smem();
+        fold_bar_and(true);
+        if (tid == 0) bar_arrive(&sx.q_ready);
+        prev_row = row;
+        if (inext < end && inext / tiles != row) img_query_load(P, inext / tiles, qv, wl);
+      } else if (inext < end && inext / tiles != row) {
+        img_query_load(P, inext / tiles, qv, wl);  // the next query's loads, one item ahead
+      }
+      const int j = t * BM + tid;
+      const float ki = j < P.n_keys ? __ldg(P.kinv + static_cast<int64_t>(b) * P.img_tiles * BM + j) : 0.f;
+      const bool ok = fold_bar_and(bar_wait_or_abort(&sx.acc_full[a], (k >> 1) & 1, abort));
+      if (!ok) {
+        if (tid == 0) img_set_abort(sx);
+        break;
+      }
+      after_sync();
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
       for (int c = 0; c < HI; c += 16) {
         float sc[16];
-        tmem_ld16(tmem + lq + c, sc);
+        tmem_ld16(tmem + lq + a * HI + c, sc);
         tmem_wait_ld();
 #pragma unroll
         for (int h = 0; h < 16; h += 4) {
@@ -819,21 +922,16 @@ __global__ void __launch_bounds__(IM_THREADS) approx_score_img_kernel(ApproxArgs
         }
       }
       if (j < P.n_keys) P.scores[row * P.n_pad + j] = ((a0 + a1) + (a2 + a3)) * ki;
-    }
-    i = walk.next_valid(P, i + 1);
-  }
-  if (!ok) {
-    if (tid == 0) {
-      raise_device_error(DSV4_ERR_WAIT_TIMEOUT);
-      // let the copies still in flight land before the CTA's shared memory goes away (bounded)
-      for (int kk = k; kk < issued; ++kk) bar_wait(&sx.full[kk % IM_SLOTS], (kk / IM_SLOTS) & 1);
-      if (mma_pending) bar_wait(&sx.mma, (k - 1) & 1);
+      before_sync();
+      __syncwarp();
+      if (lane == 0) bar_arrive(&sx.acc_free[a]);
+      i = inext;
     }
   }
   before_sync();
   __syncthreads();
   after_sync();
-  if (warp == 0) tmem_dealloc<64>(tmem);
+  if (warp == 0) tmem_dealloc<128>(tmem);
 }
 
 DSV4_ERROR_READER(indexer_tc)
