@@ -194,7 +194,33 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
     sm.abort = 0;
     bar_init_fence();
   }
-  // Q -> 8 swizzled slabs (64 heads x 128 B)
+  // gather workers (warps 1-11): this worker's (row, chunk) positions within a slab pair: c = wt + 352 k
+  // < 2048; row c / 16, chunk c % 16 (slab 2mt + chunk / 8, 16-byte chunk chunk % 8 of the row's 128 B)
+  const int wt = tid - W_WARP0 * 32;
+  int nown = 0;
+#pragma unroll
+  for (int k = 0; k < W_CHUNKS; ++k) nown += (wt + W_THREADS * k < BN * 16);
+  auto load_rows = [&](int i, int* rr) {
+#pragma unroll
+    for (int k = 0; k < W_CHUNKS; ++k) {
+      const int c = wt + W_THREADS * k;
+      int32_t v = 0;
+      if (k < nown) {
+        const int u = (tbase + i) * BN + (c >> 4);
+        int64_t r = u < L ? list_row(P, qi, u) : -1;
+        if (r >= P.n) {
+          raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
+          r = -1;
+        }
+        v = static_cast<int32_t>(r < 0 ? 0 : r);  // masked rows fetch row 0; their p is 0
+      }
+      rr[k] = v;
+    }
+  };
+  // Q -> 8 swizzled slabs (64 heads x 128 B); the first tile's row numbers and the softmax rows'
+  // validity (dependent index loads) are fetched while Q lands
+  int rr[W_CHUNKS];
+  bool valid0 = false;
   {
     const uint32_t qs = smem_u32(sm.q);
     const __nv_bfloat16* qg = P.q + qi * HB * D;
@@ -203,6 +229,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       cp_async16(qs + slab_off(hh, ch, SLAB_Q), qg + hh * D + ch * 8, true);
     }
     asm volatile("cp.async.commit_group;\n" ::);
+    if (warp >= W_WARP0 && ntiles > 0) load_rows(0, rr);
+    if (warp >= SM_WARP0) valid0 = row_valid(P, qi, tbase * BN + (warp & 3) * 32 + lane, L);
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   }
   fence_async_smem();
@@ -252,32 +280,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
     }
   } else {
     // ---------------------------------------------------------------- gather workers (warps 1-11)
-    const int wt = tid - W_WARP0 * 32;
     const bool smx = warp >= SM_WARP0;
-    // this worker's (row, chunk) positions within a slab pair: c = wt + 352 k < 2048; row c / 16,
-    // chunk c % 16 (slab 2mt + chunk / 8, 16-byte chunk chunk % 8 of the row's 128 bytes)
-    int nown = 0;
-#pragma unroll
-    for (int k = 0; k < W_CHUNKS; ++k) nown += (wt + W_THREADS * k < BN * 16);
-    auto load_rows = [&](int i, int* rr) {
-#pragma unroll
-      for (int k = 0; k < W_CHUNKS; ++k) {
-        const int c = wt + W_THREADS * k;
-        int32_t v = 0;
-        if (k < nown) {
-          const int u = (tbase + i) * BN + (c >> 4);
-          int64_t r = u < L ? list_row(P, qi, u) : -1;
-          if (r >= P.n) {
-            raise_device_error(DSV4_ERR_INDEX_OUT_OF_RANGE);
-            r = -1;
-          }
-          v = static_cast<int32_t>(r < 0 ? 0 : r);  // masked rows fetch row 0; their p is 0
-        }
-        rr[k] = v;
-      }
-    };
-    int rr[W_CHUNKS];
-    if (ntiles > 0) load_rows(0, rr);
     const uint32_t ks = smem_u32(sm.kv);
 
     // softmax state (warps 4-11)
@@ -301,7 +304,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
       }
       before_sync();
       sm_bar();
-      valid = row_valid(P, qi, tbase * BN + row, L);
+      valid = valid0;
     }
     bool ok = true;
     for (int i = 0; i < ntiles; ++i) {
