@@ -53,6 +53,7 @@ struct Smem {
   alignas(1024) uint8_t p[BN * 128];        // 16 KB: P^T rows (64 heads x bf16)
   float red[4][HB];                         // per-quadrant column maxima
   float alpha[HB];                          // rescale factors of a tile that raised m
+  float rope_c[32], rope_s[32];             // the query position's RoPE angles (rope_dim <= 64)
   uint64_t bar_full[4];                     // slab pair mt of the current tile landed (one arrival per worker)
   uint64_t bar_empty[4];                    // O^T M-tile mt done: slab pair mt free
   uint64_t bar_s, bar_p, bar_fin;           // S^T done / P^T published / everything issued done
@@ -231,6 +232,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
     asm volatile("cp.async.commit_group;\n" ::);
     if (warp >= W_WARP0 && ntiles > 0) load_rows(0, rr);
     if (warp >= SM_WARP0) valid0 = row_valid(P, qi, tbase * BN + (warp & 3) * 32 + lane, L);
+    // the RoPE angles of the query's position, once per CTA (one sincosf per lane of warp 0, which
+    // is idle here): the epilogue's inverse rotation reads them from shared memory
+    if (warp == 0 && P.rope_freqs != nullptr && P.rope_dim <= 64 && lane < P.rope_dim / 2)
+      rope_cos_sin(P.positions[qi], P.rope_freqs[lane], &sm.rope_c[lane], &sm.rope_s[lane]);
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   }
   fence_async_smem();
@@ -423,7 +428,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
         ok = __all_sync(0xffffffffu, bar_wait_or_abort(&sm.bar_fin, 0, abort));
         if (!ok && lane == 0) set_abort(sm);
       }
-      if (ok && !*abort && P.splits > 1) {
+      ok = ok && !*abort;
+      if (ok && P.splits > 1) {
         after_sync();
         // split partial: O unnormalised (relative to m), m and l per head, for the combine kernel;
         // part [s][splits][64][512] then [s][splits][64][2]
@@ -467,30 +473,46 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
             pml[(half * 32 + lane) * 2 + 1] = 0.f;
           }
         }
-      } else if (ok && !*abort) {
+      } else if (ok) {
         after_sync();
-        // epilogue: lane = dim (within the M-tile quadrant), 32 heads per thread
+        // epilogue: lane = dim (within the M-tile quadrant), 32 heads per thread. m and l are the
+        // same in every lane, so lane c computes the normaliser of head half * 32 + c once and the
+        // warp shares it (the exp and the division per head per lane took ~4.6 us)
         float inv[32];
         {
           float l[32];
           tmem_ld16(tmem + lq + COL_L + half * 32, l);
           tmem_ld16(tmem + lq + COL_L + half * 32 + 16, l + 16);
           tmem_wait_ld();
+          float mm = 0.f, ll = 0.f;
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int hh = half * 32 + c;
-            inv[c] = (m[c] == -INFINITY) ? __int_as_float(0x7fc00000)
-                                         : 1.f / (l[c] + exp2f(P.sink[hh] * LOG2E - m[c]));
-          }
+          for (int c = 0; c < 32; ++c)
+            if (c == lane) {
+              mm = m[c];
+              ll = l[c];
+            }
+          const float mine = (mm == -INFINITY) ? __int_as_float(0x7fc00000)
+                                               : 1.f / (ll + exp2f(P.sink[half * 32 + lane] * LOG2E - mm));
+#pragma unroll
+          for (int c = 0; c < 32; ++c) inv[c] = __shfl_sync(0xffffffffu, mine, c);
         }
         const bool rope = P.rope_freqs != nullptr;
         const int pos = rope ? P.positions[qi] : 0;
+        const bool bf = P.out_dtype == DSV4_BF16;
 #pragma unroll 1
         for (int mt = 0; mt < 4; ++mt) {
           const int d = mt * 128 + qd * 32 + lane;
           const bool do_rope = rope && d >= D - P.rope_dim;
           float cs = 1.f, sn = 0.f;
-          if (do_rope) rope_cos_sin(pos, P.rope_freqs[(d - (D - P.rope_dim)) >> 1], &cs, &sn);
+          if (do_rope) {
+            const int f = (d - (D - P.rope_dim)) >> 1;
+            if (P.rope_dim <= 64) {
+              cs = sm.rope_c[f];
+              sn = sm.rope_s[f];
+            } else {
+              rope_cos_sin(pos, P.rope_freqs[f], &cs, &sn);
+            }
+          }
           float v[32];
           tmem_ld16(tmem + lq + COL_O + mt * HB + half * 32, v);
           tmem_ld16(tmem + lq + COL_O + mt * HB + half * 32 + 16, v + 16);
@@ -511,7 +533,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
               }
             }
             const int64_t off = (qi * P.h + half * 32 + c) * D + d;
-            if (P.out_dtype == DSV4_BF16)
+            if (bf)
               reinterpret_cast<__nv_bfloat16*>(P.out)[off] = __float2bfloat16_rn(xo);
             else
               reinterpret_cast<float*>(P.out)[off] = xo;
