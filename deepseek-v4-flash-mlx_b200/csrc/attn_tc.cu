@@ -362,22 +362,28 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(Params P) {
         grow = true;
       }
       if (grow) {
+        bool grow_any = false;
         // exact tile maximum per head, then m = max(m, tile max); O^T and L rescaled by 2^(m_old - m)
         sm.red[qd][half * 32 + lane] = warp_col_max32(x);
         sm_bar();
-        // the rescale factors go to shared memory (every warp of a half writes the same values)
-        bool any = false;
+        // the rescale factors go to shared memory (every warp of a half writes the same values); m is
+        // the same in every lane, so lane c updates head half * 32 + c and the warp shares the result
+        float mo = 0.f;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int hh = half * 32 + c;
+        for (int c = 0; c < 32; ++c)
+          if (c == lane) mo = m[c];
+        {
+          const int hh = half * 32 + lane;
           const float tm = fmaxf(fmaxf(sm.red[0][hh], sm.red[1][hh]), fmaxf(sm.red[2][hh], sm.red[3][hh]));
-          const float mn = fmaxf(m[c], tm);
-          if (lane == c) sm.alpha[hh] = (m[c] == -INFINITY) ? 0.f : exp2f(m[c] - mn);
-          any |= (mn != m[c]) && (m[c] != -INFINITY);
-          m[c] = mn;
+          const float mn = fmaxf(mo, tm);
+          sm.alpha[hh] = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+          const bool any = __any_sync(0xffffffffu, (mn != mo) && (mo != -INFINITY));
+#pragma unroll
+          for (int c = 0; c < 32; ++c) m[c] = __shfl_sync(0xffffffffu, mn, c);
+          grow_any = any;
         }
         sm_bar();  // red[] reuse; alpha[] written
-        if (i > 0 && __any_sync(0xffffffffu, any)) {
+        if (i > 0 && grow_any) {
           // the previous tile's O^T and L MMAs completed before this tile's S^T (one commit covers all)
 #pragma unroll 1
           for (int mt = 0; mt < 4; ++mt) {
