@@ -502,42 +502,65 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
     }
     return;
   }
-  // ---- cluster merge: this CTA's slice of the 16 x 512 outputs; every thread requests, in one
-  // round of peer loads, the splits' partials of its four outputs and their (m, l), then weighs
-  // them itself (w_s = e^(m_s - M), 1 / (sum_s w_s l_s + e^(sink - M))) ----
+  // ---- cluster merge: this CTA's slice of the 16 x 512 outputs; the weights of the slice's heads
+  // (w_s = e^(m_s - M), 1 / (sum_s w_s l_s + e^(sink - M))) first, then every thread requests, in one
+  // round of peer loads, the splits' partials of its four outputs and weighs them ----
   cluster_sync_all();  // every split's partial O, m and l are in its shared memory
   const uint32_t os_s = static_cast<uint32_t>(__cvta_generic_to_shared(os));
   const uint32_t ml_s = static_cast<uint32_t>(__cvta_generic_to_shared(&sm.ml[0]));
   constexpr int NF4 = HG * (D / 4);  // 2048 float4 outputs per (query, head group)
   const int chunk = (NF4 + S - 1) / S;
   const int f0 = split * chunk, f1 = min(NF4, f0 + chunk);
-  for (int f = f0 + tid; f < f1; f += THREADS) {
-    const int hh = f / (D / 4), d = (f % (D / 4)) * 4;
-    float4 v[MAX_SPLITS];
-    float2 ml[MAX_SPLITS];
+  // the splits' weights w_s = e^(m_s - M) and the normaliser of each head of this slice, once per
+  // (head, split) (a half-warp per head, lane = split) instead of per output; the products are summed
+  // in split order as before. The P buffer is free from here.
+  constexpr int MAXH = 12;  // heads a slice touches: chunk / 128 + 2 <= 10
+  float* wbuf = reinterpret_cast<float*>(sm.p);  // [MAXH][MAX_SPLITS]
+  float* ivbuf = wbuf + MAXH * MAX_SPLITS;
+  static_assert((MAXH * MAX_SPLITS + MAXH) * 4 <= sizeof(sm.p), "merge weights fit the P buffer");
+  const int hlo = f0 / (D / 4);
+  const int nhs = f1 > f0 ? (f1 - 1) / (D / 4) - hlo + 1 : 0;
+  if (tid < (nhs * MAX_SPLITS + 31) / 32 * 32) {  // whole warps
+    const int hl = tid / MAX_SPLITS, sp = tid % MAX_SPLITS;
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (hl < nhs && sp < S) ml = dsmem_f32x2(ml_s + (hlo + hl) * 8, sp);
+    float M = ml.x;
 #pragma unroll
-    for (int sp = 0; sp < MAX_SPLITS; ++sp)
-      if (sp < S) {
-        v[sp] = dsmem_f32x4(os_s + (hh * OSTRIDE + d) * 4, sp);
-        ml[sp] = dsmem_f32x2(ml_s + hh * 8, sp);
-      }
-    float M = -INFINITY;
-#pragma unroll
-    for (int sp = 0; sp < MAX_SPLITS; ++sp)
-      if (sp < S) M = fmaxf(M, ml[sp].x);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int o = MAX_SPLITS / 2; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o, MAX_SPLITS));
+    const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
     float L = 0.f;
 #pragma unroll
+    for (int s2 = 0; s2 < MAX_SPLITS; ++s2) {
+      const float ws = __shfl_sync(0xffffffffu, w, s2, MAX_SPLITS);
+      const float ls = __shfl_sync(0xffffffffu, ml.y, s2, MAX_SPLITS);
+      if (s2 < S) L = fmaf(ws, ls, L);
+    }
+    if (hl < nhs) {
+      if (sp < S) wbuf[hl * MAX_SPLITS + sp] = w;
+      if (sp == 0)
+        ivbuf[hl] = M == -INFINITY ? __int_as_float(0x7fc00000)
+                                   : 1.f / (L + exp2f(P.sink[h0 + hlo + hl] * LOG2E - M));
+    }
+  }
+  __syncthreads();
+  for (int f = f0 + tid; f < f1; f += THREADS) {
+    const int hh = f / (D / 4), d = (f % (D / 4)) * 4;
+    const float* wh = wbuf + (hh - hlo) * MAX_SPLITS;
+    float4 v[MAX_SPLITS];
+#pragma unroll
+    for (int sp = 0; sp < MAX_SPLITS; ++sp)
+      if (sp < S) v[sp] = dsmem_f32x4(os_s + (hh * OSTRIDE + d) * 4, sp);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
     for (int sp = 0; sp < MAX_SPLITS; ++sp)
       if (sp < S) {
-        const float w = ml[sp].x == -INFINITY ? 0.f : exp2f(ml[sp].x - M);
-        L += w * ml[sp].y;
+        const float w = wh[sp];
         acc.x = fmaf(w, v[sp].x, acc.x);
         acc.y = fmaf(w, v[sp].y, acc.y);
         acc.z = fmaf(w, v[sp].z, acc.z);
         acc.w = fmaf(w, v[sp].w, acc.w);
       }
-    const float iv = M == -INFINITY ? __int_as_float(0x7fc00000) : 1.f / (L + exp2f(P.sink[h0 + hh] * LOG2E - M));
+    const float iv = ivbuf[hh - hlo];
     write_out(P, sm, qi, h0, hh, d, make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv));
   }
   cluster_sync_all();  // the peers keep their partials until every CTA of the cluster has read them
