@@ -601,6 +601,15 @@ __global__ void __launch_bounds__(128) combine_kernel(Params P) {
   const float* pml = P.part + (P.s * P.hblocks * P.splits) * (int64_t)(HB * D);
   __shared__ float s_w[64];
   __shared__ float s_inv;
+  // the first splits' partials load while warp 0 works out the weights (the loads do not depend on
+  // them); the sums below keep split order
+  const int d = threadIdx.x * 4;
+  const float* src = P.part + unit0 * (HB * D) + hh * D + d;
+  const int npre = P.splits < 4 ? P.splits : 4;
+  float4 pre[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)  // (a repeat of the last split past npre: loaded, never used)
+    pre[u] = *reinterpret_cast<const float4*>(src + static_cast<int64_t>(u < npre ? u : npre - 1) * (HB * D));
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
@@ -623,10 +632,17 @@ __global__ void __launch_bounds__(128) combine_kernel(Params P) {
                                : 1.f / (L + exp2f(P.sink[h0 + hh] * LOG2E - M));
   }
   __syncthreads();
-  const int d = threadIdx.x * 4;
-  const float* src = P.part + unit0 * (HB * D) + hh * D + d;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  int sp = 0;
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    if (u < npre) {
+      const float w = s_w[u];
+      acc.x = fmaf(w, pre[u].x, acc.x);
+      acc.y = fmaf(w, pre[u].y, acc.y);
+      acc.z = fmaf(w, pre[u].z, acc.z);
+      acc.w = fmaf(w, pre[u].w, acc.w);
+    }
+  int sp = npre;
   for (; sp + 4 <= P.splits; sp += 4) {
     float4 v[4];
 #pragma unroll
