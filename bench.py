@@ -87,7 +87,7 @@ L2_NOTE = {
 # step); config 4 on `--kernel-case attn_prefill` (4,096 of the 65,536 queries, every query with
 # 1,152 list entries), scaled by 16 to the step's eight 8,192-query launches.
 TRAFFIC = {"c2": {"indexer_topk": 4319744, "sparse_attn": 777216},
-           "c4": {"tc::attn_tc_kernel": 16 * 547425536}}
+           "c4": {"tc::attn_tc_kernel": 16 * 545708288}}
 
 
 def _pkg():
