@@ -812,7 +812,8 @@ __device__ __forceinline__ void radix_levels(const uint32_t (&key)[PER], int nv,
 
 
 constexpr int BAND_CAP = 512;  // band keys rescored per round
-constexpr int STAGE_ROWS = 64;  // band key rows staged in shared memory at a time
+constexpr int STAGE_ROWS = 128;  // band key rows staged in shared memory at a time (128: every
+                                // thread has a 4-key x 4-head task, and most bands take one round)
 constexpr int OUT_STAGE = 2048;  // selections up to this size leave through shared memory
 constexpr float EPS_C = 0x1p-14f;
 
