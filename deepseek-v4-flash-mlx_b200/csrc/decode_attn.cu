@@ -285,20 +285,33 @@ __device__ __forceinline__ void finish_q(const Params& P, Smem& sm, float (&v)[Q
 }
 
 // final value of output element (head hh, dims d..d+3), after the normalisation: inverse RoPE on
-// the rope dims (angles from the shared table), then the store
+// the rope dims (angles from the shared table), then the store. Warp-collective (every lane calls
+// it; `valid` marks the lanes that hold an element): for a bf16 output the even lane of a pair
+// holding dims d and d + 4 of one head (d a multiple of 8) stores both as one 16-byte write, which
+// halves the writes that cross the bus when the output is pinned host memory.
 __device__ __forceinline__ void write_out(const Params& P, const Smem& sm, int64_t qi, int h0, int hh, int d,
-                                          float4 v) {
-  if (P.rope_freqs != nullptr && d >= D - P.rope_dim) {
+                                          float4 v, bool valid) {
+  if (valid && P.rope_freqs != nullptr && d >= D - P.rope_dim) {
     const int f0 = (d - (D - P.rope_dim)) >> 1;
     rotate_pair(v.x, v.y, sm.rope_c[f0], sm.rope_s[f0], true, &v.x, &v.y);
     rotate_pair(v.z, v.w, sm.rope_c[f0 + 1], sm.rope_s[f0 + 1], true, &v.z, &v.w);
   }
   const int64_t off = (qi * P.h + h0 + hh) * D + d;
-  if (P.out_dtype == DSV4_BF16)
-    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(P.out) + off) =
-        make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
-  else
+  if (P.out_dtype == DSV4_BF16) {
+    const uint32_t a = pack_bf16x2(v.x, v.y), b = pack_bf16x2(v.z, v.w);
+    const uint32_t pa = __shfl_xor_sync(0xffffffffu, a, 1), pb = __shfl_xor_sync(0xffffffffu, b, 1);
+    const bool pv = __shfl_xor_sync(0xffffffffu, valid ? 1 : 0, 1) != 0;
+    const bool even = (threadIdx.x & 1) == 0;
+    const bool pair = valid && pv && (d & 7) == (even ? 0 : 4) && (reinterpret_cast<uintptr_t>(P.out) & 15) == 0;
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(P.out) + off;
+    if (pair) {
+      if (even) *reinterpret_cast<uint4*>(o) = make_uint4(a, b, pa, pb);
+    } else if (valid) {
+      *reinterpret_cast<uint2*>(o) = make_uint2(a, b);
+    }
+  } else if (valid) {
     *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.out) + off) = v;
+  }
 }
 
 // grid (splits, h / 16, s); cluster (splits, 1, 1) when splits > 1
@@ -498,7 +511,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
       const int hh = c / (D / 4), d = (c % (D / 4)) * 4;
       const float4 a = *reinterpret_cast<const float4*>(os + hh * OSTRIDE + d);
       const float iv = sm.inv[hh];
-      write_out(P, sm, qi, h0, hh, d, make_float4(a.x * iv, a.y * iv, a.z * iv, a.w * iv));
+      write_out(P, sm, qi, h0, hh, d, make_float4(a.x * iv, a.y * iv, a.z * iv, a.w * iv), true);
     }
     return;
   }
@@ -509,8 +522,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
   const uint32_t os_s = static_cast<uint32_t>(__cvta_generic_to_shared(os));
   const uint32_t ml_s = static_cast<uint32_t>(__cvta_generic_to_shared(&sm.ml[0]));
   constexpr int NF4 = HG * (D / 4);  // 2048 float4 outputs per (query, head group)
-  const int chunk = (NF4 + S - 1) / S;
-  const int f0 = split * chunk, f1 = min(NF4, f0 + chunk);
+  const int chunk = ((NF4 + S - 1) / S + 1) & ~1;  // even: a slice starts on a 16-byte store pair
+  const int f0 = min(NF4, split * chunk), f1 = min(NF4, f0 + chunk);
   // the splits' weights w_s = e^(m_s - M) and the normaliser of each head of this slice, once per
   // (head, split) (a half-warp per head, lane = split) instead of per output; the products are summed
   // in split order as before. The P buffer is free from here.
@@ -543,13 +556,15 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
     }
   }
   __syncthreads();
-  for (int f = f0 + tid; f < f1; f += THREADS) {
-    const int hh = f / (D / 4), d = (f % (D / 4)) * 4;
+  for (int fb = f0 + warp * 32; fb < f1; fb += THREADS) {  // warp-uniform: write_out is collective
+    const int f = fb + lane;
+    const bool valid = f < f1;
+    const int hh = valid ? f / (D / 4) : hlo, d = valid ? (f % (D / 4)) * 4 : 0;
     const float* wh = wbuf + (hh - hlo) * MAX_SPLITS;
     float4 v[MAX_SPLITS];
 #pragma unroll
     for (int sp = 0; sp < MAX_SPLITS; ++sp)
-      if (sp < S) v[sp] = dsmem_f32x4(os_s + (hh * OSTRIDE + d) * 4, sp);
+      if (sp < S) v[sp] = valid ? dsmem_f32x4(os_s + (hh * OSTRIDE + d) * 4, sp) : make_float4(0.f, 0.f, 0.f, 0.f);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int sp = 0; sp < MAX_SPLITS; ++sp)
@@ -561,7 +576,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_attn_kernel(Params P) {
         acc.w = fmaf(w, v[sp].w, acc.w);
       }
     const float iv = ivbuf[hh - hlo];
-    write_out(P, sm, qi, h0, hh, d, make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv));
+    write_out(P, sm, qi, h0, hh, d, make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv), valid);
   }
   cluster_sync_all();  // the peers keep their partials until every CTA of the cluster has read them
 }
