@@ -86,13 +86,24 @@ __global__ void rmsnorm_kernel(dsv4_rmsnorm_params p) {
   }
 }
 
-__global__ void rope_kernel(dsv4_rope_params p) {
+// copy_rest: out != x, and the non-rope part of every row is copied by the same launch (elements
+// [0, s * heads * (dim - rope_dim)) of the loop; the rope pairs follow)
+__global__ void rope_kernel(dsv4_rope_params p, int copy_rest) {
   pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
   pdl_trigger();
   const int half = p.rope_dim / 2;
-  const int64_t total = p.s * p.heads * half;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
-       e += (int64_t)gridDim.x * blockDim.x) {
+  const int keep = p.dim - p.rope_dim;
+  const int64_t ncopy = copy_rest ? p.s * p.heads * keep : 0;
+  const int64_t total = ncopy + p.s * p.heads * half;
+  for (int64_t e0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e0 < total;
+       e0 += (int64_t)gridDim.x * blockDim.x) {
+    if (e0 < ncopy) {
+      const int64_t rowh = e0 / keep;
+      const int i = static_cast<int>(e0 % keep);
+      store_from_float(p.out, rowh * p.dim + i, p.out_dtype, load_as_float(p.x, rowh * p.dim + i, p.x_dtype));
+      continue;
+    }
+    const int64_t e = e0 - ncopy;
     const int i = static_cast<int>(e % half);
     const int64_t rowh = e / half;           // (position, head)
     const int64_t pos_row = rowh / p.heads;
@@ -111,20 +122,6 @@ __global__ void rope_kernel(dsv4_rope_params p) {
     rotate_pair(x0, x1, c, s, p.inverse != 0, &y0, &y1);
     store_from_float(p.out, off, p.out_dtype, y0);
     store_from_float(p.out, off + 1, p.out_dtype, y1);
-  }
-}
-
-// also copies the non-rope part when out != x
-__global__ void copy_nonrope_kernel(dsv4_rope_params p) {
-  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
-  pdl_trigger();
-  const int keep = p.dim - p.rope_dim;
-  const int64_t total = p.s * p.heads * keep;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t rowh = e / keep;
-    const int i = static_cast<int>(e % keep);
-    store_from_float(p.out, rowh * p.dim + i, p.out_dtype, load_as_float(p.x, rowh * p.dim + i, p.x_dtype));
   }
 }
 
@@ -269,14 +266,11 @@ extern "C" int dsv4_rope(const dsv4_rope_params* p, void* stream) {
   DSV4_CHECK_ARG(p->cis == nullptr || p->cis_rows > 0, "dsv4_rope: cis_rows must be > 0");
   DSV4_CHECK_DTYPE(is_float_dtype(p->x_dtype) && is_float_dtype(p->out_dtype), "dsv4_rope: F32/BF16 only");
   if (p->s == 0) return DSV4_OK;
-  const int64_t total = p->s * p->heads * (p->rope_dim / 2);
+  const int copy_rest = (p->out != p->x && p->dim > p->rope_dim) ? 1 : 0;
+  const int64_t total = p->s * p->heads * ((p->rope_dim / 2) + (copy_rest ? p->dim - p->rope_dim : 0));
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 16 * num_sms()) blocks = 16 * num_sms();
-  if (p->out != p->x && p->dim > p->rope_dim) {
-    DSV4_CUDA_CHECK(launch_pdl(nr::copy_nonrope_kernel, dim3(blocks), dim3(256), 0, as_stream(stream), *p));
-    DSV4_LAUNCH_CHECK("copy_nonrope_kernel");
-  }
-  DSV4_CUDA_CHECK(launch_pdl(nr::rope_kernel, dim3(blocks), dim3(256), 0, as_stream(stream), *p));
+  DSV4_CUDA_CHECK(launch_pdl(nr::rope_kernel, dim3(blocks), dim3(256), 0, as_stream(stream), *p, copy_rest));
   DSV4_LAUNCH_CHECK("rope_kernel");
   return DSV4_OK;
 }
