@@ -70,6 +70,8 @@ __global__ void cast_kernel(const void* x, int32_t xd, void* y, int32_t yd, int6
 
 // 16-byte copy by the SMs (either side may be pinned host memory, reached over the bus through its
 // unified address); under programmatic dependent launch it waits for the previous kernel first
+constexpr int COPY_THREADS = 64;
+
 __global__ void copy16_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t n16) {
   pdl_wait();
   pdl_trigger();
@@ -162,9 +164,11 @@ int dsv4_copy(void* dst, const void* src, size_t bytes, void* stream) {
                  "dsv4_copy: addresses and size must be multiples of 16 bytes");
   if (bytes == 0) return DSV4_OK;
   const int64_t n16 = static_cast<int64_t>(bytes / 16);
-  int blocks = static_cast<int>((n16 + 255) / 256);
-  if (blocks > 2 * num_sms()) blocks = 2 * num_sms();
-  DSV4_CUDA_CHECK(launch_pdl(copy16_kernel, dim3(blocks), dim3(256), 0, as_stream(stream),
+  // small blocks spread the 16-byte loads over more SMs: more reads of pinned memory in flight at
+  // once (a 33 KB step input: 9 blocks of 256 threads -> 33 of 64, ~0.4 us less per decode step)
+  int blocks = static_cast<int>((n16 + COPY_THREADS - 1) / COPY_THREADS);
+  if (blocks > 8 * num_sms()) blocks = 8 * num_sms();
+  DSV4_CUDA_CHECK(launch_pdl(copy16_kernel, dim3(blocks), dim3(COPY_THREADS), 0, as_stream(stream),
                              reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n16));
   return DSV4_OK;
 }
@@ -176,9 +180,11 @@ int dsv4_copy_beside(void* dst, const void* src, size_t bytes, void* stream) {
                  "dsv4_copy_beside: addresses and size must be multiples of 16 bytes");
   if (bytes == 0) return DSV4_OK;
   const int64_t n16 = static_cast<int64_t>(bytes / 16);
-  int blocks = static_cast<int>((n16 + 255) / 256);
-  if (blocks > 2 * num_sms()) blocks = 2 * num_sms();
-  DSV4_CUDA_CHECK(launch_pdl(copy16_beside_kernel, dim3(blocks), dim3(256), 0, as_stream(stream),
+  // small blocks spread the 16-byte loads over more SMs: more reads of pinned memory in flight at
+  // once (a 33 KB step input: 9 blocks of 256 threads -> 33 of 64, ~0.4 us less per decode step)
+  int blocks = static_cast<int>((n16 + COPY_THREADS - 1) / COPY_THREADS);
+  if (blocks > 8 * num_sms()) blocks = 8 * num_sms();
+  DSV4_CUDA_CHECK(launch_pdl(copy16_beside_kernel, dim3(blocks), dim3(COPY_THREADS), 0, as_stream(stream),
                              reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n16));
   return DSV4_OK;
 }
