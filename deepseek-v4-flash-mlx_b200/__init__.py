@@ -13,7 +13,7 @@ Drop-in ops with the reference's call signatures (ref_torch / v4mlx), each a tor
 There is no CPU path: the ops raise on CPU tensors and when libdsv4.so is missing.
 """
 from . import _lib
-from .compressor import compressor_decode_step, compressor_prefill
+from .compressor import CompressorStep, compressor_decode_pair, compressor_decode_step, compressor_prefill
 from .decode import DecodeRunner, SparseMLACache, decode_attention, window_attention
 from .hc import hc_head, hc_post, hc_pre
 from .indexer import indexer_scores, indexer_topk, indexer_topk_into
@@ -27,6 +27,7 @@ from .sparse_attn import get_window_topk_idxs, sparse_attn, sparse_attn_rope
 
 __all__ = [
     "sparse_attn", "sparse_attn_rope", "get_window_topk_idxs", "compressor_prefill", "compressor_decode_step",
+    "compressor_decode_pair", "CompressorStep",
     "rmsnorm", "perhead_norm", "apply_rotary_emb", "precompute_freqs", "precompute_freqs_cis", "norm_rope",
     "rope", "rope_freqs", "indexer_topk", "indexer_scores", "indexer_topk_into", "linear", "linear_multi", "q_down", "q_up",
     "kv_proj", "o_grouped", "QuantWeight", "quantize_int8_g64", "SparseMLACache", "decode_attention", "DecodeRunner",

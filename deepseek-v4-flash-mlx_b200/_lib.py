@@ -134,6 +134,8 @@ SIGNATURES = {
     "dsv4_decode_window_indices": (ctypes.c_int, [i32, i32, vp, vp, vp, i32, vp]),
     "dsv4_compressor_pool": (ctypes.c_int, [ctypes.POINTER(CompressorParams), vp]),
     "dsv4_compressor_decode": (ctypes.c_int, [ctypes.POINTER(CompressorDecodeParams), vp]),
+    "dsv4_compressor_decode_pair": (ctypes.c_int, [ctypes.POINTER(CompressorDecodeParams),
+                                                   ctypes.POINTER(CompressorDecodeParams), vp]),
     "dsv4_decode_rows": (ctypes.c_int, [ctypes.POINTER(DecodeRowsParams), vp]),
     "dsv4_hc_pre": (ctypes.c_int, [ctypes.POINTER(HcParams), vp]),
     "dsv4_hc_workspace_size": (ctypes.c_size_t, [i64, i32, i32, i32]),

@@ -7,6 +7,7 @@ projections run on the projection GEMM (bf16 operands, fp32 accumulate), then on
 holds the reference's hand-off tensors plus the device ring used by `compressor_decode_step`.
 """
 import ctypes
+from typing import NamedTuple
 
 import torch
 
@@ -127,6 +128,14 @@ def _compressor_decode_op(x: torch.Tensor, wkv: torch.Tensor, wkv_scale: torch.T
         scp = linear(x, _w_join(wgate, wgate_scale), torch.float32)
     else:
         kvp, scp = proj_kv, proj_score
+    p = _decode_params(kvp, scp, ape, norm_w, ring_kv, ring_score, positions, out, out_rows, head_dim, ratio,
+                       rope_head_dim, freqs, eps, key_image, key_inv, key_norm_max, image_stride, act_quant)
+    L.check(L.lib().dsv4_compressor_decode(ctypes.byref(p), L.stream_of(x)))
+
+
+def _decode_params(kvp, scp, ape, norm_w, ring_kv, ring_score, positions, out, out_rows, head_dim, ratio,
+                   rope_head_dim, freqs, eps, key_image, key_inv, key_norm_max, image_stride, act_quant):
+    """dsv4_compressor_decode_params of one compressor's decode step."""
     kvp, scp = kvp.contiguous(), scp.contiguous()
     p = L.CompressorDecodeParams()
     p.kv, p.score, p.ape = L.ptr(kvp), L.ptr(scp), L.ptr(ape)
@@ -143,7 +152,7 @@ def _compressor_decode_op(x: torch.Tensor, wkv: torch.Tensor, wkv_scale: torch.T
     if key_image is not None:
         p.key_image, p.key_inv, p.key_norm_max = L.ptr(key_image), L.ptr(key_inv), L.ptr(key_norm_max)
         p.image_stride = image_stride
-    L.check(L.lib().dsv4_compressor_decode(ctypes.byref(p), L.stream_of(x)))
+    return p
 
 
 @_compressor_decode_op.register_fake
@@ -175,3 +184,67 @@ def compressor_decode_step(x, wkv, wgate, ape, norm_w, ring_kv, ring_score, posi
     _compressor_decode_op(x, wkv_t, wkv_s, wg_t, wg_s, ape, norm_w, ring_kv, ring_score, positions, out, out_rows,
                           int(head_dim), int(ratio), int(rope_head_dim), freqs, float(eps), pk, ps, img, inv, nmax,
                           int(stride), 2 if rotate else int(act_quant))
+
+
+class CompressorStep(NamedTuple):
+    """One compressor's share of `compressor_decode_pair`: its projections of this token
+    (kv, score) fp32 [b, 2*head_dim], its weights, ring and output rows, as `compressor_decode_step`
+    takes them."""
+    proj: tuple
+    ape: torch.Tensor
+    norm_w: torch.Tensor | None
+    ring_kv: torch.Tensor
+    ring_score: torch.Tensor
+    out: torch.Tensor
+    out_rows: torch.Tensor
+    head_dim: int
+    key_image: tuple | None = None
+    act_quant: int = 0
+
+
+@torch.library.custom_op("dsv4::compressor_decode_pair",
+                         mutates_args=("a_ring_kv", "a_ring_score", "a_out", "b_ring_kv", "b_ring_score", "b_out",
+                                       "b_key_image", "b_key_inv", "b_key_norm_max"),
+                         device_types="cuda")
+def _compressor_decode_pair_op(positions: torch.Tensor, ratio: int, rope_head_dim: int, freqs: torch.Tensor,
+                               eps: float, a_kv: torch.Tensor, a_score: torch.Tensor, a_ape: torch.Tensor,
+                               a_norm_w: torch.Tensor | None, a_ring_kv: torch.Tensor, a_ring_score: torch.Tensor,
+                               a_out: torch.Tensor, a_out_rows: torch.Tensor, a_head_dim: int, a_act_quant: int,
+                               b_kv: torch.Tensor, b_score: torch.Tensor, b_ape: torch.Tensor,
+                               b_norm_w: torch.Tensor | None, b_ring_kv: torch.Tensor, b_ring_score: torch.Tensor,
+                               b_out: torch.Tensor, b_out_rows: torch.Tensor, b_head_dim: int, b_act_quant: int,
+                               b_key_image: torch.Tensor | None, b_key_inv: torch.Tensor | None,
+                               b_key_norm_max: torch.Tensor | None, b_image_stride: int) -> None:
+    pa = _decode_params(a_kv, a_score, a_ape, a_norm_w, a_ring_kv, a_ring_score, positions, a_out, a_out_rows,
+                        a_head_dim, ratio, rope_head_dim, freqs, eps, None, None, None, 0, a_act_quant)
+    pb = _decode_params(b_kv, b_score, b_ape, b_norm_w, b_ring_kv, b_ring_score, positions, b_out, b_out_rows,
+                        b_head_dim, ratio, rope_head_dim, freqs, eps, b_key_image, b_key_inv, b_key_norm_max,
+                        b_image_stride, b_act_quant)
+    L.check(L.lib().dsv4_compressor_decode_pair(ctypes.byref(pa), ctypes.byref(pb), L.stream_of(positions)))
+
+
+@_compressor_decode_pair_op.register_fake
+def _(positions, ratio, rope_head_dim, freqs, eps, a_kv, a_score, a_ape, a_norm_w, a_ring_kv, a_ring_score, a_out,
+      a_out_rows, a_head_dim, a_act_quant, b_kv, b_score, b_ape, b_norm_w, b_ring_kv, b_ring_score, b_out, b_out_rows,
+      b_head_dim, b_act_quant, b_key_image, b_key_inv, b_key_norm_max, b_image_stride):
+    return None
+
+
+def compressor_decode_pair(a: CompressorStep, b: CompressorStep, positions, ratio=4, rope_head_dim=64, freqs=None,
+                           eps=1e-6):
+    """Two compressors' decode steps for the same tokens (a decode block's main and indexer
+    compressors, oracle/decode_engine.py:96-105 each) in one launch: each is
+    `compressor_decode_step(proj=..., key_image=..., act_quant=...)` with its own weights, ring and
+    output rows, and the results are the same. Only the second step may carry a key image. The
+    custom op `dsv4::compressor_decode_pair`."""
+    if a.key_image is not None:
+        raise ValueError("compressor_decode_pair: only the second step may append to a key image")
+    L.require_cuda(positions, a.ring_kv, a.ring_score, a.out, a.out_rows, b.ring_kv, b.ring_score, b.out, b.out_rows)
+    if freqs is None:
+        freqs = rope_freqs(rope_head_dim, positions.device)
+    img, inv, nmax, stride = b.key_image if b.key_image is not None else (None, None, None, 0)
+    _compressor_decode_pair_op(positions, int(ratio), int(rope_head_dim), freqs, float(eps),
+                               a.proj[0], a.proj[1], a.ape, a.norm_w, a.ring_kv, a.ring_score, a.out, a.out_rows,
+                               int(a.head_dim), int(a.act_quant),
+                               b.proj[0], b.proj[1], b.ape, b.norm_w, b.ring_kv, b.ring_score, b.out, b.out_rows,
+                               int(b.head_dim), int(b.act_quant), img, inv, nmax, int(stride))

@@ -296,10 +296,9 @@ __device__ __forceinline__ void append_key_image(const dsv4_compressor_decode_pa
   }
 }
 
+// the ratio-4 step of sequence blockIdx.x for one compressor (the body of decode_r4_kernel)
 template <int NP>
-__global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_decode_params p) {
-  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
-  pdl_trigger();
+__device__ __forceinline__ void decode_r4_row(const dsv4_compressor_decode_params& p) {
   constexpr int R = 4;
   __shared__ float red[33];
   const int b = blockIdx.x, tid = threadIdx.x;
@@ -396,6 +395,24 @@ __global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_deco
     if (tid < 64) store_pair(vals[0][0], vals[0][1], 2 * tid, d, p.out, p.out_rows[b], p.out_dtype);
   }
   if (p.key_image) append_key_image<NP>(p, vals, red);
+}
+
+template <int NP>
+__global__ void __launch_bounds__(THREADS) decode_r4_kernel(dsv4_compressor_decode_params p) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel is complete from here
+  pdl_trigger();
+  decode_r4_row<NP>(p);
+}
+
+// two compressors' steps in one launch (grid.y = 2; the same batch): a decode block's main and
+// indexer compressors, which read the same token's projections and write disjoint rings and rows
+template <int NP>
+__global__ void __launch_bounds__(THREADS) decode_r4_pair_kernel(dsv4_compressor_decode_params p0,
+                                                                 dsv4_compressor_decode_params p1) {
+  pdl_wait();
+  pdl_trigger();
+  const dsv4_compressor_decode_params& p = blockIdx.y ? p1 : p0;
+  decode_r4_row<NP>(p);
 }
 
 __global__ void __launch_bounds__(THREADS) decode_kernel(dsv4_compressor_decode_params p) {
@@ -498,7 +515,7 @@ extern "C" int dsv4_compressor_pool(const dsv4_compressor_params* p, void* strea
   return DSV4_OK;
 }
 
-extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream) {
+static int check_decode_params(const dsv4_compressor_decode_params* p) {
   DSV4_CHECK_ARG(p == nullptr || p->act_quant == 0 ||
                      (p->act_quant == 1 && p->head_dim % 64 == 0 && (p->head_dim - p->rope_dim) % 64 == 0) ||
                      (p->act_quant == 2 && p->head_dim == 128),
@@ -516,6 +533,12 @@ extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, vo
                                               reinterpret_cast<uintptr_t>(p->key_image) % 16 == 0),
                  "dsv4_compressor_decode: a key image needs ratio 4, head_dim 128, fp32 out, inv, norm_max, "
                  "image_stride and a 16-byte aligned image");
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream) {
+  const int rc = check_decode_params(p);
+  if (rc != DSV4_OK) return rc;
   if (p->ratio == 4 && p->head_dim <= 2 * cmp::THREADS)
     DSV4_CUDA_CHECK(launch_pdl(cmp::decode_r4_kernel<1>, dim3(p->b), dim3(cmp::THREADS), 0, as_stream(stream), *p));
   else if (p->ratio == 4)
@@ -523,5 +546,23 @@ extern "C" int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, vo
   else
     DSV4_CUDA_CHECK(launch_pdl(cmp::decode_kernel, dim3(p->b), dim3(cmp::THREADS), 0, as_stream(stream), *p));
   DSV4_LAUNCH_CHECK("compressor decode_kernel");
+  return DSV4_OK;
+}
+
+extern "C" int dsv4_compressor_decode_pair(const dsv4_compressor_decode_params* a,
+                                           const dsv4_compressor_decode_params* b, void* stream) {
+  int rc = check_decode_params(a);
+  if (rc != DSV4_OK) return rc;
+  rc = check_decode_params(b);
+  if (rc != DSV4_OK) return rc;
+  const bool one = a->b == b->b && a->ratio == 4 && b->ratio == 4 && a->head_dim <= 2 * cmp::THREADS &&
+                   b->head_dim <= 2 * cmp::THREADS;
+  if (!one) {
+    rc = dsv4_compressor_decode(a, stream);
+    return rc != DSV4_OK ? rc : dsv4_compressor_decode(b, stream);
+  }
+  DSV4_CUDA_CHECK(launch_pdl(cmp::decode_r4_pair_kernel<1>, dim3(a->b, 2), dim3(cmp::THREADS), 0, as_stream(stream),
+                             *a, *b));
+  DSV4_LAUNCH_CHECK("compressor decode_r4_pair_kernel");
   return DSV4_OK;
 }

@@ -26,7 +26,7 @@ from dataclasses import dataclass, fields
 import torch
 
 from . import _lib as L
-from .compressor import compressor_decode_step, compressor_prefill
+from .compressor import CompressorStep, compressor_decode_pair, compressor_prefill
 from .configs import DIMS, LayerDims, window_only
 from .decode import SparseMLACache, decode_attention, decode_rows, window_attention
 from .hc import hc_post, hc_pre
@@ -222,13 +222,13 @@ class DecodeBlock:
         # this token's window slot, and where the compressors emit (when (p+1) % ratio == 0)
         win_rows, comp_rows, key_rows = decode_rows(c, pos)
         _norm_rope_into(kvp, W.kv_a_norm, pos, self.freqs, c.kv_pool, win_rows, d.rope_dim, self.act_quant)
-        compressor_decode_step(xn, W.c_wkv, W.c_wgate, W.c_ape, W.c_norm, c.ring_kv, c.ring_score, pos, c.kv_pool,
-                               comp_rows, head_dim=d.head_dim, ratio=d.ratio,
-                               rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(c_kv, c_sc), act_quant=self.act_quant)
-        compressor_decode_step(xn, W.i_wkv, W.i_wgate, W.i_ape, W.i_norm, c.ring_k_idx, c.ring_s_idx, pos,
-                               c.k_idx.view(-1, d.idx_dim), key_rows, head_dim=d.idx_dim, ratio=d.ratio,
-                               rope_head_dim=d.rope_dim, freqs=self.freqs, proj=(i_kv, i_sc),
-                               key_image=(*c.key_image, c.max_comp))
+        # the main and indexer compressors' ring steps in one launch
+        compressor_decode_pair(
+            CompressorStep((c_kv, c_sc), W.c_ape, W.c_norm, c.ring_kv, c.ring_score, c.kv_pool, comp_rows,
+                           d.head_dim, act_quant=int(self.act_quant)),
+            CompressorStep((i_kv, i_sc), W.i_ape, W.i_norm, c.ring_k_idx, c.ring_s_idx, c.k_idx.view(-1, d.idx_dim),
+                           key_rows, d.idx_dim, key_image=(*c.key_image, c.max_comp)),
+            pos, ratio=d.ratio, rope_head_dim=d.rope_dim, freqs=self.freqs)
         q_idx = rope(qi.view(b, d.idx_heads, d.idx_dim), pos, self.freqs, d.rope_dim)
         idx_buf = None
         if aux is not None:

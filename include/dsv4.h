@@ -346,6 +346,13 @@ typedef struct {
   int32_t act_quant;
 } dsv4_compressor_decode_params;
 DSV4_API int dsv4_compressor_decode(const dsv4_compressor_decode_params* p, void* stream);
+/* Two decode steps (two compressors, the same batch) in one launch: a decode block's main and
+ * indexer compressors read the same token's projections and write disjoint rings and rows, so one
+ * grid serves both (each as dsv4_compressor_decode with its own params). Pairs that do not share
+ * the batch or the ratio-4 fast path run as two launches. No reference counterpart: the reference
+ * runs its compressors one after the other (oracle/decode_engine.py:96-105). */
+DSV4_API int dsv4_compressor_decode_pair(const dsv4_compressor_decode_params* a,
+                                         const dsv4_compressor_decode_params* b, void* stream);
 
 /* ---- decode-step row bookkeeping of the device-resident state (pool of bf16 rows: per-sequence
  * window rings at win_base[i], then pages of compressed rows from comp_base through block_table;

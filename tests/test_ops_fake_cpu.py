@@ -16,7 +16,8 @@ def _e(*shape, dtype=torch.float32):
 def test_every_dsv4_op_has_a_fake():
     importlib.import_module(PKG)
     from torch._library.simple_registry import singleton
-    for name in ("sparse_attn", "indexer_topk", "compressor_prefill", "compressor_decode_step", "decode_attention",
+    for name in ("sparse_attn", "indexer_topk", "compressor_prefill", "compressor_decode_step", "compressor_decode_pair",
+                 "decode_attention",
                  "linear", "linear_multi", "rmsnorm", "norm_rope", "rope_positions", "apply_rotary_emb",
                  "get_window_topk_idxs"):
         assert hasattr(torch.ops.dsv4, name), name
@@ -48,5 +49,12 @@ def test_wrappers_trace_on_fake_tensors():
         dsv4.compressor_decode_step(_e(b, 4096), w, w, _e(4, 1024), _e(512), cache.ring_kv, cache.ring_score, pos,
                                     cache.kv_pool, torch.empty(b, dtype=torch.int64, device="cuda"), freqs=_e(32),
                                     proj=(_e(b, 1024), _e(b, 1024)))
+        ib = torch.empty(b, dtype=torch.int64, device="cuda")
+        dsv4.compressor_decode_pair(
+            dsv4.CompressorStep((_e(b, 1024), _e(b, 1024)), _e(4, 1024), _e(512), cache.ring_kv, cache.ring_score,
+                                cache.kv_pool, ib, 512),
+            dsv4.CompressorStep((_e(b, 256), _e(b, 256)), _e(4, 256), _e(128), cache.ring_k_idx, cache.ring_s_idx,
+                                cache.k_idx.view(-1, 128), ib, 128, key_image=(*cache.key_image, cache.max_comp)),
+            pos, freqs=_e(32))
         o = dsv4.decode_attention(cache, _e(b, 64, 512), _e(b, 64, 128), _e(b, 64), _e(64), pos, 128, freqs=_e(32))
         assert o.shape == (b, 64, 512) and o.dtype == torch.bfloat16
