@@ -66,3 +66,39 @@ def test_sparse_mla_prefill_matches_oracle():
     ref = NR.rope_at(SA.sparse_attn_chunked(q.float(), kvcat, W.sinks, idx, 512 ** -0.5), torch.arange(s), f,
                      inverse=True)
     assert_close_bf16(o.float(), ref, what="prefill attention output")
+
+
+def test_host_prefill_matches_device_prefill():
+    """The pinned-host path (per-chunk copies on two copy streams around the compute stream, two
+    device slots reused across chunks and across calls) gives the device path's bits, for a range
+    that starts mid-sequence and ends in a partial chunk."""
+    P = importlib.import_module(PKG + ".prefill")
+    s, top_k, chunk = 2048, 96, 384
+    W, x, q, kv, q_idx, w_idx = _inputs(s, 6)
+    Wd = W.to("cuda")
+    cw = P.CompressorWeights.from_attention_weights(Wd)
+    x = x.to(torch.bfloat16)
+    want = P.sparse_mla_prefill(x.cuda(), q.cuda(), kv.cuda(), q_idx.cuda(), w_idx.cuda(), Wd.sinks, cw, top_k=top_k,
+                                chunk=chunk)
+    pin = [t.contiguous().pin_memory() for t in (x, q, kv, q_idx, w_idx)]
+    h_out = torch.full((s, 64, 512), float("nan"), dtype=torch.bfloat16).pin_memory()
+    staging = P.PrefillStaging(chunk, "cuda")
+    for _ in range(2):   # the second call reuses the staging slots
+        h_out.fill_(float("nan"))
+        P.sparse_mla_prefill_host(*pin[:2], pin[2], *pin[3:], Wd.sinks, cw, h_out, top_k=top_k, chunk=chunk,
+                                  staging=staging)
+        torch.cuda.synchronize()
+        assert torch.equal(h_out, want.cpu())
+    # a mid-sequence range [a, b) against attend_queries over the same range
+    comp, keys = P.compress_range(x.cuda(), cw, 0, s // 4)
+    a, b = 640, 1900
+    ref = P.attend_queries(q[a:b].cuda(), q_idx[a:b].cuda(), w_idx[a:b].cuda(), kv.cuda(), comp, keys, Wd.sinks, a, b,
+                           top_k, chunk)
+    part = torch.empty((b - a, 64, 512), dtype=torch.bfloat16).pin_memory()
+    P.attend_queries_host(pin[1][a:b], pin[3][a:b], pin[4][a:b], kv.cuda(), comp, keys, Wd.sinks, a, b, part, top_k,
+                          chunk, staging)
+    torch.cuda.synchronize()
+    assert torch.equal(part, ref.cpu())
+    with pytest.raises(ValueError):
+        P.attend_queries_host(q[a:b], pin[3][a:b], pin[4][a:b], kv.cuda(), comp, keys, Wd.sinks, a, b, part, top_k,
+                              chunk, staging)   # q not pinned
