@@ -210,10 +210,22 @@ def _decode_attention_op(kv_pool: torch.Tensor, k_idx: torch.Tensor, block_table
         out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
         return _fused_decode_into(out, kv_pool, k_idx, block_table, win_base, image, q, q_idx, w_idx, sink, positions,
                                   freqs, idx_buf, top_k, scale, window, ratio, page, comp_base)
+    return _split_decode(kv_pool, k_idx, block_table, win_base, image, q, q_idx, w_idx, sink, positions, freqs,
+                         idx_buf, top_k, scale, window, ratio, page, comp_base, out_dtype)
+
+
+def _split_decode(kv_pool, k_idx, block_table, win_base, image, q, q_idx, w_idx, sink, positions, freqs, idx_buf,
+                  top_k, scale, window, ratio, page, comp_base, out_dtype, fetch_q=None):
+    """Larger batches: q's norm + RoPE on a side stream beside the indexer, then the attention
+    (split over the list, merged by the combine kernel). `fetch_q` (optional) launches work on the
+    side stream before the norm (the host step's copy of q, which only the attention reads)."""
+    b = q.shape[0]
     main = torch.cuda.current_stream(q.device)
     side = _side_stream(q.device)
     side.wait_stream(main)
     with torch.cuda.stream(side):          # q's norm + rope runs beside the indexer
+        if fetch_q is not None:
+            fetch_q()
         qr = norm_rope(q, positions, freqs, weight=None)
     indexer_topk_into(idx_buf.view(b, 1, -1), q_idx.reshape(b, 1, *q_idx.shape[-2:]), w_idx.reshape(b, 1, -1),
                       k_idx, top_k, positions.view(b, 1), ratio, out_col=0, out_offset=comp_base,
@@ -313,9 +325,10 @@ class DecodeRunner:
     reference's per-token path is a Python loop of library calls, oracle/v4_fast.py:82-122; here one
     graph launch replays the kernels). `step_device` replays with inputs already on the device.
     `step_host` runs a second graph that also holds the step's copies: this token's inputs from one
-    pinned host block to the device (one copy kernel: q, q_idx, w_idx and positions sit at fixed
-    offsets of both blocks), the kernels, and the output back to pinned host memory (a second copy
-    kernel), so a step is one launch.
+    pinned host block to the device (q, q_idx, w_idx and positions sit at fixed offsets of both
+    blocks), the kernels, and the output back to pinned host memory, so a step is one launch. Below
+    16 sequences the copies are kernels (copy kernels in, the attention kernel's own stores out); from
+    16 on they are copy-engine transfers, with q's beside the indexer.
     Callers that write their inputs straight into `host_inputs()` skip the host-side staging copy.
     """
 
@@ -383,10 +396,10 @@ class DecodeRunner:
         self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
         self.graph_host = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph_host, stream=self.stream):
-            # the step's inputs and output cross the bus by kernel loads / stores of the pinned
-            # blocks, not copy-engine transfers: tens of KB, latency-bound. The inputs by one copy
-            # kernel (dsv4_copy); at decode-sized batches the attention kernel stores o into the
-            # pinned output itself, else a second copy kernel brings it back.
+            # decode-sized batches: the step's inputs and output cross the bus by kernel loads /
+            # stores of the pinned blocks, not copy-engine transfers (tens of KB, latency-bound):
+            # the inputs by copy kernels (dsv4_copy), and the attention kernel stores o into the
+            # pinned output itself.
             if self.cache.batch < FUSED_Q_MAX_BATCH:
                 # q (the block's first field) is read only by the attention: its copy runs beside
                 # the top-k selection (dsv4_copy_beside), so only q_idx, w_idx and the positions
@@ -396,9 +409,18 @@ class DecodeRunner:
                 out = self._body_into(self.h_out,
                                       before_attention=lambda: L.copy_beside_(self.d_in[:nq], self.h_in[:nq]))
             else:
-                L.copy_(self.d_in, self.h_in)
-                out = self._body()
-                L.copy_(self.h_out, out)
+                # megabytes per step: copy-engine transfers (memcpy nodes), which take no SM (a copy
+                # kernel's blocks hold the SMs in a small-shared-memory configuration, so the
+                # indexer's CTAs could not start beside it). q (4 MB at batch 64) crosses on the side
+                # stream, beside the indexer, which needs only q_idx, w_idx and the positions
+                nq = self._q_bytes
+                self.d_in[nq:].copy_(self.h_in[nq:], non_blocking=True)
+                c = self.cache
+                out = _split_decode(c.kv_pool, c.k_idx, c.block_table, c.win_base, c.key_image, self.q, self.q_idx,
+                                    self.w_idx, self.sink, self.positions, self.freqs, self.idx, self.top_k,
+                                    c.head_dim ** -0.5, c.window, c.ratio, c.page, c.comp_base, self.out_dtype,
+                                    fetch_q=lambda: self.d_in[:nq].copy_(self.h_in[:nq], non_blocking=True))
+                self.h_out.copy_(out, non_blocking=True)
         self.out_host_graph = out
 
     def host_inputs(self):

@@ -78,9 +78,10 @@ def test_implicit_window_equals_explicit_list(dsv4):
             torch.testing.assert_close(a, bb, rtol=0, atol=0, msg=f"ctx={ctx} splits={splits}")
 
 
-def test_decode_runner_graph_and_host_path(dsv4):
+@pytest.mark.parametrize("b", [1, 20])   # the fused three-kernel step; the side-stream split step
+def test_decode_runner_graph_and_host_path(dsv4, b):
     C = _cfg()
-    case = C.make_decode_case(1, 4096, 512, seeds=[1])
+    case = C.make_decode_case(b, 4096, 512, seeds=list(range(1, b + 1)))
     r = dsv4.DecodeRunner(case.cache, case.sink, 512, out_dtype=torch.float32)
     r.q.copy_(case.q), r.q_idx.copy_(case.q_idx), r.w_idx.copy_(case.w_idx), r.positions.copy_(case.positions)
     dev_out = r.step_device().clone()
