@@ -71,6 +71,11 @@ __global__ void cast_kernel(const void* x, int32_t xd, void* y, int32_t yd, int6
 // 16-byte copy by the SMs (either side may be pinned host memory, reached over the bus through its
 // unified address); under programmatic dependent launch it waits for the previous kernel first
 constexpr int COPY_THREADS = 64;
+// The copies ask for the largest shared-memory carveout although they use none: an SM changes its
+// L1 / shared split only when it is empty, so copy blocks resident under a small carveout would
+// keep a following large-shared-memory kernel (launched early by programmatic dependent launch, or
+// beside on another stream) off that SM until they leave.
+constexpr int COPY_CARVEOUT = 100;
 
 __global__ void copy16_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t n16) {
   pdl_wait();
@@ -168,6 +173,8 @@ int dsv4_copy(void* dst, const void* src, size_t bytes, void* stream) {
   // once (a 33 KB step input: 9 blocks of 256 threads -> 33 of 64, ~0.4 us less per decode step)
   int blocks = static_cast<int>((n16 + COPY_THREADS - 1) / COPY_THREADS);
   if (blocks > 8 * num_sms()) blocks = 8 * num_sms();
+  static PerDeviceOnce carve;
+  DSV4_CUDA_CHECK(set_carveout_once(carve, copy16_kernel, COPY_CARVEOUT));
   DSV4_CUDA_CHECK(launch_pdl(copy16_kernel, dim3(blocks), dim3(COPY_THREADS), 0, as_stream(stream),
                              reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n16));
   return DSV4_OK;
@@ -184,6 +191,8 @@ int dsv4_copy_beside(void* dst, const void* src, size_t bytes, void* stream) {
   // once (a 33 KB step input: 9 blocks of 256 threads -> 33 of 64, ~0.4 us less per decode step)
   int blocks = static_cast<int>((n16 + COPY_THREADS - 1) / COPY_THREADS);
   if (blocks > 8 * num_sms()) blocks = 8 * num_sms();
+  static PerDeviceOnce carve;
+  DSV4_CUDA_CHECK(set_carveout_once(carve, copy16_beside_kernel, COPY_CARVEOUT));
   DSV4_CUDA_CHECK(launch_pdl(copy16_beside_kernel, dim3(blocks), dim3(COPY_THREADS), 0, as_stream(stream),
                              reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n16));
   return DSV4_OK;

@@ -121,6 +121,13 @@ inline cudaError_t set_smem_once(PerDeviceOnce& once, K kernel, int bytes) {
   return once([&] { return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); });
 }
 
+// a kernel's preferred shared-memory carveout (percent of the unified L1 / shared array), once per
+// device through `once`
+template <typename K>
+inline cudaError_t set_carveout_once(PerDeviceOnce& once, K kernel, int percent) {
+  return once([&] { return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, percent); });
+}
+
 // ---- element access by runtime dtype ------------------------------------------------------
 __device__ __forceinline__ float load_as_float(const void* p, int64_t i, int dtype) {
   if (dtype == DSV4_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
