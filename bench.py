@@ -936,21 +936,22 @@ def bench_block(env, name, headline):
     sampler.stop()
     clocks = sampler.summary(windows=windows)
     ms = statistics.median(ms_list) / K
-    # e2e: this token's hidden states from pinned host memory, the graph, the block output back
-    hx = [x.cpu().pin_memory() for x in xs]
-    ho = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    # e2e: through BlockRunner, one graph per token holding the copy of this token's hidden states
+    # and positions in from pinned host memory, the block, and the copy of its output back
+    runners = [Lm.BlockRunner(blk, stream=stream) for blk in blocks]
+    for r in range(R):
+        hx_r, hp_r = runners[r].host_inputs()
+        hx_r.copy_(xs[r].cpu())
+        hp_r.fill_(ctx - 1)
     ecur = [0]
 
     def run_host(k):
-        with torch.cuda.stream(stream):
-            for _ in range(k):
-                r = ecur[0] % R
-                xs[r].copy_(hx[r], non_blocking=True)
-                graphs[r].replay()
-                ho[r].copy_(outs[r], non_blocking=True)
-                ecur[0] += 1
+        for _ in range(k):
+            runners[ecur[0] % R].step_host()
+            ecur[0] += 1
 
-    run_host(3)
+    run_host(max(3, 2 * R))
+    torch.cuda.synchronize()
     ems_list, _ = timed_regions(env, stream, run_host, K, reps, _NoSampler())
     ems = statistics.median(ems_list) / K
     names = ("wq_a", "wq_b", "wkv", "wo_a", "wo_b") if window_only else Lm.MATRICES
@@ -969,9 +970,12 @@ def bench_block(env, name, headline):
             "gpu_launches": None if launches is None else int(round(launches * K)),
             "gpu_launches_per_step": launches,
             "e2e": {"value": cfgd["batch"] / (ems / 1000.0), "unit": "tok/s", "ms_per_step": ems,
-                    "h2d_bytes_per_step": hx[0].numel() * 4, "d2h_bytes_per_step": ho[0].numel() * 4,
-                    "path": "host hidden states -> block graph -> host"},
+                    "h2d_bytes_per_step": runners[0].h2d_bytes(), "d2h_bytes_per_step": runners[0].d2h_bytes(),
+                    "path": "pinned host hidden states + positions -> BlockRunner graph (copy kernels in and "
+                            "out) -> pinned host output"},
             "roofline": roofline, "cpu_baseline": _cpu_baseline(env, name, headline), "clocks": clocks}
+    for rn in runners:
+        rn.release()
     del graphs
     return line
 

@@ -17,7 +17,8 @@ from .compressor import CompressorStep, compressor_decode_pair, compressor_decod
 from .decode import DecodeRunner, SparseMLACache, decode_attention, window_attention
 from .hc import hc_head, hc_post, hc_pre
 from .indexer import indexer_scores, indexer_topk, indexer_topk_into
-from .layer import AttentionWeights, DecodeBlock, layer_rope_freqs, make_attention_weights, prefill_layer
+from .layer import (AttentionWeights, BlockRunner, DecodeBlock, layer_rope_freqs, make_attention_weights,
+                    prefill_layer)
 from .prefill import (CompressorWeights, PrefillStaging, ShardedPrefill, attend_queries_host, sparse_mla_prefill,
                       sparse_mla_prefill_host)
 from .mla import (N_GROUPS, N_HEADS, HEAD_DIM, O_LORA, ROPE_HD, QuantWeight, kv_proj, linear, linear_multi, o_grouped,
@@ -32,7 +33,7 @@ __all__ = [
     "rmsnorm", "perhead_norm", "apply_rotary_emb", "precompute_freqs", "precompute_freqs_cis", "norm_rope",
     "rope", "rope_freqs", "indexer_topk", "indexer_scores", "indexer_topk_into", "linear", "linear_multi", "q_down", "q_up",
     "kv_proj", "o_grouped", "QuantWeight", "quantize_int8_g64", "SparseMLACache", "decode_attention", "DecodeRunner",
-    "AttentionWeights", "DecodeBlock", "make_attention_weights", "prefill_layer", "CompressorWeights", "ShardedPrefill",
+    "AttentionWeights", "DecodeBlock", "BlockRunner", "make_attention_weights", "prefill_layer", "CompressorWeights", "ShardedPrefill",
     "sparse_mla_prefill", "sparse_mla_prefill_host", "attend_queries_host", "PrefillStaging", "hc_pre", "hc_post", "hc_head", "window_attention", "layer_rope_freqs",
 ]
 

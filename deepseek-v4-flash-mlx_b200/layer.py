@@ -261,3 +261,80 @@ def _norm_rope_into(x, weight, positions, freqs, pool, rows, rope_dim, act_quant
 def ctypes_byref(p):
     import ctypes
     return ctypes.byref(p)
+
+
+class BlockRunner:
+    """A `DecodeBlock`'s step from pinned host memory to pinned host memory, one CUDA graph launch
+    per token (the serving-loop form of config 5): the graph holds a copy kernel that brings this
+    token's hidden states and positions in from one pinned block (x [b, dim] fp32 and positions
+    int32 [b] at fixed offsets), the block's kernels, and a copy kernel that stores the block's
+    output [b, dim] fp32 into a pinned host tensor.
+
+    The block's step changes its cache (this token's window row, the compressors' rings), so the
+    first `step_host` runs eagerly, as the token it is, and only then captures the graph that the
+    later calls replay. Callers that write their inputs straight into `host_inputs()` skip the
+    host-side staging copy. The returned output is valid after `synchronize()` and until the next
+    step."""
+
+    def __init__(self, block: DecodeBlock, stream=None):
+        self.block = block
+        b, dim = block.batch, block.dims.dim
+        dev = block.cache.kv_pool.device
+        x_bytes = -(-b * dim * 4 // 256) * 256
+        self._in_bytes = x_bytes + -(-b * 4 // 256) * 256
+        self.d_in = torch.zeros(self._in_bytes, dtype=torch.uint8, device=dev)
+        self.h_in = torch.zeros(self._in_bytes, dtype=torch.uint8).pin_memory()
+        self.x = self.d_in[:b * dim * 4].view(torch.float32).view(b, dim)
+        self.positions = self.d_in[x_bytes:x_bytes + b * 4].view(torch.int32)
+        self.h_x = self.h_in[:b * dim * 4].view(torch.float32).view(b, dim)
+        self.h_pos = self.h_in[x_bytes:x_bytes + b * 4].view(torch.int32)
+        self.h_out = torch.empty((b, dim), dtype=torch.float32).pin_memory()
+        self.stream = stream or torch.cuda.Stream(dev)
+        self.graph = None
+        self._done = None
+
+    def _body(self):
+        L.copy_(self.d_in, self.h_in)
+        out = self.block.step(self.x, self.positions)
+        L.copy_(self.h_out, out)
+
+    def host_inputs(self):
+        """The pinned host views (x, positions) that `step_host` copies from."""
+        return self.h_x, self.h_pos
+
+    def step_host(self, x=None, positions=None):
+        """Host x [b, dim] and positions [b] in (or None: the `host_inputs()` views as they are),
+        the block's output [b, dim] fp32 out, in pinned host memory."""
+        if x is not None or positions is not None:
+            if self._done is not None:
+                self._done.synchronize()   # the previous step has read the pinned block
+            if x is not None:
+                self.h_x.copy_(x)
+            if positions is not None:
+                self.h_pos.copy_(positions)
+        with torch.cuda.stream(self.stream):
+            if self.graph is None:
+                self._body()               # this token, eagerly; then the graph for the next ones
+                self.graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.graph, stream=self.stream):
+                    self._body()
+            else:
+                self.graph.replay()
+            if self._done is None:
+                self._done = torch.cuda.Event()
+            self._done.record(self.stream)
+        return self.h_out
+
+    def h2d_bytes(self):
+        return self._in_bytes
+
+    def d2h_bytes(self):
+        return self.h_out.numel() * 4
+
+    def synchronize(self):
+        self.stream.synchronize()
+
+    def release(self):
+        """Drop the captured graph (its memory returns to torch's graph pool)."""
+        self.stream.synchronize()
+        self.graph = None

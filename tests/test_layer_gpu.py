@@ -183,3 +183,46 @@ def test_decode_block_steps_keep_key_image():
         IX.indexer_topk_into(out, q, w, c.k_idx, 256, positions=pos, ratio=4, mode=mode, key_image=kimg)
         outs.append(out.cpu())
     assert torch.equal(outs[0], outs[2]) and torch.equal(outs[1], outs[2])
+
+
+@pytest.mark.parametrize("ratio", [4, 128])
+def test_block_runner_host_steps_match_eager_steps(ratio):
+    """BlockRunner (pinned host x and positions in, one graph launch per token, pinned host output
+    out) against DecodeBlock.step on an identical block, token by token: the same bits, including
+    the first, eager, call and the replays after it, and the same cache afterwards."""
+    Lm = _layer()
+    C = importlib.import_module(PKG + ".configs")
+    b, ctx = 3, 2048
+    blocks = []
+    for _ in range(2):
+        if ratio == 4:
+            case = C.make_decode_case(b, ctx, 512, seeds=[500 + i for i in range(b)])
+            W = Lm.make_attention_weights(8, quant=True).to("cuda")
+            blocks.append(Lm.DecodeBlock(W, b, ctx + 16, top_k=512, cache=case.cache))
+        else:
+            dims = C.LayerDims(ratio=128)
+            W = Lm.make_attention_weights(9, dims=dims, quant=True).to("cuda")
+            blk = Lm.DecodeBlock(W, b, ctx + 16, dims=dims)
+            g = torch.Generator().manual_seed(12)
+            blk.cache.kv_pool.copy_(torch.randn(blk.cache.kv_pool.shape, generator=g).to(torch.bfloat16))
+            blocks.append(blk)
+    eager, hosted = blocks
+    runner = Lm.BlockRunner(hosted)
+    g = torch.Generator().manual_seed(7)
+    for step in range(6):   # positions cross a compressor block end
+        x = torch.randn(b, 4096, generator=g)
+        pos = torch.tensor([ctx - 30 + step + 5 * i for i in range(b)], dtype=torch.int32)
+        want = eager.step(x.cuda(), pos.cuda()).cpu()
+        if step % 2:
+            hx, hp = runner.host_inputs()
+            hx.copy_(x), hp.copy_(pos)
+            got = runner.step_host()
+        else:
+            got = runner.step_host(x, pos)
+        runner.synchronize()
+        assert torch.equal(got, want), f"step {step}"
+    assert torch.equal(eager.cache.kv_pool, hosted.cache.kv_pool)
+    if ratio == 4:
+        assert torch.equal(eager.cache.ring_kv, hosted.cache.ring_kv)
+        assert torch.equal(eager.cache.k_idx, hosted.cache.k_idx)
+    runner.release()
