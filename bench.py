@@ -624,7 +624,9 @@ def bench_decode(env, name, headline):
     ems = statistics.median(ems_list) / K
     e2e = {"value": world * batch / (ems / 1000.0), "unit": "tok/s", "ms_per_step": ems,
            "h2d_bytes_per_step": runners[0].h2d_bytes(), "d2h_bytes_per_step": runners[0].d2h_bytes(),
-           "path": "DecodeRunner.step_host (pinned host in/out; the copies by kernel loads / stores over the bus, and the step, in one CUDA graph; q in bf16)"}
+           "path": "DecodeRunner.step_host (pinned host in/out, q in bf16; the copies and the step in one CUDA "
+                   "graph: " + ("copy kernels in, the attention's own stores out" if batch < _mod("decode").FUSED_Q_MAX_BATCH
+                                else "copy-engine transfers, q's beside the indexer") + ")"}
 
     # ---- dominant-kernel timing: each kernel of the step, alone, over the replica rotation
     kern = kernel_times(cases, runners, stream, min(max(K, 20), 4 * R))
