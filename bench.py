@@ -626,7 +626,7 @@ def bench_decode(env, name, headline):
            "h2d_bytes_per_step": runners[0].h2d_bytes(), "d2h_bytes_per_step": runners[0].d2h_bytes(),
            "path": "DecodeRunner.step_host (pinned host in/out, q in bf16; the copies and the step in one CUDA "
                    "graph: " + ("copy kernels in, the attention's own stores out" if batch < _mod("decode").FUSED_Q_MAX_BATCH
-                                else "copy-engine transfers, q's beside the indexer") + ")"}
+                                else "copy-engine transfers in, q's beside the indexer; the merge kernel's own stores out") + ")"}
 
     # ---- dominant-kernel timing: each kernel of the step, alone, over the replica rotation
     kern = kernel_times(cases, runners, stream, min(max(K, 20), 4 * R))

@@ -215,10 +215,11 @@ def _decode_attention_op(kv_pool: torch.Tensor, k_idx: torch.Tensor, block_table
 
 
 def _split_decode(kv_pool, k_idx, block_table, win_base, image, q, q_idx, w_idx, sink, positions, freqs, idx_buf,
-                  top_k, scale, window, ratio, page, comp_base, out_dtype, fetch_q=None):
+                  top_k, scale, window, ratio, page, comp_base, out_dtype, fetch_q=None, out=None):
     """Larger batches: q's norm + RoPE on a side stream beside the indexer, then the attention
     (split over the list, merged by the combine kernel). `fetch_q` (optional) launches work on the
-    side stream before the norm (the host step's copy of q, which only the attention reads)."""
+    side stream before the norm (the host step's copy of q, which only the attention reads). `out`
+    (optional, q's shape) receives the result, device memory or a pinned host block."""
     b = q.shape[0]
     main = torch.cuda.current_stream(q.device)
     side = _side_stream(q.device)
@@ -232,6 +233,9 @@ def _split_decode(kv_pool, k_idx, block_table, win_base, image, q, q_idx, w_idx,
                       block_table=block_table, page=page, key_image=image)
     main.wait_stream(side)
     qr.record_stream(main)
+    if out is not None:
+        return sparse_attn_into(out, qr, kv_pool, sink, idx_buf, float(scale), freqs, positions, 64, 0, False, 1e-6,
+                                win_base, int(window))
     return sparse_attn_rope(qr, kv_pool, sink, idx_buf, scale, positions, freqs, 64, out_dtype,
                             win_base=win_base, window=window)
 
@@ -328,7 +332,8 @@ class DecodeRunner:
     pinned host block to the device (q, q_idx, w_idx and positions sit at fixed offsets of both
     blocks), the kernels, and the output back to pinned host memory, so a step is one launch. Below
     16 sequences the copies are kernels (copy kernels in, the attention kernel's own stores out); from
-    16 on they are copy-engine transfers, with q's beside the indexer.
+    16 on the inputs are copy-engine transfers, with q's beside the indexer, and the attention's merge
+    kernel stores the output into the pinned tensor itself.
     Callers that write their inputs straight into `host_inputs()` skip the host-side staging copy.
     """
 
@@ -419,8 +424,8 @@ class DecodeRunner:
                 out = _split_decode(c.kv_pool, c.k_idx, c.block_table, c.win_base, c.key_image, self.q, self.q_idx,
                                     self.w_idx, self.sink, self.positions, self.freqs, self.idx, self.top_k,
                                     c.head_dim ** -0.5, c.window, c.ratio, c.page, c.comp_base, self.out_dtype,
-                                    fetch_q=lambda: self.d_in[:nq].copy_(self.h_in[:nq], non_blocking=True))
-                self.h_out.copy_(out, non_blocking=True)
+                                    fetch_q=lambda: self.d_in[:nq].copy_(self.h_in[:nq], non_blocking=True),
+                                    out=self.h_out)
         self.out_host_graph = out
 
     def host_inputs(self):
