@@ -17,18 +17,19 @@ def _fill(c, g):
         t.copy_(torch.randn(t.shape, generator=g))
 
 
-@pytest.mark.parametrize("b,act_quant", [(1, 0), (5, 0), (32, 1)])
-def test_pair_matches_two_steps(b, act_quant):
+@pytest.mark.parametrize("b,act_quant,hd", [(1, 0, 512), (5, 0, 512), (32, 1, 512), (4, 0, 1024)])
+def test_pair_matches_two_steps(b, act_quant, hd):
+    """hd 1024: rows wider than the one-launch kernel takes, so the pair runs as two launches."""
     dsv4 = importlib.import_module(PKG)
     D = importlib.import_module(PKG + ".decode")
     layer = importlib.import_module(PKG + ".layer")
     g = torch.Generator().manual_seed(b * 7 + act_quant)
-    caches = [D.SparseMLACache(b, 256, device=DEV) for _ in range(2)]
+    caches = [D.SparseMLACache(b, 256, head_dim=hd, device=DEV) for _ in range(2)]
     st = torch.Generator().manual_seed(11)
     for c in caches:
         _fill(c, st)
         st.manual_seed(11)
-    hd, idd = caches[0].head_dim, 128
+    idd = 128
     ape_c, ape_i = torch.randn(4, 2 * hd, generator=g) * 0.1, torch.randn(4, 2 * idd, generator=g) * 0.1
     nw_c, nw_i = torch.rand(hd, generator=g) + 0.5, torch.rand(idd, generator=g) + 0.5
     ape_c, ape_i, nw_c, nw_i = (t.to(DEV) for t in (ape_c, ape_i, nw_c, nw_i))
