@@ -58,3 +58,4 @@ def test_wrappers_trace_on_fake_tensors():
             pos, freqs=_e(32))
         o = dsv4.decode_attention(cache, _e(b, 64, 512), _e(b, 64, 128), _e(b, 64), _e(64), pos, 128, freqs=_e(32))
         assert o.shape == (b, 64, 512) and o.dtype == torch.bfloat16
+
